@@ -1,0 +1,176 @@
+/*
+ * nqb.h - C ABI of libnqb, the B200 (sm_100a) packed binary low-rank linear.
+ *
+ * One layer computes, per token t and output row o,
+ *
+ *   latent[t,k] = mid[k]  * sum_i sign(V[k,i]) * x[t,i] * pre[i]
+ *   y[t,o]      = post[o] * sum_k sign(U[o,k]) * latent[t,k]
+ *               + sum_s x[t,idx[s]] * w[o,s] (* wscale[s] for int8 w)
+ *               + bias[o]
+ *               + rscale[j] * sum_i R[j,i] * x[t,i]      (for o == row_ids[j])
+ *
+ * with U [out x rank] and V [rank x in] stored in NanoQuant packed layout v1:
+ * int32 words, column c in word c/32 at bit c%32 (LSB first), bit 1 = -1,
+ * zero tail padding.  All pointers are device pointers unless stated
+ * otherwise; every call is asynchronous on the given stream (a cudaStream_t
+ * passed as void*, NULL = legacy default stream).  No entry point allocates
+ * device memory or synchronises the host.
+ *
+ * Every function returns NQB_OK (0) or one of the NQB_ERR_* codes below and
+ * never traps; nqb_last_error() returns a message for the calling thread.
+ */
+#ifndef NQB_H
+#define NQB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NQB_ABI_VERSION 1
+
+/* status codes */
+#define NQB_OK 0
+#define NQB_ERR_INVALID_ARGUMENT 1 /* bad shape, null pointer, inconsistent descriptor */
+#define NQB_ERR_ALIGNMENT 2        /* pointer alignment below what the layout needs   */
+#define NQB_ERR_DTYPE 3            /* dtype code not accepted for this operand         */
+#define NQB_ERR_CUDA 4             /* a CUDA runtime call failed                       */
+#define NQB_ERR_WORKSPACE 5        /* workspace missing or smaller than required       */
+#define NQB_ERR_UNSUPPORTED 6      /* valid request this build does not implement      */
+#define NQB_ERR_TIMEOUT 7          /* a bounded device-side wait gave up               */
+
+/* dtype codes */
+#define NQB_F32 0
+#define NQB_F16 1
+#define NQB_BF16 2
+#define NQB_I8 3
+#define NQB_I32 4
+
+/*
+ * One packed linear, described by plain device pointers.  Optional operands
+ * are NULL (and their counts 0).  The layer descriptor is read on the host at
+ * call time only; it may live on the stack.
+ *
+ * Mirrors the operands of launch_packed_linear
+ * (src/nanoquant/runtime/cuda_kernels.py:816-874 in the reference) plus two
+ * additions the reference runtime has no type for: the int8 residual-row
+ * overlay and the product-codebook right factor.
+ */
+typedef struct nqb_linear_desc {
+  int64_t in_features;  /* n */
+  int64_t out_features; /* m */
+  int64_t rank;         /* r */
+
+  const int32_t *left_words;  /* U, [m, ceil(r/32)] layout v1                */
+  const int32_t *right_words; /* V, [r, ceil(n/32)] layout v1; NULL when the
+                                 product-codebook fields below are used      */
+
+  const void *scale_pre;  /* [n] */
+  const void *scale_mid;  /* [r] */
+  const void *scale_post; /* [m] */
+  int32_t scale_dtype;    /* F32 / F16 / BF16 */
+
+  const void *bias; /* [m] or NULL */
+  int32_t bias_dtype;
+
+  /* salient (outlier) input columns, reference packed.py:230-352 */
+  int64_t outlier_count;          /* k */
+  const int32_t *outlier_indices; /* [k], strictly increasing, pre[idx]==0 */
+  const void *outlier_values;     /* [m, k] */
+  int32_t outlier_value_dtype;    /* F32 / F16 / BF16 / I8 */
+  const void *outlier_scales;     /* [k] in scale_dtype, only for I8 values */
+
+  /* int8 residual output rows (row form of the outlier overlay) */
+  int64_t overlay_rows;          /* R */
+  const int32_t *overlay_row_ids; /* [R], strictly increasing, < m          */
+  const int8_t *overlay_values;  /* [R, n]                                  */
+  const void *overlay_scales;    /* [R] in overlay_scale_dtype              */
+  int32_t overlay_scale_dtype;
+
+  /* product-codebook right factor (product-codebook-free-k16-v1, canonical
+   * orientation): rows < free_rows are plain words, the rest one 16-bit record
+   * per word indexing two 256-entry half-word tables.                        */
+  int64_t codebook_free_rows;
+  const int32_t *codebook_free_words; /* [free_rows, ceil(n/32)]            */
+  const int32_t *codebook_payload;    /* 16-bit records, two per word       */
+  const int16_t *codebook_first;      /* [256] bits 0..15 of a coded word   */
+  const int16_t *codebook_second;     /* [256] bits 16..31 of a coded word  */
+} nqb_linear_desc;
+
+/* Library identity: NQB_ABI_VERSION of the loaded build. */
+int nqb_abi_version(void);
+
+/* Last error message of the calling thread ("" after a successful call). */
+const char *nqb_last_error(void);
+
+/*
+ * Bytes of device workspace nqb_linear needs for `tokens` tokens.
+ * The workspace is scratch owned by the caller; it holds no state between
+ * calls and must not be shared by calls that may run concurrently.
+ */
+int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, size_t *bytes);
+
+/*
+ * y[tokens, m] (fp32, row-major) = layer(x[tokens, n]).
+ * x_dtype: F32 / F16 / BF16, row-major contiguous.  Deterministic: the same
+ * inputs give bitwise-identical y on every call.
+ * Replaces launch_packed_linear (reference cuda_kernels.py:816-874), the
+ * launcher behind CudaPackedBackend.linear (reference cuda_backend.py:243-278).
+ */
+int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int64_t tokens,
+               float *y, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Two or three layers that share one input x, executed as one stage-1 and
+ * one stage-2 launch.  y_out[i] is [tokens, layers[i].out_features] fp32.
+ * Replaces launch_grouped_packed_linears (reference cuda_kernels.py:301-374);
+ * unlike the reference it accepts any rank / width alignment, bias and int8
+ * outlier scales.
+ */
+int nqb_grouped_workspace_bytes(const nqb_linear_desc *layers, int32_t count, int64_t tokens,
+                                size_t *bytes);
+int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void *x,
+                       int32_t x_dtype, int64_t tokens, float *const *y_out, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/*
+ * Dense low-rank patch epilogue: y[t,o] += sum_p L[o,p] * sum_i R[p,i] x[t,i].
+ * L [m, p], R [p, n] in patch_dtype.  Workspace: tokens*p fp32.
+ * Replaces the F.linear pair of CudaPackedBackend.linear (reference
+ * cuda_backend.py:275-277).
+ */
+int nqb_patch_accumulate(const void *x, int32_t x_dtype, int64_t tokens, int64_t in_features,
+                         int64_t out_features, int64_t patch_rank, const void *patch_left,
+                         const void *patch_right, int32_t patch_dtype, float *y, void *workspace,
+                         size_t workspace_bytes, void *stream);
+
+/*
+ * Layout-v1 packing on the device.
+ * nqb_pack_signs: signs [rows, cols] (+1/-1, F32/F16/BF16) -> words [rows, ceil(cols/32)].
+ *   Replaces pack_sign_matrix (reference packed.py:170-188).
+ * nqb_unpack_signs: words -> signs fp32 [rows, cols].  Replaces
+ *   unpack_sign_matrix (reference packed.py:204-218).  Non-zero padding bits
+ *   are reported through *bad_padding_rows (device int32, count of offending
+ *   rows; may be NULL).
+ */
+int nqb_pack_signs(const void *signs, int32_t signs_dtype, int64_t rows, int64_t cols,
+                   int32_t *words, void *stream);
+int nqb_unpack_signs(const int32_t *words, int64_t rows, int64_t cols, float *signs,
+                     int32_t *bad_padding_rows, void *stream);
+
+/*
+ * Expand a product-codebook right factor to layout-v1 words on the device.
+ * Replaces decode_product_codebook_right_words (reference
+ * product_codebook.py:110-143).
+ */
+int nqb_decode_product_codebook(const int32_t *free_words, int64_t free_rows, int64_t rank,
+                                int64_t columns, const int32_t *payload, const int16_t *first,
+                                const int16_t *second, int32_t *words_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NQB_H */

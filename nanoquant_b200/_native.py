@@ -1,0 +1,177 @@
+"""ctypes binding of ``libnqb.so`` (declarations in ``include/nqb.h``).
+
+The library is loaded from the package's ``_lib`` directory and nowhere else;
+if it is missing, :func:`library` raises, so no caller can silently fall back
+to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+from nanoquant_b200.build import LIB_PATH
+
+NQB_OK = 0
+NQB_ERR_INVALID_ARGUMENT = 1
+NQB_ERR_ALIGNMENT = 2
+NQB_ERR_DTYPE = 3
+NQB_ERR_CUDA = 4
+NQB_ERR_WORKSPACE = 5
+NQB_ERR_UNSUPPORTED = 6
+NQB_ERR_TIMEOUT = 7
+
+NQB_F32 = 0
+NQB_F16 = 1
+NQB_BF16 = 2
+NQB_I8 = 3
+NQB_I32 = 4
+
+DTYPE_CODES = {
+    torch.float32: NQB_F32,
+    torch.float16: NQB_F16,
+    torch.bfloat16: NQB_BF16,
+    torch.int8: NQB_I8,
+    torch.int32: NQB_I32,
+}
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int32
+
+
+class LinearDesc(ctypes.Structure):
+    """Mirror of ``nqb_linear_desc`` (field order and types must match nqb.h)."""
+
+    _fields_ = [
+        ("in_features", _i64),
+        ("out_features", _i64),
+        ("rank", _i64),
+        ("left_words", _c_void_p),
+        ("right_words", _c_void_p),
+        ("scale_pre", _c_void_p),
+        ("scale_mid", _c_void_p),
+        ("scale_post", _c_void_p),
+        ("scale_dtype", _i32),
+        ("bias", _c_void_p),
+        ("bias_dtype", _i32),
+        ("outlier_count", _i64),
+        ("outlier_indices", _c_void_p),
+        ("outlier_values", _c_void_p),
+        ("outlier_value_dtype", _i32),
+        ("outlier_scales", _c_void_p),
+        ("overlay_rows", _i64),
+        ("overlay_row_ids", _c_void_p),
+        ("overlay_values", _c_void_p),
+        ("overlay_scales", _c_void_p),
+        ("overlay_scale_dtype", _i32),
+        ("codebook_free_rows", _i64),
+        ("codebook_free_words", _c_void_p),
+        ("codebook_payload", _c_void_p),
+        ("codebook_first", _c_void_p),
+        ("codebook_second", _c_void_p),
+    ]
+
+
+# name -> (restype, argtypes); every symbol declared in include/nqb.h
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "nqb_abi_version": (ctypes.c_int, []),
+    "nqb_last_error": (ctypes.c_char_p, []),
+    "nqb_linear_workspace_bytes": (ctypes.c_int, [ctypes.POINTER(LinearDesc), _i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_linear": (
+        ctypes.c_int,
+        [ctypes.POINTER(LinearDesc), _c_void_p, _i32, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
+    ),
+    "nqb_grouped_workspace_bytes": (
+        ctypes.c_int,
+        [ctypes.POINTER(LinearDesc), _i32, _i64, ctypes.POINTER(ctypes.c_size_t)],
+    ),
+    "nqb_grouped_linear": (
+        ctypes.c_int,
+        [
+            ctypes.POINTER(LinearDesc),
+            _i32,
+            _c_void_p,
+            _i32,
+            _i64,
+            ctypes.POINTER(_c_void_p),
+            _c_void_p,
+            ctypes.c_size_t,
+            _c_void_p,
+        ],
+    ),
+    "nqb_patch_accumulate": (
+        ctypes.c_int,
+        [_c_void_p, _i32, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p,
+         ctypes.c_size_t, _c_void_p],
+    ),
+    "nqb_pack_signs": (ctypes.c_int, [_c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p]),
+    "nqb_unpack_signs": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "nqb_decode_product_codebook": (
+        ctypes.c_int,
+        [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    ),
+}
+
+_lock = threading.Lock()
+_library: ctypes.CDLL | None = None
+
+
+class NativeError(RuntimeError):
+    """A libnqb call returned a non-zero status."""
+
+    def __init__(self, function: str, status: int, message: str) -> None:
+        super().__init__(f"{function} failed with status {status}: {message}")
+        self.function = function
+        self.status = status
+        self.message = message
+
+
+def library_path() -> Path:
+    return LIB_PATH
+
+
+def library() -> ctypes.CDLL:
+    """Load ``libnqb.so`` once; raises if the in-tree build is missing."""
+
+    global _library
+    with _lock:
+        if _library is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"libnqb.so is not built at {LIB_PATH}; run `python -m nanoquant_b200.build`"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                function = getattr(lib, name)
+                function.restype = restype
+                function.argtypes = argtypes
+            _library = lib
+        return _library
+
+
+def check(function: str, status: int) -> None:
+    if status != NQB_OK:
+        message = library().nqb_last_error().decode("utf-8", "replace")
+        raise NativeError(function, status, message)
+
+
+def call(function: str, *args: object) -> None:
+    check(function, getattr(library(), function)(*args))
+
+
+def current_stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(value: torch.Tensor | None) -> int | None:
+    return None if value is None else value.data_ptr()
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype not in DTYPE_CODES:
+        raise ValueError(f"dtype {dtype} has no libnqb code")
+    return DTYPE_CODES[dtype]

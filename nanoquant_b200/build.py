@@ -1,0 +1,99 @@
+"""Build ``libnqb.so`` (the C-ABI CUDA library) in-tree with nvcc for sm_100a.
+
+Usage: ``python -m nanoquant_b200.build [--force]``.  The library lands in
+``nanoquant_b200/_lib/libnqb.so``; sources are ``nanoquant_b200/csrc/*.cu``.
+The build runs without a GPU (nvcc cross-compiles).
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+SOURCE_DIR = PACKAGE_DIR / "csrc"
+LIB_DIR = PACKAGE_DIR / "_lib"
+LIB_PATH = LIB_DIR / "libnqb.so"
+INCLUDE_DIR = PACKAGE_DIR.parent / "include"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler",
+    "-fPIC,-O3,-Wall",
+    "-Xptxas",
+    "-v",
+]
+
+
+def _nvcc() -> str:
+    found = shutil.which("nvcc")
+    if found:
+        return found
+    candidate = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "bin" / "nvcc"
+    if candidate.exists():
+        return str(candidate)
+    raise RuntimeError("nvcc not found; set CUDA_HOME")
+
+
+def _sources() -> list[Path]:
+    return sorted(SOURCE_DIR.glob("*.cu"))
+
+
+def _inputs() -> list[Path]:
+    return _sources() + sorted(SOURCE_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
+
+
+def is_stale() -> bool:
+    if not LIB_PATH.exists():
+        return True
+    built = LIB_PATH.stat().st_mtime
+    return any(path.stat().st_mtime > built for path in _inputs())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every ``csrc/*.cu`` and link ``libnqb.so``; returns its path."""
+
+    if not force and not is_stale():
+        return LIB_PATH
+    nvcc = _nvcc()
+    obj_dir = LIB_DIR / "obj"
+    obj_dir.mkdir(parents=True, exist_ok=True)
+    objects = []
+    for source in _sources():
+        obj = obj_dir / (source.stem + ".o")
+        cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, "-I", str(INCLUDE_DIR), "-c", str(source), "-o", str(obj)]
+        result = subprocess.run(cmd, capture_output=True, text=True)
+        if result.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {source.name}:\n{result.stdout}\n{result.stderr}")
+        if verbose:
+            sys.stderr.write(result.stderr)
+        (obj_dir / (source.stem + ".ptxas.txt")).write_text(result.stderr)
+        objects.append(str(obj))
+    tmp = LIB_DIR / "libnqb.so.tmp"
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objects, "-lcuda"]
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"nvcc link failed:\n{result.stdout}\n{result.stderr}")
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--force", action="store_true")
+    parser.add_argument("--verbose", action="store_true")
+    args = parser.parse_args()
+    path = build(force=args.force, verbose=args.verbose)
+    print(path)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,351 @@
+"""B200 (sm_100a) runtime backend for the packed binary low-rank linear.
+
+:class:`CudaPackedSm100Backend` implements the four-call ``RuntimeBackend``
+protocol of the reference runtime (``src/nanoquant/runtime/backend.py:155-166``)
+and is a drop-in for ``CudaPackedBackend``
+(``src/nanoquant/runtime/cuda_backend.py:151-278``): same capability table,
+same ``prepare``/``linear`` contract and error types, fp32 output on the
+current stream.  All arithmetic runs in ``libnqb.so`` through its C ABI; there
+is no Python or library fallback, and every entry point raises when the
+library or a CUDA device is missing.
+
+The grouped-projection helpers mirror ``prepare_cuda_projection_group`` and
+``grouped_cuda_projection`` (reference ``cuda_backend.py:65-144``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from nanoquant_b200 import _native
+from nanoquant_b200.backend import (
+    BackendCapabilities,
+    DeviceLike,
+    PreparedLayer,
+    QuantizedLinearSpec,
+    RuntimeLayerState,
+    SupportResult,
+    WorkloadSpec,
+    evaluate_capabilities,
+)
+from nanoquant_b200.logical import canonical_torch_dtype
+from nanoquant_b200.overlay import OutlierRowOverlay, OverlaidLayerState
+from nanoquant_b200.packed import PACKED_LAYOUT_VERSION, PackedLayerState
+from nanoquant_b200.product_codebook import ProductCodebookLayerState
+
+CUDA_SM100_BACKEND_NAME = "cuda-packed-sm100a"
+CUDA_SM100_BACKEND_VERSION = "1"
+_FLOAT_DTYPES = ("float16", "bfloat16", "float32")
+
+
+@dataclass(frozen=True, slots=True)
+class _Sm100Payload:
+    """Device tensors of one prepared layer; ``desc`` points into them."""
+
+    device: torch.device
+    tensors: dict[str, torch.Tensor]
+    desc: _native.LinearDesc
+    patch_left: torch.Tensor | None
+    patch_right: torch.Tensor | None
+
+
+def _to_device(value: torch.Tensor | None, device: torch.device) -> torch.Tensor | None:
+    return None if value is None else value.detach().to(device=device).contiguous()
+
+
+def _build_payload(
+    state: PackedLayerState | ProductCodebookLayerState,
+    overlay: OutlierRowOverlay | None,
+    device: torch.device,
+) -> _Sm100Payload:
+    spec = state.spec
+    tensors: dict[str, torch.Tensor] = {}
+
+    def keep(name: str, value: torch.Tensor | None) -> torch.Tensor | None:
+        moved = _to_device(value, device)
+        if moved is not None:
+            tensors[name] = moved
+        return moved
+
+    desc = _native.LinearDesc()
+    desc.in_features = spec.in_features
+    desc.out_features = spec.out_features
+    desc.rank = spec.rank
+    patch_left = patch_right = None
+    if isinstance(state, ProductCodebookLayerState) and not state.factorization_transposed:
+        # canonical orientation: keep V compact, the kernels decode records in flight
+        desc.left_words = keep("left_words", state.factor_left_words).data_ptr()
+        desc.codebook_free_rows = state.free_rows
+        desc.codebook_free_words = keep("codebook_free_words", state.factor_right_free_words).data_ptr()
+        desc.codebook_payload = keep("codebook_payload", state.factor_right_coded_payload).data_ptr()
+        desc.codebook_first = keep("codebook_first", state.first_half_words).data_ptr()
+        desc.codebook_second = keep("codebook_second", state.second_half_words).data_ptr()
+        scale_pre, scale_mid, scale_post = state.factor_scale_pre, state.factor_scale_mid, state.factor_scale_post
+        outliers = (state.outlier_indices, state.outlier_values, state.outlier_scales)
+        bias = None
+    else:
+        packed = state.to_packed() if isinstance(state, ProductCodebookLayerState) else state
+        desc.left_words = keep("left_words", packed.left_words).data_ptr()
+        desc.right_words = keep("right_words", packed.right_words).data_ptr()
+        scale_pre, scale_mid, scale_post = packed.scale_pre, packed.scale_mid, packed.scale_post
+        outliers = (packed.outlier_indices, packed.outlier_values, packed.outlier_scales)
+        bias = packed.bias
+        patch_left = keep("patch_left", packed.patch_left)
+        patch_right = keep("patch_right", packed.patch_right)
+    desc.scale_pre = keep("scale_pre", scale_pre).data_ptr()
+    desc.scale_mid = keep("scale_mid", scale_mid).data_ptr()
+    desc.scale_post = keep("scale_post", scale_post).data_ptr()
+    desc.scale_dtype = _native.dtype_code(scale_pre.dtype)
+    if bias is not None:
+        desc.bias = keep("bias", bias).data_ptr()
+        desc.bias_dtype = _native.dtype_code(bias.dtype)
+    indices, values, scales = outliers
+    if indices is not None and values is not None:
+        desc.outlier_count = int(indices.numel())
+        desc.outlier_indices = keep("outlier_indices", indices.to(torch.int32)).data_ptr()
+        desc.outlier_values = keep("outlier_values", values).data_ptr()
+        desc.outlier_value_dtype = _native.dtype_code(values.dtype)
+        if scales is not None:
+            desc.outlier_scales = keep("outlier_scales", scales.reshape(-1)).data_ptr()
+    if overlay is not None:
+        desc.overlay_rows = int(overlay.row_ids.numel())
+        desc.overlay_row_ids = keep("overlay_row_ids", overlay.row_ids).data_ptr()
+        desc.overlay_values = keep("overlay_values", overlay.values).data_ptr()
+        desc.overlay_scales = keep("overlay_scales", overlay.scales).data_ptr()
+        desc.overlay_scale_dtype = _native.dtype_code(overlay.scales.dtype)
+    return _Sm100Payload(device, tensors, desc, patch_left, patch_right)
+
+
+def _cuda_device(device: DeviceLike) -> torch.device:
+    target = torch.device(device)
+    if target.type != "cuda":
+        raise ValueError("sm100a packed backend preparation requires a CUDA device")
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is not available in this runtime")
+    if target.index is None:
+        target = torch.device("cuda", torch.cuda.current_device())
+    return target
+
+
+def _check_input(value: torch.Tensor, spec: QuantizedLinearSpec, device: torch.device) -> None:
+    """The input contract of the reference ``CudaPackedBackend.linear`` (cuda_backend.py:249-262)."""
+
+    if value.device != device:
+        raise ValueError("CUDA packed input and prepared layer must use the same device")
+    if canonical_torch_dtype(value.dtype) not in _FLOAT_DTYPES:
+        raise ValueError(f"CUDA packed input dtype is unsupported: {value.dtype}")
+    if value.ndim == 0 or value.shape[-1] != spec.in_features:
+        raise ValueError("CUDA packed input feature dimension differs from the layer")
+    if value.numel() == 0:
+        raise ValueError("CUDA packed input must contain at least one token")
+    if not value.is_contiguous():
+        raise ValueError("CUDA packed input must be contiguous")
+    if value.requires_grad:
+        raise ValueError("CUDA packed runtime does not support autograd")
+
+
+def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLinearSpec) -> torch.Tensor:
+    """Run one prepared layer on ``value`` (any leading shape) and return fp32 ``[..., out]``."""
+
+    tokens = value.numel() // spec.in_features
+    output = torch.empty((*value.shape[:-1], spec.out_features), dtype=torch.float32, device=value.device)
+    needed = ctypes.c_size_t(0)
+    desc_ref = ctypes.byref(payload.desc)
+    _native.call("nqb_linear_workspace_bytes", desc_ref, tokens, ctypes.byref(needed))
+    workspace = _workspace(needed.value, value.device)
+    stream = _native.current_stream_handle(value.device)
+    _native.call(
+        "nqb_linear",
+        desc_ref,
+        value.data_ptr(),
+        _native.dtype_code(value.dtype),
+        tokens,
+        output.data_ptr(),
+        workspace.data_ptr(),
+        workspace.numel(),
+        stream,
+    )
+    if payload.patch_left is not None and payload.patch_right is not None:
+        patch_rank = payload.patch_left.shape[1]
+        patch_space = _workspace(tokens * patch_rank * 4, value.device)
+        _native.call(
+            "nqb_patch_accumulate",
+            value.data_ptr(),
+            _native.dtype_code(value.dtype),
+            tokens,
+            spec.in_features,
+            spec.out_features,
+            patch_rank,
+            payload.patch_left.data_ptr(),
+            payload.patch_right.data_ptr(),
+            _native.dtype_code(payload.patch_left.dtype),
+            output.data_ptr(),
+            patch_space.data_ptr(),
+            patch_space.numel(),
+            stream,
+        )
+    return output
+
+
+class CudaPackedSm100Backend:
+    """sm_100a two-stage packed linear behind the reference ``RuntimeBackend`` protocol."""
+
+    name = CUDA_SM100_BACKEND_NAME
+    version = CUDA_SM100_BACKEND_VERSION
+    packed_layout = PACKED_LAYOUT_VERSION
+
+    def capabilities(self) -> BackendCapabilities:
+        return BackendCapabilities(
+            logical_formats=("nanoquant-v1",),
+            device_types=("cuda",),
+            input_dtypes=_FLOAT_DTYPES,
+            factor_dtypes=_FLOAT_DTYPES,
+            scale_dtypes=_FLOAT_DTYPES,
+            outlier_value_dtypes=(*_FLOAT_DTYPES, "int8"),
+            workload_kinds=("prefill", "decode"),
+            supports_bias=True,
+            supports_outliers=True,
+            supports_deterministic=True,
+            patch_value_dtypes=_FLOAT_DTYPES,
+        )
+
+    def supports(self, op: QuantizedLinearSpec, workload: WorkloadSpec) -> SupportResult:
+        result = evaluate_capabilities(self.capabilities(), op, workload)
+        if not result.supported:
+            return result
+        try:
+            _native.library()
+        except (RuntimeError, OSError) as error:
+            return SupportResult.rejected("NQ-INF-CUDA-KERNEL", str(error))
+        if not torch.cuda.is_available():
+            return SupportResult.rejected("NQ-INF-DEVICE-UNAVAILABLE", "CUDA is not available in this runtime")
+        capability = torch.cuda.get_device_capability()
+        if capability != (10, 0):
+            return SupportResult.rejected(
+                "NQ-INF-CUDA-CAPABILITY",
+                f"CUDA compute capability {capability[0]}.{capability[1]} is not sm_100 (B200)",
+            )
+        return result
+
+    def prepare(self, state: RuntimeLayerState, device: DeviceLike) -> PreparedLayer:
+        overlay = None
+        base = state
+        if isinstance(state, OverlaidLayerState):
+            base, overlay = state.base, state.overlay
+        if not isinstance(base, (PackedLayerState, ProductCodebookLayerState)):
+            raise TypeError(
+                "sm100a packed backend requires PackedLayerState, ProductCodebookLayerState "
+                "or OverlaidLayerState"
+            )
+        target = _cuda_device(device)
+        _native.library()
+        payload = _build_payload(base, overlay, target)
+        return PreparedLayer(self.name, self.version, state.spec, payload)
+
+    def linear(self, value: torch.Tensor, layer: PreparedLayer) -> torch.Tensor:
+        if layer.backend_name != self.name or layer.backend_version != self.version:
+            raise ValueError("prepared runtime layer belongs to a different backend")
+        if not isinstance(layer.payload, _Sm100Payload):
+            raise TypeError("prepared runtime layer has an invalid sm100a packed payload")
+        _check_input(value, layer.spec, layer.payload.device)
+        return packed_linear(value, layer.payload, layer.spec)
+
+
+@dataclass(frozen=True, slots=True)
+class Sm100ProjectionGroup:
+    """Two or three prepared layers sharing one input, run as one grouped call."""
+
+    device: torch.device
+    layers: tuple[PreparedLayer, ...]
+    descs: ctypes.Array  # type: ignore[type-arg]
+    in_features: int
+    output_features: tuple[int, ...]
+
+
+def prepare_sm100_projection_group(layers: tuple[PreparedLayer, ...]) -> Sm100ProjectionGroup | None:
+    """Group compatible prepared layers (reference ``prepare_cuda_projection_group``, cuda_backend.py:65-120).
+
+    Returns ``None`` when the layers cannot share one call, as the reference does.
+    Unlike the reference, ranks and widths need no 8-alignment and bias,
+    int8 outlier scales and overlays are allowed; a low-rank patch is not.
+    """
+
+    if len(layers) not in (2, 3):
+        return None
+    payloads = tuple(layer.payload for layer in layers)
+    if not all(isinstance(payload, _Sm100Payload) for payload in payloads):
+        return None
+    first = payloads[0]
+    in_features = layers[0].spec.in_features
+    if any(payload.device != first.device for payload in payloads):
+        return None
+    if any(layer.spec.in_features != in_features for layer in layers):
+        return None
+    if any(payload.desc.scale_dtype != first.desc.scale_dtype for payload in payloads):
+        return None
+    if any(payload.patch_left is not None for payload in payloads):
+        return None
+    descs = (_native.LinearDesc * len(layers))(*(payload.desc for payload in payloads))
+    return Sm100ProjectionGroup(
+        first.device,
+        tuple(layers),
+        descs,
+        in_features,
+        tuple(layer.spec.out_features for layer in layers),
+    )
+
+
+def grouped_sm100_projection(value: torch.Tensor, group: Sm100ProjectionGroup) -> tuple[torch.Tensor, ...]:
+    """Run a projection group on ``value``; returns one fp32 tensor per member."""
+
+    if value.device != group.device:
+        raise ValueError("grouped CUDA projection input uses a different device")
+    _check_input(value, group.layers[0].spec, group.device)
+    tokens = value.numel() // group.in_features
+    outputs = tuple(
+        torch.empty((*value.shape[:-1], width), dtype=torch.float32, device=value.device)
+        for width in group.output_features
+    )
+    count = len(group.layers)
+    needed = ctypes.c_size_t(0)
+    _native.call("nqb_grouped_workspace_bytes", group.descs, count, tokens, ctypes.byref(needed))
+    workspace = _workspace(needed.value, value.device)
+    out_ptrs = (ctypes.c_void_p * count)(*(out.data_ptr() for out in outputs))
+    _native.call(
+        "nqb_grouped_linear",
+        group.descs,
+        count,
+        value.data_ptr(),
+        _native.dtype_code(value.dtype),
+        tokens,
+        out_ptrs,
+        workspace.data_ptr(),
+        workspace.numel(),
+        _native.current_stream_handle(value.device),
+    )
+    return outputs
+
+
+# Names of the reference module, for callers that import them directly.
+prepare_cuda_projection_group = prepare_sm100_projection_group
+grouped_cuda_projection = grouped_sm100_projection
+
+
+__all__ = [
+    "CUDA_SM100_BACKEND_NAME",
+    "CUDA_SM100_BACKEND_VERSION",
+    "CudaPackedSm100Backend",
+    "Sm100ProjectionGroup",
+    "grouped_cuda_projection",
+    "grouped_sm100_projection",
+    "packed_linear",
+    "prepare_cuda_projection_group",
+    "prepare_sm100_projection_group",
+]

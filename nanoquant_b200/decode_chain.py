@@ -1,0 +1,185 @@
+"""Synthetic decoder-shaped stacks of packed linears (the benchmark workloads).
+
+A decoder layer's packed linears are the q/k/v/o attention projections and the
+gate/up/down MLP projections.  :func:`make_decoder_layers` builds random
+layout-v1 layers of a given model shape (uniform random sign bits, the scales
+of BASELINE config 0: ``|N(0,1)| * 0.05 + 0.01`` in fp16, ``scale_mid = 1``),
+directly on the GPU.  :class:`DecodeChain` runs one decode token through every
+layer with the grouped QKV and gate/up calls the reference's model shell uses
+(``src/nanoquant/runtime/torch_model.py:311-327, 492-505``), and can capture
+that step in a CUDA graph.
+
+Rank follows the reference's budget formula at a target bits-per-weight:
+``r = floor(bpw * m * n / (m + n))``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from nanoquant_b200.backend import PreparedLayer, QuantizedLinearSpec
+from nanoquant_b200.cuda_backend import (
+    CudaPackedSm100Backend,
+    Sm100ProjectionGroup,
+    grouped_sm100_projection,
+    prepare_sm100_projection_group,
+)
+from nanoquant_b200.packed import PACKED_LAYOUT_VERSION, PackedLayerState, packed_word_count
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    name: str
+    layers: int
+    hidden: int
+    intermediate: int
+    q_heads: int
+    kv_heads: int
+    head_dim: int
+    bpw: float = 1.0
+
+    def projections(self) -> dict[str, tuple[int, int]]:
+        """projection name -> (in_features, out_features)."""
+
+        q = self.q_heads * self.head_dim
+        kv = self.kv_heads * self.head_dim
+        return {
+            "q_proj": (self.hidden, q),
+            "k_proj": (self.hidden, kv),
+            "v_proj": (self.hidden, kv),
+            "o_proj": (q, self.hidden),
+            "gate_proj": (self.hidden, self.intermediate),
+            "up_proj": (self.hidden, self.intermediate),
+            "down_proj": (self.intermediate, self.hidden),
+        }
+
+    def rank(self, n: int, m: int) -> int:
+        return int(self.bpw * m * n // (m + n))
+
+
+QWEN3_8B = DecoderShape("qwen3-8b", 36, 4096, 12288, 32, 8, 128, 1.0)
+GEMMA3_1B = DecoderShape("gemma-3-1b", 26, 1152, 6912, 4, 1, 256, 1.0)
+LLAMA3_8B_055 = DecoderShape("llama-3-8b", 32, 4096, 14336, 32, 8, 128, 0.55)
+
+
+def layer_bytes(n: int, m: int, r: int, *, scale_bytes: int = 2) -> int:
+    """Algorithmic weight bytes of one packed layer: sign words plus the three scale vectors."""
+
+    return 4 * (m * packed_word_count(r) + r * packed_word_count(n)) + scale_bytes * (n + r + m)
+
+
+def random_packed_layer(name: str, n: int, m: int, r: int, generator: torch.Generator,
+                        device: torch.device) -> PackedLayerState:
+    """Uniform random signs as layout-v1 words (tail bits cleared) with config-0 style scales."""
+
+    def words(rows: int, columns: int) -> torch.Tensor:
+        per_row = packed_word_count(columns)
+        raw = torch.randint(-(2**31), 2**31 - 1, (rows, per_row), generator=generator, dtype=torch.int64,
+                            device=device)
+        tail = columns % 32
+        if tail:
+            raw[:, -1] &= (1 << tail) - 1
+        return raw.to(torch.int32).contiguous()
+
+    def scales(size: int) -> torch.Tensor:
+        return (torch.randn(size, generator=generator, device=device).abs() * 0.05 + 0.01).half()
+
+    spec = QuantizedLinearSpec(name, "nanoquant-v1", n, m, r, "float32", "float16")
+    return PackedLayerState(spec, PACKED_LAYOUT_VERSION, words(m, r), words(r, n), scales(n),
+                            torch.ones(r, device=device).half(), scales(m))
+
+
+def make_decoder_layers(shape: DecoderShape, device: torch.device, *, layers: int | None = None,
+                        seed: int = 0) -> list[dict[str, PackedLayerState]]:
+    generator = torch.Generator(device=device).manual_seed(seed)
+    result = []
+    for index in range(shape.layers if layers is None else layers):
+        block = {}
+        for proj, (n, m) in shape.projections().items():
+            block[proj] = random_packed_layer(f"blocks.{index}.{proj}", n, m, shape.rank(n, m), generator, device)
+        result.append(block)
+    return result
+
+
+@dataclass
+class _PreparedBlock:
+    qkv: Sm100ProjectionGroup
+    o_proj: PreparedLayer
+    gate_up: Sm100ProjectionGroup
+    down_proj: PreparedLayer
+
+
+class DecodeChain:
+    """All packed linears of a decoder, run for one decode step (batch ``tokens``)."""
+
+    def __init__(self, shape: DecoderShape, blocks: list[dict[str, PackedLayerState]], device: torch.device,
+                 tokens: int = 1) -> None:
+        self.shape = shape
+        self.device = device
+        self.tokens = tokens
+        self.backend = CudaPackedSm100Backend()
+        self.blocks: list[_PreparedBlock] = []
+        for block in blocks:
+            prepared = {name: self.backend.prepare(state, device) for name, state in block.items()}
+            qkv = prepare_sm100_projection_group((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]))
+            gate_up = prepare_sm100_projection_group((prepared["gate_proj"], prepared["up_proj"]))
+            if qkv is None or gate_up is None:
+                raise RuntimeError("grouped projections could not be prepared")
+            self.blocks.append(_PreparedBlock(qkv, prepared["o_proj"], gate_up, prepared["down_proj"]))
+        projections = shape.projections()
+        hidden_in = torch.randn(tokens, shape.hidden, device=device).bfloat16()
+        self.inputs = {
+            "hidden": hidden_in,
+            "attn": torch.randn(tokens, projections["o_proj"][0], device=device).bfloat16(),
+            "mlp": torch.randn(tokens, shape.hidden, device=device).bfloat16(),
+            "act": torch.randn(tokens, shape.intermediate, device=device).bfloat16(),
+        }
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.graph_output: torch.Tensor | None = None
+
+    @property
+    def launches_per_step(self) -> int:
+        """Kernel launches of one step: two stage launches per (grouped) call, four calls per layer."""
+
+        return 8 * len(self.blocks)
+
+    def algorithmic_bytes(self) -> int:
+        """Weight bytes plus activation traffic (bf16 in, fp32 out) of one step."""
+
+        total = 0
+        for proj, (n, m) in self.shape.projections().items():
+            r = self.shape.rank(n, m)
+            total += layer_bytes(n, m, r) + self.tokens * (2 * n + 4 * m)
+        return total * len(self.blocks)
+
+    def step(self) -> torch.Tensor:
+        out = None
+        for block in self.blocks:
+            grouped_sm100_projection(self.inputs["hidden"], block.qkv)
+            self.backend.linear(self.inputs["attn"], block.o_proj)
+            grouped_sm100_projection(self.inputs["mlp"], block.gate_up)
+            out = self.backend.linear(self.inputs["act"], block.down_proj)
+        assert out is not None
+        return out
+
+    def capture(self) -> None:
+        """Record :meth:`step` into a CUDA graph (after one eager warm-up on a side stream)."""
+
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.graph_output = self.step()
+        self.graph = graph
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None or self.graph_output is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+        return self.graph_output

@@ -1,0 +1,91 @@
+"""Device-side layout-v1 helpers backed by ``libnqb.so``.
+
+``pack_signs_cuda`` / ``unpack_signs_cuda`` run layout-v1 packing on the GPU
+(the reference does it on the CPU: ``src/nanoquant/runtime/packed.py:170-218``);
+``decode_product_codebook_cuda`` expands a product-codebook right factor on the
+GPU (reference ``product_codebook.py:110-143``).  They exist so the bit-level
+work of the CUDA path can be checked bit-exactly against the host format code.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from nanoquant_b200 import _native
+from nanoquant_b200.packed import packed_word_count
+
+
+def _require_cuda(value: torch.Tensor, name: str) -> None:
+    if value.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not value.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def pack_signs_cuda(signs: torch.Tensor) -> torch.Tensor:
+    """+/-1 matrix on the GPU -> layout-v1 int32 words on the GPU."""
+
+    _require_cuda(signs, "signs")
+    if signs.ndim != 2:
+        raise ValueError("signs must be a matrix")
+    rows, cols = signs.shape
+    words = torch.empty((rows, packed_word_count(cols)), dtype=torch.int32, device=signs.device)
+    _native.call(
+        "nqb_pack_signs",
+        signs.data_ptr(),
+        _native.dtype_code(signs.dtype),
+        rows,
+        cols,
+        words.data_ptr(),
+        _native.current_stream_handle(signs.device),
+    )
+    return words
+
+
+def unpack_signs_cuda(words: torch.Tensor, rows: int, columns: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Layout-v1 words on the GPU -> (fp32 +/-1 matrix, count of rows with non-zero padding)."""
+
+    _require_cuda(words, "words")
+    if words.dtype != torch.int32 or tuple(words.shape) != (rows, packed_word_count(columns)):
+        raise ValueError("words must be int32 [rows, ceil(columns/32)]")
+    signs = torch.empty((rows, columns), dtype=torch.float32, device=words.device)
+    bad = torch.zeros((1,), dtype=torch.int32, device=words.device)
+    _native.call(
+        "nqb_unpack_signs",
+        words.data_ptr(),
+        rows,
+        columns,
+        signs.data_ptr(),
+        bad.data_ptr(),
+        _native.current_stream_handle(words.device),
+    )
+    return signs, bad
+
+
+def decode_product_codebook_cuda(
+    free_words: torch.Tensor,
+    payload: torch.Tensor,
+    first: torch.Tensor,
+    second: torch.Tensor,
+    *,
+    rank: int,
+    columns: int,
+) -> torch.Tensor:
+    """Product-codebook right factor on the GPU -> layout-v1 words [rank, ceil(columns/32)]."""
+
+    for name, value in (("free_words", free_words), ("payload", payload), ("first", first), ("second", second)):
+        _require_cuda(value, name)
+    out = torch.empty((rank, packed_word_count(columns)), dtype=torch.int32, device=free_words.device)
+    _native.call(
+        "nqb_decode_product_codebook",
+        free_words.data_ptr(),
+        free_words.shape[0],
+        rank,
+        columns,
+        payload.data_ptr(),
+        first.data_ptr(),
+        second.data_ptr(),
+        out.data_ptr(),
+        _native.current_stream_handle(free_words.device),
+    )
+    return out
