@@ -97,6 +97,13 @@ typedef struct nqb_linear_desc {
   const int32_t *codebook_payload;    /* 16-bit records, two per word       */
   const int16_t *codebook_first;      /* [256] bits 0..15 of a coded word   */
   const int16_t *codebook_second;     /* [256] bits 16..31 of a coded word  */
+
+  /* Optional kernel-native copies of U and V made by nqb_repack_signs
+   * (16-byte aligned).  When both are present and the token count is 1..16,
+   * the call runs on the tensor-core decode path; otherwise on the generic
+   * CUDA-core path.  Both paths give results within the same tolerance.     */
+  const void *left_tiles;  /* nqb_repack_signs(left_words,  m, r) */
+  const void *right_tiles; /* nqb_repack_signs(right_words, r, n) */
 } nqb_linear_desc;
 
 /* Library identity: NQB_ABI_VERSION of the loaded build. */
@@ -168,6 +175,34 @@ int nqb_unpack_signs(const int32_t *words, int64_t rows, int64_t cols, float *si
 int nqb_decode_product_codebook(const int32_t *free_words, int64_t free_rows, int64_t rank,
                                 int64_t columns, const int32_t *payload, const int16_t *first,
                                 const int16_t *second, int32_t *words_out, void *stream);
+
+/*
+ * Kernel-native copy of a layout-v1 sign matrix for the tensor-core path:
+ * rows are grouped in tiles of 128; within a tile, for every 4-word chunk of a
+ * row, the 128 rows' 16-byte chunks are stored consecutively; rows and chunks
+ * are zero-padded (to a multiple of 128 rows and of 8 words per row).
+ * The reference has no counterpart: it re-reads layout v1 in every kernel
+ * (cuda_kernels.py:65-162); preparing a device layout at load time follows its
+ * own prepare-time transform for mixed-V (cuda_backend.py:209-224).
+ */
+int nqb_repack_bytes(int64_t rows, int64_t cols, size_t *bytes);
+int nqb_repack_signs(const int32_t *words, int64_t rows, int64_t cols, void *tiles, void *stream);
+
+/*
+ * Which kernels a call with these arguments would run: *path is
+ * NQB_PATH_GENERIC (CUDA-core kernels) or NQB_PATH_TENSOR_CORE (tcgen05
+ * decode kernels).  Host-only; launches nothing.
+ */
+#define NQB_PATH_GENERIC 0
+#define NQB_PATH_TENSOR_CORE 1
+int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtype, int64_t tokens,
+                    int32_t *path);
+
+/*
+ * Reads and clears the device-side status word of the tensor-core kernels
+ * (NQB_ERR_TIMEOUT when a bounded wait gave up, else NQB_OK).  Synchronous.
+ */
+int nqb_device_status(int32_t *status);
 
 #ifdef __cplusplus
 }

@@ -24,6 +24,9 @@ NQB_ERR_WORKSPACE = 5
 NQB_ERR_UNSUPPORTED = 6
 NQB_ERR_TIMEOUT = 7
 
+NQB_PATH_GENERIC = 0
+NQB_PATH_TENSOR_CORE = 1
+
 NQB_F32 = 0
 NQB_F16 = 1
 NQB_BF16 = 2
@@ -73,6 +76,8 @@ class LinearDesc(ctypes.Structure):
         ("codebook_payload", _c_void_p),
         ("codebook_first", _c_void_p),
         ("codebook_second", _c_void_p),
+        ("left_tiles", _c_void_p),
+        ("right_tiles", _c_void_p),
     ]
 
 
@@ -110,6 +115,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "nqb_pack_signs": (ctypes.c_int, [_c_void_p, _i32, _i64, _i64, _c_void_p, _c_void_p]),
     "nqb_unpack_signs": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "nqb_repack_bytes": (ctypes.c_int, [_i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_repack_signs": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p]),
+    "nqb_device_status": (ctypes.c_int, [ctypes.POINTER(_i32)]),
+    "nqb_linear_path": (ctypes.c_int, [ctypes.POINTER(LinearDesc), _i32, _i32, _i64, ctypes.POINTER(_i32)]),
     "nqb_decode_product_codebook": (
         ctypes.c_int,
         [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],

@@ -1,6 +1,8 @@
 // C ABI of libnqb (declared in include/nqb.h): argument validation,
 // workspace accounting and dispatch to the kernels.
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "nqb_decode_tc.cuh"
 #include "nqb_generic.cuh"
@@ -27,6 +29,39 @@ int cuda_status(cudaError_t err, const char *what) {
 }
 
 static bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int ensure_dynamic_smem(const void *kernel, size_t bytes) {
+  struct Entry {
+    const void *kernel;
+    int device;
+    size_t bytes;
+  };
+  static std::mutex lock;
+  static std::vector<Entry> entries;
+  // static shared memory counts against the same 48 KB default, so any
+  // non-zero dynamic size gets the attribute
+  if (bytes == 0) return NQB_OK;
+  int device = 0;
+  NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  std::lock_guard<std::mutex> guard(lock);
+  for (Entry &e : entries) {
+    if (e.kernel == kernel && e.device == device) {
+      if (e.bytes >= bytes) return NQB_OK;
+      NQB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+               "cudaFuncSetAttribute");
+      e.bytes = bytes;
+      return NQB_OK;
+    }
+  }
+  int optin = 0;
+  NQB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device), "cudaDeviceGetAttribute");
+  if (bytes > static_cast<size_t>(optin))
+    return fail(NQB_ERR_UNSUPPORTED, "kernel needs %zu B of shared memory, device allows %d", bytes, optin);
+  NQB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+           "cudaFuncSetAttribute");
+  entries.push_back({kernel, device, bytes});
+  return NQB_OK;
+}
 
 // Checks one layer descriptor; `name` prefixes messages for grouped calls.
 static int validate_layer(const nqb_linear_desc *d, const char *name) {
@@ -308,6 +343,36 @@ int nqb_unpack_signs(const int32_t *words, int64_t rows, int64_t cols, float *si
   if (rows <= 0 || cols <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "sign matrix dimensions must be positive");
   NQB_CHECK(launch_unpack(reinterpret_cast<const uint32_t *>(words), rows, cols, signs, bad_padding_rows,
                           reinterpret_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int nqb_repack_bytes(int64_t rows, int64_t cols, size_t *bytes) {
+  if (rows <= 0 || cols <= 0 || bytes == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "repack needs positive dimensions and an output pointer");
+  *bytes = repack_bytes(rows, cols);
+  return ok();
+}
+
+int nqb_repack_signs(const int32_t *words, int64_t rows, int64_t cols, void *tiles, void *stream) {
+  if (words == nullptr || tiles == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "repack operand is NULL");
+  if (rows <= 0 || cols <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "sign matrix dimensions must be positive");
+  if (!aligned(tiles, 16) || !aligned(words, 4)) return fail(NQB_ERR_ALIGNMENT, "repack buffers are misaligned");
+  NQB_CHECK(launch_repack(reinterpret_cast<const uint32_t *>(words), rows, cols, static_cast<uint32_t *>(tiles),
+                          reinterpret_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtype, int64_t tokens, int32_t *path) {
+  if (layers == nullptr || count < 1 || count > kMaxMembers || path == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "path query takes 1 to %d layers and an output pointer", kMaxMembers);
+  for (int i = 0; i < count; ++i) NQB_CHECK(validate_layer(layers + i, "layer"));
+  *path = tc_eligible(layers, count, x_dtype, tokens) ? NQB_PATH_TENSOR_CORE : NQB_PATH_GENERIC;
+  return ok();
+}
+
+int nqb_device_status(int32_t *status) {
+  if (status == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "status is NULL");
+  NQB_CHECK(tc_device_error(status));
   return ok();
 }
 

@@ -35,6 +35,11 @@ int cuda_status(cudaError_t err, const char *what);
     if (_nqb_err != cudaSuccess) return ::nqb::cuda_status(_nqb_err, what);    \
   } while (0)
 
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute is set once per (kernel, device, size
+// increase), so calls made during CUDA-graph capture do not touch it again.
+int ensure_dynamic_smem(const void *kernel, size_t bytes);
+
 inline bool is_float_dtype(int32_t dt) { return dt == NQB_F32 || dt == NQB_F16 || dt == NQB_BF16; }
 inline size_t dtype_size(int32_t dt) {
   switch (dt) {

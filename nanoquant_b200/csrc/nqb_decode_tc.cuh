@@ -5,6 +5,8 @@
 
 namespace nqb {
 
+constexpr int kMaxMembersTc = 3;
+
 // True when the tcgen05 path takes this call (shapes, dtypes, token count).
 bool tc_eligible(const nqb_linear_desc *layers, int count, int32_t x_dtype, int64_t tokens);
 // Extra workspace (beyond the fp32 latent) the tcgen05 path needs; 0 if not eligible.
@@ -12,5 +14,12 @@ size_t tc_extra_workspace_bytes(const nqb_linear_desc *layers, int count, int64_
 // Runs 1..3 layers sharing x through the tcgen05 kernels.
 int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
            float *const *ys, void *extra, size_t extra_bytes, float *latent, cudaStream_t stream);
+
+// Row-interleaved tile copy of a sign matrix (see nqb_repack_signs).
+int32_t repack_chunks(int64_t columns);
+size_t repack_bytes(int64_t rows, int64_t columns);
+int launch_repack(const uint32_t *words, int64_t rows, int64_t columns, uint32_t *tiles, cudaStream_t stream);
+// Reads and clears the tensor-core kernels' device status word.
+int tc_device_error(int32_t *out);
 
 }  // namespace nqb

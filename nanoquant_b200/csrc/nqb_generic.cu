@@ -250,21 +250,7 @@ __global__ void decode_codebook_kernel(const uint32_t *free_words, int64_t free_
 
 // --------------------------------------------------------------- launch ---
 
-static int set_smem(const void *fn, size_t bytes) {
-  if (bytes <= 48 * 1024) return NQB_OK;
-  int device = 0;
-  NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
-  int optin = 0;
-  NQB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device),
-           "cudaDeviceGetAttribute");
-  if (bytes > static_cast<size_t>(optin))
-    return fail(NQB_ERR_UNSUPPORTED, "generic kernel needs %zu B of shared memory, device allows %d",
-                bytes, optin);
-  NQB_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(bytes)),
-           "cudaFuncSetAttribute");
-  return NQB_OK;
-}
+static int set_smem(const void *fn, size_t bytes) { return ensure_dynamic_smem(fn, bytes); }
 
 int choose_tok_tile(int64_t tokens, int64_t width) {
   // keep the staged activations under ~96 KB so two blocks fit per SM

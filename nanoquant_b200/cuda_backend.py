@@ -56,10 +56,22 @@ def _to_device(value: torch.Tensor | None, device: torch.device) -> torch.Tensor
     return None if value is None else value.detach().to(device=device).contiguous()
 
 
+def _repack(words: torch.Tensor, rows: int, columns: int) -> torch.Tensor:
+    """Kernel-native tile copy of a layout-v1 sign matrix (``nqb_repack_signs``)."""
+
+    size = ctypes.c_size_t(0)
+    _native.call("nqb_repack_bytes", rows, columns, ctypes.byref(size))
+    tiles = torch.empty(size.value, dtype=torch.uint8, device=words.device)
+    _native.call("nqb_repack_signs", words.data_ptr(), rows, columns, tiles.data_ptr(),
+                 _native.current_stream_handle(words.device))
+    return tiles
+
+
 def _build_payload(
     state: PackedLayerState | ProductCodebookLayerState,
     overlay: OutlierRowOverlay | None,
     device: torch.device,
+    tensor_cores: bool = True,
 ) -> _Sm100Payload:
     spec = state.spec
     tensors: dict[str, torch.Tensor] = {}
@@ -95,6 +107,11 @@ def _build_payload(
         bias = packed.bias
         patch_left = keep("patch_left", packed.patch_left)
         patch_right = keep("patch_right", packed.patch_right)
+        if tensor_cores:
+            tensors["left_tiles"] = _repack(tensors["left_words"], spec.out_features, spec.rank)
+            tensors["right_tiles"] = _repack(tensors["right_words"], spec.rank, spec.in_features)
+            desc.left_tiles = tensors["left_tiles"].data_ptr()
+            desc.right_tiles = tensors["right_tiles"].data_ptr()
     desc.scale_pre = keep("scale_pre", scale_pre).data_ptr()
     desc.scale_mid = keep("scale_mid", scale_mid).data_ptr()
     desc.scale_post = keep("scale_post", scale_post).data_ptr()
@@ -151,6 +168,17 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+def kernel_path(layer: PreparedLayer, tokens: int, input_dtype: torch.dtype = torch.bfloat16) -> str:
+    """Which kernels ``linear`` runs for ``tokens`` tokens: ``"tensor-core"`` or ``"generic"``."""
+
+    if not isinstance(layer.payload, _Sm100Payload):
+        raise TypeError("prepared runtime layer has an invalid sm100a packed payload")
+    path = ctypes.c_int32(-1)
+    _native.call("nqb_linear_path", ctypes.byref(layer.payload.desc), 1, _native.dtype_code(input_dtype), tokens,
+                 ctypes.byref(path))
+    return "tensor-core" if path.value == _native.NQB_PATH_TENSOR_CORE else "generic"
+
+
 def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLinearSpec) -> torch.Tensor:
     """Run one prepared layer on ``value`` (any leading shape) and return fp32 ``[..., out]``."""
 
@@ -201,6 +229,11 @@ class CudaPackedSm100Backend:
     version = CUDA_SM100_BACKEND_VERSION
     packed_layout = PACKED_LAYOUT_VERSION
 
+    def __init__(self, *, tensor_cores: bool = True) -> None:
+        # tensor_cores=False keeps prepared layers on the CUDA-core kernels only
+        # (no kernel-native tile copies); used to cross-check the two paths.
+        self.tensor_cores = tensor_cores
+
     def capabilities(self) -> BackendCapabilities:
         return BackendCapabilities(
             logical_formats=("nanoquant-v1",),
@@ -246,7 +279,8 @@ class CudaPackedSm100Backend:
             )
         target = _cuda_device(device)
         _native.library()
-        payload = _build_payload(base, overlay, target)
+        with torch.cuda.device(target):
+            payload = _build_payload(base, overlay, target, self.tensor_cores)
         return PreparedLayer(self.name, self.version, state.spec, payload)
 
     def linear(self, value: torch.Tensor, layer: PreparedLayer) -> torch.Tensor:
@@ -345,6 +379,7 @@ __all__ = [
     "Sm100ProjectionGroup",
     "grouped_cuda_projection",
     "grouped_sm100_projection",
+    "kernel_path",
     "packed_linear",
     "prepare_cuda_projection_group",
     "prepare_sm100_projection_group",

@@ -146,14 +146,16 @@ def _codebook_state(fixture: dict, tag: str) -> ProductCodebookLayerState:
 def test_product_codebook_matches_reference_and_expanded_layer(tag: str) -> None:
     fixture = load("product_codebook")
     state = _codebook_state(fixture, tag)
-    backend = CudaPackedSm100Backend()
-    compact = backend.prepare(state, "cuda")
-    expanded = backend.prepare(state.to_packed(), "cuda")
     x = fixture[f"{tag}_x"].cuda()
-    compact_out = backend.linear(x, compact)
-    expanded_out = backend.linear(x, expanded)
+    # same kernels on the compact and the decoded layer: bitwise equal
+    generic = CudaPackedSm100Backend(tensor_cores=False)
+    compact_out = generic.linear(x, generic.prepare(state, "cuda"))
+    expanded_out = generic.linear(x, generic.prepare(state.to_packed(), "cuda"))
     assert torch.equal(compact_out, expanded_out)
     torch.testing.assert_close(compact_out.cpu(), fixture[f"{tag}_y"], rtol=RTOL, atol=ATOL)
+    backend = CudaPackedSm100Backend()
+    default_out = backend.linear(x, backend.prepare(state, "cuda"))
+    torch.testing.assert_close(default_out.cpu(), fixture[f"{tag}_y"], rtol=RTOL, atol=ATOL)
 
 
 def test_device_codebook_decode_is_bit_exact() -> None:
@@ -282,3 +284,54 @@ def test_cuda_graph_replay_matches_eager() -> None:
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(captured, eager)
+
+
+# ------------------------------------------------------------------ tensor-core decode path ---
+
+@pytest.mark.parametrize("tokens", (1, 3, 6, 11, 16))
+@pytest.mark.parametrize(("n", "m", "r"), ((35, 17, 33), (640, 2048, 480), (1152, 1024, 542), (4096, 1024, 819),
+                                           (6912, 1152, 987)))
+def test_tensor_core_path_matches_generic_and_oracle(n: int, m: int, r: int, tokens: int) -> None:
+    from nanoquant_b200.cuda_backend import kernel_path
+
+    state = _random_state(n, m, r, seed=3 * n + m + tokens, outliers=3, bias=True)
+    fast = CudaPackedSm100Backend()
+    slow = CudaPackedSm100Backend(tensor_cores=False)
+    fast_layer = fast.prepare(state, "cuda")
+    slow_layer = slow.prepare(state, "cuda")
+    assert kernel_path(fast_layer, tokens) == "tensor-core"
+    assert kernel_path(slow_layer, tokens) == "generic"
+    g = torch.Generator().manual_seed(tokens)
+    x = torch.randn(tokens, n, generator=g).bfloat16()
+    got = fast.linear(x.cuda(), fast_layer)
+    reference = slow.linear(x.cuda(), slow_layer)
+    expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
+    scale = float(np.abs(expected).max())
+    np.testing.assert_allclose(got.cpu().numpy(), expected, rtol=RTOL, atol=max(ATOL, 1e-5 * scale))
+    np.testing.assert_allclose(got.cpu().numpy(), reference.cpu().numpy(), rtol=RTOL, atol=max(ATOL, 1e-5 * scale))
+    assert torch.equal(got, fast.linear(x.cuda(), fast_layer))
+    status = ctypes_status()
+    assert status == 0
+
+
+def ctypes_status() -> int:
+    import ctypes
+
+    from nanoquant_b200 import _native
+
+    value = ctypes.c_int32(-1)
+    _native.call("nqb_device_status", ctypes.byref(value))
+    return value.value
+
+
+def test_tensor_core_grouped_projection_matches_members() -> None:
+    backend = CudaPackedSm100Backend()
+    states = [_random_state(4096, width, rank, seed=90 + i) for i, (width, rank) in
+              enumerate(((4096, 2048), (1024, 819), (1024, 819)))]
+    prepared = tuple(backend.prepare(state, "cuda") for state in states)
+    group = prepare_sm100_projection_group(prepared)
+    x = torch.randn(2, 4096, device="cuda").bfloat16()
+    outs = grouped_sm100_projection(x, group)
+    for out, state in zip(outs, states, strict=True):
+        expected = po.packed_linear(x.float().cpu().numpy(), oracle_from_state(state), accumulate="float64")
+        np.testing.assert_allclose(out.cpu().numpy(), expected, rtol=RTOL, atol=1e-5 * np.abs(expected).max())
