@@ -130,6 +130,25 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
                float *y, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * nqb_linear without a workspace argument, for callers that cannot allocate
+ * device memory: plugins running inside another engine's executor or
+ * processes with a fixed device-memory plan, where a cudaMalloc would bypass
+ * the host's accounting or break its stream capture.  No counterpart in the
+ * reference.
+ *
+ * Scratch comes from a static 8 MiB array in the library's device image (held
+ * on every GPU that loads the library until exit).  Calls whose workspace
+ * (nqb_linear_workspace_bytes) exceeds 8 MiB are rejected with
+ * NQB_ERR_WORKSPACE and launch nothing.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress, with that device current);
+ * make that first call before any stream capture.  All calls on a device share
+ * the one array, so calls that may overlap on the GPU (different streams, or
+ * concurrent graph replays) race: serialise them.  Allocates nothing.
+ */
+int nqb_linear_noalloc(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int64_t tokens,
+                       float *y, void *stream);
+
+/*
  * Two or three layers that share one input x, executed as one stage-1 and
  * one stage-2 launch.  y_out[i] is [tokens, layers[i].out_features] fp32.
  * Replaces launch_grouped_packed_linears (reference cuda_kernels.py:301-374);

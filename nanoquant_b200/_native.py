@@ -90,6 +90,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [ctypes.POINTER(LinearDesc), _c_void_p, _i32, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p],
     ),
+    "nqb_linear_noalloc": (
+        ctypes.c_int,
+        [ctypes.POINTER(LinearDesc), _c_void_p, _i32, _i64, _c_void_p, _c_void_p],
+    ),
     "nqb_grouped_workspace_bytes": (
         ctypes.c_int,
         [ctypes.POINTER(LinearDesc), _i32, _i64, ctypes.POINTER(ctypes.c_size_t)],
