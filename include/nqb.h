@@ -114,8 +114,11 @@ const char *nqb_last_error(void);
 
 /*
  * Bytes of device workspace nqb_linear needs for `tokens` tokens.
- * The workspace is scratch owned by the caller; it holds no state between
- * calls and must not be shared by calls that may run concurrently.
+ * The workspace is scratch owned by the caller (256-byte aligned).  Its first
+ * 16 KiB hold completion counters: zero-fill the workspace once before its
+ * first use; every call leaves that region zero again, so one workspace
+ * serves any sequence of calls (of any layer and token count) on one stream.
+ * It must not be shared by calls that may run concurrently.
  */
 int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, size_t *bytes);
 

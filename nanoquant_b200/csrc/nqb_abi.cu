@@ -128,6 +128,12 @@ static size_t latent_bytes(int64_t tokens, int64_t total_rank) {
   return align_up(static_cast<size_t>(tokens) * total_rank * sizeof(float), 256);
 }
 
+// Workspace layout shared by every call: [completion counters][latent][tensor-core partials].
+// The counter region has a fixed size and offset, so one workspace can serve
+// calls of any shape in sequence; it must be zero before its first use and
+// every call leaves it zero.
+static size_t workspace_bytes(size_t latent, size_t tc_partials) { return kCounterRegionBytes + latent + tc_partials; }
+
 static void fill_stage1_member(Stage1Member &m, const nqb_linear_desc &d, int64_t latent_offset,
                                int32_t block_begin) {
   m.words = reinterpret_cast<const uint32_t *>(d.right_words);
@@ -237,7 +243,7 @@ int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, siz
   NQB_CHECK(validate_layer(layer, "layer"));
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
   if (tokens <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "token count must be positive");
-  *bytes = latent_bytes(tokens, layer->rank) + tc_extra_workspace_bytes(layer, 1, tokens);
+  *bytes = workspace_bytes(latent_bytes(tokens, layer->rank), tc_extra_workspace_bytes(layer, 1, tokens));
   return ok();
 }
 
@@ -248,13 +254,16 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
   if (y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output y is NULL");
   const size_t need = latent_bytes(tokens, layer->rank);
   const size_t tc_need = tc_extra_workspace_bytes(layer, 1, tokens);
-  if (workspace == nullptr || workspace_bytes < need + tc_need || !aligned(workspace, 256))
-    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu", need + tc_need,
-                workspace_bytes);
+  if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
+    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
+                nqb::workspace_bytes(need, tc_need), workspace_bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  float *latent = static_cast<float *>(workspace);
+  char *base = static_cast<char *>(workspace);
+  int32_t *counters = reinterpret_cast<int32_t *>(base);
+  float *latent = reinterpret_cast<float *>(base + kCounterRegionBytes);
   if (tc_eligible(layer, 1, x_dtype, tokens)) {
-    NQB_CHECK(run_tc(layer, 1, x, x_dtype, tokens, &y, static_cast<char *>(workspace) + need, tc_need, latent, s));
+    NQB_CHECK(run_tc(layer, 1, x, x_dtype, tokens, &y, counters, base + kCounterRegionBytes + need, tc_need, latent,
+                     s));
     return ok();
   }
   float *ys[1] = {y};
@@ -272,7 +281,7 @@ int nqb_grouped_workspace_bytes(const nqb_linear_desc *layers, int32_t count, in
     NQB_CHECK(validate_layer(layers + i, "grouped member"));
     total_rank += layers[i].rank;
   }
-  *bytes = latent_bytes(tokens, total_rank) + tc_extra_workspace_bytes(layers, count, tokens);
+  *bytes = workspace_bytes(latent_bytes(tokens, total_rank), tc_extra_workspace_bytes(layers, count, tokens));
   return ok();
 }
 
@@ -295,13 +304,15 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   const size_t need = latent_bytes(tokens, total_rank);
   const size_t tc_need = tc_extra_workspace_bytes(layers, count, tokens);
-  if (workspace == nullptr || workspace_bytes < need + tc_need || !aligned(workspace, 256))
-    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu", need + tc_need,
-                workspace_bytes);
+  if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
+    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
+                nqb::workspace_bytes(need, tc_need), workspace_bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  float *latent = static_cast<float *>(workspace);
+  char *base = static_cast<char *>(workspace);
+  int32_t *counters = reinterpret_cast<int32_t *>(base);
+  float *latent = reinterpret_cast<float *>(base + kCounterRegionBytes);
   if (tc_eligible(layers, count, x_dtype, tokens)) {
-    NQB_CHECK(run_tc(layers, count, x, x_dtype, tokens, y_out, static_cast<char *>(workspace) + need, tc_need,
+    NQB_CHECK(run_tc(layers, count, x, x_dtype, tokens, y_out, counters, base + kCounterRegionBytes + need, tc_need,
                      latent, s));
     return ok();
   }

@@ -22,15 +22,20 @@
 //
 // The sign words arrive in a row-interleaved tile layout made at prepare time
 // (nqb_repack_signs): per 128-row tile and per 4-word chunk, the 128 rows'
-// 16-byte chunks are contiguous, so one CTA's whole K-slice is one contiguous
-// block that a single bulk copy (cp.async.bulk) brings into shared memory.
+// 16-byte chunks are contiguous, so one CTA's K-slice is one contiguous block
+// that bulk copies (cp.async.bulk) bring into shared memory.
+//
+// Kernels are launched with programmatic dependent launch: everything that
+// does not read the previous kernel's output (mbarrier set-up, the bulk copies
+// of the sign tiles, TMEM allocation, clearing the B image) runs before
+// griddepcontrol.wait, overlapping the previous kernel's tail.
 //
 // Integer accumulation is exact, so the only rounding is the 22-bit
 // quantisation of the activations and the final conversion to fp32; results
-// are deterministic.  Stage 1 writes per-K-split fp32 partials; stage 2 reads
-// them in a fixed order (times scale_mid) as its activations and the last CTA
-// of each output tile reduces its partials, applies scale_post, salient
-// columns, the int8 row overlay and bias, and writes y.
+// are deterministic.  Each stage writes per-K-split fp32 partials; the last
+// CTA of every row tile (atomic counter) reduces them in a fixed order:
+// stage 1 into the latent (times scale_mid), stage 2 into y (times
+// scale_post, plus salient columns, the int8 row overlay and bias).
 #include <cstring>
 
 #include "nqb_decode_tc.cuh"
@@ -50,9 +55,12 @@ constexpr int kAStageCols = 64;     // TMEM columns of A per stage
 constexpr int kDCol = 2 * kAStageCols;  // first accumulator column
 constexpr int kMaxTokens = 16;
 constexpr int kMaxStagesPerCta = 8;  // <= 2048 input columns per CTA
+constexpr int kQuadsPerThread = kMaxStagesPerCta * 64 / kThreads;
 constexpr int kDigits = 3;
 constexpr int kMaxNPad = 48;
 constexpr uint32_t kSpinLimit = 1u << 28;
+
+__host__ __device__ constexpr int n_pad_for(int tokens) { return ((kDigits * tokens + 15) / 16) * 16; }
 
 struct Member {
   const uint4 *tiles;    // row-interleaved tiles of the sign matrix
@@ -64,10 +72,11 @@ struct Member {
   int32_t stages_per_split;
   int32_t cta_begin;
   int64_t k_valid;       // valid K columns (in_features, or rank for stage 2)
-  const void *pre;       // stage 1 activation scale
-  const void *mid;       // stage 2: latent scale
+  const void *pre;       // stage 1: activation scale
+  const void *mid;       // stage 1: latent scale, applied by the reducing CTA
   int64_t act_offset;    // stage 2: first latent column of this member
-  int64_t out_offset;    // first row of this member in the partial buffer
+  int64_t out_offset;    // first row of this member in the partial / latent buffers
+  int32_t *counters;     // [row_tiles], zero on entry, left zero
   // stage 2 epilogue
   const void *post;
   const void *bias;
@@ -83,7 +92,6 @@ struct Member {
   const void *overlay_scales;
   int32_t overlay_scale_dtype;
   float *y;
-  int32_t *counters;  // [row_tiles]
 };
 
 struct Params {
@@ -96,61 +104,138 @@ struct Params {
   int32_t tokens;
   int32_t n_pad;       // MMA N
   uint32_t tmem_cols;
-  float *partial;      // this stage's output partials [splits][tokens][part_stride]
+  float *partial;      // this stage's K-split partials [splits][tokens][part_stride]
   int64_t part_stride;
-  const float *act_partial;  // stage 2: stage-1 partials [s1_splits][tokens][act_stride]
-  int32_t act_splits;
-  int64_t act_stride;
+  float *latent;       // [tokens][latent_stride]: written by stage 1, read by stage 2
+  int64_t latent_stride;
 };
 
 __device__ int g_tc_error;  // first bounded-wait failure (0 = none), for diagnostics
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_tc_error, 0, code); }
 
-// Value of activation column k (CTA-relative K range already applied) of token t.
-template <bool kStage2>
-__device__ __forceinline__ float activation(const Params &p, const Member &m, int t, int64_t k) {
-  if (k >= m.k_valid) return 0.0f;
-  if constexpr (!kStage2) {
-    return load_as_float(p.x, static_cast<int64_t>(t) * p.n + k, p.x_dtype) *
-           load_as_float(m.pre, k, p.scale_dtype);
-  } else {
-    float sum = 0.0f;
-    const float *src = p.act_partial + static_cast<int64_t>(t) * p.act_stride + m.act_offset + k;
-    for (int s = 0; s < p.act_splits; ++s)
-      sum += __ldcg(src + static_cast<int64_t>(s) * p.tokens * p.act_stride);
-    return sum * load_as_float(m.mid, k, p.scale_dtype);
-  }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t pack_digit_bytes(const int32_t (&q)[4], int digit) {
-  uint32_t out = 0;
+// Splits four fixed-point values into three signed base-256 digits each
+// (q = d0 + 256*d1 + 65536*d2, every digit in [-128, 127]) and packs digit k
+// of the four values, one byte per value, into w[k].
+__device__ __forceinline__ void split_digits(const int32_t (&q)[4], uint32_t (&w)[kDigits]) {
+  w[0] = w[1] = w[2] = 0;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     int32_t v = q[b];
-    int32_t d = 0;
-    for (int i = 0; i <= digit; ++i) {
-      d = static_cast<int8_t>(v & 0xFF);
-      v = (v - d) >> 8;
-    }
-    out |= (static_cast<uint32_t>(d) & 0xFFu) << (8 * b);
+    const int32_t d0 = static_cast<int8_t>(v & 0xFF);
+    v = (v - d0) >> 8;
+    const int32_t d1 = static_cast<int8_t>(v & 0xFF);
+    const int32_t d2 = (v - d1) >> 8;
+    w[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * b);
+    w[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * b);
+    w[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * b);
   }
-  return out;
+}
+
+// Input column of byte b of quad (stage sl, word i, bit class j, nibble s).
+__device__ __forceinline__ int quad_column(int sl, int i, int j, int s, int b) {
+  return sl * kStageCols + 32 * i + 8 * b + j + 4 * s;
+}
+
+// 2^e as a float, exactly, for e in [-126, 127].
+__device__ __forceinline__ float exp2_int(int e) { return __int_as_float((e + 127) << 23); }
+
+// Copies this CTA's K slice [k0, k0 + ncols) of the activations of every
+// token into shared memory as fp32 (zero past the valid columns): stage 1
+// x * pre, stage 2 the latent.  The dtype dispatch sits outside the loop and
+// each thread keeps 16 loads in flight before it stores any of them.
+constexpr int kStageBatch = 16;
+
+template <typename XT, typename ST>
+__device__ __forceinline__ void stage_input_slice(const XT *x, const ST *pre, int64_t n, int64_t k0, int ncols,
+                                                  int tokens, int64_t k_valid, float *out) {
+  const int total = tokens * ncols;
+  for (int base = threadIdx.x; base < total; base += kStageBatch * kThreads) {
+    float xv[kStageBatch], pv[kStageBatch];
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = base + u * kThreads;
+      xv[u] = 0.0f;
+      pv[u] = 0.0f;
+      if (i < total) {
+        const int t = i / ncols;
+        const int64_t col = k0 + (i - t * ncols);
+        if (col < k_valid) {
+          xv[u] = to_f32(x[static_cast<int64_t>(t) * n + col]);
+          pv[u] = to_f32(pre[col]);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStageBatch; ++u) {
+      const int i = base + u * kThreads;
+      if (i < total) out[i] = xv[u] * pv[u];
+    }
+  }
+}
+
+template <typename XT>
+__device__ __forceinline__ void stage_input_slice_x(const Params &p, const Member &m, int64_t k0, int ncols,
+                                                    float *out) {
+  const XT *x = static_cast<const XT *>(p.x);
+  switch (p.scale_dtype) {
+    case NQB_F32: stage_input_slice(x, static_cast<const float *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
+    case NQB_F16: stage_input_slice(x, static_cast<const __half *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
+    default: stage_input_slice(x, static_cast<const __nv_bfloat16 *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
+  }
 }
 
 template <bool kStage2>
+__device__ __forceinline__ void stage_activations(const Params &p, const Member &m, int64_t k0, int ncols,
+                                                  float *out) {
+  if constexpr (kStage2) {
+    const int total = p.tokens * ncols;
+    for (int base = threadIdx.x; base < total; base += kStageBatch * kThreads) {
+      float v[kStageBatch];
+#pragma unroll
+      for (int u = 0; u < kStageBatch; ++u) {
+        const int i = base + u * kThreads;
+        v[u] = 0.0f;
+        if (i < total) {
+          const int t = i / ncols;
+          const int64_t col = k0 + (i - t * ncols);
+          if (col < m.k_valid)
+            v[u] = __ldcg(p.latent + static_cast<int64_t>(t) * p.latent_stride + m.act_offset + col);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStageBatch; ++u) {
+        const int i = base + u * kThreads;
+        if (i < total) out[i] = v[u];
+      }
+    }
+  } else {
+    switch (p.x_dtype) {
+      case NQB_F32: stage_input_slice_x<float>(p, m, k0, ncols, out); break;
+      case NQB_F16: stage_input_slice_x<__half>(p, m, k0, ncols, out); break;
+      default: stage_input_slice_x<__nv_bfloat16>(p, m, k0, ncols, out); break;
+    }
+  }
+}
+
+template <bool kStage2, int kT>
 __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
+  constexpr int kNP = n_pad_for(kT);  // MMA N: 3 digit columns per token, multiple of 16
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint64_t s_bar_a[2];                    // A buffer b free again
   __shared__ uint64_t s_bar_done;                    // all MMAs complete
   __shared__ uint64_t s_bar_w[kMaxStagesPerCta];     // stage weights landed
   __shared__ uint32_t s_tmem;
-  __shared__ int s_exp[kMaxTokens];
-  __shared__ long long s_qsum[kMaxTokens];
-  __shared__ float s_warp_max[4][kMaxTokens];
-  __shared__ long long s_warp_q[4];
+  __shared__ int s_exp[kT];
+  __shared__ long long s_qsum[kT];
+  __shared__ float s_red_f[4 * kT];
+  __shared__ long long s_red_q[4 * kT];
   __shared__ int s_last;
-  __shared__ int s_failed;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -167,14 +252,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   const int st_end = min(st_begin + m.stages_per_split, m.k_stages);
   const int nst = st_end - st_begin;
   const int T = p.tokens;
-  const int NP = p.n_pad;
+  constexpr int NP = kNP;
   const uint32_t b_block = 32u * NP;  // bytes of one (stage, class, half) B block
 
   uint8_t *smem_w = smem;                                   // nst * 4 KB weights
   uint8_t *smem_b = smem + nst * kStageWeightBytes;         // nst * 8 * b_block digits
 
+  // ---- prologue: nothing here reads the previous kernel's output ----------
   if (tid == 0) {
-    s_failed = 0;
     ptx::mbar_init(&s_bar_a[0], 1);
     ptx::mbar_init(&s_bar_a[1], 1);
     ptx::mbar_init(&s_bar_done, 1);
@@ -182,9 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
     ptx::fence_mbar_init();
   }
   __syncthreads();
-
-  // 1. start streaming this CTA's sign words: one bulk copy per stage
   if (tid == 0) {
+    // stream this CTA's sign words: one bulk copy per 256-column stage
     const uint8_t *src = reinterpret_cast<const uint8_t *>(m.tiles) +
                          (static_cast<size_t>(tile) * m.wc + 2 * st_begin) * (kTileRows * kChunkBytes);
     for (int s = 0; s < nst; ++s) {
@@ -198,12 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
           : "memory");
     }
   }
-  // 2. tensor memory
   if (warp == 0) {
     ptx::tmem_alloc(&s_tmem, p.tmem_cols);
     ptx::tmem_relinquish();
   }
-  // 3. clear the B image (unused N rows and K positions must be zero)
   {
     uint4 *b4 = reinterpret_cast<uint4 *>(smem_b);
     const int count = nst * 8 * static_cast<int>(b_block) / 16;
@@ -213,77 +295,104 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = s_tmem;
+  allow_dependent_launch();
+  grid_dependency_wait();
 
-  // 4. quantise this K slice of the activations into the B image
+  // ---- quantise this K slice of the activations into the B image ---------
   const int64_t k0 = static_cast<int64_t>(st_begin) * kStageCols;
-  const int ncols = nst * kStageCols;
   {
-    float mx[kMaxTokens];
+    const int ncols = nst * kStageCols;
+    const int nquads = nst * 64;
+    float *s_act = reinterpret_cast<float *>(smem_b + nst * 8 * b_block);  // [T][ncols] fp32
+    stage_activations<kStage2>(p, m, k0, ncols, s_act);
+    __syncthreads();
+    // per-token maximum over the slice -> power-of-two scale 2^e
+    float mx[kT];
 #pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) mx[t] = 0.0f;
+    for (int t = 0; t < kT; ++t) mx[t] = 0.0f;
     for (int c = tid; c < ncols; c += kThreads) {
 #pragma unroll
-      for (int t = 0; t < kMaxTokens; ++t)
-        if (t < T) mx[t] = fmaxf(mx[t], fabsf(activation<kStage2>(p, m, t, k0 + c)));
+      for (int t = 0; t < kT; ++t)
+        if (t < T) mx[t] = fmaxf(mx[t], fabsf(s_act[t * ncols + c]));
     }
 #pragma unroll
-    for (int t = 0; t < kMaxTokens; ++t) {
-      float v = mx[t];
+    for (int t = 0; t < kT; ++t) {
+      if (t < T) {
+        float v = mx[t];
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-      if (lane == 0) s_warp_max[warp][t] = v;
+        for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) s_red_f[warp * kT + t] = v;
+      }
     }
     __syncthreads();
     if (tid < T) {
-      const float v = fmaxf(fmaxf(s_warp_max[0][tid], s_warp_max[1][tid]), fmaxf(s_warp_max[2][tid], s_warp_max[3][tid]));
+      const float v = fmaxf(fmaxf(s_red_f[tid], s_red_f[kT + tid]),
+                            fmaxf(s_red_f[2 * kT + tid], s_red_f[3 * kT + tid]));
       int e = 0;
       if (v > 0.0f && isfinite(v)) {
         int ex;
-        frexpf(v, &ex);  // v < 2^ex
-        e = 22 - ex;     // |a * 2^e| < 2^22
+        frexpf(v, &ex);      // v < 2^ex
+        e = 22 - ex;         // |a * 2^e| < 2^22
+        e = min(e, 126);     // keep 2^e and 2^-e normal floats (only |a| < 2^-104 loses bits)
       }
       s_exp[tid] = e;
     }
     __syncthreads();
-
-    const int nquads = nst * 64;
-    for (int t = 0; t < T; ++t) {
-      const int e = s_exp[t];
-      long long qsum = 0;
-      for (int qd = tid; qd < nquads; qd += kThreads) {
+    // quantise, split into digits, scatter into the MMA's K order
+    long long qsum[kT];
+#pragma unroll
+    for (int t = 0; t < kT; ++t) qsum[t] = 0;
+#pragma unroll
+    for (int i = 0; i < kQuadsPerThread; ++i) {
+      const int qd = tid + i * kThreads;
+      if (qd < nquads) {
         const int sl = qd >> 6;
         const int r = qd & 63;
-        const int i = r >> 3;        // word in stage
-        const int j = (r >> 1) & 3;  // bit class
-        const int s = r & 1;         // low / high nibble
-        int32_t q[4];
+        const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
+        const uint32_t block = (static_cast<uint32_t>(sl) * 4 + j) * 2 + (wi >> 2);
+        const uint32_t pk = 4 * ((wi & 3) * 2 + s);  // first K position of the quad in its MMA
+        const int c0 = quad_column(sl, wi, j, s, 0);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int64_t col = k0 + sl * kStageCols + 32 * i + 8 * b + j + 4 * s;
-          q[b] = __float2int_rn(ldexpf(activation<kStage2>(p, m, t, col), e));
-          qsum += q[b];
-        }
-        const uint32_t block = (static_cast<uint32_t>(sl) * 4 + j) * 2 + (i >> 2);
-        const uint32_t pk = 4 * ((i & 3) * 2 + s);  // first K position of the quad in its MMA
+        for (int t = 0; t < kT; ++t) {
+          if (t < T) {
+            const float scale = exp2_int(s_exp[t]);  // exact power of two
+            int32_t q[4];
 #pragma unroll
-        for (int d = 0; d < kDigits; ++d) {
-          const uint32_t nrow = 3 * t + d;
-          const uint32_t offset = block * b_block + (nrow >> 3) * 256 + (pk >> 4) * 128 + (nrow & 7) * 16 + (pk & 15);
-          *reinterpret_cast<uint32_t *>(smem_b + offset) = pack_digit_bytes(q, d);
+            for (int bb = 0; bb < 4; ++bb) {
+              q[bb] = __float2int_rn(s_act[t * ncols + c0 + 8 * bb] * scale);
+              qsum[t] += q[bb];
+            }
+            uint32_t digits[kDigits];
+            split_digits(q, digits);
+#pragma unroll
+            for (int d = 0; d < kDigits; ++d) {
+              const uint32_t nrow = 3 * t + d;
+              const uint32_t offset =
+                  block * b_block + (nrow >> 3) * 256 + (pk >> 4) * 128 + (nrow & 7) * 16 + (pk & 15);
+              *reinterpret_cast<uint32_t *>(smem_b + offset) = digits[d];
+            }
+          }
         }
       }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, off);
-      if (lane == 0) s_warp_q[warp] = qsum;
-      __syncthreads();
-      if (tid == 0) s_qsum[t] = s_warp_q[0] + s_warp_q[1] + s_warp_q[2] + s_warp_q[3];
-      __syncthreads();
     }
+#pragma unroll
+    for (int t = 0; t < kT; ++t) {
+      if (t < T) {
+        long long v = qsum[t];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) s_red_q[warp * kT + t] = v;
+      }
+    }
+    __syncthreads();
+    if (tid < T)
+      s_qsum[tid] = s_red_q[tid] + s_red_q[kT + tid] + s_red_q[2 * kT + tid] +
+                    s_red_q[3 * kT + tid];
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B image -> tensor core (async proxy)
   __syncthreads();
 
-  // 5. main loop: bits -> TMEM (A), one tcgen05.mma per (class, half) per stage
+  // ---- main loop: bits -> TMEM (A), one tcgen05.mma per (class, half) per stage
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t idesc = ptx::idesc_i8_m128(static_cast<uint32_t>(NP));
   const uint32_t b_base = ptx::smem_u32(smem_b);
@@ -336,39 +445,34 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   if (tid == 0) ptx::mma_commit(&s_bar_done);
   if (!ptx::mbar_wait_bounded(&s_bar_done, 0, kSpinLimit)) ok = false;
   ptx::tc_fence_after();
-  if (!ok) {
-    s_failed = 1;
-    record_error(NQB_ERR_TIMEOUT);
-  }
+  if (!ok) record_error(NQB_ERR_TIMEOUT);
 
-  // 6. epilogue: combine classes and digits, convert to fp32 partials
+  // ---- epilogue: combine classes and digits, write fp32 partials ---------
   const int64_t row = static_cast<int64_t>(tile) * kTileRows + tid;
   {
-    int32_t sacc[kMaxNPad];
+    int32_t sacc[kNP];
 #pragma unroll
-    for (int n = 0; n < kMaxNPad; ++n) sacc[n] = 0;
+    for (int n = 0; n < kNP; ++n) sacc[n] = 0;
 #pragma unroll
     for (int j = 0; j < kClasses; ++j) {
+      uint32_t v[kNP];
 #pragma unroll
-      for (int qb = 0; qb < kMaxNPad / 16; ++qb) {
-        if (qb * 16 < NP) {
-          uint32_t v[16];
-          ptx::tmem_ld16(tmem + lane_base + kDCol + j * NP + qb * 16, v);
-          ptx::tmem_wait_ld();
+      for (int qb = 0; qb < kNP / 16; ++qb)
+        if (qb * 16 < NP) ptx::tmem_ld16(tmem + lane_base + kDCol + j * NP + qb * 16, v + qb * 16);
+      ptx::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) sacc[qb * 16 + e] += static_cast<int32_t>(v[e]) >> j;
-        }
-      }
+      for (int e = 0; e < kNP; ++e)
+        if (e < NP) sacc[e] += static_cast<int32_t>(v[e]) >> j;
     }
     if (row < m.rows) {
 #pragma unroll
-      for (int t = 0; t < kMaxTokens; ++t) {
+      for (int t = 0; t < kT; ++t) {
         if (t < T) {
           const long long st = static_cast<long long>(sacc[3 * t]) + 256ll * sacc[3 * t + 1] +
                                65536ll * sacc[3 * t + 2];
-          const double value = ldexp(static_cast<double>(s_qsum[t] - 2 * st), -s_exp[t]);
-          p.partial[(static_cast<int64_t>(split) * T + t) * p.part_stride + m.out_offset + row] =
-              static_cast<float>(value);
+          // one rounding (int64 -> fp32), then an exact power-of-two scale
+          const float value = __ll2float_rn(s_qsum[t] - 2 * st) * exp2_int(-s_exp[t]);
+          p.partial[(static_cast<int64_t>(split) * T + t) * p.part_stride + m.out_offset + row] = value;
         }
       }
     }
@@ -377,21 +481,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem, p.tmem_cols);
 
-  if constexpr (kStage2) {
-    // 7. the last CTA of this output tile reduces the K-split partials
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int previous = atomicAdd(m.counters + tile, 1);
-      s_last = (previous == m.splits - 1);
+  // ---- the last CTA of this row tile reduces the K-split partials --------
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int previous = atomicAdd(m.counters + tile, 1);
+    s_last = (previous == m.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if constexpr (!kStage2) {
+    if (row < m.rows) {
+      const float mid = load_as_float(m.mid, row, p.scale_dtype);
+      for (int t = 0; t < T; ++t) {
+        float acc = 0.0f;
+        for (int s = 0; s < m.splits; ++s)
+          acc += __ldcg(p.partial + (static_cast<int64_t>(s) * T + t) * p.part_stride + m.out_offset + row);
+        p.latent[static_cast<int64_t>(t) * p.latent_stride + m.out_offset + row] = acc * mid;
+      }
     }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+  } else {
     if (row < m.rows) {
       const float post = load_as_float(m.post, row, p.scale_dtype);
       const float bias = m.bias != nullptr ? load_as_float(m.bias, row, m.bias_dtype) : 0.0f;
-      const int64_t out_features = m.rows;
       for (int t = 0; t < T; ++t) {
         float acc = 0.0f;
         for (int s = 0; s < m.splits; ++s)
@@ -406,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
           }
           v += sal;
         }
-        m.y[static_cast<int64_t>(t) * out_features + row] = v + bias;
+        m.y[static_cast<int64_t>(t) * m.rows + row] = v + bias;
       }
     }
     if (m.overlay_rows > 0) {
@@ -429,18 +542,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
             part += static_cast<float>(rv[i]) * load_as_float(p.x, static_cast<int64_t>(t) * p.n + i, p.x_dtype);
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-          if (lane == 0) s_warp_max[warp][0] = part;
+          if (lane == 0) s_red_f[warp] = part;
           __syncthreads();
           if (tid == 0) {
-            const float dot = (s_warp_max[0][0] + s_warp_max[1][0]) + (s_warp_max[2][0] + s_warp_max[3][0]);
+            const float dot = (s_red_f[0] + s_red_f[1]) + (s_red_f[2] + s_red_f[3]);
             m.y[static_cast<int64_t>(t) * m.rows + orow] += dot * scale;
           }
           __syncthreads();
         }
       }
     }
-    if (tid == 0) m.counters[tile] = 0;  // ready for the next call
   }
+  if (tid == 0) m.counters[tile] = 0;  // zero again for the next call
 }
 
 // ------------------------------------------------------------- repack ---
@@ -496,7 +609,12 @@ struct Plan {
 };
 
 // Split each member's K stages so the grid fills the GPU about twice.
-static Plan plan_stage(const int32_t *row_tiles, const int32_t *k_stages, int count, bool uniform, int sms) {
+// Largest K slice (in 256-column stages) per CTA for `tokens` tokens: keeps the
+// staged activations (tokens x slice fp32) and the B image within ~64 KB.
+static int max_stages_for(int64_t tokens) { return tokens <= 4 ? kMaxStagesPerCta : (tokens <= 8 ? 4 : 2); }
+
+static Plan plan_stage(const int32_t *row_tiles, const int32_t *k_stages, int count, bool uniform, int sms,
+                       int max_sps) {
   Plan plan{};
   int64_t tiles = 0;
   for (int i = 0; i < count; ++i) tiles += row_tiles[i];
@@ -507,7 +625,7 @@ static Plan plan_stage(const int32_t *row_tiles, const int32_t *k_stages, int co
   for (int i = 0; i < count; ++i) {
     int32_t splits = want < k_stages[i] ? want : k_stages[i];
     int32_t sps = (k_stages[i] + splits - 1) / splits;
-    if (sps > kMaxStagesPerCta) sps = kMaxStagesPerCta;
+    if (sps > max_sps) sps = max_sps;
     splits = (k_stages[i] + sps - 1) / sps;
     plan.splits[i] = splits;
     plan.sps[i] = sps;
@@ -531,6 +649,11 @@ static int sm_count() {
 bool tc_eligible(const nqb_linear_desc *layers, int count, int32_t x_dtype, int64_t tokens) {
   if (tokens < 1 || tokens > kMaxTokens || count < 1 || count > kMaxMembersTc) return false;
   if (!is_float_dtype(x_dtype)) return false;
+  int64_t tiles = 0;
+  for (int i = 0; i < count; ++i)
+    tiles += (layers[i].rank + tc::kTileRows - 1) / tc::kTileRows +
+             (layers[i].out_features + tc::kTileRows - 1) / tc::kTileRows;
+  if (tiles > kMaxCounters) return false;
   for (int i = 0; i < count; ++i) {
     if (layers[i].right_tiles == nullptr || layers[i].left_tiles == nullptr) return false;
     if (reinterpret_cast<uintptr_t>(layers[i].right_tiles) % 16 || reinterpret_cast<uintptr_t>(layers[i].left_tiles) % 16)
@@ -539,177 +662,171 @@ bool tc_eligible(const nqb_linear_desc *layers, int count, int32_t x_dtype, int6
   return true;
 }
 
-struct Sizes {
-  size_t partial1, partial2, counters;
+struct Layout {
+  Plan s1, s2;
+  int32_t rt1[kMaxMembersTc], ks1[kMaxMembersTc], rt2[kMaxMembersTc], ks2[kMaxMembersTc];
+  int64_t total_rank, total_out;
+  int64_t counters;                     // completion counters used (row tiles of both stages)
+  size_t partial1, partial2;            // section sizes (256-aligned)
 };
 
-static Sizes tc_sizes(const nqb_linear_desc *layers, int count, int64_t tokens) {
+static Layout tc_layout(const nqb_linear_desc *layers, int count, int64_t tokens) {
   const int sms = sm_count();
-  int32_t rt[kMaxMembersTc], ks[kMaxMembersTc];
-  int64_t total_rank = 0, total_out = 0;
-  for (int i = 0; i < count; ++i) {
-    rt[i] = static_cast<int32_t>((layers[i].rank + tc::kTileRows - 1) / tc::kTileRows);
-    ks[i] = repack_chunks(layers[i].in_features) / 2;
-    total_rank += layers[i].rank;
-  }
-  const Plan p1 = plan_stage(rt, ks, count, true, sms);
-  int32_t max_s2 = 0;
+  Layout l{};
   int64_t counters = 0;
+  int32_t max_s2 = 0;
   for (int i = 0; i < count; ++i) {
-    rt[i] = static_cast<int32_t>((layers[i].out_features + tc::kTileRows - 1) / tc::kTileRows);
-    ks[i] = repack_chunks(layers[i].rank) / 2;
-    total_out += layers[i].out_features;
-    counters += rt[i];
+    l.rt1[i] = static_cast<int32_t>((layers[i].rank + tc::kTileRows - 1) / tc::kTileRows);
+    l.ks1[i] = repack_chunks(layers[i].in_features) / 2;
+    l.rt2[i] = static_cast<int32_t>((layers[i].out_features + tc::kTileRows - 1) / tc::kTileRows);
+    l.ks2[i] = repack_chunks(layers[i].rank) / 2;
+    l.total_rank += layers[i].rank;
+    l.total_out += layers[i].out_features;
+    counters += l.rt1[i] + l.rt2[i];
   }
-  const Plan p2 = plan_stage(rt, ks, count, false, sms);
-  for (int i = 0; i < count; ++i) max_s2 = p2.splits[i] > max_s2 ? p2.splits[i] : max_s2;
-  Sizes s;
-  s.partial1 = align_up(static_cast<size_t>(p1.splits[0]) * tokens * total_rank * sizeof(float), 256);
-  s.partial2 = align_up(static_cast<size_t>(max_s2) * tokens * total_out * sizeof(float), 256);
-  s.counters = align_up(static_cast<size_t>(counters) * sizeof(int32_t), 256);
-  return s;
+  l.s1 = plan_stage(l.rt1, l.ks1, count, true, sms, max_stages_for(tokens));
+  l.s2 = plan_stage(l.rt2, l.ks2, count, false, sms, max_stages_for(tokens));
+  for (int i = 0; i < count; ++i) max_s2 = l.s2.splits[i] > max_s2 ? l.s2.splits[i] : max_s2;
+  l.counters = counters;
+  l.partial1 = align_up(static_cast<size_t>(l.s1.splits[0]) * tokens * l.total_rank * sizeof(float), 256);
+  l.partial2 = align_up(static_cast<size_t>(max_s2) * tokens * l.total_out * sizeof(float), 256);
+  return l;
 }
 
 size_t tc_extra_workspace_bytes(const nqb_linear_desc *layers, int count, int64_t tokens) {
   if (!tc_eligible(layers, count, NQB_F32, tokens)) return 0;
-  const Sizes s = tc_sizes(layers, count, tokens);
-  return s.partial1 + s.partial2 + s.counters;
+  const Layout l = tc_layout(layers, count, tokens);
+  return l.partial1 + l.partial2;
 }
 
-static int smem_bytes(int stages, int n_pad) {
-  return stages * tc::kStageWeightBytes + stages * 8 * 32 * n_pad;
+// Dynamic shared memory of one CTA: sign tiles, B image, staged activations.
+static int smem_bytes(int stages, int n_pad, int64_t tokens) {
+  return stages * tc::kStageWeightBytes + stages * 8 * 32 * n_pad +
+         static_cast<int>(tokens) * stages * tc::kStageCols * static_cast<int>(sizeof(float));
+}
+
+template <bool kStage2, int kT>
+static int launch_stage_t(const tc::Params &params, int ctas, int smem, cudaStream_t stream) {
+  const void *fn = reinterpret_cast<const void *>(tc::tc_stage_kernel<kStage2, kT>);
+  NQB_CHECK(ensure_dynamic_smem(fn, smem));
+  cudaLaunchConfig_t config;
+  std::memset(&config, 0, sizeof(config));
+  config.gridDim = dim3(ctas);
+  config.blockDim = dim3(tc::kThreads);
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  NQB_CUDA(cudaLaunchKernelEx(&config, tc::tc_stage_kernel<kStage2, kT>, params),
+           kStage2 ? "tc stage 2 launch" : "tc stage 1 launch");
+  return NQB_OK;
+}
+
+// Token buckets: each kernel instance is compiled for at most kT tokens.
+static int token_bucket(int64_t tokens) { return tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : tokens <= 8 ? 8 : 16; }
+
+template <bool kStage2>
+static int launch_stage(const tc::Params &params, int ctas, int smem, cudaStream_t stream) {
+  switch (token_bucket(params.tokens)) {
+    case 1: return launch_stage_t<kStage2, 1>(params, ctas, smem, stream);
+    case 2: return launch_stage_t<kStage2, 2>(params, ctas, smem, stream);
+    case 4: return launch_stage_t<kStage2, 4>(params, ctas, smem, stream);
+    case 8: return launch_stage_t<kStage2, 8>(params, ctas, smem, stream);
+    default: return launch_stage_t<kStage2, 16>(params, ctas, smem, stream);
+  }
 }
 
 int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
-           float *const *ys, void *extra, size_t extra_bytes, float * /*latent*/, cudaStream_t stream) {
-  const Sizes sizes = tc_sizes(layers, count, tokens);
-  if (extra_bytes < sizes.partial1 + sizes.partial2 + sizes.counters)
-    return fail(NQB_ERR_WORKSPACE, "tensor-core path workspace too small");
+           float *const *ys, int32_t *counters, void *extra, size_t extra_bytes, float *latent,
+           cudaStream_t stream) {
+  const Layout l = tc_layout(layers, count, tokens);
+  if (extra_bytes < l.partial1 + l.partial2) return fail(NQB_ERR_WORKSPACE, "tensor-core path workspace too small");
   char *ws = static_cast<char *>(extra);
   float *partial1 = reinterpret_cast<float *>(ws);
-  float *partial2 = reinterpret_cast<float *>(ws + sizes.partial1);
-  int32_t *counters = reinterpret_cast<int32_t *>(ws + sizes.partial1 + sizes.partial2);
-  const int sms = sm_count();
-  const int32_t n_pad = static_cast<int32_t>(((3 * tokens + 15) / 16) * 16);
+  float *partial2 = reinterpret_cast<float *>(ws + l.partial1);
+  const int32_t n_pad = tc::n_pad_for(token_bucket(tokens));
   const uint32_t tmem_cols = (tc::kDCol + tc::kClasses * n_pad) <= 256 ? 256u : 512u;
 
-  int64_t total_rank = 0, total_out = 0;
-  for (int i = 0; i < count; ++i) {
-    total_rank += layers[i].rank;
-    total_out += layers[i].out_features;
-  }
-
-  // ---- stage 1: latent partials = V x (x * pre)
   tc::Params p1;
   std::memset(&p1, 0, sizeof(p1));
-  {
-    int32_t rt[kMaxMembersTc], ks[kMaxMembersTc];
-    for (int i = 0; i < count; ++i) {
-      rt[i] = static_cast<int32_t>((layers[i].rank + tc::kTileRows - 1) / tc::kTileRows);
-      ks[i] = repack_chunks(layers[i].in_features) / 2;
-    }
-    const Plan plan = plan_stage(rt, ks, count, true, sms);
-    int32_t cta = 0;
-    int64_t offset = 0;
-    for (int i = 0; i < count; ++i) {
-      tc::Member &m = p1.m[i];
-      m.tiles = static_cast<const uint4 *>(layers[i].right_tiles);
-      m.rows = layers[i].rank;
-      m.wc = repack_chunks(layers[i].in_features);
-      m.row_tiles = rt[i];
-      m.k_stages = ks[i];
-      m.splits = plan.splits[i];
-      m.stages_per_split = plan.sps[i];
-      m.cta_begin = cta;
-      m.k_valid = layers[i].in_features;
-      m.pre = layers[i].scale_pre;
-      m.out_offset = offset;
-      cta += rt[i] * plan.splits[i];
-      offset += layers[i].rank;
-    }
-    p1.count = count;
-    p1.x = x;
-    p1.x_dtype = x_dtype;
-    p1.scale_dtype = layers[0].scale_dtype;
-    p1.n = layers[0].in_features;
-    p1.tokens = static_cast<int32_t>(tokens);
-    p1.n_pad = n_pad;
-    p1.tmem_cols = tmem_cols;
-    p1.partial = partial1;
-    p1.part_stride = total_rank;
-    const int smem = smem_bytes(plan.sps[0], n_pad);
-    NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(tc::tc_stage_kernel<false>), smem));
-    tc::tc_stage_kernel<false><<<cta, tc::kThreads, smem, stream>>>(p1);
-    NQB_CUDA(cudaGetLastError(), "tc stage 1 launch");
-  }
+  tc::Params p2;
+  std::memset(&p2, 0, sizeof(p2));
+  int32_t cta1 = 0, cta2 = 0, max_sps2 = 1;
+  int64_t rank_offset = 0, out_offset = 0, counter_offset = 0;
+  for (int i = 0; i < count; ++i) {
+    const nqb_linear_desc &d = layers[i];
+    tc::Member &a = p1.m[i];
+    a.tiles = static_cast<const uint4 *>(d.right_tiles);
+    a.rows = d.rank;
+    a.wc = repack_chunks(d.in_features);
+    a.row_tiles = l.rt1[i];
+    a.k_stages = l.ks1[i];
+    a.splits = l.s1.splits[i];
+    a.stages_per_split = l.s1.sps[i];
+    a.cta_begin = cta1;
+    a.k_valid = d.in_features;
+    a.pre = d.scale_pre;
+    a.mid = d.scale_mid;
+    a.out_offset = rank_offset;
+    a.counters = counters + counter_offset;
+    cta1 += l.rt1[i] * a.splits;
+    counter_offset += l.rt1[i];
 
-  // ---- stage 2: y = post * U x latent (+ salient, overlay, bias)
-  {
-    tc::Params p2;
-    std::memset(&p2, 0, sizeof(p2));
-    int32_t rt[kMaxMembersTc], ks[kMaxMembersTc];
-    for (int i = 0; i < count; ++i) {
-      rt[i] = static_cast<int32_t>((layers[i].out_features + tc::kTileRows - 1) / tc::kTileRows);
-      ks[i] = repack_chunks(layers[i].rank) / 2;
-    }
-    const Plan plan = plan_stage(rt, ks, count, false, sms);
-    int32_t cta = 0, max_sps = 1;
-    int64_t out_offset = 0, act_offset = 0, counter_offset = 0;
-    for (int i = 0; i < count; ++i) {
-      const nqb_linear_desc &d = layers[i];
-      tc::Member &m = p2.m[i];
-      m.tiles = static_cast<const uint4 *>(d.left_tiles);
-      m.rows = d.out_features;
-      m.wc = repack_chunks(d.rank);
-      m.row_tiles = rt[i];
-      m.k_stages = ks[i];
-      m.splits = plan.splits[i];
-      m.stages_per_split = plan.sps[i];
-      m.cta_begin = cta;
-      m.k_valid = d.rank;
-      m.mid = d.scale_mid;
-      m.act_offset = act_offset;
-      m.out_offset = out_offset;
-      m.post = d.scale_post;
-      m.bias = d.bias;
-      m.bias_dtype = d.bias_dtype;
-      m.outlier_count = d.outlier_count;
-      m.outlier_indices = d.outlier_indices;
-      m.outlier_values = d.outlier_values;
-      m.outlier_value_dtype = d.outlier_value_dtype;
-      m.outlier_scales = d.outlier_scales;
-      m.overlay_rows = d.overlay_rows;
-      m.overlay_row_ids = d.overlay_row_ids;
-      m.overlay_values = d.overlay_values;
-      m.overlay_scales = d.overlay_scales;
-      m.overlay_scale_dtype = d.overlay_scale_dtype;
-      m.y = ys[i];
-      m.counters = counters + counter_offset;
-      cta += rt[i] * plan.splits[i];
-      out_offset += d.out_features;
-      act_offset += d.rank;
-      counter_offset += rt[i];
-      if (plan.sps[i] > max_sps) max_sps = plan.sps[i];
-    }
-    p2.count = count;
-    p2.x = x;
-    p2.x_dtype = x_dtype;
-    p2.scale_dtype = layers[0].scale_dtype;
-    p2.n = layers[0].in_features;
-    p2.tokens = static_cast<int32_t>(tokens);
-    p2.n_pad = n_pad;
-    p2.tmem_cols = tmem_cols;
-    p2.partial = partial2;
-    p2.part_stride = total_out;
-    p2.act_partial = partial1;
-    p2.act_splits = p1.m[0].splits;
-    p2.act_stride = total_rank;
-    NQB_CUDA(cudaMemsetAsync(counters, 0, sizes.counters, stream), "counter reset");
-    const int smem = smem_bytes(max_sps, n_pad);
-    NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(tc::tc_stage_kernel<true>), smem));
-    tc::tc_stage_kernel<true><<<cta, tc::kThreads, smem, stream>>>(p2);
-    NQB_CUDA(cudaGetLastError(), "tc stage 2 launch");
+    tc::Member &b = p2.m[i];
+    b.tiles = static_cast<const uint4 *>(d.left_tiles);
+    b.rows = d.out_features;
+    b.wc = repack_chunks(d.rank);
+    b.row_tiles = l.rt2[i];
+    b.k_stages = l.ks2[i];
+    b.splits = l.s2.splits[i];
+    b.stages_per_split = l.s2.sps[i];
+    b.cta_begin = cta2;
+    b.k_valid = d.rank;
+    b.act_offset = rank_offset;
+    b.out_offset = out_offset;
+    b.counters = counters + counter_offset;
+    b.post = d.scale_post;
+    b.bias = d.bias;
+    b.bias_dtype = d.bias_dtype;
+    b.outlier_count = d.outlier_count;
+    b.outlier_indices = d.outlier_indices;
+    b.outlier_values = d.outlier_values;
+    b.outlier_value_dtype = d.outlier_value_dtype;
+    b.outlier_scales = d.outlier_scales;
+    b.overlay_rows = d.overlay_rows;
+    b.overlay_row_ids = d.overlay_row_ids;
+    b.overlay_values = d.overlay_values;
+    b.overlay_scales = d.overlay_scales;
+    b.overlay_scale_dtype = d.overlay_scale_dtype;
+    b.y = ys[i];
+    cta2 += l.rt2[i] * b.splits;
+    counter_offset += l.rt2[i];
+    if (b.stages_per_split > max_sps2) max_sps2 = b.stages_per_split;
+    rank_offset += d.rank;
+    out_offset += d.out_features;
   }
+  for (tc::Params *p : {&p1, &p2}) {
+    p->count = count;
+    p->x = x;
+    p->x_dtype = x_dtype;
+    p->scale_dtype = layers[0].scale_dtype;
+    p->n = layers[0].in_features;
+    p->tokens = static_cast<int32_t>(tokens);
+    p->n_pad = n_pad;
+    p->tmem_cols = tmem_cols;
+    p->latent = latent;
+    p->latent_stride = l.total_rank;
+  }
+  p1.partial = partial1;
+  p1.part_stride = l.total_rank;
+  p2.partial = partial2;
+  p2.part_stride = l.total_out;
+
+  NQB_CHECK(launch_stage<false>(p1, cta1, smem_bytes(l.s1.sps[0], n_pad, tokens), stream));
+  NQB_CHECK(launch_stage<true>(p2, cta2, smem_bytes(max_sps2, n_pad, tokens), stream));
   return NQB_OK;
 }
 

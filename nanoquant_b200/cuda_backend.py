@@ -168,6 +168,24 @@ def _workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+# One zero-initialised libnqb workspace per (device, stream): calls on a stream
+# are ordered, and every call leaves the workspace's counter region zero, so
+# the buffer is reused across layers and calls (like a per-stream BLAS
+# workspace).  It only grows; a grown buffer starts zeroed again.
+_STREAM_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def stream_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(device).cuda_stream)
+    current = _STREAM_WORKSPACES.get(key)
+    if current is None or current.numel() < nbytes:
+        # (during CUDA-graph capture the zero fill becomes a node of the graph)
+        current = torch.zeros(max(int(nbytes), 1 << 16), dtype=torch.uint8, device=device)
+        _STREAM_WORKSPACES[key] = current
+    return current
+
+
 def kernel_path(layer: PreparedLayer, tokens: int, input_dtype: torch.dtype = torch.bfloat16) -> str:
     """Which kernels ``linear`` runs for ``tokens`` tokens: ``"tensor-core"`` or ``"generic"``."""
 
@@ -187,7 +205,7 @@ def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLi
     needed = ctypes.c_size_t(0)
     desc_ref = ctypes.byref(payload.desc)
     _native.call("nqb_linear_workspace_bytes", desc_ref, tokens, ctypes.byref(needed))
-    workspace = _workspace(needed.value, value.device)
+    workspace = stream_workspace(needed.value, value.device)
     stream = _native.current_stream_handle(value.device)
     _native.call(
         "nqb_linear",
@@ -350,7 +368,7 @@ def grouped_sm100_projection(value: torch.Tensor, group: Sm100ProjectionGroup) -
     count = len(group.layers)
     needed = ctypes.c_size_t(0)
     _native.call("nqb_grouped_workspace_bytes", group.descs, count, tokens, ctypes.byref(needed))
-    workspace = _workspace(needed.value, value.device)
+    workspace = stream_workspace(needed.value, value.device)
     out_ptrs = (ctypes.c_void_p * count)(*(out.data_ptr() for out in outputs))
     _native.call(
         "nqb_grouped_linear",
