@@ -99,9 +99,11 @@ typedef struct nqb_linear_desc {
   const int16_t *codebook_second;     /* [256] bits 16..31 of a coded word  */
 
   /* Optional kernel-native copies of U and V made by nqb_repack_signs
-   * (16-byte aligned).  When both are present and the token count is 1..16,
-   * the call runs on the tensor-core decode path; otherwise on the generic
-   * CUDA-core path.  Both paths give results within the same tolerance.     */
+   * (16-byte aligned).  When both are present, 1..16 tokens run on the
+   * tensor-core decode path (exact integer products of 22-bit fixed-point
+   * activations) and more tokens on the tensor-core prefill path (fp16
+   * activations, fp32 accumulation); without them every call runs on the
+   * generic CUDA-core path (fp32).                                          */
   const void *left_tiles;  /* nqb_repack_signs(left_words,  m, r) */
   const void *right_tiles; /* nqb_repack_signs(right_words, r, n) */
 } nqb_linear_desc;
@@ -212,11 +214,13 @@ int nqb_repack_signs(const int32_t *words, int64_t rows, int64_t cols, void *til
 
 /*
  * Which kernels a call with these arguments would run: *path is
- * NQB_PATH_GENERIC (CUDA-core kernels) or NQB_PATH_TENSOR_CORE (tcgen05
- * decode kernels).  Host-only; launches nothing.
+ * NQB_PATH_GENERIC (CUDA-core kernels), NQB_PATH_TENSOR_CORE (tcgen05 decode
+ * kernels) or NQB_PATH_PREFILL (tcgen05 prefill kernels).  Host-only;
+ * launches nothing.
  */
 #define NQB_PATH_GENERIC 0
-#define NQB_PATH_TENSOR_CORE 1
+#define NQB_PATH_TENSOR_CORE 1 /* tcgen05 int8 decode kernels, 1..16 tokens */
+#define NQB_PATH_PREFILL 2     /* tcgen05 fp16 prefill kernels, more than 16 tokens */
 int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtype, int64_t tokens,
                     int32_t *path);
 

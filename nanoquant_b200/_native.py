@@ -26,6 +26,7 @@ NQB_ERR_TIMEOUT = 7
 
 NQB_PATH_GENERIC = 0
 NQB_PATH_TENSOR_CORE = 1
+NQB_PATH_PREFILL = 2
 
 NQB_F32 = 0
 NQB_F16 = 1

@@ -78,7 +78,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         (obj_dir / (source.stem + ".ptxas.txt")).write_text(result.stderr)
         objects.append(str(obj))
     tmp = LIB_DIR / "libnqb.so.tmp"
-    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objects, "-lcuda"]
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objects]
     result = subprocess.run(cmd, capture_output=True, text=True)
     if result.returncode != 0:
         raise RuntimeError(f"nvcc link failed:\n{result.stdout}\n{result.stderr}")

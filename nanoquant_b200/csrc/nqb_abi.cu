@@ -6,6 +6,7 @@
 
 #include "nqb_decode_tc.cuh"
 #include "nqb_generic.cuh"
+#include "nqb_prefill_tc.cuh"
 
 namespace nqb {
 
@@ -134,6 +135,12 @@ static size_t latent_bytes(int64_t tokens, int64_t total_rank) {
 // every call leaves it zero.
 static size_t workspace_bytes(size_t latent, size_t tc_partials) { return kCounterRegionBytes + latent + tc_partials; }
 
+// Path-specific workspace after the latent: tensor-core decode partials or
+// prefill fp16 activations (at most one of the two is non-zero for a call).
+static size_t path_extra_bytes(const nqb_linear_desc *layers, int count, int64_t tokens) {
+  return tc_extra_workspace_bytes(layers, count, tokens) + prefill_workspace_bytes(layers, count, tokens);
+}
+
 static void fill_stage1_member(Stage1Member &m, const nqb_linear_desc &d, int64_t latent_offset,
                                int32_t block_begin) {
   m.words = reinterpret_cast<const uint32_t *>(d.right_words);
@@ -243,7 +250,7 @@ int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, siz
   NQB_CHECK(validate_layer(layer, "layer"));
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
   if (tokens <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "token count must be positive");
-  *bytes = workspace_bytes(latent_bytes(tokens, layer->rank), tc_extra_workspace_bytes(layer, 1, tokens));
+  *bytes = workspace_bytes(latent_bytes(tokens, layer->rank), path_extra_bytes(layer, 1, tokens));
   return ok();
 }
 
@@ -253,7 +260,7 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   if (y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output y is NULL");
   const size_t need = latent_bytes(tokens, layer->rank);
-  const size_t tc_need = tc_extra_workspace_bytes(layer, 1, tokens);
+  const size_t tc_need = path_extra_bytes(layer, 1, tokens);
   if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
     return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
                 nqb::workspace_bytes(need, tc_need), workspace_bytes);
@@ -267,6 +274,10 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
     return ok();
   }
   float *ys[1] = {y};
+  if (prefill_eligible(layer, 1, x_dtype, tokens)) {
+    NQB_CHECK(run_prefill(layer, 1, x, x_dtype, tokens, ys, latent, base + kCounterRegionBytes + need, tc_need, s));
+    return ok();
+  }
   NQB_CHECK(run_generic(layer, 1, x, x_dtype, tokens, ys, latent, s));
   return ok();
 }
@@ -281,7 +292,7 @@ int nqb_grouped_workspace_bytes(const nqb_linear_desc *layers, int32_t count, in
     NQB_CHECK(validate_layer(layers + i, "grouped member"));
     total_rank += layers[i].rank;
   }
-  *bytes = workspace_bytes(latent_bytes(tokens, total_rank), tc_extra_workspace_bytes(layers, count, tokens));
+  *bytes = workspace_bytes(latent_bytes(tokens, total_rank), path_extra_bytes(layers, count, tokens));
   return ok();
 }
 
@@ -303,7 +314,7 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
   }
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   const size_t need = latent_bytes(tokens, total_rank);
-  const size_t tc_need = tc_extra_workspace_bytes(layers, count, tokens);
+  const size_t tc_need = path_extra_bytes(layers, count, tokens);
   if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
     return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
                 nqb::workspace_bytes(need, tc_need), workspace_bytes);
@@ -314,6 +325,11 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
   if (tc_eligible(layers, count, x_dtype, tokens)) {
     NQB_CHECK(run_tc(layers, count, x, x_dtype, tokens, y_out, counters, base + kCounterRegionBytes + need, tc_need,
                      latent, s));
+    return ok();
+  }
+  if (prefill_eligible(layers, count, x_dtype, tokens)) {
+    NQB_CHECK(run_prefill(layers, count, x, x_dtype, tokens, y_out, latent, base + kCounterRegionBytes + need, tc_need,
+                          s));
     return ok();
   }
   NQB_CHECK(run_generic(layers, count, x, x_dtype, tokens, y_out, latent, s));
@@ -377,13 +393,18 @@ int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtyp
   if (layers == nullptr || count < 1 || count > kMaxMembers || path == nullptr)
     return fail(NQB_ERR_INVALID_ARGUMENT, "path query takes 1 to %d layers and an output pointer", kMaxMembers);
   for (int i = 0; i < count; ++i) NQB_CHECK(validate_layer(layers + i, "layer"));
-  *path = tc_eligible(layers, count, x_dtype, tokens) ? NQB_PATH_TENSOR_CORE : NQB_PATH_GENERIC;
+  *path = tc_eligible(layers, count, x_dtype, tokens)        ? NQB_PATH_TENSOR_CORE
+          : prefill_eligible(layers, count, x_dtype, tokens) ? NQB_PATH_PREFILL
+                                                              : NQB_PATH_GENERIC;
   return ok();
 }
 
 int nqb_device_status(int32_t *status) {
   if (status == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "status is NULL");
   NQB_CHECK(tc_device_error(status));
+  int32_t prefill_status = 0;
+  NQB_CHECK(prefill_device_error(&prefill_status));
+  if (*status == NQB_OK) *status = prefill_status;
   return ok();
 }
 

@@ -187,14 +187,14 @@ def stream_workspace(nbytes: int, device: torch.device) -> torch.Tensor:
 
 
 def kernel_path(layer: PreparedLayer, tokens: int, input_dtype: torch.dtype = torch.bfloat16) -> str:
-    """Which kernels ``linear`` runs for ``tokens`` tokens: ``"tensor-core"`` or ``"generic"``."""
+    """Which kernels ``linear`` runs for ``tokens`` tokens: ``"tensor-core"``, ``"prefill"`` or ``"generic"``."""
 
     if not isinstance(layer.payload, _Sm100Payload):
         raise TypeError("prepared runtime layer has an invalid sm100a packed payload")
     path = ctypes.c_int32(-1)
     _native.call("nqb_linear_path", ctypes.byref(layer.payload.desc), 1, _native.dtype_code(input_dtype), tokens,
                  ctypes.byref(path))
-    return "tensor-core" if path.value == _native.NQB_PATH_TENSOR_CORE else "generic"
+    return {_native.NQB_PATH_TENSOR_CORE: "tensor-core", _native.NQB_PATH_PREFILL: "prefill"}.get(path.value, "generic")
 
 
 def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLinearSpec) -> torch.Tensor:

@@ -335,3 +335,47 @@ def test_tensor_core_grouped_projection_matches_members() -> None:
     for out, state in zip(outs, states, strict=True):
         expected = po.packed_linear(x.float().cpu().numpy(), oracle_from_state(state), accumulate="float64")
         np.testing.assert_allclose(out.cpu().numpy(), expected, rtol=RTOL, atol=1e-5 * np.abs(expected).max())
+
+
+# ------------------------------------------------------------------ tensor-core prefill path ---
+
+PREFILL_BOUND = 2e-3  # north-star bound on max|y - y_ref| / max|y_ref| (fp16 activations)
+
+
+@pytest.mark.parametrize(("n", "m", "r", "tokens"), ((35, 17, 33, 40), (640, 2048, 480, 17), (640, 2048, 480, 300),
+                                                      (1152, 6912, 987, 129), (4096, 4096, 2048, 256)))
+def test_prefill_path_matches_oracle(n: int, m: int, r: int, tokens: int) -> None:
+    from nanoquant_b200.cuda_backend import kernel_path
+
+    state = _random_state(n, m, r, seed=7 * n + tokens, outliers=3, bias=True)
+    backend = CudaPackedSm100Backend()
+    layer = backend.prepare(state, "cuda")
+    assert kernel_path(layer, tokens) == "prefill"
+    g = torch.Generator().manual_seed(tokens)
+    x = torch.randn(tokens, n, generator=g).bfloat16()
+    got = backend.linear(x.cuda(), layer)
+    expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
+    assert _relative_max_error(got, expected) <= PREFILL_BOUND
+    assert torch.equal(got, backend.linear(x.cuda(), layer))
+    assert ctypes_status() == 0
+
+
+def test_prefill_grouped_projection_and_overlay() -> None:
+    backend = CudaPackedSm100Backend()
+    base = _random_state(1152, 6912, 987, seed=31)
+    g = torch.Generator().manual_seed(2)
+    rows = torch.sort(torch.randperm(6912, generator=g)[:70]).values.to(torch.int32)
+    overlay = OutlierRowOverlay(rows, torch.randint(-127, 128, (70, 1152), generator=g, dtype=torch.int8),
+                                torch.full((70,), 0.002, dtype=torch.float16))
+    up = _random_state(1152, 6912, 987, seed=32)
+    layers = (backend.prepare(OverlaidLayerState(base, overlay), "cuda"), backend.prepare(up, "cuda"))
+    group = prepare_sm100_projection_group(layers)
+    x = torch.randn(64, 1152, generator=g).bfloat16()
+    gate_out, up_out = grouped_sm100_projection(x.cuda(), group)
+    gate_ref = oracle_from_state(base)
+    gate_ref.overlay_row_ids = rows.numpy()
+    gate_ref.overlay_values = overlay.values.numpy()
+    gate_ref.overlay_scales = overlay.scales.float().numpy()
+    for got, ref in ((gate_out, gate_ref), (up_out, oracle_from_state(up))):
+        expected = po.packed_linear(x.float().numpy(), ref, accumulate="float64")
+        assert _relative_max_error(got, expected) <= PREFILL_BOUND

@@ -56,7 +56,7 @@ def test_noalloc_matches_workspace_entry_point_twice(n: int, m: int, tokens: int
     state = random_packed_layer("blocks.0.proj", n, m, m * n // (m + n), generator, device)
     backend = CudaPackedSm100Backend()
     layer = backend.prepare(state, device)
-    expected_path = "tensor-core" if tokens <= 16 else "generic"
+    expected_path = "tensor-core" if tokens <= 16 else "prefill"
     assert kernel_path(layer, tokens) == expected_path
     for call in range(2):
         x = torch.randn(tokens, n, device=device, generator=generator).bfloat16()
