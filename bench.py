@@ -32,15 +32,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tok/s (bs1, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak"
+PREFILL_METRIC = "prefill tok/s (Llama-3-8B shape 0.55 bpw, 8x4096 tokens); tensor TFLOP/s vs peak"
 UNIT = "tok/s"
 
 
-def _peaks() -> tuple[float, str]:
+def _peak_table() -> dict[str, tuple[float, str]]:
+    """HBM GB/s and sustained dense bf16 TFLOP/s: measured on this pool, else the fallback figures."""
+
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return {"hbm": (float(data["hbm_gbs"]), "measured"),
+                "tensor": (float(data.get("bf16_tflops_sustained", data["bf16_tflops"])), "measured-sustained")}
+    return {"hbm": (6650.0, "fallback"), "tensor": (1400.0, "fallback-sustained")}
 
 
 class ClockSampler:
@@ -93,16 +97,21 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-def cpu_baseline(sample_layers: int, repeats: int) -> dict:
-    """Time the CPU oracle (numpy port of PackedReferenceBackend) on ``sample_layers`` Qwen3-8B layers."""
+def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
+    """Time the CPU oracle (numpy port of PackedReferenceBackend) on a bounded sample.
+
+    decode: 2 of 36 Qwen3-8B layers, one token; prefill: 1 of 32 Llama-3-8B
+    layers, 128 tokens.  The result is extrapolated to the full step.
+    """
 
     import numpy as np
 
-    from nanoquant_b200.decode_chain import QWEN3_8B
+    from nanoquant_b200 import decode_chain
     from oracle import packed_oracle as po
 
     rng = np.random.default_rng(0)
-    shape = QWEN3_8B
+    shape = decode_chain.QWEN3_8B if workload == "decode" else decode_chain.LLAMA3_8B_055
+    sample_layers, sample_tokens = (2, 1) if workload == "decode" else (1, 128)
     per_layer_seconds = []
     for _layer in range(sample_layers):
         layers = {}
@@ -121,7 +130,8 @@ def cpu_baseline(sample_layers: int, repeats: int) -> dict:
                                    (np.abs(rng.standard_normal(m)) * 0.05 + 0.01).astype(np.float16).astype(np.float32))
             layer.prepared()  # the reference unpacks once at prepare time; not timed
             layers[proj] = layer
-        inputs = {proj: rng.standard_normal((1, n)).astype(np.float32) for proj, (n, _m) in shape.projections().items()}
+        inputs = {proj: rng.standard_normal((sample_tokens, n)).astype(np.float32)
+                  for proj, (n, _m) in shape.projections().items()}
         for proj, layer in layers.items():
             po.packed_linear(inputs[proj], layer)  # warm-up
         start = time.perf_counter()
@@ -131,26 +141,29 @@ def cpu_baseline(sample_layers: int, repeats: int) -> dict:
         per_layer_seconds.append((time.perf_counter() - start) / repeats)
         del layers
     per_layer = statistics.median(per_layer_seconds)
-    step = per_layer * shape.layers
+    step = per_layer * shape.layers  # one pass of `sample_tokens` tokens through every layer
     cores = os.cpu_count() or 1
     return {
-        "value": 1.0 / step,
+        "value": sample_tokens / step,
         "unit": UNIT,
         "cores": cores,
         "kind": "port",
-        "sample": f"{sample_layers} of {shape.layers} Qwen3-8B layers x 7 projections, bs1, {repeats} reps each; "
-                  f"numpy/BLAS fp32 on {cores} host threads; step time extrapolated x{shape.layers}",
+        "sample": f"{sample_layers} of {shape.layers} {shape.name} layers x 7 projections, {sample_tokens} token(s), "
+                  f"{repeats} reps; numpy/BLAS fp32 on {cores} host threads; extrapolated to all layers",
         "ms_per_step": step * 1e3,
     }
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference arm: the reference's packed CPU algorithm (oracle port) on the host cores."""
+
     if rank != 0:
         return
-    base = cpu_baseline(sample_layers=2, repeats=max(1, args.steps))
+    spec = WORKLOADS[args.workload]
+    base = cpu_baseline(args.workload, repeats=max(1, min(args.steps, 5)))
     line = {
         "impl": "reference",
-        "metric": METRIC,
+        "metric": spec["metric"],
         "value": base["value"],
         "unit": UNIT,
         "n_gpus": args.gpus,
@@ -158,29 +171,53 @@ def run_reference(args, rank: int, world: int) -> None:
         "warmup": args.warmup,
         "ms_per_step": base["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if args.workload == "decode" else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "qwen3-8b packed linears, decode bs1 (36 layers x q,k,v,o,gate,up,down)",
-                   "global_batch": 1, "seq_len": 1, "parallelism": "cpu"},
+        "config": {"workload": spec["description"].format(layers="all"), "model": spec["model"],
+                   "parallelism": "cpu"},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+WORKLOADS = {
+    "decode": {
+        "metric": METRIC,
+        "shape": "QWEN3_8B",
+        "tokens_total": None,  # one token per rank (replicas)
+        "description": "qwen3-8b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
+        "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
+    },
+    "prefill": {
+        "metric": PREFILL_METRIC,
+        "shape": "LLAMA3_8B_055",
+        "tokens_total": 8 * 4096,  # 8 sequences x 4096 tokens, disjoint token batches per rank
+        "description": "llama-3-8b packed linears, prefill 8x4096 tokens ({layers} layers x q,k,v,o,gate,up,down)",
+        "model": "llama-3-8b-shape random-init packed weights 0.55 bpw",
+    },
+}
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--steps", type=int, default=None, help="timed steps (default 50 decode, 3 prefill)")
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("nqb", "reference"), default="nqb")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
+                        help="decode: BASELINE config 2 linears (the headline); prefill: config 3")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--layers", type=int, default=None,
-                        help="decoder layers in the step (default: all 36); fewer only for profiling runs")
+                        help="decoder layers in the step (default: all); fewer only for profiling runs")
+    parser.add_argument("--tokens", type=int, default=None,
+                        help="prefill tokens per GPU (default: 8*4096 / GPUs); smaller only for profiling runs")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps is None:
+        args.steps = 50 if args.workload == "decode" else 3
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -193,7 +230,8 @@ def main() -> None:
     import torch
     import torch.distributed as dist
 
-    from nanoquant_b200.decode_chain import QWEN3_8B, DecodeChain, make_decoder_layers
+    from nanoquant_b200 import decode_chain
+    from nanoquant_b200.decode_chain import DecodeChain, make_decoder_layers
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -206,11 +244,23 @@ def main() -> None:
         if world > 1:
             dist.barrier()
 
-    shape = QWEN3_8B
-    chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=rank), device, tokens=1)
-    chain.capture()
+    spec = WORKLOADS[args.workload]
+    shape = getattr(decode_chain, spec["shape"])
+    if spec["tokens_total"] is None:
+        tokens = 1
+    else:
+        if spec["tokens_total"] % world:
+            raise SystemExit(f"{spec['tokens_total']} tokens do not split over {world} ranks")
+        tokens = spec["tokens_total"] // world
+        if args.tokens is not None:
+            tokens = args.tokens
+    chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device, tokens=tokens)
+    use_graph = args.workload == "decode"
+    if use_graph:
+        chain.capture()
+    run_step = chain.replay if use_graph else chain.step
     for _ in range(args.warmup):
-        chain.replay()
+        run_step()
     torch.cuda.synchronize(device)
 
     stream = torch.cuda.current_stream(device)
@@ -220,25 +270,26 @@ def main() -> None:
         torch.cuda.synchronize(device)
         start.record(stream)
         for _ in range(args.steps):
-            chain.replay()
+            run_step()
         stop.record(stream)
         torch.cuda.synchronize(device)
         barrier()
     elapsed_ms = start.elapsed_time(stop)
 
-    # end to end through the public API: pinned host token in, result back to host, every step
-    host_in = torch.randn(1, shape.hidden).bfloat16().pin_memory()
-    host_out = torch.empty(chain.graph_output.shape, dtype=torch.float32).pin_memory()
+    # end to end through the public API: pinned host tokens in, result back to host, every step
+    host_in = torch.randn(tokens, shape.hidden).bfloat16().pin_memory()
+    last = run_step()
+    host_out = torch.empty(last.shape, dtype=torch.float32).pin_memory()
     for _ in range(2):
         chain.inputs["hidden"].copy_(host_in, non_blocking=True)
-        host_out.copy_(chain.replay(), non_blocking=True)
+        host_out.copy_(run_step(), non_blocking=True)
     torch.cuda.synchronize(device)
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e_start.record(stream)
     for _ in range(args.steps):
         chain.inputs["hidden"].copy_(host_in, non_blocking=True)
-        host_out.copy_(chain.replay(), non_blocking=True)
+        host_out.copy_(run_step(), non_blocking=True)
     e_stop.record(stream)
     torch.cuda.synchronize(device)
     barrier()
@@ -250,12 +301,29 @@ def main() -> None:
         elapsed_ms, e2e_ms = (float(v) for v in times.tolist())
 
     ms_per_step = elapsed_ms / args.steps
-    value = world * 1000.0 / ms_per_step
-    peak, peak_kind = _peaks()
-    step_bytes = chain.algorithmic_bytes()
-    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+    total_tokens = tokens * world
+    value = total_tokens * 1000.0 / ms_per_step
+    peaks = _peak_table()
+    if args.workload == "decode":
+        step_bytes = chain.algorithmic_bytes()
+        achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+        roofline = {
+            "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"][0], "unit": "GB/s",
+            "frac": achieved / peaks["hbm"][0], "traffic": None, "peak_kind": peaks["hbm"][1],
+            "scope": "all packed-linear kernels of one step (algorithmic bytes per step / step time)",
+            "algorithmic_bytes_per_step": step_bytes,
+        }
+    else:
+        step_flops = chain.algorithmic_flops()
+        achieved = step_flops / (ms_per_step * 1e-3) / 1e12
+        roofline = {
+            "bound": "tensor", "achieved": achieved, "peak": peaks["tensor"][0], "unit": "TFLOP/s",
+            "frac": achieved / peaks["tensor"][0], "traffic": None, "peak_kind": peaks["tensor"][1],
+            "scope": "all packed-linear kernels of one step per GPU (2*r*(m+n) flops per token and linear / step time)",
+            "algorithmic_flops_per_step_per_gpu": step_flops,
+        }
     line = {
-        "metric": METRIC,
+        "metric": spec["metric"],
         "value": value,
         "unit": UNIT,
         "n_gpus": world,
@@ -263,33 +331,23 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if args.workload == "decode" else "strong",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": "f32" if args.workload == "decode" else "f16",
         "data": "synthetic",
         "config": {
-            "workload": f"qwen3-8b packed linears, decode bs1 ({len(chain.blocks)} layers x q,k,v,o,gate,up,down; "
-                        "grouped qkv and gate/up)",
-            "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
-            "global_batch": world,
-            "seq_len": 1,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
-            "l2": "weights 875 MB > 126 MB L2 (no flush)",
-            "cuda_graph": True,
+            "workload": spec["description"].format(layers=len(chain.blocks)),
+            "model": spec["model"],
+            "global_batch": total_tokens,
+            "tokens_per_gpu": tokens,
+            "parallelism": (f"replicas{world}" if args.workload == "decode" else f"token-batches{world}")
+            if world > 1 else "single",
+            "l2": "weights larger than the 126 MB L2 (no flush)",
+            "cuda_graph": use_graph,
         },
-        "roofline": {
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": achieved / peak,
-            "traffic": None,
-            "peak_kind": peak_kind,
-            "scope": "all packed-linear kernels of one step (algorithmic bytes per step / step time)",
-            "algorithmic_bytes_per_step": step_bytes,
-        },
+        "roofline": roofline,
         "e2e": {
-            "value": world * 1000.0 * args.steps / e2e_ms,
+            "value": total_tokens * 1000.0 * args.steps / e2e_ms,
             "unit": UNIT,
             "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
             "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
@@ -298,7 +356,7 @@ def main() -> None:
         "clocks": clocks.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:
-        base = cpu_baseline(sample_layers=2, repeats=3)
+        base = cpu_baseline(args.workload)
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line), flush=True)

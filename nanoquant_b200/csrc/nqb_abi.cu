@@ -125,8 +125,12 @@ static int validate_input(const void *x, int32_t x_dtype, int64_t tokens) {
   return NQB_OK;
 }
 
-static size_t latent_bytes(int64_t tokens, int64_t total_rank) {
-  return align_up(static_cast<size_t>(tokens) * total_rank * sizeof(float), 256);
+// Latent columns reserved for a member: its rank rounded up to 4 floats, so
+// the prefill path can place every member on a 16-byte boundary.
+static int64_t latent_columns(int64_t rank) { return (rank + 3) & ~int64_t(3); }
+
+static size_t latent_bytes(int64_t tokens, int64_t total_columns) {
+  return align_up(static_cast<size_t>(tokens) * total_columns * sizeof(float), 256);
 }
 
 // Workspace layout shared by every call: [completion counters][latent][tensor-core partials].
@@ -250,7 +254,7 @@ int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, siz
   NQB_CHECK(validate_layer(layer, "layer"));
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
   if (tokens <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "token count must be positive");
-  *bytes = workspace_bytes(latent_bytes(tokens, layer->rank), path_extra_bytes(layer, 1, tokens));
+  *bytes = workspace_bytes(latent_bytes(tokens, latent_columns(layer->rank)), path_extra_bytes(layer, 1, tokens));
   return ok();
 }
 
@@ -259,7 +263,7 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
   NQB_CHECK(validate_layer(layer, "layer"));
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   if (y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output y is NULL");
-  const size_t need = latent_bytes(tokens, layer->rank);
+  const size_t need = latent_bytes(tokens, latent_columns(layer->rank));
   const size_t tc_need = path_extra_bytes(layer, 1, tokens);
   if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
     return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
@@ -290,7 +294,7 @@ int nqb_grouped_workspace_bytes(const nqb_linear_desc *layers, int32_t count, in
   int64_t total_rank = 0;
   for (int i = 0; i < count; ++i) {
     NQB_CHECK(validate_layer(layers + i, "grouped member"));
-    total_rank += layers[i].rank;
+    total_rank += latent_columns(layers[i].rank);
   }
   *bytes = workspace_bytes(latent_bytes(tokens, total_rank), path_extra_bytes(layers, count, tokens));
   return ok();
@@ -310,7 +314,7 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
     if (layers[i].scale_dtype != layers[0].scale_dtype)
       return fail(NQB_ERR_DTYPE, "grouped members must share the scale dtype");
     if (y_out[i] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output %d is NULL", i);
-    total_rank += layers[i].rank;
+    total_rank += latent_columns(layers[i].rank);
   }
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   const size_t need = latent_bytes(tokens, total_rank);

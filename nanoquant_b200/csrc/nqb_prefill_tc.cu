@@ -17,13 +17,13 @@
 //   stores it with the same pair order (position 2j <- column j, 2j+1 <-
 //   column j+16 of every 32-column group); TMA (128-byte swizzle) brings
 //   128-token x 64-column boxes into shared memory.
-// * One CTA owns two 128-row sign tiles and one 128-token tile; the K loop
-//   (128 columns per step) is pipelined over 4 shared-memory stages:
-//   warp 4 issues TMA and the sign-chunk bulk copies, warps 0-3 expand signs
-//   into a double-buffered A region of TMEM, one thread of warp 5 issues the
-//   16 MMAs of a step and commits them to the stage's "empty" barriers.
-//   Accumulators (2 x 128 x 128 fp32) stay in TMEM until the epilogue
-//   multiplies by 2^-e and the row scale and writes fp32 outputs.
+// * One CTA owns one 128-row sign tile and one 256-token tile (MMA
+//   128 x 256 x 16); the K loop (128 columns per step) is pipelined over 3
+//   shared-memory stages of 64 KB: warp 4 issues TMA and the sign-chunk bulk
+//   copy, warps 0-3 expand signs into a double-buffered A region of TMEM, one
+//   thread of warp 5 issues the 8 MMAs of a step and commits them to the
+//   stage's "empty" barriers.  The 128 x 256 fp32 accumulator stays in TMEM
+//   until the epilogue multiplies by 2^-e and the row scale and writes fp32.
 // Every mbarrier wait is bounded; a timeout sets the device status word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -37,16 +37,16 @@
 namespace nqb {
 namespace pf {
 
-constexpr int kTileRows = 128;     // sign rows per MMA (M)
-constexpr int kTokTile = 128;      // tokens per CTA (MMA N)
+constexpr int kTileRows = 128;     // sign rows per CTA (MMA M)
+constexpr int kTokTile = 256;      // tokens per CTA (MMA N)
 constexpr int kKStep = 128;        // K columns per pipeline step = one 4-word sign chunk
-constexpr int kStages = 4;
-constexpr int kAtomBytes = kTokTile * 128;             // 128 tokens x 64 fp16 (one 128-byte swizzle column)
+constexpr int kStages = 3;
+constexpr int kAtomBytes = kTokTile * 128;             // 256 tokens x 64 fp16 (one 128-byte swizzle column)
 constexpr int kBStageBytes = 2 * kAtomBytes;           // 128 K columns
 constexpr int kChunkBytes = kTileRows * 16;            // one 4-word chunk of a 128-row tile
-constexpr int kStageBytes = kBStageBytes + 2 * kChunkBytes;
-constexpr int kACols = kKStep / 2;                     // TMEM columns of A per tile per step
-constexpr int kDCol = 4 * kACols;                      // accumulators after 2 tiles x 2 buffers of A
+constexpr int kStageBytes = kBStageBytes + kChunkBytes;
+constexpr int kACols = kKStep / 2;                     // TMEM columns of A per step
+constexpr int kDCol = 2 * kACols;                      // accumulator after 2 buffers of A
 constexpr uint32_t kTmemCols = 512;
 constexpr int kThreads = 192;
 constexpr uint32_t kSpinLimit = 1u << 28;
@@ -57,7 +57,7 @@ struct Member {
   int64_t rows;
   int32_t wc;           // 4-word chunks per row
   int32_t row_tiles;
-  int32_t cta_begin;    // first blockIdx.x of this member (one CTA per pair of row tiles)
+  int32_t cta_begin;    // first blockIdx.x of this member (one CTA per row tile)
   int32_t k_steps;      // K steps of 128 columns
   const void *row_scale;  // mid (stage 1) / post (stage 2)
   const int32_t *exps;    // per-token exponent e of the fp16 activations
@@ -72,6 +72,7 @@ struct Member {
   const void *outlier_values;
   int32_t outlier_value_dtype;
   const void *outlier_scales;
+  int32_t tma_store;  // 1: write the tile with one TMA store through shared memory
 };
 
 struct Params {
@@ -96,10 +97,10 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   return d;
 }
 
-__host__ __device__ constexpr uint32_t idesc_f16_m128_n128() {
+__host__ __device__ constexpr uint32_t idesc_f16_m128(uint32_t n) {
   return (1u << 4)                // D: f32
          | (0u << 7) | (0u << 10)  // A, B: f16
-         | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+         | ((n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -119,6 +120,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int32_t x, int32_t y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -159,10 +169,13 @@ __device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr) {
 template <bool kStage2>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map0,
-                        const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2) {
+                        const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2,
+                        const __grid_constant__ CUtensorMap out0, const __grid_constant__ CUtensorMap out1,
+                        const __grid_constant__ CUtensorMap out2) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full[kStages], empty[kStages], a_full[2], a_empty[2], d_full;
   __shared__ uint32_t s_tmem;
+  __shared__ float s_unscale[kTokTile];  // 2^-e of each token of the tile (0 past the last token)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x;
@@ -174,8 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (static_cast<int32_t>(blockIdx.x) >= p.m[i].cta_begin) g = i;
   const Member &m = p.m[g];
   const CUtensorMap *map = g == 0 ? &map0 : (g == 1 ? &map1 : &map2);
-  const int tile0 = 2 * (static_cast<int>(blockIdx.x) - m.cta_begin);
-  const int ntiles = (tile0 + 1 < m.row_tiles) ? 2 : 1;
+  const CUtensorMap *out_map = g == 0 ? &out0 : (g == 1 ? &out1 : &out2);
+  const int tile0 = static_cast<int>(blockIdx.x) - m.cta_begin;
   const int tok0 = static_cast<int>(blockIdx.y) * kTokTile;
   const int K = m.k_steps;
 
@@ -195,6 +208,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tmem_alloc(&s_tmem, kTmemCols);
     ptx::tmem_relinquish();
   }
+  for (int i = tid; i < kTokTile; i += kThreads) {
+    const int64_t tok = tok0 + i;
+    s_unscale[i] = tok < p.tokens ? exp2_int(-m.exps[tok]) : 0.0f;
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -203,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     if (lane == 0) {  // producer
-      const uint32_t bytes = kBStageBytes + ntiles * kChunkBytes;
+      const uint32_t bytes = kStageBytes;
       for (int s = 0; s < K; ++s) {
         const int slot = s % kStages;
         if (s >= kStages && !ptx::mbar_wait_bounded(&empty[slot], ((s / kStages) - 1) & 1, kSpinLimit)) ok = false;
@@ -212,16 +229,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         expect_tx(&full[slot], bytes);
         tma_load_2d(base, map, s * kKStep, tok0, bar);
         tma_load_2d(base + kAtomBytes, map, s * kKStep + 64, tok0, bar);
-        for (int t = 0; t < ntiles; ++t) {
-          const uint8_t *src = reinterpret_cast<const uint8_t *>(m.tiles) +
-                               (static_cast<size_t>(tile0 + t) * m.wc + s) * kChunkBytes;
-          bulk_load(base + kBStageBytes + t * kChunkBytes, src, kChunkBytes, bar);
-        }
+        const uint8_t *src =
+            reinterpret_cast<const uint8_t *>(m.tiles) + (static_cast<size_t>(tile0) * m.wc + s) * kChunkBytes;
+        bulk_load(base + kBStageBytes, src, kChunkBytes, bar);
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {  // MMA issuer
-      const uint32_t idesc = idesc_f16_m128_n128();
+      const uint32_t idesc = idesc_f16_m128(kTokTile);
       for (int s = 0; s < K; ++s) {
         const int slot = s % kStages;
         const int buf = s & 1;
@@ -229,13 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ptx::mbar_wait_bounded(&a_full[buf], (s >> 1) & 1, kSpinLimit)) ok = false;
         ptx::tc_fence_after();
         const uint32_t bbase = ptx::smem_u32(smem + slot * kStageBytes);
-        for (int t = 0; t < ntiles; ++t) {
 #pragma unroll
-          for (int k16 = 0; k16 < kKStep / 16; ++k16) {
-            const uint64_t bdesc = desc_sw128(bbase + (k16 >> 2) * kAtomBytes + (k16 & 3) * 32);
-            mma_f16_ts(tmem + kDCol + t * kTokTile, tmem + buf * 2 * kACols + t * kACols + k16 * 8, bdesc, idesc,
-                       (s > 0 || k16 > 0) ? 1u : 0u);
-          }
+        for (int k16 = 0; k16 < kKStep / 16; ++k16) {
+          const uint64_t bdesc = desc_sw128(bbase + (k16 >> 2) * kAtomBytes + (k16 & 3) * 32);
+          mma_f16_ts(tmem + kDCol, tmem + buf * kACols + k16 * 8, bdesc, idesc, (s > 0 || k16 > 0) ? 1u : 0u);
         }
         ptx::mma_commit(&empty[slot]);
         ptx::mma_commit(&a_empty[buf]);
@@ -250,51 +262,84 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ptx::mbar_wait_bounded(&full[slot], (s / kStages) & 1, kSpinLimit)) ok = false;
       const uint4 *chunks = reinterpret_cast<const uint4 *>(smem + slot * kStageBytes + kBStageBytes);
       const uint4 c0 = chunks[tid];
-      const uint4 c1 = ntiles > 1 ? chunks[kTileRows + tid] : make_uint4(0, 0, 0, 0);
       if (s >= 2) {
         if (!ptx::mbar_wait_bounded(&a_empty[buf], ((s >> 1) - 1) & 1, kSpinLimit)) ok = false;
         ptx::tc_fence_after();
       }
-      const uint32_t a_addr = tmem + lane_base + buf * 2 * kACols;
-      expand_and_store(c0, a_addr);
-      if (ntiles > 1) expand_and_store(c1, a_addr + kACols);
+      expand_and_store(c0, tmem + lane_base + buf * kACols);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       mbar_arrive(&a_full[buf]);
     }
     if (!ptx::mbar_wait_bounded(&d_full, 0, kSpinLimit)) ok = false;
     ptx::tc_fence_after();
-    for (int t = 0; t < ntiles; ++t) {
-      const int64_t row = static_cast<int64_t>(tile0 + t) * kTileRows + tid;
-      const bool live = row < m.rows;
-      const float rscale = live ? load_as_float(m.row_scale, row, p.scale_dtype) : 0.0f;
-      float bias = 0.0f;
-      if constexpr (kStage2) {
-        if (live && m.bias != nullptr) bias = load_as_float(m.bias, row, m.bias_dtype);
+    // Epilogue.  Every value an output needs besides the accumulator is read
+    // from shared memory or registers: a global load between the global
+    // stores would be ordered behind them (possible aliasing) and serialise.
+    const int64_t row = static_cast<int64_t>(tile0) * kTileRows + tid;
+    const bool live = row < m.rows;
+    const float rscale = live ? load_as_float(m.row_scale, row, p.scale_dtype) : 0.0f;
+    float bias = 0.0f;
+    // stage 2 salient columns: x[tok0 + t][idx_s] staged (fp32) into the now idle
+    // pipeline buffers by the epilogue warps; this row's weights into registers
+    constexpr int kMaxStagedSalient = 64;  // 64 KB of the idle pipeline buffers
+    float *s_xs = reinterpret_cast<float *>(smem);
+    float *s_out = reinterpret_cast<float *>(smem + kMaxStagedSalient * kTokTile * 4);  // [token][row], 128 KB
+    int64_t staged = 0;
+    if constexpr (kStage2) {
+      if (live && m.bias != nullptr) bias = load_as_float(m.bias, row, m.bias_dtype);
+      staged = m.outlier_count <= kMaxStagedSalient ? m.outlier_count : 0;
+      for (int64_t i = tid; i < staged * kTokTile; i += kTileRows) {
+        const int64_t t = i / staged, sidx = i - t * staged;
+        const int64_t tok = tok0 + t;
+        s_xs[i] = tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx], p.x_dtype) : 0.0f;
       }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
+    }
 #pragma unroll 1
-      for (int c = 0; c < kTokTile / 16; ++c) {
-        uint32_t v[16];
-        ptx::tmem_ld16(tmem + lane_base + kDCol + t * kTokTile + c * 16, v);
-        ptx::tmem_wait_ld();
-        if (!live) continue;
+    for (int c = 0; c < kTokTile / 16; ++c) {
+      uint32_t v[16];
+      ptx::tmem_ld16(tmem + lane_base + kDCol + c * 16, v);
+      ptx::tmem_wait_ld();
+      float out[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int64_t tok = tok0 + c * 16 + e;
-          if (tok < p.tokens) {
-            float value = __uint_as_float(v[e]) * exp2_int(-m.exps[tok]) * rscale;
-            if constexpr (kStage2) {
-              for (int64_t s = 0; s < m.outlier_count; ++s) {
-                float w = load_as_float(m.outlier_values, row * m.outlier_count + s, m.outlier_value_dtype);
-                if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, s, p.scale_dtype);
-                value += load_as_float(p.x, tok * p.n + m.outlier_indices[s], p.x_dtype) * w;
-              }
-              value += bias;
+      for (int e = 0; e < 16; ++e) out[e] = __uint_as_float(v[e]) * s_unscale[c * 16 + e] * rscale + bias;
+      if constexpr (kStage2) {
+        if (live && m.outlier_count > 0) {
+          for (int64_t sidx = 0; sidx < m.outlier_count; ++sidx) {
+            float w = load_as_float(m.outlier_values, row * m.outlier_count + sidx, m.outlier_value_dtype);
+            if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, sidx, p.scale_dtype);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int t = c * 16 + e;
+              const int64_t tok = tok0 + t;
+              const float xv = sidx < staged ? s_xs[t * staged + sidx]
+                                             : (tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx],
+                                                                               p.x_dtype)
+                                                               : 0.0f);
+              out[e] += xv * w;
             }
-            m.out[tok * m.out_stride + m.out_offset + row] = value;
           }
         }
       }
+      if (m.tma_store) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) s_out[(c * 16 + e) * kTileRows + tid] = out[e];
+        continue;
+      }
+      if (!live) continue;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int64_t tok = tok0 + c * 16 + e;
+        if (tok < p.tokens) m.out[tok * m.out_stride + m.out_offset + row] = out[e];
+      }
+    }
+    if (m.tma_store) {
+      // The member's map starts at its first output column; rows past the
+      // member and tokens past `tokens` are clipped by the TMA unit.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (tid == 0) tma_store_2d(out_map, tile0 * kTileRows, tok0, ptx::smem_u32(s_out));
     }
   }
   if (!ok) atomicCAS(&g_pf_error, 0, NQB_ERR_TIMEOUT);
@@ -401,6 +446,27 @@ static int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 *out) {
   return NQB_OK;
 }
 
+// fp32 output [tokens][columns] with row stride `stride` floats, written as
+// 128-column x 256-token boxes from shared memory (no swizzle).
+static int encode_out_map(CUtensorMap *map, float *base, int64_t columns, int64_t stride, int64_t tokens) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  NQB_CHECK(tensor_map_encoder(&encode));
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(columns), static_cast<cuuint64_t>(tokens)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 4};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pf::kTileRows), static_cast<cuuint32_t>(pf::kTokTile)};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, elem,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NQB_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", static_cast<int>(r));
+  return NQB_OK;
+}
+
+// The TMA store needs a 16-byte aligned base and a row stride of whole 16-byte units.
+static bool tma_storable(const float *base, int64_t stride) {
+  return reinterpret_cast<uintptr_t>(base) % 16 == 0 && stride % 4 == 0;
+}
+
 static int encode_map(CUtensorMap *map, const void *base, int64_t k_pad, int64_t tokens) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   NQB_CHECK(tensor_map_encoder(&encode));
@@ -422,7 +488,8 @@ static int launch_gemm(const pf::Params &params, const CUtensorMap *maps, int ct
   const void *fn = reinterpret_cast<const void *>(pf::prefill_gemm_kernel<kStage2>);
   NQB_CHECK(ensure_dynamic_smem(fn, pf::kSmemBytes));
   const dim3 grid(ctas_x, static_cast<unsigned>((tokens + pf::kTokTile - 1) / pf::kTokTile));
-  pf::prefill_gemm_kernel<kStage2><<<grid, pf::kThreads, pf::kSmemBytes, stream>>>(params, maps[0], maps[1], maps[2]);
+  pf::prefill_gemm_kernel<kStage2><<<grid, pf::kThreads, pf::kSmemBytes, stream>>>(params, maps[0], maps[1], maps[2],
+                                                                                   maps[3], maps[4], maps[5]);
   NQB_CUDA(cudaGetLastError(), kStage2 ? "prefill stage 2 launch" : "prefill stage 1 launch");
   return NQB_OK;
 }
@@ -445,12 +512,14 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     exp2[i] = reinterpret_cast<int32_t *>(ws);
     ws += align_up(static_cast<size_t>(tokens) * 4, 256);
   }
-  int64_t total_rank = 0;
-  for (int i = 0; i < count; ++i) total_rank += layers[i].rank;
+  // latent members start on 16-byte boundaries (the workspace reserves each
+  // member's rank rounded up to 4 columns)
+  int64_t latent_stride = 0;
+  for (int i = 0; i < count; ++i) latent_stride += (layers[i].rank + 3) & ~int64_t(3);
   const int64_t n = layers[0].in_features;
 
   // ---- stage 1
-  CUtensorMap maps[3];
+  CUtensorMap maps[6];
   std::memset(maps, 0, sizeof(maps));
   pf::Params p1;
   std::memset(&p1, 0, sizeof(p1));
@@ -473,12 +542,15 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     m.row_scale = d.scale_mid;
     m.exps = exp1[i];
     m.out = latent;
-    m.out_stride = total_rank;
+    m.out_stride = latent_stride;
     m.out_offset = offset;
-    ctas += (m.row_tiles + 1) / 2;
-    offset += d.rank;
+    m.tma_store = tma_storable(latent + offset, latent_stride) ? 1 : 0;
+    if (m.tma_store) NQB_CHECK(encode_out_map(&maps[3 + i], latent + offset, d.rank, latent_stride, tokens));
+    ctas += m.row_tiles;
+    offset += (d.rank + 3) & ~int64_t(3);
   }
   for (int i = count; i < 3; ++i) maps[i] = maps[0];
+  for (int i = count; i < 3; ++i) maps[3 + i] = maps[3];
   p1.count = count;
   p1.tokens = tokens;
   p1.scale_dtype = layers[0].scale_dtype;
@@ -496,7 +568,7 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     const nqb_linear_desc &d = layers[i];
     const int64_t kp = k_pad_of(d.rank);
     pf::quantise_kernel<true><<<static_cast<unsigned>(tokens), 256, 0, stream>>>(
-        nullptr, 0, 0, nullptr, 0, latent, total_rank, offset, d.rank, kp, act2[i], exp2[i]);
+        nullptr, 0, 0, nullptr, 0, latent, latent_stride, offset, d.rank, kp, act2[i], exp2[i]);
     NQB_CUDA(cudaGetLastError(), "prefill quantise (stage 2) launch");
     NQB_CHECK(encode_map(&maps[i], act2[i], kp, tokens));
     pf::Member &m = p2.m[i];
@@ -518,10 +590,13 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     m.outlier_values = d.outlier_values;
     m.outlier_value_dtype = d.outlier_value_dtype;
     m.outlier_scales = d.outlier_scales;
-    ctas += (m.row_tiles + 1) / 2;
-    offset += d.rank;
+    m.tma_store = tma_storable(ys[i], d.out_features) ? 1 : 0;
+    if (m.tma_store) NQB_CHECK(encode_out_map(&maps[3 + i], ys[i], d.out_features, d.out_features, tokens));
+    ctas += m.row_tiles;
+    offset += (d.rank + 3) & ~int64_t(3);
   }
   for (int i = count; i < 3; ++i) maps[i] = maps[0];
+  for (int i = count; i < 3; ++i) maps[3 + i] = maps[3];
   p2.count = count;
   p2.tokens = tokens;
   p2.scale_dtype = layers[0].scale_dtype;

@@ -141,9 +141,24 @@ class DecodeChain:
 
     @property
     def launches_per_step(self) -> int:
-        """Kernel launches of one step: two stage launches per (grouped) call, four calls per layer."""
+        """libnqb kernel launches of one step.
 
-        return 8 * len(self.blocks)
+        Decode (tensor-core path): two stage kernels per call, four calls per
+        layer.  Prefill: per call two GEMM kernels plus one activation
+        pre-pass per member and stage (QKV 3 members, gate/up 2, o and down 1).
+        """
+
+        if self.tokens <= 16:
+            return 8 * len(self.blocks)
+        return (2 + 6 + 2 + 2 + 2 + 4 + 2 + 2) * len(self.blocks)
+
+    def algorithmic_flops(self) -> int:
+        """Multiply-adds x 2 of the two sign GEMMs of every linear: 2*r*(m+n) per token."""
+
+        total = 0
+        for n, m in self.shape.projections().values():
+            total += 2 * self.shape.rank(n, m) * (m + n) * self.tokens
+        return total * len(self.blocks)
 
     def algorithmic_bytes(self) -> int:
         """Weight bytes plus activation traffic (bf16 in, fp32 out) of one step."""
