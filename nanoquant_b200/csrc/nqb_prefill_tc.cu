@@ -19,15 +19,19 @@
 //   128-token x 64-column boxes into shared memory.
 // * One CTA owns one 128-row sign tile and one 256-token tile (MMA
 //   128 x 256 x 16); the K loop (128 columns per step) is pipelined over 3
-//   shared-memory stages of 64 KB: warp 4 issues TMA and the sign-chunk bulk
+//   shared-memory stages of 66 KB: warp 4 issues TMA and the sign-chunk bulk
 //   copy, warps 0-3 expand signs into a double-buffered A region of TMEM, one
 //   thread of warp 5 issues the 8 MMAs of a step and commits them to the
 //   stage's "empty" barriers.  The 128 x 256 fp32 accumulator stays in TMEM
-//   until the epilogue multiplies by 2^-e and the row scale and writes fp32.
+//   until the epilogue multiplies by 2^-e and the row scale, transposes the
+//   tile through the idle stage buffers and writes it with one TMA store.
+//   (Two co-resident 128 x 128 CTAs per SM measured slower: their main
+//   loops lose more than the overlapped epilogues gain.)
 // Every mbarrier wait is bounded; a timeout sets the device status word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "nqb_decode_tc.cuh"
@@ -47,13 +51,18 @@ constexpr int kChunkBytes = kTileRows * 16;            // one 4-word chunk of a 
 constexpr int kStageBytes = kBStageBytes + kChunkBytes;
 constexpr int kACols = kKStep / 2;                     // TMEM columns of A per step
 constexpr int kDCol = 2 * kACols;                      // accumulator after 2 buffers of A
-constexpr uint32_t kTmemCols = 512;
+constexpr int kCtasPerSm = 1;
+constexpr uint32_t kTmemCols = 512;  // 2 x 64 columns of signs + 256 accumulator columns (power of two)
 constexpr int kThreads = 192;
 constexpr uint32_t kSpinLimit = 1u << 28;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // +1024 for the swizzle alignment
+constexpr int kPreBytes = kKStep * 2;  // fp16 pre scales of one K step, pair order
+constexpr int kSmemBytes = kStages * (kStageBytes + kPreBytes) + 1024;  // +1024 for the swizzle alignment
+static_assert(kCtasPerSm * (kSmemBytes + 2048) <= 228 * 1024, "CTAs must fit one SM's shared memory");
+static_assert(kCtasPerSm * kTmemCols <= 512, "CTAs must fit one SM's tensor memory");
 
 struct Member {
   const uint4 *tiles;   // row-interleaved sign tiles (nqb_repack_signs)
+  const __half *pre_pairs;  // stage 1: fp16 pre scales [k_pad] in pair order, folded into the signs; or nullptr
   int64_t rows;
   int32_t wc;           // 4-word chunks per row
   int32_t row_tiles;
@@ -149,8 +158,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ float exp2_int(int e) { return __int_as_float((e + 127) << 23); }
 
 // Expands the four sign words of one row for one K step into 64 TMEM
-// columns (fp16 pairs) of this thread's lane.
-__device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr) {
+// columns (fp16 pairs) of this thread's lane.  Each pair is the fp16 pair
+// (s_j, s_j+16) with its sign bits flipped where the sign bit is 1: s = 1.0
+// without folded scales, else the pre scales of those two columns, so that
+// the MMA multiplies by +/-pre exactly (fp16 x fp16 products are exact in
+// the fp32 accumulator).
+__device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr, const uint4 *pre) {
   const uint32_t words[4] = {chunk.x, chunk.y, chunk.z, chunk.w};
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -158,8 +171,22 @@ __device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr) {
 #pragma unroll
     for (int wi = 0; wi < 2; ++wi) {
       const uint32_t w = words[half * 2 + wi];
+      uint32_t pp[16];
+      if (pre != nullptr) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[wi * 16 + j] = ((w << (15 - j)) & 0x80008000u) | 0x3C003C00u;
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = pre[(half * 2 + wi) * 4 + q];
+          pp[4 * q] = u.x;
+          pp[4 * q + 1] = u.y;
+          pp[4 * q + 2] = u.z;
+          pp[4 * q + 3] = u.w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pp[j] = 0x3C003C00u;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[wi * 16 + j] = ((w << (15 - j)) & 0x80008000u) ^ pp[j];
     }
     ptx::tmem_st16(taddr + half * 32, v);
     ptx::tmem_st16(taddr + half * 32 + 16, v + 16);
@@ -167,7 +194,7 @@ __device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr) {
 }
 
 template <bool kStage2>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     prefill_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map0,
                         const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2,
                         const __grid_constant__ CUtensorMap out0, const __grid_constant__ CUtensorMap out1,
@@ -220,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     if (lane == 0) {  // producer
-      const uint32_t bytes = kStageBytes;
+      const uint32_t bytes = kStageBytes + (m.pre_pairs != nullptr ? kPreBytes : 0);
       for (int s = 0; s < K; ++s) {
         const int slot = s % kStages;
         if (s >= kStages && !ptx::mbar_wait_bounded(&empty[slot], ((s / kStages) - 1) & 1, kSpinLimit)) ok = false;
@@ -232,6 +259,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t *src =
             reinterpret_cast<const uint8_t *>(m.tiles) + (static_cast<size_t>(tile0) * m.wc + s) * kChunkBytes;
         bulk_load(base + kBStageBytes, src, kChunkBytes, bar);
+        if (m.pre_pairs != nullptr)
+          bulk_load(ptx::smem_u32(smem + kStages * kStageBytes + slot * kPreBytes), m.pre_pairs + s * kKStep, kPreBytes,
+                    bar);
       }
     }
   } else if (warp == 5) {
@@ -266,7 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ptx::mbar_wait_bounded(&a_empty[buf], ((s >> 1) - 1) & 1, kSpinLimit)) ok = false;
         ptx::tc_fence_after();
       }
-      expand_and_store(c0, tmem + lane_base + buf * kACols);
+      const uint4 *pre = m.pre_pairs != nullptr
+                             ? reinterpret_cast<const uint4 *>(smem + kStages * kStageBytes + slot * kPreBytes)
+                             : nullptr;
+      expand_and_store(c0, tmem + lane_base + buf * kACols, pre);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       mbar_arrive(&a_full[buf]);
@@ -285,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kMaxStagedSalient = 64;  // 64 KB of the idle pipeline buffers
     float *s_xs = reinterpret_cast<float *>(smem);
     float *s_out = reinterpret_cast<float *>(smem + kMaxStagedSalient * kTokTile * 4);  // [token][row], 128 KB
+    static_assert((kMaxStagedSalient + kTileRows) * kTokTile * 4 <= kStages * kStageBytes, "epilogue buffers");
     int64_t staged = 0;
     if constexpr (kStage2) {
       if (live && m.bias != nullptr) bias = load_as_float(m.bias, row, m.bias_dtype);
@@ -297,41 +331,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
     }
 #pragma unroll 1
-    for (int c = 0; c < kTokTile / 16; ++c) {
-      uint32_t v[16];
-      ptx::tmem_ld16(tmem + lane_base + kDCol + c * 16, v);
+    for (int c2 = 0; c2 < kTokTile / 32; ++c2) {
+      // two TMEM loads in flight per wait; their registers are read only after it
+      uint32_t v32[32];
+      ptx::tmem_ld16(tmem + lane_base + kDCol + c2 * 32, v32);
+      ptx::tmem_ld16(tmem + lane_base + kDCol + c2 * 32 + 16, v32 + 16);
       ptx::tmem_wait_ld();
-      float out[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e) out[e] = __uint_as_float(v[e]) * s_unscale[c * 16 + e] * rscale + bias;
-      if constexpr (kStage2) {
-        if (live && m.outlier_count > 0) {
-          for (int64_t sidx = 0; sidx < m.outlier_count; ++sidx) {
-            float w = load_as_float(m.outlier_values, row * m.outlier_count + sidx, m.outlier_value_dtype);
-            if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, sidx, p.scale_dtype);
+      for (int half = 0; half < 2; ++half) {
+        const int c = c2 * 2 + half;
+        const uint32_t *v = v32 + half * 16;
+        float out[16];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int t = c * 16 + e;
-              const int64_t tok = tok0 + t;
-              const float xv = sidx < staged ? s_xs[t * staged + sidx]
-                                             : (tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx],
-                                                                               p.x_dtype)
-                                                               : 0.0f);
-              out[e] += xv * w;
+        for (int e = 0; e < 16; ++e) out[e] = __uint_as_float(v[e]) * s_unscale[c * 16 + e] * rscale + bias;
+        if constexpr (kStage2) {
+          if (live && m.outlier_count > 0) {
+            for (int64_t sidx = 0; sidx < m.outlier_count; ++sidx) {
+              float w = load_as_float(m.outlier_values, row * m.outlier_count + sidx, m.outlier_value_dtype);
+              if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, sidx, p.scale_dtype);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int t = c * 16 + e;
+                const int64_t tok = tok0 + t;
+                const float xv = sidx < staged ? s_xs[t * staged + sidx]
+                                               : (tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx],
+                                                                                 p.x_dtype)
+                                                                 : 0.0f);
+                out[e] += xv * w;
+              }
             }
           }
         }
-      }
-      if (m.tma_store) {
+        if (m.tma_store) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) s_out[(c * 16 + e) * kTileRows + tid] = out[e];
-        continue;
-      }
-      if (!live) continue;
+          for (int e = 0; e < 16; ++e) s_out[(c * 16 + e) * kTileRows + tid] = out[e];
+          continue;
+        }
+        if (!live) continue;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int64_t tok = tok0 + c * 16 + e;
-        if (tok < p.tokens) m.out[tok * m.out_stride + m.out_offset + row] = out[e];
+        for (int e = 0; e < 16; ++e) {
+          const int64_t tok = tok0 + c * 16 + e;
+          if (tok < p.tokens) m.out[tok * m.out_stride + m.out_offset + row] = out[e];
+        }
       }
     }
     if (m.tma_store) {
@@ -348,44 +389,228 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) ptx::tmem_dealloc(tmem, kTmemCols);
 }
 
-// Pre-pass: per token, scale the activation row of one member by 2^e
-// (max |a| * 2^e < 2^15), convert to fp16 in pair order, record e.
-// Stage 1 reads x * pre, stage 2 the fp32 latent.
-template <bool kLatent>
-__global__ void __launch_bounds__(256) quantise_kernel(const void *x, int32_t x_dtype, int64_t n, const void *pre,
-                                                       int32_t scale_dtype, const float *latent, int64_t latent_stride,
-                                                       int64_t latent_offset, int64_t k_valid, int64_t k_pad,
-                                                       __half *out, int32_t *exps) {
-  __shared__ float s_max[8];
-  const int64_t t = blockIdx.x;
-  auto value = [&](int64_t col) -> float {
-    if (col >= k_valid) return 0.0f;
-    if constexpr (kLatent) {
-      return latent[t * latent_stride + latent_offset + col];
+// Pre-pass: per token and member, scale the activation row by 2^e
+// (max |a| * 2^e < 2^15, exact), convert to fp16 in pair order, record e.
+// Stage 1 reads x * pre (all members share x), stage 2 the fp32 latent
+// slice of each member.  One warp per token; lane l owns the 32-column
+// groups l, l + 32, ...; a group is read with 16-byte loads when it lies
+// whole inside the row and the row is 16-byte aligned.
+struct PrepMember {
+  const void *scale;   // per-column scale (stage 1: pre), nullptr for none
+  int64_t src_offset;  // first source column of the member
+  int64_t k_valid;     // source columns
+  int64_t k_pad;       // fp16 columns written (multiple of 128, zero past k_valid)
+  __half *out;         // [tokens][k_pad]
+  int32_t *exps;       // [tokens]
+};
+
+struct PrepParams {
+  PrepMember m[kMaxMembersTc];
+  int32_t count;
+  const void *src;
+  int32_t src_dtype;
+  int64_t src_stride;  // elements per token row
+  int32_t scale_dtype;
+  int32_t vec_src;     // token rows and member offsets are 16-byte aligned
+  int32_t vec_scale;   // every scale vector is 16-byte aligned
+  int64_t tokens;
+  // fp16 pre scales rewritten in pair order for the stage-1 sign expansion
+  // (CTA row i writes member i's copy; pairs_count = 0 for none)
+  int32_t pairs_count;
+  const __half *pairs_src[kMaxMembersTc];
+  __half *pairs_out[kMaxMembersTc];
+  int64_t pairs_valid;
+  int64_t pairs_pad;
+};
+
+__device__ __forceinline__ void unpack8(uint4 u, int32_t dt, float *v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (dt == NQB_BF16) {
+      v[2 * q] = __uint_as_float(w[q] << 16);
+      v[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
     } else {
-      return load_as_float(x, t * n + col, x_dtype) * load_as_float(pre, col, scale_dtype);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[q]));
+      v[2 * q] = f.x;
+      v[2 * q + 1] = f.y;
     }
-  };
+  }
+}
+
+// 32 consecutive values base[idx .. idx + 31] as float; entries at or past
+// `valid` read as 0.
+__device__ __forceinline__ void load_group(const void *base, int64_t idx, int32_t dt, int64_t valid, bool vec,
+                                           float *v) {
+  if (vec && valid >= 32) {
+    if (dt == NQB_F32) {
+      const float4 *p4 = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = __ldg(p4 + q);
+        v[4 * q] = f.x;
+        v[4 * q + 1] = f.y;
+        v[4 * q + 2] = f.z;
+        v[4 * q + 3] = f.w;
+      }
+    } else {
+      const uint4 *p4 = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + idx);
+      uint4 u[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) u[q] = __ldg(p4 + q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) unpack8(u[q], dt, v + 8 * q);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = e < valid ? load_as_float(base, idx + e, dt) : 0.0f;
+  }
+}
+
+__global__ void __launch_bounds__(256) prepare_kernel(const __grid_constant__ PrepParams p) {
+  const int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= p.tokens) return;
+  const bool vsrc = p.vec_src != 0, vscale = p.vec_scale != 0;
+  for (int i = 0; i < p.count; ++i) {
+    const PrepMember &m = p.m[i];
+    const int64_t row = t * p.src_stride + m.src_offset;
+    float mx = 0.0f;
+#pragma unroll 2
+    for (int64_t g = lane; g * 32 < m.k_valid; g += 32) {
+      float v[32], sc[32];
+      load_group(p.src, row + g * 32, p.src_dtype, m.k_valid - g * 32, vsrc, v);
+      if (m.scale != nullptr) {
+        load_group(m.scale, g * 32, p.scale_dtype, m.k_valid - g * 32, vscale, sc);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= sc[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(v[e]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    int e2 = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+      int ex;
+      frexpf(mx, &ex);
+      e2 = min(15 - ex, 126);
+    }
+    const float scale = exp2_int(e2);
+    uint4 *out = reinterpret_cast<uint4 *>(m.out + t * m.k_pad);
+#pragma unroll 2
+    for (int64_t g = lane; g * 32 < m.k_pad; g += 32) {
+      float v[32], sc[32];
+      const int64_t valid = m.k_valid - g * 32;
+      load_group(p.src, row + g * 32, p.src_dtype, valid, vsrc, v);
+      if (m.scale != nullptr) {
+        load_group(m.scale, g * 32, p.scale_dtype, valid, vscale, sc);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= sc[e];
+      }
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const __half2 h = __floats2half2_rn(v[j] * scale, v[j + 16] * scale);
+        w[j] = *reinterpret_cast<const uint32_t *>(&h);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) out[g * 4 + q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+    if (lane == 0) m.exps[t] = e2;
+  }
+}
+
+// 8 consecutive values base[idx .. idx + 7] as float; entries at or past
+// `valid` read as 0.  The vector form needs base + idx 16-byte aligned.
+__device__ __forceinline__ void load8(const void *base, int64_t idx, int32_t dt, int64_t valid, bool vec, float *v) {
+  if (vec && valid >= 8) {
+    if (dt == NQB_F32) {
+      const float4 *p4 = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + idx);
+      const float4 a = __ldg(p4), b = __ldg(p4 + 1);
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
+      unpack8(__ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + idx)), dt, v);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = e < valid ? load_as_float(base, idx + e, dt) : 0.0f;
+  }
+}
+
+// Row pre-pass, one CTA per (token, member) row held in registers.  Unit u
+// of a row is the 16 columns {32g + 8h + j, 32g + 16 + 8h + j : j < 8}
+// (g = u / 2, h = u % 2): exactly the fp16 positions [32g + 16h, +16) of the
+// pair order, so every thread loads and stores whole 16-byte vectors.
+constexpr int kPrepThreads = 128;
+
+template <int kUnits>
+__global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid_constant__ PrepParams p) {
+  __shared__ float s_max[kPrepThreads / 32];
+  const int64_t t = blockIdx.x;
+  const PrepMember &m = p.m[blockIdx.y];
+  const int64_t row = t * p.src_stride + m.src_offset;
+  const int64_t units = m.k_pad / 16;
+  const bool vsrc = p.vec_src != 0, vscale = p.vec_scale != 0;
+  const int tid = threadIdx.x;
+  float v[kUnits][16];
   float mx = 0.0f;
-  for (int64_t c = threadIdx.x; c < k_valid; c += blockDim.x) mx = fmaxf(mx, fabsf(value(c)));
+#pragma unroll
+  for (int i = 0; i < kUnits; ++i) {
+    const int64_t u = tid + i * kPrepThreads;
+    if (u < units) {
+      const int64_t c0 = (u >> 1) * 32 + (u & 1) * 8;
+      load8(p.src, row + c0, p.src_dtype, m.k_valid - c0, vsrc, v[i]);
+      load8(p.src, row + c0 + 16, p.src_dtype, m.k_valid - c0 - 16, vsrc, v[i] + 8);
+      if (m.scale != nullptr) {
+        float sc[16];
+        load8(m.scale, c0, p.scale_dtype, m.k_valid - c0, vscale, sc);
+        load8(m.scale, c0 + 16, p.scale_dtype, m.k_valid - c0 - 16, vscale, sc + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[i][e] *= sc[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) mx = fmaxf(mx, fabsf(v[i][e]));
+    }
+  }
+#pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-  if ((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = mx;
+  if ((tid & 31) == 0) s_max[tid >> 5] = mx;
   __syncthreads();
-  float v = s_max[0];
-  for (int i = 1; i < 8; ++i) v = fmaxf(v, s_max[i]);
-  int e = 0;
-  if (v > 0.0f && isfinite(v)) {
+  mx = s_max[0];
+#pragma unroll
+  for (int w = 1; w < kPrepThreads / 32; ++w) mx = fmaxf(mx, s_max[w]);
+  int e2 = 0;
+  if (mx > 0.0f && isfinite(mx)) {
     int ex;
-    frexpf(v, &ex);
-    e = min(15 - ex, 126);
+    frexpf(mx, &ex);
+    e2 = min(15 - ex, 126);
   }
-  const float scale = exp2_int(e);
-  for (int64_t pos = threadIdx.x; pos < k_pad; pos += blockDim.x) {
-    const int64_t group = pos & ~int64_t(31);
-    const int64_t col = group + ((pos & 31) >> 1) + ((pos & 1) << 4);
-    out[t * k_pad + pos] = __float2half_rn(value(col) * scale);
+  const float scale = exp2_int(e2);
+  uint4 *out = reinterpret_cast<uint4 *>(m.out + t * m.k_pad);
+#pragma unroll
+  for (int i = 0; i < kUnits; ++i) {
+    const int64_t u = tid + i * kPrepThreads;
+    if (u < units) {
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const __half2 h = __floats2half2_rn(v[i][j] * scale, v[i][j + 8] * scale);
+        w[j] = *reinterpret_cast<const uint32_t *>(&h);
+      }
+      out[2 * u] = make_uint4(w[0], w[1], w[2], w[3]);
+      out[2 * u + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
   }
-  if (threadIdx.x == 0) exps[t] = e;
+  if (tid == 0) m.exps[t] = e2;
+  if (blockIdx.y == 0 && t < p.pairs_count) {
+    const __half *src = p.pairs_src[t];
+    __half *dst = p.pairs_out[t];
+    for (int64_t pos = tid; pos < p.pairs_pad; pos += kPrepThreads) {
+      const int64_t col = (pos & ~int64_t(31)) + ((pos & 31) >> 1) + ((pos & 1) << 4);
+      dst[pos] = col < p.pairs_valid ? src[col] : __float2half_rn(0.0f);
+    }
+  }
 }
 
 // Int8 residual rows for the prefill path: y[t, ids[j]] += s[j] * sum_i R[j, i] x[t, i].
@@ -418,15 +643,50 @@ bool prefill_eligible(const nqb_linear_desc *layers, int count, int32_t x_dtype,
   return true;
 }
 
+// Longest row the register-resident pre-pass takes (8 units per thread).
+constexpr int64_t kRowKernelMaxCols = 8 * pf::kPrepThreads * 16;
+
+// With fp16 pre scales (and rows the row pre-pass takes) stage 1 folds pre
+// into the sign expansion, so all members read one fp16 copy of x.
+static bool fold_pre(const nqb_linear_desc *layers) {
+  return layers[0].scale_dtype == NQB_F16 && k_pad_of(layers[0].in_features) <= kRowKernelMaxCols;
+}
+
+// Byte offsets of the prefill buffers inside the path workspace.
+struct PrefillLayout {
+  size_t act1[kMaxMembersTc], exp1[kMaxMembersTc];    // stage-1 fp16 activations, exponents (one set if folded)
+  size_t act2[kMaxMembersTc], exp2[kMaxMembersTc];    // stage-2 fp16 latent, exponents
+  size_t pairs[kMaxMembersTc];                        // pair-ordered fp16 pre scales (folded only)
+  bool fold;
+  size_t total;
+};
+
+static PrefillLayout prefill_layout(const nqb_linear_desc *layers, int count, int64_t tokens) {
+  PrefillLayout l{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align_up(bytes, 256);
+    return at;
+  };
+  const size_t t = static_cast<size_t>(tokens);
+  l.fold = fold_pre(layers);
+  for (int i = 0; i < (l.fold ? 1 : count); ++i) {
+    l.act1[i] = take(t * k_pad_of(layers[i].in_features) * 2);
+    l.exp1[i] = take(t * 4);
+  }
+  for (int i = 0; i < count; ++i) {
+    l.act2[i] = take(t * k_pad_of(layers[i].rank) * 2);
+    l.exp2[i] = take(t * 4);
+    if (l.fold) l.pairs[i] = take(k_pad_of(layers[i].in_features) * 2);
+  }
+  l.total = off;
+  return l;
+}
+
 size_t prefill_workspace_bytes(const nqb_linear_desc *layers, int count, int64_t tokens) {
   if (!prefill_eligible(layers, count, NQB_F32, tokens)) return 0;
-  size_t total = 0;
-  for (int i = 0; i < count; ++i) {
-    total += align_up(static_cast<size_t>(tokens) * k_pad_of(layers[i].in_features) * 2, 256);  // stage-1 fp16
-    total += align_up(static_cast<size_t>(tokens) * k_pad_of(layers[i].rank) * 2, 256);         // stage-2 fp16
-    total += 2 * align_up(static_cast<size_t>(tokens) * 4, 256);                                 // exponents
-  }
-  return total;
+  return prefill_layout(layers, count, tokens).total;
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the
@@ -482,6 +742,27 @@ static int encode_map(CUtensorMap *map, const void *base, int64_t k_pad, int64_t
   return NQB_OK;
 }
 
+// Row pre-pass for rows up to kRowKernelMaxCols columns, else the warp-per-token one.
+static int launch_prepare(const pf::PrepParams &params, cudaStream_t stream, const char *what) {
+  int64_t units = 0;
+  for (int i = 0; i < params.count; ++i) units = std::max<int64_t>(units, params.m[i].k_pad / 16);
+  const dim3 grid(static_cast<unsigned>(params.tokens), static_cast<unsigned>(params.count));
+  if (units <= pf::kPrepThreads) {
+    pf::prepare_rows_kernel<1><<<grid, pf::kPrepThreads, 0, stream>>>(params);
+  } else if (units <= 2 * pf::kPrepThreads) {
+    pf::prepare_rows_kernel<2><<<grid, pf::kPrepThreads, 0, stream>>>(params);
+  } else if (units <= 4 * pf::kPrepThreads) {
+    pf::prepare_rows_kernel<4><<<grid, pf::kPrepThreads, 0, stream>>>(params);
+  } else if (units <= 8 * pf::kPrepThreads) {
+    pf::prepare_rows_kernel<8><<<grid, pf::kPrepThreads, 0, stream>>>(params);
+  } else {
+    if (params.pairs_count != 0) return fail(NQB_ERR_UNSUPPORTED, "folded pre scales need the row pre-pass");
+    pf::prepare_kernel<<<static_cast<unsigned>((params.tokens + 7) / 8), 256, 0, stream>>>(params);  // warp per token
+  }
+  NQB_CUDA(cudaGetLastError(), what);
+  return NQB_OK;
+}
+
 template <bool kStage2>
 static int launch_gemm(const pf::Params &params, const CUtensorMap *maps, int ctas_x, int64_t tokens,
                        cudaStream_t stream) {
@@ -500,17 +781,16 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
   if (extra_bytes < prefill_workspace_bytes(layers, count, tokens))
     return fail(NQB_ERR_WORKSPACE, "prefill workspace too small");
   char *ws = static_cast<char *>(extra);
-  __half *act1[kMaxMembersTc], *act2[kMaxMembersTc];
+  const PrefillLayout lay = prefill_layout(layers, count, tokens);
+  __half *act1[kMaxMembersTc], *act2[kMaxMembersTc], *pairs[kMaxMembersTc];
   int32_t *exp1[kMaxMembersTc], *exp2[kMaxMembersTc];
   for (int i = 0; i < count; ++i) {
-    act1[i] = reinterpret_cast<__half *>(ws);
-    ws += align_up(static_cast<size_t>(tokens) * k_pad_of(layers[i].in_features) * 2, 256);
-    act2[i] = reinterpret_cast<__half *>(ws);
-    ws += align_up(static_cast<size_t>(tokens) * k_pad_of(layers[i].rank) * 2, 256);
-    exp1[i] = reinterpret_cast<int32_t *>(ws);
-    ws += align_up(static_cast<size_t>(tokens) * 4, 256);
-    exp2[i] = reinterpret_cast<int32_t *>(ws);
-    ws += align_up(static_cast<size_t>(tokens) * 4, 256);
+    const int i1 = lay.fold ? 0 : i;
+    act1[i] = reinterpret_cast<__half *>(ws + lay.act1[i1]);
+    exp1[i] = reinterpret_cast<int32_t *>(ws + lay.exp1[i1]);
+    act2[i] = reinterpret_cast<__half *>(ws + lay.act2[i]);
+    exp2[i] = reinterpret_cast<int32_t *>(ws + lay.exp2[i]);
+    pairs[i] = lay.fold ? reinterpret_cast<__half *>(ws + lay.pairs[i]) : nullptr;
   }
   // latent members start on 16-byte boundaries (the workspace reserves each
   // member's rank rounded up to 4 columns)
@@ -525,15 +805,41 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
   std::memset(&p1, 0, sizeof(p1));
   int ctas = 0;
   int64_t offset = 0;
+  pf::PrepParams q1;
+  std::memset(&q1, 0, sizeof(q1));
+  q1.count = count;
+  q1.src = x;
+  q1.src_dtype = x_dtype;
+  q1.src_stride = n;
+  q1.scale_dtype = layers[0].scale_dtype;
+  q1.tokens = tokens;
+  q1.vec_src = (reinterpret_cast<uintptr_t>(x) % 16 == 0 && (n * dtype_size(x_dtype)) % 16 == 0) ? 1 : 0;
+  q1.vec_scale = 1;
+  if (lay.fold) {  // x alone; the pre scales go to the sign expansion in pair order
+    q1.count = 1;
+    q1.m[0] = pf::PrepMember{nullptr, 0, n, k_pad_of(n), act1[0], exp1[0]};
+    q1.pairs_count = count;
+    q1.pairs_valid = n;
+    q1.pairs_pad = k_pad_of(n);
+    for (int i = 0; i < count; ++i) {
+      q1.pairs_src[i] = static_cast<const __half *>(layers[i].scale_pre);
+      q1.pairs_out[i] = pairs[i];
+    }
+  } else {
+    for (int i = 0; i < count; ++i) {
+      const nqb_linear_desc &d = layers[i];
+      q1.m[i] = pf::PrepMember{d.scale_pre, 0, d.in_features, k_pad_of(d.in_features), act1[i], exp1[i]};
+      if (reinterpret_cast<uintptr_t>(d.scale_pre) % 16) q1.vec_scale = 0;
+    }
+  }
+  NQB_CHECK(launch_prepare(q1, stream, "prefill activation pre-pass (stage 1) launch"));
   for (int i = 0; i < count; ++i) {
     const nqb_linear_desc &d = layers[i];
     const int64_t kp = k_pad_of(d.in_features);
-    pf::quantise_kernel<false><<<static_cast<unsigned>(tokens), 256, 0, stream>>>(
-        x, x_dtype, n, d.scale_pre, d.scale_dtype, nullptr, 0, 0, d.in_features, kp, act1[i], exp1[i]);
-    NQB_CUDA(cudaGetLastError(), "prefill quantise (stage 1) launch");
     NQB_CHECK(encode_map(&maps[i], act1[i], kp, tokens));
     pf::Member &m = p1.m[i];
     m.tiles = static_cast<const uint4 *>(d.right_tiles);
+    m.pre_pairs = pairs[i];
     m.rows = d.rank;
     m.wc = repack_chunks(d.in_features);
     m.row_tiles = static_cast<int32_t>((d.rank + pf::kTileRows - 1) / pf::kTileRows);
@@ -564,12 +870,24 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
   std::memset(&p2, 0, sizeof(p2));
   ctas = 0;
   offset = 0;
+  pf::PrepParams q2;
+  std::memset(&q2, 0, sizeof(q2));
+  q2.count = count;
+  q2.src = latent;
+  q2.src_dtype = NQB_F32;
+  q2.src_stride = latent_stride;
+  q2.tokens = tokens;
+  q2.vec_src = reinterpret_cast<uintptr_t>(latent) % 16 == 0 ? 1 : 0;
+  for (int i = 0; i < count; ++i) {
+    const nqb_linear_desc &d = layers[i];
+    q2.m[i] = pf::PrepMember{nullptr, offset, d.rank, k_pad_of(d.rank), act2[i], exp2[i]};
+    offset += (d.rank + 3) & ~int64_t(3);
+  }
+  NQB_CHECK(launch_prepare(q2, stream, "prefill activation pre-pass (stage 2) launch"));
+  offset = 0;
   for (int i = 0; i < count; ++i) {
     const nqb_linear_desc &d = layers[i];
     const int64_t kp = k_pad_of(d.rank);
-    pf::quantise_kernel<true><<<static_cast<unsigned>(tokens), 256, 0, stream>>>(
-        nullptr, 0, 0, nullptr, 0, latent, latent_stride, offset, d.rank, kp, act2[i], exp2[i]);
-    NQB_CUDA(cudaGetLastError(), "prefill quantise (stage 2) launch");
     NQB_CHECK(encode_map(&maps[i], act2[i], kp, tokens));
     pf::Member &m = p2.m[i];
     m.tiles = static_cast<const uint4 *>(d.left_tiles);

@@ -144,13 +144,13 @@ class DecodeChain:
         """libnqb kernel launches of one step.
 
         Decode (tensor-core path): two stage kernels per call, four calls per
-        layer.  Prefill: per call two GEMM kernels plus one activation
-        pre-pass per member and stage (QKV 3 members, gate/up 2, o and down 1).
+        layer.  Prefill: per call and stage one activation pre-pass and one
+        GEMM kernel.
         """
 
         if self.tokens <= 16:
             return 8 * len(self.blocks)
-        return (2 + 6 + 2 + 2 + 2 + 4 + 2 + 2) * len(self.blocks)
+        return 16 * len(self.blocks)
 
     def algorithmic_flops(self) -> int:
         """Multiply-adds x 2 of the two sign GEMMs of every linear: 2*r*(m+n) per token."""

@@ -360,6 +360,52 @@ def test_prefill_path_matches_oracle(n: int, m: int, r: int, tokens: int) -> Non
     assert ctypes_status() == 0
 
 
+@pytest.mark.parametrize(("scale_dtype", "x_dtype"), ((torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                                      (torch.float16, torch.float16), (torch.float16, torch.float32)))
+def test_prefill_scale_and_input_dtypes(scale_dtype: torch.dtype, x_dtype: torch.dtype) -> None:
+    """fp16 pre scales are folded into the sign expansion; other dtypes are applied in the pre-pass."""
+
+    from nanoquant_b200.cuda_backend import kernel_path
+
+    state = _random_state(1152, 2048, 700, seed=5, outliers=2, bias=True, scale_dtype=scale_dtype)
+    backend = CudaPackedSm100Backend()
+    layer = backend.prepare(state, "cuda")
+    assert kernel_path(layer, 96) == "prefill"
+    x = torch.randn(96, 1152, generator=torch.Generator().manual_seed(3)).to(x_dtype)
+    got = backend.linear(x.cuda(), layer)
+    expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
+    assert _relative_max_error(got, expected) <= PREFILL_BOUND
+    assert ctypes_status() == 0
+
+
+def test_prefill_rows_longer_than_the_row_pre_pass() -> None:
+    """in_features past 16384 columns takes the warp-per-token pre-pass (pre not folded)."""
+
+    state = _random_state(16416, 160, 96, seed=9)
+    backend = CudaPackedSm100Backend()
+    layer = backend.prepare(state, "cuda")
+    x = torch.randn(20, 16416, generator=torch.Generator().manual_seed(4)).bfloat16()
+    got = backend.linear(x.cuda(), layer)
+    expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
+    assert _relative_max_error(got, expected) <= PREFILL_BOUND
+    assert ctypes_status() == 0
+
+
+def test_prefill_grouped_qkv_with_unaligned_ranks() -> None:
+    """Three members whose ranks are not multiples of 4: padded latent offsets, one TMA store map each."""
+
+    backend = CudaPackedSm100Backend()
+    states = (_random_state(1024, 1024, 450, seed=41), _random_state(1024, 256, 113, seed=42),
+              _random_state(1024, 256, 113, seed=43))
+    group = prepare_sm100_projection_group(tuple(backend.prepare(s, "cuda") for s in states))
+    x = torch.randn(300, 1024, generator=torch.Generator().manual_seed(5)).bfloat16()
+    outs = grouped_sm100_projection(x.cuda(), group)
+    for got, state in zip(outs, states):
+        expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
+        assert _relative_max_error(got, expected) <= PREFILL_BOUND
+    assert ctypes_status() == 0
+
+
 def test_prefill_grouped_projection_and_overlay() -> None:
     backend = CudaPackedSm100Backend()
     base = _random_state(1152, 6912, 987, seed=31)
