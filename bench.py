@@ -2,8 +2,10 @@
 
 One step = one decode token (batch 1, BASELINE config 2 shape) through the 36
 layers x {q,k,v,o,gate,up,down} packed binary low-rank linears at ~1 bpw,
-with the grouped QKV and gate/up calls of the reference's model shell, captured
-in one CUDA graph.  Weights are random layout-v1 words (875 MB, larger than
+with the grouped QKV and gate/up calls of the reference's model shell, run as
+one persistent decode program (a grid barrier between every stage, so the
+calls stay strictly ordered); ``--engine calls`` runs the per-call kernels
+captured in one CUDA graph instead.  Weights are random layout-v1 words (875 MB, larger than
 the 126 MB L2, so no L2 flush is needed between steps); activations are
 synthetic bf16 N(0,1).
 
@@ -212,6 +214,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--layers", type=int, default=None,
                         help="decoder layers in the step (default: all); fewer only for profiling runs")
+    parser.add_argument("--engine", choices=("program", "calls"), default=None,
+                        help="decode: one persistent program launch per step (default) or per-call kernels in a "
+                             "CUDA graph")
     parser.add_argument("--tokens", type=int, default=None,
                         help="prefill tokens per GPU (default: 8*4096 / GPUs); smaller only for profiling runs")
     args = parser.parse_args()
@@ -254,8 +259,9 @@ def main() -> None:
         tokens = spec["tokens_total"] // world
         if args.tokens is not None:
             tokens = args.tokens
-    chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device, tokens=tokens)
-    use_graph = args.workload == "decode"
+    chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device, tokens=tokens,
+                        engine=args.engine)
+    use_graph = args.workload == "decode" and chain.program is None
     if use_graph:
         chain.capture()
     run_step = chain.replay if use_graph else chain.step
@@ -344,6 +350,8 @@ def main() -> None:
             if world > 1 else "single",
             "l2": "weights larger than the 126 MB L2 (no flush)",
             "cuda_graph": use_graph,
+            "engine": "persistent program (one cooperative launch per step)" if chain.program is not None
+            else "per-call kernels",
         },
         "roofline": roofline,
         "e2e": {

@@ -230,6 +230,42 @@ int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtyp
  */
 int nqb_device_status(int32_t *status);
 
+/*
+ * Persistent decode program: a fixed, ordered sequence of packed-linear calls
+ * ("ops", each 1..3 layers sharing one input, 1..16 tokens) run by ONE
+ * cooperative launch with one CTA per SM.  Ops and their two stages execute
+ * strictly in order (a grid-wide barrier after every stage, so an op may read
+ * an earlier op's output); only the sign-word streaming runs ahead of the
+ * barriers.  It replaces the reference's CUDA-graph replay of per-linear
+ * kernels for a decode step (runtime/torch_model.py:300-340 captures the
+ * per-projection Triton launches; cuda_backend.py:286-330 is the per-call
+ * launcher): results equal the per-call nqb_linear / nqb_grouped_linear
+ * tensor-core path within fp32 reduction-order rounding.
+ *
+ * Every op must take the tensor-core decode path (nqb_linear_path ==
+ * NQB_PATH_TENSOR_CORE).  The x and y device pointers, the descriptors and
+ * the device arrays they point to are captured at create time and must stay
+ * valid while the program exists.  Run needs a workspace of
+ * nqb_program_workspace_bytes (256-byte aligned) whose first 16 KiB are zero
+ * before the first run (every run leaves them zero).
+ */
+typedef struct nqb_program_op {
+  const nqb_linear_desc *layers; /* count members sharing x */
+  int32_t count;                 /* 1..3 */
+  const void *x;                 /* [tokens, in_features], x_dtype */
+  int32_t x_dtype;
+  float *const *y;               /* count outputs [tokens, out_features] fp32 */
+} nqb_program_op;
+
+typedef struct nqb_program nqb_program;
+
+int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t tokens, nqb_program **program);
+int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes);
+int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream);
+int nqb_program_destroy(nqb_program *program);
+/* Launch shape of a created program: CTAs (one per SM used) and cluster size. */
+int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size);
+
 #ifdef __cplusplus
 }
 #endif

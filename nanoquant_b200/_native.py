@@ -83,6 +83,18 @@ class LinearDesc(ctypes.Structure):
 
 
 # name -> (restype, argtypes); every symbol declared in include/nqb.h
+class ProgramOp(ctypes.Structure):
+    """Mirror of ``nqb_program_op``."""
+
+    _fields_ = [
+        ("layers", ctypes.POINTER(LinearDesc)),
+        ("count", _i32),
+        ("x", _c_void_p),
+        ("x_dtype", _i32),
+        ("y", ctypes.POINTER(_c_void_p)),
+    ]
+
+
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_abi_version": (ctypes.c_int, []),
     "nqb_last_error": (ctypes.c_char_p, []),
@@ -123,6 +135,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_repack_bytes": (ctypes.c_int, [_i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
     "nqb_repack_signs": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p]),
     "nqb_device_status": (ctypes.c_int, [ctypes.POINTER(_i32)]),
+    "nqb_program_create": (ctypes.c_int, [ctypes.POINTER(ProgramOp), _i32, _i64, ctypes.POINTER(_c_void_p)]),
+    "nqb_program_workspace_bytes": (ctypes.c_int, [_c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_program_run": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_program_destroy": (ctypes.c_int, [_c_void_p]),
+    "nqb_program_shape": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "nqb_linear_path": (ctypes.c_int, [ctypes.POINTER(LinearDesc), _i32, _i32, _i64, ctypes.POINTER(_i32)]),
     "nqb_decode_product_codebook": (
         ctypes.c_int,

@@ -7,6 +7,7 @@
 #include "nqb_decode_tc.cuh"
 #include "nqb_generic.cuh"
 #include "nqb_prefill_tc.cuh"
+#include "nqb_program.cuh"
 
 namespace nqb {
 
@@ -406,9 +407,11 @@ int nqb_linear_path(const nqb_linear_desc *layers, int32_t count, int32_t x_dtyp
 int nqb_device_status(int32_t *status) {
   if (status == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "status is NULL");
   NQB_CHECK(tc_device_error(status));
-  int32_t prefill_status = 0;
+  int32_t prefill_status = 0, program_status = 0;
   NQB_CHECK(prefill_device_error(&prefill_status));
+  NQB_CHECK(program_device_error(&program_status));
   if (*status == NQB_OK) *status = prefill_status;
+  if (*status == NQB_OK) *status = program_status;
   return ok();
 }
 

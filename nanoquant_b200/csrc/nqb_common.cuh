@@ -41,7 +41,7 @@ int cuda_status(cudaError_t err, const char *what);
 int ensure_dynamic_smem(const void *kernel, size_t bytes);
 
 inline bool is_float_dtype(int32_t dt) { return dt == NQB_F32 || dt == NQB_F16 || dt == NQB_BF16; }
-inline size_t dtype_size(int32_t dt) {
+__host__ __device__ inline size_t dtype_size(int32_t dt) {
   switch (dt) {
     case NQB_F32: return 4;
     case NQB_F16: return 2;

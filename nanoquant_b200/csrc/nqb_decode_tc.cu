@@ -39,28 +39,13 @@
 #include <cstring>
 
 #include "nqb_decode_tc.cuh"
+#include "nqb_tc_decode.cuh"
 #include "nqb_tc_ptx.cuh"
 
 namespace nqb {
 namespace tc {
 
-constexpr int kThreads = 128;       // one thread per tile row (TMEM lane)
-constexpr int kTileRows = 128;      // MMA M
-constexpr int kStageWords = 8;      // sign words per row per pipeline stage
-constexpr int kStageCols = 256;     // input columns per stage
-constexpr int kChunkBytes = 16;     // one 4-word chunk of one row
-constexpr int kStageWeightBytes = kTileRows * 2 * kChunkBytes;  // 4 KB per stage
-constexpr int kClasses = 4;         // accumulators (bit weight 2^j)
-constexpr int kAStageCols = 64;     // TMEM columns of A per stage
-constexpr int kDCol = 2 * kAStageCols;  // first accumulator column
-constexpr int kMaxTokens = 16;
-constexpr int kMaxStagesPerCta = 8;  // <= 2048 input columns per CTA
-constexpr int kQuadsPerThread = kMaxStagesPerCta * 64 / kThreads;
-constexpr int kDigits = 3;
-constexpr int kMaxNPad = 48;
 constexpr uint32_t kSpinLimit = 1u << 28;
-
-__host__ __device__ constexpr int n_pad_for(int tokens) { return ((kDigits * tokens + 15) / 16) * 16; }
 
 struct Member {
   const uint4 *tiles;    // row-interleaved tiles of the sign matrix
@@ -119,107 +104,13 @@ __device__ __forceinline__ void allow_dependent_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Splits four fixed-point values into three signed base-256 digits each
-// (q = d0 + 256*d1 + 65536*d2, every digit in [-128, 127]) and packs digit k
-// of the four values, one byte per value, into w[k].
-__device__ __forceinline__ void split_digits(const int32_t (&q)[4], uint32_t (&w)[kDigits]) {
-  w[0] = w[1] = w[2] = 0;
-#pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    int32_t v = q[b];
-    const int32_t d0 = static_cast<int8_t>(v & 0xFF);
-    v = (v - d0) >> 8;
-    const int32_t d1 = static_cast<int8_t>(v & 0xFF);
-    const int32_t d2 = (v - d1) >> 8;
-    w[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * b);
-    w[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * b);
-    w[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * b);
-  }
-}
-
-// Input column of byte b of quad (stage sl, word i, bit class j, nibble s).
-__device__ __forceinline__ int quad_column(int sl, int i, int j, int s, int b) {
-  return sl * kStageCols + 32 * i + 8 * b + j + 4 * s;
-}
-
-// 2^e as a float, exactly, for e in [-126, 127].
-__device__ __forceinline__ float exp2_int(int e) { return __int_as_float((e + 127) << 23); }
-
-// Copies this CTA's K slice [k0, k0 + ncols) of the activations of every
-// token into shared memory as fp32 (zero past the valid columns): stage 1
-// x * pre, stage 2 the latent.  The dtype dispatch sits outside the loop and
-// each thread keeps 16 loads in flight before it stores any of them.
-constexpr int kStageBatch = 16;
-
-template <typename XT, typename ST>
-__device__ __forceinline__ void stage_input_slice(const XT *x, const ST *pre, int64_t n, int64_t k0, int ncols,
-                                                  int tokens, int64_t k_valid, float *out) {
-  const int total = tokens * ncols;
-  for (int base = threadIdx.x; base < total; base += kStageBatch * kThreads) {
-    float xv[kStageBatch], pv[kStageBatch];
-#pragma unroll
-    for (int u = 0; u < kStageBatch; ++u) {
-      const int i = base + u * kThreads;
-      xv[u] = 0.0f;
-      pv[u] = 0.0f;
-      if (i < total) {
-        const int t = i / ncols;
-        const int64_t col = k0 + (i - t * ncols);
-        if (col < k_valid) {
-          xv[u] = to_f32(x[static_cast<int64_t>(t) * n + col]);
-          pv[u] = to_f32(pre[col]);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kStageBatch; ++u) {
-      const int i = base + u * kThreads;
-      if (i < total) out[i] = xv[u] * pv[u];
-    }
-  }
-}
-
-template <typename XT>
-__device__ __forceinline__ void stage_input_slice_x(const Params &p, const Member &m, int64_t k0, int ncols,
-                                                    float *out) {
-  const XT *x = static_cast<const XT *>(p.x);
-  switch (p.scale_dtype) {
-    case NQB_F32: stage_input_slice(x, static_cast<const float *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
-    case NQB_F16: stage_input_slice(x, static_cast<const __half *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
-    default: stage_input_slice(x, static_cast<const __nv_bfloat16 *>(m.pre), p.n, k0, ncols, p.tokens, m.k_valid, out); break;
-  }
-}
-
 template <bool kStage2>
 __device__ __forceinline__ void stage_activations(const Params &p, const Member &m, int64_t k0, int ncols,
                                                   float *out) {
   if constexpr (kStage2) {
-    const int total = p.tokens * ncols;
-    for (int base = threadIdx.x; base < total; base += kStageBatch * kThreads) {
-      float v[kStageBatch];
-#pragma unroll
-      for (int u = 0; u < kStageBatch; ++u) {
-        const int i = base + u * kThreads;
-        v[u] = 0.0f;
-        if (i < total) {
-          const int t = i / ncols;
-          const int64_t col = k0 + (i - t * ncols);
-          if (col < m.k_valid)
-            v[u] = __ldcg(p.latent + static_cast<int64_t>(t) * p.latent_stride + m.act_offset + col);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kStageBatch; ++u) {
-        const int i = base + u * kThreads;
-        if (i < total) out[i] = v[u];
-      }
-    }
+    stage_latent_slice(p.latent, p.latent_stride, m.act_offset, k0, ncols, p.tokens, m.k_valid, out);
   } else {
-    switch (p.x_dtype) {
-      case NQB_F32: stage_input_slice_x<float>(p, m, k0, ncols, out); break;
-      case NQB_F16: stage_input_slice_x<__half>(p, m, k0, ncols, out); break;
-      default: stage_input_slice_x<__nv_bfloat16>(p, m, k0, ncols, out); break;
-    }
+    stage_x_slice(p.x, p.x_dtype, m.pre, p.scale_dtype, p.n, k0, ncols, p.tokens, m.k_valid, out);
   }
 }
 
@@ -231,10 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   __shared__ uint64_t s_bar_done;                    // all MMAs complete
   __shared__ uint64_t s_bar_w[kMaxStagesPerCta];     // stage weights landed
   __shared__ uint32_t s_tmem;
-  __shared__ int s_exp[kT];
-  __shared__ long long s_qsum[kT];
-  __shared__ float s_red_f[4 * kT];
-  __shared__ long long s_red_q[4 * kT];
+  __shared__ BImageScratch<kT> s_bi;
+  __shared__ float s_red_f[4];
   __shared__ int s_last;
 
   const int tid = threadIdx.x;
@@ -301,96 +190,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   // ---- quantise this K slice of the activations into the B image ---------
   const int64_t k0 = static_cast<int64_t>(st_begin) * kStageCols;
   {
-    const int ncols = nst * kStageCols;
-    const int nquads = nst * 64;
     float *s_act = reinterpret_cast<float *>(smem_b + nst * 8 * b_block);  // [T][ncols] fp32
-    stage_activations<kStage2>(p, m, k0, ncols, s_act);
+    stage_activations<kStage2>(p, m, k0, nst * kStageCols, s_act);
     __syncthreads();
-    // per-token maximum over the slice -> power-of-two scale 2^e
-    float mx[kT];
-#pragma unroll
-    for (int t = 0; t < kT; ++t) mx[t] = 0.0f;
-    for (int c = tid; c < ncols; c += kThreads) {
-#pragma unroll
-      for (int t = 0; t < kT; ++t)
-        if (t < T) mx[t] = fmaxf(mx[t], fabsf(s_act[t * ncols + c]));
-    }
-#pragma unroll
-    for (int t = 0; t < kT; ++t) {
-      if (t < T) {
-        float v = mx[t];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if (lane == 0) s_red_f[warp * kT + t] = v;
-      }
-    }
-    __syncthreads();
-    if (tid < T) {
-      const float v = fmaxf(fmaxf(s_red_f[tid], s_red_f[kT + tid]),
-                            fmaxf(s_red_f[2 * kT + tid], s_red_f[3 * kT + tid]));
-      int e = 0;
-      if (v > 0.0f && isfinite(v)) {
-        int ex;
-        frexpf(v, &ex);      // v < 2^ex
-        e = 22 - ex;         // |a * 2^e| < 2^22
-        e = min(e, 126);     // keep 2^e and 2^-e normal floats (only |a| < 2^-104 loses bits)
-      }
-      s_exp[tid] = e;
-    }
-    __syncthreads();
-    // quantise, split into digits, scatter into the MMA's K order
-    long long qsum[kT];
-#pragma unroll
-    for (int t = 0; t < kT; ++t) qsum[t] = 0;
-#pragma unroll
-    for (int i = 0; i < kQuadsPerThread; ++i) {
-      const int qd = tid + i * kThreads;
-      if (qd < nquads) {
-        const int sl = qd >> 6;
-        const int r = qd & 63;
-        const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
-        const uint32_t block = (static_cast<uint32_t>(sl) * 4 + j) * 2 + (wi >> 2);
-        const uint32_t pk = 4 * ((wi & 3) * 2 + s);  // first K position of the quad in its MMA
-        const int c0 = quad_column(sl, wi, j, s, 0);
-#pragma unroll
-        for (int t = 0; t < kT; ++t) {
-          if (t < T) {
-            const float scale = exp2_int(s_exp[t]);  // exact power of two
-            int32_t q[4];
-#pragma unroll
-            for (int bb = 0; bb < 4; ++bb) {
-              q[bb] = __float2int_rn(s_act[t * ncols + c0 + 8 * bb] * scale);
-              qsum[t] += q[bb];
-            }
-            uint32_t digits[kDigits];
-            split_digits(q, digits);
-#pragma unroll
-            for (int d = 0; d < kDigits; ++d) {
-              const uint32_t nrow = 3 * t + d;
-              const uint32_t offset =
-                  block * b_block + (nrow >> 3) * 256 + (pk >> 4) * 128 + (nrow & 7) * 16 + (pk & 15);
-              *reinterpret_cast<uint32_t *>(smem_b + offset) = digits[d];
-            }
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < kT; ++t) {
-      if (t < T) {
-        long long v = qsum[t];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) s_red_q[warp * kT + t] = v;
-      }
-    }
-    __syncthreads();
-    if (tid < T)
-      s_qsum[tid] = s_red_q[tid] + s_red_q[kT + tid] + s_red_q[2 * kT + tid] +
-                    s_red_q[3 * kT + tid];
+    build_b_image<kT>(s_act, nst, T, smem_b, b_block, s_bi);
   }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // B image -> tensor core (async proxy)
-  __syncthreads();
 
   // ---- main loop: bits -> TMEM (A), one tcgen05.mma per (class, half) per stage
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
@@ -401,22 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
     const int buf = sl & 1;
     if (!ptx::mbar_wait_bounded(&s_bar_w[sl], 0, kSpinLimit)) ok = false;
     const uint4 *wsrc = reinterpret_cast<const uint4 *>(smem_w + sl * kStageWeightBytes);
-    const uint4 c0 = wsrc[tid];
-    const uint4 c1 = wsrc[kTileRows + tid];
-    const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     uint32_t a[kAStageCols];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t w = words[i];
-      const uint32_t hi = w >> 4;
-#pragma unroll
-      for (int j = 0; j < kClasses; ++j) {
-        const uint32_t mask = 0x01010101u << j;
-        const int col = j * 16 + (i >> 2) * 8 + (i & 3) * 2;
-        a[col] = w & mask;
-        a[col + 1] = hi & mask;
-      }
-    }
+    expand_slice(wsrc[tid], wsrc[kTileRows + tid], a);
     if (sl >= 2) {
       if (!ptx::mbar_wait_bounded(&s_bar_a[buf], ((sl - 2) >> 1) & 1, kSpinLimit)) ok = false;
       ptx::tc_fence_after();
@@ -429,16 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
     __syncthreads();
     if (tid == 0) {
       ptx::tc_fence_after();
-#pragma unroll
-      for (int j = 0; j < kClasses; ++j) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t block = (static_cast<uint32_t>(sl) * 4 + j) * 2 + h;
-          const uint64_t bdesc = ptx::smem_desc_kmajor(b_base + block * b_block, 128, 256);
-          ptx::mma_i8_ts(tmem + kDCol + j * NP, tmem + buf * kAStageCols + j * 16 + h * 8, bdesc, idesc,
-                         (sl > 0 || h > 0) ? 1u : 0u);
-        }
-      }
+      issue_slice_mmas(tmem, buf, sl, b_base, b_block, idesc, NP, sl == 0);
       ptx::mma_commit(&s_bar_a[buf]);
     }
   }
@@ -451,29 +232,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   const int64_t row = static_cast<int64_t>(tile) * kTileRows + tid;
   {
     int32_t sacc[kNP];
-#pragma unroll
-    for (int n = 0; n < kNP; ++n) sacc[n] = 0;
-#pragma unroll
-    for (int j = 0; j < kClasses; ++j) {
-      uint32_t v[kNP];
-#pragma unroll
-      for (int qb = 0; qb < kNP / 16; ++qb)
-        if (qb * 16 < NP) ptx::tmem_ld16(tmem + lane_base + kDCol + j * NP + qb * 16, v + qb * 16);
-      ptx::tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < kNP; ++e)
-        if (e < NP) sacc[e] += static_cast<int32_t>(v[e]) >> j;
-    }
+    drain_accumulators<kNP>(tmem, lane_base, sacc);
     if (row < m.rows) {
 #pragma unroll
       for (int t = 0; t < kT; ++t) {
-        if (t < T) {
-          const long long st = static_cast<long long>(sacc[3 * t]) + 256ll * sacc[3 * t + 1] +
-                               65536ll * sacc[3 * t + 2];
-          // one rounding (int64 -> fp32), then an exact power-of-two scale
-          const float value = __ll2float_rn(s_qsum[t] - 2 * st) * exp2_int(-s_exp[t]);
-          p.partial[(static_cast<int64_t>(split) * T + t) * p.part_stride + m.out_offset + row] = value;
-        }
+        if (t < T)
+          p.partial[(static_cast<int64_t>(split) * T + t) * p.part_stride + m.out_offset + row] =
+              token_value<kNP>(sacc, t, s_bi.qsum[t], s_bi.exp[t]);
       }
     }
   }

@@ -1,0 +1,1032 @@
+// Persistent decode program of libnqb: a whole sequence of packed-linear
+// calls (1..16 tokens) in one cooperative launch.
+//
+// A decode step is a chain of small sign-matrix products; launched one kernel
+// per stage, each pays a launch, a prologue and several global-memory round
+// trips while the weights it streams take well under a microsecond.  Here one
+// CTA per SM runs every stage of every op in order:
+//
+// * Work.  The CTAs form clusters of 4.  For each stage the host assigns the
+//   128-row tiles to clusters (balanced by sign bytes); the 4 CTAs of a
+//   cluster split every tile's K range in quarters, so each tile's partial
+//   sums meet in distributed shared memory: CTA q writes its quarter into the
+//   tile's leader CTA (tile index mod 4), which adds the four in a fixed order
+//   and runs the epilogue (scale_mid -> latent; scale_post, salient columns,
+//   bias, int8 overlay rows -> y).  No global atomics, deterministic.
+// * Arithmetic.  Exact integer MMAs with register operands
+//   (nqb_mma_decode.cuh): activations quantised per (token, K chunk) to 22-bit
+//   fixed-point digits (B fragments in shared memory), sign bits expanded by
+//   one LOP3 per A-fragment register; 8 consumer warps x 16 rows per tile.
+// * Weights.  Sign words do not depend on activations, so a producer warp
+//   streams each CTA's 4 KB slices (256 columns x 128 rows) through a ring of
+//   bulk copies as far ahead as the ring allows, across stage barriers.  The
+//   host precomputes each CTA's slice addresses in consumption order; the
+//   addresses themselves arrive by bulk copy, 64 at a time.
+// * Order.  After every stage a grid barrier (one release add per CTA on a
+//   global counter, an acquire poll).  Activations are read through L2 after
+//   the barrier, so an op may consume an earlier op's output.  The producer
+//   warp never joins a barrier: cluster exchanges use mbarriers with remote
+//   arrivals, CTA-wide steps a named barrier of the consumer warps.
+// Every wait is bounded; a timeout sets the device status word and every
+// later grid barrier gives up at once, so a failed run ends (with wrong
+// results and NQB_ERR_TIMEOUT) instead of hanging.
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "nqb_decode_tc.cuh"
+#include "nqb_mma_decode.cuh"
+#include "nqb_program.cuh"
+#include "nqb_tc_decode.cuh"
+#include "nqb_tc_ptx.cuh"
+
+namespace nqb {
+namespace prog {
+
+using namespace tc;
+
+constexpr int kClusterSize = 4;
+constexpr int kMaxRing = 48;            // ring slots (4 KB each)
+constexpr int kAddrChunk = 64;          // slice addresses per bulk copy
+constexpr int kAddrSlots = 4;           // address chunks in flight
+constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kBarrierSpinLimit = 1u << 22;  // polls of the grid-barrier counter
+constexpr int kMaxDynamicSmem = 225 * 1024;
+
+struct MemberDev {
+  const uint8_t *tiles;  // row-interleaved sign tiles
+  int64_t rows;
+  int32_t wc;            // 4-word chunks per row
+  int32_t ks;            // 256-column slices per row
+  int64_t k_valid;
+  const float *pre;       // stage 1: activation scale (fp32 copy owned by the program)
+  const float *row_scale;  // stage 1: scale_mid; stage 2: scale_post (fp32 copies)
+  int64_t act_offset;    // stage 2: first latent column of the member
+  int64_t out_offset;    // stage 1: first latent column written
+  const float *bias;     // fp32 copy or nullptr
+  int64_t outlier_count;
+  const int32_t *outlier_indices;
+  const void *outlier_values;
+  int32_t outlier_value_dtype;
+  const void *outlier_scales;
+  int32_t outlier_scale_dtype;
+  int64_t overlay_rows;
+  const int32_t *overlay_row_ids;
+  const int8_t *overlay_values;
+  const void *overlay_scales;
+  int32_t overlay_scale_dtype;
+  float *y;
+};
+
+struct OpDev {
+  MemberDev s[2][kMaxMembersTc];  // [stage][member]
+  int32_t count;
+  const void *x;
+  int32_t x_dtype;
+  int64_t n;
+  int64_t latent_stride;
+};
+
+struct Item {
+  int32_t member;
+  int32_t tile;
+};
+
+struct Params {
+  const OpDev *ops;
+  int32_t stages;              // 2 * ops
+  int32_t clusters;
+  const int32_t *stage_items;  // [stages * clusters + 1] offsets into items
+  const Item *items;
+  const uint64_t *slice_addrs;  // per-CTA lists (each padded to kAddrChunk entries)
+  const int64_t *slice_begin;   // [ctas]
+  const int32_t *slice_count;   // [ctas]
+  const uint64_t *pf_lines;     // L2 lines each CTA reads in each stage besides signs and activations
+  const int32_t *pf_begin;      // [stages * ctas + 1]
+  float *latent;
+  uint32_t *counters;           // [0] grid barrier arrivals, [1] finished clusters
+  int32_t tokens;
+  int32_t ring;                 // ring slots
+  int32_t sc;                   // slices quantised at once
+  int32_t group;                // items per exchange group (4 x leader slots)
+  // dynamic shared memory offsets
+  uint32_t off_addr, off_b, off_act, off_acc, off_exch;
+};
+
+__device__ int g_prog_error;
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_prog_error, 0, code); }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_addr(const void *local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(ptx::smem_u32(local)), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(ptx::smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ptx::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   ptx::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(ptx::smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Arrive (release, cluster scope) on the mbarrier at the same offset in CTA `rank`.
+__device__ __forceinline__ void remote_arrive(uint64_t *bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr(bar, rank))
+               : "memory");
+}
+
+// Waits (acquire, cluster scope) for phase `parity` of a local mbarrier; bounded.
+__device__ __forceinline__ bool wait_cluster(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(ptx::smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Asynchronous 16-byte store into the shared memory of CTA `rank` (same
+// offset as `local`); completion is counted on that CTA's mbarrier `bar`.
+__device__ __forceinline__ void st_async_v4(const float *local, uint32_t rank, float4 v, uint64_t *bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          cluster_addr(local, rank)),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cluster_addr(bar, rank))
+      : "memory");
+}
+
+// L2 prefetch of [p, p + bytes) by the consumer threads (one line each).
+__device__ __forceinline__ void prefetch_range(const void *ptr, int64_t bytes) {
+  const char *base = static_cast<const char *>(ptr);
+  for (int64_t off = static_cast<int64_t>(threadIdx.x) * 128; off < bytes; off += static_cast<int64_t>(mmad::kThreads) * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+}
+
+// L2 prefetch of the lines stage g of this CTA reads besides sign words and
+// activations (pre and row scales, bias, input rows), from the host-built
+// list; consumer threads other than 0.
+__device__ __forceinline__ void prefetch_stage(const Params &p, int g) {
+  if (g >= p.stages) return;
+  const int cta = static_cast<int>(blockIdx.x);
+  const int b = p.pf_begin[g * static_cast<int>(gridDim.x) + cta];
+  const int e = p.pf_begin[g * static_cast<int>(gridDim.x) + cta + 1];
+  for (int i = b + static_cast<int>(threadIdx.x) - 1; i < e; i += mmad::kThreads - 1)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.pf_lines[i]));
+}
+
+// Grid barrier number `index` over every CTA of the grid (consumer warps;
+// thread 0 adds and polls, the others issue the prefetches of stage
+// `index` + 2 meanwhile).
+__device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index) {
+  uint32_t *counter = p.counters;
+  const uint32_t ctas = gridDim.x;
+  mmad::consumer_sync();
+  if (threadIdx.x != 0) prefetch_stage(p, static_cast<int>(index) + 2);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_gpu_add(counter, 1);
+    const uint32_t target = (index + 1) * ctas;
+    uint32_t polls = 0;
+    while (ld_acquire_gpu(counter) < target) {
+      if (++polls > kBarrierSpinLimit || *reinterpret_cast<volatile int *>(&g_prog_error) != 0) {
+        record_error(NQB_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  mmad::consumer_sync();
+}
+
+// The producer lane's view of this CTA's slice-address list.
+struct Producer {
+  const uint64_t *addrs;
+  int32_t count;
+  int32_t padded;
+  uint64_t *cache;      // [kAddrSlots][kAddrChunk]
+  uint64_t *addr_bar;   // [kAddrSlots]
+  uint8_t *ring;
+  uint64_t *full;       // [ring]
+  int32_t ring_slots;
+
+  __device__ void issue_addr_chunk(int chunk) const {
+    if (chunk * kAddrChunk >= padded) return;
+    uint64_t *bar = addr_bar + (chunk % kAddrSlots);
+    expect_tx(bar, kAddrChunk * 8);
+    bulk_load(cache + (chunk % kAddrSlots) * kAddrChunk, addrs + static_cast<int64_t>(chunk) * kAddrChunk,
+              kAddrChunk * 8, bar);
+  }
+
+  // Fill ring position `pos` (slot pos % ring) with slice `pos` of this CTA's list.
+  __device__ bool produce(int pos, int slot) const {
+    const int chunk = pos / kAddrChunk;
+    if (pos % kAddrChunk == 0 && chunk >= 1) issue_addr_chunk(chunk + kAddrSlots - 1);
+    const bool ok = ptx::mbar_wait_bounded(addr_bar + (chunk % kAddrSlots), (chunk / kAddrSlots) & 1, kSpinLimit);
+    const uint64_t src = cache[(chunk % kAddrSlots) * kAddrChunk + pos % kAddrChunk];
+    expect_tx(full + slot, kStageWeightBytes);
+    bulk_load(ring + static_cast<size_t>(slot) * kStageWeightBytes, reinterpret_cast<const void *>(src),
+              kStageWeightBytes, full + slot);
+    return ok;
+  }
+};
+
+constexpr int kBlockThreads = mmad::kThreads + 32;  // 8 consumer warps + 1 producer warp
+constexpr int kProducerWarp = mmad::kWarps;
+
+// Slices quantised at once (B fragments and activations held for them).
+__host__ __device__ constexpr int slices_per_chunk(int bucket) { return bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2); }
+
+// Tiles each CTA leads per exchange group: 16 KB of exchange buffer.
+__host__ __device__ constexpr int leader_slots(int bucket) {
+  return 16384 / (kClusterSize * bucket * kTileRows * 4) > 1 ? 16384 / (kClusterSize * bucket * kTileRows * 4) : 1;
+}
+
+template <int kT>
+__global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_constant__ Params p) {
+  constexpr int kNT = mmad::n_tiles(kT);
+  constexpr int kSets = mmad::acc_sets(kNT);
+  constexpr int kQPT = mmad::quads_per_thread(slices_per_chunk(kT));
+  constexpr int kLead = leader_slots(kT);  // tiles this CTA leads per exchange group
+  constexpr int kC = mmad::kThreads;  // consumer threads
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ uint64_t s_full[kMaxRing], s_empty[kMaxRing];
+  __shared__ uint64_t s_addr_bar[kAddrSlots];
+  __shared__ uint64_t s_x_full;  // this CTA's leader buffers hold every quarter (own expect_tx + st.async bytes)
+  __shared__ uint64_t s_x_free;  // every leader has read this CTA's quarters (one arrival per leader)
+  __shared__ mmad::Scratch<kT> s_sc;
+  __shared__ float s_red_f[mmad::kWarps];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const uint32_t cluster = cluster_id();
+  const int cta = static_cast<int>(blockIdx.x);
+  const int T = p.tokens;
+  const int R = p.ring;
+
+  uint8_t *ring = smem;
+  uint64_t *addr_cache = reinterpret_cast<uint64_t *>(smem + p.off_addr);
+  uint8_t *smem_b = smem + p.off_b;
+  float *s_act = reinterpret_cast<float *>(smem + p.off_act);
+  float *s_acc = reinterpret_cast<float *>(smem + p.off_acc);    // [group][T][128]
+  float *s_exch = reinterpret_cast<float *>(smem + p.off_exch);  // [group / 4][4][T][128]
+
+  if (tid == 0) {
+    for (int s = 0; s < R; ++s) {
+      ptx::mbar_init(&s_full[s], 1);
+      ptx::mbar_init(&s_empty[s], mmad::kWarps);
+    }
+    for (int s = 0; s < kAddrSlots; ++s) ptx::mbar_init(&s_addr_bar[s], 1);
+    ptx::mbar_init(&s_x_full, 1);
+    ptx::mbar_init(&s_x_free, kClusterSize);
+    ptx::fence_mbar_init();
+  }
+  cluster_sync();  // every CTA's barriers exist before any remote arrive
+
+  bool ok = true;
+  if (warp == kProducerWarp) {
+    // ---- producer: stream this CTA's sign slices through the ring, as far
+    // ahead as the ring allows, independent of the stage barriers
+    if (lane == 0) {
+      Producer prod;
+      prod.addrs = p.slice_addrs + p.slice_begin[cta];
+      prod.count = p.slice_count[cta];
+      prod.padded = ((prod.count + kAddrChunk - 1) / kAddrChunk) * kAddrChunk;
+      prod.cache = addr_cache;
+      prod.addr_bar = s_addr_bar;
+      prod.ring = ring;
+      prod.full = s_full;
+      prod.ring_slots = R;
+      for (int c = 0; c < kAddrSlots; ++c) prod.issue_addr_chunk(c);
+      int slot = 0;
+      uint32_t phase = 0;  // ring passes completed
+      for (int pos = 0; pos < prod.count; ++pos) {
+        if (phase > 0 && !ptx::mbar_wait_bounded(&s_empty[slot], (phase - 1) & 1, kSpinLimit)) ok = false;
+        ok &= prod.produce(pos, slot);
+        if (++slot == R) {
+          slot = 0;
+          ++phase;
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- consumers: 8 warps x 16 rows of the current 128-row tile
+    int slot = 0;         // ring slot of the next slice
+    uint32_t phase = 0;   // ring passes completed
+    uint32_t xg = 0;      // exchange groups done
+    if (tid != 0) {
+      prefetch_stage(p, 0);
+      prefetch_stage(p, 1);
+    }
+    for (int g = 0; g < p.stages; ++g) {
+      const OpDev &op = p.ops[g >> 1];
+      const int st = g & 1;
+      const int ib = p.stage_items[g * p.clusters + cluster];
+      const int ie = p.stage_items[g * p.clusters + cluster + 1];
+      for (int gb = ib; gb < ie; gb += p.group) {
+        const int ge = min(gb + p.group, ie);
+        for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
+        // ---- this CTA's quarter of every item of the group, member by member
+        for (int j0 = gb; j0 < ge;) {
+          const int mi = p.items[j0].member;
+          int j1 = j0 + 1;
+          while (j1 < ge && p.items[j1].member == mi) ++j1;
+          const MemberDev &md = op.s[st][mi];
+          const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
+          const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
+          for (int c0 = lo; c0 < hi; c0 += p.sc) {
+            const int nst = min(p.sc, hi - c0);
+            const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+            int e[kT];
+            long long Q[kT];
+            if (st == 1) {
+              const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+            } else if (op.x_dtype == NQB_BF16) {
+              const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
+                                                    md.k_valid};
+              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+            } else if (op.x_dtype == NQB_F16) {
+              const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
+              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+            } else {
+              const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
+              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+            }
+            for (int j = j0; j < j1; ++j) {
+              int32_t d[kSets][kNT][4];
+#pragma unroll
+              for (int c = 0; c < kSets; ++c)
+#pragma unroll
+                for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+                  for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
+              for (int sl = 0; sl < nst; ++sl) {
+                if (!ptx::mbar_wait_bounded(&s_full[slot], phase & 1, kSpinLimit)) ok = false;
+                const mmad::SliceWords w =
+                    mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+                if (++slot == R) {
+                  slot = 0;
+                  ++phase;
+                }
+                mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
+              }
+              mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
+            }
+          }
+          j0 = j1;
+        }
+        // ---- quarters -> leaders: asynchronous stores into their shared
+        // memory, counted on each leader's s_x_full
+        if (xg > 0 && !wait_cluster(&s_x_free, (xg - 1) & 1)) ok = false;
+        mmad::consumer_sync();  // every lane's accumulation is in s_acc
+        const int per_item = T * kTileRows;
+        if (tid == 0) {
+          const int led = (ge - gb - static_cast<int>(rank) + kClusterSize - 1) / kClusterSize;
+          expect_tx(&s_x_full, static_cast<uint32_t>(led > 0 ? led : 0) * kClusterSize * per_item * 4);
+        }
+        for (int i = tid * 4; i < (ge - gb) * per_item; i += kC * 4) {
+          const int jj = i / per_item;
+          const int rest = i - jj * per_item;
+          float *dst = s_exch + (static_cast<size_t>(jj / kClusterSize) * kClusterSize + rank) * per_item + rest;
+          st_async_v4(dst, static_cast<uint32_t>(jj % kClusterSize), *reinterpret_cast<const float4 *>(s_acc + i),
+                      &s_x_full);
+        }
+        // leaders load the row scales and bias of their tiles while the quarters land
+        float lead_scale[kLead], lead_bias[kLead];
+#pragma unroll
+        for (int sidx = 0; sidx < kLead; ++sidx) {
+          lead_scale[sidx] = 0.0f;
+          lead_bias[sidx] = 0.0f;
+          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+          if (jj < ge - gb && tid < kTileRows) {
+            const Item item = p.items[gb + jj];
+            const MemberDev &md = op.s[st][item.member];
+            const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
+            if (row < md.rows) {
+              lead_scale[sidx] = __ldg(md.row_scale + row);
+              if (md.bias != nullptr) lead_bias[sidx] = __ldg(md.bias + row);
+            }
+          }
+        }
+        if (!wait_cluster(&s_x_full, xg & 1)) ok = false;
+        // ---- leaders: fixed-order sum of the four quarters, epilogue
+#pragma unroll
+        for (int sidx = 0; sidx < kLead; ++sidx) {
+          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+          if (jj >= ge - gb) break;
+          const Item item = p.items[gb + jj];
+          const MemberDev &md = op.s[st][item.member];
+          const float *ex = s_exch + static_cast<size_t>(sidx) * kClusterSize * per_item;
+          if (tid < kTileRows) {
+            const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
+            if (row < md.rows) {
+              for (int t = 0; t < T; ++t) {
+                float v = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kClusterSize; ++q) v += ex[(q * T + t) * kTileRows + tid];
+                if (st == 0) {
+                  p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * lead_scale[sidx];
+                } else {
+                  v *= lead_scale[sidx];
+                  if (md.outlier_count > 0) {
+                    float sal = 0.0f;
+                    for (int64_t s = 0; s < md.outlier_count; ++s) {
+                      float w = load_as_float(md.outlier_values, row * md.outlier_count + s, md.outlier_value_dtype);
+                      if (md.outlier_scales != nullptr) w *= load_as_float(md.outlier_scales, s, md.outlier_scale_dtype);
+                      sal += load_as_float(op.x, static_cast<int64_t>(t) * op.n + md.outlier_indices[s], op.x_dtype) *
+                             w;
+                    }
+                    v += sal;
+                  }
+                  md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
+                }
+              }
+            }
+          }
+          if (st == 1 && md.overlay_rows > 0) {
+            // int8 residual rows of this tile: all consumer threads compute each dot product
+            mmad::consumer_sync();
+            const int64_t first = static_cast<int64_t>(item.tile) * kTileRows;
+            const int64_t last = min(first + kTileRows, md.rows);
+            int64_t lo = 0, hi = md.overlay_rows;
+            while (lo < hi) {
+              const int64_t mid = (lo + hi) >> 1;
+              if (md.overlay_row_ids[mid] < first) lo = mid + 1; else hi = mid;
+            }
+            for (int64_t jr = lo; jr < md.overlay_rows && md.overlay_row_ids[jr] < last; ++jr) {
+              const int64_t orow = md.overlay_row_ids[jr];
+              const float oscale = load_as_float(md.overlay_scales, jr, md.overlay_scale_dtype);
+              const int8_t *rv = md.overlay_values + jr * op.n;
+              for (int t = 0; t < T; ++t) {
+                float part = 0.0f;
+                for (int64_t i = tid; i < op.n; i += kC)
+                  part += static_cast<float>(rv[i]) * load_as_float(op.x, static_cast<int64_t>(t) * op.n + i, op.x_dtype);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+                if (lane == 0) s_red_f[warp] = part;
+                mmad::consumer_sync();
+                if (tid == 0) {
+                  float dot = 0.0f;
+#pragma unroll
+                  for (int w = 0; w < mmad::kWarps; ++w) dot += s_red_f[w];
+                  md.y[static_cast<int64_t>(t) * md.rows + orow] += dot * oscale;
+                }
+                mmad::consumer_sync();
+              }
+            }
+          }
+        }
+        mmad::consumer_sync();  // done reading this CTA's leader buffers
+        if (tid == 0)
+          for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive(&s_x_free, r);
+        ++xg;
+      }
+      if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g));
+    }
+  }
+
+  if (!ok) record_error(NQB_ERR_TIMEOUT);
+  // every CTA stays until its peers have made their last remote arrivals
+  cluster_sync();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t finished = atomicAdd(p.counters + 1, 1u);
+    if (finished == gridDim.x - 1) {  // the last CTA zeroes the counters for the next run
+      p.counters[0] = 0;
+      p.counters[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+// fp32 copy of a scale / bias vector (program create time).
+__global__ void to_f32_kernel(const void *src, int32_t dtype, int64_t n, float *dst) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = load_as_float(src, i, dtype);
+}
+
+}  // namespace prog
+}  // namespace nqb
+
+// --------------------------------------------------------------- host ---
+
+using namespace nqb;
+
+struct nqb_program {
+  int device = 0;
+  float *scales = nullptr;  // fp32 copies of every pre / mid / post / bias vector
+  int64_t tokens = 0;
+  int bucket = 1;
+  int ctas = 0;
+  int clusters = 0;
+  int smem = 0;
+  void *arena = nullptr;
+  size_t latent_bytes = 0;
+  prog::Params params{};
+};
+
+namespace nqb {
+namespace prog {
+
+static int token_bucket(int64_t tokens) {
+  return tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : tokens <= 8 ? 8 : 16;
+}
+
+struct SmemPlan {
+  int sc, group, ring;
+  uint32_t off_addr, off_b, off_act, off_acc, off_exch, total;
+};
+
+static SmemPlan smem_plan(int bucket) {
+  SmemPlan s{};
+  s.sc = slices_per_chunk(bucket);
+  const int lead = leader_slots(bucket);
+  s.group = kClusterSize * lead;
+  const uint32_t addr = kAddrSlots * kAddrChunk * 8;
+  const uint32_t b = static_cast<uint32_t>(s.sc) * mmad::slice_frag_bytes(mmad::n_tiles(bucket));
+  const uint32_t act = static_cast<uint32_t>(bucket) * s.sc * kStageCols * 4;
+  const uint32_t acc = static_cast<uint32_t>(s.group) * bucket * kTileRows * 4;
+  const uint32_t exch = static_cast<uint32_t>(lead) * kClusterSize * bucket * kTileRows * 4;
+  const uint32_t rest = addr + b + act + acc + exch;
+  s.ring = std::min<int>(kMaxRing, static_cast<int>((kMaxDynamicSmem - rest) / kStageWeightBytes));
+  uint32_t off = static_cast<uint32_t>(s.ring) * kStageWeightBytes;
+  s.off_addr = off;
+  off += addr;
+  s.off_b = off;
+  off += b;
+  s.off_act = off;
+  off += act;
+  s.off_acc = off;
+  off += acc;
+  s.off_exch = off;
+  off += exch;
+  s.total = off;
+  return s;
+}
+
+static const void *kernel_for(int bucket) {
+  switch (bucket) {
+    case 1: return reinterpret_cast<const void *>(program_kernel<1>);
+    case 2: return reinterpret_cast<const void *>(program_kernel<2>);
+    case 4: return reinterpret_cast<const void *>(program_kernel<4>);
+    case 8: return reinterpret_cast<const void *>(program_kernel<8>);
+    default: return reinterpret_cast<const void *>(program_kernel<16>);
+  }
+}
+
+// `pre`, `row_scale` and `bias` are the program's fp32 copies of the layer's vectors.
+static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64_t rank_offset, float *y,
+                        const float *pre, const float *row_scale, const float *bias) {
+  std::memset(&m, 0, sizeof(m));
+  m.row_scale = row_scale;
+  if (stage == 0) {
+    m.tiles = static_cast<const uint8_t *>(d.right_tiles);
+    m.rows = d.rank;
+    m.wc = repack_chunks(d.in_features);
+    m.k_valid = d.in_features;
+    m.pre = pre;
+    m.out_offset = rank_offset;
+  } else {
+    m.tiles = static_cast<const uint8_t *>(d.left_tiles);
+    m.rows = d.out_features;
+    m.wc = repack_chunks(d.rank);
+    m.k_valid = d.rank;
+    m.act_offset = rank_offset;
+    m.bias = bias;
+    m.outlier_count = d.outlier_count;
+    m.outlier_indices = d.outlier_indices;
+    m.outlier_values = d.outlier_values;
+    m.outlier_value_dtype = d.outlier_value_dtype;
+    m.outlier_scales = d.outlier_scales;
+    m.outlier_scale_dtype = d.scale_dtype;
+    m.overlay_rows = d.overlay_rows;
+    m.overlay_row_ids = d.overlay_row_ids;
+    m.overlay_values = d.overlay_values;
+    m.overlay_scales = d.overlay_scales;
+    m.overlay_scale_dtype = d.overlay_scale_dtype;
+    m.y = y;
+  }
+  m.ks = m.wc / 2;
+}
+
+// Assigns a stage's tiles to clusters (largest cost first onto the least
+// loaded cluster), then orders each cluster's tiles by member and tile.
+static void assign_stage(const OpDev &op, int stage, int clusters, std::vector<std::vector<Item>> &out) {
+  struct Cand {
+    Item item;
+    int cost;
+  };
+  std::vector<Cand> cands;
+  for (int mi = 0; mi < op.count; ++mi) {
+    const MemberDev &m = op.s[stage][mi];
+    const int tiles = static_cast<int>((m.rows + kTileRows - 1) / kTileRows);
+    for (int t = 0; t < tiles; ++t) cands.push_back({{mi, t}, m.ks});
+  }
+  std::stable_sort(cands.begin(), cands.end(), [](const Cand &a, const Cand &b) { return a.cost > b.cost; });
+  std::vector<int64_t> load(clusters, 0);
+  out.assign(clusters, {});
+  for (const Cand &c : cands) {
+    const int best = static_cast<int>(std::min_element(load.begin(), load.end()) - load.begin());
+    load[best] += c.cost;
+    out[best].push_back(c.item);
+  }
+  for (auto &list : out)
+    std::sort(list.begin(), list.end(), [](const Item &a, const Item &b) {
+      return a.member != b.member ? a.member < b.member : a.tile < b.tile;
+    });
+}
+
+}  // namespace prog
+
+int program_device_error(int32_t *out) {
+  int value = 0;
+  NQB_CUDA(cudaMemcpyFromSymbol(&value, prog::g_prog_error, sizeof(int)), "read program error flag");
+  *out = value;
+  const int zero = 0;
+  NQB_CUDA(cudaMemcpyToSymbol(prog::g_prog_error, &zero, sizeof(int)), "clear program error flag");
+  return NQB_OK;
+}
+
+}  // namespace nqb
+
+extern "C" {
+
+int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t tokens, nqb_program **program) {
+  using namespace nqb::prog;
+  if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
+  *program = nullptr;
+  if (ops == nullptr || op_count < 1) return fail(NQB_ERR_INVALID_ARGUMENT, "a program needs at least one op");
+  if (tokens < 1 || tokens > kMaxTokens) return fail(NQB_ERR_UNSUPPORTED, "programs take 1 to %d tokens", kMaxTokens);
+  const int bucket = token_bucket(tokens);
+  std::vector<OpDev> opdev(op_count);
+  int64_t latent_cols = 0;
+  for (int i = 0; i < op_count; ++i) {
+    const nqb_program_op &o = ops[i];
+    if (o.layers == nullptr || o.count < 1 || o.count > kMaxMembersTc)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: 1 to %d layers", i, kMaxMembersTc);
+    if (o.x == nullptr || o.y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: x or y is NULL", i);
+    int64_t rank_total = 0;
+    for (int k = 0; k < o.count; ++k) {
+      const nqb_linear_desc &d = o.layers[k];
+      if (d.in_features != o.layers[0].in_features || d.scale_dtype != o.layers[0].scale_dtype)
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: members must share in_features and scale dtype", i);
+      if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
+      if (d.codebook_free_rows > 0) return fail(NQB_ERR_UNSUPPORTED, "op %d: compact codebook layers", i);
+      rank_total += d.rank;
+    }
+    if (!tc_eligible(o.layers, o.count, o.x_dtype, tokens))
+      return fail(NQB_ERR_UNSUPPORTED, "op %d does not take the tensor-core decode path", i);
+    latent_cols = std::max(latent_cols, rank_total);
+  }
+
+  // fp32 copies of the scale and bias vectors, so the kernel reads them with
+  // plain loads (no per-element dtype dispatch)
+  struct VecCopy {
+    const void *src;
+    int32_t dtype;
+    int64_t n;
+    size_t offset;
+  };
+  std::vector<VecCopy> copies;
+  size_t scale_floats = 0;
+  auto add_copy = [&](const void *src, int32_t dtype, int64_t n) -> size_t {
+    if (src == nullptr) return SIZE_MAX;
+    const size_t at = (scale_floats + 63) & ~size_t(63);
+    copies.push_back({src, dtype, n, at});
+    scale_floats = at + static_cast<size_t>(n);
+    return at;
+  };
+  struct MemberScales {
+    size_t pre, mid, post, bias;
+  };
+  std::vector<MemberScales> member_scales;
+  for (int i = 0; i < op_count; ++i)
+    for (int k = 0; k < ops[i].count; ++k) {
+      const nqb_linear_desc &d = ops[i].layers[k];
+      MemberScales ms;
+      ms.pre = add_copy(d.scale_pre, d.scale_dtype, d.in_features);
+      ms.mid = add_copy(d.scale_mid, d.scale_dtype, d.rank);
+      ms.post = add_copy(d.scale_post, d.scale_dtype, d.out_features);
+      ms.bias = add_copy(d.bias, d.bias_dtype, d.out_features);
+      member_scales.push_back(ms);
+    }
+  float *scales = nullptr;
+  if (cudaMalloc(&scales, std::max<size_t>(scale_floats, 64) * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NQB_ERR_CUDA, "cudaMalloc of the program's fp32 scale copies failed");
+  }
+  for (const VecCopy &c : copies) {
+    const int64_t blocks = std::min<int64_t>((c.n + 255) / 256, 1024);
+    to_f32_kernel<<<static_cast<unsigned>(blocks), 256>>>(c.src, c.dtype, c.n, scales + c.offset);
+  }
+  if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(scales);
+    return fail(NQB_ERR_CUDA, "converting the program's scales to fp32 failed");
+  }
+  auto f32 = [&](size_t offset) -> const float * { return offset == SIZE_MAX ? nullptr : scales + offset; };
+  size_t member_index = 0;
+  for (int i = 0; i < op_count; ++i) {
+    const nqb_program_op &o = ops[i];
+    OpDev &od = opdev[i];
+    std::memset(&od, 0, sizeof(od));
+    od.count = o.count;
+    od.x = o.x;
+    od.x_dtype = o.x_dtype;
+    od.n = o.layers[0].in_features;
+    int64_t offset = 0;
+    for (int k = 0; k < o.count; ++k) {
+      const MemberScales &ms = member_scales[member_index++];
+      fill_member(od.s[0][k], o.layers[k], 0, offset, nullptr, f32(ms.pre), f32(ms.mid), nullptr);
+      fill_member(od.s[1][k], o.layers[k], 1, offset, o.y[k], nullptr, f32(ms.post), f32(ms.bias));
+      offset += o.layers[k].rank;
+    }
+    od.latent_stride = offset;
+  }
+
+  int device = 0;
+  NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  const SmemPlan sp = smem_plan(bucket);
+  const void *fn = kernel_for(bucket);
+  NQB_CHECK(ensure_dynamic_smem(fn, static_cast<int>(sp.total)));
+  int sms = 0;
+  NQB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+  int clusters = 0;
+  {
+    cudaLaunchConfig_t config;
+    std::memset(&config, 0, sizeof(config));
+    config.gridDim = dim3(kClusterSize * std::max(1, sms / kClusterSize));
+    config.blockDim = dim3(kBlockThreads);
+    config.dynamicSmemBytes = sp.total;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterSize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    NQB_CUDA(cudaOccupancyMaxActiveClusters(&clusters, fn, &config), "cudaOccupancyMaxActiveClusters");
+  }
+  clusters = std::min(clusters, sms / kClusterSize);
+  if (clusters < 1) return fail(NQB_ERR_UNSUPPORTED, "no cluster of %d CTAs fits this device", kClusterSize);
+  const int ctas = clusters * kClusterSize;
+
+  // tiles per (stage, cluster), then every CTA's slice addresses in consumption order
+  // and the L2 lines it reads per stage besides sign words and activations
+  const int stages = 2 * op_count;
+  std::vector<std::vector<uint64_t>> pf(static_cast<size_t>(stages) * ctas);
+  auto add_lines = [](std::vector<uint64_t> &out, const void *base, int64_t bytes) {
+    if (base == nullptr || bytes <= 0) return;
+    const uint64_t first = reinterpret_cast<uint64_t>(base) & ~uint64_t(127);
+    const uint64_t end = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(bytes);
+    for (uint64_t a = first; a < end; a += 128) out.push_back(a);
+  };
+  std::vector<int32_t> stage_items(static_cast<size_t>(stages) * clusters + 1, 0);
+  std::vector<Item> items;
+  std::vector<std::vector<uint64_t>> lists(ctas);
+  std::vector<std::vector<Item>> per_cluster;
+  for (int g = 0; g < stages; ++g) {
+    const OpDev &op = opdev[g >> 1];
+    const int st = g & 1;
+    assign_stage(op, st, clusters, per_cluster);
+    for (int c = 0; c < clusters; ++c) {
+      stage_items[static_cast<size_t>(g) * clusters + c] = static_cast<int32_t>(items.size());
+      const std::vector<Item> &list = per_cluster[c];
+      items.insert(items.end(), list.begin(), list.end());
+      for (int q = 0; q < kClusterSize; ++q) {
+        std::vector<uint64_t> &lines = pf[static_cast<size_t>(g) * ctas + c * kClusterSize + q];
+        int last_member = -1;
+        for (size_t j = 0; j < list.size(); ++j) {
+          const MemberDev &md = op.s[st][list[j].member];
+          if (st == 0 && list[j].member != last_member) {
+            last_member = list[j].member;
+            const int64_t lo = static_cast<int64_t>(md.ks) * q / kClusterSize * kStageCols;
+            const int64_t hi = std::min<int64_t>(static_cast<int64_t>(md.ks) * (q + 1) / kClusterSize * kStageCols,
+                                                 md.k_valid);
+            if (hi > lo) {
+              add_lines(lines, md.pre + lo, (hi - lo) * 4);
+              const int64_t xs = static_cast<int64_t>(dtype_size(op.x_dtype));
+              for (int64_t t = 0; t < tokens; ++t)
+                add_lines(lines, static_cast<const char *>(op.x) + (t * op.n + lo) * xs, (hi - lo) * xs);
+            }
+          }
+          if (static_cast<int>(j % kClusterSize) == q) {
+            const int64_t r0 = static_cast<int64_t>(list[j].tile) * kTileRows;
+            const int64_t rows = std::min<int64_t>(kTileRows, md.rows - r0);
+            add_lines(lines, md.row_scale + r0, rows * 4);
+            if (md.bias != nullptr) add_lines(lines, md.bias + r0, rows * 4);
+          }
+        }
+        std::vector<uint64_t> &addrs = lists[c * kClusterSize + q];
+        for (size_t gb = 0; gb < list.size(); gb += sp.group) {
+          const size_t ge = std::min(list.size(), gb + sp.group);
+          for (size_t j0 = gb; j0 < ge;) {
+            size_t j1 = j0 + 1;
+            while (j1 < ge && list[j1].member == list[j0].member) ++j1;
+            const MemberDev &md = op.s[st][list[j0].member];
+            const int lo = md.ks * q / kClusterSize, hi = md.ks * (q + 1) / kClusterSize;
+            for (int c0 = lo; c0 < hi; c0 += sp.sc) {
+              const int nst = std::min(sp.sc, hi - c0);
+              for (size_t j = j0; j < j1; ++j)
+                for (int sl = c0; sl < c0 + nst; ++sl)
+                  addrs.push_back(reinterpret_cast<uint64_t>(md.tiles) +
+                                  (static_cast<uint64_t>(list[j].tile) * md.wc + 2ull * sl) * (kTileRows * kChunkBytes));
+            }
+            j0 = j1;
+          }
+        }
+      }
+    }
+  }
+  stage_items.back() = static_cast<int32_t>(items.size());
+  std::vector<int64_t> slice_begin(ctas);
+  std::vector<int32_t> slice_count(ctas);
+  std::vector<uint64_t> flat;
+  for (int c = 0; c < ctas; ++c) {
+    slice_begin[c] = static_cast<int64_t>(flat.size());
+    slice_count[c] = static_cast<int32_t>(lists[c].size());
+    flat.insert(flat.end(), lists[c].begin(), lists[c].end());
+    flat.resize(((flat.size() + kAddrChunk - 1) / kAddrChunk) * kAddrChunk, 0);
+  }
+  if (flat.empty()) flat.resize(kAddrChunk, 0);
+  std::vector<int32_t> pf_begin(static_cast<size_t>(stages) * ctas + 1, 0);
+  std::vector<uint64_t> pf_lines;
+  for (size_t i = 0; i < pf.size(); ++i) {
+    pf_begin[i] = static_cast<int32_t>(pf_lines.size());
+    pf_lines.insert(pf_lines.end(), pf[i].begin(), pf[i].end());
+  }
+  pf_begin.back() = static_cast<int32_t>(pf_lines.size());
+  if (pf_lines.empty()) pf_lines.push_back(0);
+
+  // one device arena for the tables
+  auto section = [](size_t bytes) { return align_up(bytes, 256); };
+  const size_t b_ops = section(sizeof(OpDev) * op_count);
+  const size_t b_si = section(sizeof(int32_t) * stage_items.size());
+  const size_t b_items = section(sizeof(Item) * std::max<size_t>(1, items.size()));
+  const size_t b_addrs = section(sizeof(uint64_t) * flat.size());
+  const size_t b_begin = section(sizeof(int64_t) * ctas);
+  const size_t b_count = section(sizeof(int32_t) * ctas);
+  const size_t b_pfb = section(sizeof(int32_t) * pf_begin.size());
+  const size_t b_pfl = section(sizeof(uint64_t) * pf_lines.size());
+  const size_t total = b_ops + b_si + b_items + b_addrs + b_begin + b_count + b_pfb + b_pfl;
+  nqb_program *prog = new (std::nothrow) nqb_program();
+  if (prog == nullptr) {
+    cudaFree(scales);
+    return fail(NQB_ERR_INVALID_ARGUMENT, "out of host memory");
+  }
+  prog->scales = scales;
+  if (cudaMalloc(&prog->arena, total) != cudaSuccess) {
+    cudaFree(scales);
+    delete prog;
+    cudaGetLastError();
+    return fail(NQB_ERR_CUDA, "cudaMalloc of %zu bytes for the program tables failed", total);
+  }
+  char *base = static_cast<char *>(prog->arena);
+  size_t off = 0;
+  auto put = [&](const void *src, size_t bytes, size_t section_bytes) -> void * {
+    void *dst = base + off;
+    if (bytes > 0) cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+    off += section_bytes;
+    return dst;
+  };
+  Params &pp = prog->params;
+  std::memset(&pp, 0, sizeof(pp));
+  pp.ops = static_cast<const OpDev *>(put(opdev.data(), sizeof(OpDev) * op_count, b_ops));
+  pp.stage_items = static_cast<const int32_t *>(put(stage_items.data(), sizeof(int32_t) * stage_items.size(), b_si));
+  pp.items = static_cast<const Item *>(put(items.data(), sizeof(Item) * items.size(), b_items));
+  pp.slice_addrs = static_cast<const uint64_t *>(put(flat.data(), sizeof(uint64_t) * flat.size(), b_addrs));
+  pp.slice_begin = static_cast<const int64_t *>(put(slice_begin.data(), sizeof(int64_t) * ctas, b_begin));
+  pp.slice_count = static_cast<const int32_t *>(put(slice_count.data(), sizeof(int32_t) * ctas, b_count));
+  pp.pf_begin = static_cast<const int32_t *>(put(pf_begin.data(), sizeof(int32_t) * pf_begin.size(), b_pfb));
+  pp.pf_lines = static_cast<const uint64_t *>(put(pf_lines.data(), sizeof(uint64_t) * pf_lines.size(), b_pfl));
+  const cudaError_t copy_status = cudaDeviceSynchronize();
+  if (copy_status != cudaSuccess) {
+    cudaFree(prog->arena);
+    cudaFree(scales);
+    delete prog;
+    return fail(NQB_ERR_CUDA, "copying the program tables failed: %s", cudaGetErrorString(copy_status));
+  }
+  pp.stages = stages;
+  pp.clusters = clusters;
+  pp.tokens = static_cast<int32_t>(tokens);
+  pp.ring = sp.ring;
+  pp.sc = sp.sc;
+  pp.group = sp.group;
+  pp.off_addr = sp.off_addr;
+  pp.off_b = sp.off_b;
+  pp.off_act = sp.off_act;
+  pp.off_acc = sp.off_acc;
+  pp.off_exch = sp.off_exch;
+  prog->device = device;
+  prog->tokens = tokens;
+  prog->bucket = bucket;
+  prog->ctas = ctas;
+  prog->clusters = clusters;
+  prog->smem = static_cast<int>(sp.total);
+  prog->latent_bytes = align_up(static_cast<size_t>(tokens) * latent_cols * sizeof(float), 256);
+  *program = prog;
+  return ok();
+}
+
+int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes) {
+  if (program == nullptr || bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program or bytes is NULL");
+  *bytes = kCounterRegionBytes + program->latent_bytes;
+  return ok();
+}
+
+int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream) {
+  using namespace nqb::prog;
+  if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
+  const size_t need = kCounterRegionBytes + program->latent_bytes;
+  if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(NQB_ERR_WORKSPACE, "program workspace needs %zu bytes aligned to 256, got %zu", need, workspace_bytes);
+  Params params = program->params;
+  params.counters = static_cast<uint32_t *>(workspace);
+  params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
+  const void *fn = kernel_for(program->bucket);
+  NQB_CHECK(ensure_dynamic_smem(fn, program->smem));
+  cudaLaunchConfig_t config;
+  std::memset(&config, 0, sizeof(config));
+  config.gridDim = dim3(program->ctas);
+  config.blockDim = dim3(kBlockThreads);
+  config.dynamicSmemBytes = program->smem;
+  config.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterSize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
+  config.attrs = attr;
+  config.numAttrs = 2;
+  void *args[] = {&params};
+  NQB_CUDA(cudaLaunchKernelExC(&config, fn, args), "program launch");
+  return ok();
+}
+
+int nqb_program_destroy(nqb_program *program) {
+  if (program == nullptr) return ok();
+  if (program->arena != nullptr) cudaFree(program->arena);
+  if (program->scales != nullptr) cudaFree(program->scales);
+  delete program;
+  return ok();
+}
+
+int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size) {
+  if (program == nullptr || ctas == nullptr || cluster_size == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "program, ctas or cluster_size is NULL");
+  *ctas = program->ctas;
+  *cluster_size = nqb::prog::kClusterSize;
+  return ok();
+}
+
+}  // extern "C"

@@ -4,10 +4,13 @@ A decoder layer's packed linears are the q/k/v/o attention projections and the
 gate/up/down MLP projections.  :func:`make_decoder_layers` builds random
 layout-v1 layers of a given model shape (uniform random sign bits, the scales
 of BASELINE config 0: ``|N(0,1)| * 0.05 + 0.01`` in fp16, ``scale_mid = 1``),
-directly on the GPU.  :class:`DecodeChain` runs one decode token through every
+directly on the GPU.  :class:`DecodeChain` runs one decode step through every
 layer with the grouped QKV and gate/up calls the reference's model shell uses
-(``src/nanoquant/runtime/torch_model.py:311-327, 492-505``), and can capture
-that step in a CUDA graph.
+(``src/nanoquant/runtime/torch_model.py:311-327, 492-505``).  Its engines:
+``"program"`` (default for 1..16 tokens) compiles the whole step into one
+persistent :class:`~nanoquant_b200.program.DecodeProgram` launch; ``"calls"``
+issues one libnqb call per projection group (optionally captured in a CUDA
+graph, like the reference's decode loop).
 
 Rank follows the reference's budget formula at a target bits-per-weight:
 ``r = floor(bpw * m * n / (m + n))``.
@@ -27,6 +30,7 @@ from nanoquant_b200.cuda_backend import (
     prepare_sm100_projection_group,
 )
 from nanoquant_b200.packed import PACKED_LAYOUT_VERSION, PackedLayerState, packed_word_count
+from nanoquant_b200.program import DecodeProgram, ProgramOp
 
 
 @dataclass(frozen=True)
@@ -115,10 +119,17 @@ class DecodeChain:
     """All packed linears of a decoder, run for one decode step (batch ``tokens``)."""
 
     def __init__(self, shape: DecoderShape, blocks: list[dict[str, PackedLayerState]], device: torch.device,
-                 tokens: int = 1) -> None:
+                 tokens: int = 1, engine: str | None = None) -> None:
+        if engine is None:
+            engine = "program" if tokens <= 16 else "calls"
+        if engine not in ("program", "calls"):
+            raise ValueError(f"unknown engine {engine!r}")
+        if engine == "program" and tokens > 16:
+            raise ValueError("the program engine takes 1..16 tokens")
         self.shape = shape
         self.device = device
         self.tokens = tokens
+        self.engine = engine
         self.backend = CudaPackedSm100Backend()
         self.blocks: list[_PreparedBlock] = []
         for block in blocks:
@@ -138,16 +149,27 @@ class DecodeChain:
         }
         self.graph: torch.cuda.CUDAGraph | None = None
         self.graph_output: torch.Tensor | None = None
+        self.program: DecodeProgram | None = None
+        if engine == "program":
+            ops = []
+            for block in self.blocks:
+                ops += [ProgramOp(block.qkv.layers, self.inputs["hidden"]),
+                        ProgramOp((block.o_proj,), self.inputs["attn"]),
+                        ProgramOp(block.gate_up.layers, self.inputs["mlp"]),
+                        ProgramOp((block.down_proj,), self.inputs["act"])]
+            self.program = DecodeProgram(ops)
 
     @property
     def launches_per_step(self) -> int:
         """libnqb kernel launches of one step.
 
-        Decode (tensor-core path): two stage kernels per call, four calls per
-        layer.  Prefill: per call and stage one activation pre-pass and one
-        GEMM kernel.
+        Program engine: one launch per step.  Per-call decode (tensor-core
+        path): two stage kernels per call, four calls per layer.  Prefill: per
+        call and stage one activation pre-pass and one GEMM kernel.
         """
 
+        if self.program is not None:
+            return 1
         if self.tokens <= 16:
             return 8 * len(self.blocks)
         return 16 * len(self.blocks)
@@ -170,6 +192,8 @@ class DecodeChain:
         return total * len(self.blocks)
 
     def step(self) -> torch.Tensor:
+        if self.program is not None:
+            return self.program.run()[-1][0]
         out = None
         for block in self.blocks:
             grouped_sm100_projection(self.inputs["hidden"], block.qkv)

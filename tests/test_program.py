@@ -1,0 +1,137 @@
+"""Persistent decode program (``nqb_program_*``) against the oracle and the per-call path.
+
+A program runs a fixed sequence of packed-linear calls in one cooperative
+launch.  These tests build programs from the same layers as the per-call
+tests, chain ops through each other's outputs (an op reads the fp32 output of
+an earlier op, so the grid barriers must order them), and compare every output
+with the float64 oracle within the tensor-core decode tolerance.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from nanoquant_b200 import (
+    CudaPackedSm100Backend,
+    OutlierRowOverlay,
+    OverlaidLayerState,
+    _native,
+    grouped_sm100_projection,
+    prepare_sm100_projection_group,
+)
+from nanoquant_b200.program import DecodeProgram, ProgramOp
+from oracle import packed_oracle as po
+from tests.test_cuda_parity import ATOL, RTOL, _random_state, ctypes_status, oracle_from_state
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _require_gpu() -> None:
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test needs CUDA")
+
+
+def _check(got: torch.Tensor, x: torch.Tensor, state) -> None:
+    expected = po.packed_linear(x.float().cpu().numpy(), oracle_from_state(state), accumulate="float64")
+    scale = float(np.abs(expected).max())
+    np.testing.assert_allclose(got.cpu().numpy(), expected, rtol=RTOL, atol=max(ATOL, 1e-5 * scale))
+
+
+@pytest.mark.parametrize("tokens", (1, 3, 16))
+def test_program_chain_matches_oracle(tokens: int) -> None:
+    backend = CudaPackedSm100Backend()
+    g = torch.Generator().manual_seed(tokens)
+    qkv_states = [_random_state(4096, w, r, seed=10 + i) for i, (w, r) in enumerate(((4096, 2048), (1024, 819),
+                                                                                       (1024, 819)))]
+    o_state = _random_state(4096, 4096, 2048, seed=20, outliers=3, bias=True)
+    gu_states = [_random_state(1152, 6912, 987, seed=30 + i) for i in range(2)]
+    down_state = _random_state(6912, 1152, 987, seed=40, bias=True)
+    qkv = tuple(backend.prepare(s, "cuda") for s in qkv_states)
+    o_proj = backend.prepare(o_state, "cuda")
+    gate_up = tuple(backend.prepare(s, "cuda") for s in gu_states)
+    down = backend.prepare(down_state, "cuda")
+
+    x0 = torch.randn(tokens, 4096, generator=g).bfloat16().cuda()
+    x2 = torch.randn(tokens, 1152, generator=g).bfloat16().cuda()
+    q_out = torch.empty(tokens, 4096, device="cuda")
+    gate_out = torch.empty(tokens, 6912, device="cuda")
+    ops = [
+        ProgramOp(qkv, x0),
+        ProgramOp((o_proj,), q_out),      # reads op 0's q output
+        ProgramOp(gate_up, x2),
+        ProgramOp((down,), gate_out),     # reads op 2's gate output
+    ]
+    outputs = [
+        (q_out, torch.empty(tokens, 1024, device="cuda"), torch.empty(tokens, 1024, device="cuda")),
+        (torch.empty(tokens, 4096, device="cuda"),),
+        (gate_out, torch.empty(tokens, 6912, device="cuda")),
+        (torch.empty(tokens, 1152, device="cuda"),),
+    ]
+    program = DecodeProgram(ops, outputs=outputs)
+    assert program.ctas >= 4 and program.ctas % program.cluster_size == 0
+    results = program.run()
+    torch.cuda.synchronize()
+    for got, state in zip(results[0], qkv_states):
+        _check(got, x0, state)
+    _check(results[1][0], q_out, o_state)
+    for got, state in zip(results[2], gu_states):
+        _check(got, x2, state)
+    _check(results[3][0], gate_out, down_state)
+    # the per-call tensor-core path on the same inputs agrees
+    # (both round their 22-bit activation quantisation per K chunk, and the
+    # chunks differ, so they agree to the same tolerance as with the oracle)
+    per_call = grouped_sm100_projection(x0, prepare_sm100_projection_group(qkv)) + (backend.linear(q_out, o_proj),)
+    for got, ref in zip((*results[0], results[1][0]), per_call):
+        atol = max(ATOL, 1e-5 * float(ref.abs().max()))
+        torch.testing.assert_close(got, ref, rtol=RTOL, atol=atol)
+    assert ctypes_status() == 0
+
+
+def test_program_is_deterministic_and_leaves_counters_zero() -> None:
+    backend = CudaPackedSm100Backend()
+    states = [_random_state(2048, 5632, 1500, seed=50 + i) for i in range(2)]
+    layers = tuple(backend.prepare(s, "cuda") for s in states)
+    x = torch.randn(2, 2048, generator=torch.Generator().manual_seed(1)).bfloat16().cuda()
+    program = DecodeProgram([ProgramOp(layers, x), ProgramOp(layers[:1], x)])
+    first = [tuple(t.clone() for t in op) for op in program.run()]
+    second = program.run()
+    torch.cuda.synchronize()
+    for a_op, b_op in zip(first, second):
+        for a, b in zip(a_op, b_op):
+            assert torch.equal(a, b)
+    assert int(program.workspace[:16384].count_nonzero()) == 0
+    _check(second[1][0], x, states[0])
+    assert ctypes_status() == 0
+
+
+def test_program_applies_overlay_rows_and_salient_columns() -> None:
+    backend = CudaPackedSm100Backend()
+    base = _random_state(1152, 6912, 987, seed=61, outliers=4, bias=True)
+    g = torch.Generator().manual_seed(2)
+    rows = torch.sort(torch.randperm(6912, generator=g)[:70]).values.to(torch.int32)
+    overlay = OutlierRowOverlay(rows, torch.randint(-127, 128, (70, 1152), generator=g, dtype=torch.int8),
+                                torch.full((70,), 0.002, dtype=torch.float16))
+    layer = backend.prepare(OverlaidLayerState(base, overlay), "cuda")
+    x = torch.randn(5, 1152, generator=g).bfloat16().cuda()
+    out = DecodeProgram([ProgramOp((layer,), x)]).run()[0][0]
+    torch.cuda.synchronize()
+    ref = oracle_from_state(base)
+    ref.overlay_row_ids = rows.numpy()
+    ref.overlay_values = overlay.values.numpy()
+    ref.overlay_scales = overlay.scales.float().numpy()
+    expected = po.packed_linear(x.float().cpu().numpy(), ref, accumulate="float64")
+    scale = float(np.abs(expected).max())
+    np.testing.assert_allclose(out.cpu().numpy(), expected, rtol=RTOL, atol=max(ATOL, 1e-5 * scale))
+    assert ctypes_status() == 0
+
+
+def test_program_rejects_prefill_token_counts() -> None:
+    backend = CudaPackedSm100Backend()
+    layer = backend.prepare(_random_state(640, 2048, 480, seed=70), "cuda")
+    x = torch.zeros(17, 640, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(_native.NativeError) as info:
+        DecodeProgram([ProgramOp((layer,), x)])
+    assert info.value.status == _native.NQB_ERR_UNSUPPORTED
