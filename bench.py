@@ -99,6 +99,18 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def _device_status() -> int:
+    """libnqb's device status word (NQB_OK = 0; NQB_ERR_TIMEOUT when a bounded wait gave up)."""
+
+    import ctypes
+
+    from nanoquant_b200 import _native
+
+    value = ctypes.c_int32(-1)
+    _native.call("nqb_device_status", ctypes.byref(value))
+    return value.value
+
+
 def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
     """Time the CPU oracle (numpy port of PackedReferenceBackend) on a bounded sample.
 
@@ -281,6 +293,9 @@ def main() -> None:
         torch.cuda.synchronize(device)
         barrier()
     elapsed_ms = start.elapsed_time(stop)
+    status = _device_status()
+    if status != 0:
+        raise SystemExit(f"libnqb device status {status} after the timed region (a bounded wait gave up)")
 
     # end to end through the public API: pinned host tokens in, result back to host, every step
     host_in = torch.randn(tokens, shape.hidden).bfloat16().pin_memory()

@@ -50,9 +50,9 @@ constexpr int kClusterSize = 4;
 constexpr int kMaxRing = 48;            // ring slots (4 KB each)
 constexpr int kAddrChunk = 64;          // slice addresses per bulk copy
 constexpr int kAddrSlots = 4;           // address chunks in flight
-constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kBarrierSpinLimit = 1u << 22;  // polls of the grid-barrier counter
-constexpr int kMaxDynamicSmem = 225 * 1024;
+constexpr int kMaxDynamicSmem = 220 * 1024;  // + static shared memory <= 227 KB
 
 struct MemberDev {
   const uint8_t *tiles;  // row-interleaved sign tiles
@@ -93,6 +93,20 @@ struct Item {
   int32_t tile;
 };
 
+// Everything a CTA's consumers read about one stage, staged into shared
+// memory by the producer warp one stage ahead: the op's fields, the members'
+// descriptors of that stage and the cluster's tile list.
+constexpr int kMaxStageItems = 64;
+struct __align__(16) StageInfo {
+  MemberDev md[kMaxMembersTc];
+  const void *x;
+  int64_t n;
+  int64_t latent_stride;
+  int32_t x_dtype;
+  int32_t n_items;
+  Item items[kMaxStageItems];
+};
+
 struct Params {
   const OpDev *ops;
   int32_t stages;              // 2 * ops
@@ -111,12 +125,26 @@ struct Params {
   int32_t sc;                   // slices quantised at once
   int32_t group;                // items per exchange group (4 x leader slots)
   // dynamic shared memory offsets
-  uint32_t off_addr, off_b, off_act, off_acc, off_exch;
+  uint32_t off_addr, off_b, off_acc, off_exch;
 };
 
 __device__ int g_prog_error;
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_prog_error, 0, code); }
+
+__device__ __forceinline__ bool program_failed() { return *reinterpret_cast<volatile int *>(&g_prog_error) != 0; }
+
+// Bounded wait for phase `parity` of a CTA-local mbarrier.  On timeout it
+// records NQB_ERR_TIMEOUT at once; every wait gives up early once any wait
+// of the program has failed, so a failed run ends quickly.
+__device__ __forceinline__ bool wait_local(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && program_failed()) return false;
+  }
+  record_error(NQB_ERR_TIMEOUT);
+  return false;
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -167,9 +195,11 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Arrive (release, cluster scope) on the mbarrier at the same offset in CTA `rank`.
-__device__ __forceinline__ void remote_arrive(uint64_t *bar, uint32_t rank) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr(bar, rank))
+// Arrive (relaxed, cluster scope) on the mbarrier at the same offset in CTA
+// `rank`.  Used to hand back exchange buffers whose values this thread's CTA
+// has already consumed, so no ordering of earlier memory operations is needed.
+__device__ __forceinline__ void remote_arrive_relaxed(uint64_t *bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr(bar, rank))
                : "memory");
 }
 
@@ -185,7 +215,9 @@ __device__ __forceinline__ bool wait_cluster(uint64_t *bar, uint32_t parity) {
         : "r"(ptx::smem_u32(bar)), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 1023) == 1023 && program_failed()) return false;
   }
+  record_error(NQB_ERR_TIMEOUT);
   return false;
 }
 
@@ -208,31 +240,71 @@ __device__ __forceinline__ void prefetch_range(const void *ptr, int64_t bytes) {
 
 // L2 prefetch of the lines stage g of this CTA reads besides sign words and
 // activations (pre and row scales, bias, input rows), from the host-built
-// list; consumer threads other than 0.
-__device__ __forceinline__ void prefetch_stage(const Params &p, int g) {
+// list; the 32 lanes of the info warp.
+__device__ __forceinline__ void prefetch_stage(const Params &p, int g, int lane) {
   if (g >= p.stages) return;
   const int cta = static_cast<int>(blockIdx.x);
   const int b = p.pf_begin[g * static_cast<int>(gridDim.x) + cta];
   const int e = p.pf_begin[g * static_cast<int>(gridDim.x) + cta + 1];
-  for (int i = b + static_cast<int>(threadIdx.x) - 1; i < e; i += mmad::kThreads - 1)
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.pf_lines[i]));
+  for (int i = b + lane; i < e; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.pf_lines[i]));
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *ptr) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// Until the grid-barrier counter reaches `target`; false after a bounded
+// number of polls (or at once when another wait has failed).
+__device__ __forceinline__ bool wait_counter(const uint32_t *counter, uint32_t target) {
+  for (uint32_t polls = 0; polls < kBarrierSpinLimit; ++polls) {
+    if (ld_acquire_gpu(counter) >= target) return true;
+    if (program_failed()) return false;
+    __nanosleep(64);
+  }
+  record_error(NQB_ERR_TIMEOUT);
+  return false;
+}
+
+// Copies stage g's tables for this CTA's cluster into `info` (the 32 lanes of
+// the info warp; 4-byte words).
+__device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t cluster, int lane, StageInfo &info) {
+  const OpDev &op = p.ops[g >> 1];
+  const int st = g & 1;
+  const int ib = p.stage_items[g * p.clusters + cluster];
+  const int ie = p.stage_items[g * p.clusters + cluster + 1];
+  const int n_items = min(ie - ib, kMaxStageItems);
+  const uint32_t *md_src = reinterpret_cast<const uint32_t *>(&op.s[st][0]);
+  uint32_t *md_dst = reinterpret_cast<uint32_t *>(&info.md[0]);
+  constexpr int kMdWords = static_cast<int>(sizeof(MemberDev) * kMaxMembersTc / 4);
+  for (int i = lane; i < kMdWords; i += 32) md_dst[i] = md_src[i];
+  const uint32_t *it_src = reinterpret_cast<const uint32_t *>(p.items + ib);
+  uint32_t *it_dst = reinterpret_cast<uint32_t *>(&info.items[0]);
+  for (int i = lane; i < n_items * 2; i += 32) it_dst[i] = it_src[i];
+  if (lane == 0) {
+    info.x = op.x;
+    info.n = op.n;
+    info.latent_stride = op.latent_stride;
+    info.x_dtype = op.x_dtype;
+    info.n_items = n_items;
+  }
 }
 
 // Grid barrier number `index` over every CTA of the grid (consumer warps;
-// thread 0 adds and polls, the others issue the prefetches of stage
-// `index` + 2 meanwhile).
+// thread 0 adds and polls).
 __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index) {
   uint32_t *counter = p.counters;
   const uint32_t ctas = gridDim.x;
   mmad::consumer_sync();
-  if (threadIdx.x != 0) prefetch_stage(p, static_cast<int>(index) + 2);
   if (threadIdx.x == 0) {
     __threadfence();
     red_release_gpu_add(counter, 1);
     const uint32_t target = (index + 1) * ctas;
     uint32_t polls = 0;
     while (ld_acquire_gpu(counter) < target) {
-      if (++polls > kBarrierSpinLimit || *reinterpret_cast<volatile int *>(&g_prog_error) != 0) {
+      if (program_failed()) break;
+      if (++polls > kBarrierSpinLimit) {
         record_error(NQB_ERR_TIMEOUT);
         break;
       }
@@ -264,7 +336,7 @@ struct Producer {
   __device__ bool produce(int pos, int slot) const {
     const int chunk = pos / kAddrChunk;
     if (pos % kAddrChunk == 0 && chunk >= 1) issue_addr_chunk(chunk + kAddrSlots - 1);
-    const bool ok = ptx::mbar_wait_bounded(addr_bar + (chunk % kAddrSlots), (chunk / kAddrSlots) & 1, kSpinLimit);
+    const bool ok = wait_local(addr_bar + (chunk % kAddrSlots), (chunk / kAddrSlots) & 1);
     const uint64_t src = cache[(chunk % kAddrSlots) * kAddrChunk + pos % kAddrChunk];
     expect_tx(full + slot, kStageWeightBytes);
     bulk_load(ring + static_cast<size_t>(slot) * kStageWeightBytes, reinterpret_cast<const void *>(src),
@@ -273,8 +345,12 @@ struct Producer {
   }
 };
 
-constexpr int kBlockThreads = mmad::kThreads + 32;  // 8 consumer warps + 1 producer warp
+// 8 consumer warps, the sign-ring producer warp, and a warp that stages each
+// stage's tables and prefetches its scales (two warps, so that neither
+// role's waiting can starve the other within one warp).
+constexpr int kBlockThreads = mmad::kThreads + 64;
 constexpr int kProducerWarp = mmad::kWarps;
+constexpr int kInfoWarp = mmad::kWarps + 1;
 
 // Slices quantised at once (B fragments and activations held for them).
 __host__ __device__ constexpr int slices_per_chunk(int bucket) { return bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2); }
@@ -296,6 +372,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   __shared__ uint64_t s_addr_bar[kAddrSlots];
   __shared__ uint64_t s_x_full;  // this CTA's leader buffers hold every quarter (own expect_tx + st.async bytes)
   __shared__ uint64_t s_x_free;  // every leader has read this CTA's quarters (one arrival per leader)
+  __shared__ uint64_t s_info_full[2];  // s_info[b] holds the next stage of parity b
+  __shared__ StageInfo s_info[2];
   __shared__ mmad::Scratch<kT> s_sc;
   __shared__ float s_red_f[mmad::kWarps];
 
@@ -311,7 +389,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   uint8_t *ring = smem;
   uint64_t *addr_cache = reinterpret_cast<uint64_t *>(smem + p.off_addr);
   uint8_t *smem_b = smem + p.off_b;
-  float *s_act = reinterpret_cast<float *>(smem + p.off_act);
   float *s_acc = reinterpret_cast<float *>(smem + p.off_acc);    // [group][T][128]
   float *s_exch = reinterpret_cast<float *>(smem + p.off_exch);  // [group / 4][4][T][128]
 
@@ -323,6 +400,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     for (int s = 0; s < kAddrSlots; ++s) ptx::mbar_init(&s_addr_bar[s], 1);
     ptx::mbar_init(&s_x_full, 1);
     ptx::mbar_init(&s_x_free, kClusterSize);
+    ptx::mbar_init(&s_info_full[0], 1);
+    ptx::mbar_init(&s_info_full[1], 1);
     ptx::fence_mbar_init();
   }
   cluster_sync();  // every CTA's barriers exist before any remote arrive
@@ -345,7 +424,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       int slot = 0;
       uint32_t phase = 0;  // ring passes completed
       for (int pos = 0; pos < prod.count; ++pos) {
-        if (phase > 0 && !ptx::mbar_wait_bounded(&s_empty[slot], (phase - 1) & 1, kSpinLimit)) ok = false;
+        if (phase > 0 && !wait_local(&s_empty[slot], (phase - 1) & 1)) ok = false;
         ok &= prod.produce(pos, slot);
         if (++slot == R) {
           slot = 0;
@@ -354,29 +433,40 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       }
     }
     __syncwarp();
+  } else if (warp == kInfoWarp) {
+    // ---- stage g's tables into s_info[g % 2] and an L2 prefetch of its
+    // scales and inputs, once stage g - 1 has started (so stage g - 2, the
+    // buffer's previous user, is finished everywhere)
+    for (int g = 0; g < p.stages; ++g) {
+      if (g >= 2) {
+        if (lane == 0 && !wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x)) ok = false;
+        __syncwarp();
+      }
+      stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cta(&s_info_full[g & 1]);
+      prefetch_stage(p, g, lane);
+    }
   } else {
     // ---- consumers: 8 warps x 16 rows of the current 128-row tile
     int slot = 0;         // ring slot of the next slice
     uint32_t phase = 0;   // ring passes completed
     uint32_t xg = 0;      // exchange groups done
-    if (tid != 0) {
-      prefetch_stage(p, 0);
-      prefetch_stage(p, 1);
-    }
     for (int g = 0; g < p.stages; ++g) {
-      const OpDev &op = p.ops[g >> 1];
       const int st = g & 1;
-      const int ib = p.stage_items[g * p.clusters + cluster];
-      const int ie = p.stage_items[g * p.clusters + cluster + 1];
+      if (!wait_local(&s_info_full[g & 1], (g >> 1) & 1)) ok = false;
+      const StageInfo &op = s_info[g & 1];
+      const int ib = 0;
+      const int ie = op.n_items;
       for (int gb = ib; gb < ie; gb += p.group) {
         const int ge = min(gb + p.group, ie);
         for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
         // ---- this CTA's quarter of every item of the group, member by member
         for (int j0 = gb; j0 < ge;) {
-          const int mi = p.items[j0].member;
+          const int mi = op.items[j0].member;
           int j1 = j0 + 1;
-          while (j1 < ge && p.items[j1].member == mi) ++j1;
-          const MemberDev &md = op.s[st][mi];
+          while (j1 < ge && op.items[j1].member == mi) ++j1;
+          const MemberDev &md = op.md[mi];
           const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
           const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
           for (int c0 = lo; c0 < hi; c0 += p.sc) {
@@ -407,7 +497,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
 #pragma unroll
                   for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
               for (int sl = 0; sl < nst; ++sl) {
-                if (!ptx::mbar_wait_bounded(&s_full[slot], phase & 1, kSpinLimit)) ok = false;
+                if (!wait_local(&s_full[slot], phase & 1)) ok = false;
                 const mmad::SliceWords w =
                     mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
                 __syncwarp();
@@ -447,8 +537,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           lead_bias[sidx] = 0.0f;
           const int jj = static_cast<int>(rank) + sidx * kClusterSize;
           if (jj < ge - gb && tid < kTileRows) {
-            const Item item = p.items[gb + jj];
-            const MemberDev &md = op.s[st][item.member];
+            const Item item = op.items[gb + jj];
+            const MemberDev &md = op.md[item.member];
             const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
             if (row < md.rows) {
               lead_scale[sidx] = __ldg(md.row_scale + row);
@@ -457,21 +547,41 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           }
         }
         if (!wait_cluster(&s_x_full, xg & 1)) ok = false;
-        // ---- leaders: fixed-order sum of the four quarters, epilogue
+        // ---- leaders: fixed-order sum of the four quarters into registers,
+        // then release the exchange buffers before any global store
+        float vsum[kLead][kT];
+#pragma unroll
+        for (int sidx = 0; sidx < kLead; ++sidx) {
+          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+          const float *ex = s_exch + static_cast<size_t>(sidx) * kClusterSize * per_item;
+#pragma unroll
+          for (int t = 0; t < kT; ++t) {
+            float v = 0.0f;
+            if (jj < ge - gb && t < T && tid < kTileRows) {
+#pragma unroll
+              for (int q = 0; q < kClusterSize; ++q) v += ex[(q * T + t) * kTileRows + tid];
+            }
+            vsum[sidx][t] = v;
+          }
+        }
+        mmad::consumer_sync();  // done reading this CTA's leader buffers
+        if (tid == 0)
+          for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive_relaxed(&s_x_free, r);
+        ++xg;
+        // ---- epilogue of the led tiles
 #pragma unroll
         for (int sidx = 0; sidx < kLead; ++sidx) {
           const int jj = static_cast<int>(rank) + sidx * kClusterSize;
           if (jj >= ge - gb) break;
-          const Item item = p.items[gb + jj];
-          const MemberDev &md = op.s[st][item.member];
-          const float *ex = s_exch + static_cast<size_t>(sidx) * kClusterSize * per_item;
+          const Item item = op.items[gb + jj];
+          const MemberDev &md = op.md[item.member];
           if (tid < kTileRows) {
             const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
             if (row < md.rows) {
-              for (int t = 0; t < T; ++t) {
-                float v = 0.0f;
 #pragma unroll
-                for (int q = 0; q < kClusterSize; ++q) v += ex[(q * T + t) * kTileRows + tid];
+              for (int t = 0; t < kT; ++t) {
+                if (t >= T) break;
+                float v = vsum[sidx][t];
                 if (st == 0) {
                   p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * lead_scale[sidx];
                 } else {
@@ -524,10 +634,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             }
           }
         }
-        mmad::consumer_sync();  // done reading this CTA's leader buffers
-        if (tid == 0)
-          for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive(&s_x_free, r);
-        ++xg;
       }
       if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g));
     }
@@ -583,7 +689,7 @@ static int token_bucket(int64_t tokens) {
 
 struct SmemPlan {
   int sc, group, ring;
-  uint32_t off_addr, off_b, off_act, off_acc, off_exch, total;
+  uint32_t off_addr, off_b, off_acc, off_exch, total;
 };
 
 static SmemPlan smem_plan(int bucket) {
@@ -593,18 +699,15 @@ static SmemPlan smem_plan(int bucket) {
   s.group = kClusterSize * lead;
   const uint32_t addr = kAddrSlots * kAddrChunk * 8;
   const uint32_t b = static_cast<uint32_t>(s.sc) * mmad::slice_frag_bytes(mmad::n_tiles(bucket));
-  const uint32_t act = static_cast<uint32_t>(bucket) * s.sc * kStageCols * 4;
   const uint32_t acc = static_cast<uint32_t>(s.group) * bucket * kTileRows * 4;
   const uint32_t exch = static_cast<uint32_t>(lead) * kClusterSize * bucket * kTileRows * 4;
-  const uint32_t rest = addr + b + act + acc + exch;
+  const uint32_t rest = addr + b + acc + exch;
   s.ring = std::min<int>(kMaxRing, static_cast<int>((kMaxDynamicSmem - rest) / kStageWeightBytes));
   uint32_t off = static_cast<uint32_t>(s.ring) * kStageWeightBytes;
   s.off_addr = off;
   off += addr;
   s.off_b = off;
   off += b;
-  s.off_act = off;
-  off += act;
   s.off_acc = off;
   off += acc;
   s.off_exch = off;
@@ -829,6 +932,15 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const uint64_t end = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(bytes);
     for (uint64_t a = first; a < end; a += 128) out.push_back(a);
   };
+  // lines of the program's own tables (op descriptors, tile lists): arena
+  // offsets tagged in bit 63, turned into addresses once the arena exists
+  constexpr uint64_t kArenaTag = uint64_t(1) << 63;
+  const size_t arena_ops = 0;
+  const size_t arena_items = align_up(sizeof(OpDev) * op_count, 256) +
+                             align_up(sizeof(int32_t) * (static_cast<size_t>(stages) * clusters + 1), 256);
+  auto add_arena_lines = [&](std::vector<uint64_t> &out, size_t offset, size_t bytes) {
+    for (size_t a = offset & ~size_t(127); a < offset + bytes; a += 128) out.push_back(kArenaTag | a);
+  };
   std::vector<int32_t> stage_items(static_cast<size_t>(stages) * clusters + 1, 0);
   std::vector<Item> items;
   std::vector<std::vector<uint64_t>> lists(ctas);
@@ -837,12 +949,19 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const OpDev &op = opdev[g >> 1];
     const int st = g & 1;
     assign_stage(op, st, clusters, per_cluster);
+    for (int c = 0; c < clusters; ++c)
+      if (per_cluster[c].size() > static_cast<size_t>(kMaxStageItems))
+        return fail(NQB_ERR_UNSUPPORTED, "op %d stage %d: more than %d row tiles per cluster", g >> 1, st + 1,
+                    kMaxStageItems);
     for (int c = 0; c < clusters; ++c) {
       stage_items[static_cast<size_t>(g) * clusters + c] = static_cast<int32_t>(items.size());
       const std::vector<Item> &list = per_cluster[c];
       items.insert(items.end(), list.begin(), list.end());
       for (int q = 0; q < kClusterSize; ++q) {
         std::vector<uint64_t> &lines = pf[static_cast<size_t>(g) * ctas + c * kClusterSize + q];
+        if (st == 0) add_arena_lines(lines, arena_ops + sizeof(OpDev) * (g >> 1), sizeof(OpDev));
+        add_arena_lines(lines, arena_items + sizeof(Item) * stage_items[static_cast<size_t>(g) * clusters + c],
+                        sizeof(Item) * list.size());
         int last_member = -1;
         for (size_t j = 0; j < list.size(); ++j) {
           const MemberDev &md = op.s[st][list[j].member];
@@ -939,6 +1058,8 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   };
   Params &pp = prog->params;
   std::memset(&pp, 0, sizeof(pp));
+  for (uint64_t &line : pf_lines)
+    if (line & kArenaTag) line = reinterpret_cast<uint64_t>(base) + (line & ~kArenaTag);
   pp.ops = static_cast<const OpDev *>(put(opdev.data(), sizeof(OpDev) * op_count, b_ops));
   pp.stage_items = static_cast<const int32_t *>(put(stage_items.data(), sizeof(int32_t) * stage_items.size(), b_si));
   pp.items = static_cast<const Item *>(put(items.data(), sizeof(Item) * items.size(), b_items));
@@ -962,7 +1083,6 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   pp.group = sp.group;
   pp.off_addr = sp.off_addr;
   pp.off_b = sp.off_b;
-  pp.off_act = sp.off_act;
   pp.off_acc = sp.off_acc;
   pp.off_exch = sp.off_exch;
   prog->device = device;
