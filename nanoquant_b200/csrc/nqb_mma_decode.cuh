@@ -32,7 +32,7 @@ constexpr int kTileRows = 128;
 constexpr int kSliceCols = 256;
 constexpr int kSliceBytes = 4096;         // 128 rows x 8 words
 constexpr uint32_t kFragBytes = 256;      // one (K block, N tile) B fragment block: 32 lanes x 8 bytes
-constexpr int kMaxSliceQuant = 8;         // slices quantised at once
+constexpr int kMaxSliceQuant = 16;        // slices quantised at once
 
 __host__ __device__ constexpr int n_tiles(int tokens) { return (3 * tokens + 7) / 8; }
 
@@ -86,7 +86,7 @@ struct Scratch {
   long long red_q[kWarps * kT];
 };
 
-// Quads of one chunk held per consumer thread: nst <= 8 slices x 64 quads.
+// Quads of one chunk held per consumer thread: nst <= 16 slices x 64 quads.
 __host__ __device__ constexpr int quads_per_thread(int max_slices) { return (max_slices * 64 + kThreads - 1) / kThreads; }
 
 // Loads the chunk's activations (every load issued before any is used),

@@ -134,6 +134,18 @@ __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_prog_error
 
 __device__ __forceinline__ bool program_failed() { return *reinterpret_cast<volatile int *>(&g_prog_error) != 0; }
 
+// Bounded wait with back-off, for the producer warps (they run ahead and are
+// not on the critical path; sleeping leaves the issue slots to the MMA warps).
+__device__ __forceinline__ bool wait_local_backoff(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && program_failed()) return false;
+    __nanosleep(32);
+  }
+  record_error(NQB_ERR_TIMEOUT);
+  return false;
+}
+
 // Bounded wait for phase `parity` of a CTA-local mbarrier.  On timeout it
 // records NQB_ERR_TIMEOUT at once; every wait gives up early once any wait
 // of the program has failed, so a failed run ends quickly.
@@ -298,7 +310,8 @@ __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index) {
   const uint32_t ctas = gridDim.x;
   mmad::consumer_sync();
   if (threadIdx.x == 0) {
-    __threadfence();
+    // release: this CTA's stores (ordered before this thread by the named
+    // barrier) are visible to every CTA that acquires the count
     red_release_gpu_add(counter, 1);
     const uint32_t target = (index + 1) * ctas;
     uint32_t polls = 0;
@@ -353,7 +366,9 @@ constexpr int kProducerWarp = mmad::kWarps;
 constexpr int kInfoWarp = mmad::kWarps + 1;
 
 // Slices quantised at once (B fragments and activations held for them).
-__host__ __device__ constexpr int slices_per_chunk(int bucket) { return bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2); }
+__host__ __device__ constexpr int slices_per_chunk(int bucket) {
+  return bucket <= 2 ? 16 : (bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2));
+}
 
 // Tiles each CTA leads per exchange group: 16 KB of exchange buffer.
 __host__ __device__ constexpr int leader_slots(int bucket) {
@@ -424,7 +439,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       int slot = 0;
       uint32_t phase = 0;  // ring passes completed
       for (int pos = 0; pos < prod.count; ++pos) {
-        if (phase > 0 && !wait_local(&s_empty[slot], (phase - 1) & 1)) ok = false;
+        if (phase > 0 && !wait_local_backoff(&s_empty[slot], (phase - 1) & 1)) ok = false;
         ok &= prod.produce(pos, slot);
         if (++slot == R) {
           slot = 0;
