@@ -14,7 +14,9 @@
  * zero tail padding.  All pointers are device pointers unless stated
  * otherwise; every call is asynchronous on the given stream (a cudaStream_t
  * passed as void*, NULL = legacy default stream).  No entry point allocates
- * device memory or synchronises the host.
+ * device memory or synchronises the host, except the program set-up calls
+ * (nqb_program_create / _destroy) and the diagnostics readers
+ * (nqb_device_status, nqb_program_trace).
  *
  * Every function returns NQB_OK (0) or one of the NQB_ERR_* codes below and
  * never traps; nqb_last_error() returns a message for the calling thread.
@@ -265,6 +267,14 @@ int nqb_program_run(const nqb_program *program, void *workspace, size_t workspac
 int nqb_program_destroy(nqb_program *program);
 /* Launch shape of a created program: CTAs (one per SM used) and cluster size. */
 int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size);
+/*
+ * Phase trace of the last run (trace build only, libnqb_trace.so; the normal
+ * build returns NQB_ERR_UNSUPPORTED): SM cycles per [cta][stage][phase] spent
+ * by the CTA's first consumer thread; count >= ctas * 2 * ops * 11.  Phases:
+ * tables, quantise, wait-signs, mma, drain, send, wait-quarters, sum,
+ * release, epilogue, grid-barrier.  Synchronous.
+ */
+int nqb_program_trace(const nqb_program *program, int64_t *cycles, size_t count);
 
 #ifdef __cplusplus
 }

@@ -8,12 +8,13 @@ to another implementation.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-from nanoquant_b200.build import LIB_PATH
+from nanoquant_b200.build import LIB_PATH, TRACE_LIB_PATH
 
 NQB_OK = 0
 NQB_ERR_INVALID_ARGUMENT = 1
@@ -140,6 +141,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_program_run": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
     "nqb_program_destroy": (ctypes.c_int, [_c_void_p]),
     "nqb_program_shape": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "nqb_program_trace": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_i64), ctypes.c_size_t]),
     "nqb_linear_path": (ctypes.c_int, [ctypes.POINTER(LinearDesc), _i32, _i32, _i64, ctypes.POINTER(_i32)]),
     "nqb_decode_product_codebook": (
         ctypes.c_int,
@@ -162,7 +164,9 @@ class NativeError(RuntimeError):
 
 
 def library_path() -> Path:
-    return LIB_PATH
+    """The in-tree library; ``NQB_LIBRARY=trace`` selects the phase-trace build."""
+
+    return TRACE_LIB_PATH if os.environ.get("NQB_LIBRARY") == "trace" else LIB_PATH
 
 
 def library() -> ctypes.CDLL:
@@ -171,11 +175,12 @@ def library() -> ctypes.CDLL:
     global _library
     with _lock:
         if _library is None:
-            if not LIB_PATH.exists():
+            path = library_path()
+            if not path.exists():
                 raise RuntimeError(
-                    f"libnqb.so is not built at {LIB_PATH}; run `python -m nanoquant_b200.build`"
+                    f"{path.name} is not built at {path}; run `python -m nanoquant_b200.build`"
                 )
-            lib = ctypes.CDLL(str(LIB_PATH))
+            lib = ctypes.CDLL(str(path))
             for name, (restype, argtypes) in SIGNATURES.items():
                 function = getattr(lib, name)
                 function.restype = restype

@@ -1,8 +1,12 @@
 """Build ``libnqb.so`` (the C-ABI CUDA library) in-tree with nvcc for sm_100a.
 
-Usage: ``python -m nanoquant_b200.build [--force]``.  The library lands in
-``nanoquant_b200/_lib/libnqb.so``; sources are ``nanoquant_b200/csrc/*.cu``.
-The build runs without a GPU (nvcc cross-compiles).
+Usage: ``python -m nanoquant_b200.build [--force] [--trace]``.  The library
+lands in ``nanoquant_b200/_lib/libnqb.so``; sources are
+``nanoquant_b200/csrc/*.cu``.  ``--trace`` builds the same sources with
+``NQB_PHASE_TRACE`` into ``_lib/libnqb_trace.so``: the persistent decode
+program then records per-stage cycle counts of its phases
+(``nqb_program_trace``; see ``nanoquant_b200.program_trace``).  The build runs
+without a GPU (nvcc cross-compiles).
 """
 
 from __future__ import annotations
@@ -18,6 +22,7 @@ PACKAGE_DIR = Path(__file__).resolve().parent
 SOURCE_DIR = PACKAGE_DIR / "csrc"
 LIB_DIR = PACKAGE_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libnqb.so"
+TRACE_LIB_PATH = LIB_DIR / "libnqb_trace.so"
 INCLUDE_DIR = PACKAGE_DIR.parent / "include"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -51,25 +56,28 @@ def _inputs() -> list[Path]:
     return _sources() + sorted(SOURCE_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+def is_stale(trace: bool = False) -> bool:
+    path = TRACE_LIB_PATH if trace else LIB_PATH
+    if not path.exists():
         return True
-    built = LIB_PATH.stat().st_mtime
-    return any(path.stat().st_mtime > built for path in _inputs())
+    built = path.stat().st_mtime
+    return any(source.stat().st_mtime > built for source in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every ``csrc/*.cu`` and link ``libnqb.so``; returns its path."""
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    """Compile every ``csrc/*.cu`` and link ``libnqb.so`` (or the trace build); returns its path."""
 
-    if not force and not is_stale():
-        return LIB_PATH
+    target = TRACE_LIB_PATH if trace else LIB_PATH
+    if not force and not is_stale(trace):
+        return target
     nvcc = _nvcc()
-    obj_dir = LIB_DIR / "obj"
+    obj_dir = LIB_DIR / ("obj_trace" if trace else "obj")
     obj_dir.mkdir(parents=True, exist_ok=True)
+    defines = ["-DNQB_PHASE_TRACE"] if trace else []
     objects = []
     for source in _sources():
         obj = obj_dir / (source.stem + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, "-I", str(INCLUDE_DIR), "-c", str(source), "-o", str(obj)]
+        cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, *defines, "-I", str(INCLUDE_DIR), "-c", str(source), "-o", str(obj)]
         result = subprocess.run(cmd, capture_output=True, text=True)
         if result.returncode != 0:
             raise RuntimeError(f"nvcc failed for {source.name}:\n{result.stdout}\n{result.stderr}")
@@ -77,21 +85,22 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             sys.stderr.write(result.stderr)
         (obj_dir / (source.stem + ".ptxas.txt")).write_text(result.stderr)
         objects.append(str(obj))
-    tmp = LIB_DIR / "libnqb.so.tmp"
+    tmp = target.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objects]
     result = subprocess.run(cmd, capture_output=True, text=True)
     if result.returncode != 0:
         raise RuntimeError(f"nvcc link failed:\n{result.stdout}\n{result.stderr}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, target)
+    return target
 
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--force", action="store_true")
     parser.add_argument("--verbose", action="store_true")
+    parser.add_argument("--trace", action="store_true", help="build the phase-trace variant libnqb_trace.so")
     args = parser.parse_args()
-    path = build(force=args.force, verbose=args.verbose)
+    path = build(force=args.force, verbose=args.verbose, trace=args.trace)
     print(path)
 
 

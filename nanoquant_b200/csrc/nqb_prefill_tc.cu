@@ -542,11 +542,11 @@ __device__ __forceinline__ void load8(const void *base, int64_t idx, int32_t dt,
 // of a row is the 16 columns {32g + 8h + j, 32g + 16 + 8h + j : j < 8}
 // (g = u / 2, h = u % 2): exactly the fp16 positions [32g + 16h, +16) of the
 // pair order, so every thread loads and stores whole 16-byte vectors.
-constexpr int kPrepThreads = 128;
+constexpr int kPrepThreads = 128;  // threads per row for rows up to 512 units (8192 columns)
 
-template <int kUnits>
-__global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid_constant__ PrepParams p) {
-  __shared__ float s_max[kPrepThreads / 32];
+template <int kUnits, int kRowThreads = kPrepThreads>
+__global__ void __launch_bounds__(kRowThreads) prepare_rows_kernel(const __grid_constant__ PrepParams p) {
+  __shared__ float s_max[kRowThreads / 32];
   const int64_t t = blockIdx.x;
   const PrepMember &m = p.m[blockIdx.y];
   const int64_t row = t * p.src_stride + m.src_offset;
@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid
   float mx = 0.0f;
 #pragma unroll
   for (int i = 0; i < kUnits; ++i) {
-    const int64_t u = tid + i * kPrepThreads;
+    const int64_t u = tid + i * kRowThreads;
     if (u < units) {
       const int64_t c0 = (u >> 1) * 32 + (u & 1) * 8;
       load8(p.src, row + c0, p.src_dtype, m.k_valid - c0, vsrc, v[i]);
@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid
   __syncthreads();
   mx = s_max[0];
 #pragma unroll
-  for (int w = 1; w < kPrepThreads / 32; ++w) mx = fmaxf(mx, s_max[w]);
+  for (int w = 1; w < kRowThreads / 32; ++w) mx = fmaxf(mx, s_max[w]);
   int e2 = 0;
   if (mx > 0.0f && isfinite(mx)) {
     int ex;
@@ -590,7 +590,7 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid
   uint4 *out = reinterpret_cast<uint4 *>(m.out + t * m.k_pad);
 #pragma unroll
   for (int i = 0; i < kUnits; ++i) {
-    const int64_t u = tid + i * kPrepThreads;
+    const int64_t u = tid + i * kRowThreads;
     if (u < units) {
       uint32_t w[8];
 #pragma unroll
@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(kPrepThreads) prepare_rows_kernel(const __grid
   if (blockIdx.y == 0 && t < p.pairs_count) {
     const __half *src = p.pairs_src[t];
     __half *dst = p.pairs_out[t];
-    for (int64_t pos = tid; pos < p.pairs_pad; pos += kPrepThreads) {
+    for (int64_t pos = tid; pos < p.pairs_pad; pos += kRowThreads) {
       const int64_t col = (pos & ~int64_t(31)) + ((pos & 31) >> 1) + ((pos & 1) << 4);
       dst[pos] = col < p.pairs_valid ? src[col] : __float2half_rn(0.0f);
     }
@@ -643,8 +643,8 @@ bool prefill_eligible(const nqb_linear_desc *layers, int count, int32_t x_dtype,
   return true;
 }
 
-// Longest row the register-resident pre-pass takes (8 units per thread).
-constexpr int64_t kRowKernelMaxCols = 8 * pf::kPrepThreads * 16;
+// Longest row the register-resident pre-pass takes (8 units per thread, 256 threads).
+constexpr int64_t kRowKernelMaxCols = 8 * 256 * 16;
 
 // With fp16 pre scales (and rows the row pre-pass takes) stage 1 folds pre
 // into the sign expansion, so all members read one fp16 copy of x.
@@ -753,8 +753,10 @@ static int launch_prepare(const pf::PrepParams &params, cudaStream_t stream, con
     pf::prepare_rows_kernel<2><<<grid, pf::kPrepThreads, 0, stream>>>(params);
   } else if (units <= 4 * pf::kPrepThreads) {
     pf::prepare_rows_kernel<4><<<grid, pf::kPrepThreads, 0, stream>>>(params);
-  } else if (units <= 8 * pf::kPrepThreads) {
-    pf::prepare_rows_kernel<8><<<grid, pf::kPrepThreads, 0, stream>>>(params);
+  } else if (units <= 4 * 256) {  // wide rows: 256 threads per row keep 16 warps per SM
+    pf::prepare_rows_kernel<4, 256><<<grid, 256, 0, stream>>>(params);
+  } else if (units <= 8 * 256) {
+    pf::prepare_rows_kernel<8, 256><<<grid, 256, 0, stream>>>(params);
   } else {
     if (params.pairs_count != 0) return fail(NQB_ERR_UNSUPPORTED, "folded pre scales need the row pre-pass");
     pf::prepare_kernel<<<static_cast<unsigned>((params.tokens + 7) / 8), 256, 0, stream>>>(params);  // warp per token

@@ -130,6 +130,52 @@ struct Params {
 
 __device__ int g_prog_error;
 
+// Phase trace (built with NQB_PHASE_TRACE only): per CTA and stage, the SM
+// cycles consumer thread 0 spent in each phase of the stage.
+enum TracePhase {
+  kTraceTables = 0,   // stage start -> first quantisation (tables, accumulator reset)
+  kTraceQuantise,     // activation loads, maxima, digit scatter
+  kTraceWaitSigns,    // waiting for sign slices in the ring
+  kTraceMma,          // sign-word loads + MMA issue
+  kTraceDrain,        // accumulators -> fp32 partials
+  kTraceSend,         // partials -> leaders (st.async), row-scale loads
+  kTraceWaitQuarters, // waiting for the four quarters
+  kTraceSum,          // fixed-order sum
+  kTraceRelease,      // exchange buffers handed back
+  kTraceEpilogue,     // scales, bias, salient columns, stores
+  kTraceGridBarrier,  // grid barrier after the stage
+  kTracePhases
+};
+constexpr int kTraceMaxCtas = 160;
+constexpr int kTraceMaxStages = 512;
+#ifdef NQB_PHASE_TRACE
+__device__ long long g_trace[kTraceMaxCtas][kTraceMaxStages][kTracePhases];
+#define NQB_TRACE_BEGIN            \
+  long long trace_t = clock64();   \
+  long long trace_c[kTracePhases]; \
+  for (int trace_k = 0; trace_k < kTracePhases; ++trace_k) trace_c[trace_k] = 0;
+#define NQB_TRACE(phase)             \
+  do {                               \
+    const long long now = clock64(); \
+    trace_c[phase] += now - trace_t; \
+    trace_t = now;                   \
+  } while (0)
+#define NQB_TRACE_FLUSH(stage)                                                                 \
+  do {                                                                                         \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceMaxCtas && (stage) < kTraceMaxStages)           \
+      for (int trace_k = 0; trace_k < kTracePhases; ++trace_k)                                 \
+        g_trace[blockIdx.x][stage][trace_k] = trace_c[trace_k];                                \
+  } while (0)
+#else
+#define NQB_TRACE_BEGIN
+#define NQB_TRACE(phase) \
+  do {                   \
+  } while (0)
+#define NQB_TRACE_FLUSH(stage) \
+  do {                         \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_prog_error, 0, code); }
 
 __device__ __forceinline__ bool program_failed() { return *reinterpret_cast<volatile int *>(&g_prog_error) != 0; }
@@ -473,6 +519,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       const StageInfo &op = s_info[g & 1];
       const int ib = 0;
       const int ie = op.n_items;
+      NQB_TRACE_BEGIN
       for (int gb = ib; gb < ie; gb += p.group) {
         const int ge = min(gb + p.group, ie);
         for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
@@ -489,6 +536,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
             int e[kT];
             long long Q[kT];
+            NQB_TRACE(kTraceTables);
             if (st == 1) {
               const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
               mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
@@ -503,6 +551,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
               const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
               mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
             }
+            NQB_TRACE(kTraceQuantise);
             for (int j = j0; j < j1; ++j) {
               int32_t d[kSets][kNT][4];
 #pragma unroll
@@ -512,7 +561,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
 #pragma unroll
                   for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
               for (int sl = 0; sl < nst; ++sl) {
+                NQB_TRACE(kTraceMma);
                 if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+                NQB_TRACE(kTraceWaitSigns);
                 const mmad::SliceWords w =
                     mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
                 __syncwarp();
@@ -523,7 +574,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                 }
                 mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
               }
+              NQB_TRACE(kTraceMma);
               mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
+              NQB_TRACE(kTraceDrain);
             }
           }
           j0 = j1;
@@ -561,7 +614,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             }
           }
         }
+        NQB_TRACE(kTraceSend);
         if (!wait_cluster(&s_x_full, xg & 1)) ok = false;
+        NQB_TRACE(kTraceWaitQuarters);
         // ---- leaders: fixed-order sum of the four quarters into registers,
         // then release the exchange buffers before any global store
         float vsum[kLead][kT];
@@ -579,10 +634,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             vsum[sidx][t] = v;
           }
         }
+        NQB_TRACE(kTraceSum);
         mmad::consumer_sync();  // done reading this CTA's leader buffers
         if (tid == 0)
           for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive_relaxed(&s_x_free, r);
         ++xg;
+        NQB_TRACE(kTraceRelease);
         // ---- epilogue of the led tiles
 #pragma unroll
         for (int sidx = 0; sidx < kLead; ++sidx) {
@@ -650,7 +707,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           }
         }
       }
+      NQB_TRACE(kTraceEpilogue);
       if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g));
+      NQB_TRACE(kTraceGridBarrier);
+      NQB_TRACE_FLUSH(g);
     }
   }
 
@@ -1154,6 +1214,29 @@ int nqb_program_destroy(nqb_program *program) {
   if (program->scales != nullptr) cudaFree(program->scales);
   delete program;
   return ok();
+}
+
+int nqb_program_trace(const nqb_program *program, int64_t *cycles, size_t count) {
+#ifdef NQB_PHASE_TRACE
+  if (program == nullptr || cycles == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program or cycles is NULL");
+  const size_t need = static_cast<size_t>(program->ctas) * program->params.stages * nqb::prog::kTracePhases;
+  if (count < need) return fail(NQB_ERR_INVALID_ARGUMENT, "trace buffer needs %zu entries", need);
+  static long long host[nqb::prog::kTraceMaxCtas][nqb::prog::kTraceMaxStages][nqb::prog::kTracePhases];
+  NQB_CUDA(cudaMemcpyFromSymbol(host, nqb::prog::g_trace, sizeof(host)), "read the phase trace");
+  const int ctas = std::min(program->ctas, nqb::prog::kTraceMaxCtas);
+  const int stages = std::min(program->params.stages, nqb::prog::kTraceMaxStages);
+  std::memset(cycles, 0, need * sizeof(int64_t));
+  for (int c = 0; c < ctas; ++c)
+    for (int g = 0; g < stages; ++g)
+      for (int k = 0; k < nqb::prog::kTracePhases; ++k)
+        cycles[(static_cast<size_t>(c) * program->params.stages + g) * nqb::prog::kTracePhases + k] = host[c][g][k];
+  return ok();
+#else
+  (void)program;
+  (void)cycles;
+  (void)count;
+  return fail(NQB_ERR_UNSUPPORTED, "phase tracing needs the trace build (python -m nanoquant_b200.build --trace)");
+#endif
 }
 
 int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size) {

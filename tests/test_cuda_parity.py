@@ -378,13 +378,14 @@ def test_prefill_scale_and_input_dtypes(scale_dtype: torch.dtype, x_dtype: torch
     assert ctypes_status() == 0
 
 
-def test_prefill_rows_longer_than_the_row_pre_pass() -> None:
-    """in_features past 16384 columns takes the warp-per-token pre-pass (pre not folded)."""
+@pytest.mark.parametrize("n", (16416, 33000))
+def test_prefill_rows_longer_than_the_row_pre_pass(n: int) -> None:
+    """Wide rows: 256 threads per row (16416), and past 32768 columns the warp-per-token pre-pass (pre not folded)."""
 
-    state = _random_state(16416, 160, 96, seed=9)
+    state = _random_state(n, 160, 96, seed=9)
     backend = CudaPackedSm100Backend()
     layer = backend.prepare(state, "cuda")
-    x = torch.randn(20, 16416, generator=torch.Generator().manual_seed(4)).bfloat16()
+    x = torch.randn(20, n, generator=torch.Generator().manual_seed(4)).bfloat16()
     got = backend.linear(x.cuda(), layer)
     expected = po.packed_linear(x.float().numpy(), oracle_from_state(state), accumulate="float64")
     assert _relative_max_error(got, expected) <= PREFILL_BOUND
