@@ -203,6 +203,21 @@ int nqb_decode_product_codebook(const int32_t *free_words, int64_t free_rows, in
                                 const int16_t *second, int32_t *words_out, void *stream);
 
 /*
+ * Expand a mixed-V right factor (format mixed-v-free-k10-pair9-v1) to
+ * layout-v1 words on the device: rows [0, free_rows) are copied from
+ * free_words [free_rows, ceil(columns/32)]; every later word is
+ * codebook[index] with the bit pair `pair` flipped, read from one 19-bit
+ * record (index = bits 0..9, pair = bits 10..18, LSB-first across the
+ * payload words; pairs (a, b), a < b < 32, numbered lexicographically).
+ * codebook holds 1024 words.  Pair ids above 495 are the caller's to reject
+ * (the kernel stays in bounds for any payload).  Replaces
+ * launch_decode_mixed_v_right_words (reference cuda_kernels.py:877-910, the
+ * Triton kernel at :11-62).
+ */
+int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t rank, int64_t columns,
+                       const int32_t *payload, const int32_t *codebook, int32_t *words_out, void *stream);
+
+/*
  * Kernel-native copy of a layout-v1 sign matrix for the tensor-core path:
  * rows are grouped in tiles of 128; within a tile, for every 4-word chunk of a
  * row, the 128 rows' 16-byte chunks are stored consecutively; rows and chunks

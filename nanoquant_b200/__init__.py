@@ -43,6 +43,16 @@ from nanoquant_b200.packed import (
     supports_vector_word_loads,
     unpack_sign_matrix,
 )
+from nanoquant_b200.mixed_v import (
+    MIXED_V_FORMAT_VERSION,
+    MixedVLayerState,
+    decode_mixed_v_right_words,
+    mixed_v_correction_pair_table,
+    mixed_v_from_packed_words,
+    mixed_v_payload_word_count,
+    pack_mixed_v_records,
+    unpack_mixed_v_records,
+)
 from nanoquant_b200.product_codebook import (
     PRODUCT_CODEBOOK_FORMAT_VERSION,
     ProductCodebookLayerState,
@@ -55,6 +65,14 @@ from nanoquant_b200.product_codebook import (
 )
 
 __all__ = [
+    "MIXED_V_FORMAT_VERSION",
+    "MixedVLayerState",
+    "decode_mixed_v_right_words",
+    "mixed_v_correction_pair_table",
+    "mixed_v_from_packed_words",
+    "mixed_v_payload_word_count",
+    "pack_mixed_v_records",
+    "unpack_mixed_v_records",
     "BackendCapabilities",
     "CUDA_SM100_BACKEND_NAME",
     "CUDA_SM100_BACKEND_VERSION",

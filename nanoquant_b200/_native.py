@@ -147,6 +147,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
+    "nqb_decode_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -430,4 +430,17 @@ int nqb_decode_product_codebook(const int32_t *free_words, int64_t free_rows, in
   return ok();
 }
 
+int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t rank, int64_t columns,
+                       const int32_t *payload, const int32_t *codebook, int32_t *words_out, void *stream) {
+  if (free_words == nullptr || payload == nullptr || codebook == nullptr || words_out == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "mixed-V operand is NULL");
+  if (free_rows <= 0 || free_rows >= rank || columns <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "mixed-V free rows must be between zero and rank");
+  NQB_CHECK(launch_decode_mixed_v(reinterpret_cast<const uint32_t *>(free_words), free_rows, rank, columns,
+                                  reinterpret_cast<const uint32_t *>(payload),
+                                  reinterpret_cast<const uint32_t *>(codebook),
+                                  reinterpret_cast<uint32_t *>(words_out), reinterpret_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
 }  // extern "C"

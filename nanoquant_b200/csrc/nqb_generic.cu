@@ -248,6 +248,40 @@ __global__ void decode_codebook_kernel(const uint32_t *free_words, int64_t free_
            (static_cast<uint32_t>(second[record >> 8]) << 16);
 }
 
+// Mixed-V right factor: the first free_rows rows are plain words; every
+// word of the remaining rows is one 19-bit record (bits 0..9: index into
+// the 1024-word codebook, bits 10..18: id of the bit pair to flip), records
+// packed LSB-first across consecutive uint32 words.  Pair ids enumerate
+// (a, b), a < b < 32, in lexicographic order.  Shifts and the codebook index
+// are masked, so any payload stays in bounds; ids 496..511 are rejected by
+// the host before a launch.
+__device__ __forceinline__ uint32_t pair_mask(uint32_t id) {
+  uint32_t a = 0;
+  while (a < 30 && id >= 31 - a) {  // pairs (a, a+1 .. 31): 31 - a of them
+    id -= 31 - a;
+    ++a;
+  }
+  const uint32_t b = a + 1 + id;
+  return (1u << a) | (1u << (b & 31u));
+}
+
+__global__ void decode_mixed_v_kernel(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t wpr,
+                                      const uint32_t *payload, const uint32_t *codebook, uint32_t *out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rank * wpr) return;
+  if (i < free_rows * wpr) {
+    out[i] = free_words[i];
+    return;
+  }
+  const int64_t bit = (i - free_rows * wpr) * kMixedRecordBits;
+  const int64_t word = bit >> 5;
+  const uint32_t shift = static_cast<uint32_t>(bit & 31);
+  uint32_t record = payload[word] >> shift;
+  if (shift > 32 - kMixedRecordBits) record |= payload[word + 1] << (32 - shift);
+  record &= (1u << kMixedRecordBits) - 1;
+  out[i] = codebook[record & 1023u] ^ pair_mask(record >> 10);
+}
+
 // --------------------------------------------------------------- launch ---
 
 static int set_smem(const void *fn, size_t bytes) { return ensure_dynamic_smem(fn, bytes); }
@@ -310,6 +344,15 @@ int launch_unpack(const uint32_t *words, int64_t rows, int64_t cols, float *sign
   unpack_signs_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(words, rows, cols, wpr,
                                                                                       signs, bad_rows);
   NQB_CUDA(cudaGetLastError(), "unpack_signs_kernel launch");
+  return NQB_OK;
+}
+
+int launch_decode_mixed_v(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,
+                          const uint32_t *payload, const uint32_t *codebook, uint32_t *out, cudaStream_t stream) {
+  const int64_t items = rank * ((cols + 31) / 32);
+  decode_mixed_v_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
+      free_words, free_rows, rank, (cols + 31) / 32, payload, codebook, out);
+  NQB_CUDA(cudaGetLastError(), "decode_mixed_v_kernel launch");
   return NQB_OK;
 }
 

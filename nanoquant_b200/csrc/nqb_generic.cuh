@@ -84,6 +84,9 @@ int launch_pack(const void *signs, int32_t dt, int64_t rows, int64_t cols, uint3
                 cudaStream_t stream);
 int launch_unpack(const uint32_t *words, int64_t rows, int64_t cols, float *signs, int32_t *bad_rows,
                   cudaStream_t stream);
+constexpr int kMixedRecordBits = 19;  // 10-bit codebook index + 9-bit pair id
+int launch_decode_mixed_v(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,
+                          const uint32_t *payload, const uint32_t *codebook, uint32_t *out, cudaStream_t stream);
 int launch_decode_codebook(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,
                            const uint16_t *payload, const uint16_t *first, const uint16_t *second,
                            uint32_t *out, cudaStream_t stream);

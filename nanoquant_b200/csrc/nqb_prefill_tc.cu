@@ -41,24 +41,26 @@
 namespace nqb {
 namespace pf {
 
-constexpr int kTileRows = 128;     // sign rows per CTA (MMA M)
-constexpr int kTokTile = 256;      // tokens per CTA (MMA N)
+constexpr int kTileRows = 128;     // sign rows per tile (MMA M)
+constexpr int kTokTile = 192;      // tokens per tile (MMA N): two accumulators + two A buffers fill TMEM
 constexpr int kKStep = 128;        // K columns per pipeline step = one 4-word sign chunk
-constexpr int kStages = 3;
-constexpr int kAtomBytes = kTokTile * 128;             // 256 tokens x 64 fp16 (one 128-byte swizzle column)
+constexpr int kStages = 4;
+constexpr int kAtomBytes = kTokTile * 128;             // 192 tokens x 64 fp16 (one 128-byte swizzle column)
 constexpr int kBStageBytes = 2 * kAtomBytes;           // 128 K columns
 constexpr int kChunkBytes = kTileRows * 16;            // one 4-word chunk of a 128-row tile
-constexpr int kStageBytes = kBStageBytes + kChunkBytes;
 constexpr int kACols = kKStep / 2;                     // TMEM columns of A per step
-constexpr int kDCol = 2 * kACols;                      // accumulator after 2 buffers of A
-constexpr int kCtasPerSm = 1;
-constexpr uint32_t kTmemCols = 512;  // 2 x 64 columns of signs + 256 accumulator columns (power of two)
-constexpr int kThreads = 192;
-constexpr uint32_t kSpinLimit = 1u << 28;
+constexpr int kDCol = 2 * kACols;                      // accumulator 0; accumulator 1 follows
+constexpr uint32_t kTmemCols = 512;                    // 2 x 64 (A) + 2 x 192 (D)
+constexpr int kThreads = 320;                          // 10 warps: 4 expand, 1 TMA, 1 MMA, 4 epilogue
+constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr int kPreBytes = kKStep * 2;  // fp16 pre scales of one K step, pair order
-constexpr int kSmemBytes = kStages * (kStageBytes + kPreBytes) + 1024;  // +1024 for the swizzle alignment
-static_assert(kCtasPerSm * (kSmemBytes + 2048) <= 228 * 1024, "CTAs must fit one SM's shared memory");
-static_assert(kCtasPerSm * kTmemCols <= 512, "CTAs must fit one SM's tensor memory");
+constexpr int kOutTok = 16;                            // tokens per output box (TMA store)
+constexpr int kOutBytes = kOutTok * kTileRows * 4;     // one fp32 [16 tokens][128 rows] box
+constexpr int kSmemBytes =
+    kStages * (kBStageBytes + kChunkBytes + kPreBytes) + 2 * kOutBytes + 1024;  // +1024: swizzle alignment
+static_assert(kDCol + 2 * kTokTile <= static_cast<int>(kTmemCols), "two accumulators must fit tensor memory");
+static_assert(kSmemBytes + 4096 <= 227 * 1024, "the stage ring must fit shared memory");
+static_assert(kAtomBytes % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
 
 struct Member {
   const uint4 *tiles;   // row-interleaved sign tiles (nqb_repack_signs)
@@ -66,7 +68,7 @@ struct Member {
   int64_t rows;
   int32_t wc;           // 4-word chunks per row
   int32_t row_tiles;
-  int32_t cta_begin;    // first blockIdx.x of this member (one CTA per row tile)
+  int32_t cta_begin;    // first row tile of this member among all members
   int32_t k_steps;      // K steps of 128 columns
   const void *row_scale;  // mid (stage 1) / post (stage 2)
   const int32_t *exps;    // per-token exponent e of the fp16 activations
@@ -81,12 +83,14 @@ struct Member {
   const void *outlier_values;
   int32_t outlier_value_dtype;
   const void *outlier_scales;
-  int32_t tma_store;  // 1: write the tile with one TMA store through shared memory
+  int32_t tma_store;  // 1: output boxes leave through shared memory by TMA store
 };
 
 struct Params {
   Member m[kMaxMembersTc];
   int32_t count;
+  int32_t total_row_tiles;  // row tiles of all members
+  int32_t tok_tiles;
   int64_t tokens;
   int32_t scale_dtype;
   const void *x;  // original input (stage-2 salient columns)
@@ -131,13 +135,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// Issues one TMA store of a shared-memory box as its own bulk group.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int32_t x, int32_t y, uint32_t src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(x), "r"(y), "r"(src)
                : "memory");
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -193,31 +197,80 @@ __device__ __forceinline__ void expand_and_store(uint4 chunk, uint32_t taddr, co
   }
 }
 
+// Persistent tile loop.  Tile t (of Σ row tiles × token tiles, token-tile
+// major so concurrent CTAs share their activations in L2) goes to CTA
+// t mod gridDim.x.  Four roles run concurrently over the CTA's tiles:
+//   warps 0-3  expand each K step's sign words into TMEM (A, double buffer);
+//              lane 0 of each warp arrives for the warp;
+//   warp 4     streams B boxes, sign chunks and pre pairs into the stage ring;
+//   warp 5     issues the MMAs of a tile into accumulator d = tile & 1;
+//   warps 6-9  drain accumulator d of the previous tile (epilogue) while the
+//              MMAs fill the other one.
+// Every wait is bounded and gives up early once any wait has failed.
+struct TileRef {
+  int g;      // member
+  int tile0;  // row tile within the member
+  int tok0;   // first token
+};
+
+__device__ __forceinline__ TileRef tile_ref(const Params &p, int t) {
+  const int tok_tile = t / p.total_row_tiles;
+  const int rt = t - tok_tile * p.total_row_tiles;
+  int g = 0;
+  for (int i = 1; i < p.count; ++i)
+    if (rt >= p.m[i].cta_begin) g = i;
+  return TileRef{g, rt - p.m[g].cta_begin, tok_tile * kTokTile};
+}
+
+__device__ __forceinline__ bool pf_failed() { return *reinterpret_cast<volatile int *>(&g_pf_error) != 0; }
+
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && pf_failed()) return false;
+  }
+  atomicCAS(&g_pf_error, 0, NQB_ERR_TIMEOUT);
+  return false;
+}
+
+// Bounded wait with back-off by one lane, then the warp: for the epilogue
+// warps, which wait out a whole main loop and must not load the shared-memory
+// pipe the expansion warps use.
+__device__ __forceinline__ void pf_wait_warp(uint64_t *bar, uint32_t parity) {
+  if ((threadIdx.x & 31) == 0) {
+    uint32_t i = 0;
+    while (!ptx::mbar_try_wait(bar, parity)) {
+      if (++i >= kSpinLimit) {
+        atomicCAS(&g_pf_error, 0, NQB_ERR_TIMEOUT);
+        break;
+      }
+      if ((i & 255) == 255 && pf_failed()) break;
+      __nanosleep(200);
+    }
+  }
+  __syncwarp();
+}
+
 template <bool kStage2>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map0,
                         const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2,
                         const __grid_constant__ CUtensorMap out0, const __grid_constant__ CUtensorMap out1,
                         const __grid_constant__ CUtensorMap out2) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[kStages], empty[kStages], a_full[2], a_empty[2], d_full;
+  __shared__ uint64_t full[kStages], empty[kStages], a_full[2], a_empty[2], d_full[2], d_empty[2];
   __shared__ uint32_t s_tmem;
-  __shared__ float s_unscale[kTokTile];  // 2^-e of each token of the tile (0 past the last token)
+  __shared__ float s_unscale[2][kTokTile];  // 2^-e of each token of the tile in accumulator d (0 past the end)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *s_b = smem;                                   // [kStages][kBStageBytes], 1024-aligned atoms
+  uint8_t *s_chunk = smem + kStages * kBStageBytes;      // [kStages][kChunkBytes]
+  uint8_t *s_pre = s_chunk + kStages * kChunkBytes;      // [kStages][kPreBytes]
+  float *s_out = reinterpret_cast<float *>(s_pre + kStages * kPreBytes);  // [2][kOutTok][kTileRows] fp32
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-
-  int g = 0;
-  for (int i = 1; i < p.count; ++i)
-    if (static_cast<int32_t>(blockIdx.x) >= p.m[i].cta_begin) g = i;
-  const Member &m = p.m[g];
-  const CUtensorMap *map = g == 0 ? &map0 : (g == 1 ? &map1 : &map2);
-  const CUtensorMap *out_map = g == 0 ? &out0 : (g == 1 ? &out1 : &out2);
-  const int tile0 = static_cast<int>(blockIdx.x) - m.cta_begin;
-  const int tok0 = static_cast<int>(blockIdx.y) * kTokTile;
-  const int K = m.k_steps;
+  const int tiles = p.total_row_tiles * p.tok_tiles;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -225,165 +278,183 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       ptx::mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      ptx::mbar_init(&a_full[b], 128);
+      ptx::mbar_init(&a_full[b], 4);  // one arrival per expansion warp
       ptx::mbar_init(&a_empty[b], 1);
+      ptx::mbar_init(&d_full[b], 1);
+      ptx::mbar_init(&d_empty[b], 128);
     }
-    ptx::mbar_init(&d_full, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 0) {
     ptx::tmem_alloc(&s_tmem, kTmemCols);
     ptx::tmem_relinquish();
   }
-  for (int i = tid; i < kTokTile; i += kThreads) {
-    const int64_t tok = tok0 + i;
-    s_unscale[i] = tok < p.tokens ? exp2_int(-m.exps[tok]) : 0.0f;
-  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = s_tmem;
-  bool ok = true;
 
   if (warp == 4) {
-    if (lane == 0) {  // producer
-      const uint32_t bytes = kStageBytes + (m.pre_pairs != nullptr ? kPreBytes : 0);
-      for (int s = 0; s < K; ++s) {
-        const int slot = s % kStages;
-        if (s >= kStages && !ptx::mbar_wait_bounded(&empty[slot], ((s / kStages) - 1) & 1, kSpinLimit)) ok = false;
-        const uint32_t base = ptx::smem_u32(smem + slot * kStageBytes);
-        const uint32_t bar = ptx::smem_u32(&full[slot]);
-        expect_tx(&full[slot], bytes);
-        tma_load_2d(base, map, s * kKStep, tok0, bar);
-        tma_load_2d(base + kAtomBytes, map, s * kKStep + 64, tok0, bar);
-        const uint8_t *src =
-            reinterpret_cast<const uint8_t *>(m.tiles) + (static_cast<size_t>(tile0) * m.wc + s) * kChunkBytes;
-        bulk_load(base + kBStageBytes, src, kChunkBytes, bar);
-        if (m.pre_pairs != nullptr)
-          bulk_load(ptx::smem_u32(smem + kStages * kStageBytes + slot * kPreBytes), m.pre_pairs + s * kKStep, kPreBytes,
-                    bar);
+    if (lane == 0) {  // ---- producer
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const TileRef tr = tile_ref(p, t);
+        const Member &m = p.m[tr.g];
+        const CUtensorMap *map = tr.g == 0 ? &map0 : (tr.g == 1 ? &map1 : &map2);
+        const uint32_t bytes = kBStageBytes + kChunkBytes + (m.pre_pairs != nullptr ? kPreBytes : 0);
+        for (int s = 0; s < m.k_steps; ++s, ++it) {
+          const int slot = static_cast<int>(it % kStages);
+          if (it >= kStages) pf_wait(&empty[slot], ((it / kStages) - 1) & 1);
+          const uint32_t bar = ptx::smem_u32(&full[slot]);
+          expect_tx(&full[slot], bytes);
+          const uint32_t base = ptx::smem_u32(s_b + slot * kBStageBytes);
+          tma_load_2d(base, map, s * kKStep, tr.tok0, bar);
+          tma_load_2d(base + kAtomBytes, map, s * kKStep + 64, tr.tok0, bar);
+          const uint8_t *src =
+              reinterpret_cast<const uint8_t *>(m.tiles) + (static_cast<size_t>(tr.tile0) * m.wc + s) * kChunkBytes;
+          bulk_load(ptx::smem_u32(s_chunk + slot * kChunkBytes), src, kChunkBytes, bar);
+          if (m.pre_pairs != nullptr)
+            bulk_load(ptx::smem_u32(s_pre + slot * kPreBytes), m.pre_pairs + s * kKStep, kPreBytes, bar);
+        }
       }
     }
   } else if (warp == 5) {
-    if (lane == 0) {  // MMA issuer
+    if (lane == 0) {  // ---- MMA issuer
       const uint32_t idesc = idesc_f16_m128(kTokTile);
-      for (int s = 0; s < K; ++s) {
-        const int slot = s % kStages;
-        const int buf = s & 1;
-        if (!ptx::mbar_wait_bounded(&full[slot], (s / kStages) & 1, kSpinLimit)) ok = false;
-        if (!ptx::mbar_wait_bounded(&a_full[buf], (s >> 1) & 1, kSpinLimit)) ok = false;
+      uint32_t it = 0, tc = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+        const TileRef tr = tile_ref(p, t);
+        const int k_steps = p.m[tr.g].k_steps;
+        const uint32_t d = tc & 1;
+        if (tc >= 2) pf_wait(&d_empty[d], ((tc >> 1) - 1) & 1);
         ptx::tc_fence_after();
-        const uint32_t bbase = ptx::smem_u32(smem + slot * kStageBytes);
+        for (int s = 0; s < k_steps; ++s, ++it) {
+          const int slot = static_cast<int>(it % kStages);
+          pf_wait(&full[slot], (it / kStages) & 1);
+          const uint32_t buf = it & 1;
+          pf_wait(&a_full[buf], (it >> 1) & 1);
+          ptx::tc_fence_after();
+          const uint32_t bbase = ptx::smem_u32(s_b + slot * kBStageBytes);
 #pragma unroll
-        for (int k16 = 0; k16 < kKStep / 16; ++k16) {
-          const uint64_t bdesc = desc_sw128(bbase + (k16 >> 2) * kAtomBytes + (k16 & 3) * 32);
-          mma_f16_ts(tmem + kDCol, tmem + buf * kACols + k16 * 8, bdesc, idesc, (s > 0 || k16 > 0) ? 1u : 0u);
+          for (int k16 = 0; k16 < kKStep / 16; ++k16) {
+            const uint64_t bdesc = desc_sw128(bbase + (k16 >> 2) * kAtomBytes + (k16 & 3) * 32);
+            mma_f16_ts(tmem + kDCol + d * kTokTile, tmem + buf * kACols + k16 * 8, bdesc, idesc,
+                       (s > 0 || k16 > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[slot]);
+          ptx::mma_commit(&a_empty[buf]);
         }
-        ptx::mma_commit(&empty[slot]);
-        ptx::mma_commit(&a_empty[buf]);
+        ptx::mma_commit(&d_full[d]);
       }
-      ptx::mma_commit(&d_full);
     }
-  } else {  // warps 0-3: sign expansion, then the epilogue
+  } else if (warp < 4) {
+    // ---- sign expansion into TMEM: thread tid owns tile row tid (TMEM lane tid)
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    for (int s = 0; s < K; ++s) {
-      const int slot = s % kStages;
-      const int buf = s & 1;
-      if (!ptx::mbar_wait_bounded(&full[slot], (s / kStages) & 1, kSpinLimit)) ok = false;
-      const uint4 *chunks = reinterpret_cast<const uint4 *>(smem + slot * kStageBytes + kBStageBytes);
-      const uint4 c0 = chunks[tid];
-      if (s >= 2) {
-        if (!ptx::mbar_wait_bounded(&a_empty[buf], ((s >> 1) - 1) & 1, kSpinLimit)) ok = false;
-        ptx::tc_fence_after();
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const TileRef tr = tile_ref(p, t);
+      const Member &m = p.m[tr.g];
+      for (int s = 0; s < m.k_steps; ++s, ++it) {
+        const int slot = static_cast<int>(it % kStages);
+        pf_wait(&full[slot], (it / kStages) & 1);
+        const uint4 c0 = reinterpret_cast<const uint4 *>(s_chunk + slot * kChunkBytes)[tid];
+        const uint32_t buf = it & 1;
+        if (it >= 2) {
+          pf_wait(&a_empty[buf], ((it >> 1) - 1) & 1);
+          ptx::tc_fence_after();
+        }
+        const uint4 *pre = m.pre_pairs != nullptr ? reinterpret_cast<const uint4 *>(s_pre + slot * kPreBytes) : nullptr;
+        expand_and_store(c0, tmem + lane_base + buf * kACols, pre);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[buf]);
       }
-      const uint4 *pre = m.pre_pairs != nullptr
-                             ? reinterpret_cast<const uint4 *>(smem + kStages * kStageBytes + slot * kPreBytes)
-                             : nullptr;
-      expand_and_store(c0, tmem + lane_base + buf * kACols, pre);
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      mbar_arrive(&a_full[buf]);
     }
-    if (!ptx::mbar_wait_bounded(&d_full, 0, kSpinLimit)) ok = false;
-    ptx::tc_fence_after();
-    // Epilogue.  Every value an output needs besides the accumulator is read
-    // from shared memory or registers: a global load between the global
-    // stores would be ordered behind them (possible aliasing) and serialise.
-    const int64_t row = static_cast<int64_t>(tile0) * kTileRows + tid;
-    const bool live = row < m.rows;
-    const float rscale = live ? load_as_float(m.row_scale, row, p.scale_dtype) : 0.0f;
-    float bias = 0.0f;
-    // stage 2 salient columns: x[tok0 + t][idx_s] staged (fp32) into the now idle
-    // pipeline buffers by the epilogue warps; this row's weights into registers
-    constexpr int kMaxStagedSalient = 64;  // 64 KB of the idle pipeline buffers
-    float *s_xs = reinterpret_cast<float *>(smem);
-    float *s_out = reinterpret_cast<float *>(smem + kMaxStagedSalient * kTokTile * 4);  // [token][row], 128 KB
-    static_assert((kMaxStagedSalient + kTileRows) * kTokTile * 4 <= kStages * kStageBytes, "epilogue buffers");
-    int64_t staged = 0;
-    if constexpr (kStage2) {
-      if (live && m.bias != nullptr) bias = load_as_float(m.bias, row, m.bias_dtype);
-      staged = m.outlier_count <= kMaxStagedSalient ? m.outlier_count : 0;
-      for (int64_t i = tid; i < staged * kTokTile; i += kTileRows) {
-        const int64_t t = i / staged, sidx = i - t * staged;
-        const int64_t tok = tok0 + t;
-        s_xs[i] = tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx], p.x_dtype) : 0.0f;
+  } else {
+    // ---- epilogue warps 6-9: warp w reads TMEM lanes 32 * (w % 4) .. +32.
+    // Each 16-token half of a 32-column TMEM load becomes one fp32
+    // [16 tokens][128 rows] box in shared memory (two buffers) that thread 0
+    // of the group writes out with a TMA store; the store of the box two
+    // halves back must have finished reading its buffer first.  Rows past the
+    // member and tokens past the end are clipped by the store.
+    const int et = tid - 6 * 32;  // 0..127
+    const int quarter = warp & 3;
+    const int lrow = quarter * 32 + lane;  // row within the tile
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    uint32_t tc = 0;
+    uint32_t boxes = 0;  // boxes staged so far; buffer = boxes & 1
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+      const TileRef tr = tile_ref(p, t);
+      const Member &m = p.m[tr.g];
+      const CUtensorMap *out_map = tr.g == 0 ? &out0 : (tr.g == 1 ? &out1 : &out2);
+      const uint32_t d = tc & 1;
+      // the four epilogue warps are past tile tc - 2: s_unscale[d] is free
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      for (int i = et; i < kTokTile; i += 128) {
+        const int64_t tok = tr.tok0 + i;
+        s_unscale[d][i] = tok < p.tokens ? exp2_int(-m.exps[tok]) : 0.0f;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps only
-    }
+      const int64_t row = static_cast<int64_t>(tr.tile0) * kTileRows + lrow;
+      const bool live = row < m.rows;
+      const float rscale = live ? load_as_float(m.row_scale, row, p.scale_dtype) : 0.0f;
+      const float bias = (kStage2 && live && m.bias != nullptr) ? load_as_float(m.bias, row, m.bias_dtype) : 0.0f;
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      pf_wait_warp(&d_full[d], (tc >> 1) & 1);
+      ptx::tc_fence_after();
 #pragma unroll 1
-    for (int c2 = 0; c2 < kTokTile / 32; ++c2) {
-      // two TMEM loads in flight per wait; their registers are read only after it
-      uint32_t v32[32];
-      ptx::tmem_ld16(tmem + lane_base + kDCol + c2 * 32, v32);
-      ptx::tmem_ld16(tmem + lane_base + kDCol + c2 * 32 + 16, v32 + 16);
-      ptx::tmem_wait_ld();
+      for (int c2 = 0; c2 < kTokTile / 32; ++c2) {
+        if (tr.tok0 + c2 * 32 >= p.tokens) break;  // uniform over the group
+        uint32_t v[32];
+        ptx::tmem_ld16(tmem + lane_base + kDCol + d * kTokTile + c2 * 32, v);
+        ptx::tmem_ld16(tmem + lane_base + kDCol + d * kTokTile + c2 * 32 + 16, v + 16);
+        ptx::tmem_wait_ld();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int c = c2 * 2 + half;
-        const uint32_t *v = v32 + half * 16;
-        float out[16];
+        for (int h = 0; h < 2; ++h) {
+          const int t0 = c2 * 32 + h * 16;  // first token of the box within the tile
+          float out[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) out[e] = __uint_as_float(v[e]) * s_unscale[c * 16 + e] * rscale + bias;
-        if constexpr (kStage2) {
-          if (live && m.outlier_count > 0) {
-            for (int64_t sidx = 0; sidx < m.outlier_count; ++sidx) {
-              float w = load_as_float(m.outlier_values, row * m.outlier_count + sidx, m.outlier_value_dtype);
-              if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, sidx, p.scale_dtype);
+          for (int e = 0; e < 16; ++e) out[e] = __uint_as_float(v[h * 16 + e]) * s_unscale[d][t0 + e] * rscale + bias;
+          if constexpr (kStage2) {
+            if (live && m.outlier_count > 0) {
+              for (int64_t sidx = 0; sidx < m.outlier_count; ++sidx) {
+                float w = load_as_float(m.outlier_values, row * m.outlier_count + sidx, m.outlier_value_dtype);
+                if (m.outlier_scales != nullptr) w *= load_as_float(m.outlier_scales, sidx, p.scale_dtype);
+                const int32_t col = m.outlier_indices[sidx];
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const int t = c * 16 + e;
-                const int64_t tok = tok0 + t;
-                const float xv = sidx < staged ? s_xs[t * staged + sidx]
-                                               : (tok < p.tokens ? load_as_float(p.x, tok * p.n + m.outlier_indices[sidx],
-                                                                                 p.x_dtype)
-                                                                 : 0.0f);
-                out[e] += xv * w;
+                for (int e = 0; e < 16; ++e) {
+                  const int64_t tok = tr.tok0 + t0 + e;
+                  if (tok < p.tokens) out[e] += load_as_float(p.x, tok * p.n + col, p.x_dtype) * w;
+                }
               }
             }
           }
-        }
-        if (m.tma_store) {
+          if (m.tma_store) {
+            if (tr.tok0 + t0 >= p.tokens) continue;  // uniform over the group
+            float *buf = s_out + (boxes & 1) * (kOutTok * kTileRows);
+            ++boxes;
+            if (et == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");
 #pragma unroll
-          for (int e = 0; e < 16; ++e) s_out[(c * 16 + e) * kTileRows + tid] = out[e];
-          continue;
-        }
-        if (!live) continue;
+            for (int e = 0; e < 16; ++e) buf[e * kTileRows + lrow] = out[e];
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (et == 0)
+              tma_store_2d(out_map, tr.tile0 * kTileRows, static_cast<int32_t>(tr.tok0 + t0), ptx::smem_u32(buf));
+          } else if (live) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int64_t tok = tok0 + c * 16 + e;
-          if (tok < p.tokens) m.out[tok * m.out_stride + m.out_offset + row] = out[e];
+            for (int e = 0; e < 16; ++e) {
+              const int64_t tok = tr.tok0 + t0 + e;
+              if (tok < p.tokens) m.out[tok * m.out_stride + m.out_offset + row] = out[e];
+            }
+          }
         }
       }
+      ptx::tc_fence_before();
+      mbar_arrive(&d_empty[d]);
     }
-    if (m.tma_store) {
-      // The member's map starts at its first output column; rows past the
-      // member and tokens past `tokens` are clipped by the TMA unit.
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid == 0) tma_store_2d(out_map, tile0 * kTileRows, tok0, ptx::smem_u32(s_out));
-    }
+    if (et == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
-  if (!ok) atomicCAS(&g_pf_error, 0, NQB_ERR_TIMEOUT);
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem, kTmemCols);
@@ -706,14 +777,14 @@ static int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 *out) {
   return NQB_OK;
 }
 
-// fp32 output [tokens][columns] with row stride `stride` floats, written as
-// 128-column x 256-token boxes from shared memory (no swizzle).
+// fp32 output [tokens][columns] with a row stride of `stride` floats, written
+// as [16 tokens][128 columns] boxes from shared memory (no swizzle).
 static int encode_out_map(CUtensorMap *map, float *base, int64_t columns, int64_t stride, int64_t tokens) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   NQB_CHECK(tensor_map_encoder(&encode));
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(columns), static_cast<cuuint64_t>(tokens)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * 4};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pf::kTileRows), static_cast<cuuint32_t>(pf::kTokTile)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(pf::kTileRows), static_cast<cuuint32_t>(pf::kOutTok)};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, elem,
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -765,12 +836,18 @@ static int launch_prepare(const pf::PrepParams &params, cudaStream_t stream, con
   return NQB_OK;
 }
 
+// Persistent launch: one CTA per SM (or per tile when there are fewer tiles).
 template <bool kStage2>
-static int launch_gemm(const pf::Params &params, const CUtensorMap *maps, int ctas_x, int64_t tokens,
+static int launch_gemm(pf::Params &params, const CUtensorMap *maps, int row_tiles, int64_t tokens,
                        cudaStream_t stream) {
   const void *fn = reinterpret_cast<const void *>(pf::prefill_gemm_kernel<kStage2>);
   NQB_CHECK(ensure_dynamic_smem(fn, pf::kSmemBytes));
-  const dim3 grid(ctas_x, static_cast<unsigned>((tokens + pf::kTokTile - 1) / pf::kTokTile));
+  params.total_row_tiles = row_tiles;
+  params.tok_tiles = static_cast<int32_t>((tokens + pf::kTokTile - 1) / pf::kTokTile);
+  const int64_t tiles = static_cast<int64_t>(row_tiles) * params.tok_tiles;
+  int device = 0, sms = 148;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
   pf::prefill_gemm_kernel<kStage2><<<grid, pf::kThreads, pf::kSmemBytes, stream>>>(params, maps[0], maps[1], maps[2],
                                                                                    maps[3], maps[4], maps[5]);
   NQB_CUDA(cudaGetLastError(), kStage2 ? "prefill stage 2 launch" : "prefill stage 1 launch");
@@ -779,7 +856,7 @@ static int launch_gemm(const pf::Params &params, const CUtensorMap *maps, int ct
 
 int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
                 float *const *ys, float *latent, void *extra, size_t extra_bytes, cudaStream_t stream) {
-  if (tokens > 65535ll * pf::kTokTile) return fail(NQB_ERR_UNSUPPORTED, "prefill token count too large");
+  if (tokens > (1ll << 22)) return fail(NQB_ERR_UNSUPPORTED, "prefill token count too large");
   if (extra_bytes < prefill_workspace_bytes(layers, count, tokens))
     return fail(NQB_ERR_WORKSPACE, "prefill workspace too small");
   char *ws = static_cast<char *>(extra);
@@ -801,7 +878,7 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
   const int64_t n = layers[0].in_features;
 
   // ---- stage 1
-  CUtensorMap maps[6];
+  CUtensorMap maps[6];  // activation maps of up to three members, then their output maps
   std::memset(maps, 0, sizeof(maps));
   pf::Params p1;
   std::memset(&p1, 0, sizeof(p1));
@@ -858,7 +935,6 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     offset += (d.rank + 3) & ~int64_t(3);
   }
   for (int i = count; i < 3; ++i) maps[i] = maps[0];
-  for (int i = count; i < 3; ++i) maps[3 + i] = maps[3];
   p1.count = count;
   p1.tokens = tokens;
   p1.scale_dtype = layers[0].scale_dtype;
@@ -903,6 +979,8 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     m.out = ys[i];
     m.out_stride = d.out_features;
     m.out_offset = 0;
+    m.tma_store = tma_storable(ys[i], d.out_features) ? 1 : 0;
+    if (m.tma_store) NQB_CHECK(encode_out_map(&maps[3 + i], ys[i], d.out_features, d.out_features, tokens));
     m.bias = d.bias;
     m.bias_dtype = d.bias_dtype;
     m.outlier_count = d.outlier_count;
@@ -910,13 +988,10 @@ int run_prefill(const nqb_linear_desc *layers, int count, const void *x, int32_t
     m.outlier_values = d.outlier_values;
     m.outlier_value_dtype = d.outlier_value_dtype;
     m.outlier_scales = d.outlier_scales;
-    m.tma_store = tma_storable(ys[i], d.out_features) ? 1 : 0;
-    if (m.tma_store) NQB_CHECK(encode_out_map(&maps[3 + i], ys[i], d.out_features, d.out_features, tokens));
     ctas += m.row_tiles;
     offset += (d.rank + 3) & ~int64_t(3);
   }
   for (int i = count; i < 3; ++i) maps[i] = maps[0];
-  for (int i = count; i < 3; ++i) maps[3 + i] = maps[3];
   p2.count = count;
   p2.tokens = tokens;
   p2.scale_dtype = layers[0].scale_dtype;

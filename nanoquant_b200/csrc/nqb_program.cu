@@ -898,7 +898,6 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       if (d.in_features != o.layers[0].in_features || d.scale_dtype != o.layers[0].scale_dtype)
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: members must share in_features and scale dtype", i);
       if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
-      if (d.codebook_free_rows > 0) return fail(NQB_ERR_UNSUPPORTED, "op %d: compact codebook layers", i);
       rank_total += d.rank;
     }
     if (!tc_eligible(o.layers, o.count, o.x_dtype, tokens))

@@ -34,6 +34,7 @@ from nanoquant_b200.backend import (
 from nanoquant_b200.logical import canonical_torch_dtype
 from nanoquant_b200.overlay import OutlierRowOverlay, OverlaidLayerState
 from nanoquant_b200.packed import PACKED_LAYOUT_VERSION, PackedLayerState
+from nanoquant_b200.mixed_v import MixedVLayerState
 from nanoquant_b200.product_codebook import ProductCodebookLayerState
 
 CUDA_SM100_BACKEND_NAME = "cuda-packed-sm100a"
@@ -68,7 +69,7 @@ def _repack(words: torch.Tensor, rows: int, columns: int) -> torch.Tensor:
 
 
 def _build_payload(
-    state: PackedLayerState | ProductCodebookLayerState,
+    state: PackedLayerState | ProductCodebookLayerState | MixedVLayerState,
     overlay: OutlierRowOverlay | None,
     device: torch.device,
     tensor_cores: bool = True,
@@ -98,10 +99,34 @@ def _build_payload(
         scale_pre, scale_mid, scale_post = state.factor_scale_pre, state.factor_scale_mid, state.factor_scale_post
         outliers = (state.outlier_indices, state.outlier_values, state.outlier_scales)
         bias = None
+        if tensor_cores:
+            # the tensor-core paths read kernel-native tiles: decode V on the
+            # device once and tile both factors (the compact records stay the
+            # generic kernels' input)
+            from nanoquant_b200.device_ops import decode_product_codebook_cuda
+
+            right_words = decode_product_codebook_cuda(
+                tensors["codebook_free_words"], tensors["codebook_payload"], tensors["codebook_first"],
+                tensors["codebook_second"], rank=spec.rank, columns=spec.in_features)
+            tensors["left_tiles"] = _repack(tensors["left_words"], spec.out_features, spec.rank)
+            tensors["right_tiles"] = _repack(right_words, spec.rank, spec.in_features)
+            desc.left_tiles = tensors["left_tiles"].data_ptr()
+            desc.right_tiles = tensors["right_tiles"].data_ptr()
     else:
-        packed = state.to_packed() if isinstance(state, ProductCodebookLayerState) else state
+        if isinstance(state, MixedVLayerState):
+            # expand the 19-bit records once on the device, like the reference
+            # backend (cuda_backend.py:209-224); the layer then runs as packed
+            from nanoquant_b200.device_ops import decode_mixed_v_cuda
+
+            tensors["right_words"] = decode_mixed_v_cuda(
+                _to_device(state.free_right_words, device), _to_device(state.coded_payload, device),
+                _to_device(state.codebook_words, device), rank=spec.rank, columns=spec.in_features)
+            packed = state
+        else:
+            packed = state.to_packed() if isinstance(state, ProductCodebookLayerState) else state
+            keep("right_words", packed.right_words)
         desc.left_words = keep("left_words", packed.left_words).data_ptr()
-        desc.right_words = keep("right_words", packed.right_words).data_ptr()
+        desc.right_words = tensors["right_words"].data_ptr()
         scale_pre, scale_mid, scale_post = packed.scale_pre, packed.scale_mid, packed.scale_post
         outliers = (packed.outlier_indices, packed.outlier_values, packed.outlier_scales)
         bias = packed.bias
@@ -290,10 +315,10 @@ class CudaPackedSm100Backend:
         base = state
         if isinstance(state, OverlaidLayerState):
             base, overlay = state.base, state.overlay
-        if not isinstance(base, (PackedLayerState, ProductCodebookLayerState)):
+        if not isinstance(base, (PackedLayerState, ProductCodebookLayerState, MixedVLayerState)):
             raise TypeError(
-                "sm100a packed backend requires PackedLayerState, ProductCodebookLayerState "
-                "or OverlaidLayerState"
+                "sm100a packed backend requires PackedLayerState, MixedVLayerState, "
+                "ProductCodebookLayerState or OverlaidLayerState"
             )
         target = _cuda_device(device)
         _native.library()

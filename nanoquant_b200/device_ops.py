@@ -89,3 +89,42 @@ def decode_product_codebook_cuda(
         _native.current_stream_handle(free_words.device),
     )
     return out
+
+
+def decode_mixed_v_cuda(
+    free_words: torch.Tensor,
+    payload: torch.Tensor,
+    codebook: torch.Tensor,
+    *,
+    rank: int,
+    columns: int,
+) -> torch.Tensor:
+    """Mixed-V right factor on the GPU -> layout-v1 words [rank, ceil(columns/32)] (``nqb_decode_mixed_v``).
+
+    The records must be valid (``MixedVLayerState`` validates them on
+    construction); the kernel stays in bounds for any payload.
+    """
+
+    for name, value in (("free_words", free_words), ("payload", payload), ("codebook", codebook)):
+        _require_cuda(value, name)
+        if value.dtype != torch.int32 or not value.is_contiguous():
+            raise ValueError(f"mixed-V {name} must be contiguous int32")
+    words_per_row = packed_word_count(columns)
+    free_rows = int(free_words.shape[0])
+    if tuple(free_words.shape) != (free_rows, words_per_row) or tuple(codebook.shape) != (1024,):
+        raise ValueError("mixed-V free words or codebook shape differs")
+    if payload.numel() * 32 < (rank - free_rows) * words_per_row * 19:
+        raise ValueError("mixed-V payload is shorter than its records")
+    out = torch.empty((rank, words_per_row), dtype=torch.int32, device=free_words.device)
+    _native.call(
+        "nqb_decode_mixed_v",
+        free_words.data_ptr(),
+        free_rows,
+        rank,
+        columns,
+        payload.data_ptr(),
+        codebook.data_ptr(),
+        out.data_ptr(),
+        _native.current_stream_handle(free_words.device),
+    )
+    return out

@@ -18,6 +18,7 @@ from dataclasses import dataclass
 
 import torch
 
+from nanoquant_b200.mixed_v import MixedVLayerState
 from nanoquant_b200.packed import PackedLayerState
 from nanoquant_b200.product_codebook import ProductCodebookLayerState
 
@@ -57,12 +58,12 @@ class OutlierRowOverlay:
 class OverlaidLayerState:
     """A packed or product-codebook layer plus an int8 residual-row overlay."""
 
-    base: PackedLayerState | ProductCodebookLayerState
+    base: PackedLayerState | ProductCodebookLayerState | MixedVLayerState
     overlay: OutlierRowOverlay
 
     def __post_init__(self) -> None:
-        if not isinstance(self.base, (PackedLayerState, ProductCodebookLayerState)):
-            raise TypeError("overlay base must be a PackedLayerState or ProductCodebookLayerState")
+        if not isinstance(self.base, (PackedLayerState, ProductCodebookLayerState, MixedVLayerState)):
+            raise TypeError("overlay base must be a PackedLayerState, ProductCodebookLayerState or MixedVLayerState")
         self.overlay.validate(self.spec.out_features, self.spec.in_features)
 
     @property

@@ -8,8 +8,10 @@ second table for bits 16..31.  Records are packed two per int32 word, low half
 first.  When the factorisation was fitted transposed, decoding transposes back to
 the canonical orientation.
 
-The CUDA backend decodes these records inside the stage-1 kernel instead of
-expanding them at prepare time; this module is the host-side container.
+The CUDA backend's generic kernels decode these records inside stage 1; the
+tensor-core paths expand V once at prepare time on the device
+(``nqb_decode_product_codebook``) into their tile layout.  This module is the
+host-side container.
 """
 
 from __future__ import annotations

@@ -24,6 +24,7 @@ from dataclasses import replace
 import torch
 
 from nanoquant_b200.backend import PreparedLayer
+from nanoquant_b200.mixed_v import MixedVLayerState
 from nanoquant_b200.overlay import OutlierRowOverlay, OverlaidLayerState
 from nanoquant_b200.packed import PackedLayerState
 from nanoquant_b200.product_codebook import ProductCodebookLayerState
@@ -54,12 +55,12 @@ def row_range(out_features: int, world: int, rank: int, multiple: int = TILE_ROW
     return min(first * multiple, out_features), min(last * multiple, out_features)
 
 
-def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLayerState, start: int,
-               stop: int) -> PackedLayerState | OverlaidLayerState:
+def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLayerState | MixedVLayerState,
+               start: int, stop: int) -> PackedLayerState | OverlaidLayerState:
     """The layer restricted to output rows ``[start, stop)`` (stage 1 unchanged).
 
-    Product-codebook layers are decoded to layout v1 first (their V is the
-    stage-1 factor, kept whole; only U rows are sliced).
+    Product-codebook and mixed-V layers are decoded to layout v1 first (their
+    V is the stage-1 factor, kept whole; only U rows are sliced).
     """
 
     if isinstance(state, OverlaidLayerState):
@@ -72,10 +73,10 @@ def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLay
         overlay = OutlierRowOverlay((ids[keep] - start).to(torch.int32).contiguous(),
                                     state.overlay.values[keep].contiguous(), state.overlay.scales[keep].contiguous())
         return OverlaidLayerState(base, overlay)
-    if isinstance(state, ProductCodebookLayerState):
+    if isinstance(state, (ProductCodebookLayerState, MixedVLayerState)):
         state = state.to_packed()
     if not isinstance(state, PackedLayerState):
-        raise TypeError("shard_rows takes packed, product-codebook or overlaid layers")
+        raise TypeError("shard_rows takes packed, mixed-V, product-codebook or overlaid layers")
     spec = state.spec
     if not 0 <= start < stop <= spec.out_features:
         raise ValueError("row shard must be a non-empty range inside the output rows")

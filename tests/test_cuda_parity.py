@@ -158,6 +158,33 @@ def test_product_codebook_matches_reference_and_expanded_layer(tag: str) -> None
     torch.testing.assert_close(default_out.cpu(), fixture[f"{tag}_y"], rtol=RTOL, atol=ATOL)
 
 
+def test_product_codebook_layer_on_tensor_core_paths() -> None:
+    """A compact codebook layer (C4 shape: Gemma-1B gate) takes the tensor-core decode and prefill paths."""
+
+    from nanoquant_b200.cuda_backend import kernel_path
+    from nanoquant_b200.program import DecodeProgram, ProgramOp
+
+    fixture = load("product_codebook")
+    state = _codebook_state(fixture, "c4like")
+    n = state.spec.in_features
+    backend = CudaPackedSm100Backend()
+    layer = backend.prepare(state, "cuda")
+    oracle = oracle_from_state(state.to_packed())
+    g = torch.Generator().manual_seed(11)
+    for tokens, path in ((1, "tensor-core"), (5, "tensor-core"), (64, "prefill")):
+        assert kernel_path(layer, tokens) == path
+        x = torch.randn(tokens, n, generator=g).bfloat16()
+        got = backend.linear(x.cuda(), layer)
+        expected = po.packed_linear(x.float().numpy(), oracle, accumulate="float64")
+        bound = PREFILL_BOUND if path == "prefill" else 2e-5
+        assert _relative_max_error(got, expected) <= bound
+    x = torch.randn(1, n, generator=g).bfloat16().cuda()
+    out = DecodeProgram([ProgramOp((layer,), x)]).run()[0][0]
+    expected = po.packed_linear(x.float().cpu().numpy(), oracle, accumulate="float64")
+    assert _relative_max_error(out, expected) <= 2e-5
+    assert ctypes_status() == 0
+
+
 def test_device_codebook_decode_is_bit_exact() -> None:
     fixture = load("product_codebook")
     n, m, r, free_rows, _ = (int(v) for v in fixture["c4like_shape"])
