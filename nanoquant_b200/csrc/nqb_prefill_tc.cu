@@ -258,7 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap out0, const __grid_constant__ CUtensorMap out1,
                         const __grid_constant__ CUtensorMap out2) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t full[kStages], empty[kStages], a_full[2], a_empty[2], d_full[2], d_empty[2];
+  // full[s]: stage s landed; empty[s]: the MMAs of the step that used stage s
+  // are done (also frees that step's A buffer); a_full[b]: A buffer b expanded
+  __shared__ uint64_t full[kStages], empty[kStages], a_full[2], d_full[2], d_empty[2];
   __shared__ uint32_t s_tmem;
   __shared__ float s_unscale[2][kTokTile];  // 2^-e of each token of the tile in accumulator d (0 past the end)
 
@@ -279,7 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&a_full[b], 4);  // one arrival per expansion warp
-      ptx::mbar_init(&a_empty[b], 1);
       ptx::mbar_init(&d_full[b], 1);
       ptx::mbar_init(&d_empty[b], 128);
     }
@@ -329,8 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tc >= 2) pf_wait(&d_empty[d], ((tc >> 1) - 1) & 1);
         ptx::tc_fence_after();
         for (int s = 0; s < k_steps; ++s, ++it) {
+          // a_full implies full: the expansion warps waited for this stage
+          // before they arrived (one wait and one commit per step keep the
+          // issuing thread's work below the MMAs' 768 cycles)
           const int slot = static_cast<int>(it % kStages);
-          pf_wait(&full[slot], (it / kStages) & 1);
           const uint32_t buf = it & 1;
           pf_wait(&a_full[buf], (it >> 1) & 1);
           ptx::tc_fence_after();
@@ -342,7 +345,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                        (s > 0 || k16 > 0) ? 1u : 0u);
           }
           ptx::mma_commit(&empty[slot]);
-          ptx::mma_commit(&a_empty[buf]);
         }
         ptx::mma_commit(&d_full[d]);
       }
@@ -359,8 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         pf_wait(&full[slot], (it / kStages) & 1);
         const uint4 c0 = reinterpret_cast<const uint4 *>(s_chunk + slot * kChunkBytes)[tid];
         const uint32_t buf = it & 1;
-        if (it >= 2) {
-          pf_wait(&a_empty[buf], ((it >> 1) - 1) & 1);
+        if (it >= 2) {  // A buffer `buf` is free once step it - 2's MMAs are done
+          pf_wait(&empty[(it - 2) % kStages], ((it - 2) / kStages) & 1);
           ptx::tc_fence_after();
         }
         const uint4 *pre = m.pre_pairs != nullptr ? reinterpret_cast<const uint4 *>(s_pre + slot * kPreBytes) : nullptr;
