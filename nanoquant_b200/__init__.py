@@ -43,6 +43,11 @@ from nanoquant_b200.packed import (
     supports_vector_word_loads,
     unpack_sign_matrix,
 )
+from nanoquant_b200.artifact import (
+    OpenPackedArtifact,
+    PackedArtifactError,
+    open_packed_artifact,
+)
 from nanoquant_b200.mixed_v import (
     MIXED_V_FORMAT_VERSION,
     MixedVLayerState,
@@ -65,6 +70,9 @@ from nanoquant_b200.product_codebook import (
 )
 
 __all__ = [
+    "OpenPackedArtifact",
+    "PackedArtifactError",
+    "open_packed_artifact",
     "MIXED_V_FORMAT_VERSION",
     "MixedVLayerState",
     "decode_mixed_v_right_words",

@@ -13,6 +13,9 @@ bit-identical to the reference, which the golden fixtures check.
 
 from __future__ import annotations
 
+from collections.abc import Iterator
+from contextlib import contextmanager
+from contextvars import ContextVar
 from dataclasses import dataclass
 
 import numpy as np
@@ -131,10 +134,9 @@ def _check_packed_matrix(words: torch.Tensor, rows: int, columns: int) -> None:
         )
     tail = columns % PACKED_WORD_BITS
     if tail:
-        last = words[:, -1].detach().to("cpu").numpy().view(np.uint32)
-        padding_mask = np.uint32(0xFFFFFFFF ^ ((1 << tail) - 1))
-        if bool(np.any(last & padding_mask)):
-            raise ValueError("packed sign matrix has a non-zero padding bit")
+        padding_mask = -(1 << tail)  # bits tail..31 of an int32 word
+        _value_check((words[:, -1].detach() & padding_mask).ne(0).any(),
+                     "packed sign matrix has a non-zero padding bit")
 
 
 def unpack_sign_matrix(
@@ -159,9 +161,55 @@ def _factor_dtype(name: str) -> torch.dtype:
     return parse_torch_dtype(name)
 
 
+# Value checks (padding bits, finiteness, salient-index order) read tensor
+# contents.  Outside `deferred_value_checks` each one raises at once, which
+# costs a device synchronisation per check for device tensors; inside it they
+# are recorded as 0-dim flags and evaluated together when the block exits.
+_DEFERRED: ContextVar[list[tuple[torch.Tensor, str]] | None] = ContextVar("nanoquant_b200_deferred_checks",
+                                                                          default=None)
+
+
+def _value_check(failed: torch.Tensor, message: str) -> None:
+    pending = _DEFERRED.get()
+    if pending is None:
+        if bool(failed):
+            raise ValueError(message)
+    else:
+        pending.append((failed.reshape(()), message))
+
+
+@contextmanager
+def deferred_value_checks() -> Iterator[None]:
+    """Defer the value checks of the packed layers constructed in the block.
+
+    Shape, dtype and presence checks still raise at construction.  At exit the
+    recorded flags are copied to the host in one transfer per device and the
+    first failed check, in construction order, raises its ``ValueError``.
+    """
+
+    pending: list[tuple[torch.Tensor, str]] = []
+    token = _DEFERRED.set(pending)
+    try:
+        yield
+    finally:
+        _DEFERRED.reset(token)
+    if not pending:
+        return
+    failed = [False] * len(pending)
+    by_device: dict[torch.device, list[int]] = {}
+    for index, (flag, _) in enumerate(pending):
+        by_device.setdefault(flag.device, []).append(index)
+    for device, indices in by_device.items():
+        values = torch.stack([pending[i][0] for i in indices]).to("cpu")
+        for i, value in zip(indices, values.tolist(), strict=True):
+            failed[i] = bool(value)
+    for (_, message), bad in zip(pending, failed, strict=True):
+        if bad:
+            raise ValueError(message)
+
+
 def _require_finite(value: torch.Tensor, message: str) -> None:
-    if not bool(torch.isfinite(value).all()):
-        raise ValueError(message)
+    _value_check(~torch.isfinite(value).all(), message)
 
 
 @dataclass(frozen=True, slots=True)
@@ -235,14 +283,16 @@ class PackedLayerState:
             if canonical_torch_dtype(values.dtype) != spec.outlier_value_dtype:
                 raise ValueError("packed layer outlier value dtype differs")
             positions = indices.to(torch.int64)
-            if bool((positions < 0).any()) or bool((positions >= spec.in_features).any()):
-                raise ValueError("packed layer outlier index is outside the input dimension")
-            if not bool((positions[1:] > positions[:-1]).all()):
-                raise ValueError("packed layer outlier indices must be strictly increasing")
+            _value_check(((positions < 0) | (positions >= spec.in_features)).any(),
+                         "packed layer outlier index is outside the input dimension")
+            _value_check(~(positions[1:] > positions[:-1]).all(),
+                         "packed layer outlier indices must be strictly increasing")
             # The kernels add salient columns on a separate path, so their pre-scale
-            # must be exactly zero (reference packed.py:303-307).
-            if bool((self.scale_pre.index_select(0, positions.to(self.scale_pre.device)) != 0).any()):
-                raise ValueError("packed llama.cpp salient columns require exactly zero scale_pre entries")
+            # must be exactly zero (reference packed.py:303-307).  (Clamped so that
+            # a deferred check never indexes out of range.)
+            safe = positions.clamp(0, spec.in_features - 1).to(self.scale_pre.device)
+            _value_check((self.scale_pre.index_select(0, safe) != 0).any(),
+                         "packed llama.cpp salient columns require exactly zero scale_pre entries")
             if values.dtype not in (torch.int8, torch.float16, torch.bfloat16, torch.float32):
                 raise ValueError("packed llama.cpp salient value dtype is unsupported")
             if values.is_floating_point():
@@ -334,6 +384,7 @@ __all__ = [
     "PACKED_WORD_DTYPE",
     "PackedLayerState",
     "PackedLayoutMetadata",
+    "deferred_value_checks",
     "pack_logical_layer",
     "pack_sign_matrix",
     "packed_row_stride_bytes",

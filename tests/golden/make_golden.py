@@ -6,8 +6,9 @@ Run in a checkout that has the reference source tree::
 
 It imports the reference's own runtime (``nanoquant.runtime``) and records, for
 seeded inputs, what the reference computes: layout-v1 words, product-codebook
-and mixed-V decodes, and ``PackedReferenceBackend.linear`` outputs on fp32
-input (``src/nanoquant/runtime/reference.py:184-235``).  The fixtures are
+and mixed-V decodes, ``PackedReferenceBackend.linear`` outputs on fp32
+input (``src/nanoquant/runtime/reference.py:184-235``), and a small packed
+artifact written by the reference's artifact writer.  The fixtures are
 small ``.npz`` files; tests and the oracle read them and never need the
 reference itself.  Half-precision tensors are stored as their raw 16-bit
 patterns with a ``<name>__dtype`` tag.
@@ -248,6 +249,57 @@ def make_mixed_v(rt) -> None:
     )
 
 
+def make_packed_artifact(rt) -> None:
+    """A two-block packed artifact written by the reference's own writer
+    (``packed_artifact.py:306-372``) plus what its ``load_layer`` returns."""
+
+    import shutil
+
+    def layer(name, n, m, r, seed, scale_dtype, *, outliers=0, patch=False):
+        g = torch.Generator().manual_seed(seed)
+        spec = rt.QuantizedLinearSpec(
+            name, "nanoquant-v1", n, m, r, "float32", str(scale_dtype).removeprefix("torch."),
+            outlier_count=outliers, outlier_value_dtype="int8" if outliers else None,
+            has_outlier_scales=bool(outliers), has_bias=True,
+            patch_rank=2 if patch else 0, patch_value_dtype="float32" if patch else None,
+        )
+        pre = (torch.randn(n, generator=g).abs() * 0.05 + 0.01).to(scale_dtype)
+        idx = None
+        if outliers:
+            idx = torch.sort(torch.randperm(n, generator=g)[:outliers]).values.to(torch.int64)
+            pre[idx] = 0
+        return rt.pack_logical_layer(rt.LogicalLayerState(
+            spec, _signs(g, m, r), _signs(g, r, n), pre,
+            (torch.randn(r, generator=g).abs() + 0.5).to(scale_dtype),
+            (torch.randn(m, generator=g).abs() * 0.05 + 0.01).to(scale_dtype),
+            bias=torch.randn(m, generator=g).to(scale_dtype),
+            outlier_indices=idx,
+            outlier_values=torch.randint(-127, 128, (m, outliers), generator=g, dtype=torch.int8) if outliers else None,
+            outlier_scales=torch.full((outliers,), 0.002).to(scale_dtype) if outliers else None,
+            patch_left=torch.randn(m, 2, generator=g) if patch else None,
+            patch_right=torch.randn(2, n, generator=g) if patch else None,
+        ))
+
+    blocks = {
+        0: [layer("blocks.0.self_attn.q_proj", 35, 3, 33, 61, torch.float32, outliers=2),
+            layer("blocks.0.mlp.up_proj", 97, 50, 40, 62, torch.float16)],
+        1: [layer("blocks.1.self_attn.o_proj", 64, 17, 9, 63, torch.bfloat16, patch=True)],
+    }
+    names = [state.spec.name for states in blocks.values() for state in states]
+    root = HERE / "packed_artifact"
+    if root.exists():
+        shutil.rmtree(root)
+    metadata = rt.RuntimeModelMetadata("fixture/model", "revision", "fixture", "config", "tokenizer")
+    artifact = rt.write_packed_artifact(root, metadata, "0" * 64, blocks)
+    out: dict = {}
+    for name in names:
+        loaded = artifact.load_layer(name)
+        for field in ("left_words", "right_words", "scale_pre", "scale_mid", "scale_post", "bias",
+                      "outlier_indices", "outlier_values", "outlier_scales", "patch_left", "patch_right"):
+            _store(getattr(loaded, field), f"{name}:{field}", out)
+    np.savez_compressed(HERE / "packed_artifact_layers.npz", **out)
+
+
 def main() -> None:
     if len(sys.argv) > 1:
         sys.path.insert(0, sys.argv[1])
@@ -259,6 +311,7 @@ def main() -> None:
     make_grouped(rt)
     make_product_codebook(rt)
     make_mixed_v(rt)
+    make_packed_artifact(rt)
     print("fixtures written to", HERE)
 
 
