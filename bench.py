@@ -114,8 +114,9 @@ def _device_status() -> int:
 def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
     """Time the CPU oracle (numpy port of PackedReferenceBackend) on a bounded sample.
 
-    decode: 2 of 36 Qwen3-8B layers, one token; prefill: 1 of 32 Llama-3-8B
-    layers, 128 tokens.  The result is extrapolated to the full step.
+    decode workloads: 2 layers of the shape at the workload's token count;
+    prefill: 1 of 32 Llama-3-8B layers, 128 tokens.  The result is
+    extrapolated to the full step.
     """
 
     import numpy as np
@@ -124,8 +125,9 @@ def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
     from oracle import packed_oracle as po
 
     rng = np.random.default_rng(0)
-    shape = decode_chain.QWEN3_8B if workload == "decode" else decode_chain.LLAMA3_8B_055
-    sample_layers, sample_tokens = (2, 1) if workload == "decode" else (1, 128)
+    spec = WORKLOADS[workload]
+    shape = getattr(decode_chain, spec["shape"])
+    sample_layers, sample_tokens = (2, spec["decode_tokens"]) if spec["kind"] == "decode" else (1, 128)
     per_layer_seconds = []
     for _layer in range(sample_layers):
         layers = {}
@@ -185,7 +187,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "warmup": args.warmup,
         "ms_per_step": base["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak" if args.workload == "decode" else "strong",
+        "scaling": "weak" if spec["kind"] == "decode" else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
@@ -199,13 +201,35 @@ def run_reference(args, rank: int, world: int) -> None:
 
 WORKLOADS = {
     "decode": {
+        "kind": "decode",
         "metric": METRIC,
         "shape": "QWEN3_8B",
         "tokens_total": None,  # one token per rank (replicas)
+        "decode_tokens": 1,
         "description": "qwen3-8b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
         "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
     },
+    # BASELINE config 2 at batch 16 and config 1: extra lines beside the headline
+    "decode-bs16": {
+        "kind": "decode",
+        "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak",
+        "shape": "QWEN3_8B",
+        "tokens_total": None,
+        "decode_tokens": 16,
+        "description": "qwen3-8b packed linears, decode bs16 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
+        "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
+    },
+    "decode-gemma1b": {
+        "kind": "decode",
+        "metric": "decode tok/s (bs1, Gemma-3-1B shape ~1 bpw); packed-GEMV HBM GB/s vs peak",
+        "shape": "GEMMA3_1B",
+        "tokens_total": None,
+        "decode_tokens": 1,
+        "description": "gemma-3-1b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
+        "model": "gemma-3-1b-shape random-init packed weights ~1 bpw",
+    },
     "prefill": {
+        "kind": "prefill",
         "metric": PREFILL_METRIC,
         "shape": "LLAMA3_8B_055",
         "tokens_total": 8 * 4096,  # 8 sequences x 4096 tokens, disjoint token batches per rank
@@ -234,7 +258,7 @@ def main() -> None:
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = 50 if args.workload == "decode" else 3
+        args.steps = 50 if WORKLOADS[args.workload]["kind"] == "decode" else 3
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -264,7 +288,7 @@ def main() -> None:
     spec = WORKLOADS[args.workload]
     shape = getattr(decode_chain, spec["shape"])
     if spec["tokens_total"] is None:
-        tokens = 1
+        tokens = spec["decode_tokens"]
     else:
         if spec["tokens_total"] % world:
             raise SystemExit(f"{spec['tokens_total']} tokens do not split over {world} ranks")
@@ -273,7 +297,8 @@ def main() -> None:
             tokens = args.tokens
     chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device, tokens=tokens,
                         engine=args.engine)
-    use_graph = args.workload == "decode" and chain.program is None
+    decode = spec["kind"] == "decode"
+    use_graph = decode and chain.program is None
     if use_graph:
         chain.capture()
     run_step = chain.replay if use_graph else chain.step
@@ -325,7 +350,7 @@ def main() -> None:
     total_tokens = tokens * world
     value = total_tokens * 1000.0 / ms_per_step
     peaks = _peak_table()
-    if args.workload == "decode":
+    if decode:
         step_bytes = chain.algorithmic_bytes()
         achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
         roofline = {
@@ -352,16 +377,16 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak" if args.workload == "decode" else "strong",
+        "scaling": "weak" if decode else "strong",
         "vs_baseline": None,
-        "dtype": "f32" if args.workload == "decode" else "f16",
+        "dtype": "f32" if decode else "f16",
         "data": "synthetic",
         "config": {
             "workload": spec["description"].format(layers=len(chain.blocks)),
             "model": spec["model"],
             "global_batch": total_tokens,
             "tokens_per_gpu": tokens,
-            "parallelism": (f"replicas{world}" if args.workload == "decode" else f"token-batches{world}")
+            "parallelism": (f"replicas{world}" if decode else f"token-batches{world}")
             if world > 1 else "single",
             "l2": "weights larger than the 126 MB L2 (no flush)",
             "cuda_graph": use_graph,
