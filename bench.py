@@ -1,6 +1,6 @@
 """Benchmark: decode tokens/s through all packed linears of a Qwen3-8B-shaped decoder (bs1).
 
-One step = one decode token (batch 1, BASELINE config 2 shape) through the 36
+One step = one decode token (batch 1, Qwen3-8B shape) through the 36
 layers x {q,k,v,o,gate,up,down} packed binary low-rank linears at ~1 bpw,
 with the grouped QKV and gate/up calls of the reference's model shell, run as
 one persistent decode program (a grid barrier between every stage, so the
@@ -209,7 +209,7 @@ WORKLOADS = {
         "description": "qwen3-8b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
         "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
     },
-    # BASELINE config 2 at batch 16 and config 1: extra lines beside the headline
+    # Qwen3-8B at batch 16 and the Gemma-3-1B decode step: extra lines beside the headline
     "decode-bs16": {
         "kind": "decode",
         "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak",
@@ -246,7 +246,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("nqb", "reference"), default="nqb")
     parser.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
-                        help="decode: BASELINE config 2 linears (the headline); prefill: config 3")
+                        help="decode: Qwen3-8B packed linears at batch 1 (the headline); prefill: Llama-3-8B 0.55 bpw, "
+                             "8 x 4096 tokens")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--layers", type=int, default=None,
                         help="decoder layers in the step (default: all); fewer only for profiling runs")

@@ -3,7 +3,7 @@
 A decoder layer's packed linears are the q/k/v/o attention projections and the
 gate/up/down MLP projections.  :func:`make_decoder_layers` builds random
 layout-v1 layers of a given model shape (uniform random sign bits, the scales
-of BASELINE config 0: ``|N(0,1)| * 0.05 + 0.01`` in fp16, ``scale_mid = 1``),
+``|N(0,1)| * 0.05 + 0.01`` in fp16 for pre and post, ``scale_mid = 1``),
 directly on the GPU.  :class:`DecodeChain` runs one decode step through every
 layer with the grouped QKV and gate/up calls the reference's model shell uses
 (``src/nanoquant/runtime/torch_model.py:311-327, 492-505``).  Its engines:

@@ -12,9 +12,9 @@ one rank with the same arithmetic as the unsharded call:
   and int8 overlay rows); one all-gather of the fp32 ``y`` slices over NCCL
   joins them.  Row ranges are multiples of the 128-row tensor-core tile.
 
-The reference has no multi-GPU path for this operator; the partitions follow
-BASELINE's north star ("disjoint token batches, plus an optional row-shard of
-U with an NCCL all-gather").
+The reference has no multi-GPU path for this operator; prefill is split by
+disjoint token batches, with an optional row shard of U joined by an NCCL
+all-gather.
 """
 
 from __future__ import annotations

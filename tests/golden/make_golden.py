@@ -143,7 +143,7 @@ def make_linear(rt) -> None:
                  outlier_count=2)
     _packed_case(rt, "ggml_96_64_64_f16", n=96, r=64, m=64, tokens=(8,), seed=35, outlier_dtype=torch.float16,
                  outlier_count=7)
-    # BASELINE config 0: Gemma-3-270m MLP up-proj, 640 -> 2048, rank 480, fp16 scales, mid = 1
+    # Gemma-3-270m MLP up-proj, 640 -> 2048, rank 480, fp16 scales, mid = 1
     for tokens in (1, 8):
         _packed_case(rt, f"c0_t{tokens}", n=640, m=2048, r=480, tokens=(tokens,), seed=0,
                      scale_dtype=torch.float16, baseline_scales=True)

@@ -4,7 +4,7 @@ Tolerances: the reference's own GPU test bound ``rtol=2e-5, atol=2e-4`` against
 an fp32 restatement (reference ``tests/unit/test_runtime_cuda_backend.py:491``)
 on the small fixtures; bit-exact for every integer/bit path (pack, unpack,
 codebook decode); bitwise replay determinism; and for large layers the
-``max|y - y_ref| / max|y_ref| <= 2e-3`` bound of the north-star spec.
+``max|y - y_ref| / max|y_ref| <= 2e-3`` accuracy bound of the operator.
 """
 
 from __future__ import annotations
@@ -366,7 +366,7 @@ def test_tensor_core_grouped_projection_matches_members() -> None:
 
 # ------------------------------------------------------------------ tensor-core prefill path ---
 
-PREFILL_BOUND = 2e-3  # north-star bound on max|y - y_ref| / max|y_ref| (fp16 activations)
+PREFILL_BOUND = 2e-3  # the operator's bound on max|y - y_ref| / max|y_ref| (fp16 activations)
 
 
 @pytest.mark.parametrize(("n", "m", "r", "tokens"), ((35, 17, 33, 40), (640, 2048, 480, 17), (640, 2048, 480, 300),

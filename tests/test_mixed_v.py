@@ -60,7 +60,7 @@ def _records(n: int, coded_rows: int, rng: np.random.Generator) -> tuple[np.ndar
 
 def mixed_v_state(n: int, m: int, r: int, free_rows: int, seed: int, *, bias: bool = False,
                   outliers: int = 0) -> MixedVLayerState:
-    """Random mixed-V layer: random U, free V rows and records; scales as the BASELINE configs."""
+    """Random mixed-V layer: random U, free V rows and records; fp16 scales |N(0,1)| * 0.05 + 0.01."""
 
     g = torch.Generator().manual_seed(seed)
     rng = np.random.default_rng(seed)
