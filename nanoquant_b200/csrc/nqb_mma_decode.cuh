@@ -89,20 +89,19 @@ struct Scratch {
 // Quads of one chunk held per consumer thread: nst <= 16 slices x 64 quads.
 __host__ __device__ constexpr int quads_per_thread(int max_slices) { return (max_slices * 64 + kThreads - 1) / kThreads; }
 
-// Loads the chunk's activations (every load issued before any is used),
-// quantises them per token to 22-bit fixed point (2^e from the chunk
-// maximum), scatters the signed base-256 digits into B fragments and returns
-// per token e and Q = sum q.  Two consumer barriers; the first also orders
-// this chunk's fragment writes after every warp's previous MMAs.
-template <int kT, int kQPT, typename Loader>
-__device__ __forceinline__ void quantize_chunk(const Loader &src, int nst, int T, uint8_t *smem_b, Scratch<kT> &sc,
-                                               int (&e)[kT], long long (&Q)[kT]) {
-  constexpr int kNT = n_tiles(kT);
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int nquads = nst * 64;
+// This consumer thread's activations of one chunk: kQPT quads of four
+// columns, kT tokens each.
+template <int kT, int kQPT>
+struct ChunkValues {
   float v[kQPT][4][kT];
+};
+
+// Issues every load of the chunk's activations; nothing here waits for them,
+// so a caller can issue the next chunk's loads before the current chunk's MMAs.
+template <int kT, int kQPT, typename Loader>
+__device__ __forceinline__ void load_chunk(const Loader &src, int nst, int T, ChunkValues<kT, kQPT> &cv) {
+  const int tid = threadIdx.x;
+  const int nquads = nst * 64;
 #pragma unroll
   for (int i = 0; i < kQPT; ++i) {
     const int qd = tid + i * kThreads;
@@ -112,8 +111,23 @@ __device__ __forceinline__ void quantize_chunk(const Loader &src, int nst, int T
 #pragma unroll
     for (int b = 0; b < 4; ++b)
 #pragma unroll
-      for (int t = 0; t < kT; ++t) v[i][b][t] = (qd < nquads && t < T) ? src(t, c0 + 8 * b) : 0.0f;
+      for (int t = 0; t < kT; ++t) cv.v[i][b][t] = (qd < nquads && t < T) ? src(t, c0 + 8 * b) : 0.0f;
   }
+}
+
+// Quantises loaded activations per token to 22-bit fixed point (2^e from the
+// chunk maximum), scatters the signed base-256 digits into B fragments and
+// returns per token e and Q = sum q.  Two consumer barriers; the first also
+// orders this chunk's fragment writes after every warp's previous MMAs.
+template <int kT, int kQPT>
+__device__ __forceinline__ void quantize_loaded(const ChunkValues<kT, kQPT> &cv, int nst, int T, uint8_t *smem_b,
+                                                Scratch<kT> &sc, int (&e)[kT], long long (&Q)[kT]) {
+  constexpr int kNT = n_tiles(kT);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nquads = nst * 64;
+  const auto &v = cv.v;
   float mx[kT];
 #pragma unroll
   for (int t = 0; t < kT; ++t) {
@@ -188,6 +202,15 @@ __device__ __forceinline__ void quantize_chunk(const Loader &src, int nst, int T
     for (int w = 0; w < kWarps; ++w) x += sc.red_q[w * kT + t];
     Q[t] = x;
   }
+}
+
+// load_chunk then quantize_loaded.
+template <int kT, int kQPT, typename Loader>
+__device__ __forceinline__ void quantize_chunk(const Loader &src, int nst, int T, uint8_t *smem_b, Scratch<kT> &sc,
+                                               int (&e)[kT], long long (&Q)[kT]) {
+  ChunkValues<kT, kQPT> cv;
+  load_chunk<kT, kQPT>(src, nst, T, cv);
+  quantize_loaded<kT, kQPT>(cv, nst, T, smem_b, sc, e, Q);
 }
 
 // This lane's four sign words of one slice: rows (16 warp + g) and +8, words

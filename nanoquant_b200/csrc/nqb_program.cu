@@ -421,11 +421,32 @@ __host__ __device__ constexpr int leader_slots(int bucket) {
   return 16384 / (kClusterSize * bucket * kTileRows * 4) > 1 ? 16384 / (kClusterSize * bucket * kTileRows * 4) : 1;
 }
 
+// Advances (j0, j1, c0, hi) to the next (member run, chunk) unit of the
+// group [.., ge) with a non-empty K range for this cluster rank: items
+// [j0, j1) share a member; chunk c0 covers slices [c0, min(c0 + sc, hi)).
+// Start with j0 = j1 = first item, c0 = hi = 0.  False once the group is done.
+__device__ __forceinline__ bool next_unit(const StageInfo &op, int ge, int rank, int sc, int &j0, int &j1, int &c0,
+                                          int &hi) {
+  c0 += sc;
+  while (c0 >= hi) {
+    j0 = j1;
+    if (j0 >= ge) return false;
+    const int mi = op.items[j0].member;
+    j1 = j0 + 1;
+    while (j1 < ge && op.items[j1].member == mi) ++j1;
+    const int ks = op.md[mi].ks;
+    c0 = ks * rank / kClusterSize;
+    hi = ks * (rank + 1) / kClusterSize;
+  }
+  return true;
+}
+
 template <int kT>
 __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_constant__ Params p) {
   constexpr int kNT = mmad::n_tiles(kT);
   constexpr int kSets = mmad::acc_sets(kNT);
   constexpr int kQPT = mmad::quads_per_thread(slices_per_chunk(kT));
+  constexpr bool kPrefetchUnits = kT == 1;  // two chunks of activations in registers only at one token
   constexpr int kLead = leader_slots(kT);  // tiles this CTA leads per exchange group
   constexpr int kC = mmad::kThreads;  // consumer threads
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -523,42 +544,52 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       for (int gb = ib; gb < ie; gb += p.group) {
         const int ge = min(gb + p.group, ie);
         for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
-        // ---- this CTA's quarter of every item of the group, member by member
-        for (int j0 = gb; j0 < ge;) {
-          const int mi = op.items[j0].member;
-          int j1 = j0 + 1;
-          while (j1 < ge && op.items[j1].member == mi) ++j1;
-          const MemberDev &md = op.md[mi];
-          const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
-          const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
-          for (int c0 = lo; c0 < hi; c0 += p.sc) {
+        if constexpr (kPrefetchUnits) {
+          // ---- this CTA's quarter of every item of the group, one (member run,
+          // chunk) unit at a time.  At one token the next unit's activation
+          // loads are issued before this unit's MMAs, so their L2 round trip
+          // is hidden behind the MMAs instead of opening the next unit.
+          auto load_unit = [&](int j, int c0, int hi, mmad::ChunkValues<kT, kQPT> &cv) {
+            const MemberDev &md = op.md[op.items[j].member];
             const int nst = min(p.sc, hi - c0);
             const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+            if (st == 1) {
+              mmad::load_chunk<kT, kQPT>(mmad::LatentLoader{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid},
+                                         nst, T, cv);
+            } else if (op.x_dtype == NQB_BF16) {
+              mmad::load_chunk<kT, kQPT>(mmad::XLoader<__nv_bfloat16>{static_cast<const __nv_bfloat16 *>(op.x), md.pre,
+                                                                     op.n, k0, md.k_valid},
+                                         nst, T, cv);
+            } else if (op.x_dtype == NQB_F16) {
+              mmad::load_chunk<kT, kQPT>(
+                  mmad::XLoader<__half>{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
+            } else {
+              mmad::load_chunk<kT, kQPT>(
+                  mmad::XLoader<float>{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
+            }
+          };
+          int j0 = gb, j1 = gb, c0 = 0, hi = 0;
+          bool have = next_unit(op, ge, static_cast<int>(rank), p.sc, j0, j1, c0, hi);
+          mmad::ChunkValues<kT, kQPT> cur;
+          if (have) load_unit(j0, c0, hi, cur);
+          while (have) {
+            int nj0 = j0, nj1 = j1, nc0 = c0, nhi = hi;
+            const bool more = next_unit(op, ge, static_cast<int>(rank), p.sc, nj0, nj1, nc0, nhi);
+            mmad::ChunkValues<kT, kQPT> nxt;
+            if (kPrefetchUnits && more) load_unit(nj0, nc0, nhi, nxt);
+            const int nst = min(p.sc, hi - c0);
             int e[kT];
             long long Q[kT];
             NQB_TRACE(kTraceTables);
-            if (st == 1) {
-              const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
-              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-            } else if (op.x_dtype == NQB_BF16) {
-              const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
-                                                    md.k_valid};
-              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-            } else if (op.x_dtype == NQB_F16) {
-              const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
-              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-            } else {
-              const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
-              mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-            }
+            mmad::quantize_loaded<kT, kQPT>(cur, nst, T, smem_b, s_sc, e, Q);
             NQB_TRACE(kTraceQuantise);
             for (int j = j0; j < j1; ++j) {
               int32_t d[kSets][kNT][4];
-#pragma unroll
+  #pragma unroll
               for (int c = 0; c < kSets; ++c)
-#pragma unroll
+  #pragma unroll
                 for (int nt = 0; nt < kNT; ++nt)
-#pragma unroll
+  #pragma unroll
                   for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
               for (int sl = 0; sl < nst; ++sl) {
                 NQB_TRACE(kTraceMma);
@@ -578,8 +609,78 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
               mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
               NQB_TRACE(kTraceDrain);
             }
+            j0 = nj0;
+            j1 = nj1;
+            c0 = nc0;
+            hi = nhi;
+            have = more;
+            if (have) {
+              if constexpr (kPrefetchUnits) {
+                cur = nxt;
+              } else {
+                load_unit(j0, c0, hi, cur);
+              }
+            }
           }
-          j0 = j1;
+        } else {
+          // ---- this CTA's quarter of every item of the group, member by member
+          for (int j0 = gb; j0 < ge;) {
+            const int mi = op.items[j0].member;
+            int j1 = j0 + 1;
+            while (j1 < ge && op.items[j1].member == mi) ++j1;
+            const MemberDev &md = op.md[mi];
+            const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
+            const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
+            for (int c0 = lo; c0 < hi; c0 += p.sc) {
+              const int nst = min(p.sc, hi - c0);
+              const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+              int e[kT];
+              long long Q[kT];
+              NQB_TRACE(kTraceTables);
+              if (st == 1) {
+                const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_BF16) {
+                const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
+                                                      md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_F16) {
+                const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              } else {
+                const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              }
+              NQB_TRACE(kTraceQuantise);
+              for (int j = j0; j < j1; ++j) {
+                int32_t d[kSets][kNT][4];
+  #pragma unroll
+                for (int c = 0; c < kSets; ++c)
+  #pragma unroll
+                  for (int nt = 0; nt < kNT; ++nt)
+  #pragma unroll
+                    for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
+                for (int sl = 0; sl < nst; ++sl) {
+                  NQB_TRACE(kTraceMma);
+                  if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+                  NQB_TRACE(kTraceWaitSigns);
+                  const mmad::SliceWords w =
+                      mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+                  if (++slot == R) {
+                    slot = 0;
+                    ++phase;
+                  }
+                  mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
+                }
+                NQB_TRACE(kTraceMma);
+                mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
+                NQB_TRACE(kTraceDrain);
+              }
+            }
+            j0 = j1;
+          }
         }
         // ---- quarters -> leaders: asynchronous stores into their shared
         // memory, counted on each leader's s_x_full
