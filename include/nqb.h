@@ -149,8 +149,8 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
  * NQB_ERR_WORKSPACE and launch nothing.  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress, with that device current);
  * make that first call before any stream capture.  All calls on a device share
- * the one array, so calls that may overlap on the GPU (different streams, or
- * concurrent graph replays) race: serialise them.  Allocates nothing.
+ * the one array, so calls that may overlap on the GPU (for example calls on
+ * different streams) race: serialise them.  Allocates nothing.
  */
 int nqb_linear_noalloc(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int64_t tokens,
                        float *y, void *stream);
