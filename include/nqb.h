@@ -218,6 +218,47 @@ int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t ran
                        const int32_t *payload, const int32_t *codebook, int32_t *words_out, void *stream);
 
 /*
+ * Decode-step shell (batch 1..16): the non-packed work of a decoder step
+ * around its packed linears.  The reference runs these in its model shell
+ * (runtime/torch_model.py:185-421) with Triton kernels pinned to one geometry
+ * (cuda_kernels.py:401-812: RoPE, decode attention, cache update, bf16
+ * output projection); these take any head count and cache length.
+ * Asynchronous on `stream`; no allocation, no synchronisation.
+ *
+ * nqb_rmsnorm: per token, h += delta (when delta is not NULL, h written
+ *   back), out = h * rsqrt(mean(h^2) + eps) * weight.  h, delta fp32
+ *   [tokens, hidden]; weight [hidden]; out [tokens, hidden] in out_dtype.
+ * nqb_qk_norm_rope: q fp32 [tokens, q_heads, head_dim], k and v fp32
+ *   [tokens, kv_heads, head_dim].  q and k heads: RMSNorm over the head with
+ *   q_weight / k_weight (either may be NULL: no norm), then rotate-half RoPE
+ *   with cos_table / sin_table rows [tokens, head_dim]; q to q_out (bf16,
+ *   shaped like q), k and v to the bf16 caches [kv_heads, cache_len, head_dim]
+ *   at row position + t.  head_dim is 64, 128 or 256.
+ * nqb_decode_attention: q bf16 [tokens, q_heads, head_dim]; token t attends
+ *   to cache rows [0, keys + t) of kv head (q head / (q_heads / kv_heads))
+ *   with scale head_dim^-1/2; out bf16 [tokens, q_heads * head_dim].
+ *   Split-K partials go to the workspace (nqb_decode_attention_workspace_bytes).
+ * nqb_silu_mul: out[i] = silu(gate[i]) * up[i] over `count` fp32 values.
+ * nqb_gemv_bf16: out[t, r] = sum_c weight[r, c] * x[t, c]; weight bf16
+ *   [rows, cols] (cols a multiple of 8, at most 51200, 16-byte aligned),
+ *   x bf16 [tokens, cols], out fp32 [tokens, rows].
+ */
+int nqb_rmsnorm(float *h, const float *delta, const void *weight, int32_t weight_dtype, int64_t tokens,
+                int64_t hidden, float eps, void *out, int32_t out_dtype, void *stream);
+int nqb_qk_norm_rope(const float *q, const float *k, const float *v, const void *q_weight, const void *k_weight,
+                     int32_t weight_dtype, const float *cos_table, const float *sin_table, int64_t tokens,
+                     int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, void *q_out, void *k_cache,
+                     void *v_cache, int64_t cache_len, int64_t position, void *stream);
+int nqb_decode_attention_workspace_bytes(int64_t keys, int64_t tokens, int32_t q_heads, int32_t head_dim,
+                                         size_t *bytes);
+int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len, int64_t keys,
+                         int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim, void *out,
+                         void *workspace, size_t workspace_bytes, void *stream);
+int nqb_silu_mul(const float *gate, const float *up, int64_t count, void *out, int32_t out_dtype, void *stream);
+int nqb_gemv_bf16(const void *weight, int64_t rows, int64_t cols, const void *x, int64_t tokens, float *out,
+                  void *stream);
+
+/*
  * Kernel-native copy of a layout-v1 sign matrix for the tensor-core path:
  * rows are grouped in tiles of 128; within a tile, for every 4-word chunk of a
  * row, the 128 rows' 16-byte chunks are stored consecutively; rows and chunks

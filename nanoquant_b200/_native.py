@@ -148,6 +148,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
     "nqb_decode_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "nqb_rmsnorm": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64, ctypes.c_float, _c_void_p, _i32,
+                                   _c_void_p]),
+    "nqb_qk_norm_rope": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p,
+                                        _i64, _i32, _i32, _i32, ctypes.c_float, _c_void_p, _c_void_p, _c_void_p, _i64,
+                                        _i64, _c_void_p]),
+    "nqb_decode_attention_workspace_bytes": (ctypes.c_int, [_i64, _i64, _i32, _i32, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_decode_attention": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _i32, _i32,
+                                            _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_silu_mul": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _i32, _c_void_p]),
+    "nqb_gemv_bf16": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
 }
 
 _lock = threading.Lock()

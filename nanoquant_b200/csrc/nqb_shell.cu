@@ -1,0 +1,491 @@
+// Decode-step shell kernels (batch 1..16): the work of a decoder step around
+// its packed linears -- RMSNorm with the residual add, per-head q/k RMSNorm
+// with rotate-half RoPE and the KV-cache append, split-K grouped-query
+// attention over the bf16 cache, the SwiGLU product, and the bf16 output
+// projection (lm head) as an HBM-streaming GEMV.
+//
+// Every reduction runs in a fixed order (warp shuffles, then the warps'
+// partials in index order), so results are bitwise reproducible.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "nqb.h"
+#include "nqb_common.cuh"
+
+namespace nqb {
+namespace shell {
+
+__device__ __forceinline__ void store_as(void *p, int64_t i, int32_t dt, float v) {
+  if (dt == NQB_F32) {
+    static_cast<float *>(p)[i] = v;
+  } else if (dt == NQB_BF16) {
+    static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  } else {
+    static_cast<__half *>(p)[i] = __float2half_rn(v);
+  }
+}
+
+// Sum over the block (blockDim.x a multiple of 32, at most 1024 threads).
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float s = 0.0f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += scratch[w];
+  __syncthreads();
+  return s;
+}
+
+// One block per token: h += delta (when given, written back), then
+// out = h * rsqrt(mean(h^2) + eps) * w.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *delta, const void *w, int32_t w_dt,
+                                                      int64_t hidden, float eps, void *out, int32_t out_dt) {
+  __shared__ float scratch[32];
+  const int64_t t = blockIdx.x;
+  float *row = h + t * hidden;
+  const float *drow = delta != nullptr ? delta + t * hidden : nullptr;
+  float ss = 0.0f;
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+    float v = row[i];
+    if (drow != nullptr) {
+      v += drow[i];
+      row[i] = v;
+    }
+    ss += v * v;
+  }
+  const float r = rsqrtf(block_sum(ss, scratch) / static_cast<float>(hidden) + eps);
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x)
+    store_as(out, t * hidden + i, out_dt, row[i] * r * load_as_float(w, i, w_dt));
+}
+
+// One warp per (token, head) over q heads, then k heads, then v heads.  Lane
+// l holds dimensions [l * kDpl, (l + 1) * kDpl); the rotate-half partner of a
+// dimension is in lane l ^ 16.  q and k: RMSNorm over the head (weight
+// optional), then RoPE with the token's cos/sin rows; q goes to q_out, k and
+// v to the caches at position + t.
+template <int kDpl>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const float *q, const float *k, const float *v, const void *qw, const void *kw, int32_t w_dt, const float *cos_t,
+    const float *sin_t, int64_t tokens, int32_t q_heads, int32_t kv_heads, float eps, __nv_bfloat16 *q_out,
+    __nv_bfloat16 *kcache, __nv_bfloat16 *vcache, int64_t cache_len, int64_t position) {
+  constexpr int kHd = 32 * kDpl;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int heads = q_heads + 2 * kv_heads;
+  if (gw >= tokens * heads) return;  // uniform over the warp
+  const int64_t t = gw / heads;
+  const int hh = static_cast<int>(gw - t * heads);
+  const int d0 = lane * kDpl;
+  const float *src;
+  const void *w = nullptr;
+  __nv_bfloat16 *dst;
+  bool rope = true;
+  if (hh < q_heads) {
+    src = q + (t * q_heads + hh) * kHd;
+    w = qw;
+    dst = q_out + (t * q_heads + hh) * kHd;
+  } else if (hh < q_heads + kv_heads) {
+    const int kh = hh - q_heads;
+    src = k + (t * kv_heads + kh) * kHd;
+    w = kw;
+    dst = kcache + (static_cast<int64_t>(kh) * cache_len + position + t) * kHd;
+  } else {
+    const int vh = hh - q_heads - kv_heads;
+    src = v + (t * kv_heads + vh) * kHd;
+    dst = vcache + (static_cast<int64_t>(vh) * cache_len + position + t) * kHd;
+    rope = false;
+  }
+  float x[kDpl];
+#pragma unroll
+  for (int j = 0; j < kDpl; ++j) x[j] = src[d0 + j];
+  if (rope) {  // uniform over the warp
+    if (w != nullptr) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kDpl; ++j) ss += x[j] * x[j];
+      const float r = rsqrtf(warp_sum(ss) / static_cast<float>(kHd) + eps);
+#pragma unroll
+      for (int j = 0; j < kDpl; ++j) x[j] = x[j] * r * load_as_float(w, d0 + j, w_dt);
+    }
+    float partner[kDpl];
+#pragma unroll
+    for (int j = 0; j < kDpl; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, x[j], 16);
+    const float *c = cos_t + t * kHd;
+    const float *s = sin_t + t * kHd;
+    const float sign = lane < 16 ? -1.0f : 1.0f;  // rotate_half: (-x2, x1)
+#pragma unroll
+    for (int j = 0; j < kDpl; ++j) x[j] = x[j] * c[d0 + j] + sign * partner[j] * s[d0 + j];
+  }
+#pragma unroll
+  for (int j = 0; j < kDpl; ++j) dst[d0 + j] = __float2bfloat16_rn(x[j]);
+}
+
+// kDpl consecutive bf16 values (4, 8 or 16 bytes, aligned) as floats.
+template <int kDpl>
+__device__ __forceinline__ void load_bf16_row(const __nv_bfloat16 *p, float (&out)[kDpl]) {
+  if constexpr (kDpl == 2) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+    out[0] = f.x;
+    out[1] = f.y;
+  } else if constexpr (kDpl == 4) {
+    const uint2 raw = *reinterpret_cast<const uint2 *>(p);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      out[2 * i] = f.x;
+      out[2 * i + 1] = f.y;
+    }
+  } else {
+    static_assert(kDpl == 8, "2, 4 or 8 values per lane");
+    const uint4 raw = *reinterpret_cast<const uint4 *>(p);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      out[2 * i] = f.x;
+      out[2 * i + 1] = f.y;
+    }
+  }
+}
+
+// Split-K attention partials.  Grid (kv_heads, splits, tokens); one warp per
+// q head of the kv head's group.  Token t sees keys [0, keys + t); split sp
+// covers [sp * chunk, min((sp + 1) * chunk, keys + t)).  Keys go in blocks of
+// kB: the block's K and V rows are loaded before any is used and its kB
+// dot-product reductions are interleaved, so one block costs about one
+// memory round trip.  Writes (acc[hd], m, l) of an online softmax per
+// (token, q head, split).
+template <int kDpl>
+__global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bfloat16 *kc, const __nv_bfloat16 *vc,
+                                         int64_t cache_len, int64_t keys, int32_t q_heads, int32_t kv_heads,
+                                         int32_t splits, int64_t chunk, float scale, float *part) {
+  constexpr int kHd = 32 * kDpl;
+  constexpr int kB = kDpl <= 4 ? 8 : 4;
+  const int kh = blockIdx.x, sp = blockIdx.y;
+  const int64_t t = blockIdx.z;
+  const int group = q_heads / kv_heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qh = kh * group + warp;
+  const int d0 = lane * kDpl;
+  const int64_t visible = keys + t;
+  const int64_t j0 = static_cast<int64_t>(sp) * chunk;
+  const int64_t j1 = min(j0 + chunk, visible);
+  float qv[kDpl], acc[kDpl];
+  load_bf16_row<kDpl>(q + (t * q_heads + qh) * kHd + d0, qv);
+#pragma unroll
+  for (int j = 0; j < kDpl; ++j) {
+    qv[j] *= scale;
+    acc[j] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  const __nv_bfloat16 *kbase = kc + static_cast<int64_t>(kh) * cache_len * kHd + d0;
+  const __nv_bfloat16 *vbase = vc + static_cast<int64_t>(kh) * cache_len * kHd + d0;
+  for (int64_t j = j0; j < j1; j += kB) {
+    const int nb = static_cast<int>(min(static_cast<int64_t>(kB), j1 - j));
+    float kv[kB][kDpl], vv[kB][kDpl];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int64_t row = j + (b < nb ? b : 0);  // rows past the block re-read row j (masked below)
+      load_bf16_row<kDpl>(kbase + row * kHd, kv[b]);
+      load_bf16_row<kDpl>(vbase + row * kHd, vv[b]);
+    }
+    float sc[kB];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      float d = 0.0f;
+#pragma unroll
+      for (int e = 0; e < kDpl; ++e) d += qv[e] * kv[b][e];
+      sc[b] = d;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+      for (int b = 0; b < kB; ++b) sc[b] += __shfl_xor_sync(0xffffffffu, sc[b], off);
+    }
+    float mb = sc[0];
+#pragma unroll
+    for (int b = 1; b < kB; ++b)
+      if (b < nb) mb = fmaxf(mb, sc[b]);
+    const float mn = fmaxf(m, mb);
+    const float corr = expf(m - mn);
+    l *= corr;
+#pragma unroll
+    for (int e = 0; e < kDpl; ++e) acc[e] *= corr;
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      if (b < nb) {
+        const float p = expf(sc[b] - mn);
+        l += p;
+#pragma unroll
+        for (int e = 0; e < kDpl; ++e) acc[e] += p * vv[b][e];
+      }
+    }
+    m = mn;
+  }
+  float *o = part + ((t * q_heads + qh) * splits + sp) * (kHd + 2);
+#pragma unroll
+  for (int e = 0; e < kDpl; ++e) o[d0 + e] = acc[e];
+  if (lane == 0) {
+    o[kHd] = m;
+    o[kHd + 1] = l;
+  }
+}
+
+// One warp per (token, q head): joins the splits in index order.
+template <int kDpl>
+__global__ void attention_combine_kernel(const float *part, int32_t splits, int64_t tokens, int32_t q_heads,
+                                         __nv_bfloat16 *out) {
+  constexpr int kHd = 32 * kDpl;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= tokens * q_heads) return;
+  const float *base = part + gw * splits * (kHd + 2);
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, base[s * (kHd + 2) + kHd]);
+  float den = 0.0f, num[kDpl];
+#pragma unroll
+  for (int e = 0; e < kDpl; ++e) num[e] = 0.0f;
+  for (int s = 0; s < splits; ++s) {
+    const float *p = base + s * (kHd + 2);
+    const float f = p[kHd] == -INFINITY ? 0.0f : expf(p[kHd] - mx);
+    den += f * p[kHd + 1];
+#pragma unroll
+    for (int e = 0; e < kDpl; ++e) num[e] += f * p[lane * kDpl + e];
+  }
+  const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+  for (int e = 0; e < kDpl; ++e) out[gw * kHd + lane * kDpl + e] = __float2bfloat16_rn(num[e] * inv);
+}
+
+__global__ void silu_mul_kernel(const float *gate, const float *up, int64_t n, void *out, int32_t out_dt) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float g = gate[i];
+  store_as(out, i, out_dt, g / (1.0f + expf(-g)) * up[i]);
+}
+
+// out[t][r] = sum_c W[r][c] x[t][c] for kT tokens; W bf16 [rows][cols] with
+// cols % 8 == 0 and 16-byte aligned rows, streamed once with 16-byte loads;
+// x staged in shared memory as fp32.  One warp per row, rows strided over
+// the grid's warps.
+template <int kT>
+__global__ void __launch_bounds__(256) gemv_bf16_kernel(const __nv_bfloat16 *w, const __nv_bfloat16 *x, int64_t rows,
+                                                        int64_t cols, int64_t x_stride, float *out, int64_t out_stride) {
+  extern __shared__ float xs[];  // [kT][cols]
+  for (int64_t i = threadIdx.x; i < kT * cols; i += blockDim.x) {
+    const int64_t t = i / cols;
+    xs[i] = __bfloat162float(x[t * x_stride + (i - t * cols)]);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t units = cols / 8;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const uint4 *wr = reinterpret_cast<const uint4 *>(w + r * cols);
+    float acc[kT];
+#pragma unroll
+    for (int t = 0; t < kT; ++t) acc[t] = 0.0f;
+#pragma unroll 4
+    for (int64_t u = lane; u < units; u += 32) {
+      const uint4 raw = __ldcs(wr + u);
+      const __nv_bfloat162 *pairs = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(pairs[e]);
+#pragma unroll
+        for (int t = 0; t < kT; ++t) {
+          const float *xr = xs + t * cols + u * 8 + 2 * e;
+          acc[t] += f.x * xr[0] + f.y * xr[1];
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kT; ++t) {
+      const float s = warp_sum(acc[t]);
+      if (lane == 0) out[t * out_stride + r] = s;
+    }
+  }
+}
+
+// Splits of the attention: 64 keys each (eight blocks of eight per warp), at
+// most 64.  (32-key splits measured slower: the combine over twice as many
+// partials costs more than the shorter key loop saves.)
+int splits_for(int64_t keys, int64_t tokens) {
+  const int64_t most = keys + tokens - 1;
+  const int64_t s = (most + 63) / 64;
+  return static_cast<int>(s < 1 ? 1 : (s > 64 ? 64 : s));
+}
+
+int launch_sm_count() {
+  int device = 0, sms = 148;
+  if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  return sms;
+}
+
+}  // namespace shell
+}  // namespace nqb
+
+using namespace nqb;
+
+extern "C" {
+
+int nqb_rmsnorm(float *h, const float *delta, const void *weight, int32_t weight_dtype, int64_t tokens, int64_t hidden,
+                float eps, void *out, int32_t out_dtype, void *stream) {
+  if (h == nullptr || weight == nullptr || out == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "rmsnorm operand is NULL");
+  if (tokens <= 0 || hidden <= 0 || !(eps >= 0.0f)) return fail(NQB_ERR_INVALID_ARGUMENT, "rmsnorm shape or eps invalid");
+  if (!is_float_dtype(weight_dtype) || !is_float_dtype(out_dtype)) return fail(NQB_ERR_DTYPE, "rmsnorm dtype invalid");
+  shell::rmsnorm_kernel<<<static_cast<unsigned>(tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      h, delta, weight, weight_dtype, hidden, eps, out, out_dtype);
+  NQB_CUDA(cudaGetLastError(), "rmsnorm launch");
+  return ok();
+}
+
+int nqb_qk_norm_rope(const float *q, const float *k, const float *v, const void *q_weight, const void *k_weight,
+                     int32_t weight_dtype, const float *cos_table, const float *sin_table, int64_t tokens,
+                     int32_t q_heads, int32_t kv_heads, int32_t head_dim, float eps, void *q_out, void *k_cache,
+                     void *v_cache, int64_t cache_len, int64_t position, void *stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || cos_table == nullptr || sin_table == nullptr || q_out == nullptr ||
+      k_cache == nullptr || v_cache == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "rope operand is NULL");
+  if (tokens <= 0 || q_heads <= 0 || kv_heads <= 0 || position < 0 || position + tokens > cache_len)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "rope shape or cache position invalid");
+  if ((q_weight != nullptr || k_weight != nullptr) && !is_float_dtype(weight_dtype))
+    return fail(NQB_ERR_DTYPE, "rope norm weight dtype invalid");
+  const int64_t warps = tokens * (q_heads + 2 * kv_heads);
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  auto s = static_cast<cudaStream_t>(stream);
+  auto *qo = static_cast<__nv_bfloat16 *>(q_out);
+  auto *kc = static_cast<__nv_bfloat16 *>(k_cache);
+  auto *vc = static_cast<__nv_bfloat16 *>(v_cache);
+  switch (head_dim) {
+    case 64:
+      shell::qk_norm_rope_kernel<2><<<blocks, 256, 0, s>>>(q, k, v, q_weight, k_weight, weight_dtype, cos_table,
+                                                            sin_table, tokens, q_heads, kv_heads, eps, qo, kc, vc,
+                                                            cache_len, position);
+      break;
+    case 128:
+      shell::qk_norm_rope_kernel<4><<<blocks, 256, 0, s>>>(q, k, v, q_weight, k_weight, weight_dtype, cos_table,
+                                                            sin_table, tokens, q_heads, kv_heads, eps, qo, kc, vc,
+                                                            cache_len, position);
+      break;
+    case 256:
+      shell::qk_norm_rope_kernel<8><<<blocks, 256, 0, s>>>(q, k, v, q_weight, k_weight, weight_dtype, cos_table,
+                                                            sin_table, tokens, q_heads, kv_heads, eps, qo, kc, vc,
+                                                            cache_len, position);
+      break;
+    default:
+      return fail(NQB_ERR_UNSUPPORTED, "head_dim %d is not 64, 128 or 256", head_dim);
+  }
+  NQB_CUDA(cudaGetLastError(), "rope launch");
+  return ok();
+}
+
+int nqb_decode_attention_workspace_bytes(int64_t keys, int64_t tokens, int32_t q_heads, int32_t head_dim,
+                                         size_t *bytes) {
+  if (bytes == nullptr || keys <= 0 || tokens <= 0 || q_heads <= 0 || head_dim <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "attention workspace query is invalid");
+  *bytes = static_cast<size_t>(tokens) * q_heads * shell::splits_for(keys, tokens) * (head_dim + 2) * sizeof(float);
+  return ok();
+}
+
+int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len, int64_t keys,
+                         int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim, void *out,
+                         void *workspace, size_t workspace_bytes, void *stream) {
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || workspace == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "attention operand is NULL");
+  if (tokens <= 0 || keys <= 0 || keys + tokens - 1 > cache_len || kv_heads <= 0 || q_heads % kv_heads != 0 ||
+      q_heads / kv_heads > 32)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "attention shape invalid (keys, cache length or head grouping)");
+  size_t need = 0;
+  NQB_CHECK(nqb_decode_attention_workspace_bytes(keys, tokens, q_heads, head_dim, &need));
+  if (workspace_bytes < need) return fail(NQB_ERR_WORKSPACE, "attention workspace too small");
+  const int splits = shell::splits_for(keys, tokens);
+  const int64_t chunk = (keys + tokens - 1 + splits - 1) / splits;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+  const dim3 grid(static_cast<unsigned>(kv_heads), static_cast<unsigned>(splits), static_cast<unsigned>(tokens));
+  const unsigned threads = static_cast<unsigned>(32 * (q_heads / kv_heads));
+  const unsigned cblocks = static_cast<unsigned>((tokens * q_heads * 32 + 255) / 256);
+  auto s = static_cast<cudaStream_t>(stream);
+  auto *qp = static_cast<const __nv_bfloat16 *>(q);
+  auto *kc = static_cast<const __nv_bfloat16 *>(k_cache);
+  auto *vc = static_cast<const __nv_bfloat16 *>(v_cache);
+  auto *part = static_cast<float *>(workspace);
+  auto *o = static_cast<__nv_bfloat16 *>(out);
+  switch (head_dim) {
+    case 64:
+      shell::attention_partial_kernel<2><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
+                                                                   splits, chunk, scale, part);
+      shell::attention_combine_kernel<2><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
+      break;
+    case 128:
+      shell::attention_partial_kernel<4><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
+                                                                   splits, chunk, scale, part);
+      shell::attention_combine_kernel<4><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
+      break;
+    case 256:
+      shell::attention_partial_kernel<8><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
+                                                                   splits, chunk, scale, part);
+      shell::attention_combine_kernel<8><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
+      break;
+    default:
+      return fail(NQB_ERR_UNSUPPORTED, "head_dim %d is not 64, 128 or 256", head_dim);
+  }
+  NQB_CUDA(cudaGetLastError(), "attention launch");
+  return ok();
+}
+
+int nqb_silu_mul(const float *gate, const float *up, int64_t count, void *out, int32_t out_dtype, void *stream) {
+  if (gate == nullptr || up == nullptr || out == nullptr || count <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "silu_mul operand is NULL or empty");
+  if (!is_float_dtype(out_dtype)) return fail(NQB_ERR_DTYPE, "silu_mul output dtype invalid");
+  shell::silu_mul_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      gate, up, count, out, out_dtype);
+  NQB_CUDA(cudaGetLastError(), "silu_mul launch");
+  return ok();
+}
+
+int nqb_gemv_bf16(const void *weight, int64_t rows, int64_t cols, const void *x, int64_t tokens, float *out,
+                  void *stream) {
+  if (weight == nullptr || x == nullptr || out == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "gemv operand is NULL");
+  if (rows <= 0 || cols <= 0 || tokens <= 0 || cols % 8 != 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "gemv needs positive sizes and a multiple of 8 columns");
+  if (reinterpret_cast<uintptr_t>(weight) % 16 != 0) return fail(NQB_ERR_ALIGNMENT, "gemv weight is not 16-byte aligned");
+  if (cols * 4 > 200 * 1024) return fail(NQB_ERR_UNSUPPORTED, "gemv rows longer than %d columns", 200 * 1024 / 4);
+  auto s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(shell::launch_sm_count() * 8);
+  auto *w = static_cast<const __nv_bfloat16 *>(weight);
+  auto *xp = static_cast<const __nv_bfloat16 *>(x);
+  for (int64_t t0 = 0; t0 < tokens;) {
+    const int64_t left = tokens - t0;
+    const int group = left >= 8 && cols * 8 * 4 <= 200 * 1024   ? 8
+                      : left >= 4 && cols * 4 * 4 <= 200 * 1024 ? 4
+                      : left >= 2 && cols * 2 * 4 <= 200 * 1024 ? 2
+                                                                 : 1;
+    const size_t smem = static_cast<size_t>(group) * cols * sizeof(float);
+    const void *fn = group == 8   ? reinterpret_cast<const void *>(shell::gemv_bf16_kernel<8>)
+                     : group == 4 ? reinterpret_cast<const void *>(shell::gemv_bf16_kernel<4>)
+                     : group == 2 ? reinterpret_cast<const void *>(shell::gemv_bf16_kernel<2>)
+                                  : reinterpret_cast<const void *>(shell::gemv_bf16_kernel<1>);
+    NQB_CHECK(ensure_dynamic_smem(fn, smem));
+    const __nv_bfloat16 *xt = xp + t0 * cols;
+    float *ot = out + t0 * rows;
+    if (group == 8)
+      shell::gemv_bf16_kernel<8><<<grid, 256, smem, s>>>(w, xt, rows, cols, cols, ot, rows);
+    else if (group == 4)
+      shell::gemv_bf16_kernel<4><<<grid, 256, smem, s>>>(w, xt, rows, cols, cols, ot, rows);
+    else if (group == 2)
+      shell::gemv_bf16_kernel<2><<<grid, 256, smem, s>>>(w, xt, rows, cols, cols, ot, rows);
+    else
+      shell::gemv_bf16_kernel<1><<<grid, 256, smem, s>>>(w, xt, rows, cols, cols, ot, rows);
+    NQB_CUDA(cudaGetLastError(), "gemv launch");
+    t0 += group;
+  }
+  return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,283 @@
+"""A Qwen3-style decoder step around the packed linears (batch 1..16).
+
+The decode-step shell: what a decoder layer does besides its seven packed
+projections.  Per layer
+
+    xn   = rmsnorm(h) * w_in                       (bf16)
+    q, k, v = qkv(xn)                              (one persistent program)
+    q, k = rope(rmsnorm_head(q) * q_norm), rope(rmsnorm_head(k) * k_norm)
+    cache[pos + t] <- k, v                         (bf16 caches)
+    a    = attention(q, cache)                     (grouped-query, split-K)
+    h   += o_proj(a);   xn2 = rmsnorm(h) * w_post
+    h   += down(silu(gate(xn2)) * up(xn2))
+
+then ``logits = lm_head(rmsnorm(h) * w_final)`` with a dense bf16 lm head.
+The shell kernels are ``nqb_rmsnorm``, ``nqb_qk_norm_rope``,
+``nqb_decode_attention``, ``nqb_silu_mul`` and ``nqb_gemv_bf16``; the packed
+projections run as four decode programs per layer.  This mirrors the
+reference's model shell (``src/nanoquant/runtime/torch_model.py:185-421``),
+which runs the same math with torch modules and Triton kernels pinned to one
+geometry (``cuda_kernels.py:401-812``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from nanoquant_b200 import _native
+from nanoquant_b200.cuda_backend import CudaPackedSm100Backend
+from nanoquant_b200.decode_chain import DecoderShape, make_decoder_layers
+from nanoquant_b200.program import DecodeProgram, ProgramOp
+
+
+def _stream(device: torch.device) -> int:
+    return _native.current_stream_handle(device)
+
+
+def rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
+    """``h += delta`` (when given), ``out = h * rsqrt(mean(h^2) + eps) * weight`` per token (``nqb_rmsnorm``)."""
+
+    tokens, hidden = h.shape
+    _native.call("nqb_rmsnorm", h.data_ptr(), 0 if delta is None else delta.data_ptr(), weight.data_ptr(),
+                 _native.dtype_code(weight.dtype), tokens, hidden, ctypes.c_float(eps), out.data_ptr(),
+                 _native.dtype_code(out.dtype), _stream(h.device))
+
+
+def qk_norm_rope(q, k, v, q_weight, k_weight, cos, sin, q_out, k_cache, v_cache, position: int, eps: float,
+                 q_heads: int, kv_heads: int, head_dim: int) -> None:
+    """Per-head q/k RMSNorm and rotate-half RoPE; k, v appended to the caches (``nqb_qk_norm_rope``)."""
+
+    tokens = q.shape[0]
+    _native.call("nqb_qk_norm_rope", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                 0 if q_weight is None else q_weight.data_ptr(), 0 if k_weight is None else k_weight.data_ptr(),
+                 _native.dtype_code(q_weight.dtype if q_weight is not None else torch.float32), cos.data_ptr(),
+                 sin.data_ptr(), tokens, q_heads, kv_heads, head_dim, ctypes.c_float(eps), q_out.data_ptr(),
+                 k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[1], position, _stream(q.device))
+
+
+def attention_workspace_bytes(keys: int, tokens: int, q_heads: int, head_dim: int) -> int:
+    size = ctypes.c_size_t(0)
+    _native.call("nqb_decode_attention_workspace_bytes", keys, tokens, q_heads, head_dim, ctypes.byref(size))
+    return size.value
+
+
+def decode_attention(q, k_cache, v_cache, keys: int, q_heads: int, kv_heads: int, head_dim: int, out,
+                     workspace: torch.Tensor) -> None:
+    """Grouped-query attention of ``tokens`` queries over the caches (``nqb_decode_attention``)."""
+
+    _native.call("nqb_decode_attention", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[1], keys,
+                 q.shape[0], q_heads, kv_heads, head_dim, out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                 _stream(q.device))
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
+    """``out = silu(gate) * up`` (``nqb_silu_mul``)."""
+
+    _native.call("nqb_silu_mul", gate.data_ptr(), up.data_ptr(), gate.numel(), out.data_ptr(),
+                 _native.dtype_code(out.dtype), _stream(gate.device))
+
+
+def gemv_bf16(weight: torch.Tensor, x: torch.Tensor, out: torch.Tensor) -> None:
+    """``out[t] = weight @ x[t]`` with a bf16 ``weight`` streamed once (``nqb_gemv_bf16``)."""
+
+    _native.call("nqb_gemv_bf16", weight.data_ptr(), weight.shape[0], weight.shape[1], x.data_ptr(), x.shape[0],
+                 out.data_ptr(), _stream(x.device))
+
+
+def rope_tables(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin rows ``[len(positions), head_dim]`` (halves duplicated), fp32."""
+
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    angles = positions.to(torch.float64)[:, None] * inv[None, :]
+    emb = torch.cat((angles, angles), dim=-1)
+    return emb.cos().float(), emb.sin().float()
+
+
+@dataclass
+class ShellWeights:
+    """The dense (non-packed) weights of one decoder: per-layer norms, final norm, lm head."""
+
+    input_norm: list[torch.Tensor]
+    post_norm: list[torch.Tensor]
+    q_norm: list[torch.Tensor]
+    k_norm: list[torch.Tensor]
+    final_norm: torch.Tensor
+    lm_head: torch.Tensor
+
+
+def random_shell_weights(shape: DecoderShape, vocab: int, device: torch.device, *, layers: int | None = None,
+                         seed: int = 1) -> ShellWeights:
+    """bf16 norms ``1 + N(0, 0.02)`` and a bf16 lm head ``N(0, 0.02)`` (random init)."""
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    count = shape.layers if layers is None else layers
+
+    def norm(size: int) -> torch.Tensor:
+        return (1.0 + 0.02 * torch.randn(size, generator=g, device=device)).bfloat16()
+
+    return ShellWeights(
+        [norm(shape.hidden) for _ in range(count)], [norm(shape.hidden) for _ in range(count)],
+        [norm(shape.head_dim) for _ in range(count)], [norm(shape.head_dim) for _ in range(count)],
+        norm(shape.hidden), (0.02 * torch.randn(vocab, shape.hidden, generator=g, device=device)).bfloat16())
+
+
+class Qwen3DecodeStep:
+    """One decode step of ``tokens`` new tokens at cache position ``position``.
+
+    ``blocks``: per layer the packed states of q/k/v/o/gate/up/down (as from
+    :func:`make_decoder_layers`); ``shell``: the dense weights; the KV caches
+    hold ``position`` prior tokens (rows ``[0, position)``, random N(0, 1)
+    here) and get the new tokens' keys and values at rows ``position + t``.
+    :meth:`step` returns the fp32 logits ``[tokens, vocab]``; the position
+    does not advance (each step recomputes the same tokens), so replays of a
+    captured step are identical.
+    """
+
+    def __init__(self, shape: DecoderShape, blocks, shell: ShellWeights, device: torch.device, *, tokens: int = 1,
+                 position: int = 0, cache_len: int | None = None, eps: float = 1e-6, rope_theta: float = 1e6,
+                 kv_init: torch.Generator | None = None) -> None:
+        if not 1 <= tokens <= 16:
+            raise ValueError("a decode step takes 1 to 16 tokens")
+        self.shape, self.device, self.tokens, self.position, self.eps = shape, device, tokens, position, eps
+        self.shell = shell
+        self.cache_len = cache_len if cache_len is not None else position + tokens
+        if position + tokens > self.cache_len:
+            raise ValueError("the cache is too short for the step's tokens")
+        backend = CudaPackedSm100Backend()
+        hd, hq, hkv = shape.head_dim, shape.q_heads, shape.kv_heads
+        f32 = {"dtype": torch.float32, "device": device}
+        bf16 = {"dtype": torch.bfloat16, "device": device}
+        self.hidden_in = torch.zeros(tokens, shape.hidden, **f32)  # the step's input embeddings
+        self.h = torch.zeros(tokens, shape.hidden, **f32)  # residual stream
+        self.xn = torch.zeros(tokens, shape.hidden, **bf16)
+        self.q_rot = torch.zeros(tokens, hq * hd, **bf16)
+        self.attn = torch.zeros(tokens, hq * hd, **bf16)
+        self.act = torch.zeros(tokens, shape.intermediate, **bf16)
+        self.logits = torch.zeros(tokens, shell.lm_head.shape[0], **f32)
+        self.keys = position + 1
+        self.attn_ws = torch.empty(attention_workspace_bytes(self.keys, tokens, hq, hd), dtype=torch.uint8,
+                                   device=device)
+        self.cos, self.sin = (t.to(device) for t in rope_tables(
+            torch.arange(position, position + tokens), hd, rope_theta))
+        g = kv_init if kv_init is not None else torch.Generator(device=device).manual_seed(2)
+        self.layers = []
+        for block in blocks:
+            prepared = {name: backend.prepare(state, device) for name, state in block.items()}
+            q = torch.zeros(tokens, hq * hd, **f32)
+            k = torch.zeros(tokens, hkv * hd, **f32)
+            v = torch.zeros(tokens, hkv * hd, **f32)
+            o = torch.zeros(tokens, shape.hidden, **f32)
+            gate = torch.zeros(tokens, shape.intermediate, **f32)
+            up = torch.zeros(tokens, shape.intermediate, **f32)
+            down = torch.zeros(tokens, shape.hidden, **f32)
+            kc = torch.zeros(hkv, self.cache_len, hd, **bf16)
+            vc = torch.zeros(hkv, self.cache_len, hd, **bf16)
+            if position:
+                kc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
+                vc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
+            self.layers.append({
+                "prog_qkv": DecodeProgram([ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]),
+                                                     self.xn)], outputs=[(q, k, v)]),
+                "prog_o": DecodeProgram([ProgramOp((prepared["o_proj"],), self.attn)], outputs=[(o,)]),
+                "prog_gate_up": DecodeProgram([ProgramOp((prepared["gate_proj"], prepared["up_proj"]), self.xn)],
+                                              outputs=[(gate, up)]),
+                "prog_down": DecodeProgram([ProgramOp((prepared["down_proj"],), self.act)], outputs=[(down,)]),
+                "q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc, "v_cache": vc,
+                "prepared": prepared,
+            })
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def kernel_launches(self) -> int:
+        """Kernels one step launches: per layer 4 programs, 2 norms, rope, attention (2) and SwiGLU; then the
+        final norm and the lm head (the input copy is a library copy)."""
+
+        return len(self.layers) * 10 + 2
+
+    def step(self, hidden: torch.Tensor | None = None) -> torch.Tensor:
+        """Run the step on the current stream from ``hidden`` (the new tokens' embeddings; default: the
+        last ones given)."""
+
+        s, hd = self.shape, self.shape.head_dim
+        if hidden is not None:
+            self.hidden_in.copy_(hidden)
+        self.h.copy_(self.hidden_in)
+        delta = None
+        for index, layer in enumerate(self.layers):
+            rmsnorm(self.h, delta, self.shell.input_norm[index], self.eps, self.xn)
+            layer["prog_qkv"].run()
+            qk_norm_rope(layer["q"], layer["k"], layer["v"], self.shell.q_norm[index], self.shell.k_norm[index],
+                         self.cos, self.sin, self.q_rot, layer["k_cache"], layer["v_cache"], self.position, self.eps,
+                         s.q_heads, s.kv_heads, hd)
+            decode_attention(self.q_rot, layer["k_cache"], layer["v_cache"], self.keys, s.q_heads, s.kv_heads, hd,
+                             self.attn, self.attn_ws)
+            layer["prog_o"].run()
+            rmsnorm(self.h, layer["o"], self.shell.post_norm[index], self.eps, self.xn)
+            layer["prog_gate_up"].run()
+            silu_mul(layer["gate"], layer["up"], self.act)
+            layer["prog_down"].run()
+            delta = layer["down"]
+        rmsnorm(self.h, delta, self.shell.final_norm, self.eps, self.xn)
+        gemv_bf16(self.shell.lm_head, self.xn, self.logits)
+        return self.logits
+
+    def capture(self) -> None:
+        """Record one step (from the current input) into a CUDA graph; :meth:`replay` then reruns it."""
+
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step()
+        self.graph = graph
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+        return self.logits
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes one step must move: packed weights and scales, KV rows read, lm head, norms."""
+
+        s = self.shape
+        packed = 0
+        for layer in self.layers:
+            for prepared in layer["prepared"].values():
+                spec = prepared.spec
+                packed += (spec.out_features * ((spec.rank + 31) // 32) + spec.rank * ((spec.in_features + 31) // 32)) * 4
+                packed += (spec.in_features + spec.rank + spec.out_features) * 2
+        kv = len(self.layers) * 2 * s.kv_heads * (self.keys + self.tokens - 1) * s.head_dim * 2
+        head = self.shell.lm_head.numel() * 2
+        norms = len(self.layers) * (2 * s.hidden + 2 * s.head_dim) * 2 + s.hidden * 2
+        return packed + kv + head + norms
+
+
+def build_qwen3_step(shape: DecoderShape, device: torch.device, *, vocab: int, tokens: int = 1, position: int = 0,
+                     layers: int | None = None, seed: int = 0) -> Qwen3DecodeStep:
+    """Random-init packed layers and shell weights of ``shape`` wired into one decode step."""
+
+    blocks = make_decoder_layers(shape, device, layers=layers, seed=seed)
+    shell = random_shell_weights(shape, vocab, device, layers=len(blocks), seed=seed + 1)
+    return Qwen3DecodeStep(shape, blocks, shell, device, tokens=tokens, position=position)
+
+
+__all__ = [
+    "Qwen3DecodeStep",
+    "ShellWeights",
+    "attention_workspace_bytes",
+    "build_qwen3_step",
+    "decode_attention",
+    "gemv_bf16",
+    "qk_norm_rope",
+    "random_shell_weights",
+    "rmsnorm",
+    "rope_tables",
+    "silu_mul",
+]

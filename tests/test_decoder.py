@@ -1,0 +1,214 @@
+"""Decode-step shell (``nanoquant_b200.decoder``) against torch formulas and the decoder oracle.
+
+CPU tests pin the oracle's pieces (bf16 rounding, RMSNorm, RoPE, attention)
+to torch's own formulations.  ``gpu`` tests check each shell kernel against
+a torch or float64 reference of the same op, and a two-layer decoder step
+(packed projections + shell) against ``oracle.decoder_oracle`` with the
+full-model bound: logits cosine >= 0.9999.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import decoder_oracle as do
+
+
+def test_oracle_bf16_rounding_matches_torch() -> None:
+    x = (np.random.default_rng(0).standard_normal(10000) * 10).astype(np.float32)
+    x[:4] = (1.00390625, 1.01171875, -3.0e-39, 65504.0)  # ties and tiny values
+    expected = torch.from_numpy(x).bfloat16().float().numpy()
+    assert np.array_equal(do.bf16(x), expected)
+
+
+def test_oracle_pieces_match_torch_formulas() -> None:
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((3, 64)).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(64)).astype(np.float32)
+    t = torch.from_numpy(x).double()
+    ref = (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * torch.from_numpy(w).double()).float().numpy()
+    np.testing.assert_allclose(do.rmsnorm(x, w, 1e-6), ref, rtol=1e-6, atol=1e-6)
+    cos, sin = do.rope_tables(np.arange(5, 8), 64, 1e6)
+    rot = do.rotate(x, cos, sin)
+    # a rotation keeps the norm of every (i, i + 32) pair
+    np.testing.assert_allclose(rot[:, :32] ** 2 + rot[:, 32:] ** 2, x[:, :32] ** 2 + x[:, 32:] ** 2, rtol=1e-5)
+    q = rng.standard_normal((2, 4, 64)).astype(np.float32)
+    kc = rng.standard_normal((2, 40, 64)).astype(np.float32)
+    vc = rng.standard_normal((2, 40, 64)).astype(np.float32)
+    out = do.attention(q, kc, vc, 30)
+    for tok in range(2):
+        for h in range(4):
+            s = torch.from_numpy(kc[h // 2, : 30 + tok]).double() @ torch.from_numpy(q[tok, h]).double() / 8.0
+            ref = torch.softmax(s, 0) @ torch.from_numpy(vc[h // 2, : 30 + tok]).double()
+            np.testing.assert_allclose(out[tok, h], ref.numpy(), rtol=1e-5, atol=1e-6)
+
+
+# ------------------------------------------------------------------ GPU ---
+
+
+def _gpu() -> torch.device:
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test needs CUDA")
+    return torch.device("cuda", 0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("delta", (False, True))
+def test_rmsnorm_kernel(delta: bool) -> None:
+    from nanoquant_b200.decoder import rmsnorm
+
+    dev = _gpu()
+    g = torch.Generator(device=dev).manual_seed(3)
+    h = torch.randn(5, 4096, generator=g, device=dev)
+    d = torch.randn(5, 4096, generator=g, device=dev) if delta else None
+    w = (1 + 0.02 * torch.randn(4096, generator=g, device=dev)).bfloat16()
+    out = torch.empty(5, 4096, dtype=torch.bfloat16, device=dev)
+    ref_h = h + d if delta else h.clone()
+    rmsnorm(h, d, w, 1e-6, out)
+    torch.testing.assert_close(h, ref_h, rtol=0, atol=0)
+    hd = ref_h.double()
+    ref = (hd * torch.rsqrt(hd.pow(2).mean(-1, keepdim=True) + 1e-6) * w.double()).float()
+    torch.testing.assert_close(out.float(), ref, rtol=8e-3, atol=1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("head_dim", (64, 128, 256))
+def test_qk_norm_rope_kernel(head_dim: int) -> None:
+    from nanoquant_b200.decoder import qk_norm_rope, rope_tables
+
+    dev = _gpu()
+    g = torch.Generator(device=dev).manual_seed(head_dim)
+    tokens, hq, hkv, pos, cache = 3, 8, 2, 11, 20
+    q = torch.randn(tokens, hq * head_dim, generator=g, device=dev)
+    k = torch.randn(tokens, hkv * head_dim, generator=g, device=dev)
+    v = torch.randn(tokens, hkv * head_dim, generator=g, device=dev)
+    qw = (1 + 0.02 * torch.randn(head_dim, generator=g, device=dev)).bfloat16()
+    kw = (1 + 0.02 * torch.randn(head_dim, generator=g, device=dev)).bfloat16()
+    cos, sin = (t.to(dev) for t in rope_tables(torch.arange(pos, pos + tokens), head_dim, 1e6))
+    q_out = torch.empty(tokens, hq * head_dim, dtype=torch.bfloat16, device=dev)
+    kc = torch.zeros(hkv, cache, head_dim, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    qk_norm_rope(q, k, v, qw, kw, cos, sin, q_out, kc, vc, pos, 1e-6, hq, hkv, head_dim)
+    c, s = do.rope_tables(np.arange(pos, pos + tokens), head_dim, 1e6)
+    ref_q = do.rotate(do.rmsnorm(q.cpu().numpy().reshape(tokens, hq, head_dim), qw.float().cpu().numpy(), 1e-6),
+                      c[:, None], s[:, None])
+    ref_k = do.rotate(do.rmsnorm(k.cpu().numpy().reshape(tokens, hkv, head_dim), kw.float().cpu().numpy(), 1e-6),
+                      c[:, None], s[:, None])
+    np.testing.assert_allclose(q_out.float().cpu().numpy().reshape(tokens, hq, head_dim), ref_q, rtol=8e-3, atol=8e-3)
+    for t in range(tokens):
+        np.testing.assert_allclose(kc[:, pos + t].float().cpu().numpy(), ref_k[t], rtol=8e-3, atol=8e-3)
+        np.testing.assert_array_equal(vc[:, pos + t].float().cpu().numpy(),
+                                      do.bf16(v.cpu().numpy().reshape(tokens, hkv, head_dim)[t]))
+    assert not kc[:, :pos].any() and not kc[:, pos + tokens:].any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("head_dim", "keys", "tokens"),
+                         ((64, 1, 1), (128, 300, 3), (128, 2049, 1), (128, 2049, 16), (256, 77, 16)))
+def test_decode_attention_kernel(head_dim: int, keys: int, tokens: int) -> None:
+    from nanoquant_b200.decoder import attention_workspace_bytes, decode_attention
+
+    dev = _gpu()
+    g = torch.Generator(device=dev).manual_seed(keys)
+    hq, hkv, cache = 8, 2, keys + tokens + 5
+    q = torch.randn(tokens, hq * head_dim, generator=g, device=dev).bfloat16()
+    kc = torch.randn(hkv, cache, head_dim, generator=g, device=dev).bfloat16()
+    vc = torch.randn(hkv, cache, head_dim, generator=g, device=dev).bfloat16()
+    out = torch.empty(tokens, hq * head_dim, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(attention_workspace_bytes(keys, tokens, hq, head_dim), dtype=torch.uint8, device=dev)
+    decode_attention(q, kc, vc, keys, hq, hkv, head_dim, out, ws)
+    ref = do.attention(q.float().cpu().numpy().reshape(tokens, hq, head_dim), kc.float().cpu().numpy(),
+                       vc.float().cpu().numpy(), keys)
+    np.testing.assert_allclose(out.float().cpu().numpy().reshape(tokens, hq, head_dim), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens", (1, 3, 9, 16))
+def test_silu_mul_and_gemv_kernels(tokens: int) -> None:
+    from nanoquant_b200.decoder import gemv_bf16, silu_mul
+
+    dev = _gpu()
+    g = torch.Generator(device=dev).manual_seed(tokens)
+    gate = torch.randn(tokens, 700, generator=g, device=dev)
+    up = torch.randn(tokens, 700, generator=g, device=dev)
+    act = torch.empty(tokens, 700, dtype=torch.bfloat16, device=dev)
+    silu_mul(gate, up, act)
+    torch.testing.assert_close(act.float(), (torch.nn.functional.silu(gate) * up).bfloat16().float(), rtol=8e-3,
+                               atol=8e-3)
+    w = (0.02 * torch.randn(1003, 4096, generator=g, device=dev)).bfloat16()
+    x = torch.randn(tokens, 4096, generator=g, device=dev).bfloat16()
+    out = torch.empty(tokens, 1003, device=dev)
+    gemv_bf16(w, x, out)
+    ref = (x.double() @ w.double().T).float()
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+
+
+def _tiny_shape():
+    from nanoquant_b200.decode_chain import DecoderShape
+
+    return DecoderShape("tiny", 2, 256, 512, 4, 2, 64, 1.0)
+
+
+def _host_state(state):
+    from dataclasses import fields, replace
+
+    moved = {f.name: getattr(state, f.name).cpu() for f in fields(state)
+             if isinstance(getattr(state, f.name), torch.Tensor)}
+    return replace(state, **moved)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens", (1, 3))
+def test_decoder_step_matches_oracle(tokens: int) -> None:
+    from nanoquant_b200.decode_chain import make_decoder_layers
+    from nanoquant_b200.decoder import Qwen3DecodeStep, random_shell_weights
+    from tests.test_cuda_parity import oracle_from_state
+
+    dev = _gpu()
+    shape = _tiny_shape()
+    blocks = make_decoder_layers(shape, dev, layers=2, seed=4)
+    shell = random_shell_weights(shape, 1000, dev, layers=2, seed=5)
+    step = Qwen3DecodeStep(shape, blocks, shell, dev, tokens=tokens, position=37)
+    k0 = [layer["k_cache"].float().cpu().numpy() for layer in step.layers]
+    v0 = [layer["v_cache"].float().cpu().numpy() for layer in step.layers]
+    hidden = torch.randn(tokens, shape.hidden, generator=torch.Generator(device=dev).manual_seed(6), device=dev)
+    logits = step.step(hidden).cpu().numpy()
+    torch.cuda.synchronize()
+    layers = [{name: oracle_from_state(_host_state(state)) for name, state in block.items()} for block in blocks]
+    norms = {
+        "input_norm": [w.float().cpu().numpy() for w in shell.input_norm],
+        "post_norm": [w.float().cpu().numpy() for w in shell.post_norm],
+        "q_norm": [w.float().cpu().numpy() for w in shell.q_norm],
+        "k_norm": [w.float().cpu().numpy() for w in shell.k_norm],
+        "final_norm": shell.final_norm.float().cpu().numpy(),
+        "lm_head": shell.lm_head.float().cpu().numpy(),
+    }
+    ref, k1, v1 = do.decode_step(hidden.cpu().numpy(), layers, norms, k0, v0, position=37, q_heads=4, kv_heads=2,
+                                 head_dim=64, eps=1e-6, theta=1e6)
+    for a, b in zip(logits, ref, strict=True):
+        cosine = float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+        assert cosine >= 0.9999, cosine
+    assert float(np.abs(logits - ref).max() / np.abs(ref).max()) <= 2e-2
+    for i, layer in enumerate(step.layers):
+        got_v = layer["v_cache"].float().cpu().numpy()
+        np.testing.assert_array_equal(got_v[:, :37], v0[i][:, :37])
+        np.testing.assert_allclose(got_v[:, 37:37 + tokens], v1[i][:, 37:37 + tokens], rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(layer["k_cache"].float().cpu().numpy()[:, 37:37 + tokens],
+                                   k1[i][:, 37:37 + tokens], rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+def test_decoder_step_graph_replay_is_bitwise_eager() -> None:
+    from nanoquant_b200.decoder import build_qwen3_step
+
+    dev = _gpu()
+    step = build_qwen3_step(_tiny_shape(), dev, vocab=512, tokens=2, position=9, layers=2, seed=7)
+    hidden = torch.randn(2, 256, generator=torch.Generator(device=dev).manual_seed(8), device=dev)
+    eager = step.step(hidden).clone()
+    step.capture()
+    first = step.replay().clone()
+    second = step.replay().clone()
+    torch.cuda.synchronize()
+    assert torch.equal(eager, first) and torch.equal(first, second)
