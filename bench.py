@@ -170,13 +170,63 @@ def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
     }
 
 
+def cpu_baseline_step(repeats: int = 1) -> dict:
+    """CPU time of a full Qwen3-8B step, composed of three timed parts.
+
+    It adds the packed linears (``cpu_baseline("decode")``, the oracle on 2
+    of 36 layers), the shell math of the decoder oracle (norms, q/k norm and
+    RoPE, attention over 2049 cached rows, SwiGLU) timed on 2 layers, and the
+    151936 x 4096 lm head, all extrapolated to one step.
+    """
+
+    import numpy as np
+
+    from nanoquant_b200 import decode_chain
+    from oracle import decoder_oracle as do
+
+    shape = decode_chain.QWEN3_8B
+    hd, hkv, hq = shape.head_dim, shape.kv_heads, shape.q_heads
+    linears = cpu_baseline("decode", repeats=1)
+    rng = np.random.default_rng(0)
+    caches = do.bf16(rng.standard_normal((hkv, STEP_POSITION + 1, hd)).astype(np.float32))
+    h = rng.standard_normal((1, shape.hidden)).astype(np.float32)
+    w = np.ones(shape.hidden, np.float32)
+    qkv = rng.standard_normal((1, (hq + 2 * hkv) * hd)).astype(np.float32)
+    gate = rng.standard_normal((1, shape.intermediate)).astype(np.float32)
+    cos, sin = do.rope_tables(np.arange(STEP_POSITION, STEP_POSITION + 1), hd, 1e6)
+    sample_layers = 2
+    start = time.perf_counter()
+    for _ in range(repeats * sample_layers):
+        xn = do.bf16(do.rmsnorm(h, w, 1e-6))
+        q = do.bf16(do.rotate(do.rmsnorm(qkv[:, : hq * hd].reshape(1, hq, hd), np.ones(hd, np.float32), 1e-6),
+                              cos[:, None], sin[:, None]))
+        do.attention(q, caches, caches, STEP_POSITION + 1)
+        xn = do.bf16(do.rmsnorm(h + xn, w, 1e-6))
+        do.bf16(gate / (1.0 + np.exp(-gate)) * gate)
+    shell_layer = (time.perf_counter() - start) / (repeats * sample_layers)
+    head = (0.02 * rng.standard_normal((STEP_VOCAB, shape.hidden))).astype(np.float32)
+    start = time.perf_counter()
+    _ = head @ h[0]
+    head_s = time.perf_counter() - start
+    step = linears["ms_per_step"] * 1e-3 + shell_layer * shape.layers + head_s
+    cores = os.cpu_count() or 1
+    return {
+        "value": 1.0 / step, "unit": UNIT, "cores": cores, "kind": "port",
+        "sample": f"packed linears: {linears['sample']}; shell (oracle norms, rope, attention over "
+                  f"{STEP_POSITION + 1} rows, swiglu) on {sample_layers} layers and the {STEP_VOCAB} x "
+                  f"{shape.hidden} lm head, extrapolated to {shape.layers} layers",
+        "ms_per_step": step * 1e3,
+    }
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """The reference arm: the reference's packed CPU algorithm (oracle port) on the host cores."""
 
     if rank != 0:
         return
     spec = WORKLOADS[args.workload]
-    base = cpu_baseline(args.workload, repeats=max(1, min(args.steps, 5)))
+    base = (cpu_baseline_step() if spec["kind"] == "step"
+            else cpu_baseline(args.workload, repeats=max(1, min(args.steps, 5))))
     line = {
         "impl": "reference",
         "metric": spec["metric"],
@@ -187,7 +237,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "warmup": args.warmup,
         "ms_per_step": base["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak" if spec["kind"] == "decode" else "strong",
+        "scaling": "weak" if spec["kind"] != "prefill" else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
@@ -197,6 +247,32 @@ def run_reference(args, rank: int, world: int) -> None:
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+class _StepAdapter:
+    """A full decoder step (``nanoquant_b200.decoder``) behind the DecodeChain methods the timing loop uses."""
+
+    def __init__(self, step) -> None:
+        self.step_obj = step
+        self.inputs = {"hidden": step.hidden_in}
+        self.blocks = step.layers
+        self.program = None
+        self.launches_per_step = step.kernel_launches()
+
+    def capture(self) -> None:
+        self.step_obj.capture()
+
+    def replay(self):
+        return self.step_obj.replay()
+
+    def step(self):
+        return self.step_obj.step()
+
+    def algorithmic_bytes(self) -> int:
+        return self.step_obj.algorithmic_bytes()
+
+
+STEP_VOCAB, STEP_POSITION = 151936, 2048
 
 
 WORKLOADS = {
@@ -227,6 +303,16 @@ WORKLOADS = {
         "decode_tokens": 1,
         "description": "gemma-3-1b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
         "model": "gemma-3-1b-shape random-init packed weights ~1 bpw",
+    },
+    "decode-step": {
+        "kind": "step",
+        "metric": "decode tok/s (bs1, full Qwen3-8B-shaped step: packed linears + shell + lm head); HBM GB/s vs peak",
+        "shape": "QWEN3_8B",
+        "tokens_total": None,
+        "decode_tokens": 1,
+        "description": "qwen3-8b decode step bs1 ({layers} layers: norms, packed q/k/v/o/gate/up/down, q/k norm + "
+                       "rope, attention over 2048 cached tokens, swiglu; final norm; bf16 lm head 151936 x 4096)",
+        "model": "qwen3-8b-shape random-init: packed weights ~1 bpw, bf16 norms and lm head, bf16 kv cache N(0,1)",
     },
     "prefill": {
         "kind": "prefill",
@@ -259,7 +345,7 @@ def main() -> None:
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = 50 if WORKLOADS[args.workload]["kind"] == "decode" else 3
+        args.steps = 50 if WORKLOADS[args.workload]["kind"] != "prefill" else 3
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -296,9 +382,15 @@ def main() -> None:
         tokens = spec["tokens_total"] // world
         if args.tokens is not None:
             tokens = args.tokens
-    chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device, tokens=tokens,
-                        engine=args.engine)
-    decode = spec["kind"] == "decode"
+    if spec["kind"] == "step":
+        from nanoquant_b200.decoder import build_qwen3_step
+
+        chain = _StepAdapter(build_qwen3_step(shape, device, vocab=STEP_VOCAB, tokens=tokens, position=STEP_POSITION,
+                                              layers=args.layers))
+    else:
+        chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device,
+                            tokens=tokens, engine=args.engine)
+    decode = spec["kind"] in ("decode", "step")
     use_graph = decode and chain.program is None
     if use_graph:
         chain.capture()
@@ -357,7 +449,9 @@ def main() -> None:
         roofline = {
             "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"][0], "unit": "GB/s",
             "frac": achieved / peaks["hbm"][0], "traffic": None, "peak_kind": peaks["hbm"][1],
-            "scope": "all packed-linear kernels of one step (algorithmic bytes per step / step time)",
+            "scope": ("the whole decoder step: packed weights and scales, kv rows read, norms, lm head"
+                      if spec["kind"] == "step" else
+                      "all packed-linear kernels of one step (algorithmic bytes per step / step time)"),
             "algorithmic_bytes_per_step": step_bytes,
         }
     else:
@@ -391,8 +485,9 @@ def main() -> None:
             if world > 1 else "single",
             "l2": "weights larger than the 126 MB L2 (no flush)",
             "cuda_graph": use_graph,
-            "engine": "persistent program (one cooperative launch per step)" if chain.program is not None
-            else "per-call kernels",
+            "engine": ("persistent program (one cooperative launch per step)" if chain.program is not None
+                       else "decode programs (4 per layer) + shell kernels in one CUDA graph" if spec["kind"] == "step"
+                       else "per-call kernels"),
         },
         "roofline": roofline,
         "e2e": {
@@ -405,7 +500,7 @@ def main() -> None:
         "clocks": clocks.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:
-        base = cpu_baseline(args.workload)
+        base = cpu_baseline_step() if spec["kind"] == "step" else cpu_baseline(args.workload)
         line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line), flush=True)
