@@ -307,12 +307,19 @@ int nqb_device_status(int32_t *status);
  * nqb_program_workspace_bytes (256-byte aligned) whose first 16 KiB are zero
  * before the first run (every run leaves them zero).
  */
+/* Program op input code: x is the gate and x2 the up projection, both fp32
+ * [tokens, in_features]; the op reads silu(gate) * up (a SwiGLU product) as
+ * its input, so a gate/up op and the down op that consumes it share one
+ * program.  Members of such an op carry no salient columns or overlay rows. */
+#define NQB_X_SWIGLU 16
+
 typedef struct nqb_program_op {
   const nqb_linear_desc *layers; /* count members sharing x */
   int32_t count;                 /* 1..3 */
   const void *x;                 /* [tokens, in_features], x_dtype */
-  int32_t x_dtype;
+  int32_t x_dtype;               /* NQB_F32 / NQB_F16 / NQB_BF16, or NQB_X_SWIGLU */
   float *const *y;               /* count outputs [tokens, out_features] fp32 */
+  const void *x2;                /* NQB_X_SWIGLU only: the up projection; else NULL */
 } nqb_program_op;
 
 typedef struct nqb_program nqb_program;

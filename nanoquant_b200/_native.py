@@ -34,6 +34,7 @@ NQB_F16 = 1
 NQB_BF16 = 2
 NQB_I8 = 3
 NQB_I32 = 4
+NQB_X_SWIGLU = 16  # program-op input: silu(x) * x2, both fp32
 
 DTYPE_CODES = {
     torch.float32: NQB_F32,
@@ -93,6 +94,7 @@ class ProgramOp(ctypes.Structure):
         ("x", _c_void_p),
         ("x_dtype", _i32),
         ("y", ctypes.POINTER(_c_void_p)),
+        ("x2", _c_void_p),
     ]
 
 

@@ -66,6 +66,25 @@ struct XLoader {  // stage 1: x * pre, pre in fp32
   }
 };
 
+struct SwigluLoader {  // stage 1 of a down projection: silu(gate) * up * pre, gate and up fp32
+  const float *gate;
+  const float *up;
+  const float *pre;
+  int64_t stride;
+  int64_t k0;
+  int64_t k_valid;
+  __device__ __forceinline__ float operator()(int t, int col) const {
+    const int64_t k = k0 + col;
+    if (k >= k_valid) return 0.0f;
+    const int64_t i = static_cast<int64_t>(t) * stride + k;
+    const float g = __ldcg(gate + i);
+    // fast exp and divide keep the T=1 prefetch loop free of spills; clamping
+    // the exponent at 80 keeps the divisor below 2^126, inside __fdividef's
+    // range (silu(g) for g < -80 is below 1e-33 either way)
+    return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f))) * __ldcg(up + i) * __ldg(pre + k);
+  }
+};
+
 struct LatentLoader {  // stage 2: the fp32 latent slice of one member
   const float *latent;
   int64_t stride;

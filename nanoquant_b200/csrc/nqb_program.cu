@@ -83,6 +83,7 @@ struct OpDev {
   MemberDev s[2][kMaxMembersTc];  // [stage][member]
   int32_t count;
   const void *x;
+  const void *x2;  // NQB_X_SWIGLU: the up projection (x is the gate)
   int32_t x_dtype;
   int64_t n;
   int64_t latent_stride;
@@ -100,6 +101,7 @@ constexpr int kMaxStageItems = 64;
 struct __align__(16) StageInfo {
   MemberDev md[kMaxMembersTc];
   const void *x;
+  const void *x2;
   int64_t n;
   int64_t latent_stride;
   int32_t x_dtype;
@@ -342,6 +344,7 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
   for (int i = lane; i < n_items * 2; i += 32) it_dst[i] = it_src[i];
   if (lane == 0) {
     info.x = op.x;
+    info.x2 = op.x2;
     info.n = op.n;
     info.latent_stride = op.latent_stride;
     info.x_dtype = op.x_dtype;
@@ -556,6 +559,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             if (st == 1) {
               mmad::load_chunk<kT, kQPT>(mmad::LatentLoader{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid},
                                          nst, T, cv);
+            } else if (op.x_dtype == NQB_X_SWIGLU) {
+              mmad::load_chunk<kT, kQPT>(mmad::SwigluLoader{static_cast<const float *>(op.x),
+                                                            static_cast<const float *>(op.x2), md.pre, op.n, k0,
+                                                            md.k_valid},
+                                         nst, T, cv);
             } else if (op.x_dtype == NQB_BF16) {
               mmad::load_chunk<kT, kQPT>(mmad::XLoader<__nv_bfloat16>{static_cast<const __nv_bfloat16 *>(op.x), md.pre,
                                                                      op.n, k0, md.k_valid},
@@ -639,6 +647,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
               NQB_TRACE(kTraceTables);
               if (st == 1) {
                 const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_X_SWIGLU) {
+                const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                            md.pre, op.n, k0, md.k_valid};
                 mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
               } else if (op.x_dtype == NQB_BF16) {
                 const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
@@ -993,6 +1005,12 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     if (o.layers == nullptr || o.count < 1 || o.count > kMaxMembersTc)
       return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: 1 to %d layers", i, kMaxMembersTc);
     if (o.x == nullptr || o.y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: x or y is NULL", i);
+    const bool swiglu = o.x_dtype == NQB_X_SWIGLU;
+    if (swiglu && o.x2 == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a SwiGLU input needs x2", i);
+    if (swiglu)
+      for (int k = 0; k < o.count; ++k)
+        if (o.layers[k].outlier_count > 0 || o.layers[k].overlay_rows > 0)
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: SwiGLU inputs take no salient columns or overlay rows", i);
     int64_t rank_total = 0;
     for (int k = 0; k < o.count; ++k) {
       const nqb_linear_desc &d = o.layers[k];
@@ -1001,7 +1019,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
       rank_total += d.rank;
     }
-    if (!tc_eligible(o.layers, o.count, o.x_dtype, tokens))
+    if (!tc_eligible(o.layers, o.count, swiglu ? NQB_F32 : o.x_dtype, tokens))
       return fail(NQB_ERR_UNSUPPORTED, "op %d does not take the tensor-core decode path", i);
     latent_cols = std::max(latent_cols, rank_total);
   }
@@ -1058,6 +1076,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     std::memset(&od, 0, sizeof(od));
     od.count = o.count;
     od.x = o.x;
+    od.x2 = o.x_dtype == NQB_X_SWIGLU ? o.x2 : nullptr;
     od.x_dtype = o.x_dtype;
     od.n = o.layers[0].in_features;
     int64_t offset = 0;
@@ -1147,9 +1166,13 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
                                                  md.k_valid);
             if (hi > lo) {
               add_lines(lines, md.pre + lo, (hi - lo) * 4);
-              const int64_t xs = static_cast<int64_t>(dtype_size(op.x_dtype));
-              for (int64_t t = 0; t < tokens; ++t)
+              const bool swiglu = op.x_dtype == NQB_X_SWIGLU;
+              const int64_t xs = swiglu ? 4 : static_cast<int64_t>(dtype_size(op.x_dtype));
+              for (int64_t t = 0; t < tokens; ++t) {
                 add_lines(lines, static_cast<const char *>(op.x) + (t * op.n + lo) * xs, (hi - lo) * xs);
+                if (swiglu)
+                  add_lines(lines, static_cast<const char *>(op.x2) + (t * op.n + lo) * xs, (hi - lo) * xs);
+              }
             }
           }
           if (static_cast<int>(j % kClusterSize) == q) {

@@ -14,7 +14,10 @@ projections.  Per layer
 then ``logits = lm_head(rmsnorm(h) * w_final)`` with a dense bf16 lm head.
 The shell kernels are ``nqb_rmsnorm``, ``nqb_qk_norm_rope``,
 ``nqb_decode_attention``, ``nqb_silu_mul`` and ``nqb_gemv_bf16``; the packed
-projections run as four decode programs per layer.  This mirrors the
+projections run as three decode programs per layer: qkv, o, and an MLP
+program whose second op forms ``silu(gate) * up`` as it loads its input (so
+``nqb_silu_mul`` runs only for a down projection with salient columns, which
+the fused input does not take).  This mirrors the
 reference's model shell (``src/nanoquant/runtime/torch_model.py:185-421``),
 which runs the same math with torch modules and Triton kernels pinned to one
 geometry (``cuda_kernels.py:401-812``).
@@ -182,19 +185,31 @@ class Qwen3DecodeStep:
                 "prog_qkv": DecodeProgram([ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]),
                                                      self.xn)], outputs=[(q, k, v)]),
                 "prog_o": DecodeProgram([ProgramOp((prepared["o_proj"],), self.attn)], outputs=[(o,)]),
-                "prog_gate_up": DecodeProgram([ProgramOp((prepared["gate_proj"], prepared["up_proj"]), self.xn)],
-                                              outputs=[(gate, up)]),
-                "prog_down": DecodeProgram([ProgramOp((prepared["down_proj"],), self.act)], outputs=[(down,)]),
+                "prog_mlp": self._mlp_program(prepared, gate, up, down),
                 "q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc, "v_cache": vc,
                 "prepared": prepared,
             })
         self.graph: torch.cuda.CUDAGraph | None = None
 
-    def kernel_launches(self) -> int:
-        """Kernels one step launches: per layer 4 programs, 2 norms, rope, attention (2) and SwiGLU; then the
-        final norm and the lm head (the input copy is a library copy)."""
+    def _mlp_program(self, prepared: dict, gate: torch.Tensor, up: torch.Tensor,
+                     down: torch.Tensor) -> DecodeProgram | tuple[DecodeProgram, DecodeProgram]:
+        """gate/up then down in one program with the SwiGLU product formed as the down op loads it; a down
+        projection with salient columns or overlay rows keeps two programs around ``nqb_silu_mul``."""
 
-        return len(self.layers) * 10 + 2
+        gate_up = ProgramOp((prepared["gate_proj"], prepared["up_proj"]), self.xn)
+        desc = prepared["down_proj"].payload.desc
+        if desc.outlier_count == 0 and desc.overlay_rows == 0:
+            return DecodeProgram([gate_up, ProgramOp((prepared["down_proj"],), gate, x2=up)],
+                                 outputs=[(gate, up), (down,)])
+        return (DecodeProgram([gate_up], outputs=[(gate, up)]),
+                DecodeProgram([ProgramOp((prepared["down_proj"],), self.act)], outputs=[(down,)]))
+
+    def kernel_launches(self) -> int:
+        """Kernels one step launches: per layer 3 programs (4 with a split MLP, plus its SwiGLU kernel), 2 norms,
+        rope and attention (2); then the final norm and the lm head (the input copy is a library copy)."""
+
+        split = sum(isinstance(layer["prog_mlp"], tuple) for layer in self.layers)
+        return len(self.layers) * 8 + 2 * split + 2
 
     def step(self, hidden: torch.Tensor | None = None) -> torch.Tensor:
         """Run the step on the current stream from ``hidden`` (the new tokens' embeddings; default: the
@@ -215,9 +230,13 @@ class Qwen3DecodeStep:
                              self.attn, self.attn_ws)
             layer["prog_o"].run()
             rmsnorm(self.h, layer["o"], self.shell.post_norm[index], self.eps, self.xn)
-            layer["prog_gate_up"].run()
-            silu_mul(layer["gate"], layer["up"], self.act)
-            layer["prog_down"].run()
+            mlp = layer["prog_mlp"]
+            if isinstance(mlp, tuple):
+                mlp[0].run()
+                silu_mul(layer["gate"], layer["up"], self.act)
+                mlp[1].run()
+            else:
+                mlp.run()
             delta = layer["down"]
         rmsnorm(self.h, delta, self.shell.final_norm, self.eps, self.xn)
         gemv_bf16(self.shell.lm_head, self.xn, self.logits)

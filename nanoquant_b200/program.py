@@ -28,10 +28,18 @@ from nanoquant_b200.cuda_backend import _Sm100Payload, _check_input
 
 @dataclass(frozen=True)
 class ProgramOp:
-    """One call: ``layers`` (1..3 sharing ``x``) -> one fp32 output per layer."""
+    """One call: ``layers`` (1..3 sharing ``x``) -> one fp32 output per layer.
+
+    With ``x2`` set, ``x`` is a gate and ``x2`` an up projection (both fp32,
+    same shape) and the op's input is their SwiGLU product
+    ``silu(x) * x2``, formed as the op loads it: the SwiGLU MLP's down
+    projection (reference ``runtime/torch_model.py:395-421``) then shares a
+    program with the gate/up op that produces its inputs.
+    """
 
     layers: tuple[PreparedLayer, ...]
     x: torch.Tensor
+    x2: torch.Tensor | None = None
 
 
 class DecodeProgram:
@@ -59,6 +67,11 @@ class DecodeProgram:
                 raise ValueError("all program tensors must be on one device")
             spec = op.layers[0].spec
             _check_input(op.x, spec, device)
+            if op.x2 is not None:
+                if op.x.dtype != torch.float32 or op.x2.dtype != torch.float32:
+                    raise ValueError("SwiGLU op inputs are fp32")
+                if op.x2.shape != op.x.shape or not op.x2.is_contiguous() or op.x2.device != device:
+                    raise ValueError("SwiGLU op x2 must be a contiguous tensor shaped like x on x's device")
             op_tokens = op.x.numel() // spec.in_features
             if tokens is None:
                 tokens = op_tokens
@@ -79,12 +92,13 @@ class DecodeProgram:
             self.outputs.append(outs)
             descs = (_native.LinearDesc * len(payloads))(*(payload.desc for payload in payloads))
             ys = (ctypes.c_void_p * len(outs))(*(out.data_ptr() for out in outs))
-            self._keep.extend((descs, ys, op.x, outs, op.layers))
+            self._keep.extend((descs, ys, op.x, op.x2, outs, op.layers))
             c_ops[index].layers = descs
             c_ops[index].count = len(payloads)
             c_ops[index].x = op.x.data_ptr()
-            c_ops[index].x_dtype = _native.dtype_code(op.x.dtype)
+            c_ops[index].x_dtype = _native.dtype_code(op.x.dtype) if op.x2 is None else _native.NQB_X_SWIGLU
             c_ops[index].y = ys
+            c_ops[index].x2 = None if op.x2 is None else op.x2.data_ptr()
         assert tokens is not None
         self.device = device
         self.tokens = tokens

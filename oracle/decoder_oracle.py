@@ -4,7 +4,8 @@ The checker for ``nanoquant_b200.decoder``: numpy float32 arithmetic (float64
 where noted), the packed projections through ``packed_oracle.packed_linear``,
 and bf16 rounding (round to nearest even) at the points where the device path
 stores bf16: the normalised activations, the rotated queries and keys, the
-cache rows, the attention output and the SwiGLU product.  The layer math
+cache rows and the attention output.  The SwiGLU product stays float32: the
+device forms it as the down projection loads its input.  The layer math
 follows the reference model shell (``src/nanoquant/runtime/torch_model.py:
 185-421``: RMSNorm, per-head q/k RMSNorm, rotate-half RoPE, grouped-query
 attention, SwiGLU MLP, residual adds, final norm and lm head).  Only tests
@@ -97,7 +98,7 @@ def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: l
         xn = bf16(rmsnorm(h, norms["post_norm"][i], eps))
         gate = linear(xn, proj["gate_proj"])
         up = linear(xn, proj["up_proj"])
-        act = bf16(gate / (1.0 + np.exp(-gate)) * up)
+        act = (gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)
         h = h + linear(act, proj["down_proj"])
     xn = bf16(rmsnorm(h, norms["final_norm"], eps))
     logits = (xn.astype(np.float64) @ norms["lm_head"].astype(np.float64).T).astype(np.float32)

@@ -147,3 +147,42 @@ def test_program_rejects_layers_with_a_patch() -> None:
     x = torch.zeros(1, state.spec.in_features, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError, match="patch"):
         DecodeProgram([ProgramOp((layer,), x)])
+
+
+@pytest.mark.parametrize("tokens", (1, 4, 16))
+def test_program_swiglu_input_matches_oracle(tokens: int) -> None:
+    """gate/up then down in one program: the down op forms silu(gate) * up as it loads its input."""
+
+    backend = CudaPackedSm100Backend()
+    gu_states = [_random_state(1152, 6912, 987, seed=80 + i) for i in range(2)]
+    down_state = _random_state(6912, 1152, 987, seed=90, bias=True)
+    gate_up = tuple(backend.prepare(s, "cuda") for s in gu_states)
+    down = backend.prepare(down_state, "cuda")
+    x = torch.randn(tokens, 1152, generator=torch.Generator().manual_seed(tokens)).bfloat16().cuda()
+    gate = torch.empty(tokens, 6912, device="cuda")
+    up = torch.empty(tokens, 6912, device="cuda")
+    out = torch.empty(tokens, 1152, device="cuda")
+    program = DecodeProgram([ProgramOp(gate_up, x), ProgramOp((down,), gate, x2=up)],
+                            outputs=[(gate, up), (out,)])
+    program.run()
+    torch.cuda.synchronize()
+    _check(gate, x, gu_states[0])
+    _check(up, x, gu_states[1])
+    act = torch.nn.functional.silu(gate) * up   # fp32, from the program's own gate/up outputs
+    _check(out, act, down_state)
+    assert ctypes_status() == 0
+
+
+def test_program_swiglu_input_rejects_salient_columns_and_bad_x2() -> None:
+    backend = CudaPackedSm100Backend()
+    salient = backend.prepare(_random_state(1024, 640, 480, seed=95, outliers=2), "cuda")
+    plain = backend.prepare(_random_state(1024, 640, 480, seed=96), "cuda")
+    gate = torch.zeros(1, 1024, device="cuda")
+    up = torch.zeros(1, 1024, device="cuda")
+    with pytest.raises(_native.NativeError) as info:
+        DecodeProgram([ProgramOp((salient,), gate, x2=up)])
+    assert info.value.status == _native.NQB_ERR_UNSUPPORTED
+    with pytest.raises(ValueError, match="fp32"):
+        DecodeProgram([ProgramOp((plain,), gate.bfloat16(), x2=up.bfloat16())])
+    with pytest.raises(ValueError, match="shaped like x"):
+        DecodeProgram([ProgramOp((plain,), gate, x2=torch.zeros(2, 1024, device="cuda"))])
