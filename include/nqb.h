@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NQB_ABI_VERSION 1
+#define NQB_ABI_VERSION 2
 
 /* status codes */
 #define NQB_OK 0
@@ -108,6 +108,16 @@ typedef struct nqb_linear_desc {
    * generic CUDA-core path (fp32).                                          */
   const void *left_tiles;  /* nqb_repack_signs(left_words,  m, r) */
   const void *right_tiles; /* nqb_repack_signs(right_words, r, n) */
+
+  /* Dense low-rank patch, y += L (R x) (reference cuda_backend.py:275-277,
+   * reference.py:224-232).  nqb_linear applies it itself: on the tensor-core
+   * decode path and in programs fused into the two stages (stage 1 also forms
+   * the patch latent R x, stage 2's epilogue adds L times it); on the other
+   * paths as two small kernels after stage 2.  patch_rank 0 = no patch.     */
+  int64_t patch_rank;      /* p */
+  const void *patch_left;  /* [m, p] in patch_dtype */
+  const void *patch_right; /* [p, n] in patch_dtype */
+  int32_t patch_dtype;     /* F32 / F16 / BF16 */
 } nqb_linear_desc;
 
 /* Library identity: NQB_ABI_VERSION of the loaded build. */
@@ -170,7 +180,10 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
 
 /*
  * Dense low-rank patch epilogue: y[t,o] += sum_p L[o,p] * sum_i R[p,i] x[t,i].
- * L [m, p], R [p, n] in patch_dtype.  Workspace: tokens*p fp32.
+ * L [m, p], R [p, n] in patch_dtype.  Workspace: tokens*p fp32.  A layer
+ * whose descriptor carries the patch needs no separate call: nqb_linear
+ * applies it (fused on the decode paths); this entry point stays for callers
+ * that keep the patch outside the descriptor.
  * Replaces the F.linear pair of CudaPackedBackend.linear (reference
  * cuda_backend.py:275-277).
  */

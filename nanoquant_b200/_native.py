@@ -81,6 +81,10 @@ class LinearDesc(ctypes.Structure):
         ("codebook_second", _c_void_p),
         ("left_tiles", _c_void_p),
         ("right_tiles", _c_void_p),
+        ("patch_rank", ctypes.c_int64),
+        ("patch_left", _c_void_p),
+        ("patch_right", _c_void_p),
+        ("patch_dtype", ctypes.c_int32),
     ]
 
 

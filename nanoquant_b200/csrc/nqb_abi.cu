@@ -115,6 +115,14 @@ static int validate_layer(const nqb_linear_desc *d, const char *name) {
     if (!is_float_dtype(d->overlay_scale_dtype))
       return fail(NQB_ERR_DTYPE, "%s: overlay scale dtype %d is not F32/F16/BF16", name, d->overlay_scale_dtype);
   }
+  if (d->patch_rank < 0 || d->patch_rank > (1ll << 20))
+    return fail(NQB_ERR_INVALID_ARGUMENT, "%s: patch rank must be between 0 and 2^20", name);
+  if (d->patch_rank > 0) {
+    if (d->patch_left == nullptr || d->patch_right == nullptr)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "%s: patch factors are NULL", name);
+    if (!is_float_dtype(d->patch_dtype))
+      return fail(NQB_ERR_DTYPE, "%s: patch dtype %d is not F32/F16/BF16", name, d->patch_dtype);
+  }
   return NQB_OK;
 }
 
@@ -132,6 +140,17 @@ static int64_t latent_columns(int64_t rank) { return (rank + 3) & ~int64_t(3); }
 
 static size_t latent_bytes(int64_t tokens, int64_t total_columns) {
   return align_up(static_cast<size_t>(tokens) * total_columns * sizeof(float), 256);
+}
+
+// Latent region of a call: the members' latents, then their patch latents
+// (member i's [tokens][patch_rank_i] block after those of members < i).
+static size_t latent_region_bytes(const nqb_linear_desc *layers, int count, int64_t tokens) {
+  int64_t columns = 0, patch = 0;
+  for (int i = 0; i < count; ++i) {
+    columns += latent_columns(layers[i].rank);
+    patch += layers[i].patch_rank;
+  }
+  return latent_bytes(tokens, columns) + latent_bytes(tokens, patch);
 }
 
 // Workspace layout shared by every call: [completion counters][latent][tensor-core partials].
@@ -255,35 +274,61 @@ int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, siz
   NQB_CHECK(validate_layer(layer, "layer"));
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
   if (tokens <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "token count must be positive");
-  *bytes = workspace_bytes(latent_bytes(tokens, latent_columns(layer->rank)), path_extra_bytes(layer, 1, tokens));
+  *bytes = workspace_bytes(latent_region_bytes(layer, 1, tokens), path_extra_bytes(layer, 1, tokens));
   return ok();
 }
+
+}  // extern "C"
+
+namespace nqb {
+
+// Runs 1..3 validated layers sharing x on the path their shapes take.  The
+// tensor-core decode path applies each member's patch inside its stages; the
+// prefill and generic paths add it with two small kernels per patched member.
+static int run_layers(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
+                      float *const *ys, void *workspace, size_t workspace_bytes_given, void *stream) {
+  const size_t need = latent_region_bytes(layers, count, tokens);
+  const size_t tc_need = path_extra_bytes(layers, count, tokens);
+  if (workspace == nullptr || workspace_bytes_given < workspace_bytes(need, tc_need) || !aligned(workspace, 256))
+    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
+                workspace_bytes(need, tc_need), workspace_bytes_given);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char *base = static_cast<char *>(workspace);
+  int32_t *counters = reinterpret_cast<int32_t *>(base);
+  float *latent = reinterpret_cast<float *>(base + kCounterRegionBytes);
+  int64_t columns = 0;
+  for (int i = 0; i < count; ++i) columns += latent_columns(layers[i].rank);
+  float *patch = reinterpret_cast<float *>(base + kCounterRegionBytes + latent_bytes(tokens, columns));
+  char *extra = base + kCounterRegionBytes + need;
+  if (tc_eligible(layers, count, x_dtype, tokens))
+    return run_tc(layers, count, x, x_dtype, tokens, ys, counters, extra, tc_need, latent, patch, s);
+  if (prefill_eligible(layers, count, x_dtype, tokens)) {
+    NQB_CHECK(run_prefill(layers, count, x, x_dtype, tokens, ys, latent, extra, tc_need, s));
+  } else {
+    NQB_CHECK(run_generic(layers, count, x, x_dtype, tokens, ys, latent, s));
+  }
+  int64_t patch_offset = 0;
+  for (int i = 0; i < count; ++i) {
+    const nqb_linear_desc &d = layers[i];
+    if (d.patch_rank == 0) continue;
+    NQB_CHECK(launch_patch(x, x_dtype, tokens, d.in_features, d.out_features, d.patch_rank, d.patch_left,
+                           d.patch_right, d.patch_dtype, ys[i], patch + tokens * patch_offset, s));
+    patch_offset += d.patch_rank;
+  }
+  return NQB_OK;
+}
+
+}  // namespace nqb
+
+extern "C" {
 
 int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int64_t tokens, float *y,
                void *workspace, size_t workspace_bytes, void *stream) {
   NQB_CHECK(validate_layer(layer, "layer"));
   NQB_CHECK(validate_input(x, x_dtype, tokens));
   if (y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output y is NULL");
-  const size_t need = latent_bytes(tokens, latent_columns(layer->rank));
-  const size_t tc_need = path_extra_bytes(layer, 1, tokens);
-  if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
-    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
-                nqb::workspace_bytes(need, tc_need), workspace_bytes);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  char *base = static_cast<char *>(workspace);
-  int32_t *counters = reinterpret_cast<int32_t *>(base);
-  float *latent = reinterpret_cast<float *>(base + kCounterRegionBytes);
-  if (tc_eligible(layer, 1, x_dtype, tokens)) {
-    NQB_CHECK(run_tc(layer, 1, x, x_dtype, tokens, &y, counters, base + kCounterRegionBytes + need, tc_need, latent,
-                     s));
-    return ok();
-  }
   float *ys[1] = {y};
-  if (prefill_eligible(layer, 1, x_dtype, tokens)) {
-    NQB_CHECK(run_prefill(layer, 1, x, x_dtype, tokens, ys, latent, base + kCounterRegionBytes + need, tc_need, s));
-    return ok();
-  }
-  NQB_CHECK(run_generic(layer, 1, x, x_dtype, tokens, ys, latent, s));
+  NQB_CHECK(run_layers(layer, 1, x, x_dtype, tokens, ys, workspace, workspace_bytes, stream));
   return ok();
 }
 
@@ -292,12 +337,8 @@ int nqb_grouped_workspace_bytes(const nqb_linear_desc *layers, int32_t count, in
     return fail(NQB_ERR_INVALID_ARGUMENT, "grouped call takes 1 to %d layers", kMaxMembers);
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
   if (tokens <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "token count must be positive");
-  int64_t total_rank = 0;
-  for (int i = 0; i < count; ++i) {
-    NQB_CHECK(validate_layer(layers + i, "grouped member"));
-    total_rank += latent_columns(layers[i].rank);
-  }
-  *bytes = workspace_bytes(latent_bytes(tokens, total_rank), path_extra_bytes(layers, count, tokens));
+  for (int i = 0; i < count; ++i) NQB_CHECK(validate_layer(layers + i, "grouped member"));
+  *bytes = workspace_bytes(latent_region_bytes(layers, count, tokens), path_extra_bytes(layers, count, tokens));
   return ok();
 }
 
@@ -307,7 +348,6 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
   if (layers == nullptr || count < 1 || count > kMaxMembers)
     return fail(NQB_ERR_INVALID_ARGUMENT, "grouped call takes 1 to %d layers", kMaxMembers);
   if (y_out == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output list is NULL");
-  int64_t total_rank = 0;
   for (int i = 0; i < count; ++i) {
     NQB_CHECK(validate_layer(layers + i, "grouped member"));
     if (layers[i].in_features != layers[0].in_features)
@@ -315,29 +355,9 @@ int nqb_grouped_linear(const nqb_linear_desc *layers, int32_t count, const void 
     if (layers[i].scale_dtype != layers[0].scale_dtype)
       return fail(NQB_ERR_DTYPE, "grouped members must share the scale dtype");
     if (y_out[i] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "output %d is NULL", i);
-    total_rank += latent_columns(layers[i].rank);
   }
   NQB_CHECK(validate_input(x, x_dtype, tokens));
-  const size_t need = latent_bytes(tokens, total_rank);
-  const size_t tc_need = path_extra_bytes(layers, count, tokens);
-  if (workspace == nullptr || workspace_bytes < nqb::workspace_bytes(need, tc_need) || !aligned(workspace, 256))
-    return fail(NQB_ERR_WORKSPACE, "workspace needs %zu bytes aligned to 256, got %zu",
-                nqb::workspace_bytes(need, tc_need), workspace_bytes);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  char *base = static_cast<char *>(workspace);
-  int32_t *counters = reinterpret_cast<int32_t *>(base);
-  float *latent = reinterpret_cast<float *>(base + kCounterRegionBytes);
-  if (tc_eligible(layers, count, x_dtype, tokens)) {
-    NQB_CHECK(run_tc(layers, count, x, x_dtype, tokens, y_out, counters, base + kCounterRegionBytes + need, tc_need,
-                     latent, s));
-    return ok();
-  }
-  if (prefill_eligible(layers, count, x_dtype, tokens)) {
-    NQB_CHECK(run_prefill(layers, count, x, x_dtype, tokens, y_out, latent, base + kCounterRegionBytes + need, tc_need,
-                          s));
-    return ok();
-  }
-  NQB_CHECK(run_generic(layers, count, x, x_dtype, tokens, y_out, latent, s));
+  NQB_CHECK(run_layers(layers, count, x, x_dtype, tokens, y_out, workspace, workspace_bytes, stream));
   return ok();
 }
 

@@ -35,7 +35,10 @@
 // are deterministic.  Each stage writes per-K-split fp32 partials; the last
 // CTA of every row tile (atomic counter) reduces them in a fixed order:
 // stage 1 into the latent (times scale_mid), stage 2 into y (times
-// scale_post, plus salient columns, the int8 row overlay and bias).
+// scale_post, plus salient columns, the int8 row overlay, the low-rank patch
+// and bias).  A patched layer's patch latent R x is formed in stage 1 by the
+// member's CTAs (patch rows spread over them, while their MMAs run) and
+// stage 2's reducing CTA adds L times it per row.
 #include <cstring>
 
 #include "nqb_decode_tc.cuh"
@@ -77,6 +80,11 @@ struct Member {
   const void *overlay_scales;
   int32_t overlay_scale_dtype;
   float *y;
+  // low-rank patch: stage 1 reads R [p, n], stage 2 L [m, p]
+  int64_t patch_rank;
+  const void *patch_factor;
+  int32_t patch_dtype;
+  float *patch_latent;   // [tokens][patch_rank]: written by stage 1, read by stage 2
 };
 
 struct Params {
@@ -114,7 +122,46 @@ __device__ __forceinline__ void stage_activations(const Params &p, const Member 
   }
 }
 
-template <bool kStage2, int kT>
+// Patch latent rows q = first, first + step, ... of member m (whole CTA):
+// patch_latent[t][q] = sum_i x[t, i] R[q, i], fp32, fixed summation order.
+// (Plain arguments: a reference to the kernel's parameters would make the
+// kernel copy them to local memory.)
+template <int kT>
+__device__ __noinline__ void patch_latent_rows(const void *x, int32_t x_dtype, int64_t n, int T, int64_t rows,
+                                               const void *factor, int32_t dtype, float *out, int64_t first,
+                                               int64_t step, float *s_part) {
+  constexpr int kW = kThreads / 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int64_t q = first; q < rows; q += step) {
+    float part[kT];
+#pragma unroll
+    for (int t = 0; t < kT; ++t) part[t] = 0.0f;
+    for (int64_t i = tid; i < n; i += kThreads) {
+      const float r = load_as_float(factor, q * n + i, dtype);
+#pragma unroll
+      for (int t = 0; t < kT; ++t)
+        if (t < T) part[t] += load_as_float(x, static_cast<int64_t>(t) * n + i, x_dtype) * r;
+    }
+#pragma unroll
+    for (int t = 0; t < kT; ++t) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part[t] += __shfl_xor_sync(0xffffffffu, part[t], off);
+      if (lane == 0) s_part[warp * kT + t] = part[t];
+    }
+    __syncthreads();
+    if (tid < T) {
+      float v = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kW; ++w) v += s_part[w * kT + tid];
+      out[static_cast<int64_t>(tid) * rows + q] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// kPatch: some member has a low-rank patch; calls without one run an instance
+// with the patch steps compiled out.
+template <bool kStage2, int kT, bool kPatch>
 __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   constexpr int kNP = n_pad_for(kT);  // MMA N: 3 digit columns per token, multiple of 16
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -124,6 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
   __shared__ uint32_t s_tmem;
   __shared__ BImageScratch<kT> s_bi;
   __shared__ float s_red_f[4];
+  __shared__ float s_patch[(kThreads / 32) * kT];
   __shared__ int s_last;
 
   const int tid = threadIdx.x;
@@ -224,6 +272,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
     }
   }
   if (tid == 0) ptx::mma_commit(&s_bar_done);
+  if constexpr (!kStage2 && kPatch) {
+    // this CTA's share of the patch latent while the tensor cores finish
+    if (m.patch_rank > 0)
+      patch_latent_rows<kT>(p.x, p.x_dtype, p.n, T, m.patch_rank, m.patch_factor, m.patch_dtype, m.patch_latent, local,
+                            static_cast<int64_t>(m.row_tiles) * m.splits, s_patch);
+  }
   if (!ptx::mbar_wait_bounded(&s_bar_done, 0, kSpinLimit)) ok = false;
   ptx::tc_fence_after();
   if (!ok) record_error(NQB_ERR_TIMEOUT);
@@ -283,6 +337,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_stage_kernel(const Params p) {
             sal += load_as_float(p.x, static_cast<int64_t>(t) * p.n + m.outlier_indices[s], p.x_dtype) * w;
           }
           v += sal;
+        }
+        if constexpr (kPatch) {
+          if (m.patch_rank > 0) {
+            float pv = 0.0f;
+            for (int64_t q = 0; q < m.patch_rank; ++q)
+              pv += load_as_float(m.patch_factor, row * m.patch_rank + q, m.patch_dtype) *
+                    __ldcg(m.patch_latent + static_cast<int64_t>(t) * m.patch_rank + q);
+            v += pv;
+          }
         }
         m.y[static_cast<int64_t>(t) * m.rows + row] = v + bias;
       }
@@ -470,9 +533,9 @@ static int smem_bytes(int stages, int n_pad, int64_t tokens) {
          static_cast<int>(tokens) * stages * tc::kStageCols * static_cast<int>(sizeof(float));
 }
 
-template <bool kStage2, int kT>
+template <bool kStage2, int kT, bool kPatch>
 static int launch_stage_t(const tc::Params &params, int ctas, int smem, cudaStream_t stream) {
-  const void *fn = reinterpret_cast<const void *>(tc::tc_stage_kernel<kStage2, kT>);
+  const void *fn = reinterpret_cast<const void *>(tc::tc_stage_kernel<kStage2, kT, kPatch>);
   NQB_CHECK(ensure_dynamic_smem(fn, smem));
   cudaLaunchConfig_t config;
   std::memset(&config, 0, sizeof(config));
@@ -485,7 +548,7 @@ static int launch_stage_t(const tc::Params &params, int ctas, int smem, cudaStre
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attr;
   config.numAttrs = 1;
-  NQB_CUDA(cudaLaunchKernelEx(&config, tc::tc_stage_kernel<kStage2, kT>, params),
+  NQB_CUDA(cudaLaunchKernelEx(&config, tc::tc_stage_kernel<kStage2, kT, kPatch>, params),
            kStage2 ? "tc stage 2 launch" : "tc stage 1 launch");
   return NQB_OK;
 }
@@ -493,19 +556,25 @@ static int launch_stage_t(const tc::Params &params, int ctas, int smem, cudaStre
 // Token buckets: each kernel instance is compiled for at most kT tokens.
 static int token_bucket(int64_t tokens) { return tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : tokens <= 8 ? 8 : 16; }
 
-template <bool kStage2>
-static int launch_stage(const tc::Params &params, int ctas, int smem, cudaStream_t stream) {
+template <bool kStage2, bool kPatch>
+static int launch_stage_p(const tc::Params &params, int ctas, int smem, cudaStream_t stream) {
   switch (token_bucket(params.tokens)) {
-    case 1: return launch_stage_t<kStage2, 1>(params, ctas, smem, stream);
-    case 2: return launch_stage_t<kStage2, 2>(params, ctas, smem, stream);
-    case 4: return launch_stage_t<kStage2, 4>(params, ctas, smem, stream);
-    case 8: return launch_stage_t<kStage2, 8>(params, ctas, smem, stream);
-    default: return launch_stage_t<kStage2, 16>(params, ctas, smem, stream);
+    case 1: return launch_stage_t<kStage2, 1, kPatch>(params, ctas, smem, stream);
+    case 2: return launch_stage_t<kStage2, 2, kPatch>(params, ctas, smem, stream);
+    case 4: return launch_stage_t<kStage2, 4, kPatch>(params, ctas, smem, stream);
+    case 8: return launch_stage_t<kStage2, 8, kPatch>(params, ctas, smem, stream);
+    default: return launch_stage_t<kStage2, 16, kPatch>(params, ctas, smem, stream);
   }
 }
 
+template <bool kStage2>
+static int launch_stage(const tc::Params &params, int ctas, int smem, bool patch, cudaStream_t stream) {
+  return patch ? launch_stage_p<kStage2, true>(params, ctas, smem, stream)
+               : launch_stage_p<kStage2, false>(params, ctas, smem, stream);
+}
+
 int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
-           float *const *ys, int32_t *counters, void *extra, size_t extra_bytes, float *latent,
+           float *const *ys, int32_t *counters, void *extra, size_t extra_bytes, float *latent, float *patch,
            cudaStream_t stream) {
   const Layout l = tc_layout(layers, count, tokens);
   if (extra_bytes < l.partial1 + l.partial2) return fail(NQB_ERR_WORKSPACE, "tensor-core path workspace too small");
@@ -520,7 +589,7 @@ int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dt
   tc::Params p2;
   std::memset(&p2, 0, sizeof(p2));
   int32_t cta1 = 0, cta2 = 0, max_sps2 = 1;
-  int64_t rank_offset = 0, out_offset = 0, counter_offset = 0;
+  int64_t rank_offset = 0, out_offset = 0, counter_offset = 0, patch_offset = 0;
   for (int i = 0; i < count; ++i) {
     const nqb_linear_desc &d = layers[i];
     tc::Member &a = p1.m[i];
@@ -567,6 +636,15 @@ int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dt
     b.overlay_scales = d.overlay_scales;
     b.overlay_scale_dtype = d.overlay_scale_dtype;
     b.y = ys[i];
+    if (d.patch_rank > 0) {
+      float *pl = patch + tokens * patch_offset;
+      a.patch_rank = b.patch_rank = d.patch_rank;
+      a.patch_dtype = b.patch_dtype = d.patch_dtype;
+      a.patch_factor = d.patch_right;
+      b.patch_factor = d.patch_left;
+      a.patch_latent = b.patch_latent = pl;
+      patch_offset += d.patch_rank;
+    }
     cta2 += l.rt2[i] * b.splits;
     counter_offset += l.rt2[i];
     if (b.stages_per_split > max_sps2) max_sps2 = b.stages_per_split;
@@ -590,8 +668,9 @@ int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dt
   p2.partial = partial2;
   p2.part_stride = l.total_out;
 
-  NQB_CHECK(launch_stage<false>(p1, cta1, smem_bytes(l.s1.sps[0], n_pad, tokens), stream));
-  NQB_CHECK(launch_stage<true>(p2, cta2, smem_bytes(max_sps2, n_pad, tokens), stream));
+  const bool patched = patch_offset > 0;
+  NQB_CHECK(launch_stage<false>(p1, cta1, smem_bytes(l.s1.sps[0], n_pad, tokens), patched, stream));
+  NQB_CHECK(launch_stage<true>(p2, cta2, smem_bytes(max_sps2, n_pad, tokens), patched, stream));
   return NQB_OK;
 }
 

@@ -18,7 +18,7 @@ size_t tc_extra_workspace_bytes(const nqb_linear_desc *layers, int count, int64_
 // Runs 1..3 layers sharing x through the tcgen05 kernels.
 // `counters` is the zero-on-entry counter region; `extra` holds the partials.
 int run_tc(const nqb_linear_desc *layers, int count, const void *x, int32_t x_dtype, int64_t tokens,
-           float *const *ys, int32_t *counters, void *extra, size_t extra_bytes, float *latent,
+           float *const *ys, int32_t *counters, void *extra, size_t extra_bytes, float *latent, float *patch,
            cudaStream_t stream);
 
 // Row-interleaved tile copy of a sign matrix (see nqb_repack_signs).

@@ -12,7 +12,10 @@
 //   sums meet in distributed shared memory: CTA q writes its quarter into the
 //   tile's leader CTA (tile index mod 4), which adds the four in a fixed order
 //   and runs the epilogue (scale_mid -> latent; scale_post, salient columns,
-//   bias, int8 overlay rows -> y).  No global atomics, deterministic.
+//   low-rank patch, bias, int8 overlay rows -> y).  No global atomics,
+//   deterministic.  A patched layer's patch latent R x is formed in stage 1
+//   (its rows spread over all CTAs, after their tiles) in latent columns
+//   after the op's ranks.
 // * Arithmetic.  Exact integer MMAs with register operands
 //   (nqb_mma_decode.cuh): activations quantised per (token, K chunk) to 22-bit
 //   fixed-point digits (B fragments in shared memory), sign bits expanded by
@@ -77,6 +80,10 @@ struct MemberDev {
   const void *overlay_scales;
   int32_t overlay_scale_dtype;
   float *y;
+  int64_t patch_rank;         // low-rank patch: stage 1 reads R [p, n], stage 2 L [m, p]
+  const void *patch_factor;
+  int32_t patch_dtype;
+  int64_t patch_offset;       // first latent column of the member's patch latent
 };
 
 struct OpDev {
@@ -85,6 +92,7 @@ struct OpDev {
   const void *x;
   const void *x2;  // NQB_X_SWIGLU: the up projection (x is the gate)
   int32_t x_dtype;
+  int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
   int64_t n;
   int64_t latent_stride;
 };
@@ -106,6 +114,7 @@ struct __align__(16) StageInfo {
   int64_t latent_stride;
   int32_t x_dtype;
   int32_t n_items;
+  int32_t patch_rows;
   Item items[kMaxStageItems];
 };
 
@@ -349,6 +358,7 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
     info.latent_stride = op.latent_stride;
     info.x_dtype = op.x_dtype;
     info.n_items = n_items;
+    info.patch_rows = op.patch_rows;
   }
 }
 
@@ -373,6 +383,46 @@ __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index) {
     }
   }
   mmad::consumer_sync();
+}
+
+// Stage 1's patch latents, formed by the info warp of every CTA while the
+// consumer warps run the stage's tiles: the op's patched members' patch rows,
+// numbered across members, go to CTAs round-robin; row q of member k is
+// latent[t][patch_offset_k + q] = sum_i x[t, i] R_k[q, i] (fp32, fixed order).
+// Inputs are read through L2: an earlier op of the program may have written them.
+__device__ __forceinline__ void patch_rows_warp(const Params &p, const OpDev &op, int cta, int ctas, int lane) {
+  const int T = p.tokens;
+  int64_t base = 0;  // patch rows of earlier members
+  for (int k = 0; k < op.count; ++k) {
+    const MemberDev &md = op.s[0][k];
+    if (md.patch_rank <= 0) continue;
+    for (int64_t q = ((cta - base) % ctas + ctas) % ctas; q < md.patch_rank; q += ctas) {
+      for (int t0 = 0; t0 < T; t0 += 4) {  // four tokens at a time: few registers beside the consumers'
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int64_t i = lane; i < op.n; i += 32) {
+          const float r = load_as_float(md.patch_factor, q * op.n + i, md.patch_dtype);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (t0 + u >= T) break;
+            const int64_t xi = static_cast<int64_t>(t0 + u) * op.n + i;
+            float xv;
+            if (op.x_dtype == NQB_F32) xv = __ldcg(static_cast<const float *>(op.x) + xi);
+            else if (op.x_dtype == NQB_BF16) xv = __bfloat162float(__ldcg(static_cast<const __nv_bfloat16 *>(op.x) + xi));
+            else xv = __half2float(__ldcg(static_cast<const __half *>(op.x) + xi));
+            part[u] += xv * r;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) part[u] += __shfl_xor_sync(0xffffffffu, part[u], off);
+          if (lane == 0 && t0 + u < T)
+            p.latent[static_cast<int64_t>(t0 + u) * op.latent_stride + md.patch_offset + q] = part[u];
+        }
+      }
+    }
+    base += md.patch_rank;
+  }
 }
 
 // The producer lane's view of this CTA's slice-address list.
@@ -444,7 +494,10 @@ __device__ __forceinline__ bool next_unit(const StageInfo &op, int ge, int rank,
   return true;
 }
 
-template <int kT>
+// kPatch: some op has a patched member.  Programs without one run an
+// instance with every patch step compiled out (those steps cost time in the
+// stage loop even when never taken).
+template <int kT, bool kPatch>
 __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_constant__ Params p) {
   constexpr int kNT = mmad::n_tiles(kT);
   constexpr int kSets = mmad::acc_sets(kNT);
@@ -461,6 +514,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   __shared__ StageInfo s_info[2];
   __shared__ mmad::Scratch<kT> s_sc;
   __shared__ float s_red_f[mmad::kWarps];
+  __shared__ uint64_t s_patch_done;  // the info warp formed this CTA's patch rows of the current stage 1
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -487,6 +541,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     ptx::mbar_init(&s_x_free, kClusterSize);
     ptx::mbar_init(&s_info_full[0], 1);
     ptx::mbar_init(&s_info_full[1], 1);
+    ptx::mbar_init(&s_patch_done, 1);
     ptx::fence_mbar_init();
   }
   cluster_sync();  // every CTA's barriers exist before any remote arrive
@@ -521,7 +576,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   } else if (warp == kInfoWarp) {
     // ---- stage g's tables into s_info[g % 2] and an L2 prefetch of its
     // scales and inputs, once stage g - 1 has started (so stage g - 2, the
-    // buffer's previous user, is finished everywhere)
+    // buffer's previous user, is finished everywhere); then, when stage g - 1
+    // is a stage 1 with patched members, this CTA's share of their patch
+    // latents (stage g - 1's inputs are complete once stage g - 2 is)
     for (int g = 0; g < p.stages; ++g) {
       if (g >= 2) {
         if (lane == 0 && !wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x)) ok = false;
@@ -530,6 +587,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
       __syncwarp();
       if (lane == 0) mbar_arrive_cta(&s_info_full[g & 1]);
+      if constexpr (kPatch) {
+        if ((g & 1) == 1 && s_info[(g - 1) & 1].patch_rows > 0) {  // stage g - 1's tables, staged last pass
+          patch_rows_warp(p, p.ops[g >> 1], cta, static_cast<int>(gridDim.x), lane);
+          __threadfence();  // the rows are visible GPU-wide before the consumers' barrier release
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cta(&s_patch_done);
+        }
+      }
       prefetch_stage(p, g, lane);
     }
   } else {
@@ -537,6 +602,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     int slot = 0;         // ring slot of the next slice
     uint32_t phase = 0;   // ring passes completed
     uint32_t xg = 0;      // exchange groups done
+    uint32_t patched = 0;  // patched stage 1s done
     for (int g = 0; g < p.stages; ++g) {
       const int st = g & 1;
       if (!wait_local(&s_info_full[g & 1], (g >> 1) & 1)) ok = false;
@@ -781,6 +847,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                     }
                     v += sal;
                   }
+                  if constexpr (kPatch) {
+                    if (md.patch_rank > 0) {
+                      const float *pl = p.latent + static_cast<int64_t>(t) * op.latent_stride + md.patch_offset;
+                      float pv = 0.0f;
+                      for (int64_t q = 0; q < md.patch_rank; ++q)
+                        pv += load_as_float(md.patch_factor, row * md.patch_rank + q, md.patch_dtype) * __ldcg(pl + q);
+                      v += pv;
+                    }
+                  }
                   md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
                 }
               }
@@ -821,6 +896,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         }
       }
       NQB_TRACE(kTraceEpilogue);
+      if constexpr (kPatch) {
+        if (st == 0 && op.patch_rows > 0) {
+          // this CTA's patch rows (info warp) are written before its barrier arrival
+          if (tid == 0 && !wait_local(&s_patch_done, patched & 1)) ok = false;
+          ++patched;
+        }
+      }
       if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g));
       NQB_TRACE(kTraceGridBarrier);
       NQB_TRACE_FLUSH(g);
@@ -860,6 +942,7 @@ struct nqb_program {
   float *scales = nullptr;  // fp32 copies of every pre / mid / post / bias vector
   int64_t tokens = 0;
   int bucket = 1;
+  bool patch = false;  // runs the patch-capable kernel instance
   int ctas = 0;
   int clusters = 0;
   int smem = 0;
@@ -904,14 +987,19 @@ static SmemPlan smem_plan(int bucket) {
   return s;
 }
 
-static const void *kernel_for(int bucket) {
+template <bool kPatch>
+static const void *kernel_for_t(int bucket) {
   switch (bucket) {
-    case 1: return reinterpret_cast<const void *>(program_kernel<1>);
-    case 2: return reinterpret_cast<const void *>(program_kernel<2>);
-    case 4: return reinterpret_cast<const void *>(program_kernel<4>);
-    case 8: return reinterpret_cast<const void *>(program_kernel<8>);
-    default: return reinterpret_cast<const void *>(program_kernel<16>);
+    case 1: return reinterpret_cast<const void *>(program_kernel<1, kPatch>);
+    case 2: return reinterpret_cast<const void *>(program_kernel<2, kPatch>);
+    case 4: return reinterpret_cast<const void *>(program_kernel<4, kPatch>);
+    case 8: return reinterpret_cast<const void *>(program_kernel<8, kPatch>);
+    default: return reinterpret_cast<const void *>(program_kernel<16, kPatch>);
   }
+}
+
+static const void *kernel_for(int bucket, bool patch) {
+  return patch ? kernel_for_t<true>(bucket) : kernel_for_t<false>(bucket);
 }
 
 // `pre`, `row_scale` and `bias` are the program's fp32 copies of the layer's vectors.
@@ -926,6 +1014,7 @@ static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64
     m.k_valid = d.in_features;
     m.pre = pre;
     m.out_offset = rank_offset;
+    m.patch_factor = d.patch_right;
   } else {
     m.tiles = static_cast<const uint8_t *>(d.left_tiles);
     m.rows = d.out_features;
@@ -945,7 +1034,10 @@ static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64
     m.overlay_scales = d.overlay_scales;
     m.overlay_scale_dtype = d.overlay_scale_dtype;
     m.y = y;
+    m.patch_factor = d.patch_left;
   }
+  m.patch_rank = d.patch_rank;
+  m.patch_dtype = d.patch_dtype;
   m.ks = m.wc / 2;
 }
 
@@ -1009,11 +1101,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     if (swiglu && o.x2 == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a SwiGLU input needs x2", i);
     if (swiglu)
       for (int k = 0; k < o.count; ++k)
-        if (o.layers[k].outlier_count > 0 || o.layers[k].overlay_rows > 0)
-          return fail(NQB_ERR_UNSUPPORTED, "op %d: SwiGLU inputs take no salient columns or overlay rows", i);
+        if (o.layers[k].outlier_count > 0 || o.layers[k].overlay_rows > 0 || o.layers[k].patch_rank > 0)
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: SwiGLU inputs take no salient columns, overlay rows or patch", i);
     int64_t rank_total = 0;
     for (int k = 0; k < o.count; ++k) {
       const nqb_linear_desc &d = o.layers[k];
+      if (d.patch_rank < 0 || d.patch_rank > (1ll << 20) ||
+          (d.patch_rank > 0 && (d.patch_left == nullptr || d.patch_right == nullptr || !is_float_dtype(d.patch_dtype))))
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has an invalid low-rank patch", i, k);
       if (d.in_features != o.layers[0].in_features || d.scale_dtype != o.layers[0].scale_dtype)
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: members must share in_features and scale dtype", i);
       if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
@@ -1021,7 +1116,9 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     }
     if (!tc_eligible(o.layers, o.count, swiglu ? NQB_F32 : o.x_dtype, tokens))
       return fail(NQB_ERR_UNSUPPORTED, "op %d does not take the tensor-core decode path", i);
-    latent_cols = std::max(latent_cols, rank_total);
+    int64_t patch_total = 0;
+    for (int k = 0; k < o.count; ++k) patch_total += o.layers[k].patch_rank;
+    latent_cols = std::max(latent_cols, rank_total + patch_total);
   }
 
   // fp32 copies of the scale and bias vectors, so the kernel reads them with
@@ -1086,13 +1183,20 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       fill_member(od.s[1][k], o.layers[k], 1, offset, o.y[k], nullptr, f32(ms.post), f32(ms.bias));
       offset += o.layers[k].rank;
     }
+    for (int k = 0; k < o.count; ++k) {  // patch latents after the ranks
+      od.s[0][k].patch_offset = od.s[1][k].patch_offset = offset;
+      offset += o.layers[k].patch_rank;
+      od.patch_rows += static_cast<int32_t>(o.layers[k].patch_rank);
+    }
     od.latent_stride = offset;
   }
 
   int device = 0;
   NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
   const SmemPlan sp = smem_plan(bucket);
-  const void *fn = kernel_for(bucket);
+  bool patch = false;
+  for (int i = 0; i < op_count; ++i) patch = patch || opdev[i].patch_rows > 0;
+  const void *fn = kernel_for(bucket, patch);
   NQB_CHECK(ensure_dynamic_smem(fn, static_cast<int>(sp.total)));
   int sms = 0;
   NQB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
@@ -1286,6 +1390,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   prog->device = device;
   prog->tokens = tokens;
   prog->bucket = bucket;
+  prog->patch = patch;
   prog->ctas = ctas;
   prog->clusters = clusters;
   prog->smem = static_cast<int>(sp.total);
@@ -1309,7 +1414,7 @@ int nqb_program_run(const nqb_program *program, void *workspace, size_t workspac
   Params params = program->params;
   params.counters = static_cast<uint32_t *>(workspace);
   params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
-  const void *fn = kernel_for(program->bucket);
+  const void *fn = kernel_for(program->bucket, program->patch);
   NQB_CHECK(ensure_dynamic_smem(fn, program->smem));
   cudaLaunchConfig_t config;
   std::memset(&config, 0, sizeof(config));

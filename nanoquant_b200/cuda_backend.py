@@ -158,6 +158,12 @@ def _build_payload(
         desc.overlay_values = keep("overlay_values", overlay.values).data_ptr()
         desc.overlay_scales = keep("overlay_scales", overlay.scales).data_ptr()
         desc.overlay_scale_dtype = _native.dtype_code(overlay.scales.dtype)
+    if patch_left is not None and patch_right is not None:
+        # the library applies the patch inside nqb_linear (fused into the decode stages)
+        desc.patch_rank = int(patch_left.shape[1])
+        desc.patch_left = patch_left.data_ptr()
+        desc.patch_right = patch_right.data_ptr()
+        desc.patch_dtype = _native.dtype_code(patch_left.dtype)
     return _Sm100Payload(device, tensors, desc, patch_left, patch_right)
 
 
@@ -243,25 +249,6 @@ def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLi
         workspace.numel(),
         stream,
     )
-    if payload.patch_left is not None and payload.patch_right is not None:
-        patch_rank = payload.patch_left.shape[1]
-        patch_space = _workspace(tokens * patch_rank * 4, value.device)
-        _native.call(
-            "nqb_patch_accumulate",
-            value.data_ptr(),
-            _native.dtype_code(value.dtype),
-            tokens,
-            spec.in_features,
-            spec.out_features,
-            patch_rank,
-            payload.patch_left.data_ptr(),
-            payload.patch_right.data_ptr(),
-            _native.dtype_code(payload.patch_left.dtype),
-            output.data_ptr(),
-            patch_space.data_ptr(),
-            patch_space.numel(),
-            stream,
-        )
     return output
 
 
@@ -351,7 +338,8 @@ def prepare_sm100_projection_group(layers: tuple[PreparedLayer, ...]) -> Sm100Pr
 
     Returns ``None`` when the layers cannot share one call, as the reference does.
     Unlike the reference, ranks and widths need no 8-alignment and bias,
-    int8 outlier scales and overlays are allowed; a low-rank patch is not.
+    int8 outlier scales, overlays and a low-rank patch are allowed (the
+    library applies each member's patch inside the grouped call).
     """
 
     if len(layers) not in (2, 3):
@@ -366,8 +354,6 @@ def prepare_sm100_projection_group(layers: tuple[PreparedLayer, ...]) -> Sm100Pr
     if any(layer.spec.in_features != in_features for layer in layers):
         return None
     if any(payload.desc.scale_dtype != first.desc.scale_dtype for payload in payloads):
-        return None
-    if any(payload.patch_left is not None for payload in payloads):
         return None
     descs = (_native.LinearDesc * len(layers))(*(payload.desc for payload in payloads))
     return Sm100ProjectionGroup(

@@ -60,9 +60,6 @@ class DecodeProgram:
             payloads = tuple(layer.payload for layer in op.layers)
             if not all(isinstance(payload, _Sm100Payload) for payload in payloads):
                 raise TypeError("program ops need layers prepared by CudaPackedSm100Backend")
-            if any(payload.patch_left is not None for payload in payloads):
-                # the C descriptors carry no patch factors: the program would drop them
-                raise ValueError("program ops do not take layers with a low-rank patch")
             if op.x.device != device:
                 raise ValueError("all program tensors must be on one device")
             spec = op.layers[0].spec

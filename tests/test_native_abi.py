@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol() -> None:
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.nqb_abi_version() == 1
+    assert lib.nqb_abi_version() == 2
 
 
 def _desc() -> _native.LinearDesc:
@@ -56,6 +56,47 @@ def test_workspace_size_is_reported_without_a_device() -> None:
     assert size.value >= 8 * 16 * 4 and size.value % 256 == 0
 
 
+def test_workspace_holds_the_patch_latent() -> None:
+    plain, patched = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    desc = _desc()
+    assert _status("nqb_linear_workspace_bytes", ctypes.byref(desc), 8, ctypes.byref(plain))[0] == _native.NQB_OK
+    desc.patch_rank, desc.patch_left, desc.patch_right, desc.patch_dtype = 24, 0x80000, 0x90000, _native.NQB_BF16
+    assert _status("nqb_linear_workspace_bytes", ctypes.byref(desc), 8, ctypes.byref(patched))[0] == _native.NQB_OK
+    assert patched.value - plain.value == 768  # 8 tokens x 24 fp32, rounded to 256 bytes
+
+
+def test_ctypes_structs_match_the_header(tmp_path) -> None:
+    """Every field of the ctypes mirrors sits at the C compiler's offset for ``include/nqb.h``."""
+
+    import shutil
+    import subprocess
+
+    compiler = shutil.which("gcc") or shutil.which("cc")
+    if compiler is None:
+        pytest.skip("no C compiler")
+    structs = {"nqb_linear_desc": _native.LinearDesc, "nqb_program_op": _native.ProgramOp}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "nqb.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["  return 0;", "}"]
+    source = tmp_path / "layout.c"
+    source.write_text("\n".join(lines) + "\n")
+    include = Path(__file__).resolve().parents[1] / "include"
+    exe = tmp_path / "layout"
+    subprocess.run([compiler, "-std=c11", f"-I{include}", str(source), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    seen = {}
+    for line in filter(None, out):
+        cname, field, value = line.split()
+        seen[(cname, field)] = int(value)
+    for cname, cls in structs.items():
+        assert seen[(cname, "sizeof")] == ctypes.sizeof(cls), cname
+        for field, _ in cls._fields_:
+            assert seen[(cname, field)] == getattr(cls, field).offset, (cname, field)
+
+
 @pytest.mark.parametrize(
     ("mutate", "code", "message"),
     [
@@ -70,6 +111,10 @@ def test_workspace_size_is_reported_without_a_device() -> None:
         (lambda d: setattr(d, "outlier_count", 65), _native.NQB_ERR_INVALID_ARGUMENT, "outlier count"),
         (lambda d: (setattr(d, "codebook_payload", 0x40000)), _native.NQB_ERR_INVALID_ARGUMENT, "not both"),
         (lambda d: setattr(d, "overlay_rows", 33), _native.NQB_ERR_INVALID_ARGUMENT, "overlay row count"),
+        (lambda d: setattr(d, "patch_rank", -1), _native.NQB_ERR_INVALID_ARGUMENT, "patch rank"),
+        (lambda d: setattr(d, "patch_rank", 4), _native.NQB_ERR_INVALID_ARGUMENT, "patch factors are NULL"),
+        (lambda d: (setattr(d, "patch_rank", 4), setattr(d, "patch_left", 0x80000), setattr(d, "patch_right", 0x80000),
+                    setattr(d, "patch_dtype", _native.NQB_I8)), _native.NQB_ERR_DTYPE, "patch dtype"),
     ],
 )
 def test_descriptor_validation(mutate, code: int, message: str) -> None:

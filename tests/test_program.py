@@ -137,18 +137,6 @@ def test_program_rejects_prefill_token_counts() -> None:
     assert info.value.status == _native.NQB_ERR_UNSUPPORTED
 
 
-def test_program_rejects_layers_with_a_patch() -> None:
-    from tests.fixtures import load
-    from tests.test_cuda_parity import state_from_case
-
-    state = state_from_case(load("linear_fixture_patch"))
-    assert state.patch_left is not None
-    layer = CudaPackedSm100Backend().prepare(state, "cuda")
-    x = torch.zeros(1, state.spec.in_features, dtype=torch.bfloat16, device="cuda")
-    with pytest.raises(ValueError, match="patch"):
-        DecodeProgram([ProgramOp((layer,), x)])
-
-
 @pytest.mark.parametrize("tokens", (1, 4, 16))
 def test_program_swiglu_input_matches_oracle(tokens: int) -> None:
     """gate/up then down in one program: the down op forms silu(gate) * up as it loads its input."""
