@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NQB_ABI_VERSION 2
+#define NQB_ABI_VERSION 3
 
 /* status codes */
 #define NQB_OK 0
@@ -118,7 +118,32 @@ typedef struct nqb_linear_desc {
   const void *patch_left;  /* [m, p] in patch_dtype */
   const void *patch_right; /* [p, n] in patch_dtype */
   int32_t patch_dtype;     /* F32 / F16 / BF16 */
+
+  /* Mixed-V right factor kept coded for decode programs (optional; NULL
+   * coded_right_tiles = none).  Programs stream the coded tiles of V and
+   * decode the 19-bit records in stage 1; the 128-row tiles below
+   * ceil(coded_free_rows / 128) * 128 still come from right_tiles, which the
+   * per-call paths keep using for every row.                                 */
+  const void *coded_right_tiles;  /* nqb_repack_mixed_v(payload, r, n, coded_free_rows) */
+  const int32_t *coded_codebook;  /* [1024] full sign words, 16-byte aligned       */
+  int64_t coded_free_rows;        /* the layer's plain (free) rows                 */
 } nqb_linear_desc;
+
+/*
+ * Coded tiles of a mixed-V right factor (mixed-v-free-k10-pair9-v1: rows
+ * below free_rows plain, every later word one 19-bit record, packed back to
+ * back from bit 0 of `payload`).  The tiles of 128 rows from
+ * ceil(free_rows / 128) on keep one record per word, widened to 20 bits with
+ * the pair id resolved (codebook index | a << 10 | b << 15, a < b the two
+ * flipped bits): per tile and per 256-column slice, row r's 8 records (words
+ * 8s .. 8s+7, zero past the row) sit back to back from bit 160 r, so one
+ * tile slice is 2560 bytes against 4096 for sign words.  No counterpart in the reference, whose backend expands the
+ * records before its kernels run (cuda_backend.py:209-224); this layout feeds
+ * the decode programs' stage-1 record decode.
+ */
+int nqb_mixed_v_tiles_bytes(int64_t rank, int64_t in_features, int64_t free_rows, size_t *bytes);
+int nqb_repack_mixed_v(const int32_t *payload, int64_t rank, int64_t in_features, int64_t free_rows,
+                       void *out, void *stream);
 
 /* Library identity: NQB_ABI_VERSION of the loaded build. */
 int nqb_abi_version(void);

@@ -85,6 +85,9 @@ class LinearDesc(ctypes.Structure):
         ("patch_left", _c_void_p),
         ("patch_right", _c_void_p),
         ("patch_dtype", ctypes.c_int32),
+        ("coded_right_tiles", _c_void_p),
+        ("coded_codebook", _c_void_p),
+        ("coded_free_rows", ctypes.c_int64),
     ]
 
 
@@ -154,6 +157,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
     ),
     "nqb_decode_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "nqb_mixed_v_tiles_bytes": (ctypes.c_int, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_repack_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p]),
     "nqb_rmsnorm": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64, ctypes.c_float, _c_void_p, _i32,
                                    _c_void_p]),
     "nqb_qk_norm_rope": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p,

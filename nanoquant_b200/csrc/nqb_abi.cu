@@ -115,6 +115,14 @@ static int validate_layer(const nqb_linear_desc *d, const char *name) {
     if (!is_float_dtype(d->overlay_scale_dtype))
       return fail(NQB_ERR_DTYPE, "%s: overlay scale dtype %d is not F32/F16/BF16", name, d->overlay_scale_dtype);
   }
+  if (d->coded_right_tiles != nullptr) {
+    if (d->coded_codebook == nullptr || d->right_tiles == nullptr)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "%s: coded tiles need the codebook and the plain right tiles", name);
+    if (d->coded_free_rows <= 0 || d->coded_free_rows >= d->rank)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "%s: coded free rows must be between zero and rank", name);
+    if (!aligned(d->coded_right_tiles, 16) || !aligned(d->coded_codebook, 16))
+      return fail(NQB_ERR_ALIGNMENT, "%s: coded tiles and codebook must be 16-byte aligned", name);
+  }
   if (d->patch_rank < 0 || d->patch_rank > (1ll << 20))
     return fail(NQB_ERR_INVALID_ARGUMENT, "%s: patch rank must be between 0 and 2^20", name);
   if (d->patch_rank > 0) {
@@ -460,6 +468,25 @@ int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t ran
                                   reinterpret_cast<const uint32_t *>(payload),
                                   reinterpret_cast<const uint32_t *>(codebook),
                                   reinterpret_cast<uint32_t *>(words_out), reinterpret_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int nqb_mixed_v_tiles_bytes(int64_t rank, int64_t in_features, int64_t free_rows, size_t *bytes) {
+  if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (free_rows <= 0 || free_rows >= rank || in_features <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "mixed-V free rows must be between zero and rank");
+  *bytes = mixed_v_tiles_bytes(rank, in_features, free_rows);
+  return ok();
+}
+
+int nqb_repack_mixed_v(const int32_t *payload, int64_t rank, int64_t in_features, int64_t free_rows, void *out,
+                       void *stream) {
+  if (payload == nullptr || out == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "mixed-V operand is NULL");
+  if (free_rows <= 0 || free_rows >= rank || in_features <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "mixed-V free rows must be between zero and rank");
+  if (!aligned(out, 16)) return fail(NQB_ERR_ALIGNMENT, "coded tiles must be 16-byte aligned");
+  NQB_CHECK(launch_repack_mixed_v(reinterpret_cast<const uint32_t *>(payload), rank, in_features, free_rows,
+                                  static_cast<uint8_t *>(out), reinterpret_cast<cudaStream_t>(stream)));
   return ok();
 }
 

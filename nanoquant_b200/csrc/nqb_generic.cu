@@ -282,6 +282,48 @@ __global__ void decode_mixed_v_kernel(const uint32_t *free_words, int64_t free_r
   out[i] = codebook[record & 1023u] ^ pair_mask(record >> 10);
 }
 
+// Coded tiles of a mixed-V right factor (nqb_repack_mixed_v): one thread per
+// (coded tile, slice, row) writes the row's 20-byte block of 8 tile records
+// (index | a << 10 | b << 15: the pair id resolved, so the decode needs no
+// pair table).
+__global__ void repack_mixed_v_kernel(const uint32_t *payload, int64_t rank, int64_t wpr, int64_t free_rows,
+                                      int64_t first_tile, int64_t coded_tiles, int32_t slices, uint8_t *out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= coded_tiles * slices * kMixedTileRows) return;
+  const int64_t row_in_tile = i % kMixedTileRows;
+  const int64_t ts = i / kMixedTileRows;  // coded tile * slices + slice
+  const int64_t slice = ts % slices;
+  const int64_t row = (first_tile + ts / slices) * kMixedTileRows + row_in_tile;
+  uint8_t *dst = out + ts * kMixedSliceBytes + row_in_tile * (8 * kMixedTileRecordBits / 8);
+  uint64_t acc = 0;
+  int bits = 0;
+  for (int j = 0; j < 8; ++j) {
+    const int64_t w = slice * 8 + j;
+    uint32_t tile_record = 0;
+    if (row < rank && w < wpr) {
+      const int64_t bit = ((row - free_rows) * wpr + w) * kMixedRecordBits;
+      const uint32_t shift = static_cast<uint32_t>(bit & 31);
+      uint32_t record = payload[bit >> 5] >> shift;
+      if (shift > 32 - kMixedRecordBits) record |= payload[(bit >> 5) + 1] << (32 - shift);
+      record &= (1u << kMixedRecordBits) - 1;
+      uint32_t id = record >> 10, a = 0;
+      while (a < 30 && id >= 31 - a) {  // pair id -> (a, b), as pair_mask
+        id -= 31 - a;
+        ++a;
+      }
+      const uint32_t b = (a + 1 + id) & 31u;
+      tile_record = (record & 1023u) | (a << 10) | (b << 15);
+    }
+    acc |= static_cast<uint64_t>(tile_record) << bits;
+    bits += kMixedTileRecordBits;
+    while (bits >= 8) {
+      *dst++ = static_cast<uint8_t>(acc & 0xFFu);
+      acc >>= 8;
+      bits -= 8;
+    }
+  }
+}
+
 // --------------------------------------------------------------- launch ---
 
 static int set_smem(const void *fn, size_t bytes) { return ensure_dynamic_smem(fn, bytes); }
@@ -353,6 +395,28 @@ int launch_decode_mixed_v(const uint32_t *free_words, int64_t free_rows, int64_t
   decode_mixed_v_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
       free_words, free_rows, rank, (cols + 31) / 32, payload, codebook, out);
   NQB_CUDA(cudaGetLastError(), "decode_mixed_v_kernel launch");
+  return NQB_OK;
+}
+
+int64_t mixed_v_first_coded_tile(int64_t free_rows) { return (free_rows + kMixedTileRows - 1) / kMixedTileRows; }
+
+size_t mixed_v_tiles_bytes(int64_t rank, int64_t columns, int64_t free_rows) {
+  const int64_t tiles = (rank + kMixedTileRows - 1) / kMixedTileRows - mixed_v_first_coded_tile(free_rows);
+  const int64_t slices = (words_for(columns) + 7) / 8;
+  return tiles > 0 ? static_cast<size_t>(tiles * slices) * kMixedSliceBytes : 0;
+}
+
+int launch_repack_mixed_v(const uint32_t *payload, int64_t rank, int64_t columns, int64_t free_rows, uint8_t *out,
+                          cudaStream_t stream) {
+  const int64_t first = mixed_v_first_coded_tile(free_rows);
+  const int64_t tiles = (rank + kMixedTileRows - 1) / kMixedTileRows - first;
+  if (tiles <= 0) return NQB_OK;
+  const int64_t wpr = words_for(columns);
+  const int32_t slices = static_cast<int32_t>((wpr + 7) / 8);
+  const int64_t items = tiles * slices * kMixedTileRows;
+  repack_mixed_v_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
+      payload, rank, wpr, free_rows, first, tiles, slices, out);
+  NQB_CUDA(cudaGetLastError(), "repack_mixed_v_kernel launch");
   return NQB_OK;
 }
 

@@ -85,6 +85,16 @@ int launch_pack(const void *signs, int32_t dt, int64_t rows, int64_t cols, uint3
 int launch_unpack(const uint32_t *words, int64_t rows, int64_t cols, float *signs, int32_t *bad_rows,
                   cudaStream_t stream);
 constexpr int kMixedRecordBits = 19;  // 10-bit codebook index + 9-bit pair id
+// Coded mixed-V tiles (nqb_repack_mixed_v): 128-row tiles, per 256-column
+// slice 8 tile records per row, each 20 bits (codebook index, then the two
+// flipped bit positions a and b, 5 bits each), row r's from bit 160 r.
+constexpr int kMixedTileRows = 128;
+constexpr int kMixedTileRecordBits = 20;
+constexpr int kMixedSliceBytes = kMixedTileRows * 8 * kMixedTileRecordBits / 8;  // 2560
+int64_t mixed_v_first_coded_tile(int64_t free_rows);
+size_t mixed_v_tiles_bytes(int64_t rank, int64_t columns, int64_t free_rows);
+int launch_repack_mixed_v(const uint32_t *payload, int64_t rank, int64_t columns, int64_t free_rows, uint8_t *out,
+                          cudaStream_t stream);
 int launch_decode_mixed_v(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,
                           const uint32_t *payload, const uint32_t *codebook, uint32_t *out, cudaStream_t stream);
 int launch_decode_codebook(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,

@@ -56,6 +56,12 @@ constexpr int kAddrSlots = 4;           // address chunks in flight
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr uint32_t kBarrierSpinLimit = 1u << 22;  // polls of the grid-barrier counter
 constexpr int kMaxDynamicSmem = 220 * 1024;  // + static shared memory <= 227 KB
+// Coded mixed-V slices (nqb_repack_mixed_v): 128 rows x 8 20-bit records
+// (codebook index | a << 10 | b << 15), row r's from bit 160 r; a member's
+// 1024-word codebook is staged in shared memory per stage 1.
+constexpr uint32_t kCodedSliceBytes = 2560;
+constexpr uint32_t kCodedRowBits = 160;
+constexpr int kCodebookWords = 1024;
 
 struct MemberDev {
   const uint8_t *tiles;  // row-interleaved sign tiles
@@ -84,6 +90,10 @@ struct MemberDev {
   const void *patch_factor;
   int32_t patch_dtype;
   int64_t patch_offset;       // first latent column of the member's patch latent
+  // stage 1 of a mixed-V member: tiles from coded_from on stream as records
+  const uint8_t *coded_tiles;
+  const uint32_t *codebook;   // [1024] words, bulk-copied into shared memory per stage
+  int32_t coded_from;         // first coded tile (INT32_MAX: none)
 };
 
 struct OpDev {
@@ -137,6 +147,7 @@ struct Params {
   int32_t group;                // items per exchange group (4 x leader slots)
   // dynamic shared memory offsets
   uint32_t off_addr, off_b, off_acc, off_exch;
+  uint32_t off_cb;              // mixed-V codebooks [kMaxMembersTc][1024]
 };
 
 __device__ int g_prog_error;
@@ -425,6 +436,17 @@ __device__ __forceinline__ void patch_rows_warp(const Params &p, const OpDev &op
   }
 }
 
+__device__ __forceinline__ uint32_t coded_record(const uint32_t *w, int row, int j) {
+  const uint32_t bit = static_cast<uint32_t>(row) * kCodedRowBits + static_cast<uint32_t>(j) * 20u;
+  const uint32_t i = bit >> 5;  // i + 1 <= 640 stays inside the 4 KB ring slot
+  return __funnelshift_r(w[i], w[i + 1], bit & 31u) & 0xFFFFFu;
+}
+
+// Record -> sign word: codebook word with bits a and b flipped.
+__device__ __forceinline__ uint32_t decode_record(const uint32_t *cb, uint32_t rec) {
+  return cb[rec & 1023u] ^ (1u << ((rec >> 10) & 31u)) ^ (1u << (rec >> 15));
+}
+
 // The producer lane's view of this CTA's slice-address list.
 struct Producer {
   const uint64_t *addrs;
@@ -444,15 +466,24 @@ struct Producer {
               kAddrChunk * 8, bar);
   }
 
-  // Fill ring position `pos` (slot pos % ring) with slice `pos` of this CTA's list.
+  // Fill ring position `pos` (slot pos % ring) with slice `pos` of this CTA's
+  // list.  With kMixed, bit 0 of an address marks a coded slice (2432 bytes).
+  template <bool kMixed>
   __device__ bool produce(int pos, int slot) const {
     const int chunk = pos / kAddrChunk;
     if (pos % kAddrChunk == 0 && chunk >= 1) issue_addr_chunk(chunk + kAddrSlots - 1);
     const bool ok = wait_local(addr_bar + (chunk % kAddrSlots), (chunk / kAddrSlots) & 1);
-    const uint64_t src = cache[(chunk % kAddrSlots) * kAddrChunk + pos % kAddrChunk];
-    expect_tx(full + slot, kStageWeightBytes);
-    bulk_load(ring + static_cast<size_t>(slot) * kStageWeightBytes, reinterpret_cast<const void *>(src),
-              kStageWeightBytes, full + slot);
+    uint64_t src = cache[(chunk % kAddrSlots) * kAddrChunk + pos % kAddrChunk];
+    uint32_t bytes = kStageWeightBytes;
+    if constexpr (kMixed) {
+      if (src & 1u) {
+        bytes = kCodedSliceBytes;
+        src &= ~uint64_t(1);
+      }
+    }
+    expect_tx(full + slot, bytes);
+    bulk_load(ring + static_cast<size_t>(slot) * kStageWeightBytes, reinterpret_cast<const void *>(src), bytes,
+              full + slot);
     return ok;
   }
 };
@@ -494,10 +525,10 @@ __device__ __forceinline__ bool next_unit(const StageInfo &op, int ge, int rank,
   return true;
 }
 
-// kPatch: some op has a patched member.  Programs without one run an
-// instance with every patch step compiled out (those steps cost time in the
-// stage loop even when never taken).
-template <int kT, bool kPatch>
+// kPatch: some op has a patched member; kMixed: some member streams coded
+// mixed-V tiles.  Programs without them run instances with those steps
+// compiled out (the steps cost time in the stage loop even when never taken).
+template <int kT, bool kPatch, bool kMixed>
 __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_constant__ Params p) {
   constexpr int kNT = mmad::n_tiles(kT);
   constexpr int kSets = mmad::acc_sets(kNT);
@@ -565,7 +596,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       uint32_t phase = 0;  // ring passes completed
       for (int pos = 0; pos < prod.count; ++pos) {
         if (phase > 0 && !wait_local_backoff(&s_empty[slot], (phase - 1) & 1)) ok = false;
-        ok &= prod.produce(pos, slot);
+        ok &= prod.template produce<kMixed>(pos, slot);
         if (++slot == R) {
           slot = 0;
           ++phase;
@@ -586,7 +617,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       }
       stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
       __syncwarp();
-      if (lane == 0) mbar_arrive_cta(&s_info_full[g & 1]);
+      if (lane == 0) {
+        // a stage 1 with mixed-V members also brings their codebooks (the
+        // previous stage 1, their last reader, has finished everywhere)
+        uint32_t coded = 0;
+        if constexpr (kMixed) {
+          if ((g & 1) == 0)
+            for (int k = 0; k < kMaxMembersTc; ++k) coded += s_info[g & 1].md[k].coded_tiles != nullptr ? 1u : 0u;
+        }
+        if (coded == 0) {
+          mbar_arrive_cta(&s_info_full[g & 1]);
+        } else {
+          uint32_t *cb = reinterpret_cast<uint32_t *>(smem + p.off_cb);
+          expect_tx(&s_info_full[g & 1], coded * kCodebookWords * 4u);
+          for (int k = 0; k < kMaxMembersTc; ++k)
+            if (s_info[g & 1].md[k].coded_tiles != nullptr)
+              bulk_load(cb + k * kCodebookWords, s_info[g & 1].md[k].codebook, kCodebookWords * 4u,
+                        &s_info_full[g & 1]);
+        }
+      }
       if constexpr (kPatch) {
         if ((g & 1) == 1 && s_info[(g - 1) & 1].patch_rows > 0) {  // stage g - 1's tables, staged last pass
           patch_rows_warp(p, p.ops[g >> 1], cta, static_cast<int>(gridDim.x), lane);
@@ -609,6 +658,36 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       const StageInfo &op = s_info[g & 1];
       const int ib = 0;
       const int ie = op.n_items;
+      // kMixed: item j's slices, the records of a coded tile decoded where a
+      // plain tile's words are loaded (whether item j is coded is read once)
+      auto mixed_slices = [&](int j, int nst, auto &d) {
+        const Item item = op.items[j];
+        const uint32_t *cb = (st == 0 && item.tile >= op.md[item.member].coded_from)
+                                 ? reinterpret_cast<const uint32_t *>(smem + p.off_cb) + item.member * kCodebookWords
+                                 : nullptr;
+        for (int sl = 0; sl < nst; ++sl) {
+          if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+          const uint8_t *src = ring + static_cast<size_t>(slot) * kStageWeightBytes;
+          mmad::SliceWords w;
+          if (cb != nullptr) {
+            const uint32_t *rw = reinterpret_cast<const uint32_t *>(src);
+            const int r0 = warp * 16 + (lane >> 2), tig = lane & 3;
+            w.w00 = decode_record(cb, coded_record(rw, r0, tig));
+            w.w10 = decode_record(cb, coded_record(rw, r0 + 8, tig));
+            w.w01 = decode_record(cb, coded_record(rw, r0, 4 + tig));
+            w.w11 = decode_record(cb, coded_record(rw, r0 + 8, 4 + tig));
+          } else {
+            w = mmad::load_slice_words(src, warp, lane);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+          if (++slot == R) {
+            slot = 0;
+            ++phase;
+          }
+          mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
+        }
+      };
       NQB_TRACE_BEGIN
       for (int gb = ib; gb < ie; gb += p.group) {
         const int ge = min(gb + p.group, ie);
@@ -665,19 +744,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                 for (int nt = 0; nt < kNT; ++nt)
   #pragma unroll
                   for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
-              for (int sl = 0; sl < nst; ++sl) {
-                NQB_TRACE(kTraceMma);
-                if (!wait_local(&s_full[slot], phase & 1)) ok = false;
-                NQB_TRACE(kTraceWaitSigns);
-                const mmad::SliceWords w =
-                    mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
-                if (++slot == R) {
-                  slot = 0;
-                  ++phase;
+              if constexpr (kMixed) {
+                mixed_slices(j, nst, d);
+              } else {
+                for (int sl = 0; sl < nst; ++sl) {
+                  NQB_TRACE(kTraceMma);
+                  if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+                  NQB_TRACE(kTraceWaitSigns);
+                  const mmad::SliceWords w =
+                      mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
+                  __syncwarp();
+                  if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+                  if (++slot == R) {
+                    slot = 0;
+                    ++phase;
+                  }
+                  mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
                 }
-                mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
               }
               NQB_TRACE(kTraceMma);
               mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
@@ -738,19 +821,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                   for (int nt = 0; nt < kNT; ++nt)
   #pragma unroll
                     for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
-                for (int sl = 0; sl < nst; ++sl) {
-                  NQB_TRACE(kTraceMma);
-                  if (!wait_local(&s_full[slot], phase & 1)) ok = false;
-                  NQB_TRACE(kTraceWaitSigns);
-                  const mmad::SliceWords w =
-                      mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
-                  __syncwarp();
-                  if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
-                  if (++slot == R) {
-                    slot = 0;
-                    ++phase;
+                if constexpr (kMixed) {
+                  mixed_slices(j, nst, d);
+                } else {
+                  for (int sl = 0; sl < nst; ++sl) {
+                    NQB_TRACE(kTraceMma);
+                    if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+                    NQB_TRACE(kTraceWaitSigns);
+                    const mmad::SliceWords w =
+                        mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+                    if (++slot == R) {
+                      slot = 0;
+                      ++phase;
+                    }
+                    mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
                   }
-                  mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
                 }
                 NQB_TRACE(kTraceMma);
                 mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
@@ -943,6 +1030,7 @@ struct nqb_program {
   int64_t tokens = 0;
   int bucket = 1;
   bool patch = false;  // runs the patch-capable kernel instance
+  bool mixed = false;  // runs the coded mixed-V instance
   int ctas = 0;
   int clusters = 0;
   int smem = 0;
@@ -960,10 +1048,10 @@ static int token_bucket(int64_t tokens) {
 
 struct SmemPlan {
   int sc, group, ring;
-  uint32_t off_addr, off_b, off_acc, off_exch, total;
+  uint32_t off_addr, off_b, off_acc, off_exch, off_cb, total;
 };
 
-static SmemPlan smem_plan(int bucket) {
+static SmemPlan smem_plan(int bucket, bool mixed) {
   SmemPlan s{};
   s.sc = slices_per_chunk(bucket);
   const int lead = leader_slots(bucket);
@@ -972,7 +1060,8 @@ static SmemPlan smem_plan(int bucket) {
   const uint32_t b = static_cast<uint32_t>(s.sc) * mmad::slice_frag_bytes(mmad::n_tiles(bucket));
   const uint32_t acc = static_cast<uint32_t>(s.group) * bucket * kTileRows * 4;
   const uint32_t exch = static_cast<uint32_t>(lead) * kClusterSize * bucket * kTileRows * 4;
-  const uint32_t rest = addr + b + acc + exch;
+  const uint32_t cb = mixed ? kMaxMembersTc * kCodebookWords * 4u : 0u;
+  const uint32_t rest = addr + b + acc + exch + cb;
   s.ring = std::min<int>(kMaxRing, static_cast<int>((kMaxDynamicSmem - rest) / kStageWeightBytes));
   uint32_t off = static_cast<uint32_t>(s.ring) * kStageWeightBytes;
   s.off_addr = off;
@@ -983,23 +1072,26 @@ static SmemPlan smem_plan(int bucket) {
   off += acc;
   s.off_exch = off;
   off += exch;
+  s.off_cb = off;
+  off += cb;
   s.total = off;
   return s;
 }
 
-template <bool kPatch>
+template <bool kPatch, bool kMixed>
 static const void *kernel_for_t(int bucket) {
   switch (bucket) {
-    case 1: return reinterpret_cast<const void *>(program_kernel<1, kPatch>);
-    case 2: return reinterpret_cast<const void *>(program_kernel<2, kPatch>);
-    case 4: return reinterpret_cast<const void *>(program_kernel<4, kPatch>);
-    case 8: return reinterpret_cast<const void *>(program_kernel<8, kPatch>);
-    default: return reinterpret_cast<const void *>(program_kernel<16, kPatch>);
+    case 1: return reinterpret_cast<const void *>(program_kernel<1, kPatch, kMixed>);
+    case 2: return reinterpret_cast<const void *>(program_kernel<2, kPatch, kMixed>);
+    case 4: return reinterpret_cast<const void *>(program_kernel<4, kPatch, kMixed>);
+    case 8: return reinterpret_cast<const void *>(program_kernel<8, kPatch, kMixed>);
+    default: return reinterpret_cast<const void *>(program_kernel<16, kPatch, kMixed>);
   }
 }
 
-static const void *kernel_for(int bucket, bool patch) {
-  return patch ? kernel_for_t<true>(bucket) : kernel_for_t<false>(bucket);
+static const void *kernel_for(int bucket, bool patch, bool mixed) {
+  if (mixed) return patch ? kernel_for_t<true, true>(bucket) : kernel_for_t<false, true>(bucket);
+  return patch ? kernel_for_t<true, false>(bucket) : kernel_for_t<false, false>(bucket);
 }
 
 // `pre`, `row_scale` and `bias` are the program's fp32 copies of the layer's vectors.
@@ -1015,6 +1107,11 @@ static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64
     m.pre = pre;
     m.out_offset = rank_offset;
     m.patch_factor = d.patch_right;
+    if (d.coded_right_tiles != nullptr) {
+      m.coded_tiles = static_cast<const uint8_t *>(d.coded_right_tiles);
+      m.codebook = reinterpret_cast<const uint32_t *>(d.coded_codebook);
+      m.coded_from = static_cast<int32_t>((d.coded_free_rows + kTileRows - 1) / kTileRows);
+    }
   } else {
     m.tiles = static_cast<const uint8_t *>(d.left_tiles);
     m.rows = d.out_features;
@@ -1038,6 +1135,7 @@ static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64
   }
   m.patch_rank = d.patch_rank;
   m.patch_dtype = d.patch_dtype;
+  if (m.coded_tiles == nullptr) m.coded_from = INT32_MAX;
   m.ks = m.wc / 2;
 }
 
@@ -1109,6 +1207,10 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       if (d.patch_rank < 0 || d.patch_rank > (1ll << 20) ||
           (d.patch_rank > 0 && (d.patch_left == nullptr || d.patch_right == nullptr || !is_float_dtype(d.patch_dtype))))
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has an invalid low-rank patch", i, k);
+      if (d.coded_right_tiles != nullptr &&
+          (d.coded_codebook == nullptr || d.coded_free_rows <= 0 || d.coded_free_rows >= d.rank ||
+           reinterpret_cast<uintptr_t>(d.coded_right_tiles) % 16 || reinterpret_cast<uintptr_t>(d.coded_codebook) % 16))
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has invalid coded mixed-V tiles", i, k);
       if (d.in_features != o.layers[0].in_features || d.scale_dtype != o.layers[0].scale_dtype)
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: members must share in_features and scale dtype", i);
       if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
@@ -1193,10 +1295,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
 
   int device = 0;
   NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
-  const SmemPlan sp = smem_plan(bucket);
-  bool patch = false;
-  for (int i = 0; i < op_count; ++i) patch = patch || opdev[i].patch_rows > 0;
-  const void *fn = kernel_for(bucket, patch);
+  bool patch = false, mixed = false;
+  for (int i = 0; i < op_count; ++i) {
+    patch = patch || opdev[i].patch_rows > 0;
+    for (int k = 0; k < opdev[i].count; ++k) mixed = mixed || opdev[i].s[0][k].coded_tiles != nullptr;
+  }
+  const SmemPlan sp = smem_plan(bucket, mixed);
+  if (sp.off_cb % 16) return fail(NQB_ERR_UNSUPPORTED, "codebook buffer is misaligned");
+  const void *fn = kernel_for(bucket, patch, mixed);
   NQB_CHECK(ensure_dynamic_smem(fn, static_cast<int>(sp.total)));
   int sms = 0;
   NQB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
@@ -1297,9 +1403,15 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
             for (int c0 = lo; c0 < hi; c0 += sp.sc) {
               const int nst = std::min(sp.sc, hi - c0);
               for (size_t j = j0; j < j1; ++j)
-                for (int sl = c0; sl < c0 + nst; ++sl)
-                  addrs.push_back(reinterpret_cast<uint64_t>(md.tiles) +
-                                  (static_cast<uint64_t>(list[j].tile) * md.wc + 2ull * sl) * (kTileRows * kChunkBytes));
+                for (int sl = c0; sl < c0 + nst; ++sl) {
+                  if (st == 0 && list[j].tile >= md.coded_from)  // coded slice: bit 0 set
+                    addrs.push_back((reinterpret_cast<uint64_t>(md.coded_tiles) +
+                                     (static_cast<uint64_t>(list[j].tile - md.coded_from) * md.ks + sl) *
+                                         kCodedSliceBytes) | 1u);
+                  else
+                    addrs.push_back(reinterpret_cast<uint64_t>(md.tiles) +
+                                    (static_cast<uint64_t>(list[j].tile) * md.wc + 2ull * sl) * (kTileRows * kChunkBytes));
+                }
             }
             j0 = j1;
           }
@@ -1387,10 +1499,12 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   pp.off_b = sp.off_b;
   pp.off_acc = sp.off_acc;
   pp.off_exch = sp.off_exch;
+  pp.off_cb = sp.off_cb;
   prog->device = device;
   prog->tokens = tokens;
   prog->bucket = bucket;
   prog->patch = patch;
+  prog->mixed = mixed;
   prog->ctas = ctas;
   prog->clusters = clusters;
   prog->smem = static_cast<int>(sp.total);
@@ -1414,7 +1528,7 @@ int nqb_program_run(const nqb_program *program, void *workspace, size_t workspac
   Params params = program->params;
   params.counters = static_cast<uint32_t *>(workspace);
   params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
-  const void *fn = kernel_for(program->bucket, program->patch);
+  const void *fn = kernel_for(program->bucket, program->patch, program->mixed);
   NQB_CHECK(ensure_dynamic_smem(fn, program->smem));
   cudaLaunchConfig_t config;
   std::memset(&config, 0, sizeof(config));

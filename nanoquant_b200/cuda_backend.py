@@ -73,6 +73,7 @@ def _build_payload(
     overlay: OutlierRowOverlay | None,
     device: torch.device,
     tensor_cores: bool = True,
+    coded_mixed_v: bool = False,
 ) -> _Sm100Payload:
     spec = state.spec
     tensors: dict[str, torch.Tensor] = {}
@@ -137,6 +138,18 @@ def _build_payload(
             tensors["right_tiles"] = _repack(tensors["right_words"], spec.rank, spec.in_features)
             desc.left_tiles = tensors["left_tiles"].data_ptr()
             desc.right_tiles = tensors["right_tiles"].data_ptr()
+            if coded_mixed_v and isinstance(state, MixedVLayerState):
+                # decode programs stream V's coded rows as records and decode them in stage 1
+                from nanoquant_b200.device_ops import repack_mixed_v_cuda
+
+                codebook = tensors.setdefault("coded_codebook",
+                                              _to_device(state.codebook_words, device).contiguous().clone())
+                tensors["coded_right_tiles"] = repack_mixed_v_cuda(
+                    _to_device(state.coded_payload, device).contiguous(), rank=spec.rank, columns=spec.in_features,
+                    free_rows=state.free_rows)
+                desc.coded_right_tiles = tensors["coded_right_tiles"].data_ptr()
+                desc.coded_codebook = codebook.data_ptr()
+                desc.coded_free_rows = state.free_rows
     desc.scale_pre = keep("scale_pre", scale_pre).data_ptr()
     desc.scale_mid = keep("scale_mid", scale_mid).data_ptr()
     desc.scale_post = keep("scale_post", scale_post).data_ptr()
@@ -259,10 +272,15 @@ class CudaPackedSm100Backend:
     version = CUDA_SM100_BACKEND_VERSION
     packed_layout = PACKED_LAYOUT_VERSION
 
-    def __init__(self, *, tensor_cores: bool = True) -> None:
+    def __init__(self, *, tensor_cores: bool = True, coded_mixed_v: bool = False) -> None:
         # tensor_cores=False keeps prepared layers on the CUDA-core kernels only
         # (no kernel-native tile copies); used to cross-check the two paths.
+        # coded_mixed_v=True also keeps a mixed-V layer's V as coded tiles, which
+        # decode programs stream and decode in stage 1 (38 % fewer V bytes; at
+        # batch 1 the record decode costs more time than the bytes save, so the
+        # expanded tiles are the default).
         self.tensor_cores = tensor_cores
+        self.coded_mixed_v = coded_mixed_v
 
     def capabilities(self) -> BackendCapabilities:
         return BackendCapabilities(
@@ -310,7 +328,7 @@ class CudaPackedSm100Backend:
         target = _cuda_device(device)
         _native.library()
         with torch.cuda.device(target):
-            payload = _build_payload(base, overlay, target, self.tensor_cores)
+            payload = _build_payload(base, overlay, target, self.tensor_cores, self.coded_mixed_v)
         return PreparedLayer(self.name, self.version, state.spec, payload)
 
     def linear(self, value: torch.Tensor, layer: PreparedLayer) -> torch.Tensor:

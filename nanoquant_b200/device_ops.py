@@ -9,6 +9,8 @@ work of the CUDA path can be checked bit-exactly against the host format code.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from nanoquant_b200 import _native
@@ -127,4 +129,26 @@ def decode_mixed_v_cuda(
         out.data_ptr(),
         _native.current_stream_handle(free_words.device),
     )
+    return out
+
+
+def repack_mixed_v_cuda(payload: torch.Tensor, *, rank: int, columns: int, free_rows: int) -> torch.Tensor:
+    """Coded mixed-V tiles for decode programs (``nqb_repack_mixed_v``) -> uint8 bytes.
+
+    Tiles of 128 rows from ``ceil(free_rows / 128)`` on keep their 19-bit
+    records: per 256-column slice, row ``r``'s 8 records back to back from bit
+    ``152 r`` (2432 bytes per tile slice).
+    """
+
+    _require_cuda(payload, "payload")
+    if payload.dtype != torch.int32 or not payload.is_contiguous():
+        raise ValueError("mixed-V payload must be contiguous int32")
+    if payload.numel() * 32 < (rank - free_rows) * packed_word_count(columns) * 19:
+        raise ValueError("mixed-V payload is shorter than its records")
+    size = ctypes.c_size_t(0)
+    _native.call("nqb_mixed_v_tiles_bytes", rank, columns, free_rows, ctypes.byref(size))
+    out = torch.zeros(max(size.value, 16), dtype=torch.uint8, device=payload.device)
+    if size.value:
+        _native.call("nqb_repack_mixed_v", payload.data_ptr(), rank, columns, free_rows, out.data_ptr(),
+                     _native.current_stream_handle(payload.device))
     return out
