@@ -41,11 +41,59 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
 }
 
 // One block per token: h += delta (when given, written back), then
-// out = h * rsqrt(mean(h^2) + eps) * w.
+// out = h * rsqrt(mean(h^2) + eps) * w.  Rows of up to kRmsVec * 1024 values
+// (a multiple of 4, 16-byte aligned) stay in registers: every load of the row
+// is issued before any is used (one memory round trip instead of one per
+// loop step, which the in-place write-back otherwise forces).
+constexpr int kRmsVec = 8;  // float4 pieces per thread (256 threads: hidden <= 8192)
+
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *delta, const void *w, int32_t w_dt,
                                                       int64_t hidden, float eps, void *out, int32_t out_dt) {
   __shared__ float scratch[32];
   const int64_t t = blockIdx.x;
+  const bool vec = hidden % 4 == 0 && hidden <= 1024 * kRmsVec &&
+                   reinterpret_cast<uintptr_t>(h) % 16 == 0 && (delta == nullptr || reinterpret_cast<uintptr_t>(delta) % 16 == 0);
+  if (vec) {
+    float4 *row4 = reinterpret_cast<float4 *>(h + t * hidden);
+    const float4 *d4 = delta != nullptr ? reinterpret_cast<const float4 *>(delta + t * hidden) : nullptr;
+    const int n4 = static_cast<int>(hidden / 4);
+    float4 v[kRmsVec];
+#pragma unroll
+    for (int j = 0; j < kRmsVec; ++j) {
+      const int i = threadIdx.x + j * 256;
+      v[j] = i < n4 ? row4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    if (d4 != nullptr) {
+#pragma unroll
+      for (int j = 0; j < kRmsVec; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < n4) {
+          const float4 d = d4[i];
+          v[j].x += d.x;
+          v[j].y += d.y;
+          v[j].z += d.z;
+          v[j].w += d.w;
+          row4[i] = v[j];
+        }
+      }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kRmsVec; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    const float r = rsqrtf(block_sum(ss, scratch) / static_cast<float>(hidden) + eps);
+#pragma unroll
+    for (int j = 0; j < kRmsVec; ++j) {
+      const int i = threadIdx.x + j * 256;
+      if (i < n4) {
+        const int64_t c = t * hidden + 4 * static_cast<int64_t>(i);
+        store_as(out, c, out_dt, v[j].x * r * load_as_float(w, 4 * i, w_dt));
+        store_as(out, c + 1, out_dt, v[j].y * r * load_as_float(w, 4 * i + 1, w_dt));
+        store_as(out, c + 2, out_dt, v[j].z * r * load_as_float(w, 4 * i + 2, w_dt));
+        store_as(out, c + 3, out_dt, v[j].w * r * load_as_float(w, 4 * i + 3, w_dt));
+      }
+    }
+    return;
+  }
   float *row = h + t * hidden;
   const float *drow = delta != nullptr ? delta + t * hidden : nullptr;
   float ss = 0.0f;
@@ -153,13 +201,26 @@ __device__ __forceinline__ void load_bf16_row(const __nv_bfloat16 *p, float (&ou
   }
 }
 
+constexpr int kStageKeys = 64;  // K and V rows staged in shared memory at once
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // Split-K attention partials.  Grid (kv_heads, splits, tokens); one warp per
 // q head of the kv head's group.  Token t sees keys [0, keys + t); split sp
-// covers [sp * chunk, min((sp + 1) * chunk, keys + t)).  Keys go in blocks of
-// kB: the block's K and V rows are loaded before any is used and its kB
-// dot-product reductions are interleaved, so one block costs about one
-// memory round trip.  Writes (acc[hd], m, l) of an online softmax per
-// (token, q head, split).
+// covers [sp * chunk, min((sp + 1) * chunk, keys + t)).  The block copies up
+// to 64 of its K and V rows at once into shared memory (16-byte cp.async,
+// all in flight together: one memory round trip, the rows of a kv head are
+// contiguous) and the group's warps read them from there, keys in blocks of
+// kB with the kB dot-product reductions interleaved.  Writes (acc[hd], m, l)
+// of an online softmax per (token, q head, split).
 template <int kDpl>
 __global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bfloat16 *kc, const __nv_bfloat16 *vc,
                                          int64_t cache_len, int64_t keys, int32_t q_heads, int32_t kv_heads,
@@ -183,49 +244,64 @@ __global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bflo
     acc[j] = 0.0f;
   }
   float m = -INFINITY, l = 0.0f;
-  const __nv_bfloat16 *kbase = kc + static_cast<int64_t>(kh) * cache_len * kHd + d0;
-  const __nv_bfloat16 *vbase = vc + static_cast<int64_t>(kh) * cache_len * kHd + d0;
-  for (int64_t j = j0; j < j1; j += kB) {
-    const int nb = static_cast<int>(min(static_cast<int64_t>(kB), j1 - j));
-    float kv[kB][kDpl], vv[kB][kDpl];
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const int64_t row = j + (b < nb ? b : 0);  // rows past the block re-read row j (masked below)
-      load_bf16_row<kDpl>(kbase + row * kHd, kv[b]);
-      load_bf16_row<kDpl>(vbase + row * kHd, vv[b]);
+  extern __shared__ __align__(16) uint8_t s_rows[];  // [kStageKeys][kHd] K rows, then V rows
+  __nv_bfloat16 *sk = reinterpret_cast<__nv_bfloat16 *>(s_rows);
+  __nv_bfloat16 *sv = sk + kStageKeys * kHd;
+  const char *kg = reinterpret_cast<const char *>(kc + static_cast<int64_t>(kh) * cache_len * kHd);
+  const char *vg = reinterpret_cast<const char *>(vc + static_cast<int64_t>(kh) * cache_len * kHd);
+  for (int64_t s0 = j0; s0 < j1; s0 += kStageKeys) {
+    const int rows = static_cast<int>(min(static_cast<int64_t>(kStageKeys), j1 - s0));
+    const int chunks = rows * kHd * 2 / 16;  // 16-byte pieces per matrix
+    for (int i = threadIdx.x; i < 2 * chunks; i += blockDim.x) {
+      const bool is_v = i >= chunks;
+      const int c = is_v ? i - chunks : i;
+      cp_async16(reinterpret_cast<char *>(is_v ? sv : sk) + c * 16, (is_v ? vg : kg) + s0 * kHd * 2 + c * 16);
     }
-    float sc[kB];
+    cp_async_wait_all();
+    __syncthreads();
+    for (int j = 0; j < rows; j += kB) {
+      const int nb = min(kB, rows - j);
+      float kv[kB][kDpl], vv[kB][kDpl];
 #pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      float d = 0.0f;
-#pragma unroll
-      for (int e = 0; e < kDpl; ++e) d += qv[e] * kv[b][e];
-      sc[b] = d;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-      for (int b = 0; b < kB; ++b) sc[b] += __shfl_xor_sync(0xffffffffu, sc[b], off);
-    }
-    float mb = sc[0];
-#pragma unroll
-    for (int b = 1; b < kB; ++b)
-      if (b < nb) mb = fmaxf(mb, sc[b]);
-    const float mn = fmaxf(m, mb);
-    const float corr = expf(m - mn);
-    l *= corr;
-#pragma unroll
-    for (int e = 0; e < kDpl; ++e) acc[e] *= corr;
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      if (b < nb) {
-        const float p = expf(sc[b] - mn);
-        l += p;
-#pragma unroll
-        for (int e = 0; e < kDpl; ++e) acc[e] += p * vv[b][e];
+      for (int b = 0; b < kB; ++b) {
+        const int row = j + (b < nb ? b : 0);  // rows past the block re-read row j (masked below)
+        load_bf16_row<kDpl>(sk + row * kHd + d0, kv[b]);
+        load_bf16_row<kDpl>(sv + row * kHd + d0, vv[b]);
       }
+      float sc[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < kDpl; ++e) d += qv[e] * kv[b][e];
+        sc[b] = d;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int b = 0; b < kB; ++b) sc[b] += __shfl_xor_sync(0xffffffffu, sc[b], off);
+      }
+      float mb = sc[0];
+#pragma unroll
+      for (int b = 1; b < kB; ++b)
+        if (b < nb) mb = fmaxf(mb, sc[b]);
+      const float mn = fmaxf(m, mb);
+      const float corr = expf(m - mn);
+      l *= corr;
+#pragma unroll
+      for (int e = 0; e < kDpl; ++e) acc[e] *= corr;
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        if (b < nb) {
+          const float p = expf(sc[b] - mn);
+          l += p;
+#pragma unroll
+          for (int e = 0; e < kDpl; ++e) acc[e] += p * vv[b][e];
+        }
+      }
+      m = mn;
     }
-    m = mn;
+    __syncthreads();  // every warp is done with the staged rows before the next copy
   }
   float *o = part + ((t * q_heads + qh) * splits + sp) * (kHd + 2);
 #pragma unroll
@@ -245,17 +321,40 @@ __global__ void attention_combine_kernel(const float *part, int32_t splits, int6
   const int lane = threadIdx.x & 31;
   if (gw >= tokens * q_heads) return;
   const float *base = part + gw * splits * (kHd + 2);
-  float mx = -INFINITY;
-  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, base[s * (kHd + 2) + kHd]);
-  float den = 0.0f, num[kDpl];
+  // (m, l) of split lane and lane + 32 (splits <= 64), read once in parallel
+  const float m0 = lane < splits ? base[lane * (kHd + 2) + kHd] : -INFINITY;
+  const float m1 = lane + 32 < splits ? base[(lane + 32) * (kHd + 2) + kHd] : -INFINITY;
+  const float l0 = lane < splits ? base[lane * (kHd + 2) + kHd + 1] : 0.0f;
+  const float l1 = lane + 32 < splits ? base[(lane + 32) * (kHd + 2) + kHd + 1] : 0.0f;
+  float mx = fmaxf(m0, m1);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float f0 = m0 == -INFINITY ? 0.0f : expf(m0 - mx);
+  const float f1 = m1 == -INFINITY ? 0.0f : expf(m1 - mx);
+  float den = f0 * l0 + f1 * l1;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  // weighted sum of the splits' vectors, eight splits' loads in flight at once
+  float num[kDpl];
 #pragma unroll
   for (int e = 0; e < kDpl; ++e) num[e] = 0.0f;
-  for (int s = 0; s < splits; ++s) {
-    const float *p = base + s * (kHd + 2);
-    const float f = p[kHd] == -INFINITY ? 0.0f : expf(p[kHd] - mx);
-    den += f * p[kHd + 1];
+  for (int s0 = 0; s0 < splits; s0 += 8) {
+    float vals[8][kDpl];
 #pragma unroll
-    for (int e = 0; e < kDpl; ++e) num[e] += f * p[lane * kDpl + e];
+    for (int u = 0; u < 8; ++u) {
+      const int s = min(s0 + u, splits - 1);
+#pragma unroll
+      for (int e = 0; e < kDpl; ++e) vals[u][e] = base[s * (kHd + 2) + lane * kDpl + e];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int s = s0 + u;
+      const float f = __shfl_sync(0xffffffffu, (s & 32) ? f1 : f0, s & 31);
+      if (s < splits) {
+#pragma unroll
+        for (int e = 0; e < kDpl; ++e) num[e] += f * vals[u][e];
+      }
+    }
   }
   const float inv = den > 0.0f ? 1.0f / den : 0.0f;
 #pragma unroll
@@ -320,6 +419,8 @@ int splits_for(int64_t keys, int64_t tokens) {
   const int64_t s = (most + 63) / 64;
   return static_cast<int>(s < 1 ? 1 : (s > 64 ? 64 : s));
 }
+
+size_t attention_smem_bytes(int head_dim) { return 2ull * kStageKeys * head_dim * sizeof(__nv_bfloat16); }
 
 int launch_sm_count() {
   int device = 0, sms = 148;
@@ -418,18 +519,24 @@ int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache
   auto *o = static_cast<__nv_bfloat16 *>(out);
   switch (head_dim) {
     case 64:
-      shell::attention_partial_kernel<2><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
-                                                                   splits, chunk, scale, part);
+      NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<2>),
+                                    shell::attention_smem_bytes(64)));
+      shell::attention_partial_kernel<2><<<grid, threads, shell::attention_smem_bytes(64), s>>>(
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
       shell::attention_combine_kernel<2><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     case 128:
-      shell::attention_partial_kernel<4><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
-                                                                   splits, chunk, scale, part);
+      NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<4>),
+                                    shell::attention_smem_bytes(128)));
+      shell::attention_partial_kernel<4><<<grid, threads, shell::attention_smem_bytes(128), s>>>(
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
       shell::attention_combine_kernel<4><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     case 256:
-      shell::attention_partial_kernel<8><<<grid, threads, 0, s>>>(qp, kc, vc, cache_len, keys, q_heads, kv_heads,
-                                                                   splits, chunk, scale, part);
+      NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<8>),
+                                    shell::attention_smem_bytes(256)));
+      shell::attention_partial_kernel<8><<<grid, threads, shell::attention_smem_bytes(256), s>>>(
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
       shell::attention_combine_kernel<8><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     default:
