@@ -365,6 +365,16 @@ typedef struct nqb_program nqb_program;
 int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t tokens, nqb_program **program);
 int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes);
 int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream);
+/*
+ * nqb_program_run as a programmatic dependent launch of the preceding kernel
+ * on the stream: the program's producer warps start streaming sign words while
+ * that kernel finishes; everything that reads activations or the workspace
+ * waits for its completion.  For a program that follows other kernels (a
+ * decoder step's norm and attention kernels); a run right after a run of a
+ * program measured slower than nqb_program_run.
+ */
+int nqb_program_run_dependent(const nqb_program *program, void *workspace, size_t workspace_bytes,
+                              void *stream);
 int nqb_program_destroy(nqb_program *program);
 /* Launch shape of a created program: CTAs (one per SM used) and cluster size. */
 int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size);

@@ -148,6 +148,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_program_create": (ctypes.c_int, [ctypes.POINTER(ProgramOp), _i32, _i64, ctypes.POINTER(_c_void_p)]),
     "nqb_program_workspace_bytes": (ctypes.c_int, [_c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "nqb_program_run": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_program_run_dependent": (ctypes.c_int, [_c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
     "nqb_program_destroy": (ctypes.c_int, [_c_void_p]),
     "nqb_program_shape": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "nqb_program_trace": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_i64), ctypes.c_size_t]),

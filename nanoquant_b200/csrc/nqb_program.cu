@@ -576,6 +576,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     ptx::fence_mbar_init();
   }
   cluster_sync();  // every CTA's barriers exist before any remote arrive
+  // Run by nqb_program_run_dependent, the program is a programmatic dependent
+  // of the preceding kernel: only the producer warp runs ahead (sign words,
+  // which no kernel writes); every other warp first waits for the preceding
+  // kernel to complete (its outputs are this program's inputs).  After a
+  // plain launch the wait returns at once.
+  if (warp != kProducerWarp) asm volatile("griddepcontrol.wait;" ::: "memory");
 
   bool ok = true;
   if (warp == kProducerWarp) {
@@ -1519,8 +1525,13 @@ int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes) {
   return ok();
 }
 
-int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream) {
-  using namespace nqb::prog;
+}  // extern "C"
+
+namespace nqb {
+namespace prog {
+
+static int launch_program(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream,
+                          bool dependent) {
   if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
   const size_t need = kCounterRegionBytes + program->latent_bytes;
   if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
@@ -1536,17 +1547,34 @@ int nqb_program_run(const nqb_program *program, void *workspace, size_t workspac
   config.blockDim = dim3(kBlockThreads);
   config.dynamicSmemBytes = program->smem;
   config.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = kClusterSize;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
+  attr[2].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[2].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attr;
-  config.numAttrs = 2;
+  config.numAttrs = dependent ? 3 : 2;
   void *args[] = {&params};
   NQB_CUDA(cudaLaunchKernelExC(&config, fn, args), "program launch");
+  return NQB_OK;
+}
+
+}  // namespace prog
+}  // namespace nqb
+
+extern "C" {
+
+int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream) {
+  NQB_CHECK(nqb::prog::launch_program(program, workspace, workspace_bytes, stream, false));
+  return ok();
+}
+
+int nqb_program_run_dependent(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream) {
+  NQB_CHECK(nqb::prog::launch_program(program, workspace, workspace_bytes, stream, true));
   return ok();
 }
 

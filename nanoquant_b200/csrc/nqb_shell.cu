@@ -29,6 +29,11 @@ __device__ __forceinline__ void store_as(void *p, int64_t i, int32_t dt, float v
 }
 
 // Sum over the block (blockDim.x a multiple of 32, at most 1024 threads).
+// Lets a decode program launched as this kernel's programmatic dependent
+// (nqb_program_run_dependent) launch now and start streaming its sign words;
+// the program still waits for this kernel's completion before reading its output.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float block_sum(float v, float *scratch) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -50,6 +55,7 @@ constexpr int kRmsVec = 8;  // float4 pieces per thread (256 threads: hidden <= 
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *delta, const void *w, int32_t w_dt,
                                                       int64_t hidden, float eps, void *out, int32_t out_dt) {
   __shared__ float scratch[32];
+  allow_dependents();
   const int64_t t = blockIdx.x;
   const bool vec = hidden % 4 == 0 && hidden <= 1024 * kRmsVec &&
                    reinterpret_cast<uintptr_t>(h) % 16 == 0 && (delta == nullptr || reinterpret_cast<uintptr_t>(delta) % 16 == 0);
@@ -317,6 +323,7 @@ template <int kDpl>
 __global__ void attention_combine_kernel(const float *part, int32_t splits, int64_t tokens, int32_t q_heads,
                                          __nv_bfloat16 *out) {
   constexpr int kHd = 32 * kDpl;
+  allow_dependents();
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= tokens * q_heads) return;

@@ -222,21 +222,21 @@ class Qwen3DecodeStep:
         delta = None
         for index, layer in enumerate(self.layers):
             rmsnorm(self.h, delta, self.shell.input_norm[index], self.eps, self.xn)
-            layer["prog_qkv"].run()
+            layer["prog_qkv"].run(dependent=True)
             qk_norm_rope(layer["q"], layer["k"], layer["v"], self.shell.q_norm[index], self.shell.k_norm[index],
                          self.cos, self.sin, self.q_rot, layer["k_cache"], layer["v_cache"], self.position, self.eps,
                          s.q_heads, s.kv_heads, hd)
             decode_attention(self.q_rot, layer["k_cache"], layer["v_cache"], self.keys, s.q_heads, s.kv_heads, hd,
                              self.attn, self.attn_ws)
-            layer["prog_o"].run()
+            layer["prog_o"].run(dependent=True)
             rmsnorm(self.h, layer["o"], self.shell.post_norm[index], self.eps, self.xn)
             mlp = layer["prog_mlp"]
             if isinstance(mlp, tuple):
-                mlp[0].run()
+                mlp[0].run(dependent=True)
                 silu_mul(layer["gate"], layer["up"], self.act)
-                mlp[1].run()
+                mlp[1].run(dependent=True)
             else:
-                mlp.run()
+                mlp.run(dependent=True)
             delta = layer["down"]
         rmsnorm(self.h, delta, self.shell.final_norm, self.eps, self.xn)
         gemv_bf16(self.shell.lm_head, self.xn, self.logits)

@@ -111,13 +111,19 @@ class DecodeProgram:
         self.ctas = ctas.value
         self.cluster_size = cluster.value
 
-    def run(self) -> list[tuple[torch.Tensor, ...]]:
-        """Launch the program on the current stream; returns the bound outputs."""
+    def run(self, *, dependent: bool = False) -> list[tuple[torch.Tensor, ...]]:
+        """Launch the program on the current stream; returns the bound outputs.
+
+        ``dependent=True`` launches it as a programmatic dependent of the
+        preceding kernel (``nqb_program_run_dependent``): its sign words stream
+        in while that kernel finishes.  For a program that follows other
+        kernels; back-to-back runs of programs are faster without it.
+        """
 
         if self._handle is None:
             raise RuntimeError("program was closed")
         _native.call(
-            "nqb_program_run",
+            "nqb_program_run_dependent" if dependent else "nqb_program_run",
             self._handle,
             self.workspace.data_ptr(),
             self.workspace.numel(),
