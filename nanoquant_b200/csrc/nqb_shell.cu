@@ -208,6 +208,27 @@ __device__ __forceinline__ void load_bf16_row(const __nv_bfloat16 *p, float (&ou
 }
 
 constexpr int kStageKeys = 64;  // K and V rows staged in shared memory at once
+// A split's partial row: hd accumulators, m, l and two pad floats, so every
+// row (and every lane's slice of it) starts on a 16-byte boundary.
+constexpr int kPartPad = 4;
+
+template <int kDpl>
+__device__ __forceinline__ void load_f32_slice(const float *p, float (&out)[kDpl]) {
+  if constexpr (kDpl == 2) {
+    const float2 v = *reinterpret_cast<const float2 *>(p);
+    out[0] = v.x;
+    out[1] = v.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kDpl; i += 4) {
+      const float4 v = *reinterpret_cast<const float4 *>(p + i);
+      out[i] = v.x;
+      out[i + 1] = v.y;
+      out[i + 2] = v.z;
+      out[i + 3] = v.w;
+    }
+  }
+}
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -309,9 +330,9 @@ __global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bflo
     }
     __syncthreads();  // every warp is done with the staged rows before the next copy
   }
-  float *o = part + ((t * q_heads + qh) * splits + sp) * (kHd + 2);
+  float *o = part + ((t * q_heads + qh) * splits + sp) * (kHd + kPartPad);
 #pragma unroll
-  for (int e = 0; e < kDpl; ++e) o[d0 + e] = acc[e];
+  for (int e = 0; e < kDpl; ++e) o[d0 + e] = acc[e];  // contiguous: the compiler vectorises
   if (lane == 0) {
     o[kHd] = m;
     o[kHd + 1] = l;
@@ -327,12 +348,12 @@ __global__ void attention_combine_kernel(const float *part, int32_t splits, int6
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= tokens * q_heads) return;
-  const float *base = part + gw * splits * (kHd + 2);
+  const float *base = part + gw * splits * (kHd + kPartPad);
   // (m, l) of split lane and lane + 32 (splits <= 64), read once in parallel
-  const float m0 = lane < splits ? base[lane * (kHd + 2) + kHd] : -INFINITY;
-  const float m1 = lane + 32 < splits ? base[(lane + 32) * (kHd + 2) + kHd] : -INFINITY;
-  const float l0 = lane < splits ? base[lane * (kHd + 2) + kHd + 1] : 0.0f;
-  const float l1 = lane + 32 < splits ? base[(lane + 32) * (kHd + 2) + kHd + 1] : 0.0f;
+  const float m0 = lane < splits ? base[lane * (kHd + kPartPad) + kHd] : -INFINITY;
+  const float m1 = lane + 32 < splits ? base[(lane + 32) * (kHd + kPartPad) + kHd] : -INFINITY;
+  const float l0 = lane < splits ? base[lane * (kHd + kPartPad) + kHd + 1] : 0.0f;
+  const float l1 = lane + 32 < splits ? base[(lane + 32) * (kHd + kPartPad) + kHd + 1] : 0.0f;
   float mx = fmaxf(m0, m1);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -341,20 +362,21 @@ __global__ void attention_combine_kernel(const float *part, int32_t splits, int6
   float den = f0 * l0 + f1 * l1;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-  // weighted sum of the splits' vectors, eight splits' loads in flight at once
+  // weighted sum of the splits' vectors: a lane's slice of a split is one
+  // aligned vector load (rows padded to hd + 4 floats), kU splits in flight
+  constexpr int kU = kDpl <= 4 ? 16 : 8;
   float num[kDpl];
 #pragma unroll
   for (int e = 0; e < kDpl; ++e) num[e] = 0.0f;
-  for (int s0 = 0; s0 < splits; s0 += 8) {
-    float vals[8][kDpl];
+  for (int s0 = 0; s0 < splits; s0 += kU) {
+    float vals[kU][kDpl];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int s = min(s0 + u, splits - 1);
-#pragma unroll
-      for (int e = 0; e < kDpl; ++e) vals[u][e] = base[s * (kHd + 2) + lane * kDpl + e];
+      load_f32_slice<kDpl>(base + s * (kHd + kPartPad) + lane * kDpl, vals[u]);
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < kU; ++u) {
       const int s = s0 + u;
       const float f = __shfl_sync(0xffffffffu, (s & 32) ? f1 : f0, s & 31);
       if (s < splits) {
@@ -497,7 +519,8 @@ int nqb_decode_attention_workspace_bytes(int64_t keys, int64_t tokens, int32_t q
                                          size_t *bytes) {
   if (bytes == nullptr || keys <= 0 || tokens <= 0 || q_heads <= 0 || head_dim <= 0)
     return fail(NQB_ERR_INVALID_ARGUMENT, "attention workspace query is invalid");
-  *bytes = static_cast<size_t>(tokens) * q_heads * shell::splits_for(keys, tokens) * (head_dim + 2) * sizeof(float);
+  *bytes = static_cast<size_t>(tokens) * q_heads * shell::splits_for(keys, tokens) * (head_dim + shell::kPartPad) *
+           sizeof(float);
   return ok();
 }
 
