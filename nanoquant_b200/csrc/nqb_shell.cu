@@ -418,18 +418,19 @@ __global__ void __launch_bounds__(256) gemv_bf16_kernel(const __nv_bfloat16 *w, 
     float acc[kT];
 #pragma unroll
     for (int t = 0; t < kT; ++t) acc[t] = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
     for (int64_t u = lane; u < units; u += 32) {
       const uint4 raw = __ldcs(wr + u);
       const __nv_bfloat162 *pairs = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+      const float2 f0 = __bfloat1622float2(pairs[0]), f1 = __bfloat1622float2(pairs[1]);
+      const float2 f2 = __bfloat1622float2(pairs[2]), f3 = __bfloat1622float2(pairs[3]);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(pairs[e]);
-#pragma unroll
-        for (int t = 0; t < kT; ++t) {
-          const float *xr = xs + t * cols + u * 8 + 2 * e;
-          acc[t] += f.x * xr[0] + f.y * xr[1];
-        }
+      for (int t = 0; t < kT; ++t) {
+        // x as two 16-byte shared loads (cols % 8 == 0 keeps them aligned)
+        const float4 *xv = reinterpret_cast<const float4 *>(xs + t * cols + u * 8);
+        const float4 a = xv[0], b = xv[1];
+        acc[t] += f0.x * a.x + f0.y * a.y + f1.x * a.z + f1.y * a.w + f2.x * b.x + f2.y * b.y + f3.x * b.z +
+                  f3.y * b.w;
       }
     }
 #pragma unroll
