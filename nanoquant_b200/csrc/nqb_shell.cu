@@ -28,12 +28,12 @@ __device__ __forceinline__ void store_as(void *p, int64_t i, int32_t dt, float v
   }
 }
 
-// Sum over the block (blockDim.x a multiple of 32, at most 1024 threads).
 // Lets a decode program launched as this kernel's programmatic dependent
 // (nqb_program_run_dependent) launch now and start streaming its sign words;
 // the program still waits for this kernel's completion before reading its output.
 __device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Sum over the block (blockDim.x a multiple of 32, at most 1024 threads).
 __device__ __forceinline__ float block_sum(float v, float *scratch) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -52,22 +52,55 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
 // loop step, which the in-place write-back otherwise forces).
 constexpr int kRmsVec = 8;  // float4 pieces per thread (256 threads: hidden <= 8192)
 
+// Elements i .. i + 3 of a float vector (16-byte aligned base, i % 4 == 0).
+__device__ __forceinline__ float4 load4_as_float(const void *p, int64_t i, int32_t dt) {
+  if (dt == NQB_F32) return __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i));
+  const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p) + i));
+  float2 a, b;
+  if (dt == NQB_BF16) {
+    a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.x));
+    b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.y));
+  } else {
+    a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+  }
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ void store4_as(void *p, int64_t i, int32_t dt, float4 v) {
+  if (dt == NQB_F32) {
+    *reinterpret_cast<float4 *>(static_cast<float *>(p) + i) = v;
+    return;
+  }
+  uint2 raw;
+  if (dt == NQB_BF16) {
+    *reinterpret_cast<__nv_bfloat162 *>(&raw.x) = __floats2bfloat162_rn(v.x, v.y);
+    *reinterpret_cast<__nv_bfloat162 *>(&raw.y) = __floats2bfloat162_rn(v.z, v.w);
+  } else {
+    *reinterpret_cast<__half2 *>(&raw.x) = __floats2half2_rn(v.x, v.y);
+    *reinterpret_cast<__half2 *>(&raw.y) = __floats2half2_rn(v.z, v.w);
+  }
+  *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(p) + i) = raw;
+}
+
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *delta, const void *w, int32_t w_dt,
                                                       int64_t hidden, float eps, void *out, int32_t out_dt) {
   __shared__ float scratch[32];
   allow_dependents();
   const int64_t t = blockIdx.x;
-  const bool vec = hidden % 4 == 0 && hidden <= 1024 * kRmsVec &&
-                   reinterpret_cast<uintptr_t>(h) % 16 == 0 && (delta == nullptr || reinterpret_cast<uintptr_t>(delta) % 16 == 0);
+  const bool vec = hidden % 4 == 0 && hidden <= 1024 * kRmsVec && reinterpret_cast<uintptr_t>(h) % 16 == 0 &&
+                   (delta == nullptr || reinterpret_cast<uintptr_t>(delta) % 16 == 0) &&
+                   reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
   if (vec) {
     float4 *row4 = reinterpret_cast<float4 *>(h + t * hidden);
     const float4 *d4 = delta != nullptr ? reinterpret_cast<const float4 *>(delta + t * hidden) : nullptr;
     const int n4 = static_cast<int>(hidden / 4);
-    float4 v[kRmsVec];
+    float4 v[kRmsVec], wv[kRmsVec];  // the weights load with the row, before the reduction
 #pragma unroll
     for (int j = 0; j < kRmsVec; ++j) {
       const int i = threadIdx.x + j * 256;
       v[j] = i < n4 ? row4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      wv[j] = i < n4 ? load4_as_float(w, 4 * static_cast<int64_t>(i), w_dt) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     if (d4 != nullptr) {
 #pragma unroll
@@ -90,13 +123,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *del
 #pragma unroll
     for (int j = 0; j < kRmsVec; ++j) {
       const int i = threadIdx.x + j * 256;
-      if (i < n4) {
-        const int64_t c = t * hidden + 4 * static_cast<int64_t>(i);
-        store_as(out, c, out_dt, v[j].x * r * load_as_float(w, 4 * i, w_dt));
-        store_as(out, c + 1, out_dt, v[j].y * r * load_as_float(w, 4 * i + 1, w_dt));
-        store_as(out, c + 2, out_dt, v[j].z * r * load_as_float(w, 4 * i + 2, w_dt));
-        store_as(out, c + 3, out_dt, v[j].w * r * load_as_float(w, 4 * i + 3, w_dt));
-      }
+      if (i < n4)
+        store4_as(out, t * hidden + 4 * static_cast<int64_t>(i), out_dt,
+                  make_float4(v[j].x * r * wv[j].x, v[j].y * r * wv[j].y, v[j].z * r * wv[j].z, v[j].w * r * wv[j].w));
     }
     return;
   }

@@ -56,15 +56,19 @@ def _gpu() -> torch.device:
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("delta", (False, True))
-def test_rmsnorm_kernel(delta: bool) -> None:
+@pytest.mark.parametrize(("hidden", "w_dtype", "out_dtype"), (
+    (4096, torch.bfloat16, torch.bfloat16), (4096, torch.float32, torch.float32), (1152, torch.float16, torch.float16),
+    (1150, torch.bfloat16, torch.bfloat16), (12288, torch.bfloat16, torch.float32)))
+def test_rmsnorm_kernel(delta: bool, hidden: int, w_dtype: torch.dtype, out_dtype: torch.dtype) -> None:
+    # rows of up to 8192 values (a multiple of 4) take the register path; 1150 and 12288 the loop
     from nanoquant_b200.decoder import rmsnorm
 
     dev = _gpu()
     g = torch.Generator(device=dev).manual_seed(3)
-    h = torch.randn(5, 4096, generator=g, device=dev)
-    d = torch.randn(5, 4096, generator=g, device=dev) if delta else None
-    w = (1 + 0.02 * torch.randn(4096, generator=g, device=dev)).bfloat16()
-    out = torch.empty(5, 4096, dtype=torch.bfloat16, device=dev)
+    h = torch.randn(5, hidden, generator=g, device=dev)
+    d = torch.randn(5, hidden, generator=g, device=dev) if delta else None
+    w = (1 + 0.02 * torch.randn(hidden, generator=g, device=dev)).to(w_dtype)
+    out = torch.empty(5, hidden, dtype=out_dtype, device=dev)
     ref_h = h + d if delta else h.clone()
     rmsnorm(h, d, w, 1e-6, out)
     torch.testing.assert_close(h, ref_h, rtol=0, atol=0)
