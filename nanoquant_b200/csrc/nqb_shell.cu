@@ -182,9 +182,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     dst = vcache + (static_cast<int64_t>(vh) * cache_len + position + t) * kHd;
     rope = false;
   }
-  float x[kDpl];
+  // the head's values, norm weights and cos/sin rows load together (one round trip)
+  float x[kDpl], wv[kDpl], cv[kDpl], sv[kDpl];
+  const float *c = cos_t + t * kHd;
+  const float *sn = sin_t + t * kHd;
 #pragma unroll
-  for (int j = 0; j < kDpl; ++j) x[j] = src[d0 + j];
+  for (int j = 0; j < kDpl; ++j) {
+    x[j] = src[d0 + j];
+    wv[j] = rope && w != nullptr ? load_as_float(w, d0 + j, w_dt) : 1.0f;
+    cv[j] = rope ? c[d0 + j] : 0.0f;
+    sv[j] = rope ? sn[d0 + j] : 0.0f;
+  }
   if (rope) {  // uniform over the warp
     if (w != nullptr) {
       float ss = 0.0f;
@@ -192,16 +200,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       for (int j = 0; j < kDpl; ++j) ss += x[j] * x[j];
       const float r = rsqrtf(warp_sum(ss) / static_cast<float>(kHd) + eps);
 #pragma unroll
-      for (int j = 0; j < kDpl; ++j) x[j] = x[j] * r * load_as_float(w, d0 + j, w_dt);
+      for (int j = 0; j < kDpl; ++j) x[j] = x[j] * r * wv[j];
     }
     float partner[kDpl];
 #pragma unroll
     for (int j = 0; j < kDpl; ++j) partner[j] = __shfl_xor_sync(0xffffffffu, x[j], 16);
-    const float *c = cos_t + t * kHd;
-    const float *s = sin_t + t * kHd;
     const float sign = lane < 16 ? -1.0f : 1.0f;  // rotate_half: (-x2, x1)
 #pragma unroll
-    for (int j = 0; j < kDpl; ++j) x[j] = x[j] * c[d0 + j] + sign * partner[j] * s[d0 + j];
+    for (int j = 0; j < kDpl; ++j) x[j] = x[j] * cv[j] + sign * partner[j] * sv[j];
   }
 #pragma unroll
   for (int j = 0; j < kDpl; ++j) dst[d0 + j] = __float2bfloat16_rn(x[j]);
