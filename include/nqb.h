@@ -157,9 +157,19 @@ const char *nqb_last_error(void);
  * 16 KiB hold completion counters: zero-fill the workspace once before its
  * first use; every call leaves that region zero again, so one workspace
  * serves any sequence of calls (of any layer and token count) on one stream.
- * It must not be shared by calls that may run concurrently.
+ * It must not be shared by calls that may run concurrently; after a call that
+ * overlapped another on the same workspace, or after nqb_device_status
+ * reported NQB_ERR_TIMEOUT, zero the counters again (nqb_workspace_reset).
  */
 int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, size_t *bytes);
+
+/*
+ * Zeroes the 16 KiB counter region at the start of a workspace (of nqb_linear,
+ * nqb_grouped_linear or a program run) on `stream`, with cudaMemsetAsync; no
+ * allocation.  No counterpart in the reference, which allocates its scratch
+ * per call (cuda_kernels.py:816-874).
+ */
+int nqb_workspace_reset(void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * y[tokens, m] (fp32, row-major) = layer(x[tokens, n]).
@@ -183,7 +193,9 @@ int nqb_linear(const nqb_linear_desc *layer, const void *x, int32_t x_dtype, int
  * (nqb_linear_workspace_bytes) exceeds 8 MiB are rejected with
  * NQB_ERR_WORKSPACE and launch nothing.  The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress, with that device current);
- * make that first call before any stream capture.  All calls on a device share
+ * make that first call before any stream capture.  Every call first zeroes the
+ * array's counter region on its stream (cudaMemsetAsync), so a call that gave
+ * up a bounded wait does not spoil later ones.  All calls on a device share
  * the one array, so calls that may overlap on the GPU (for example calls on
  * different streams) race: serialise them.  Allocates nothing.
  */
@@ -276,6 +288,8 @@ int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t ran
  *   to cache rows [0, keys + t) of kv head (q head / (q_heads / kv_heads))
  *   with scale head_dim^-1/2; out bf16 [tokens, q_heads * head_dim].
  *   Split-K partials go to the workspace (nqb_decode_attention_workspace_bytes).
+ *   Alignment (else NQB_ERR_ALIGNMENT): k_cache, v_cache and workspace 16
+ *   bytes; q and out head_dim / 16 bytes (8 for head_dim 128).
  * nqb_silu_mul: out[i] = silu(gate[i]) * up[i] over `count` fp32 values.
  * nqb_gemv_bf16: out[t, r] = sum_c weight[r, c] * x[t, c]; weight bf16
  *   [rows, cols] (cols a multiple of 8, at most 51200, 16-byte aligned),
@@ -378,6 +392,19 @@ int nqb_program_run_dependent(const nqb_program *program, void *workspace, size_
 int nqb_program_destroy(nqb_program *program);
 /* Launch shape of a created program: CTAs (one per SM used) and cluster size. */
 int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size);
+/*
+ * Failure-path tests.  nqb_debug_set_barrier_limit sets how many polls a
+ * program's grid barrier makes before it gives up (0 restores the default of
+ * 2^22) for later launches; nqb_program_debug_barrier_skew makes every grid
+ * barrier of later runs of `program` wait for `skew` arrivals that never come
+ * (0 turns it off).  A run with a skew gives up each barrier after the limit,
+ * reports NQB_ERR_TIMEOUT through nqb_device_status, leaves its outputs
+ * undefined and its workspace counters zero, and a later run without the skew
+ * is correct again.  No counterpart in the reference (its kernels wait on
+ * nothing).
+ */
+int nqb_debug_set_barrier_limit(uint32_t polls);
+int nqb_program_debug_barrier_skew(nqb_program *program, uint32_t skew);
 /*
  * Phase trace of the last run (trace build only, libnqb_trace.so; the normal
  * build returns NQB_ERR_UNSUPPORTED): SM cycles per [cta][stage][phase] spent

@@ -170,6 +170,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                             _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
     "nqb_silu_mul": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _i32, _c_void_p]),
     "nqb_gemv_bf16": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
+    "nqb_workspace_reset": (ctypes.c_int, [_c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_debug_set_barrier_limit": (ctypes.c_int, [ctypes.c_uint32]),
+    "nqb_program_debug_barrier_skew": (ctypes.c_int, [_c_void_p, ctypes.c_uint32]),
 }
 
 _lock = threading.Lock()

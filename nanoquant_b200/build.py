@@ -16,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PACKAGE_DIR = Path(__file__).resolve().parent
@@ -74,9 +75,13 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
     obj_dir = LIB_DIR / ("obj_trace" if trace else "obj")
     obj_dir.mkdir(parents=True, exist_ok=True)
     defines = ["-DNQB_PHASE_TRACE"] if trace else []
-    objects = []
-    for source in _sources():
+    headers = sorted(SOURCE_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
+    newest_header = max((h.stat().st_mtime for h in headers), default=0.0)
+
+    def compile_one(source: Path) -> str:
         obj = obj_dir / (source.stem + ".o")
+        if not force and obj.exists() and obj.stat().st_mtime > max(source.stat().st_mtime, newest_header):
+            return str(obj)  # up to date (incremental rebuild)
         cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, *defines, "-I", str(INCLUDE_DIR), "-c", str(source), "-o", str(obj)]
         result = subprocess.run(cmd, capture_output=True, text=True)
         if result.returncode != 0:
@@ -84,7 +89,11 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
         if verbose:
             sys.stderr.write(result.stderr)
         (obj_dir / (source.stem + ".ptxas.txt")).write_text(result.stderr)
-        objects.append(str(obj))
+        return str(obj)
+
+    # the translation units are independent: compile them in parallel
+    with ThreadPoolExecutor(max_workers=max(1, min(len(_sources()), os.cpu_count() or 1))) as pool:
+        objects = list(pool.map(compile_one, _sources()))
     tmp = target.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objects]
     result = subprocess.run(cmd, capture_output=True, text=True)

@@ -278,6 +278,14 @@ int nqb_abi_version(void) { return NQB_ABI_VERSION; }
 
 const char *nqb_last_error(void) { return g_last_error; }
 
+int nqb_workspace_reset(void *workspace, size_t workspace_bytes, void *stream) {
+  if (workspace == nullptr || workspace_bytes < kCounterRegionBytes)
+    return fail(NQB_ERR_WORKSPACE, "workspace must hold at least the %zu-byte counter region", kCounterRegionBytes);
+  NQB_CUDA(cudaMemsetAsync(workspace, 0, kCounterRegionBytes, static_cast<cudaStream_t>(stream)),
+           "zeroing the workspace counters");
+  return ok();
+}
+
 int nqb_linear_workspace_bytes(const nqb_linear_desc *layer, int64_t tokens, size_t *bytes) {
   NQB_CHECK(validate_layer(layer, "layer"));
   if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");

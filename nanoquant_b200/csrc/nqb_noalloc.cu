@@ -11,6 +11,7 @@
 #include <mutex>
 
 #include "nqb_common.cuh"
+#include "nqb_decode_tc.cuh"
 
 namespace {
 
@@ -59,8 +60,13 @@ extern "C" int nqb_linear_noalloc(const nqb_linear_desc *layer, const void *x, i
                      needed, kNoAllocScratchBytes);
   void *scratch = nullptr;
   NQB_CHECK(scratch_address(&scratch));
-  // The shared array is handed over as nqb_linear's workspace; that path
-  // zeroes (on the stream) the only part that must start at zero, its
-  // completion counters, and overwrites the rest before reading it.
+  // The shared array is handed over as nqb_linear's workspace.  Its first
+  // kCounterRegionBytes hold completion counters that must be zero when a call
+  // starts; nqb_linear leaves them zero, but a call that overlapped another one
+  // on the GPU or gave up a bounded wait may not have, and no caller can reach
+  // this array to repair it.  So every call zeroes them first, on its stream
+  // (a memset, no allocation); the rest of the array is written before it is read.
+  NQB_CUDA(cudaMemsetAsync(scratch, 0, nqb::kCounterRegionBytes, static_cast<cudaStream_t>(stream)),
+           "zeroing the no-alloc scratch counters");
   return nqb_linear(layer, x, x_dtype, tokens, y, scratch, kNoAllocScratchBytes, stream);
 }

@@ -30,10 +30,15 @@
 //   the barrier, so an op may consume an earlier op's output.  The producer
 //   warp never joins a barrier: cluster exchanges use mbarriers with remote
 //   arrivals, CTA-wide steps a named barrier of the consumer warps.
-// Every wait is bounded; a timeout sets the device status word and every
-// later grid barrier gives up at once, so a failed run ends (with wrong
-// results and NQB_ERR_TIMEOUT) instead of hanging.
+// Every wait is bounded.  Only the grid barriers depend on other clusters:
+// when one gives up, it sets the device status word and every later grid
+// barrier gives up at once, so a failed run ends (with wrong results and
+// NQB_ERR_TIMEOUT) instead of hanging.  The CTA-local and cluster waits (sign
+// copies, stage tables, partial-sum exchange) always complete, so they do not
+// give up early: a failed run still consumes every slice it copied and keeps
+// its stage tables consistent, and no copy is in flight when a CTA exits.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -54,7 +59,7 @@ constexpr int kMaxRing = 48;            // ring slots (4 KB each)
 constexpr int kAddrChunk = 64;          // slice addresses per bulk copy
 constexpr int kAddrSlots = 4;           // address chunks in flight
 constexpr uint32_t kSpinLimit = 1u << 22;
-constexpr uint32_t kBarrierSpinLimit = 1u << 22;  // polls of the grid-barrier counter
+constexpr uint32_t kBarrierSpinLimit = 1u << 22;  // default polls of the grid-barrier counter
 constexpr int kMaxDynamicSmem = 220 * 1024;  // + static shared memory <= 227 KB
 // Coded mixed-V slices (nqb_repack_mixed_v): 128 rows x 8 20-bit records
 // (codebook index | a << 10 | b << 15), row r's from bit 160 r; a member's
@@ -141,6 +146,8 @@ struct Params {
   const int32_t *pf_begin;      // [stages * ctas + 1]
   float *latent;
   uint32_t *counters;           // [0] grid barrier arrivals, [1] finished clusters
+  uint32_t barrier_limit;       // polls before a grid barrier gives up
+  uint32_t barrier_skew;        // added to every barrier target (tests: a barrier that cannot complete)
   int32_t tokens;
   int32_t ring;                 // ring slots
   int32_t sc;                   // slices quantised at once
@@ -207,20 +214,18 @@ __device__ __forceinline__ bool program_failed() { return *reinterpret_cast<vola
 __device__ __forceinline__ bool wait_local_backoff(uint64_t *bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && program_failed()) return false;
     __nanosleep(32);
   }
   record_error(NQB_ERR_TIMEOUT);
   return false;
 }
 
-// Bounded wait for phase `parity` of a CTA-local mbarrier.  On timeout it
-// records NQB_ERR_TIMEOUT at once; every wait gives up early once any wait
-// of the program has failed, so a failed run ends quickly.
+// Bounded wait for phase `parity` of a CTA-local mbarrier; on timeout it
+// records NQB_ERR_TIMEOUT.  The phases it waits for are completed by this CTA
+// (or by its copies), so it never gives up early.
 __device__ __forceinline__ bool wait_local(uint64_t *bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023) == 1023 && program_failed()) return false;
   }
   record_error(NQB_ERR_TIMEOUT);
   return false;
@@ -295,7 +300,6 @@ __device__ __forceinline__ bool wait_cluster(uint64_t *bar, uint32_t parity) {
         : "r"(ptx::smem_u32(bar)), "r"(parity)
         : "memory");
     if (done) return true;
-    if ((i & 1023) == 1023 && program_failed()) return false;
   }
   record_error(NQB_ERR_TIMEOUT);
   return false;
@@ -335,10 +339,10 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *ptr) {
   return v;
 }
 
-// Until the grid-barrier counter reaches `target`; false after a bounded
-// number of polls (or at once when another wait has failed).
-__device__ __forceinline__ bool wait_counter(const uint32_t *counter, uint32_t target) {
-  for (uint32_t polls = 0; polls < kBarrierSpinLimit; ++polls) {
+// Until the grid-barrier counter reaches `target`; false after `limit` polls
+// (or at once when a grid barrier has failed).
+__device__ __forceinline__ bool wait_counter(const uint32_t *counter, uint32_t target, uint32_t limit) {
+  for (uint32_t polls = 0; polls < limit; ++polls) {
     if (ld_acquire_gpu(counter) >= target) return true;
     if (program_failed()) return false;
     __nanosleep(64);
@@ -374,20 +378,22 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
 }
 
 // Grid barrier number `index` over every CTA of the grid (consumer warps;
-// thread 0 adds and polls).
-__device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index) {
+// thread 0 adds and polls).  On entry every consumer is done with the stage's
+// tables: thread 0 first hands their buffer back (`info_free`).
+__device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index, uint64_t *info_free) {
   uint32_t *counter = p.counters;
   const uint32_t ctas = gridDim.x;
   mmad::consumer_sync();
   if (threadIdx.x == 0) {
+    mbar_arrive_cta(info_free);
     // release: this CTA's stores (ordered before this thread by the named
     // barrier) are visible to every CTA that acquires the count
     red_release_gpu_add(counter, 1);
-    const uint32_t target = (index + 1) * ctas;
+    const uint32_t target = (index + 1) * ctas + p.barrier_skew;
     uint32_t polls = 0;
     while (ld_acquire_gpu(counter) < target) {
       if (program_failed()) break;
-      if (++polls > kBarrierSpinLimit) {
+      if (++polls > p.barrier_limit) {
         record_error(NQB_ERR_TIMEOUT);
         break;
       }
@@ -542,6 +548,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   __shared__ uint64_t s_x_full;  // this CTA's leader buffers hold every quarter (own expect_tx + st.async bytes)
   __shared__ uint64_t s_x_free;  // every leader has read this CTA's quarters (one arrival per leader)
   __shared__ uint64_t s_info_full[2];  // s_info[b] holds the next stage of parity b
+  __shared__ uint64_t s_info_free[2];  // the consumers are done with s_info[b]'s stage
   __shared__ StageInfo s_info[2];
   __shared__ mmad::Scratch<kT> s_sc;
   __shared__ float s_red_f[mmad::kWarps];
@@ -572,6 +579,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     ptx::mbar_init(&s_x_free, kClusterSize);
     ptx::mbar_init(&s_info_full[0], 1);
     ptx::mbar_init(&s_info_full[1], 1);
+    ptx::mbar_init(&s_info_free[0], 1);
+    ptx::mbar_init(&s_info_free[1], 1);
     ptx::mbar_init(&s_patch_done, 1);
     ptx::fence_mbar_init();
   }
@@ -618,7 +627,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     // latents (stage g - 1's inputs are complete once stage g - 2 is)
     for (int g = 0; g < p.stages; ++g) {
       if (g >= 2) {
-        if (lane == 0 && !wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x)) ok = false;
+        // stage g - 2 (the buffer's previous user) finished everywhere, so
+        // stage g - 1's inputs are complete; then, even when that grid wait
+        // gave up, this CTA's consumers are done with the buffer
+        if (lane == 0) {
+          if (!wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x + p.barrier_skew, p.barrier_limit))
+            ok = false;
+          if (!wait_local(&s_info_free[g & 1], ((g >> 1) - 1) & 1)) ok = false;
+        }
         __syncwarp();
       }
       stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
@@ -996,7 +1012,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           ++patched;
         }
       }
-      if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g));
+      if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g), &s_info_free[g & 1]);
       NQB_TRACE(kTraceGridBarrier);
       NQB_TRACE_FLUSH(g);
     }
@@ -1042,6 +1058,7 @@ struct nqb_program {
   int smem = 0;
   void *arena = nullptr;
   size_t latent_bytes = 0;
+  uint32_t barrier_skew = 0;  // tests only: extra arrivals every grid barrier waits for
   prog::Params params{};
 };
 
@@ -1530,6 +1547,10 @@ int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes) {
 namespace nqb {
 namespace prog {
 
+// Grid-barrier poll limit of the next launches (0: kBarrierSpinLimit); tests
+// shorten it to make a barrier that cannot complete give up quickly.
+static std::atomic<uint32_t> g_barrier_limit{0};
+
 static int launch_program(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream,
                           bool dependent) {
   if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
@@ -1539,6 +1560,9 @@ static int launch_program(const nqb_program *program, void *workspace, size_t wo
   Params params = program->params;
   params.counters = static_cast<uint32_t *>(workspace);
   params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
+  const uint32_t limit = g_barrier_limit.load();
+  params.barrier_limit = limit != 0 ? limit : kBarrierSpinLimit;
+  params.barrier_skew = program->barrier_skew;
   const void *fn = kernel_for(program->bucket, program->patch, program->mixed);
   NQB_CHECK(ensure_dynamic_smem(fn, program->smem));
   cudaLaunchConfig_t config;
@@ -1607,6 +1631,17 @@ int nqb_program_trace(const nqb_program *program, int64_t *cycles, size_t count)
   (void)count;
   return fail(NQB_ERR_UNSUPPORTED, "phase tracing needs the trace build (python -m nanoquant_b200.build --trace)");
 #endif
+}
+
+int nqb_debug_set_barrier_limit(uint32_t polls) {
+  nqb::prog::g_barrier_limit.store(polls);
+  return ok();
+}
+
+int nqb_program_debug_barrier_skew(nqb_program *program, uint32_t skew) {
+  if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
+  program->barrier_skew = skew;
+  return ok();
 }
 
 int nqb_program_shape(const nqb_program *program, int32_t *ctas, int32_t *cluster_size) {

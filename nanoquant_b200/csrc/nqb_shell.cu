@@ -568,6 +568,13 @@ int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache
   if (tokens <= 0 || keys <= 0 || keys + tokens - 1 > cache_len || kv_heads <= 0 || q_heads % kv_heads != 0 ||
       q_heads / kv_heads > 32)
     return fail(NQB_ERR_INVALID_ARGUMENT, "attention shape invalid (keys, cache length or head grouping)");
+  // 16-byte cp.async of cache rows and vector loads of q and of the partials
+  const uintptr_t q_align = static_cast<uintptr_t>(head_dim / 32) * 2;
+  if (reinterpret_cast<uintptr_t>(k_cache) % 16 || reinterpret_cast<uintptr_t>(v_cache) % 16 ||
+      reinterpret_cast<uintptr_t>(workspace) % 16 ||
+      (q_align > 1 && (reinterpret_cast<uintptr_t>(q) % q_align || reinterpret_cast<uintptr_t>(out) % q_align)))
+    return fail(NQB_ERR_ALIGNMENT, "attention caches and workspace need 16-byte alignment, q and out %zu-byte alignment",
+                static_cast<size_t>(q_align));
   size_t need = 0;
   NQB_CHECK(nqb_decode_attention_workspace_bytes(keys, tokens, q_heads, head_dim, &need));
   if (workspace_bytes < need) return fail(NQB_ERR_WORKSPACE, "attention workspace too small");

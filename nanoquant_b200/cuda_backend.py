@@ -16,7 +16,7 @@ The grouped-projection helpers mirror ``prepare_cuda_projection_group`` and
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass
+from dataclasses import dataclass, fields
 
 import torch
 
@@ -25,6 +25,7 @@ from nanoquant_b200.backend import (
     BackendCapabilities,
     DeviceLike,
     PreparedLayer,
+    ProjectionMemberSpec,
     QuantizedLinearSpec,
     RuntimeLayerState,
     SupportResult,
@@ -180,6 +181,43 @@ def _build_payload(
     return _Sm100Payload(device, tensors, desc, patch_left, patch_right)
 
 
+def _adopt_spec(spec) -> QuantizedLinearSpec:
+    """This package's spec with the fields of ``spec`` (an instance of the reference's equal dataclass)."""
+
+    if isinstance(spec, QuantizedLinearSpec):
+        return spec
+    values = {f.name: getattr(spec, f.name) for f in fields(QuantizedLinearSpec)}
+    values["members"] = tuple(ProjectionMemberSpec(m.name, m.row_start, m.row_end) for m in values["members"])
+    return QuantizedLinearSpec(**values)
+
+
+_ADOPTABLE = {cls.__name__: cls for cls in (PackedLayerState, MixedVLayerState, ProductCodebookLayerState)}
+
+
+def adopt_layer_state(state: object) -> object:
+    """The reference runtime's own layer states as this package's equal types.
+
+    The reference loader (``packed_artifact.py:196-223``) and planner
+    (``planning.py:234-260``) hand ``prepare`` instances of
+    ``nanoquant.runtime``'s ``PackedLayerState``, ``MixedVLayerState`` and
+    ``ProductCodebookLayerState``; their fields are the ones this package's
+    classes declare (same names, meanings and tensor layouts), so such a state
+    is rebuilt field by field, through this package's validation.  Other
+    objects are returned unchanged.
+    """
+
+    target = _ADOPTABLE.get(type(state).__name__)
+    if target is None or isinstance(state, target):
+        return state
+    try:
+        values = {f.name: getattr(state, f.name) for f in fields(target)}
+    except AttributeError as error:
+        raise TypeError(f"{type(state).__module__}.{type(state).__name__} lacks a field of {target.__name__}: "
+                        f"{error}") from error
+    values["spec"] = _adopt_spec(values["spec"])
+    return target(**values)
+
+
 def _cuda_device(device: DeviceLike) -> torch.device:
     target = torch.device(device)
     if target.type != "cuda":
@@ -241,11 +279,22 @@ def kernel_path(layer: PreparedLayer, tokens: int, input_dtype: torch.dtype = to
     return {_native.NQB_PATH_TENSOR_CORE: "tensor-core", _native.NQB_PATH_PREFILL: "prefill"}.get(path.value, "generic")
 
 
-def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLinearSpec) -> torch.Tensor:
-    """Run one prepared layer on ``value`` (any leading shape) and return fp32 ``[..., out]``."""
+def packed_linear(value: torch.Tensor, payload: _Sm100Payload, spec: QuantizedLinearSpec,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Run one prepared layer on ``value`` (any leading shape) and return fp32 ``[..., out]``.
+
+    ``out``, when given, is a contiguous fp32 tensor of ``tokens * out_features``
+    elements on the same device that receives the result (no allocation).
+    """
 
     tokens = value.numel() // spec.in_features
-    output = torch.empty((*value.shape[:-1], spec.out_features), dtype=torch.float32, device=value.device)
+    if out is None:
+        output = torch.empty((*value.shape[:-1], spec.out_features), dtype=torch.float32, device=value.device)
+    else:
+        if (out.dtype != torch.float32 or not out.is_contiguous() or out.device != value.device
+                or out.numel() != tokens * spec.out_features):
+            raise ValueError("out must be a contiguous fp32 tensor of tokens * out_features elements on x's device")
+        output = out
     needed = ctypes.c_size_t(0)
     desc_ref = ctypes.byref(payload.desc)
     _native.call("nqb_linear_workspace_bytes", desc_ref, tokens, ctypes.byref(needed))
@@ -316,10 +365,18 @@ class CudaPackedSm100Backend:
         return result
 
     def prepare(self, state: RuntimeLayerState, device: DeviceLike) -> PreparedLayer:
+        """Copy ``state`` to ``device`` and build the kernel-native tiles.
+
+        Accepts this package's layer states and the reference runtime's own
+        (adopted field by field, :func:`adopt_layer_state`); the returned
+        layer carries ``state.spec`` itself, so the reference planner's
+        ``layer.spec == state.spec`` check holds (``planning.py:251-253``).
+        """
+
         overlay = None
-        base = state
-        if isinstance(state, OverlaidLayerState):
-            base, overlay = state.base, state.overlay
+        base = adopt_layer_state(state)
+        if isinstance(base, OverlaidLayerState):
+            base, overlay = adopt_layer_state(base.base), base.overlay
         if not isinstance(base, (PackedLayerState, ProductCodebookLayerState, MixedVLayerState)):
             raise TypeError(
                 "sm100a packed backend requires PackedLayerState, MixedVLayerState, "
@@ -338,6 +395,16 @@ class CudaPackedSm100Backend:
             raise TypeError("prepared runtime layer has an invalid sm100a packed payload")
         _check_input(value, layer.spec, layer.payload.device)
         return packed_linear(value, layer.payload, layer.spec)
+
+    def linear_into(self, value: torch.Tensor, layer: PreparedLayer, out: torch.Tensor) -> torch.Tensor:
+        """:meth:`linear` writing into ``out`` (contiguous fp32, ``tokens * out_features`` elements)."""
+
+        if layer.backend_name != self.name or layer.backend_version != self.version:
+            raise ValueError("prepared runtime layer belongs to a different backend")
+        if not isinstance(layer.payload, _Sm100Payload):
+            raise TypeError("prepared runtime layer has an invalid sm100a packed payload")
+        _check_input(value, layer.spec, layer.payload.device)
+        return packed_linear(value, layer.payload, layer.spec, out)
 
 
 @dataclass(frozen=True, slots=True)
@@ -424,6 +491,7 @@ __all__ = [
     "CUDA_SM100_BACKEND_VERSION",
     "CudaPackedSm100Backend",
     "Sm100ProjectionGroup",
+    "adopt_layer_state",
     "grouped_cuda_projection",
     "grouped_sm100_projection",
     "kernel_path",

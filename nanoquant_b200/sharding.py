@@ -56,15 +56,18 @@ def row_range(out_features: int, world: int, rank: int, multiple: int = TILE_ROW
 
 
 def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLayerState | MixedVLayerState,
-               start: int, stop: int) -> PackedLayerState | OverlaidLayerState:
+               start: int, stop: int, *, pad_to: int | None = None) -> PackedLayerState | OverlaidLayerState:
     """The layer restricted to output rows ``[start, stop)`` (stage 1 unchanged).
 
     Product-codebook and mixed-V layers are decoded to layout v1 first (their
-    V is the stage-1 factor, kept whole; only U rows are sliced).
+    V is the stage-1 factor, kept whole; only U rows are sliced).  With
+    ``pad_to`` the shard gets ``pad_to - (stop - start)`` extra rows of zero
+    words and zero scale, bias, salient and patch weights, which compute
+    exactly 0; ``start == stop`` is then allowed (a rank without rows).
     """
 
     if isinstance(state, OverlaidLayerState):
-        base = shard_rows(state.base, start, stop)
+        base = shard_rows(state.base, start, stop, pad_to=pad_to)
         assert isinstance(base, PackedLayerState)
         ids = state.overlay.row_ids.to(torch.int64)
         keep = (ids >= start) & (ids < stop)
@@ -78,14 +81,21 @@ def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLay
     if not isinstance(state, PackedLayerState):
         raise TypeError("shard_rows takes packed, mixed-V, product-codebook or overlaid layers")
     spec = state.spec
-    if not 0 <= start < stop <= spec.out_features:
+    rows_out = stop - start if pad_to is None else pad_to
+    if not 0 <= start <= stop <= spec.out_features or rows_out < stop - start or rows_out <= 0:
         raise ValueError("row shard must be a non-empty range inside the output rows")
+    extra = rows_out - (stop - start)
 
     def rows(value: torch.Tensor | None) -> torch.Tensor | None:
-        return None if value is None else value[start:stop].contiguous()
+        if value is None:
+            return None
+        part = value[start:stop]
+        if extra:
+            part = torch.cat((part, torch.zeros((extra, *value.shape[1:]), dtype=value.dtype, device=value.device)))
+        return part.contiguous()
 
     return PackedLayerState(
-        replace(spec, out_features=stop - start),
+        replace(spec, out_features=rows_out),
         state.layout,
         rows(state.left_words),
         state.right_words,
@@ -101,12 +111,48 @@ def shard_rows(state: PackedLayerState | OverlaidLayerState | ProductCodebookLay
     )
 
 
+class RowShardWork:
+    """An all-gather of one :class:`RowShardedLinear` call in flight.
+
+    ``wait()`` orders the caller's current stream after the gather (on CUDA; on
+    the CPU the gather has already finished); ``result()`` waits and returns
+    the full ``[..., out_features]`` output.
+    """
+
+    def __init__(self, owner: "RowShardedLinear", buffer: torch.Tensor, lead: tuple[int, ...], event, work) -> None:
+        self.owner, self.buffer, self.lead, self.event, self.work = owner, buffer, lead, event, work
+
+    def wait(self) -> torch.Tensor:
+        """Waits for the gather; returns the gathered ``[world, tokens, width]`` buffer (no copy)."""
+
+        if self.event is not None:
+            torch.cuda.current_stream(self.buffer.device).wait_event(self.event)
+        elif self.work is not None:
+            self.work.wait()
+        return self.buffer
+
+    def result(self) -> torch.Tensor:
+        gathered = self.wait()
+        world, tokens, width = gathered.shape
+        m = self.owner.out_features
+        if tokens == 1:  # decode: the rank slots already sit in output order
+            flat = gathered.view(1, world * width)[:, :m]
+        else:  # one transposing copy: rank-major slots -> token-major rows
+            flat = gathered.permute(1, 0, 2).reshape(tokens, world * width)[:, :m]
+        return flat.reshape(*self.lead, m)
+
+
 class RowShardedLinear:
     """One packed linear split over the ranks of ``group`` by U rows.
 
-    ``backend`` prepares this rank's shard on ``device``; calling the object
-    runs the local linear and all-gathers the fp32 slices into the full
-    ``[..., out_features]`` output (identical on every rank).
+    Every rank runs stage 1 in full and stage 2 on its whole 128-row tiles of
+    U, padded with zero rows to the widest rank's row count, so each rank's
+    slice of the output has one shape.  The local slice is written straight
+    into this rank's slot of a preallocated ``[world, tokens, width]`` buffer,
+    and one in-place ``all_gather_into_tensor`` fills the other slots; on CUDA
+    the gather runs on a side stream, so :meth:`start` returns while it is in
+    flight and the caller's next kernels overlap it.  Calling the object runs
+    :meth:`start` and returns the full output (identical on every rank).
     """
 
     def __init__(self, backend, state, device: torch.device | str, *, group=None, world: int | None = None,
@@ -121,21 +167,49 @@ class RowShardedLinear:
         self.width = max(stop - start for start, stop in self.ranges)
         start, stop = self.ranges[self.rank]
         self.backend = backend
-        self.local: PreparedLayer | None = (backend.prepare(shard_rows(state, start, stop), device)
-                                            if stop > start else None)
+        self.local: PreparedLayer = backend.prepare(shard_rows(state, start, stop, pad_to=self.width), device)
         self.device = torch.device(device)
+        self._buffers: dict[int, torch.Tensor] = {}
+        self._stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
-    def __call__(self, value: torch.Tensor) -> torch.Tensor:
+    def buffer(self, tokens: int) -> torch.Tensor:
+        """The gather buffer ``[world, tokens, width]`` for ``tokens`` tokens (kept across calls)."""
+
+        buf = self._buffers.get(tokens)
+        if buf is None:
+            buf = torch.empty((self.world, tokens, self.width), dtype=torch.float32, device=self.device)
+            self._buffers[tokens] = buf
+        return buf
+
+    def start(self, value: torch.Tensor) -> RowShardWork:
+        """Local rows into this rank's slot, then the all-gather (asynchronous on CUDA)."""
+
         import torch.distributed as dist
 
-        lead = value.shape[:-1]
-        start, stop = self.ranges[self.rank]
-        padded = torch.zeros((*lead, self.width), dtype=torch.float32, device=value.device)
-        if self.local is not None:
-            padded[..., : stop - start] = self.backend.linear(value, self.local)
-        parts = [torch.empty_like(padded) for _ in range(self.world)]
-        dist.all_gather(parts, padded, group=self.group)
-        return torch.cat([part[..., : hi - lo] for part, (lo, hi) in zip(parts, self.ranges)], dim=-1)
+        lead = tuple(value.shape[:-1])
+        tokens = value.numel() // value.shape[-1]
+        buf = self.buffer(tokens)
+        slot = buf[self.rank]
+        linear_into = getattr(self.backend, "linear_into", None)
+        if linear_into is not None:
+            linear_into(value.reshape(tokens, value.shape[-1]), self.local, slot)
+        else:
+            slot.copy_(self.backend.linear(value, self.local).reshape(tokens, self.width))
+        if self._stream is None:
+            work = dist.all_gather_into_tensor(buf.view(-1), slot.reshape(-1), group=self.group, async_op=True)
+            work.wait()
+            return RowShardWork(self, buf, lead, None, None)
+        current = torch.cuda.current_stream(self.device)
+        self._stream.wait_stream(current)
+        with torch.cuda.stream(self._stream):
+            dist.all_gather_into_tensor(buf.view(-1), slot.reshape(-1), group=self.group)
+            done = torch.cuda.Event()
+            done.record(self._stream)
+        buf.record_stream(self._stream)
+        return RowShardWork(self, buf, lead, done, None)
+
+    def __call__(self, value: torch.Tensor) -> torch.Tensor:
+        return self.start(value).result()
 
 
-__all__ = ["RowShardedLinear", "TILE_ROWS", "row_range", "shard_rows", "token_range"]
+__all__ = ["RowShardWork", "RowShardedLinear", "TILE_ROWS", "row_range", "shard_rows", "token_range"]

@@ -176,3 +176,32 @@ def test_prepare_refuses_cpu_device() -> None:
                              case["scale_pre"], case["scale_mid"], case["scale_post"])
     with pytest.raises(ValueError, match="requires a CUDA device"):
         CudaPackedSm100Backend().prepare(state, "cpu")
+
+
+@pytest.mark.parametrize(
+    "q, k, v, out, workspace",
+    [
+        (0x10004, 0x20000, 0x30000, 0x40000, 0x50000),  # q 4-byte aligned, head_dim 128 needs 8
+        (0x10000, 0x20008, 0x30000, 0x40000, 0x50000),  # k cache 8-byte aligned, needs 16
+        (0x10000, 0x20000, 0x30008, 0x40000, 0x50000),  # v cache
+        (0x10000, 0x20000, 0x30000, 0x40002, 0x50000),  # out
+        (0x10000, 0x20000, 0x30000, 0x40000, 0x50004),  # workspace
+    ],
+)
+def test_decode_attention_rejects_misaligned_operands(q, k, v, out, workspace) -> None:
+    status, message = _status("nqb_decode_attention", q, k, v, 4096, 2049, 1, 32, 8, 128, out, workspace,
+                              1 << 24, None)
+    assert status == _native.NQB_ERR_ALIGNMENT, message
+    assert "alignment" in message
+
+
+def test_workspace_reset_needs_the_counter_region() -> None:
+    status, message = _status("nqb_workspace_reset", 0x10000, 1024, None)
+    assert status == _native.NQB_ERR_WORKSPACE, message
+    status, message = _status("nqb_workspace_reset", None, 1 << 20, None)
+    assert status == _native.NQB_ERR_WORKSPACE, message
+
+
+def test_debug_barrier_skew_rejects_a_null_program() -> None:
+    status, _ = _status("nqb_program_debug_barrier_skew", None, 1)
+    assert status == _native.NQB_ERR_INVALID_ARGUMENT

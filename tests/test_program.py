@@ -174,3 +174,53 @@ def test_program_swiglu_input_rejects_salient_columns_and_bad_x2() -> None:
         DecodeProgram([ProgramOp((plain,), gate.bfloat16(), x2=up.bfloat16())])
     with pytest.raises(ValueError, match="shaped like x"):
         DecodeProgram([ProgramOp((plain,), gate, x2=torch.zeros(2, 1024, device="cuda"))])
+
+
+def _device_status() -> int:
+    import ctypes
+
+    status = ctypes.c_int32(-1)
+    _native.call("nqb_device_status", ctypes.byref(status))
+    return status.value
+
+
+def test_program_grid_barrier_timeout_is_reported_and_recovered() -> None:
+    """A grid barrier that cannot complete gives up, reports NQB_ERR_TIMEOUT and leaves the program reusable.
+
+    The failure is made on the host: every barrier of the skewed run waits for
+    one arrival more than the grid has CTAs, with a short poll limit, so each
+    gives up after its limit instead of hanging.  The run's outputs are
+    undefined; its workspace counters must be zero afterwards, and the next run
+    on the same workspace must equal the run before it bit for bit.
+    """
+
+    backend = CudaPackedSm100Backend()
+    states = [_random_state(1152, 6912, 987, seed=70 + i) for i in range(2)]
+    down_state = _random_state(6912, 1152, 987, seed=72, bias=True)
+    gate_up = tuple(backend.prepare(s, "cuda") for s in states)
+    down = backend.prepare(down_state, "cuda")
+    x = torch.randn(1, 1152, generator=torch.Generator().manual_seed(7)).bfloat16().cuda()
+    gate = torch.empty(1, 6912, device="cuda")
+    program = DecodeProgram([ProgramOp(gate_up, x), ProgramOp((down,), gate)],
+                            outputs=[(gate, torch.empty(1, 6912, device="cuda")), (torch.empty(1, 1152, device="cuda"),)])
+    assert _device_status() == _native.NQB_OK
+    before = [t.clone() for op in program.run() for t in op]
+    torch.cuda.synchronize()
+    assert _device_status() == _native.NQB_OK
+
+    _native.call("nqb_debug_set_barrier_limit", 1 << 12)
+    _native.call("nqb_program_debug_barrier_skew", program._handle, 1)
+    try:
+        program.run()
+        torch.cuda.synchronize()
+        assert _device_status() == _native.NQB_ERR_TIMEOUT
+        assert int(program.workspace[:16384].count_nonzero()) == 0
+    finally:
+        _native.call("nqb_program_debug_barrier_skew", program._handle, 0)
+        _native.call("nqb_debug_set_barrier_limit", 0)
+
+    after = [t.clone() for op in program.run() for t in op]
+    torch.cuda.synchronize()
+    assert _device_status() == _native.NQB_OK
+    for a, b in zip(before, after):
+        assert torch.equal(a, b)

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import os
 import socket
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -167,6 +168,43 @@ def test_row_shard_and_token_batches_over_two_gloo_ranks(tmp_path) -> None:
         out = torch.load(tmp_path / f"rank{rank}.pt")
         torch.testing.assert_close(out["rows"], full, rtol=0, atol=1e-6)
         torch.testing.assert_close(out["tokens"], full, rtol=0, atol=1e-6)
+
+
+def _absent_rank_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    """Rank 1 never joins the row-shard all-gather; rank 0's call must end with an error, not hang."""
+
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    outcome = "absent"
+    try:
+        state = _state(96, 300, 40, seed=3)
+        sharded = RowShardedLinear(OracleBackend(), state, "cpu")
+        if rank == 0:
+            start = time.monotonic()
+            try:
+                sharded(torch.randn(2, 96, generator=torch.Generator().manual_seed(5)))
+                outcome = "returned"
+            except RuntimeError as error:
+                outcome = f"raised after {time.monotonic() - start:.1f}s: {type(error).__name__}"
+        else:
+            time.sleep(8.0)  # stays alive but never calls the collective
+    finally:
+        (Path(result_dir) / f"rank{rank}.txt").write_text(outcome)
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(180)
+def test_row_shard_gather_times_out_when_a_rank_never_joins(tmp_path) -> None:
+    world = 2
+    mp.spawn(_absent_rank_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    outcome = (tmp_path / "rank0.txt").read_text()
+    assert outcome.startswith("raised after"), outcome
+    assert float(outcome.split()[2].rstrip("s:")) < 30.0
+    assert (tmp_path / "rank1.txt").read_text() == "absent"
 
 
 if __name__ == "__main__":  # pragma: no cover
