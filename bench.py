@@ -1,21 +1,37 @@
-"""Benchmark: decode tokens/s through all packed linears of a Qwen3-8B-shaped decoder (bs1).
+"""Benchmark of NanoQuant's packed binary low-rank linear on B200: one JSON line.
 
-One step = one decode token (batch 1, Qwen3-8B shape) through the 36
-layers x {q,k,v,o,gate,up,down} packed binary low-rank linears at ~1 bpw,
-with the grouped QKV and gate/up calls of the reference's model shell, run as
-one persistent decode program (a grid barrier between every stage, so the
-calls stay strictly ordered); ``--engine calls`` runs the per-call kernels
-captured in one CUDA graph instead.  Weights are random layout-v1 words (875 MB, larger than
-the 126 MB L2, so no L2 flush is needed between steps); activations are
-synthetic bf16 N(0,1).
+Default workload ``decode`` (the metric's own config): one
+decode token (batch 1) through the full Qwen3-8B-shaped decoder step -- 36
+layers of RMSNorm, packed q/k/v/o/gate/up/down projections at ~1 bpw (layout
+v1 words, fp16 scales), q/k norm + RoPE, grouped-query attention over 2048
+cached bf16 tokens, SwiGLU, the final norm and the 151936 x 4096 bf16 lm
+head -- replayed from one CUDA graph.  Weights are random (2.4 GB per step,
+larger than the 126 MB L2, so no L2 flush is needed); inputs are synthetic.
 
-Prints one JSON line (rank 0).  ``--impl reference`` times the CPU oracle
-(the reference's packed CPU algorithm restated in numpy) on a bounded sample
-of the same workload on the host cores instead.
+The same line carries:
+* ``roofline`` for the dominant kernel, the persistent decode program that
+  runs the packed linears: the step's 252 packed linears as one program
+  launch, timed with CUDA events (algorithmic bytes per launch / launch time);
+  ``step_roofline`` is the whole step's bytes over the step time;
+* ``e2e``: the same step through the public API with the token's hidden
+  state copied in from pinned host memory and the logits copied back;
+* ``cpu_baseline``: the reference's CPU path for the same step (the oracle
+  port of ``PackedReferenceBackend`` and the model shell) on the host cores;
+* ``prefill``: BASELINE config 3 (Llama-3-8B, 0.55 bpw, 8 x 4096 tokens) by
+  disjoint token batches over the ranks, and with ``N > 1`` ``row_shard``:
+  one 4096-token sequence with every linear's U rows split over the ranks and
+  the output slices all-gathered over NCCL.
 
-Launch: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]``;
+Other workloads (``--workload``): ``decode-bs16`` (config 2 at batch 16),
+``linears`` / ``linears-bs16`` (the packed linears alone), ``prefill``
+(config 3 alone), ``single-linear`` (config 0, ``--tokens`` 1 or 8) and
+``single-linear-stacked`` (config 0 x 1024 layers in one program).
+
+Launch: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload W]``;
 for N > 1 under ``torch.distributed.run``: decode does not shard, so every
-rank runs an independent replica ("replicas only") and ``value`` sums them.
+rank runs an independent replica ("replicas only") and ``value`` sums them;
+the prefill token batches split the 8 x 4096 tokens over the ranks.
+``--impl reference`` times the CPU path alone (rank 0; other ranks exit).
 """
 
 from __future__ import annotations
@@ -34,8 +50,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tok/s (bs1, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak"
-PREFILL_METRIC = "prefill tok/s (Llama-3-8B shape 0.55 bpw, 8x4096 tokens); tensor TFLOP/s vs peak"
 UNIT = "tok/s"
+STEP_VOCAB, STEP_POSITION = 151936, 2048
+PREFILL_TOKENS = 8 * 4096
 
 
 def _peak_table() -> dict[str, tuple[float, str]]:
@@ -47,6 +64,23 @@ def _peak_table() -> dict[str, tuple[float, str]]:
         return {"hbm": (float(data["hbm_gbs"]), "measured"),
                 "tensor": (float(data.get("bf16_tflops_sustained", data["bf16_tflops"])), "measured-sustained")}
     return {"hbm": (6650.0, "fallback"), "tensor": (1400.0, "fallback-sustained")}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 class ClockSampler:
@@ -111,359 +145,557 @@ def _device_status() -> int:
     return value.value
 
 
-def cpu_baseline(workload: str = "decode", repeats: int = 3) -> dict:
-    """Time the CPU oracle (numpy port of PackedReferenceBackend) on a bounded sample.
+# ----------------------------------------------------------- CPU baseline ---
 
-    decode workloads: 2 layers of the shape at the workload's token count;
-    prefill: 1 of 32 Llama-3-8B layers, 128 tokens.  The result is
-    extrapolated to the full step.
+def _qwen3_cpu_step(tokens: int, layers: int = 36):
+    from nanoquant_b200.decode_chain import QWEN3_8B as s
+    from oracle.decoder_oracle import CpuDecodeStep
+
+    return CpuDecodeStep(layers=layers, hidden=s.hidden, intermediate=s.intermediate, q_heads=s.q_heads,
+                         kv_heads=s.kv_heads, head_dim=s.head_dim, vocab=STEP_VOCAB, position=STEP_POSITION,
+                         tokens=tokens, pool=1)
+
+
+def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: float = 240.0) -> dict:
+    """The reference's CPU path for the full step: ``warmup`` untimed then ``steps`` timed full steps.
+
+    Every step runs all 36 layers and the lm head.  When ``warmup + steps``
+    full steps would exceed ``budget_s``, each step runs only a prefix of the
+    layers (the sample string says how many) and its time is scaled to 36.
     """
+
+    setup = time.perf_counter()
+    cpu = _qwen3_cpu_step(tokens)
+    setup_s = time.perf_counter() - setup
+    start = time.perf_counter()
+    cpu.step()  # first warm-up step, also the estimate
+    first = time.perf_counter() - start
+    full_layers = cpu.layers
+    if first * (warmup + steps) > budget_s:
+        cpu.layers = max(1, int(full_layers * budget_s / (first * (warmup + steps))))
+    for _ in range(max(0, warmup - 1)):
+        cpu.step()
+    start = time.perf_counter()
+    for _ in range(steps):
+        cpu.step()
+    per_step = (time.perf_counter() - start) / steps
+    head_note = ""
+    if cpu.layers != full_layers:
+        # scale the layer part to all layers; the lm head runs once per step either way
+        per_step = per_step * full_layers / cpu.layers
+        head_note = f" (each step ran {cpu.layers} of {full_layers} layers + the lm head; time scaled to all layers)"
+    threads = _cpu_threads()
+    return {
+        "value": tokens / per_step, "unit": UNIT, "cores": threads, "kind": "port",
+        "cpu_model": _cpu_model(), "ms_per_step": per_step * 1e3, "steps": steps, "warmup": warmup,
+        "sample": f"full qwen3-8b decode step, {tokens} token(s): 36 layers of the oracle port of "
+                  f"PackedReferenceBackend.linear (fp32 numpy/BLAS on dense +/-1 signs unpacked once) and the model "
+                  f"shell (norms, q/k norm + rope, attention over {STEP_POSITION + 1} cached rows, swiglu), final "
+                  f"norm and the {STEP_VOCAB} x 4096 lm head; {threads} host threads ({_cpu_model()}); {steps} timed "
+                  f"step(s) after {warmup} warm-up{head_note}; setup {setup_s:.0f} s untimed",
+    }
+
+
+def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200) -> dict:
+    """The oracle port of ``PackedReferenceBackend.linear`` on one config-0 layer."""
 
     import numpy as np
 
-    from nanoquant_b200 import decode_chain
     from oracle import packed_oracle as po
 
     rng = np.random.default_rng(0)
-    spec = WORKLOADS[workload]
-    shape = getattr(decode_chain, spec["shape"])
-    sample_layers, sample_tokens = (2, spec["decode_tokens"]) if spec["kind"] == "decode" else (1, 128)
-    per_layer_seconds = []
-    for _layer in range(sample_layers):
-        layers = {}
-        for proj, (n, m) in shape.projections().items():
-            r = shape.rank(n, m)
 
-            def words(rows, cols):
-                raw = rng.integers(0, 2**32, size=(rows, po.word_count(cols)), dtype=np.uint64).astype(np.uint32)
-                if cols % 32:
-                    raw[:, -1] &= np.uint32((1 << (cols % 32)) - 1)
-                return raw.view(np.int32)
+    def words(rows, cols):
+        raw = rng.integers(0, 2**32, size=(rows, po.word_count(cols)), dtype=np.uint64).astype(np.uint32)
+        if cols % 32:
+            raw[:, -1] &= np.uint32((1 << (cols % 32)) - 1)
+        return raw.view(np.int32)
 
-            layer = po.OracleLayer(n, m, r, words(m, r), words(r, n),
-                                   (np.abs(rng.standard_normal(n)) * 0.05 + 0.01).astype(np.float16).astype(np.float32),
-                                   np.ones(r, np.float32),
-                                   (np.abs(rng.standard_normal(m)) * 0.05 + 0.01).astype(np.float16).astype(np.float32))
-            layer.prepared()  # the reference unpacks once at prepare time; not timed
-            layers[proj] = layer
-        inputs = {proj: rng.standard_normal((sample_tokens, n)).astype(np.float32)
-                  for proj, (n, _m) in shape.projections().items()}
-        for proj, layer in layers.items():
-            po.packed_linear(inputs[proj], layer)  # warm-up
-        start = time.perf_counter()
-        for _ in range(repeats):
-            for proj, layer in layers.items():
-                po.packed_linear(inputs[proj], layer)
-        per_layer_seconds.append((time.perf_counter() - start) / repeats)
-        del layers
-    per_layer = statistics.median(per_layer_seconds)
-    step = per_layer * shape.layers  # one pass of `sample_tokens` tokens through every layer
-    cores = os.cpu_count() or 1
-    return {
-        "value": sample_tokens / step,
-        "unit": UNIT,
-        "cores": cores,
-        "kind": "port",
-        "sample": f"{sample_layers} of {shape.layers} {shape.name} layers x 7 projections, {sample_tokens} token(s), "
-                  f"{repeats} reps; numpy/BLAS fp32 on {cores} host threads; extrapolated to all layers",
-        "ms_per_step": step * 1e3,
-    }
+    scale = lambda k: (np.abs(rng.standard_normal(k)) * 0.05 + 0.01).astype(np.float16).astype(np.float32)  # noqa: E731
+    layer = po.OracleLayer(n, m, r, words(m, r), words(r, n), scale(n), np.ones(r, np.float32), scale(m))
+    layer.prepared()
+    x = rng.standard_normal((tokens, n)).astype(np.float32)
+    for _ in range(3):
+        po.packed_linear(x, layer)
+    start = time.perf_counter()
+    for _ in range(repeats):
+        po.packed_linear(x, layer)
+    per = (time.perf_counter() - start) / repeats
+    threads = _cpu_threads()
+    return {"value": tokens / per, "unit": UNIT, "cores": threads, "kind": "port", "ms_per_step": per * 1e3,
+            "cpu_model": _cpu_model(),
+            "sample": f"one {n}->{m} r{r} layer, {tokens} token(s), {repeats} calls of the oracle port of "
+                      f"PackedReferenceBackend.linear (fp32) on {threads} host threads ({_cpu_model()})"}
 
 
-def cpu_baseline_step(repeats: int = 1) -> dict:
-    """CPU time of a full Qwen3-8B step, composed of three timed parts.
-
-    It adds the packed linears (``cpu_baseline("decode")``, the oracle on 2
-    of 36 layers), the shell math of the decoder oracle (norms, q/k norm and
-    RoPE, attention over 2049 cached rows, SwiGLU) timed on 2 layers, and the
-    151936 x 4096 lm head, all extrapolated to one step.
-    """
+def cpu_prefill_baseline(tokens: int = 128) -> dict:
+    """The oracle port on 1 of 32 Llama-3-8B (0.55 bpw) layers at ``tokens`` tokens, scaled to 32 layers."""
 
     import numpy as np
 
-    from nanoquant_b200 import decode_chain
-    from oracle import decoder_oracle as do
+    from nanoquant_b200.decode_chain import LLAMA3_8B_055 as shape
+    from oracle import packed_oracle as po
 
-    shape = decode_chain.QWEN3_8B
-    hd, hkv, hq = shape.head_dim, shape.kv_heads, shape.q_heads
-    linears = cpu_baseline("decode", repeats=1)
     rng = np.random.default_rng(0)
-    caches = do.bf16(rng.standard_normal((hkv, STEP_POSITION + 1, hd)).astype(np.float32))
-    h = rng.standard_normal((1, shape.hidden)).astype(np.float32)
-    w = np.ones(shape.hidden, np.float32)
-    qkv = rng.standard_normal((1, (hq + 2 * hkv) * hd)).astype(np.float32)
-    gate = rng.standard_normal((1, shape.intermediate)).astype(np.float32)
-    cos, sin = do.rope_tables(np.arange(STEP_POSITION, STEP_POSITION + 1), hd, 1e6)
-    sample_layers = 2
+    layers = {}
+    for proj, (n, m) in shape.projections().items():
+        r = shape.rank(n, m)
+        left = rng.integers(0, 2**32, size=(m, po.word_count(r)), dtype=np.uint64).astype(np.uint32)
+        right = rng.integers(0, 2**32, size=(r, po.word_count(n)), dtype=np.uint64).astype(np.uint32)
+        if r % 32:
+            left[:, -1] &= np.uint32((1 << (r % 32)) - 1)
+        if n % 32:
+            right[:, -1] &= np.uint32((1 << (n % 32)) - 1)
+        layer = po.OracleLayer(n, m, r, left.view(np.int32), right.view(np.int32),
+                               np.full(n, 0.03, np.float32), np.ones(r, np.float32), np.full(m, 0.03, np.float32))
+        layer.prepared()
+        layers[proj] = layer
+    xs = {proj: rng.standard_normal((tokens, n)).astype(np.float32) for proj, (n, _m) in shape.projections().items()}
     start = time.perf_counter()
-    for _ in range(repeats * sample_layers):
-        xn = do.bf16(do.rmsnorm(h, w, 1e-6))
-        q = do.bf16(do.rotate(do.rmsnorm(qkv[:, : hq * hd].reshape(1, hq, hd), np.ones(hd, np.float32), 1e-6),
-                              cos[:, None], sin[:, None]))
-        do.attention(q, caches, caches, STEP_POSITION + 1)
-        xn = do.bf16(do.rmsnorm(h + xn, w, 1e-6))
-        do.bf16(gate / (1.0 + np.exp(-gate)) * gate)
-    shell_layer = (time.perf_counter() - start) / (repeats * sample_layers)
-    head = (0.02 * rng.standard_normal((STEP_VOCAB, shape.hidden))).astype(np.float32)
-    start = time.perf_counter()
-    _ = head @ h[0]
-    head_s = time.perf_counter() - start
-    step = linears["ms_per_step"] * 1e-3 + shell_layer * shape.layers + head_s
-    cores = os.cpu_count() or 1
-    return {
-        "value": 1.0 / step, "unit": UNIT, "cores": cores, "kind": "port",
-        "sample": f"packed linears: {linears['sample']}; shell (oracle norms, rope, attention over "
-                  f"{STEP_POSITION + 1} rows, swiglu) on {sample_layers} layers and the {STEP_VOCAB} x "
-                  f"{shape.hidden} lm head, extrapolated to {shape.layers} layers",
-        "ms_per_step": step * 1e3,
-    }
+    for proj, layer in layers.items():
+        po.packed_linear(xs[proj], layer)
+    per_layer = time.perf_counter() - start
+    step = per_layer * shape.layers
+    threads = _cpu_threads()
+    return {"value": tokens / step, "unit": UNIT, "cores": threads, "kind": "port", "ms_per_step": step * 1e3,
+            "cpu_model": _cpu_model(),
+            "sample": f"1 of 32 llama-3-8b layers (7 projections, 0.55 bpw), {tokens} tokens, oracle port of "
+                      f"PackedReferenceBackend.linear (fp32) on {threads} host threads ({_cpu_model()}); "
+                      f"scaled to 32 layers"}
 
 
-def run_reference(args, rank: int, world: int) -> None:
-    """The reference arm: the reference's packed CPU algorithm (oracle port) on the host cores."""
+# --------------------------------------------------------------- runners ---
+
+class StepRunner:
+    """The full Qwen3-8B-shaped decode step (``nanoquant_b200.decoder``), replayed from a CUDA graph."""
+
+    bound = "hbm"
+
+    def __init__(self, device, tokens: int, layers: int | None) -> None:
+        from nanoquant_b200.decode_chain import QWEN3_8B
+        from nanoquant_b200.decoder import build_qwen3_step
+
+        self.step_obj = build_qwen3_step(QWEN3_8B, device, vocab=STEP_VOCAB, tokens=tokens, position=STEP_POSITION,
+                                         layers=layers)
+        self.tokens = tokens
+        self.layers = len(self.step_obj.layers)
+        self.input = self.step_obj.hidden_in
+        self.launches_per_step = self.step_obj.kernel_launches()
+        self.step_obj.capture()
+
+    def run(self):
+        return self.step_obj.replay()
+
+    def algorithmic_bytes(self) -> int:
+        return self.step_obj.algorithmic_bytes()
+
+
+class ChainRunner:
+    """Packed linears only (``DecodeChain``): one persistent program launch per step, or per-call kernels."""
+
+    bound = "hbm"
+
+    def __init__(self, shape, device, tokens: int, layers: int | None, engine: str | None = None) -> None:
+        from nanoquant_b200.decode_chain import DecodeChain, make_decoder_layers
+
+        self.chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=layers, seed=0), device,
+                                 tokens=tokens, engine=engine)
+        self.tokens = tokens
+        self.layers = len(self.chain.blocks)
+        self.input = self.chain.inputs["hidden"]
+        self.launches_per_step = self.chain.launches_per_step
+        if self.chain.program is None:
+            self.chain.capture()
+
+    def run(self):
+        return self.chain.step() if self.chain.program is not None else self.chain.replay()
+
+    def algorithmic_bytes(self) -> int:
+        return self.chain.algorithmic_bytes()
+
+
+class PrefillRunner:
+    """Llama-3-8B (0.55 bpw) packed linears on ``tokens`` tokens per rank (tensor-core prefill kernels)."""
+
+    bound = "tensor"
+
+    def __init__(self, device, tokens: int, layers: int | None) -> None:
+        from nanoquant_b200.decode_chain import LLAMA3_8B_055, DecodeChain, make_decoder_layers
+
+        self.chain = DecodeChain(LLAMA3_8B_055, make_decoder_layers(LLAMA3_8B_055, device, layers=layers, seed=0),
+                                 device, tokens=tokens, engine="calls")
+        self.tokens = tokens
+        self.layers = len(self.chain.blocks)
+        self.input = self.chain.inputs["hidden"]
+        self.launches_per_step = self.chain.launches_per_step
+
+    def run(self):
+        return self.chain.step()
+
+    def algorithmic_flops(self) -> int:
+        return self.chain.algorithmic_flops()
+
+
+class SingleLinearRunner:
+    """BASELINE config 0 (640 -> 2048, rank 480): one ``CudaPackedSm100Backend.linear`` call, captured in a graph."""
+
+    bound = "hbm"
+
+    def __init__(self, device, tokens: int) -> None:
+        import torch
+
+        from nanoquant_b200 import CudaPackedSm100Backend
+        from nanoquant_b200.decode_chain import layer_bytes, random_packed_layer
+
+        n, m, r = 640, 2048, 480
+        g = torch.Generator(device=device).manual_seed(0)
+        self.backend = CudaPackedSm100Backend()
+        self.layer = self.backend.prepare(random_packed_layer("blocks.0.mlp.up_proj", n, m, r, g, device), device)
+        self.input = torch.randn(tokens, n, generator=g, device=device).bfloat16()
+        self.tokens, self.layers, self.launches_per_step = tokens, 1, 2
+        self._bytes = layer_bytes(n, m, r) + tokens * (2 * n + 4 * m)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            self.backend.linear(self.input, self.layer)  # warm-up outside capture (workspace, smem attributes)
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.output = self.backend.linear(self.input, self.layer)
+
+    def run(self):
+        self.graph.replay()
+        return self.output
+
+    def algorithmic_bytes(self) -> int:
+        return self._bytes
+
+
+class StackedLinearRunner:
+    """BASELINE config 0 (2048 x 640, rank 480) as ``count`` independent layers run as one program."""
+
+    bound = "hbm"
+
+    def __init__(self, device, tokens: int, count: int) -> None:
+        import torch
+
+        from nanoquant_b200 import CudaPackedSm100Backend
+        from nanoquant_b200.decode_chain import layer_bytes, random_packed_layer
+        from nanoquant_b200.program import DecodeProgram, ProgramOp
+
+        n, m, r = 640, 2048, 480
+        g = torch.Generator(device=device).manual_seed(0)
+        backend = CudaPackedSm100Backend()
+        self.input = torch.randn(tokens, n, generator=g, device=device).bfloat16()
+        self.layers_prepared = [backend.prepare(random_packed_layer(f"stack.{i}.up_proj", n, m, r, g, device), device)
+                                for i in range(count)]
+        self.program = DecodeProgram([ProgramOp((layer,), self.input) for layer in self.layers_prepared])
+        self.tokens = tokens
+        self.layers = count
+        self.launches_per_step = 1
+        self._bytes = count * (layer_bytes(n, m, r) + tokens * (2 * n + 4 * m))
+
+    def run(self):
+        return self.program.run()[-1][0]
+
+    def algorithmic_bytes(self) -> int:
+        return self._bytes
+
+
+WORKLOADS = {
+    "decode": {"kind": "step", "metric": METRIC, "tokens": 1,
+               "description": "qwen3-8b decode step bs1 ({layers} layers: norms, packed q/k/v/o/gate/up/down, q/k "
+                              "norm + rope, attention over 2048 cached tokens, swiglu; final norm; bf16 lm head "
+                              "151936 x 4096)",
+               "model": "qwen3-8b-shape random-init: packed weights ~1 bpw (layout v1, fp16 scales), bf16 norms and "
+                        "lm head, bf16 kv cache N(0,1)"},
+    "decode-bs16": {"kind": "step", "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); HBM GB/s vs peak",
+                    "tokens": 16,
+                    "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head, 2048 cached "
+                                   "tokens)",
+                    "model": "qwen3-8b-shape random-init, as decode"},
+    "linears": {"kind": "linears", "metric": "packed-linear decode tok/s (bs1, Qwen3-8B shape ~1 bpw); HBM GB/s",
+                "tokens": 1,
+                "description": "qwen3-8b packed linears only, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; "
+                               "grouped qkv and gate/up)",
+                "model": "qwen3-8b-shape random-init packed weights ~1 bpw"},
+    "linears-bs16": {"kind": "linears", "metric": "packed-linear decode tok/s (bs16, Qwen3-8B shape); HBM GB/s",
+                     "tokens": 16,
+                     "description": "qwen3-8b packed linears only, decode bs16 ({layers} layers)",
+                     "model": "qwen3-8b-shape random-init packed weights ~1 bpw"},
+    "prefill": {"kind": "prefill",
+                "metric": "prefill tok/s (Llama-3-8B shape 0.55 bpw, 8x4096 tokens); tensor TFLOP/s vs peak",
+                "description": "llama-3-8b packed linears, prefill 8x4096 tokens ({layers} layers x "
+                               "q,k,v,o,gate,up,down)",
+                "model": "llama-3-8b-shape random-init packed weights 0.55 bpw"},
+    "single-linear": {"kind": "single", "metric": "single packed linear tok/s (2048x640 r480); HBM GB/s",
+                      "tokens": 1,
+                      "description": "one 640->2048 rank-480 packed linear (config 0), {tokens} token(s)",
+                      "model": "config 0: iid sign words, fp16 scales |N(0,1)|*0.05+0.01, bf16 x N(0,1)"},
+    "single-linear-stacked": {"kind": "stacked",
+                              "metric": "stacked packed linears tok/s (1024 x 2048x640 r480); HBM GB/s",
+                              "tokens": 1,
+                              "description": "1024 independent 640->2048 rank-480 layers (config 0) in one program, "
+                                             "{tokens} token(s)",
+                              "model": "config 0 x 1024 (165 MB of weights, larger than L2)"},
+}
+
+
+def _build(name: str, device, tokens: int, layers: int | None, engine: str | None):
+    from nanoquant_b200 import decode_chain
+
+    kind = WORKLOADS[name]["kind"]
+    if kind == "step":
+        return StepRunner(device, tokens, layers)
+    if kind == "linears":
+        return ChainRunner(decode_chain.QWEN3_8B, device, tokens, layers, engine)
+    if kind == "prefill":
+        return PrefillRunner(device, tokens, layers)
+    if kind == "single":
+        return SingleLinearRunner(device, tokens)
+    return StackedLinearRunner(device, tokens, 1024)
+
+
+# ----------------------------------------------------------------- timing ---
+
+class Timer:
+    """Times ``steps`` runs of a callable on the device: barrier + synchronize on both sides, max over ranks."""
+
+    def __init__(self, device, world: int) -> None:
+        self.device, self.world = device, world
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max_over_ranks(self, *values: float) -> list[float]:
+        if self.world == 1:
+            return list(values)
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor(values, dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def time(self, run, steps: int, warmup: int, clocks_index: int | None = None) -> tuple[float, dict | None]:
+        import torch
+
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize(self.device)
+        stream = torch.cuda.current_stream(self.device)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(clocks_index) if clocks_index is not None else None
+        if sampler is not None:
+            sampler.__enter__()
+        try:
+            self.barrier()
+            torch.cuda.synchronize(self.device)
+            start.record(stream)
+            for _ in range(steps):
+                run()
+            stop.record(stream)
+            torch.cuda.synchronize(self.device)
+            self.barrier()
+        finally:
+            if sampler is not None:
+                sampler.__exit__()
+        (elapsed,) = self.max_over_ranks(start.elapsed_time(stop))
+        return elapsed / steps, (sampler.summary() if sampler is not None else None)
+
+
+def _check_status(where: str) -> None:
+    status = _device_status()
+    if status != 0:
+        raise SystemExit(f"libnqb device status {status} after {where} (a bounded wait gave up)")
+
+
+def _hbm_roofline(bytes_per: int, ms: float, peaks: dict, scope: str) -> dict:
+    achieved = bytes_per / (ms * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm"][0], "unit": "GB/s",
+            "frac": achieved / peaks["hbm"][0], "traffic": None, "peak_kind": peaks["hbm"][1],
+            "algorithmic_bytes_per_launch": bytes_per, "launch_ms": ms, "scope": scope}
+
+
+def _tensor_roofline(flops: int, ms: float, peaks: dict, scope: str) -> dict:
+    achieved = flops / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": peaks["tensor"][0], "unit": "TFLOP/s",
+            "frac": achieved / peaks["tensor"][0], "traffic": None, "peak_kind": peaks["tensor"][1],
+            "algorithmic_flops_per_step_per_gpu": flops, "scope": scope}
+
+
+def _prefill_extra(device, timer: Timer, world: int, rank: int, peaks: dict) -> dict:
+    """Config 3 by disjoint token batches: rank g takes 32768 / N tokens of the 8 x 4096 (no collective)."""
+
+    import torch
+
+    from nanoquant_b200.sharding import token_range
+
+    lo, hi = token_range(PREFILL_TOKENS, world, rank)
+    runner = PrefillRunner(device, hi - lo, None)
+    ms, _ = timer.time(runner.run, 3, 3)
+    _check_status("the prefill token batches")
+    flops = runner.algorithmic_flops()
+    del runner
+    torch.cuda.empty_cache()
+    return {"value": PREFILL_TOKENS * 1000.0 / ms, "unit": UNIT, "ms_per_step": ms, "n_gpus": world,
+            "parallelism": f"token-batches{world}", "tokens_per_gpu": hi - lo, "scaling": "strong",
+            "config": "llama-3-8b 0.55 bpw, 32 layers x 7 packed linears, 8 x 4096 tokens split over the ranks",
+            "roofline": _tensor_roofline(flops, ms, peaks, "per-GPU packed-linear flops / step time")}
+
+
+def _row_shard_extra(device, timer: Timer, world: int, rank: int) -> dict:
+    """One 4096-token sequence through 32 Llama-3-8B layers with every linear's U rows split over the ranks.
+
+    Each linear runs stage 1 in full and stage 2 on this rank's rows, then
+    all-gathers the fp32 output slices (NCCL, on a side stream); the next
+    linear's kernels overlap that gather.
+    """
+
+    import torch
+
+    from nanoquant_b200 import CudaPackedSm100Backend
+    from nanoquant_b200.decode_chain import LLAMA3_8B_055 as shape
+    from nanoquant_b200.decode_chain import make_decoder_layers
+    from nanoquant_b200.sharding import RowShardedLinear
+
+    tokens = 4096
+    backend = CudaPackedSm100Backend()
+    blocks = make_decoder_layers(shape, device, seed=0)
+    side = torch.cuda.Stream(device)  # one gather stream: NCCL serialises a communicator's collectives anyway
+    linears = [RowShardedLinear(backend, state, device, stream=side) for block in blocks for state in block.values()]
+    del blocks
+    g = torch.Generator(device=device).manual_seed(3)
+    inputs = {n: torch.randn(tokens, n, generator=g, device=device).bfloat16()
+              for n in {lin.local.spec.in_features for lin in linears}}
+
+    def run():
+        works = [lin.start(inputs[lin.local.spec.in_features]) for lin in linears]
+        for work in works:
+            work.wait()
+
+    ms, _ = timer.time(run, 3, 3)
+    _check_status("the row-shard run")
+    gathered = sum(tokens * lin.width * world * 4 for lin in linears)
+    del linears
+    torch.cuda.empty_cache()
+    return {"value": tokens * 1000.0 / ms, "unit": UNIT, "ms_per_step": ms, "n_gpus": world,
+            "parallelism": f"u-row-shard{world}", "tokens": tokens, "scaling": "strong",
+            "gathered_bytes_per_step": gathered,
+            "config": "llama-3-8b 0.55 bpw, 32 layers x 7 packed linears on one 4096-token sequence; U rows split "
+                      "over the ranks, fp32 output slices all-gathered in place (NCCL) on a side stream"}
+
+
+def run_reference(args, rank: int) -> None:
+    """The reference arm: the reference's CPU path (the oracle port) on the host cores, rank 0 only."""
 
     if rank != 0:
         return
     spec = WORKLOADS[args.workload]
-    base = (cpu_baseline_step() if spec["kind"] == "step"
-            else cpu_baseline(args.workload, repeats=max(1, min(args.steps, 5))))
+    kind = spec["kind"]
+    tokens = args.tokens or spec.get("tokens", 1)
+    if kind == "step":
+        base = cpu_step_baseline(tokens, steps=args.steps, warmup=args.warmup)
+    elif kind == "prefill":
+        base = cpu_prefill_baseline()
+    elif kind in ("single", "stacked"):
+        base = cpu_linear_baseline(640, 2048, 480, tokens)
+    else:
+        raise SystemExit(f"no CPU reference path for workload {args.workload}")
     line = {
         "impl": "reference",
         "metric": spec["metric"],
         "value": base["value"],
         "unit": UNIT,
         "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": base.get("steps", args.steps),
+        "warmup": base.get("warmup", args.warmup),
         "ms_per_step": base["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak" if spec["kind"] != "prefill" else "strong",
+        "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": spec["description"].format(layers="all"), "model": spec["model"],
-                   "parallelism": "cpu"},
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "config": {"workload": spec["description"].format(layers="all", tokens=tokens), "parallelism": "cpu",
+                   "cpu_model": base["cpu_model"]},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")},
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-class _StepAdapter:
-    """A full decoder step (``nanoquant_b200.decoder``) behind the DecodeChain methods the timing loop uses."""
-
-    def __init__(self, step) -> None:
-        self.step_obj = step
-        self.inputs = {"hidden": step.hidden_in}
-        self.blocks = step.layers
-        self.program = None
-        self.launches_per_step = step.kernel_launches()
-
-    def capture(self) -> None:
-        self.step_obj.capture()
-
-    def replay(self):
-        return self.step_obj.replay()
-
-    def step(self):
-        return self.step_obj.step()
-
-    def algorithmic_bytes(self) -> int:
-        return self.step_obj.algorithmic_bytes()
-
-
-STEP_VOCAB, STEP_POSITION = 151936, 2048
-
-
-WORKLOADS = {
-    "decode": {
-        "kind": "decode",
-        "metric": METRIC,
-        "shape": "QWEN3_8B",
-        "tokens_total": None,  # one token per rank (replicas)
-        "decode_tokens": 1,
-        "description": "qwen3-8b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
-        "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
-    },
-    # Qwen3-8B at batch 16 and the Gemma-3-1B decode step: extra lines beside the headline
-    "decode-bs16": {
-        "kind": "decode",
-        "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak",
-        "shape": "QWEN3_8B",
-        "tokens_total": None,
-        "decode_tokens": 16,
-        "description": "qwen3-8b packed linears, decode bs16 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
-        "model": "qwen3-8b-shape random-init packed weights ~1 bpw",
-    },
-    "decode-gemma1b": {
-        "kind": "decode",
-        "metric": "decode tok/s (bs1, Gemma-3-1B shape ~1 bpw); packed-GEMV HBM GB/s vs peak",
-        "shape": "GEMMA3_1B",
-        "tokens_total": None,
-        "decode_tokens": 1,
-        "description": "gemma-3-1b packed linears, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; grouped qkv and gate/up)",
-        "model": "gemma-3-1b-shape random-init packed weights ~1 bpw",
-    },
-    "decode-step": {
-        "kind": "step",
-        "metric": "decode tok/s (bs1, full Qwen3-8B-shaped step: packed linears + shell + lm head); HBM GB/s vs peak",
-        "shape": "QWEN3_8B",
-        "tokens_total": None,
-        "decode_tokens": 1,
-        "description": "qwen3-8b decode step bs1 ({layers} layers: norms, packed q/k/v/o/gate/up/down, q/k norm + "
-                       "rope, attention over 2048 cached tokens, swiglu; final norm; bf16 lm head 151936 x 4096)",
-        "model": "qwen3-8b-shape random-init: packed weights ~1 bpw, bf16 norms and lm head, bf16 kv cache N(0,1)",
-    },
-    "prefill": {
-        "kind": "prefill",
-        "metric": PREFILL_METRIC,
-        "shape": "LLAMA3_8B_055",
-        "tokens_total": 8 * 4096,  # 8 sequences x 4096 tokens, disjoint token batches per rank
-        "description": "llama-3-8b packed linears, prefill 8x4096 tokens ({layers} layers x q,k,v,o,gate,up,down)",
-        "model": "llama-3-8b-shape random-init packed weights 0.55 bpw",
-    },
-}
-
-
 def main() -> None:
-    parser = argparse.ArgumentParser(description=__doc__)
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=None, help="timed steps (default 50 decode, 3 prefill)")
+    parser.add_argument("--steps", type=int, default=None, help="timed steps (default 20; 3 for prefill)")
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("nqb", "reference"), default="nqb")
-    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
-                        help="decode: Qwen3-8B packed linears at batch 1 (the headline); prefill: Llama-3-8B 0.55 bpw, "
-                             "8 x 4096 tokens")
-    parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--layers", type=int, default=None,
-                        help="decoder layers in the step (default: all); fewer only for profiling runs")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="decode")
+    parser.add_argument("--tokens", type=int, default=None, help="tokens per step (single linear: 1 or 8)")
+    parser.add_argument("--layers", type=int, default=None, help="decoder layers (default all; fewer only to profile)")
     parser.add_argument("--engine", choices=("program", "calls"), default=None,
-                        help="decode: one persistent program launch per step (default) or per-call kernels in a "
-                             "CUDA graph")
-    parser.add_argument("--tokens", type=int, default=None,
-                        help="prefill tokens per GPU (default: 8*4096 / GPUs); smaller only for profiling runs")
+                        help="linears workloads: one persistent program per step (default) or per-call kernels")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extras", action="store_true", help="skip the linears / prefill / row-shard lines")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    spec = WORKLOADS[args.workload]
     if args.steps is None:
-        args.steps = 50 if WORKLOADS[args.workload]["kind"] != "prefill" else 3
+        args.steps = 3 if spec["kind"] == "prefill" else 20
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        run_reference(args, rank)
         return
 
     import torch
     import torch.distributed as dist
-
-    from nanoquant_b200 import decode_chain
-    from nanoquant_b200.decode_chain import DecodeChain, make_decoder_layers
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-
-    def barrier() -> None:
-        if world > 1:
-            dist.barrier()
-
-    spec = WORKLOADS[args.workload]
-    shape = getattr(decode_chain, spec["shape"])
-    if spec["tokens_total"] is None:
-        tokens = spec["decode_tokens"]
-    else:
-        if spec["tokens_total"] % world:
-            raise SystemExit(f"{spec['tokens_total']} tokens do not split over {world} ranks")
-        tokens = spec["tokens_total"] // world
-        if args.tokens is not None:
-            tokens = args.tokens
-    if spec["kind"] == "step":
-        from nanoquant_b200.decoder import build_qwen3_step
-
-        chain = _StepAdapter(build_qwen3_step(shape, device, vocab=STEP_VOCAB, tokens=tokens, position=STEP_POSITION,
-                                              layers=args.layers))
-    else:
-        chain = DecodeChain(shape, make_decoder_layers(shape, device, layers=args.layers, seed=0), device,
-                            tokens=tokens, engine=args.engine)
-    decode = spec["kind"] in ("decode", "step")
-    use_graph = decode and chain.program is None
-    if use_graph:
-        chain.capture()
-    run_step = chain.replay if use_graph else chain.step
-    for _ in range(args.warmup):
-        run_step()
-    torch.cuda.synchronize(device)
-
-    stream = torch.cuda.current_stream(device)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        barrier()
-        torch.cuda.synchronize(device)
-        start.record(stream)
-        for _ in range(args.steps):
-            run_step()
-        stop.record(stream)
-        torch.cuda.synchronize(device)
-        barrier()
-    elapsed_ms = start.elapsed_time(stop)
-    status = _device_status()
-    if status != 0:
-        raise SystemExit(f"libnqb device status {status} after the timed region (a bounded wait gave up)")
-
-    # end to end through the public API: pinned host tokens in, result back to host, every step
-    host_in = torch.randn(tokens, shape.hidden).bfloat16().pin_memory()
-    last = run_step()
-    host_out = torch.empty(last.shape, dtype=torch.float32).pin_memory()
-    for _ in range(2):
-        chain.inputs["hidden"].copy_(host_in, non_blocking=True)
-        host_out.copy_(run_step(), non_blocking=True)
-    torch.cuda.synchronize(device)
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e_start.record(stream)
-    for _ in range(args.steps):
-        chain.inputs["hidden"].copy_(host_in, non_blocking=True)
-        host_out.copy_(run_step(), non_blocking=True)
-    e_stop.record(stream)
-    torch.cuda.synchronize(device)
-    barrier()
-    e2e_ms = e_start.elapsed_time(e_stop)
-
-    if world > 1:
-        times = torch.tensor([elapsed_ms, e2e_ms], device=device)
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-        elapsed_ms, e2e_ms = (float(v) for v in times.tolist())
-
-    ms_per_step = elapsed_ms / args.steps
-    total_tokens = tokens * world
-    value = total_tokens * 1000.0 / ms_per_step
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    timer = Timer(device, world)
     peaks = _peak_table()
-    if decode:
-        step_bytes = chain.algorithmic_bytes()
-        achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
-        roofline = {
-            "bound": "hbm", "achieved": achieved, "peak": peaks["hbm"][0], "unit": "GB/s",
-            "frac": achieved / peaks["hbm"][0], "traffic": None, "peak_kind": peaks["hbm"][1],
-            "scope": ("the whole decoder step: packed weights and scales, kv rows read, norms, lm head"
-                      if spec["kind"] == "step" else
-                      "all packed-linear kernels of one step (algorithmic bytes per step / step time)"),
-            "algorithmic_bytes_per_step": step_bytes,
-        }
+
+    kind = spec["kind"]
+    if kind == "prefill":
+        lo, hi = 0, PREFILL_TOKENS
+        if args.tokens is None:
+            from nanoquant_b200.sharding import token_range
+
+            lo, hi = token_range(PREFILL_TOKENS, world, rank)
+        tokens = args.tokens or (hi - lo)
     else:
-        step_flops = chain.algorithmic_flops()
-        achieved = step_flops / (ms_per_step * 1e-3) / 1e12
-        roofline = {
-            "bound": "tensor", "achieved": achieved, "peak": peaks["tensor"][0], "unit": "TFLOP/s",
-            "frac": achieved / peaks["tensor"][0], "traffic": None, "peak_kind": peaks["tensor"][1],
-            "scope": "all packed-linear kernels of one step per GPU (2*r*(m+n) flops per token and linear / step time)",
-            "algorithmic_flops_per_step_per_gpu": step_flops,
-        }
-    line = {
+        tokens = args.tokens or spec["tokens"]
+    runner = _build(args.workload, device, tokens, args.layers, args.engine)
+    ms_per_step, clocks = timer.time(runner.run, args.steps, args.warmup, clocks_index=local_rank)
+    _check_status("the timed region")
+
+    # end to end through the public API: the step's input from pinned host
+    # memory and its output back to pinned host memory, every step
+    host_in = torch.randn(tuple(runner.input.shape)).to(runner.input.dtype).pin_memory()
+    out = runner.run()
+    host_out = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        runner.input.copy_(host_in, non_blocking=True)
+        host_out.copy_(runner.run(), non_blocking=True)
+
+    e2e_ms, _ = timer.time(e2e_step, args.steps, 2)
+    _check_status("the end-to-end run")
+
+    total_tokens = tokens * world if kind != "prefill" else (args.tokens * world if args.tokens else PREFILL_TOKENS)
+    value = total_tokens * 1000.0 / ms_per_step
+    line: dict = {
         "metric": spec["metric"],
         "value": value,
         "unit": UNIT,
@@ -472,36 +704,74 @@ def main() -> None:
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak" if decode else "strong",
+        "scaling": "strong" if kind == "prefill" else "weak",
         "vs_baseline": None,
-        "dtype": "f32" if decode else "f16",
+        "dtype": "f16" if kind == "prefill" else "f32",
         "data": "synthetic",
         "config": {
-            "workload": spec["description"].format(layers=len(chain.blocks)),
+            "workload": spec["description"].format(layers=getattr(runner, "layers", 1), tokens=tokens),
             "model": spec["model"],
             "global_batch": total_tokens,
             "tokens_per_gpu": tokens,
-            "parallelism": (f"replicas{world}" if decode else f"token-batches{world}")
+            "parallelism": (f"token-batches{world}" if kind == "prefill" else f"replicas{world}")
             if world > 1 else "single",
-            "l2": "weights larger than the 126 MB L2 (no flush)",
-            "cuda_graph": use_graph,
-            "engine": ("persistent program (one cooperative launch per step)" if chain.program is not None
-                       else "decode programs (4 per layer) + shell kernels in one CUDA graph" if spec["kind"] == "step"
-                       else "per-call kernels"),
+            "l2": "weights larger than the 126 MB L2 (no flush)" if kind != "single" else
+                  "161 KB of weights stay in L2 across steps (config 0 is smaller than L2)",
         },
-        "roofline": roofline,
         "e2e": {
-            "value": total_tokens * 1000.0 * args.steps / e2e_ms,
+            "value": total_tokens * 1000.0 / e2e_ms,
             "unit": UNIT,
             "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
             "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
         },
-        "gpu_launches": chain.launches_per_step * args.steps,
-        "clocks": clocks.summary(),
+        "gpu_launches": runner.launches_per_step * args.steps,
+        "clocks": clocks,
     }
-    if rank == 0 and not args.no_cpu_baseline:
-        base = cpu_baseline_step() if spec["kind"] == "step" else cpu_baseline(args.workload)
-        line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if kind == "prefill":
+        line["roofline"] = _tensor_roofline(runner.algorithmic_flops(), ms_per_step, peaks,
+                                            "all packed-linear kernels of one step per GPU (2*r*(m+n) flops per "
+                                            "token and linear / step time)")
+    else:
+        step_bytes = runner.algorithmic_bytes()
+        scope = {"step": "the whole decoder step: packed weights and scales, kv rows read, norms, lm head",
+                 "linears": "the persistent decode program: every packed linear of the step in one launch",
+                 "single": "one launch pair of the config-0 layer", "stacked": "the program of 1024 layers"}[kind]
+        line["roofline"] = _hbm_roofline(step_bytes, ms_per_step, peaks, scope)
+    del runner
+    torch.cuda.empty_cache()
+
+    if kind == "step" and not args.no_extras:
+        # the dominant kernel of the step: the packed linears as one program launch
+        line["step_roofline"] = line["roofline"]
+        from nanoquant_b200.decode_chain import QWEN3_8B
+
+        linears = ChainRunner(QWEN3_8B, device, tokens, args.layers)
+        lin_ms, _ = timer.time(linears.run, args.steps, args.warmup)
+        _check_status("the linears-only run")
+        line["roofline"] = _hbm_roofline(linears.algorithmic_bytes(), lin_ms, peaks,
+                                         "dominant kernel: the persistent decode program running all 252 packed "
+                                         "linears of the step in one launch (bytes per launch / launch time, CUDA "
+                                         "events over the same number of launches)")
+        line["linears"] = {"value": tokens * world * 1000.0 / lin_ms, "unit": UNIT, "ms_per_step": lin_ms,
+                           "algorithmic_bytes_per_step": linears.algorithmic_bytes()}
+        del linears
+        torch.cuda.empty_cache()
+    if not args.no_extras and kind != "prefill":
+        line["prefill"] = _prefill_extra(device, timer, world, rank, peaks)
+        if world > 1:
+            line["row_shard"] = _row_shard_extra(device, timer, world, rank)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if kind == "step":
+            base = cpu_step_baseline(tokens)
+        elif kind == "prefill":
+            base = cpu_prefill_baseline()
+        elif kind in ("single", "stacked"):
+            base = cpu_linear_baseline(640, 2048, 480, tokens)
+        else:
+            base = None
+        if base is not None:
+            line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -156,7 +156,7 @@ class RowShardedLinear:
     """
 
     def __init__(self, backend, state, device: torch.device | str, *, group=None, world: int | None = None,
-                 rank: int | None = None) -> None:
+                 rank: int | None = None, stream: torch.cuda.Stream | None = None) -> None:
         import torch.distributed as dist
 
         self.group = group
@@ -170,7 +170,8 @@ class RowShardedLinear:
         self.local: PreparedLayer = backend.prepare(shard_rows(state, start, stop, pad_to=self.width), device)
         self.device = torch.device(device)
         self._buffers: dict[int, torch.Tensor] = {}
-        self._stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        # the gather stream (several sharded linears may share one)
+        self._stream = (stream or torch.cuda.Stream(self.device)) if self.device.type == "cuda" else None
 
     def buffer(self, tokens: int) -> torch.Tensor:
         """The gather buffer ``[world, tokens, width]`` for ``tokens`` tokens (kept across calls)."""

@@ -22,9 +22,14 @@ from oracle import packed_oracle as po
 def bf16(x: np.ndarray) -> np.ndarray:
     """Round float32 values to bfloat16 (nearest even), returned as float32."""
 
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    r = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    return r.astype(np.uint32).view(np.float32)
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    # round half to even on the 16 dropped bits (uint32 arithmetic: no finite
+    # value carries past bit 31)
+    r = (u >> 16) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    return r.view(np.float32)
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
@@ -64,6 +69,65 @@ def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, keys: int
     return out
 
 
+def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_cache: np.ndarray, *,
+                 position: int, q_heads: int, kv_heads: int, head_dim: int, eps: float, cos: np.ndarray,
+                 sin: np.ndarray, accumulate: str = "float64") -> np.ndarray:
+    """One Qwen3-style layer on the residual stream ``h [T, hidden]``; returns the new ``h``.
+
+    ``proj``: ``OracleLayer`` per projection name; ``norms``: this layer's
+    ``input_norm``, ``post_norm``, ``q_norm`` and ``k_norm``.  The caches are
+    updated in place at rows ``position + t``.
+    """
+
+    tokens = h.shape[0]
+
+    def linear(x: np.ndarray, layer) -> np.ndarray:
+        return po.packed_linear(x, layer, accumulate=accumulate).astype(np.float32)
+
+    xn = bf16(rmsnorm(h, norms["input_norm"], eps))
+    q = linear(xn, proj["q_proj"]).reshape(tokens, q_heads, head_dim)
+    k = linear(xn, proj["k_proj"]).reshape(tokens, kv_heads, head_dim)
+    v = linear(xn, proj["v_proj"]).reshape(tokens, kv_heads, head_dim)
+    q = bf16(rotate(rmsnorm(q, norms["q_norm"], eps), cos[:, None, :], sin[:, None, :]))
+    k = bf16(rotate(rmsnorm(k, norms["k_norm"], eps), cos[:, None, :], sin[:, None, :]))
+    for t in range(tokens):
+        k_cache[:, position + t] = k[t]
+        v_cache[:, position + t] = bf16(v[t])
+    a = bf16(attention(q, k_cache, v_cache, position + 1).reshape(tokens, q_heads * head_dim))
+    h = h + linear(a, proj["o_proj"])
+    xn = bf16(rmsnorm(h, norms["post_norm"], eps))
+    gate = linear(xn, proj["gate_proj"])
+    up = linear(xn, proj["up_proj"])
+    with np.errstate(over="ignore"):  # exp(-gate) overflows to inf for very negative gates: silu -> 0
+        act = (gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)
+    return h + linear(act, proj["down_proj"])
+
+
+def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_norm: np.ndarray,
+                          lm_head: np.ndarray, *, position: int, q_heads: int, kv_heads: int, head_dim: int,
+                          eps: float, theta: float, accumulate: str = "float64",
+                          head_accumulate: str = "float64") -> np.ndarray:
+    """Logits ``[T, vocab]`` of a step whose layers arrive one at a time.
+
+    ``layer_at(i)`` returns ``(proj, norms, k_cache, v_cache)`` of layer i (the
+    caches are updated in place), so a caller can build each layer's dense
+    signs just before it runs and drop them after: host memory stays at one
+    layer for any depth.
+    """
+
+    tokens = hidden.shape[0]
+    h = hidden.astype(np.float32).copy()
+    cos, sin = rope_tables(np.arange(position, position + tokens), head_dim, theta)
+    for i in range(layer_count):
+        proj, norms, k_cache, v_cache = layer_at(i)
+        h = decode_layer(h, proj, norms, k_cache, v_cache, position=position, q_heads=q_heads, kv_heads=kv_heads,
+                         head_dim=head_dim, eps=eps, cos=cos, sin=sin, accumulate=accumulate)
+    xn = bf16(rmsnorm(h, final_norm, eps))
+    if head_accumulate == "float64":
+        return (xn.astype(np.float64) @ lm_head.astype(np.float64).T).astype(np.float32)
+    return (xn @ np.asarray(lm_head, dtype=np.float32).T).astype(np.float32)
+
+
 def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: list[np.ndarray],
                 v_caches: list[np.ndarray], *, position: int, q_heads: int, kv_heads: int, head_dim: int,
                 eps: float, theta: float) -> tuple[np.ndarray, list[np.ndarray], list[np.ndarray]]:
@@ -74,35 +138,86 @@ def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: l
     ``final_norm``, ``lm_head`` (float32 arrays holding bf16 values).
     """
 
-    tokens = hidden.shape[0]
-    h = hidden.astype(np.float32).copy()
-    cos, sin = rope_tables(np.arange(position, position + tokens), head_dim, theta)
     k_caches = [c.copy() for c in k_caches]
     v_caches = [c.copy() for c in v_caches]
 
-    def linear(x: np.ndarray, layer) -> np.ndarray:
-        return po.packed_linear(x, layer, accumulate="float64").astype(np.float32)
+    def layer_at(i: int):
+        per_layer = {name: norms[name][i] for name in ("input_norm", "post_norm", "q_norm", "k_norm")}
+        return layers[i], per_layer, k_caches[i], v_caches[i]
 
-    for i, proj in enumerate(layers):
-        xn = bf16(rmsnorm(h, norms["input_norm"][i], eps))
-        q = linear(xn, proj["q_proj"]).reshape(tokens, q_heads, head_dim)
-        k = linear(xn, proj["k_proj"]).reshape(tokens, kv_heads, head_dim)
-        v = linear(xn, proj["v_proj"]).reshape(tokens, kv_heads, head_dim)
-        q = bf16(rotate(rmsnorm(q, norms["q_norm"][i], eps), cos[:, None, :], sin[:, None, :]))
-        k = bf16(rotate(rmsnorm(k, norms["k_norm"][i], eps), cos[:, None, :], sin[:, None, :]))
-        for t in range(tokens):
-            k_caches[i][:, position + t] = k[t]
-            v_caches[i][:, position + t] = bf16(v[t])
-        a = bf16(attention(q, k_caches[i], v_caches[i], position + 1).reshape(tokens, q_heads * head_dim))
-        h = h + linear(a, proj["o_proj"])
-        xn = bf16(rmsnorm(h, norms["post_norm"][i], eps))
-        gate = linear(xn, proj["gate_proj"])
-        up = linear(xn, proj["up_proj"])
-        act = (gate / (1.0 + np.exp(-gate)) * up).astype(np.float32)
-        h = h + linear(act, proj["down_proj"])
-    xn = bf16(rmsnorm(h, norms["final_norm"], eps))
-    logits = (xn.astype(np.float64) @ norms["lm_head"].astype(np.float64).T).astype(np.float32)
+    logits = decode_step_streaming(hidden, len(layers), layer_at, norms["final_norm"], norms["lm_head"],
+                                   position=position, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, eps=eps,
+                                   theta=theta)
     return logits, k_caches, v_caches
 
 
-__all__ = ["attention", "bf16", "decode_step", "rmsnorm", "rope_tables", "rotate"]
+class CpuDecodeStep:
+    """A full decode step of a Qwen3-shaped decoder on the host cores: the timed CPU baseline.
+
+    The reference's CPU path for one step: its model shell's math (the
+    functions above) around ``PackedReferenceBackend.linear`` on every
+    projection (``packed_oracle.packed_linear``, fp32 like the reference on
+    fp32 inputs), then the dense lm head.  Every step runs all ``layers``
+    layers; their packed weights cycle through a pool of ``pool`` distinct
+    random layers (dense fp32 signs, unpacked once, as the reference's
+    ``prepare`` does), so host memory stays bounded while each layer still
+    streams its own ~0.8 GB of dense weights from DRAM.
+    """
+
+    def __init__(self, *, layers: int, hidden: int, intermediate: int, q_heads: int, kv_heads: int, head_dim: int,
+                 vocab: int, position: int, tokens: int = 1, pool: int = 2, bpw: float = 1.0, seed: int = 0,
+                 eps: float = 1e-6, theta: float = 1e6) -> None:
+        rng = np.random.default_rng(seed)
+        self.layers, self.tokens, self.position = layers, tokens, position
+        self.q_heads, self.kv_heads, self.head_dim, self.eps = q_heads, kv_heads, head_dim, eps
+        q, kv = q_heads * head_dim, kv_heads * head_dim
+        shapes = {"q_proj": (hidden, q), "k_proj": (hidden, kv), "v_proj": (hidden, kv), "o_proj": (q, hidden),
+                  "gate_proj": (hidden, intermediate), "up_proj": (hidden, intermediate),
+                  "down_proj": (intermediate, hidden)}
+
+        def words(rows: int, cols: int) -> np.ndarray:
+            raw = rng.integers(0, 2**32, size=(rows, po.word_count(cols)), dtype=np.uint64).astype(np.uint32)
+            if cols % 32:
+                raw[:, -1] &= np.uint32((1 << (cols % 32)) - 1)
+            return raw.view(np.int32)
+
+        def scales(size: int) -> np.ndarray:
+            return (np.abs(rng.standard_normal(size)) * 0.05 + 0.01).astype(np.float16).astype(np.float32)
+
+        def norm(size: int) -> np.ndarray:
+            return bf16((1.0 + 0.02 * rng.standard_normal(size)).astype(np.float32))
+
+        self.pool = []
+        for _ in range(pool):
+            proj = {}
+            for name, (n, m) in shapes.items():
+                r = int(bpw * m * n // (m + n))
+                layer = po.OracleLayer(n, m, r, words(m, r), words(r, n), scales(n), np.ones(r, np.float32),
+                                       scales(m))
+                layer.prepared()
+                proj[name] = layer
+            norms = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(head_dim),
+                     "k_norm": norm(head_dim)}
+            k = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
+            v = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
+            self.pool.append((proj, norms, k, v))
+        self.final_norm = norm(hidden)
+        # the 0.6 G-entry head: torch's generator and bf16 rounding (round to
+        # nearest even, as bf16() above) are several times faster than numpy's here
+        import torch
+
+        head = torch.randn(vocab, hidden, generator=torch.Generator().manual_seed(seed + 1)) * 0.02
+        self.lm_head = head.bfloat16().float().numpy()
+        self.theta = theta
+        self.hidden = rng.standard_normal((tokens, hidden), dtype=np.float32)
+
+    def step(self) -> np.ndarray:
+        pool = self.pool
+        return decode_step_streaming(self.hidden, self.layers, lambda i: pool[i % len(pool)], self.final_norm,
+                                     self.lm_head, position=self.position, q_heads=self.q_heads,
+                                     kv_heads=self.kv_heads, head_dim=self.head_dim, eps=self.eps, theta=self.theta,
+                                     accumulate="float32", head_accumulate="float32")
+
+
+__all__ = ["CpuDecodeStep", "attention", "bf16", "decode_layer", "decode_step", "decode_step_streaming",
+           "rmsnorm", "rope_tables", "rotate"]

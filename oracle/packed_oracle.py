@@ -28,11 +28,25 @@ fp32 inputs give fp32 matmuls (numpy/BLAS sgemm here, torch sgemm there).
 
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 
 import numpy as np
 
 WORD_BITS = 32
+
+# byte value -> its 8 columns as +/-1 (bit j of the byte is column j; 1 = -1)
+_BYTE_SIGNS = (1.0 - 2.0 * ((np.arange(256)[:, None] >> np.arange(8)) & 1)).astype(np.float32)
+_THREADS = max(1, min(32, os.cpu_count() or 1))
+_POOL: ThreadPoolExecutor | None = None
+
+
+def _pool() -> ThreadPoolExecutor:
+    global _POOL
+    if _POOL is None:
+        _POOL = ThreadPoolExecutor(_THREADS)
+    return _POOL
 
 
 # ---------------------------------------------------------------- layout v1 ---
@@ -83,11 +97,24 @@ def unpack_signs(words: np.ndarray, rows: int, columns: int) -> np.ndarray:
         raise ValueError("packed sign matrix must be int32 [rows, ceil(columns/32)]")
     if not padding_is_zero(words, columns):
         raise ValueError("packed sign matrix has a non-zero padding bit")
-    unsigned = words.view(np.uint32).astype(np.uint64)
-    lanes = np.arange(WORD_BITS, dtype=np.uint64)
-    bits = (unsigned[:, :, None] >> lanes) & np.uint64(1)
-    bits = bits.reshape(rows, -1)[:, :columns]
-    return (1.0 - 2.0 * bits.astype(np.float32)).astype(np.float32)
+    # little-endian words: byte b of word w holds columns 32w + 8b .. 32w + 8b + 7,
+    # least significant bit first, so each byte expands to its 8 columns in
+    # order through a 256-entry table of +/-1 rows (threads take row blocks:
+    # the copy is bound by first touches of the output pages)
+    raw = np.ascontiguousarray(words).view(np.uint8)
+    out = np.empty((rows, raw.shape[1] * 8), dtype=np.float32)
+    block = max(1, -(-rows // (4 * _THREADS)))
+
+    def expand(lo: int) -> None:
+        hi = min(rows, lo + block)
+        np.take(_BYTE_SIGNS, raw[lo:hi], axis=0, out=out[lo:hi].reshape(hi - lo, -1, 8))
+
+    if rows * raw.shape[1] < (1 << 16):
+        for lo in range(0, rows, block):
+            expand(lo)
+    else:
+        list(_pool().map(expand, range(0, rows, block)))
+    return out if out.shape[1] == columns else np.ascontiguousarray(out[:, :columns])
 
 
 # ----------------------------------------------------------- packed layer ---
