@@ -23,6 +23,7 @@ The same line carries:
   the output slices all-gathered over NCCL.
 
 Other workloads (``--workload``): ``decode-bs16`` (config 2 at batch 16),
+``gemma1b`` (config 1: the full Gemma-3-1B-shaped step from token ids),
 ``linears`` / ``linears-bs16`` (the packed linears alone), ``prefill``
 (config 3 alone), ``single-linear`` (config 0, ``--tokens`` 1 or 8) and
 ``single-linear-stacked`` (config 0 x 1024 layers in one program).
@@ -52,6 +53,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode tok/s (bs1, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs peak"
 UNIT = "tok/s"
 STEP_VOCAB, STEP_POSITION = 151936, 2048
+GEMMA_POSITION = 1024
 PREFILL_TOKENS = 8 * 4096
 
 
@@ -196,6 +198,30 @@ def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: fl
     }
 
 
+def cpu_gemma_baseline(tokens: int, steps: int = 3, warmup: int = 1) -> dict:
+    """The reference's CPU path for the full Gemma-3-1B step (26 layers, no vocabulary head)."""
+
+    from nanoquant_b200.decode_chain import GEMMA3_1B as s
+    from oracle.decoder_oracle import CpuDecodeStep
+
+    cpu = CpuDecodeStep(layers=s.layers, hidden=s.hidden, intermediate=s.intermediate, q_heads=s.q_heads,
+                        kv_heads=s.kv_heads, head_dim=s.head_dim, vocab=0, position=GEMMA_POSITION, tokens=tokens,
+                        pool=2, family="gemma")
+    for _ in range(warmup):
+        cpu.step()
+    start = time.perf_counter()
+    for _ in range(steps):
+        cpu.step()
+    per_step = (time.perf_counter() - start) / steps
+    threads = _cpu_threads()
+    return {"value": tokens / per_step, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": _cpu_model(),
+            "ms_per_step": per_step * 1e3, "steps": steps, "warmup": warmup,
+            "sample": f"full gemma-3-1b decode step, {tokens} token(s): 26 layers of the oracle port of "
+                      f"PackedReferenceBackend.linear (fp32, two distinct layers' weights cycled) and the Gemma-3 "
+                      f"shell (sandwich norms, q/k norm + rope, windowed attention over {GEMMA_POSITION + 1} rows, "
+                      f"gated gelu), final norm; {threads} host threads ({_cpu_model()}); {steps} timed steps"}
+
+
 def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200) -> dict:
     """The oracle port of ``PackedReferenceBackend.linear`` on one config-0 layer."""
 
@@ -282,6 +308,37 @@ class StepRunner:
         self.input = self.step_obj.hidden_in
         self.launches_per_step = self.step_obj.kernel_launches()
         self.step_obj.capture()
+
+    def run(self):
+        return self.step_obj.replay()
+
+    def algorithmic_bytes(self) -> int:
+        return self.step_obj.algorithmic_bytes()
+
+
+class GemmaStepRunner:
+    """The full Gemma-3-1B-shaped decode step (config 1) from token ids, replayed from a CUDA graph."""
+
+    bound = "hbm"
+
+    def __init__(self, device, tokens: int, layers: int | None) -> None:
+        import torch
+
+        from nanoquant_b200.decode_chain import GEMMA3_1B
+        from nanoquant_b200.decoder import build_gemma3_step
+
+        self.step_obj = build_gemma3_step(GEMMA3_1B, device, tokens=tokens, position=GEMMA_POSITION, layers=layers)
+        self.tokens = tokens
+        self.layers = len(self.step_obj.layers)
+        self.input = self.step_obj.ids
+        self.step_obj.ids.copy_(torch.arange(tokens, device=device) * 97 + 11)
+        self.launches_per_step = self.step_obj.kernel_launches()
+        self.step_obj.capture()
+
+    def host_input(self):
+        import torch
+
+        return (torch.arange(self.tokens) * 131 + 5).to(torch.int64)
 
     def run(self):
         return self.step_obj.replay()
@@ -415,6 +472,13 @@ WORKLOADS = {
                     "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head, 2048 cached "
                                    "tokens)",
                     "model": "qwen3-8b-shape random-init, as decode"},
+    "gemma1b": {"kind": "gemma", "metric": "decode tok/s (bs1, Gemma-3-1B shape ~1 bpw); HBM GB/s vs peak",
+                "tokens": 1,
+                "description": "gemma-3-1b decode step bs1 ({layers} layers: bf16 embedding, sandwich norms, packed "
+                               "q/k/v/o/gate/up/down, q/k norm + rope, attention over 1024 cached tokens (512-key "
+                               "window on local layers), gated gelu; final norm; no vocabulary head)",
+                "model": "gemma-3-1b-shape random-init: packed weights ~1 bpw (layout v1, fp16 scales), bf16 norms "
+                         "1+N(0,0.02) and embedding, bf16 kv cache N(0,1)"},
     "linears": {"kind": "linears", "metric": "packed-linear decode tok/s (bs1, Qwen3-8B shape ~1 bpw); HBM GB/s",
                 "tokens": 1,
                 "description": "qwen3-8b packed linears only, decode bs1 ({layers} layers x q,k,v,o,gate,up,down; "
@@ -448,6 +512,8 @@ def _build(name: str, device, tokens: int, layers: int | None, engine: str | Non
     kind = WORKLOADS[name]["kind"]
     if kind == "step":
         return StepRunner(device, tokens, layers)
+    if kind == "gemma":
+        return GemmaStepRunner(device, tokens, layers)
     if kind == "linears":
         return ChainRunner(decode_chain.QWEN3_8B, device, tokens, layers, engine)
     if kind == "prefill":
@@ -600,6 +666,8 @@ def run_reference(args, rank: int) -> None:
     tokens = args.tokens or spec.get("tokens", 1)
     if kind == "step":
         base = cpu_step_baseline(tokens, steps=args.steps, warmup=args.warmup)
+    elif kind == "gemma":
+        base = cpu_gemma_baseline(tokens, steps=args.steps, warmup=args.warmup)
     elif kind == "prefill":
         base = cpu_prefill_baseline()
     elif kind in ("single", "stacked"):
@@ -682,7 +750,8 @@ def main() -> None:
 
     # end to end through the public API: the step's input from pinned host
     # memory and its output back to pinned host memory, every step
-    host_in = torch.randn(tuple(runner.input.shape)).to(runner.input.dtype).pin_memory()
+    host_in = (runner.host_input() if hasattr(runner, "host_input")
+               else torch.randn(tuple(runner.input.shape)).to(runner.input.dtype)).pin_memory()
     out = runner.run()
     host_out = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
 
@@ -734,6 +803,7 @@ def main() -> None:
     else:
         step_bytes = runner.algorithmic_bytes()
         scope = {"step": "the whole decoder step: packed weights and scales, kv rows read, norms, lm head",
+                 "gemma": "the whole decoder step: packed weights and scales, kv rows read, norms, embedding rows",
                  "linears": "the persistent decode program: every packed linear of the step in one launch",
                  "single": "one launch pair of the config-0 layer", "stacked": "the program of 1024 layers"}[kind]
         line["roofline"] = _hbm_roofline(step_bytes, ms_per_step, peaks, scope)
@@ -764,6 +834,8 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if kind == "step":
             base = cpu_step_baseline(tokens)
+        elif kind == "gemma":
+            base = cpu_gemma_baseline(tokens)
         elif kind == "prefill":
             base = cpu_prefill_baseline()
         elif kind in ("single", "stacked"):

@@ -290,6 +290,19 @@ int nqb_decode_mixed_v(const int32_t *free_words, int64_t free_rows, int64_t ran
  *   Split-K partials go to the workspace (nqb_decode_attention_workspace_bytes).
  *   Alignment (else NQB_ERR_ALIGNMENT): k_cache, v_cache and workspace 16
  *   bytes; q and out head_dim / 16 bytes (8 for head_dim 128).
+ * nqb_rmsnorm_residual: nqb_rmsnorm whose delta is normalised first when
+ *   delta_weight is given: h += delta * rsqrt(mean(delta^2) + eps) *
+ *   delta_weight, then out = h * rsqrt(mean(h^2) + eps) * weight (both
+ *   weights in weight_dtype).  Gemma-3's sandwich norms: the post-attention
+ *   (or post-feedforward) norm of the delta, the residual add and the next
+ *   pre-norm in one pass (reference runtime/torch_model.py:637-653).
+ * nqb_decode_attention_window: nqb_decode_attention where token t sees only
+ *   the last `window` rows [keys + t - window, keys + t) (window 0: all);
+ *   Gemma-3's sliding-window layers (torch_model.py:573-614).
+ * nqb_embedding_bf16: out[t, :] = float(weight[ids[t], :]) * scale; weight
+ *   bf16 [rows, dim], ids int64 [tokens], out fp32 [tokens, dim]; an id
+ *   outside [0, rows) gives a zero row.  Replaces launch_bfloat16_embedding
+ *   (reference cuda_kernels.py:620-668).
  * nqb_silu_mul: out[i] = silu(gate[i]) * up[i] over `count` fp32 values.
  * nqb_gemv_bf16: out[t, r] = sum_c weight[r, c] * x[t, c]; weight bf16
  *   [rows, cols] (cols a multiple of 8, at most 51200, 16-byte aligned),
@@ -306,6 +319,14 @@ int nqb_decode_attention_workspace_bytes(int64_t keys, int64_t tokens, int32_t q
 int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len, int64_t keys,
                          int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim, void *out,
                          void *workspace, size_t workspace_bytes, void *stream);
+int nqb_rmsnorm_residual(float *h, const float *delta, const void *delta_weight, const void *weight,
+                         int32_t weight_dtype, int64_t tokens, int64_t hidden, float eps, void *out, int32_t out_dtype,
+                         void *stream);
+int nqb_decode_attention_window(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len,
+                                int64_t keys, int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                                int64_t window, void *out, void *workspace, size_t workspace_bytes, void *stream);
+int nqb_embedding_bf16(const int64_t *ids, int64_t tokens, const void *weight, int64_t rows, int64_t dim, float scale,
+                       float *out, void *stream);
 int nqb_silu_mul(const float *gate, const float *up, int64_t count, void *out, int32_t out_dtype, void *stream);
 int nqb_gemv_bf16(const void *weight, int64_t rows, int64_t cols, const void *x, int64_t tokens, float *out,
                   void *stream);
@@ -364,14 +385,18 @@ int nqb_device_status(int32_t *status);
  * its input, so a gate/up op and the down op that consumes it share one
  * program.  Members of such an op carry no salient columns or overlay rows. */
 #define NQB_X_SWIGLU 16
+/* Program op input code: like NQB_X_SWIGLU with gelu_tanh(gate) * up, the
+ * tanh form of GELU (Gemma-3's gated-GELU MLP, reference
+ * runtime/torch_model.py:460-505).                                          */
+#define NQB_X_GEGLU 17
 
 typedef struct nqb_program_op {
   const nqb_linear_desc *layers; /* count members sharing x */
   int32_t count;                 /* 1..3 */
   const void *x;                 /* [tokens, in_features], x_dtype */
-  int32_t x_dtype;               /* NQB_F32 / NQB_F16 / NQB_BF16, or NQB_X_SWIGLU */
+  int32_t x_dtype;               /* NQB_F32 / NQB_F16 / NQB_BF16, NQB_X_SWIGLU or NQB_X_GEGLU */
   float *const *y;               /* count outputs [tokens, out_features] fp32 */
-  const void *x2;                /* NQB_X_SWIGLU only: the up projection; else NULL */
+  const void *x2;                /* NQB_X_SWIGLU / NQB_X_GEGLU: the up projection; else NULL */
 } nqb_program_op;
 
 typedef struct nqb_program nqb_program;

@@ -35,6 +35,7 @@ NQB_BF16 = 2
 NQB_I8 = 3
 NQB_I32 = 4
 NQB_X_SWIGLU = 16  # program-op input: silu(x) * x2, both fp32
+NQB_X_GEGLU = 17  # program-op input: gelu_tanh(x) * x2, both fp32
 
 DTYPE_CODES = {
     torch.float32: NQB_F32,
@@ -171,6 +172,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_silu_mul": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _i32, _c_void_p]),
     "nqb_gemv_bf16": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "nqb_workspace_reset": (ctypes.c_int, [_c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_rmsnorm_residual": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64,
+                                            ctypes.c_float, _c_void_p, _i32, _c_void_p]),
+    "nqb_decode_attention_window": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _i32,
+                                                   _i32, _i64, _c_void_p, _c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_embedding_bf16": (ctypes.c_int, [_c_void_p, _i64, _c_void_p, _i64, _i64, ctypes.c_float, _c_void_p,
+                                          _c_void_p]),
     "nqb_debug_set_barrier_limit": (ctypes.c_int, [ctypes.c_uint32]),
     "nqb_program_debug_barrier_skew": (ctypes.c_int, [_c_void_p, ctypes.c_uint32]),
 }

@@ -85,6 +85,31 @@ struct SwigluLoader {  // stage 1 of a down projection: silu(gate) * up * pre, g
   }
 };
 
+// GELU (tanh form, Hendrycks & Gimpel 2016) of g: 0.5 g (1 + tanh(u)),
+// u = sqrt(2/pi) (g + 0.044715 g^3), with tanh(u) = 1 - 2 / (1 + e^(2u)).  The
+// exponent is clamped to +-80 so the divisor stays inside __fdividef's range
+// (tanh is +-1 to float precision there).
+__device__ __forceinline__ float gelu_tanh(float g) {
+  const float u = 0.7978845608028654f * (g + 0.044715f * g * g * g);
+  const float e = __expf(fminf(fmaxf(2.0f * u, -80.0f), 80.0f));
+  return 0.5f * g * (2.0f - __fdividef(2.0f, 1.0f + e));
+}
+
+struct GegluLoader {  // stage 1 of a gated-GELU down projection: gelu_tanh(gate) * up * pre
+  const float *gate;
+  const float *up;
+  const float *pre;
+  int64_t stride;
+  int64_t k0;
+  int64_t k_valid;
+  __device__ __forceinline__ float operator()(int t, int col) const {
+    const int64_t k = k0 + col;
+    if (k >= k_valid) return 0.0f;
+    const int64_t i = static_cast<int64_t>(t) * stride + k;
+    return gelu_tanh(__ldcg(gate + i)) * __ldcg(up + i) * __ldg(pre + k);
+  }
+};
+
 struct LatentLoader {  // stage 2: the fp32 latent slice of one member
   const float *latent;
   int64_t stride;

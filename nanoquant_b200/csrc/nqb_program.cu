@@ -105,7 +105,7 @@ struct OpDev {
   MemberDev s[2][kMaxMembersTc];  // [stage][member]
   int32_t count;
   const void *x;
-  const void *x2;  // NQB_X_SWIGLU: the up projection (x is the gate)
+  const void *x2;  // NQB_X_SWIGLU / NQB_X_GEGLU: the up projection (x is the gate)
   int32_t x_dtype;
   int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
   int64_t n;
@@ -731,6 +731,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                                                             static_cast<const float *>(op.x2), md.pre, op.n, k0,
                                                             md.k_valid},
                                          nst, T, cv);
+            } else if (op.x_dtype == NQB_X_GEGLU) {
+              mmad::load_chunk<kT, kQPT>(mmad::GegluLoader{static_cast<const float *>(op.x),
+                                                           static_cast<const float *>(op.x2), md.pre, op.n, k0,
+                                                           md.k_valid},
+                                         nst, T, cv);
             } else if (op.x_dtype == NQB_BF16) {
               mmad::load_chunk<kT, kQPT>(mmad::XLoader<__nv_bfloat16>{static_cast<const __nv_bfloat16 *>(op.x), md.pre,
                                                                      op.n, k0, md.k_valid},
@@ -822,6 +827,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
               } else if (op.x_dtype == NQB_X_SWIGLU) {
                 const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
                                             md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_X_GEGLU) {
+                const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                           md.pre, op.n, k0, md.k_valid};
                 mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
               } else if (op.x_dtype == NQB_BF16) {
                 const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
@@ -1218,12 +1227,12 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     if (o.layers == nullptr || o.count < 1 || o.count > kMaxMembersTc)
       return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: 1 to %d layers", i, kMaxMembersTc);
     if (o.x == nullptr || o.y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: x or y is NULL", i);
-    const bool swiglu = o.x_dtype == NQB_X_SWIGLU;
-    if (swiglu && o.x2 == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a SwiGLU input needs x2", i);
+    const bool swiglu = o.x_dtype == NQB_X_SWIGLU || o.x_dtype == NQB_X_GEGLU;
+    if (swiglu && o.x2 == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a gated input needs x2", i);
     if (swiglu)
       for (int k = 0; k < o.count; ++k)
         if (o.layers[k].outlier_count > 0 || o.layers[k].overlay_rows > 0 || o.layers[k].patch_rank > 0)
-          return fail(NQB_ERR_UNSUPPORTED, "op %d: SwiGLU inputs take no salient columns, overlay rows or patch", i);
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: gated inputs take no salient columns, overlay rows or patch", i);
     int64_t rank_total = 0;
     for (int k = 0; k < o.count; ++k) {
       const nqb_linear_desc &d = o.layers[k];
@@ -1298,7 +1307,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     std::memset(&od, 0, sizeof(od));
     od.count = o.count;
     od.x = o.x;
-    od.x2 = o.x_dtype == NQB_X_SWIGLU ? o.x2 : nullptr;
+    od.x2 = (o.x_dtype == NQB_X_SWIGLU || o.x_dtype == NQB_X_GEGLU) ? o.x2 : nullptr;
     od.x_dtype = o.x_dtype;
     od.n = o.layers[0].in_features;
     int64_t offset = 0;
@@ -1399,7 +1408,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
                                                  md.k_valid);
             if (hi > lo) {
               add_lines(lines, md.pre + lo, (hi - lo) * 4);
-              const bool swiglu = op.x_dtype == NQB_X_SWIGLU;
+              const bool swiglu = op.x_dtype == NQB_X_SWIGLU || op.x_dtype == NQB_X_GEGLU;
               const int64_t xs = swiglu ? 4 : static_cast<int64_t>(dtype_size(op.x_dtype));
               for (int64_t t = 0; t < tokens; ++t) {
                 add_lines(lines, static_cast<const char *>(op.x) + (t * op.n + lo) * xs, (hi - lo) * xs);

@@ -83,14 +83,20 @@ __device__ __forceinline__ void store4_as(void *p, int64_t i, int32_t dt, float4
   *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(p) + i) = raw;
 }
 
+//
+// With `dw` (the delta's own norm weight), the delta is normalised before the
+// add: h += delta * rsqrt(mean(delta^2) + eps) * dw (Gemma-3's post-attention
+// and post-feedforward norms), then out is formed from the new h as above.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *delta, const void *w, int32_t w_dt,
-                                                      int64_t hidden, float eps, void *out, int32_t out_dt) {
+                                                      int64_t hidden, float eps, void *out, int32_t out_dt,
+                                                      const void *dw = nullptr) {
   __shared__ float scratch[32];
   allow_dependents();
   const int64_t t = blockIdx.x;
   const bool vec = hidden % 4 == 0 && hidden <= 1024 * kRmsVec && reinterpret_cast<uintptr_t>(h) % 16 == 0 &&
                    (delta == nullptr || reinterpret_cast<uintptr_t>(delta) % 16 == 0) &&
-                   reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+                   reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(dw) % 16 == 0;
   if (vec) {
     float4 *row4 = reinterpret_cast<float4 *>(h + t * hidden);
     const float4 *d4 = delta != nullptr ? reinterpret_cast<const float4 *>(delta + t * hidden) : nullptr;
@@ -103,15 +109,36 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *del
       wv[j] = i < n4 ? load4_as_float(w, 4 * static_cast<int64_t>(i), w_dt) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     if (d4 != nullptr) {
+      float4 dv[kRmsVec], dwv[kRmsVec];
+#pragma unroll
+      for (int j = 0; j < kRmsVec; ++j) {
+        const int i = threadIdx.x + j * 256;
+        dv[j] = i < n4 ? d4[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        dwv[j] = dw != nullptr && i < n4 ? load4_as_float(dw, 4 * static_cast<int64_t>(i), w_dt)
+                                         : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      }
+      if (dw != nullptr) {
+        float dss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kRmsVec; ++j)
+          dss += dv[j].x * dv[j].x + dv[j].y * dv[j].y + dv[j].z * dv[j].z + dv[j].w * dv[j].w;
+        const float dr = rsqrtf(block_sum(dss, scratch) / static_cast<float>(hidden) + eps);
+#pragma unroll
+        for (int j = 0; j < kRmsVec; ++j) {
+          dv[j].x = dv[j].x * dr * dwv[j].x;
+          dv[j].y = dv[j].y * dr * dwv[j].y;
+          dv[j].z = dv[j].z * dr * dwv[j].z;
+          dv[j].w = dv[j].w * dr * dwv[j].w;
+        }
+      }
 #pragma unroll
       for (int j = 0; j < kRmsVec; ++j) {
         const int i = threadIdx.x + j * 256;
         if (i < n4) {
-          const float4 d = d4[i];
-          v[j].x += d.x;
-          v[j].y += d.y;
-          v[j].z += d.z;
-          v[j].w += d.w;
+          v[j].x += dv[j].x;
+          v[j].y += dv[j].y;
+          v[j].z += dv[j].z;
+          v[j].w += dv[j].w;
           row4[i] = v[j];
         }
       }
@@ -131,11 +158,17 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float *h, const float *del
   }
   float *row = h + t * hidden;
   const float *drow = delta != nullptr ? delta + t * hidden : nullptr;
+  float dr = 1.0f;
+  if (drow != nullptr && dw != nullptr) {
+    float dss = 0.0f;
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) dss += drow[i] * drow[i];
+    dr = rsqrtf(block_sum(dss, scratch) / static_cast<float>(hidden) + eps);
+  }
   float ss = 0.0f;
   for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
     float v = row[i];
     if (drow != nullptr) {
-      v += drow[i];
+      v += dw != nullptr ? drow[i] * dr * load_as_float(dw, i, w_dt) : drow[i];
       row[i] = v;
     }
     ss += v * v;
@@ -286,7 +319,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <int kDpl>
 __global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bfloat16 *kc, const __nv_bfloat16 *vc,
                                          int64_t cache_len, int64_t keys, int32_t q_heads, int32_t kv_heads,
-                                         int32_t splits, int64_t chunk, float scale, float *part) {
+                                         int32_t splits, int64_t chunk, float scale, float *part, int64_t window) {
   constexpr int kHd = 32 * kDpl;
   constexpr int kB = kDpl <= 4 ? 8 : 4;
   const int kh = blockIdx.x, sp = blockIdx.y;
@@ -296,8 +329,10 @@ __global__ void attention_partial_kernel(const __nv_bfloat16 *q, const __nv_bflo
   const int qh = kh * group + warp;
   const int d0 = lane * kDpl;
   const int64_t visible = keys + t;
-  const int64_t j0 = static_cast<int64_t>(sp) * chunk;
-  const int64_t j1 = min(j0 + chunk, visible);
+  // a sliding window of `window` keys ends at the token's own row
+  const int64_t first = window > 0 && visible > window ? visible - window : 0;
+  const int64_t j0 = max(static_cast<int64_t>(sp) * chunk, first);
+  const int64_t j1 = min(static_cast<int64_t>(sp) * chunk + chunk, visible);
   float qv[kDpl], acc[kDpl];
   load_bf16_row<kDpl>(q + (t * q_heads + qh) * kHd + d0, qv);
 #pragma unroll
@@ -425,6 +460,37 @@ __global__ void attention_combine_kernel(const float *part, int32_t splits, int6
   for (int e = 0; e < kDpl; ++e) out[gw * kHd + lane * kDpl + e] = __float2bfloat16_rn(num[e] * inv);
 }
 
+// out[t, :] = float(W[ids[t], :]) * scale: one block per token, 16-byte
+// loads of the bf16 row (dim a multiple of 8, 16-byte aligned rows) or a
+// scalar loop; an id outside [0, rows) gives a zero row.
+__global__ void __launch_bounds__(256) embedding_bf16_kernel(const int64_t *ids, const __nv_bfloat16 *w, int64_t rows,
+                                                             int64_t dim, float scale, float *out) {
+  allow_dependents();
+  const int64_t t = blockIdx.x;
+  const int64_t id = ids[t];
+  float *o = out + t * dim;
+  const bool valid = id >= 0 && id < rows;
+  if (dim % 8 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(w + (valid ? id : 0) * dim);
+    for (int64_t u = threadIdx.x; u < dim / 8; u += blockDim.x) {
+      float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f), b = a;
+      if (valid) {
+        const uint4 raw = __ldg(src + u);
+        const __nv_bfloat162 *pairs = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+        const float2 f0 = __bfloat1622float2(pairs[0]), f1 = __bfloat1622float2(pairs[1]);
+        const float2 f2 = __bfloat1622float2(pairs[2]), f3 = __bfloat1622float2(pairs[3]);
+        a = make_float4(f0.x * scale, f0.y * scale, f1.x * scale, f1.y * scale);
+        b = make_float4(f2.x * scale, f2.y * scale, f3.x * scale, f3.y * scale);
+      }
+      reinterpret_cast<float4 *>(o)[2 * u] = a;
+      reinterpret_cast<float4 *>(o)[2 * u + 1] = b;
+    }
+    return;
+  }
+  for (int64_t i = threadIdx.x; i < dim; i += blockDim.x)
+    o[i] = valid ? __bfloat162float(w[id * dim + i]) * scale : 0.0f;
+}
+
 __global__ void silu_mul_kernel(const float *gate, const float *up, int64_t n, void *out, int32_t out_dt) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -502,12 +568,31 @@ extern "C" {
 
 int nqb_rmsnorm(float *h, const float *delta, const void *weight, int32_t weight_dtype, int64_t tokens, int64_t hidden,
                 float eps, void *out, int32_t out_dtype, void *stream) {
+  return nqb_rmsnorm_residual(h, delta, nullptr, weight, weight_dtype, tokens, hidden, eps, out, out_dtype, stream);
+}
+
+int nqb_rmsnorm_residual(float *h, const float *delta, const void *delta_weight, const void *weight,
+                         int32_t weight_dtype, int64_t tokens, int64_t hidden, float eps, void *out, int32_t out_dtype,
+                         void *stream) {
   if (h == nullptr || weight == nullptr || out == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "rmsnorm operand is NULL");
+  if (delta_weight != nullptr && delta == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "rmsnorm delta weight given without a delta");
   if (tokens <= 0 || hidden <= 0 || !(eps >= 0.0f)) return fail(NQB_ERR_INVALID_ARGUMENT, "rmsnorm shape or eps invalid");
   if (!is_float_dtype(weight_dtype) || !is_float_dtype(out_dtype)) return fail(NQB_ERR_DTYPE, "rmsnorm dtype invalid");
   shell::rmsnorm_kernel<<<static_cast<unsigned>(tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      h, delta, weight, weight_dtype, hidden, eps, out, out_dtype);
+      h, delta, weight, weight_dtype, hidden, eps, out, out_dtype, delta_weight);
   NQB_CUDA(cudaGetLastError(), "rmsnorm launch");
+  return ok();
+}
+
+int nqb_embedding_bf16(const int64_t *ids, int64_t tokens, const void *weight, int64_t rows, int64_t dim, float scale,
+                       float *out, void *stream) {
+  if (ids == nullptr || weight == nullptr || out == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "embedding operand is NULL");
+  if (tokens <= 0 || rows <= 0 || dim <= 0) return fail(NQB_ERR_INVALID_ARGUMENT, "embedding shape invalid");
+  shell::embedding_bf16_kernel<<<static_cast<unsigned>(tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16 *>(weight), rows, dim, scale, out);
+  NQB_CUDA(cudaGetLastError(), "embedding launch");
   return ok();
 }
 
@@ -563,6 +648,14 @@ int nqb_decode_attention_workspace_bytes(int64_t keys, int64_t tokens, int32_t q
 int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len, int64_t keys,
                          int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim, void *out,
                          void *workspace, size_t workspace_bytes, void *stream) {
+  return nqb_decode_attention_window(q, k_cache, v_cache, cache_len, keys, tokens, q_heads, kv_heads, head_dim, 0, out,
+                                     workspace, workspace_bytes, stream);
+}
+
+int nqb_decode_attention_window(const void *q, const void *k_cache, const void *v_cache, int64_t cache_len,
+                                int64_t keys, int64_t tokens, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                                int64_t window, void *out, void *workspace, size_t workspace_bytes, void *stream) {
+  if (window < 0) return fail(NQB_ERR_INVALID_ARGUMENT, "attention window must be >= 0");
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || workspace == nullptr)
     return fail(NQB_ERR_INVALID_ARGUMENT, "attention operand is NULL");
   if (tokens <= 0 || keys <= 0 || keys + tokens - 1 > cache_len || kv_heads <= 0 || q_heads % kv_heads != 0 ||
@@ -595,21 +688,21 @@ int nqb_decode_attention(const void *q, const void *k_cache, const void *v_cache
       NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<2>),
                                     shell::attention_smem_bytes(64)));
       shell::attention_partial_kernel<2><<<grid, threads, shell::attention_smem_bytes(64), s>>>(
-          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part, window);
       shell::attention_combine_kernel<2><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     case 128:
       NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<4>),
                                     shell::attention_smem_bytes(128)));
       shell::attention_partial_kernel<4><<<grid, threads, shell::attention_smem_bytes(128), s>>>(
-          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part, window);
       shell::attention_combine_kernel<4><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     case 256:
       NQB_CHECK(ensure_dynamic_smem(reinterpret_cast<const void *>(shell::attention_partial_kernel<8>),
                                     shell::attention_smem_bytes(256)));
       shell::attention_partial_kernel<8><<<grid, threads, shell::attention_smem_bytes(256), s>>>(
-          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part);
+          qp, kc, vc, cache_len, keys, q_heads, kv_heads, splits, chunk, scale, part, window);
       shell::attention_combine_kernel<8><<<cblocks, 256, 0, s>>>(part, splits, tokens, q_heads, o);
       break;
     default:

@@ -40,11 +40,19 @@ def _stream(device: torch.device) -> int:
     return _native.current_stream_handle(device)
 
 
-def rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
-    """``h += delta`` (when given), ``out = h * rsqrt(mean(h^2) + eps) * weight`` per token (``nqb_rmsnorm``)."""
+def rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float, out: torch.Tensor,
+            delta_weight: torch.Tensor | None = None) -> None:
+    """``h += delta`` (when given), ``out = h * rsqrt(mean(h^2) + eps) * weight`` per token (``nqb_rmsnorm``).
+
+    With ``delta_weight`` the delta is RMS-normalised with it before the add
+    (``nqb_rmsnorm_residual``: Gemma-3's post-attention / post-feedforward norms).
+    """
 
     tokens, hidden = h.shape
-    _native.call("nqb_rmsnorm", h.data_ptr(), 0 if delta is None else delta.data_ptr(), weight.data_ptr(),
+    if delta_weight is not None and delta_weight.dtype != weight.dtype:
+        raise ValueError("both norm weights share one dtype")
+    _native.call("nqb_rmsnorm_residual", h.data_ptr(), 0 if delta is None else delta.data_ptr(),
+                 0 if delta_weight is None else delta_weight.data_ptr(), weight.data_ptr(),
                  _native.dtype_code(weight.dtype), tokens, hidden, ctypes.c_float(eps), out.data_ptr(),
                  _native.dtype_code(out.dtype), _stream(h.device))
 
@@ -68,12 +76,22 @@ def attention_workspace_bytes(keys: int, tokens: int, q_heads: int, head_dim: in
 
 
 def decode_attention(q, k_cache, v_cache, keys: int, q_heads: int, kv_heads: int, head_dim: int, out,
-                     workspace: torch.Tensor) -> None:
-    """Grouped-query attention of ``tokens`` queries over the caches (``nqb_decode_attention``)."""
+                     workspace: torch.Tensor, window: int = 0) -> None:
+    """Grouped-query attention of ``tokens`` queries over the caches (``nqb_decode_attention_window``).
 
-    _native.call("nqb_decode_attention", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[1], keys,
-                 q.shape[0], q_heads, kv_heads, head_dim, out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-                 _stream(q.device))
+    ``window > 0``: token t sees only the last ``window`` cache rows ending at its own.
+    """
+
+    _native.call("nqb_decode_attention_window", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                 k_cache.shape[1], keys, q.shape[0], q_heads, kv_heads, head_dim, window, out.data_ptr(),
+                 workspace.data_ptr(), workspace.numel(), _stream(q.device))
+
+
+def embedding_bf16(ids: torch.Tensor, weight: torch.Tensor, scale: float, out: torch.Tensor) -> None:
+    """``out[t] = weight[ids[t]] * scale`` in fp32 (``nqb_embedding_bf16``)."""
+
+    _native.call("nqb_embedding_bf16", ids.data_ptr(), ids.numel(), weight.data_ptr(), weight.shape[0],
+                 weight.shape[1], ctypes.c_float(scale), out.data_ptr(), _stream(ids.device))
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
@@ -278,6 +296,208 @@ class Qwen3DecodeStep:
         return packed + kv + head + norms
 
 
+@dataclass
+class GemmaShellWeights:
+    """The dense weights of a Gemma-3 decoder: per-layer norms (stored weights w, applied as 1 + w), the final
+    norm and the bf16 embedding table."""
+
+    input_norm: list[torch.Tensor]
+    post_attention_norm: list[torch.Tensor]
+    pre_feedforward_norm: list[torch.Tensor]
+    post_feedforward_norm: list[torch.Tensor]
+    q_norm: list[torch.Tensor]
+    k_norm: list[torch.Tensor]
+    final_norm: torch.Tensor
+    embedding: torch.Tensor
+
+
+def random_gemma_shell_weights(shape: DecoderShape, vocab: int, device: torch.device, *, layers: int | None = None,
+                               seed: int = 1) -> GemmaShellWeights:
+    """bf16 norm weights ``1 + N(0, 0.02)`` and a bf16 embedding table ``N(0, 1)`` (random init)."""
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    count = shape.layers if layers is None else layers
+
+    def norm(size: int) -> torch.Tensor:
+        return (1.0 + 0.02 * torch.randn(size, generator=g, device=device)).bfloat16()
+
+    def per_layer(size: int) -> list[torch.Tensor]:
+        return [norm(size) for _ in range(count)]
+
+    return GemmaShellWeights(per_layer(shape.hidden), per_layer(shape.hidden), per_layer(shape.hidden),
+                             per_layer(shape.hidden), per_layer(shape.head_dim), per_layer(shape.head_dim),
+                             norm(shape.hidden), torch.randn(vocab, shape.hidden, generator=g, device=device).bfloat16())
+
+
+class Gemma3DecodeStep:
+    """One Gemma-3 decode step of ``tokens`` new tokens at cache position ``position``.
+
+    Per layer (reference ``runtime/torch_model.py:233-681``, HF Gemma-3
+    semantics): ``xn = rmsnorm(h) * (1 + w_in)``; q, k, v (one program); q/k
+    head norms ``(1 + w)`` and rotate-half RoPE (local layers theta 1e4 with a
+    ``sliding_window``-key window, every ``global_every``-th layer global with
+    theta 1e6 and full attention); attention scaled by ``head_dim^-1/2``
+    (``query_pre_attn_scalar`` = head_dim); o; ``h += rmsnorm(o) * (1 +
+    w_post_attn)``; ``xn = rmsnorm(h) * (1 + w_pre_ff)``; the gated-GELU MLP
+    (gate/up and down with ``gelu_tanh(gate) * up`` formed as down loads it,
+    one program); ``h += rmsnorm(down) * (1 + w_post_ff)``.  The sandwich
+    norms run as ``nqb_rmsnorm_residual`` with the next pre-norm fused in.  The
+    step starts from token ids (``nqb_embedding_bf16``, scale ``sqrt(hidden)``
+    rounded to bf16 as Gemma's normaliser is) and returns the final-normed
+    hidden states ``[tokens, hidden]`` fp32 (config 1 has no vocabulary head).
+    Activations fed to the packed projections are fp32, like the reference's
+    fp32 decode path; q, the caches and the attention output are bf16.
+    """
+
+    def __init__(self, shape: DecoderShape, blocks, shell: GemmaShellWeights, device: torch.device, *,
+                 tokens: int = 1, position: int = 0, cache_len: int | None = None, eps: float = 1e-6,
+                 sliding_window: int = 512, global_every: int = 6, local_theta: float = 1e4,
+                 global_theta: float = 1e6, kv_init: torch.Generator | None = None) -> None:
+        if not 1 <= tokens <= 16:
+            raise ValueError("a decode step takes 1 to 16 tokens")
+        self.shape, self.device, self.tokens, self.position, self.eps = shape, device, tokens, position, eps
+        self.shell = shell
+        self.cache_len = cache_len if cache_len is not None else position + tokens
+        if position + tokens > self.cache_len:
+            raise ValueError("the cache is too short for the step's tokens")
+        backend = CudaPackedSm100Backend()
+        hd, hq, hkv = shape.head_dim, shape.q_heads, shape.kv_heads
+        f32 = {"dtype": torch.float32, "device": device}
+        bf16 = {"dtype": torch.bfloat16, "device": device}
+
+        def gemma(w: torch.Tensor) -> torch.Tensor:  # Gemma's RMSNorm applies (1 + w), computed in fp32
+            return (1.0 + w.float()).contiguous()
+
+        self.w_in = [gemma(w) for w in shell.input_norm]
+        self.w_post_attn = [gemma(w) for w in shell.post_attention_norm]
+        self.w_pre_ff = [gemma(w) for w in shell.pre_feedforward_norm]
+        self.w_post_ff = [gemma(w) for w in shell.post_feedforward_norm]
+        self.w_q = [gemma(w) for w in shell.q_norm]
+        self.w_k = [gemma(w) for w in shell.k_norm]
+        self.w_final = gemma(shell.final_norm)
+        self.embed_scale = float(torch.tensor(shape.hidden ** 0.5).bfloat16().float())
+        self.ids = torch.zeros(tokens, dtype=torch.int64, device=device)  # the step's input token ids
+        self.h = torch.zeros(tokens, shape.hidden, **f32)
+        self.xn = torch.zeros(tokens, shape.hidden, **f32)
+        self.out = torch.zeros(tokens, shape.hidden, **f32)
+        self.q_rot = torch.zeros(tokens, hq * hd, **bf16)
+        self.attn = torch.zeros(tokens, hq * hd, **bf16)
+        self.keys = position + 1
+        self.attn_ws = torch.empty(attention_workspace_bytes(self.keys, tokens, hq, hd), dtype=torch.uint8,
+                                   device=device)
+        positions = torch.arange(position, position + tokens)
+        self.rope = {theta: tuple(t.to(device) for t in rope_tables(positions, hd, theta))
+                     for theta in (local_theta, global_theta)}
+        g = kv_init if kv_init is not None else torch.Generator(device=device).manual_seed(2)
+        self.layers = []
+        for index, block in enumerate(blocks):
+            prepared = {name: backend.prepare(state, device) for name, state in block.items()}
+            q = torch.zeros(tokens, hq * hd, **f32)
+            k = torch.zeros(tokens, hkv * hd, **f32)
+            v = torch.zeros(tokens, hkv * hd, **f32)
+            o = torch.zeros(tokens, shape.hidden, **f32)
+            gate = torch.zeros(tokens, shape.intermediate, **f32)
+            up = torch.zeros(tokens, shape.intermediate, **f32)
+            down = torch.zeros(tokens, shape.hidden, **f32)
+            kc = torch.zeros(hkv, self.cache_len, hd, **bf16)
+            vc = torch.zeros(hkv, self.cache_len, hd, **bf16)
+            if position:
+                kc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
+                vc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
+            is_global = (index + 1) % global_every == 0
+            self.layers.append({
+                "prog_qkv": DecodeProgram([ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]),
+                                                     self.xn)], outputs=[(q, k, v)]),
+                "prog_o": DecodeProgram([ProgramOp((prepared["o_proj"],), self.attn)], outputs=[(o,)]),
+                "prog_mlp": DecodeProgram([ProgramOp((prepared["gate_proj"], prepared["up_proj"]), self.xn),
+                                           ProgramOp((prepared["down_proj"],), gate, x2=up, activation="gelu_tanh")],
+                                          outputs=[(gate, up), (down,)]),
+                "q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc, "v_cache": vc,
+                "prepared": prepared, "window": 0 if is_global else sliding_window,
+                "theta": global_theta if is_global else local_theta,
+            })
+        self.graph: torch.cuda.CUDAGraph | None = None
+
+    def kernel_launches(self) -> int:
+        """Kernels one step launches: the embedding and the first norm, then per layer 3 programs, rope,
+        attention (2) and 2 norms."""
+
+        return 2 + 8 * len(self.layers)
+
+    def step(self, ids: torch.Tensor | None = None) -> torch.Tensor:
+        s, hd = self.shape, self.shape.head_dim
+        if ids is not None:
+            self.ids.copy_(ids)
+        embedding_bf16(self.ids, self.shell.embedding, self.embed_scale, self.h)
+        rmsnorm(self.h, None, self.w_in[0], self.eps, self.xn)
+        last = len(self.layers) - 1
+        for index, layer in enumerate(self.layers):
+            cos, sin = self.rope[layer["theta"]]
+            layer["prog_qkv"].run(dependent=True)
+            qk_norm_rope(layer["q"], layer["k"], layer["v"], self.w_q[index], self.w_k[index], cos, sin, self.q_rot,
+                         layer["k_cache"], layer["v_cache"], self.position, self.eps, s.q_heads, s.kv_heads, hd)
+            decode_attention(self.q_rot, layer["k_cache"], layer["v_cache"], self.keys, s.q_heads, s.kv_heads, hd,
+                             self.attn, self.attn_ws, window=layer["window"])
+            layer["prog_o"].run(dependent=True)
+            rmsnorm(self.h, layer["o"], self.w_pre_ff[index], self.eps, self.xn, delta_weight=self.w_post_attn[index])
+            layer["prog_mlp"].run(dependent=True)
+            if index < last:
+                rmsnorm(self.h, layer["down"], self.w_in[index + 1], self.eps, self.xn,
+                        delta_weight=self.w_post_ff[index])
+            else:
+                rmsnorm(self.h, layer["down"], self.w_final, self.eps, self.out, delta_weight=self.w_post_ff[index])
+        return self.out
+
+    def capture(self) -> None:
+        """Record one step (from the current ids) into a CUDA graph; :meth:`replay` then reruns it."""
+
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.step()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step()
+        self.graph = graph
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+        return self.out
+
+    def algorithmic_bytes(self) -> int:
+        """Bytes one step must move: packed weights and scales, the KV rows attention reads, norms, embedding rows."""
+
+        s = self.shape
+        packed = 0
+        for layer in self.layers:
+            for prepared in layer["prepared"].values():
+                spec = prepared.spec
+                packed += (spec.out_features * ((spec.rank + 31) // 32) + spec.rank * ((spec.in_features + 31) // 32)) * 4
+                packed += (spec.in_features + spec.rank + spec.out_features) * 2
+        kv = 0
+        for layer in self.layers:
+            rows = 0
+            for t in range(self.tokens):
+                visible = self.keys + t
+                rows = max(rows, min(visible, layer["window"]) if layer["window"] else visible)
+            kv += 2 * s.kv_heads * rows * s.head_dim * 2
+        norms = len(self.layers) * (4 * s.hidden + 2 * s.head_dim) * 2 + s.hidden * 2
+        return packed + kv + norms + self.tokens * s.hidden * 2
+
+
+def build_gemma3_step(shape: DecoderShape, device: torch.device, *, vocab: int = 262144, tokens: int = 1,
+                      position: int = 0, layers: int | None = None, seed: int = 0) -> Gemma3DecodeStep:
+    """Random-init packed layers and Gemma shell weights of ``shape`` wired into one decode step."""
+
+    blocks = make_decoder_layers(shape, device, layers=layers, seed=seed)
+    shell = random_gemma_shell_weights(shape, vocab, device, layers=len(blocks), seed=seed + 1)
+    return Gemma3DecodeStep(shape, blocks, shell, device, tokens=tokens, position=position)
+
+
 def build_qwen3_step(shape: DecoderShape, device: torch.device, *, vocab: int, tokens: int = 1, position: int = 0,
                      layers: int | None = None, seed: int = 0) -> Qwen3DecodeStep:
     """Random-init packed layers and shell weights of ``shape`` wired into one decode step."""
@@ -288,7 +508,12 @@ def build_qwen3_step(shape: DecoderShape, device: torch.device, *, vocab: int, t
 
 
 __all__ = [
+    "Gemma3DecodeStep",
+    "GemmaShellWeights",
     "Qwen3DecodeStep",
+    "build_gemma3_step",
+    "embedding_bf16",
+    "random_gemma_shell_weights",
     "ShellWeights",
     "attention_workspace_bytes",
     "build_qwen3_step",

@@ -31,15 +31,18 @@ class ProgramOp:
     """One call: ``layers`` (1..3 sharing ``x``) -> one fp32 output per layer.
 
     With ``x2`` set, ``x`` is a gate and ``x2`` an up projection (both fp32,
-    same shape) and the op's input is their SwiGLU product
-    ``silu(x) * x2``, formed as the op loads it: the SwiGLU MLP's down
-    projection (reference ``runtime/torch_model.py:395-421``) then shares a
-    program with the gate/up op that produces its inputs.
+    same shape) and the op's input is their gated product, formed as the op
+    loads it: ``silu(x) * x2`` (SwiGLU, ``activation="silu"``) or
+    ``gelu_tanh(x) * x2`` (Gemma-3's gated GELU, ``activation="gelu_tanh"``).
+    The MLP's down projection (reference ``runtime/torch_model.py:395-421``,
+    ``:460-505``) then shares a program with the gate/up op that produces its
+    inputs.
     """
 
     layers: tuple[PreparedLayer, ...]
     x: torch.Tensor
     x2: torch.Tensor | None = None
+    activation: str = "silu"
 
 
 class DecodeProgram:
@@ -93,7 +96,12 @@ class DecodeProgram:
             c_ops[index].layers = descs
             c_ops[index].count = len(payloads)
             c_ops[index].x = op.x.data_ptr()
-            c_ops[index].x_dtype = _native.dtype_code(op.x.dtype) if op.x2 is None else _native.NQB_X_SWIGLU
+            if op.x2 is None:
+                c_ops[index].x_dtype = _native.dtype_code(op.x.dtype)
+            elif op.activation in ("silu", "gelu_tanh"):
+                c_ops[index].x_dtype = _native.NQB_X_SWIGLU if op.activation == "silu" else _native.NQB_X_GEGLU
+            else:
+                raise ValueError(f"unknown gate activation {op.activation!r}")
             c_ops[index].y = ys
             c_ops[index].x2 = None if op.x2 is None else op.x2.data_ptr()
         assert tokens is not None

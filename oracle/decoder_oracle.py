@@ -52,17 +52,22 @@ def rotate(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
     return (x * cos + rotated * sin).astype(np.float32)
 
 
-def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, keys: int) -> np.ndarray:
-    """``q [T, Hq, hd]``; caches ``[Hkv, L, hd]``; token t sees rows ``[0, keys + t)`` (float64 math)."""
+def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, keys: int, window: int = 0) -> np.ndarray:
+    """``q [T, Hq, hd]``; caches ``[Hkv, L, hd]``; token t sees rows ``[0, keys + t)`` (float64 math).
+
+    ``window > 0``: only the last ``window`` of those rows (Gemma-3's sliding
+    layers mask keys at positions <= query position - window).
+    """
 
     tokens, q_heads, hd = q.shape
     group = q_heads // k_cache.shape[0]
     out = np.zeros((tokens, q_heads, hd), np.float32)
     for t in range(tokens):
+        first = max(0, keys + t - window) if window > 0 else 0
         for h in range(q_heads):
             kv = h // group
-            k = k_cache[kv, : keys + t].astype(np.float64)
-            v = v_cache[kv, : keys + t].astype(np.float64)
+            k = k_cache[kv, first: keys + t].astype(np.float64)
+            v = v_cache[kv, first: keys + t].astype(np.float64)
             s = (k @ q[t, h].astype(np.float64)) / np.sqrt(hd)
             p = np.exp(s - s.max())
             out[t, h] = (p @ v) / p.sum()
@@ -151,8 +156,74 @@ def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: l
     return logits, k_caches, v_caches
 
 
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    """The tanh form of GELU (``gelu_pytorch_tanh``, Gemma-3's MLP activation), in float64."""
+
+    x = x.astype(np.float64)
+    return (0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))).astype(np.float32)
+
+
+def gemma_decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_cache: np.ndarray, *,
+                       position: int, q_heads: int, kv_heads: int, head_dim: int, eps: float, cos: np.ndarray,
+                       sin: np.ndarray, window: int, accumulate: str = "float64") -> np.ndarray:
+    """One Gemma-3 layer on ``h [T, hidden]`` (reference ``runtime/torch_model.py:233-681``, HF Gemma-3 math).
+
+    ``norms`` hold the *effective* weights ``1 + w`` of ``input_norm``,
+    ``post_attention_norm``, ``pre_feedforward_norm``, ``post_feedforward_norm``,
+    ``q_norm`` and ``k_norm``.  Activations into the projections stay fp32
+    (the reference's fp32 decode path); q, k, v and the attention output are
+    rounded to bf16 where the device stores them.
+    """
+
+    tokens = h.shape[0]
+
+    def linear(x: np.ndarray, layer) -> np.ndarray:
+        return po.packed_linear(x, layer, accumulate=accumulate).astype(np.float32)
+
+    xn = rmsnorm(h, norms["input_norm"], eps)
+    q = linear(xn, proj["q_proj"]).reshape(tokens, q_heads, head_dim)
+    k = linear(xn, proj["k_proj"]).reshape(tokens, kv_heads, head_dim)
+    v = linear(xn, proj["v_proj"]).reshape(tokens, kv_heads, head_dim)
+    q = bf16(rotate(rmsnorm(q, norms["q_norm"], eps), cos[:, None, :], sin[:, None, :]))
+    k = bf16(rotate(rmsnorm(k, norms["k_norm"], eps), cos[:, None, :], sin[:, None, :]))
+    for t in range(tokens):
+        k_cache[:, position + t] = k[t]
+        v_cache[:, position + t] = bf16(v[t])
+    a = bf16(attention(q, k_cache, v_cache, position + 1, window).reshape(tokens, q_heads * head_dim))
+    h = h + rmsnorm(linear(a, proj["o_proj"]), norms["post_attention_norm"], eps)
+    xn = rmsnorm(h, norms["pre_feedforward_norm"], eps)
+    act = gelu_tanh(linear(xn, proj["gate_proj"])) * linear(xn, proj["up_proj"])
+    return h + rmsnorm(linear(act, proj["down_proj"]), norms["post_feedforward_norm"], eps)
+
+
+def gemma_decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_norm: np.ndarray, *,
+                                position: int, q_heads: int, kv_heads: int, head_dim: int, eps: float,
+                                sliding_window: int = 512, global_every: int = 6, local_theta: float = 1e4,
+                                global_theta: float = 1e6, accumulate: str = "float64") -> np.ndarray:
+    """Final-normed hidden states ``[T, hidden]`` of a Gemma-3 step from the embedded ``hidden``.
+
+    ``layer_at(i)`` returns ``(proj, norms, k_cache, v_cache)`` of layer i
+    (effective ``1 + w`` norm weights; caches updated in place).  Layer i is
+    global (full attention, ``global_theta``) when ``(i + 1) % global_every ==
+    0``, else local (``sliding_window`` keys, ``local_theta``).
+    """
+
+    tokens = hidden.shape[0]
+    h = hidden.astype(np.float32).copy()
+    positions = np.arange(position, position + tokens)
+    tables = {theta: rope_tables(positions, head_dim, theta) for theta in (local_theta, global_theta)}
+    for i in range(layer_count):
+        is_global = (i + 1) % global_every == 0
+        cos, sin = tables[global_theta if is_global else local_theta]
+        proj, norms, k_cache, v_cache = layer_at(i)
+        h = gemma_decode_layer(h, proj, norms, k_cache, v_cache, position=position, q_heads=q_heads,
+                               kv_heads=kv_heads, head_dim=head_dim, eps=eps, cos=cos, sin=sin,
+                               window=0 if is_global else sliding_window, accumulate=accumulate)
+    return rmsnorm(h, final_norm, eps)
+
+
 class CpuDecodeStep:
-    """A full decode step of a Qwen3-shaped decoder on the host cores: the timed CPU baseline.
+    """A full decode step of a Qwen3- or Gemma-3-shaped decoder on the host cores: the timed CPU baseline.
 
     The reference's CPU path for one step: its model shell's math (the
     functions above) around ``PackedReferenceBackend.linear`` on every
@@ -166,8 +237,9 @@ class CpuDecodeStep:
 
     def __init__(self, *, layers: int, hidden: int, intermediate: int, q_heads: int, kv_heads: int, head_dim: int,
                  vocab: int, position: int, tokens: int = 1, pool: int = 2, bpw: float = 1.0, seed: int = 0,
-                 eps: float = 1e-6, theta: float = 1e6) -> None:
+                 eps: float = 1e-6, theta: float = 1e6, family: str = "qwen3") -> None:
         rng = np.random.default_rng(seed)
+        self.family = family
         self.layers, self.tokens, self.position = layers, tokens, position
         self.q_heads, self.kv_heads, self.head_dim, self.eps = q_heads, kv_heads, head_dim, eps
         q, kv = q_heads * head_dim, kv_heads * head_dim
@@ -196,22 +268,36 @@ class CpuDecodeStep:
                                        scales(m))
                 layer.prepared()
                 proj[name] = layer
-            norms = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(head_dim),
-                     "k_norm": norm(head_dim)}
+            if family == "gemma":  # effective weights 1 + w of Gemma's norms
+                norms = {name: 1.0 + norm(hidden) for name in ("input_norm", "post_attention_norm",
+                                                                "pre_feedforward_norm", "post_feedforward_norm")}
+                norms.update(q_norm=1.0 + norm(head_dim), k_norm=1.0 + norm(head_dim))
+            else:
+                norms = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(head_dim),
+                         "k_norm": norm(head_dim)}
             k = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
             v = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
             self.pool.append((proj, norms, k, v))
-        self.final_norm = norm(hidden)
+        self.final_norm = norm(hidden) + (1.0 if family == "gemma" else 0.0)
+        self.theta = theta
+        self.hidden = rng.standard_normal((tokens, hidden), dtype=np.float32)
+        if family == "gemma":  # no vocabulary head
+            self.lm_head = None
+            return
         # the 0.6 G-entry head: torch's generator and bf16 rounding (round to
         # nearest even, as bf16() above) are several times faster than numpy's here
         import torch
 
         head = torch.randn(vocab, hidden, generator=torch.Generator().manual_seed(seed + 1)) * 0.02
         self.lm_head = head.bfloat16().float().numpy()
-        self.theta = theta
-        self.hidden = rng.standard_normal((tokens, hidden), dtype=np.float32)
 
     def step(self) -> np.ndarray:
+        if self.family == "gemma":
+            pool = self.pool
+            return gemma_decode_step_streaming(self.hidden, self.layers, lambda i: pool[i % len(pool)],
+                                               self.final_norm, position=self.position, q_heads=self.q_heads,
+                                               kv_heads=self.kv_heads, head_dim=self.head_dim, eps=self.eps,
+                                               accumulate="float32")
         pool = self.pool
         return decode_step_streaming(self.hidden, self.layers, lambda i: pool[i % len(pool)], self.final_norm,
                                      self.lm_head, position=self.position, q_heads=self.q_heads,
@@ -220,4 +306,4 @@ class CpuDecodeStep:
 
 
 __all__ = ["CpuDecodeStep", "attention", "bf16", "decode_layer", "decode_step", "decode_step_streaming",
-           "rmsnorm", "rope_tables", "rotate"]
+           "gelu_tanh", "gemma_decode_layer", "gemma_decode_step_streaming", "rmsnorm", "rope_tables", "rotate"]
