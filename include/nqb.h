@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NQB_ABI_VERSION 3
+#define NQB_ABI_VERSION 4
 
 /* status codes */
 #define NQB_OK 0
@@ -390,6 +390,64 @@ int nqb_device_status(int32_t *status);
  * runtime/torch_model.py:460-505).                                          */
 #define NQB_X_GEGLU 17
 
+/*
+ * Decoder-step extensions of a program op (nqb_program_op.ext; NULL = a plain
+ * linear op).  With them one program runs a whole Qwen3-style decode step
+ * (reference runtime/torch_model.py:185-421 runs it as separate modules):
+ *
+ * - Residual-stream input (norm_stats != NULL, linear ops): x is the fp32
+ *   residual stream h [tokens, in_features]; the op's input is
+ *   h * rsqrt(sum(h^2) / in_features + eps) * norm_weight, with sum(h^2) per
+ *   token added up (in tile order) from norm_stats [ceil(in_features/128)]
+ *   [tokens]: per-128-row partial sums written by nqb_residual_stats or by a
+ *   NQB_EPI_RESIDUAL epilogue.  The weight is folded into the input scale and
+ *   the norm factor applied to the latent, so h is read once.
+ * - Epilogue (stage 2 of linear ops):
+ *   NQB_EPI_STORE    y = out (plain);
+ *   NQB_EPI_RESIDUAL y[0] is h: h += out, and out_stats [ceil(m/128)][tokens]
+ *                    receives the new h's per-tile sums of squares;
+ *   NQB_EPI_QK_ROPE  members q, k, v with head_dim 128 (one 128-row tile per
+ *                    head): per-head RMSNorm of q and k with q_norm_weight /
+ *                    k_norm_weight (NULL: none), rotate-half RoPE with the
+ *                    cos/sin rows [tokens][128], then q -> `q` (bf16
+ *                    [tokens, q_heads * 128]) and k, v -> the bf16 caches
+ *                    [kv_heads, cache_len, 128] at row position + t.  y is
+ *                    not written.
+ *   Members of these epilogues carry no int8 overlay rows.
+ * - NQB_OP_ATTENTION (layers NULL, count 0, x / y NULL): grouped-query
+ *   attention of `q` over the caches, token t seeing rows [0, position + 1 + t),
+ *   scale head_dim^-1/2, bf16 result to attn_out [tokens, q_heads * 128];
+ *   head_dim 128 and q_heads == 4 * kv_heads.  It takes two stages of the
+ *   program (split-K partials over all CTAs, then their fixed-order join).
+ */
+#define NQB_OP_LINEAR 0
+#define NQB_OP_ATTENTION 1
+#define NQB_EPI_STORE 0
+#define NQB_EPI_RESIDUAL 1
+#define NQB_EPI_QK_ROPE 2
+
+typedef struct nqb_program_op_ext {
+  int32_t kind;              /* NQB_OP_LINEAR / NQB_OP_ATTENTION */
+  int32_t epilogue;          /* NQB_EPI_* (linear ops) */
+  const float *norm_stats;   /* residual-stream input: per-tile sums of h^2, or NULL */
+  const void *norm_weight;   /* [in_features] */
+  int32_t norm_weight_dtype; /* F32 / F16 / BF16 */
+  float eps;                 /* of the input norm and of the q/k head norms */
+  float *out_stats;          /* NQB_EPI_RESIDUAL: per-tile sums of the new h^2 */
+  int32_t q_heads, kv_heads, head_dim;
+  const void *q_norm_weight; /* [head_dim] or NULL */
+  const void *k_norm_weight; /* [head_dim] or NULL */
+  int32_t qk_norm_dtype;
+  const float *cos_table;    /* [tokens][head_dim] */
+  const float *sin_table;
+  void *q;                   /* bf16 [tokens, q_heads * head_dim] */
+  void *k_cache;             /* bf16 [kv_heads, cache_len, head_dim] */
+  void *v_cache;
+  int64_t cache_len;
+  int64_t position;          /* first row of this step's tokens in the caches */
+  void *attn_out;            /* NQB_OP_ATTENTION: bf16 [tokens, q_heads * head_dim] */
+} nqb_program_op_ext;
+
 typedef struct nqb_program_op {
   const nqb_linear_desc *layers; /* count members sharing x */
   int32_t count;                 /* 1..3 */
@@ -397,11 +455,19 @@ typedef struct nqb_program_op {
   int32_t x_dtype;               /* NQB_F32 / NQB_F16 / NQB_BF16, NQB_X_SWIGLU or NQB_X_GEGLU */
   float *const *y;               /* count outputs [tokens, out_features] fp32 */
   const void *x2;                /* NQB_X_SWIGLU / NQB_X_GEGLU: the up projection; else NULL */
+  const nqb_program_op_ext *ext; /* decoder-step extensions, or NULL */
 } nqb_program_op;
 
 typedef struct nqb_program nqb_program;
 
 int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t tokens, nqb_program **program);
+/*
+ * Per-128-row partial sums of squares of the fp32 residual stream h [tokens,
+ * hidden]: stats[i][t] = sum of h[t][128 i .. 128 i + 127]^2 (fixed order), the
+ * norm_stats a program's first residual-stream op reads.  No counterpart in
+ * the reference (its RMSNorm module reduces the row itself).
+ */
+int nqb_residual_stats(const float *h, int64_t tokens, int64_t hidden, float *stats, void *stream);
 int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes);
 int nqb_program_run(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream);
 /*

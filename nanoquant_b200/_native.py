@@ -92,7 +92,41 @@ class LinearDesc(ctypes.Structure):
     ]
 
 
-# name -> (restype, argtypes); every symbol declared in include/nqb.h
+NQB_OP_LINEAR = 0
+NQB_OP_ATTENTION = 1
+NQB_EPI_STORE = 0
+NQB_EPI_RESIDUAL = 1
+NQB_EPI_QK_ROPE = 2
+
+
+class ProgramOpExt(ctypes.Structure):
+    """Mirror of ``nqb_program_op_ext``."""
+
+    _fields_ = [
+        ("kind", _i32),
+        ("epilogue", _i32),
+        ("norm_stats", _c_void_p),
+        ("norm_weight", _c_void_p),
+        ("norm_weight_dtype", _i32),
+        ("eps", ctypes.c_float),
+        ("out_stats", _c_void_p),
+        ("q_heads", _i32),
+        ("kv_heads", _i32),
+        ("head_dim", _i32),
+        ("q_norm_weight", _c_void_p),
+        ("k_norm_weight", _c_void_p),
+        ("qk_norm_dtype", _i32),
+        ("cos_table", _c_void_p),
+        ("sin_table", _c_void_p),
+        ("q", _c_void_p),
+        ("k_cache", _c_void_p),
+        ("v_cache", _c_void_p),
+        ("cache_len", _i64),
+        ("position", _i64),
+        ("attn_out", _c_void_p),
+    ]
+
+
 class ProgramOp(ctypes.Structure):
     """Mirror of ``nqb_program_op``."""
 
@@ -103,7 +137,11 @@ class ProgramOp(ctypes.Structure):
         ("x_dtype", _i32),
         ("y", ctypes.POINTER(_c_void_p)),
         ("x2", _c_void_p),
+        ("ext", ctypes.POINTER(ProgramOpExt)),
     ]
+
+
+# name -> (restype, argtypes); every symbol declared in include/nqb.h
 
 
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
@@ -172,6 +210,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_silu_mul": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _c_void_p, _i32, _c_void_p]),
     "nqb_gemv_bf16": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p]),
     "nqb_workspace_reset": (ctypes.c_int, [_c_void_p, ctypes.c_size_t, _c_void_p]),
+    "nqb_residual_stats": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p]),
     "nqb_rmsnorm_residual": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64,
                                             ctypes.c_float, _c_void_p, _i32, _c_void_p]),
     "nqb_decode_attention_window": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _i32,

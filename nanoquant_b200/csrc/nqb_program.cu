@@ -110,6 +110,23 @@ struct OpDev {
   int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
   int64_t n;
   int64_t latent_stride;
+  // decoder-step extensions (nqb_program_op_ext)
+  int32_t kind;            // NQB_OP_LINEAR / NQB_OP_ATTENTION
+  int32_t epilogue;        // NQB_EPI_*
+  const float *norm_stats;  // residual-stream input: [stat_tiles][tokens] partial sums of h^2
+  int32_t stat_tiles;
+  float eps;
+  float inv_n;
+  float *out_stats;        // NQB_EPI_RESIDUAL: [tiles][tokens]
+  int32_t q_heads, kv_heads;
+  const float *q_norm, *k_norm;  // fp32 copies, or nullptr
+  const float *cos_t, *sin_t;    // [tokens][128]
+  __nv_bfloat16 *q;              // [tokens][q_heads * 128]
+  __nv_bfloat16 *k_cache, *v_cache;
+  int64_t cache_len, position;
+  __nv_bfloat16 *attn_out;
+  int32_t att_splits;
+  int64_t att_chunk;
 };
 
 struct Item {
@@ -155,6 +172,8 @@ struct Params {
   // dynamic shared memory offsets
   uint32_t off_addr, off_b, off_acc, off_exch;
   uint32_t off_cb;              // mixed-V codebooks [kMaxMembersTc][1024]
+  uint32_t off_epi;             // decoder-step epilogue scratch: [tokens][128] + [4][tokens] floats
+  float *att_part;              // attention partials [tokens * q_heads][splits][kAttRow]
 };
 
 __device__ int g_prog_error;
@@ -531,10 +550,289 @@ __device__ __forceinline__ bool next_unit(const StageInfo &op, int ge, int rank,
   return true;
 }
 
+// ------------------------------------------------------ decoder-step ops ---
+
+constexpr int kAttHd = 128;                 // head_dim of the fused attention and q/k epilogue
+constexpr int kAttGroup = 4;                // q heads per kv head
+constexpr int kAttSub = 32 / kAttGroup;     // keys per warp sub-block (group x keys = 32 lanes)
+constexpr int kAttRow = kAttHd + 4;         // a partial: acc[128], m, l, two pad floats (16-byte rows)
+
+// Named barrier of the 128 leader threads (consumer warps 0..3).
+__device__ __forceinline__ void leader_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+// Sum over the 32 lanes of v[i] for i < 32, transposed: afterwards lane l holds
+// the total of v[l] (31 shuffles instead of 32 x 5).
+__device__ __forceinline__ float transposed_sum32(float (&v)[32], int lane) {
+  // step `half`: 2 * half values are live; this lane keeps the half of them
+  // that matches its lane bit and adds its partner's copy of the same indices
+#pragma unroll
+  for (int half = 16; half >= 1; half >>= 1) {
+    const bool upper = (lane & half) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < half) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+      }
+    }
+  }
+  return v[0];
+}
+
+__device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&raw.y));
+  out[0] = a.x;
+  out[1] = a.y;
+  out[2] = b.x;
+  out[3] = b.y;
+}
+
+// Attention partials of one CTA: unit `blockIdx.x` = (kv head, key split),
+// for every token of the step.  The 8 consumer warps take 8-key sub-blocks in
+// turn; per sub-block a lane loads its 4 dims of the 8 K and V rows (all
+// loads in flight together), the 4 heads x 8 keys dot products are summed
+// across the warp in one transposed reduction (lane = head * 8 + key), and an
+// online softmax updates each head's (m, l, acc).  The warps' partials meet in
+// shared memory (fixed order) and one partial per (token, q head, split) goes
+// to the workspace.  K/V rows are read through L2 (.cg): this step's rows were
+// written by the preceding stage.
+__device__ __noinline__ void attention_partials(const Params &p, const OpDev &op, float *scratch) {
+  const int T = p.tokens;
+  const int units = op.kv_heads * op.att_splits;
+  const int cta = static_cast<int>(blockIdx.x);
+  if (cta >= units) return;  // uniform over the CTA
+  const int kvh = cta / op.att_splits, sp = cta - kvh * op.att_splits;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float scale = rsqrtf(static_cast<float>(kAttHd));
+  const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
+  const __nv_bfloat16 *vbase = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
+  for (int t = 0; t < T; ++t) {
+    const int64_t visible = op.position + 1 + t;
+    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+    const int64_t k1 = min(k0 + op.att_chunk, visible);
+    float qv[kAttGroup][4], acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
+#pragma unroll
+    for (int h = 0; h < kAttGroup; ++h) {
+      const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(
+          op.q + (static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * kAttHd + lane * 4));
+      bf16x4_to_float(raw, qv[h]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qv[h][e] *= scale;
+        acc[h][e] = 0.0f;
+      }
+      m[h] = -INFINITY;
+      l[h] = 0.0f;
+    }
+    for (int64_t b0 = k0 + warp * kAttSub; b0 < k1; b0 += kAttSub * mmad::kWarps) {
+      const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
+      uint2 kr[kAttSub], vr[kAttSub];
+#pragma unroll
+      for (int j = 0; j < kAttSub; ++j) {
+        const int64_t row = b0 + (j < nk ? j : 0);  // rows past the block re-read row b0 (masked below)
+        kr[j] = __ldcg(reinterpret_cast<const uint2 *>(kbase + row * kAttHd));
+        vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + row * kAttHd));
+      }
+      float sv[32];
+#pragma unroll
+      for (int j = 0; j < kAttSub; ++j) {
+        float kf[4];
+        bf16x4_to_float(kr[j], kf);
+#pragma unroll
+        for (int h = 0; h < kAttGroup; ++h)
+          sv[h * kAttSub + j] = qv[h][0] * kf[0] + qv[h][1] * kf[1] + qv[h][2] * kf[2] + qv[h][3] * kf[3];
+      }
+      const int own_h = lane / kAttSub, own_j = lane % kAttSub;
+      float sc = transposed_sum32(sv, lane);
+      if (own_j >= nk) sc = -INFINITY;
+      float mb = sc;
+#pragma unroll
+      for (int off = 1; off < kAttSub; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+      float mn[kAttGroup], corr[kAttGroup];
+#pragma unroll
+      for (int h = 0; h < kAttGroup; ++h) {
+        mn[h] = fmaxf(m[h], __shfl_sync(0xffffffffu, mb, h * kAttSub));  // finite: the block has a key
+        corr[h] = __expf(m[h] - mn[h]);  // exp(-inf) = 0 on the first block
+      }
+      const float pr = own_j < nk ? __expf(sc - mn[own_h]) : 0.0f;
+      float ps = pr;
+#pragma unroll
+      for (int off = 1; off < kAttSub; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+#pragma unroll
+      for (int h = 0; h < kAttGroup; ++h) {
+        l[h] = l[h] * corr[h] + __shfl_sync(0xffffffffu, ps, h * kAttSub);
+        m[h] = mn[h];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[h][e] *= corr[h];
+      }
+#pragma unroll
+      for (int j = 0; j < kAttSub; ++j) {
+        float vf[4];
+        bf16x4_to_float(vr[j], vf);
+#pragma unroll
+        for (int h = 0; h < kAttGroup; ++h) {
+          const float pj = __shfl_sync(0xffffffffu, pr, h * kAttSub + j);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[h][e] += pj * vf[e];
+        }
+      }
+    }
+    // the warps' partials -> shared memory [warp][head][kAttRow]
+#pragma unroll
+    for (int h = 0; h < kAttGroup; ++h) {
+      float *row = scratch + (warp * kAttGroup + h) * kAttRow;
+      *reinterpret_cast<float4 *>(row + lane * 4) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+      if (lane == 0) {
+        row[kAttHd] = m[h];
+        row[kAttHd + 1] = l[h];
+      }
+    }
+    mmad::consumer_sync();
+    {
+      // thread tid: head tid / 64, dims 2 (tid % 64) .. +1; warps joined in index order
+      const int h = tid >> 6, d = (tid & 63) * 2;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < mmad::kWarps; ++w) mx = fmaxf(mx, scratch[(w * kAttGroup + h) * kAttRow + kAttHd]);
+      float a0 = 0.0f, a1 = 0.0f, ls = 0.0f;
+#pragma unroll
+      for (int w = 0; w < mmad::kWarps; ++w) {
+        const float *row = scratch + (w * kAttGroup + h) * kAttRow;
+        const float mw = row[kAttHd];
+        const float f = mw == -INFINITY ? 0.0f : __expf(mw - mx);
+        a0 += f * row[d];
+        a1 += f * row[d + 1];
+        ls += f * row[kAttHd + 1];
+      }
+      float *out = p.att_part +
+                   ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * op.att_splits + sp) * kAttRow;
+      *reinterpret_cast<float2 *>(out + d) = make_float2(a0, a1);
+      if ((tid & 63) == 0) {
+        out[kAttHd] = mx;
+        out[kAttHd + 1] = ls;
+      }
+    }
+    mmad::consumer_sync();  // the scratch is reused by the next token
+  }
+}
+
+// Joins the splits' partials of every (token, q head) in split order, one
+// warp per row (lane: 4 dims), and writes the bf16 attention output.
+__device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
+  const int rows = p.tokens * op.q_heads;
+  const int lane = threadIdx.x & 31;
+  const int stride = static_cast<int>(gridDim.x) * mmad::kWarps;
+  for (int r = static_cast<int>(blockIdx.x) * mmad::kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
+    const float *base = p.att_part + static_cast<int64_t>(r) * op.att_splits * kAttRow;
+    const float m0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd) : -INFINITY;
+    const float l0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd + 1) : 0.0f;
+    float mx = m0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float f0 = m0 == -INFINITY ? 0.0f : __expf(m0 - mx);
+    float den = f0 * l0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+    float num[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int sidx = 0; sidx < op.att_splits; ++sidx) {
+      const float f = __shfl_sync(0xffffffffu, f0, sidx);
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + sidx * kAttRow + lane * 4));
+      num[0] += f * v.x;
+      num[1] += f * v.y;
+      num[2] += f * v.z;
+      num[3] += f * v.w;
+    }
+    const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+    __nv_bfloat16 *o = op.attn_out + static_cast<int64_t>(r) * kAttHd + lane * 4;
+    *reinterpret_cast<__nv_bfloat162 *>(o) = __floats2bfloat162_rn(num[0] * inv, num[1] * inv);
+    *reinterpret_cast<__nv_bfloat162 *>(o + 2) = __floats2bfloat162_rn(num[2] * inv, num[3] * inv);
+  }
+}
+
+// NQB_EPI_RESIDUAL for one tile (the 128 leader threads): h += out, and the
+// tile's sums of squares of the new h per token to out_stats.
+template <int kT>
+__device__ __forceinline__ void residual_epilogue(const OpDev &op, const MemberDev &md, int tile, const float (&outv)[kT],
+                                                  int T, float *red) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row = static_cast<int64_t>(tile) * kTileRows + tid;
+  float sq[kT];
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    sq[t] = 0.0f;
+    if (t < T && row < md.rows) {
+      const int64_t i = static_cast<int64_t>(t) * md.rows + row;
+      const float hn = __ldcg(md.y + i) + outv[t];
+      md.y[i] = hn;
+      sq[t] = hn * hn;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    const float w = warp_sum(sq[t]);
+    if (lane == 0) red[warp * kT + t] = w;
+  }
+  leader_sync();
+  if (tid < T) op.out_stats[static_cast<int64_t>(tile) * T + tid] = (red[tid] + red[kT + tid]) + (red[2 * kT + tid] + red[3 * kT + tid]);
+  leader_sync();  // red is reused by the next tile
+}
+
+// NQB_EPI_QK_ROPE for one tile = one head (the 128 leader threads, d = tid):
+// q and k heads get RMSNorm and rotate-half RoPE, v heads are copied; all go
+// out as bf16 (q to op.q, k and v to the caches at row position + t).
+template <int kT>
+__device__ __forceinline__ void qk_rope_epilogue(const OpDev &op, int member, int tile, const float (&outv)[kT], int T,
+                                                 float *xs, float *red) {
+  const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+  if (member == 2) {
+#pragma unroll
+    for (int t = 0; t < kT; ++t)
+      if (t < T)
+        op.v_cache[(static_cast<int64_t>(tile) * op.cache_len + op.position + t) * kAttHd + d] =
+            __float2bfloat16_rn(outv[t]);
+    return;
+  }
+  const float *w = member == 0 ? op.q_norm : op.k_norm;
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    const float ss = warp_sum(t < T ? outv[t] * outv[t] : 0.0f);
+    if (lane == 0) red[warp * kT + t] = ss;
+  }
+  leader_sync();
+  const float wd = w != nullptr ? w[d] : 1.0f;
+  float xn[kT];
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    xn[t] = outv[t];
+    if (t < T && w != nullptr) {
+      const float ss = (red[t] + red[kT + t]) + (red[2 * kT + t] + red[3 * kT + t]);
+      xn[t] = outv[t] * rsqrtf(ss / static_cast<float>(kAttHd) + op.eps) * wd;
+    }
+    if (t < T) xs[t * kAttHd + d] = xn[t];
+  }
+  leader_sync();
+  const float sign = d < kAttHd / 2 ? -1.0f : 1.0f;  // rotate_half: (-x2, x1)
+#pragma unroll
+  for (int t = 0; t < kT; ++t) {
+    if (t >= T) break;
+    const float partner = xs[t * kAttHd + (d ^ (kAttHd / 2))];
+    const float o = xn[t] * op.cos_t[t * kAttHd + d] + sign * partner * op.sin_t[t * kAttHd + d];
+    if (member == 0)
+      op.q[(static_cast<int64_t>(t) * op.q_heads + tile) * kAttHd + d] = __float2bfloat16_rn(o);
+    else
+      op.k_cache[(static_cast<int64_t>(tile) * op.cache_len + op.position + t) * kAttHd + d] = __float2bfloat16_rn(o);
+  }
+  leader_sync();  // xs and red are reused by the next tile
+}
+
 // kPatch: some op has a patched member; kMixed: some member streams coded
-// mixed-V tiles.  Programs without them run instances with those steps
-// compiled out (the steps cost time in the stage loop even when never taken).
-template <int kT, bool kPatch, bool kMixed>
+// mixed-V tiles; kStep: some op uses the decoder-step extensions (residual
+// input norm, fused epilogues, attention).  Programs without them run
+// instances with those steps compiled out (the steps cost time in the stage
+// loop even when never taken).
+template <int kT, bool kPatch, bool kMixed, bool kStep>
 __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_constant__ Params p) {
   constexpr int kNT = mmad::n_tiles(kT);
   constexpr int kSets = mmad::acc_sets(kNT);
@@ -553,6 +851,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   __shared__ mmad::Scratch<kT> s_sc;
   __shared__ float s_red_f[mmad::kWarps];
   __shared__ uint64_t s_patch_done;  // the info warp formed this CTA's patch rows of the current stage 1
+  __shared__ float s_rms[kT];        // residual-stream input: the stage's per-token norm factors
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -568,6 +867,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   uint8_t *smem_b = smem + p.off_b;
   float *s_acc = reinterpret_cast<float *>(smem + p.off_acc);    // [group][T][128]
   float *s_exch = reinterpret_cast<float *>(smem + p.off_exch);  // [group / 4][4][T][128]
+  float *s_epi = reinterpret_cast<float *>(smem + p.off_epi);    // [T][128] then [4][kT] (fused epilogues)
 
   if (tid == 0) {
     for (int s = 0; s < R; ++s) {
@@ -680,6 +980,27 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       const StageInfo &op = s_info[g & 1];
       const int ib = 0;
       const int ie = op.n_items;
+      const OpDev &gop = p.ops[g >> 1];  // the op's decoder-step fields (read-only, global)
+      int op_kind = NQB_OP_LINEAR, op_epi = NQB_EPI_STORE;
+      bool normed = false;
+      if constexpr (kStep) {
+        op_kind = gop.kind;
+        op_epi = st == 1 ? gop.epilogue : NQB_EPI_STORE;
+        normed = st == 0 && gop.norm_stats != nullptr;
+        if (op_kind == NQB_OP_ATTENTION) {
+          // split-K partials over the CTAs (stage 1 of the op), then their join;
+          // the CTA's exchange buffers are idle during these stages
+          if (st == 0)
+            attention_partials(p, gop, s_acc);
+          else
+            attention_join(p, gop);
+        } else if (normed && tid < T) {
+          // h's per-tile sums of squares (written before this stage) -> the norm factor
+          float ss = 0.0f;
+          for (int i = 0; i < gop.stat_tiles; ++i) ss += __ldcg(gop.norm_stats + static_cast<int64_t>(i) * T + tid);
+          s_rms[tid] = rsqrtf(ss * gop.inv_n + gop.eps);  // read in the leader epilogue, after several barriers
+        }
+      }
       // kMixed: item j's slices, the records of a coded tile decoded where a
       // plain tile's words are loaded (whether item j is coded is read once)
       auto mixed_slices = [&](int j, int nst, auto &d) {
@@ -944,6 +1265,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           if (jj >= ge - gb) break;
           const Item item = op.items[gb + jj];
           const MemberDev &md = op.md[item.member];
+          float outv[kT];  // stage-2 values for the fused epilogues
+#pragma unroll
+          for (int t = 0; t < kT; ++t) outv[t] = 0.0f;
           if (tid < kTileRows) {
             const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
             if (row < md.rows) {
@@ -952,7 +1276,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                 if (t >= T) break;
                 float v = vsum[sidx][t];
                 if (st == 0) {
-                  p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * lead_scale[sidx];
+                  float f = lead_scale[sidx];
+                  if constexpr (kStep) {
+                    if (normed) f *= s_rms[t];
+                  }
+                  p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * f;
                 } else {
                   v *= lead_scale[sidx];
                   if (md.outlier_count > 0) {
@@ -974,10 +1302,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                       v += pv;
                     }
                   }
-                  md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
+                  if (kStep && op_epi != NQB_EPI_STORE)
+                    outv[t] = v + lead_bias[sidx];
+                  else
+                    md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
                 }
               }
             }
+          }
+          if constexpr (kStep) {
+            if (op_epi == NQB_EPI_RESIDUAL && tid < kTileRows)
+              residual_epilogue<kT>(gop, md, item.tile, outv, T, s_epi + kT * kTileRows);
+            else if (op_epi == NQB_EPI_QK_ROPE && tid < kTileRows)
+              qk_rope_epilogue<kT>(gop, item.member, item.tile, outv, T, s_epi, s_epi + kT * kTileRows);
           }
           if (st == 1 && md.overlay_rows > 0) {
             // int8 residual rows of this tile: all consumer threads compute each dot product
@@ -1041,6 +1378,29 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   }
 }
 
+// dst[i] *= w[i] (program create time: a norm weight folded into an input scale).
+__global__ void mul_f32_kernel(float *dst, const float *w, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] *= w[i];
+}
+
+// stats[i][t] = sum over the 128 rows i*128 .. of h[t][row]^2: one warp per (tile, token), fixed order.
+__global__ void residual_stats_kernel(const float *h, int64_t tokens, int64_t hidden, float *stats) {
+  const int64_t tiles = (hidden + kTileRows - 1) / kTileRows;
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= tiles * tokens) return;
+  const int64_t tile = w / tokens, t = w - tile * tokens;
+  float s = 0.0f;
+  for (int64_t r = tile * kTileRows + lane; r < min((tile + 1) * kTileRows, hidden); r += 32) {
+    const float v = h[t * hidden + r];
+    s += v * v;
+  }
+  s = warp_sum(s);
+  if (lane == 0) stats[tile * tokens + t] = s;
+}
+
 // fp32 copy of a scale / bias vector (program create time).
 __global__ void to_f32_kernel(const void *src, int32_t dtype, int64_t n, float *dst) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -1062,6 +1422,8 @@ struct nqb_program {
   int bucket = 1;
   bool patch = false;  // runs the patch-capable kernel instance
   bool mixed = false;  // runs the coded mixed-V instance
+  bool step = false;   // runs the decoder-step instance
+  size_t att_part_bytes = 0;  // attention partials after the latent in the workspace
   int ctas = 0;
   int clusters = 0;
   int smem = 0;
@@ -1080,7 +1442,7 @@ static int token_bucket(int64_t tokens) {
 
 struct SmemPlan {
   int sc, group, ring;
-  uint32_t off_addr, off_b, off_acc, off_exch, off_cb, total;
+  uint32_t off_addr, off_b, off_acc, off_exch, off_cb, off_epi, total;
 };
 
 static SmemPlan smem_plan(int bucket, bool mixed) {
@@ -1093,7 +1455,9 @@ static SmemPlan smem_plan(int bucket, bool mixed) {
   const uint32_t acc = static_cast<uint32_t>(s.group) * bucket * kTileRows * 4;
   const uint32_t exch = static_cast<uint32_t>(lead) * kClusterSize * bucket * kTileRows * 4;
   const uint32_t cb = mixed ? kMaxMembersTc * kCodebookWords * 4u : 0u;
-  const uint32_t rest = addr + b + acc + exch + cb;
+  // fused decoder-step epilogues: [tokens][128] values, then [4][tokens] partial sums
+  const uint32_t epi = static_cast<uint32_t>(align_up(static_cast<size_t>(bucket) * (kTileRows + 4) * 4, 16));
+  const uint32_t rest = addr + b + acc + exch + cb + epi;
   s.ring = std::min<int>(kMaxRing, static_cast<int>((kMaxDynamicSmem - rest) / kStageWeightBytes));
   uint32_t off = static_cast<uint32_t>(s.ring) * kStageWeightBytes;
   s.off_addr = off;
@@ -1106,24 +1470,28 @@ static SmemPlan smem_plan(int bucket, bool mixed) {
   off += exch;
   s.off_cb = off;
   off += cb;
+  s.off_epi = off;
+  off += epi;
   s.total = off;
   return s;
 }
 
-template <bool kPatch, bool kMixed>
+template <bool kPatch, bool kMixed, bool kStep>
 static const void *kernel_for_t(int bucket) {
   switch (bucket) {
-    case 1: return reinterpret_cast<const void *>(program_kernel<1, kPatch, kMixed>);
-    case 2: return reinterpret_cast<const void *>(program_kernel<2, kPatch, kMixed>);
-    case 4: return reinterpret_cast<const void *>(program_kernel<4, kPatch, kMixed>);
-    case 8: return reinterpret_cast<const void *>(program_kernel<8, kPatch, kMixed>);
-    default: return reinterpret_cast<const void *>(program_kernel<16, kPatch, kMixed>);
+    case 1: return reinterpret_cast<const void *>(program_kernel<1, kPatch, kMixed, kStep>);
+    case 2: return reinterpret_cast<const void *>(program_kernel<2, kPatch, kMixed, kStep>);
+    case 4: return reinterpret_cast<const void *>(program_kernel<4, kPatch, kMixed, kStep>);
+    case 8: return reinterpret_cast<const void *>(program_kernel<8, kPatch, kMixed, kStep>);
+    default: return reinterpret_cast<const void *>(program_kernel<16, kPatch, kMixed, kStep>);
   }
 }
 
-static const void *kernel_for(int bucket, bool patch, bool mixed) {
-  if (mixed) return patch ? kernel_for_t<true, true>(bucket) : kernel_for_t<false, true>(bucket);
-  return patch ? kernel_for_t<true, false>(bucket) : kernel_for_t<false, false>(bucket);
+// Step programs (decoder-step extensions) take no patched or coded mixed-V members.
+static const void *kernel_for(int bucket, bool patch, bool mixed, bool step) {
+  if (step) return kernel_for_t<false, false, true>(bucket);
+  if (mixed) return patch ? kernel_for_t<true, true, false>(bucket) : kernel_for_t<false, true, false>(bucket);
+  return patch ? kernel_for_t<true, false, false>(bucket) : kernel_for_t<false, false, false>(bucket);
 }
 
 // `pre`, `row_scale` and `bias` are the program's fp32 copies of the layer's vectors.
@@ -1222,8 +1590,26 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   const int bucket = token_bucket(tokens);
   std::vector<OpDev> opdev(op_count);
   int64_t latent_cols = 0;
+  bool step = false;
   for (int i = 0; i < op_count; ++i) {
     const nqb_program_op &o = ops[i];
+    const nqb_program_op_ext *e = o.ext;
+    if (e != nullptr) {
+      step = true;
+      if (e->kind == NQB_OP_ATTENTION) {
+        if (e->head_dim != kAttHd || e->kv_heads < 1 || e->q_heads != kAttGroup * e->kv_heads)
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: fused attention takes head_dim %d and %d q heads per kv head", i,
+                      kAttHd, kAttGroup);
+        if (e->q == nullptr || e->k_cache == nullptr || e->v_cache == nullptr || e->attn_out == nullptr ||
+            e->position < 0 || e->position + tokens > e->cache_len)
+          return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: attention operands or cache position invalid", i);
+        if (reinterpret_cast<uintptr_t>(e->q) % 16 || reinterpret_cast<uintptr_t>(e->k_cache) % 16 ||
+            reinterpret_cast<uintptr_t>(e->v_cache) % 16 || reinterpret_cast<uintptr_t>(e->attn_out) % 16)
+          return fail(NQB_ERR_ALIGNMENT, "op %d: attention operands need 16-byte alignment", i);
+        continue;
+      }
+      if (e->kind != NQB_OP_LINEAR) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: unknown op kind %d", i, e->kind);
+    }
     if (o.layers == nullptr || o.count < 1 || o.count > kMaxMembersTc)
       return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: 1 to %d layers", i, kMaxMembersTc);
     if (o.x == nullptr || o.y == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: x or y is NULL", i);
@@ -1253,6 +1639,35 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     int64_t patch_total = 0;
     for (int k = 0; k < o.count; ++k) patch_total += o.layers[k].patch_rank;
     latent_cols = std::max(latent_cols, rank_total + patch_total);
+    if (e != nullptr) {
+      for (int k = 0; k < o.count; ++k)
+        if (o.layers[k].patch_rank > 0 || o.layers[k].coded_right_tiles != nullptr || o.layers[k].overlay_rows > 0)
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: decoder-step ops take no patch, coded mixed-V tiles or overlay rows", i);
+      if (e->norm_stats != nullptr) {
+        if (o.x_dtype != NQB_F32 || e->norm_weight == nullptr || !is_float_dtype(e->norm_weight_dtype) ||
+            !(e->eps >= 0.0f))
+          return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a residual-stream input is fp32 h with a norm weight", i);
+        for (int k = 0; k < o.count; ++k)
+          if (o.layers[k].outlier_count > 0)
+            return fail(NQB_ERR_UNSUPPORTED, "op %d: residual-stream inputs take no salient columns", i);
+      }
+      if (e->epilogue == NQB_EPI_RESIDUAL) {
+        if (o.count != 1 || e->out_stats == nullptr)
+          return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: a residual epilogue has one member and out_stats", i);
+      } else if (e->epilogue == NQB_EPI_QK_ROPE) {
+        if (e->head_dim != kAttHd || o.count != 3 || e->kv_heads < 1 ||
+            o.layers[0].out_features != static_cast<int64_t>(e->q_heads) * kAttHd ||
+            o.layers[1].out_features != static_cast<int64_t>(e->kv_heads) * kAttHd ||
+            o.layers[2].out_features != static_cast<int64_t>(e->kv_heads) * kAttHd)
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: the q/k epilogue takes q, k, v members of head_dim %d", i, kAttHd);
+        if (e->cos_table == nullptr || e->sin_table == nullptr || e->q == nullptr || e->k_cache == nullptr ||
+            e->v_cache == nullptr || e->position < 0 || e->position + tokens > e->cache_len ||
+            ((e->q_norm_weight != nullptr || e->k_norm_weight != nullptr) && !is_float_dtype(e->qk_norm_dtype)))
+          return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: q/k epilogue operands or cache position invalid", i);
+      } else if (e->epilogue != NQB_EPI_STORE) {
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: unknown epilogue %d", i, e->epilogue);
+      }
+    }
   }
 
   // fp32 copies of the scale and bias vectors, so the kernel reads them with
@@ -1276,8 +1691,22 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     size_t pre, mid, post, bias;
   };
   std::vector<MemberScales> member_scales;
+  struct OpScales {
+    size_t norm_weight = SIZE_MAX, q_norm = SIZE_MAX, k_norm = SIZE_MAX;
+  };
+  std::vector<OpScales> op_scales(op_count);
+  for (int i = 0; i < op_count; ++i) {
+    const nqb_program_op_ext *e = ops[i].ext;
+    if (e == nullptr || e->kind != NQB_OP_LINEAR) continue;
+    if (e->norm_stats != nullptr)
+      op_scales[i].norm_weight = add_copy(e->norm_weight, e->norm_weight_dtype, ops[i].layers[0].in_features);
+    if (e->epilogue == NQB_EPI_QK_ROPE) {
+      op_scales[i].q_norm = add_copy(e->q_norm_weight, e->qk_norm_dtype, kAttHd);
+      op_scales[i].k_norm = add_copy(e->k_norm_weight, e->qk_norm_dtype, kAttHd);
+    }
+  }
   for (int i = 0; i < op_count; ++i)
-    for (int k = 0; k < ops[i].count; ++k) {
+    for (int k = 0; k < (ops[i].ext != nullptr && ops[i].ext->kind == NQB_OP_ATTENTION ? 0 : ops[i].count); ++k) {
       const nqb_linear_desc &d = ops[i].layers[k];
       MemberScales ms;
       ms.pre = add_copy(d.scale_pre, d.scale_dtype, d.in_features);
@@ -1295,6 +1724,18 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const int64_t blocks = std::min<int64_t>((c.n + 255) / 256, 1024);
     to_f32_kernel<<<static_cast<unsigned>(blocks), 256>>>(c.src, c.dtype, c.n, scales + c.offset);
   }
+  // residual-stream inputs: the norm weight folds into each member's input scale (pre := pre * w)
+  for (int i = 0, mi = 0; i < op_count; ++i) {
+    const bool attention = ops[i].ext != nullptr && ops[i].ext->kind == NQB_OP_ATTENTION;
+    const int members = attention ? 0 : ops[i].count;
+    if (op_scales[i].norm_weight != SIZE_MAX)
+      for (int k = 0; k < members; ++k) {
+        const int64_t n = ops[i].layers[k].in_features;
+        mul_f32_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1024)), 256>>>(
+            scales + member_scales[mi + k].pre, scales + op_scales[i].norm_weight, n);
+      }
+    mi += members;
+  }
   if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(scales);
     return fail(NQB_ERR_CUDA, "converting the program's scales to fp32 failed");
@@ -1305,6 +1746,31 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const nqb_program_op &o = ops[i];
     OpDev &od = opdev[i];
     std::memset(&od, 0, sizeof(od));
+    const nqb_program_op_ext *e = o.ext;
+    od.kind = e != nullptr ? e->kind : NQB_OP_LINEAR;
+    if (e != nullptr) {
+      od.epilogue = e->epilogue;
+      od.eps = e->eps;
+      od.out_stats = e->out_stats;
+      od.q_heads = e->q_heads;
+      od.kv_heads = e->kv_heads;
+      od.cos_t = e->cos_table;
+      od.sin_t = e->sin_table;
+      od.q = static_cast<__nv_bfloat16 *>(e->q);
+      od.k_cache = static_cast<__nv_bfloat16 *>(e->k_cache);
+      od.v_cache = static_cast<__nv_bfloat16 *>(e->v_cache);
+      od.cache_len = e->cache_len;
+      od.position = e->position;
+      od.attn_out = static_cast<__nv_bfloat16 *>(e->attn_out);
+      od.q_norm = f32(op_scales[i].q_norm);
+      od.k_norm = f32(op_scales[i].k_norm);
+      if (e->kind == NQB_OP_ATTENTION) continue;  // no members; the splits are set once the grid is known
+      if (e->norm_stats != nullptr) {
+        od.norm_stats = e->norm_stats;
+        od.stat_tiles = static_cast<int32_t>((o.layers[0].in_features + kTileRows - 1) / kTileRows);
+        od.inv_n = 1.0f / static_cast<float>(o.layers[0].in_features);
+      }
+    }
     od.count = o.count;
     od.x = o.x;
     od.x2 = (o.x_dtype == NQB_X_SWIGLU || o.x_dtype == NQB_X_GEGLU) ? o.x2 : nullptr;
@@ -1332,9 +1798,10 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     patch = patch || opdev[i].patch_rows > 0;
     for (int k = 0; k < opdev[i].count; ++k) mixed = mixed || opdev[i].s[0][k].coded_tiles != nullptr;
   }
+  if (step && (patch || mixed)) return fail(NQB_ERR_UNSUPPORTED, "decoder-step programs take no patch or mixed-V tiles");
   const SmemPlan sp = smem_plan(bucket, mixed);
   if (sp.off_cb % 16) return fail(NQB_ERR_UNSUPPORTED, "codebook buffer is misaligned");
-  const void *fn = kernel_for(bucket, patch, mixed);
+  const void *fn = kernel_for(bucket, patch, mixed, step);
   NQB_CHECK(ensure_dynamic_smem(fn, static_cast<int>(sp.total)));
   int sms = 0;
   NQB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
@@ -1357,6 +1824,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   clusters = std::min(clusters, sms / kClusterSize);
   if (clusters < 1) return fail(NQB_ERR_UNSUPPORTED, "no cluster of %d CTAs fits this device", kClusterSize);
   const int ctas = clusters * kClusterSize;
+  // fused attention: one (kv head, key split) unit per CTA, at most 32 splits
+  size_t att_floats = 0;
+  for (int i = 0; i < op_count; ++i) {
+    OpDev &od = opdev[i];
+    if (od.kind != NQB_OP_ATTENTION) continue;
+    od.att_splits = std::max(1, std::min(32, ctas / od.kv_heads));
+    const int64_t most = od.position + tokens;  // keys the last token sees
+    od.att_chunk = (most + od.att_splits - 1) / od.att_splits;
+    att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.q_heads * od.att_splits * kAttRow);
+  }
 
   // tiles per (stage, cluster), then every CTA's slice addresses in consumption order
   // and the L2 lines it reads per stage besides sign words and activations
@@ -1384,6 +1861,22 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   for (int g = 0; g < stages; ++g) {
     const OpDev &op = opdev[g >> 1];
     const int st = g & 1;
+    if (op.kind == NQB_OP_ATTENTION && st == 0) {
+      // each CTA's unit (kv head, key split): its K and V rows go on the L2
+      // prefetch list of the stage two ahead of this one (the rows before this
+      // step's tokens do not change during the program)
+      const int target = std::max(0, g - 2);
+      for (int c = 0; c < ctas && c < op.kv_heads * op.att_splits; ++c) {
+        const int kvh = c / op.att_splits, spl = c % op.att_splits;
+        const int64_t k0 = static_cast<int64_t>(spl) * op.att_chunk;
+        const int64_t k1 = std::min(k0 + op.att_chunk, op.position + tokens);
+        if (k1 <= k0) continue;
+        const int64_t off = (static_cast<int64_t>(kvh) * op.cache_len + k0) * kAttHd;
+        std::vector<uint64_t> &lines = pf[static_cast<size_t>(target) * ctas + c];
+        add_lines(lines, op.k_cache + off, (k1 - k0) * kAttHd * 2);
+        add_lines(lines, op.v_cache + off, (k1 - k0) * kAttHd * 2);
+      }
+    }
     assign_stage(op, st, clusters, per_cluster);
     for (int c = 0; c < clusters; ++c)
       if (per_cluster[c].size() > static_cast<size_t>(kMaxStageItems))
@@ -1541,13 +2034,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   prog->clusters = clusters;
   prog->smem = static_cast<int>(sp.total);
   prog->latent_bytes = align_up(static_cast<size_t>(tokens) * latent_cols * sizeof(float), 256);
+  prog->att_part_bytes = align_up(att_floats * sizeof(float), 256);
+  prog->step = step;
+  pp.off_epi = sp.off_epi;
   *program = prog;
   return ok();
 }
 
 int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes) {
   if (program == nullptr || bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program or bytes is NULL");
-  *bytes = kCounterRegionBytes + program->latent_bytes;
+  *bytes = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes;
   return ok();
 }
 
@@ -1563,16 +2059,18 @@ static std::atomic<uint32_t> g_barrier_limit{0};
 static int launch_program(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream,
                           bool dependent) {
   if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
-  const size_t need = kCounterRegionBytes + program->latent_bytes;
+  const size_t need = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes;
   if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(NQB_ERR_WORKSPACE, "program workspace needs %zu bytes aligned to 256, got %zu", need, workspace_bytes);
   Params params = program->params;
   params.counters = static_cast<uint32_t *>(workspace);
   params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
+  params.att_part =
+      reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes + program->latent_bytes);
   const uint32_t limit = g_barrier_limit.load();
   params.barrier_limit = limit != 0 ? limit : kBarrierSpinLimit;
   params.barrier_skew = program->barrier_skew;
-  const void *fn = kernel_for(program->bucket, program->patch, program->mixed);
+  const void *fn = kernel_for(program->bucket, program->patch, program->mixed, program->step);
   NQB_CHECK(ensure_dynamic_smem(fn, program->smem));
   cudaLaunchConfig_t config;
   std::memset(&config, 0, sizeof(config));
@@ -1640,6 +2138,16 @@ int nqb_program_trace(const nqb_program *program, int64_t *cycles, size_t count)
   (void)count;
   return fail(NQB_ERR_UNSUPPORTED, "phase tracing needs the trace build (python -m nanoquant_b200.build --trace)");
 #endif
+}
+
+int nqb_residual_stats(const float *h, int64_t tokens, int64_t hidden, float *stats, void *stream) {
+  if (h == nullptr || stats == nullptr || tokens <= 0 || hidden <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "residual stats operands invalid");
+  const int64_t warps = (hidden + nqb::prog::kTileRows - 1) / nqb::prog::kTileRows * tokens;
+  nqb::prog::residual_stats_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0,
+                                      static_cast<cudaStream_t>(stream)>>>(h, tokens, hidden, stats);
+  NQB_CUDA(cudaGetLastError(), "residual stats launch");
+  return ok();
 }
 
 int nqb_debug_set_barrier_limit(uint32_t polls) {

@@ -145,6 +145,12 @@ def random_shell_weights(shape: DecoderShape, vocab: int, device: torch.device, 
         norm(shape.hidden), (0.02 * torch.randn(vocab, shape.hidden, generator=g, device=device)).bfloat16())
 
 
+def residual_stats(h: torch.Tensor, stats: torch.Tensor) -> None:
+    """Per-128-row sums of squares of the residual stream ``h [T, hidden]`` into ``stats`` (``nqb_residual_stats``)."""
+
+    _native.call("nqb_residual_stats", h.data_ptr(), h.shape[0], h.shape[1], stats.data_ptr(), _stream(h.device))
+
+
 class Qwen3DecodeStep:
     """One decode step of ``tokens`` new tokens at cache position ``position``.
 
@@ -155,13 +161,28 @@ class Qwen3DecodeStep:
     :meth:`step` returns the fp32 logits ``[tokens, vocab]``; the position
     does not advance (each step recomputes the same tokens), so replays of a
     captured step are identical.
+
+    ``engine="fused"`` (default; head_dim 128, 4 q heads per kv head): every
+    layer runs inside ONE persistent program -- per layer a q/k/v op that
+    normalises the residual stream as it loads it and ends in the q/k norm,
+    RoPE and cache append, the attention op, o with the residual add, gate/up
+    with the post-attention norm folded in, and down (SwiGLU input) with the
+    residual add -- then the final norm and the lm head: four launches per
+    step.  The normalised activations stay fp32 (no bf16 rounding).
+    ``engine="shell"``: three programs per layer around separate shell kernels
+    (norms, q/k norm + RoPE, attention), with bf16 normalised activations.
     """
 
     def __init__(self, shape: DecoderShape, blocks, shell: ShellWeights, device: torch.device, *, tokens: int = 1,
                  position: int = 0, cache_len: int | None = None, eps: float = 1e-6, rope_theta: float = 1e6,
-                 kv_init: torch.Generator | None = None) -> None:
+                 kv_init: torch.Generator | None = None, engine: str | None = None) -> None:
         if not 1 <= tokens <= 16:
             raise ValueError("a decode step takes 1 to 16 tokens")
+        fusable = shape.head_dim == 128 and shape.q_heads == 4 * shape.kv_heads
+        engine = engine or ("fused" if fusable else "shell")
+        if engine not in ("fused", "shell") or (engine == "fused" and not fusable):
+            raise ValueError(f"engine {engine!r} is not available for this shape")
+        self.engine = engine
         self.shape, self.device, self.tokens, self.position, self.eps = shape, device, tokens, position, eps
         self.shell = shell
         self.cache_len = cache_len if cache_len is not None else position + tokens
@@ -199,15 +220,64 @@ class Qwen3DecodeStep:
             if position:
                 kc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
                 vc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
-            self.layers.append({
-                "prog_qkv": DecodeProgram([ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]),
-                                                     self.xn)], outputs=[(q, k, v)]),
-                "prog_o": DecodeProgram([ProgramOp((prepared["o_proj"],), self.attn)], outputs=[(o,)]),
-                "prog_mlp": self._mlp_program(prepared, gate, up, down),
-                "q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc, "v_cache": vc,
-                "prepared": prepared,
-            })
+            layer = {"q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc,
+                     "v_cache": vc, "prepared": prepared}
+            if engine == "shell":
+                layer.update({
+                    "prog_qkv": DecodeProgram([ProgramOp((prepared["q_proj"], prepared["k_proj"],
+                                                          prepared["v_proj"]), self.xn)], outputs=[(q, k, v)]),
+                    "prog_o": DecodeProgram([ProgramOp((prepared["o_proj"],), self.attn)], outputs=[(o,)]),
+                    "prog_mlp": self._mlp_program(prepared, gate, up, down),
+                })
+            self.layers.append(layer)
+        self.program: DecodeProgram | None = None
+        if engine == "fused":
+            self.stats = torch.zeros((shape.hidden + 127) // 128, tokens, **f32)
+            self.program = self._fused_program()
         self.graph: torch.cuda.CUDAGraph | None = None
+
+    def _fused_program(self) -> DecodeProgram:
+        """Every layer as five ops of one program (q/k/v, attention, o, gate/up, down)."""
+
+        s = self.shape
+        ops, outputs = [], []
+        w_dtype = _native.dtype_code(self.shell.input_norm[0].dtype)
+
+        def ext(**fields) -> _native.ProgramOpExt:
+            e = _native.ProgramOpExt()
+            e.kind = _native.NQB_OP_LINEAR
+            e.epilogue = _native.NQB_EPI_STORE
+            e.eps = self.eps
+            for name, value in fields.items():
+                setattr(e, name, value)
+            return e
+
+        for index, layer in enumerate(self.layers):
+            prepared = layer["prepared"]
+            cache = {"q": self.q_rot.data_ptr(), "k_cache": layer["k_cache"].data_ptr(),
+                     "v_cache": layer["v_cache"].data_ptr(), "cache_len": self.cache_len, "position": self.position,
+                     "q_heads": s.q_heads, "kv_heads": s.kv_heads, "head_dim": s.head_dim}
+            ops.append(ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]), self.h, ext=ext(
+                epilogue=_native.NQB_EPI_QK_ROPE, norm_stats=self.stats.data_ptr(),
+                norm_weight=self.shell.input_norm[index].data_ptr(), norm_weight_dtype=w_dtype,
+                q_norm_weight=self.shell.q_norm[index].data_ptr(), k_norm_weight=self.shell.k_norm[index].data_ptr(),
+                qk_norm_dtype=_native.dtype_code(self.shell.q_norm[index].dtype), cos_table=self.cos.data_ptr(),
+                sin_table=self.sin.data_ptr(), **cache)))
+            outputs.append((layer["q"], layer["k"], layer["v"]))  # not written: the epilogue stores q and the caches
+            ops.append(ProgramOp((), None, ext=ext(kind=_native.NQB_OP_ATTENTION, attn_out=self.attn.data_ptr(),
+                                                   **cache)))
+            outputs.append(())
+            ops.append(ProgramOp((prepared["o_proj"],), self.attn, ext=ext(
+                epilogue=_native.NQB_EPI_RESIDUAL, out_stats=self.stats.data_ptr())))
+            outputs.append((self.h,))
+            ops.append(ProgramOp((prepared["gate_proj"], prepared["up_proj"]), self.h, ext=ext(
+                norm_stats=self.stats.data_ptr(), norm_weight=self.shell.post_norm[index].data_ptr(),
+                norm_weight_dtype=w_dtype)))
+            outputs.append((layer["gate"], layer["up"]))
+            ops.append(ProgramOp((prepared["down_proj"],), layer["gate"], x2=layer["up"], ext=ext(
+                epilogue=_native.NQB_EPI_RESIDUAL, out_stats=self.stats.data_ptr())))
+            outputs.append((self.h,))
+        return DecodeProgram(ops, outputs=outputs)
 
     def _mlp_program(self, prepared: dict, gate: torch.Tensor, up: torch.Tensor,
                      down: torch.Tensor) -> DecodeProgram | tuple[DecodeProgram, DecodeProgram]:
@@ -223,9 +293,12 @@ class Qwen3DecodeStep:
                 DecodeProgram([ProgramOp((prepared["down_proj"],), self.act)], outputs=[(down,)]))
 
     def kernel_launches(self) -> int:
-        """Kernels one step launches: per layer 3 programs (4 with a split MLP, plus its SwiGLU kernel), 2 norms,
-        rope and attention (2); then the final norm and the lm head (the input copy is a library copy)."""
+        """Kernels one step launches.  Fused: the residual statistics, the program, the final norm and the lm head.
+        Shell: per layer 3 programs (4 with a split MLP, plus its SwiGLU kernel), 2 norms, rope and attention (2);
+        then the final norm and the lm head (the input copy is a library copy)."""
 
+        if self.engine == "fused":
+            return 4
         split = sum(isinstance(layer["prog_mlp"], tuple) for layer in self.layers)
         return len(self.layers) * 8 + 2 * split + 2
 
@@ -237,6 +310,12 @@ class Qwen3DecodeStep:
         if hidden is not None:
             self.hidden_in.copy_(hidden)
         self.h.copy_(self.hidden_in)
+        if self.program is not None:
+            residual_stats(self.h, self.stats)
+            self.program.run(dependent=True)
+            rmsnorm(self.h, None, self.shell.final_norm, self.eps, self.xn)
+            gemv_bf16(self.shell.lm_head, self.xn, self.logits)
+            return self.logits
         delta = None
         for index, layer in enumerate(self.layers):
             rmsnorm(self.h, delta, self.shell.input_norm[index], self.eps, self.xn)
@@ -521,6 +600,7 @@ __all__ = [
     "gemv_bf16",
     "qk_norm_rope",
     "random_shell_weights",
+    "residual_stats",
     "rmsnorm",
     "rope_tables",
     "silu_mul",

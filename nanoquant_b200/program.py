@@ -40,9 +40,17 @@ class ProgramOp:
     """
 
     layers: tuple[PreparedLayer, ...]
-    x: torch.Tensor
+    x: torch.Tensor | None
     x2: torch.Tensor | None = None
     activation: str = "silu"
+    # decoder-step extensions (``nqb_program_op_ext``): a residual-stream input
+    # norm, a fused epilogue (residual add with norm statistics, or q/k head
+    # norm + RoPE + KV-cache append), or an attention op (no layers, no x)
+    ext: _native.ProgramOpExt | None = None
+
+    @property
+    def is_attention(self) -> bool:
+        return self.ext is not None and self.ext.kind == _native.NQB_OP_ATTENTION
 
 
 class DecodeProgram:
@@ -51,13 +59,29 @@ class DecodeProgram:
     def __init__(self, ops: Sequence[ProgramOp], *, outputs: Sequence[Sequence[torch.Tensor]] | None = None) -> None:
         if not ops:
             raise ValueError("a program needs at least one op")
-        device = ops[0].x.device
+        linear_ops = [op for op in ops if not op.is_attention]
+        if not linear_ops:
+            raise ValueError("a program needs at least one linear op")
+        device = linear_ops[0].x.device
         tokens = None
         self.ops = tuple(ops)
         self.outputs: list[tuple[torch.Tensor, ...]] = []
         self._keep: list[object] = []
         c_ops = (_native.ProgramOp * len(ops))()
         for index, op in enumerate(ops):
+            if op.is_attention:
+                if op.layers or op.x is not None:
+                    raise ValueError("an attention op has no layers and no x")
+                self.outputs.append(())
+                self._keep.append(op.ext)
+                c_ops[index].layers = None
+                c_ops[index].count = 0
+                c_ops[index].x = None
+                c_ops[index].x_dtype = 0
+                c_ops[index].y = None
+                c_ops[index].x2 = None
+                c_ops[index].ext = ctypes.pointer(op.ext)
+                continue
             if not 1 <= len(op.layers) <= 3:
                 raise ValueError("an op has 1 to 3 layers")
             payloads = tuple(layer.payload for layer in op.layers)
@@ -104,7 +128,11 @@ class DecodeProgram:
                 raise ValueError(f"unknown gate activation {op.activation!r}")
             c_ops[index].y = ys
             c_ops[index].x2 = None if op.x2 is None else op.x2.data_ptr()
-        assert tokens is not None
+            c_ops[index].ext = None if op.ext is None else ctypes.pointer(op.ext)
+            if op.ext is not None:
+                self._keep.append(op.ext)
+        if tokens is None:
+            raise ValueError("a program needs at least one linear op")
         self.device = device
         self.tokens = tokens
         handle = ctypes.c_void_p(None)

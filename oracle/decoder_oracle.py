@@ -76,20 +76,23 @@ def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, keys: int
 
 def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_cache: np.ndarray, *,
                  position: int, q_heads: int, kv_heads: int, head_dim: int, eps: float, cos: np.ndarray,
-                 sin: np.ndarray, accumulate: str = "float64") -> np.ndarray:
+                 sin: np.ndarray, accumulate: str = "float64", xn_bf16: bool = True) -> np.ndarray:
     """One Qwen3-style layer on the residual stream ``h [T, hidden]``; returns the new ``h``.
 
     ``proj``: ``OracleLayer`` per projection name; ``norms``: this layer's
     ``input_norm``, ``post_norm``, ``q_norm`` and ``k_norm``.  The caches are
-    updated in place at rows ``position + t``.
+    updated in place at rows ``position + t``.  ``xn_bf16``: the normalised
+    activations are rounded to bf16 before the projections (the device's
+    shell engine stores them as bf16; its fused engine keeps them fp32).
     """
 
     tokens = h.shape[0]
+    rnd = bf16 if xn_bf16 else (lambda value: value)
 
     def linear(x: np.ndarray, layer) -> np.ndarray:
         return po.packed_linear(x, layer, accumulate=accumulate).astype(np.float32)
 
-    xn = bf16(rmsnorm(h, norms["input_norm"], eps))
+    xn = rnd(rmsnorm(h, norms["input_norm"], eps))
     q = linear(xn, proj["q_proj"]).reshape(tokens, q_heads, head_dim)
     k = linear(xn, proj["k_proj"]).reshape(tokens, kv_heads, head_dim)
     v = linear(xn, proj["v_proj"]).reshape(tokens, kv_heads, head_dim)
@@ -100,7 +103,7 @@ def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_
         v_cache[:, position + t] = bf16(v[t])
     a = bf16(attention(q, k_cache, v_cache, position + 1).reshape(tokens, q_heads * head_dim))
     h = h + linear(a, proj["o_proj"])
-    xn = bf16(rmsnorm(h, norms["post_norm"], eps))
+    xn = rnd(rmsnorm(h, norms["post_norm"], eps))
     gate = linear(xn, proj["gate_proj"])
     up = linear(xn, proj["up_proj"])
     with np.errstate(over="ignore"):  # exp(-gate) overflows to inf for very negative gates: silu -> 0
@@ -111,7 +114,7 @@ def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_
 def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_norm: np.ndarray,
                           lm_head: np.ndarray, *, position: int, q_heads: int, kv_heads: int, head_dim: int,
                           eps: float, theta: float, accumulate: str = "float64",
-                          head_accumulate: str = "float64") -> np.ndarray:
+                          head_accumulate: str = "float64", xn_bf16: bool = True) -> np.ndarray:
     """Logits ``[T, vocab]`` of a step whose layers arrive one at a time.
 
     ``layer_at(i)`` returns ``(proj, norms, k_cache, v_cache)`` of layer i (the
@@ -126,7 +129,7 @@ def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_
     for i in range(layer_count):
         proj, norms, k_cache, v_cache = layer_at(i)
         h = decode_layer(h, proj, norms, k_cache, v_cache, position=position, q_heads=q_heads, kv_heads=kv_heads,
-                         head_dim=head_dim, eps=eps, cos=cos, sin=sin, accumulate=accumulate)
+                         head_dim=head_dim, eps=eps, cos=cos, sin=sin, accumulate=accumulate, xn_bf16=xn_bf16)
     xn = bf16(rmsnorm(h, final_norm, eps))
     if head_accumulate == "float64":
         return (xn.astype(np.float64) @ lm_head.astype(np.float64).T).astype(np.float32)
@@ -135,7 +138,7 @@ def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_
 
 def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: list[np.ndarray],
                 v_caches: list[np.ndarray], *, position: int, q_heads: int, kv_heads: int, head_dim: int,
-                eps: float, theta: float) -> tuple[np.ndarray, list[np.ndarray], list[np.ndarray]]:
+                eps: float, theta: float, xn_bf16: bool = True) -> tuple[np.ndarray, list[np.ndarray], list[np.ndarray]]:
     """Logits ``[T, vocab]`` and the updated caches.
 
     ``layers[i]``: ``OracleLayer`` per projection name; ``norms``: lists
@@ -152,7 +155,7 @@ def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: l
 
     logits = decode_step_streaming(hidden, len(layers), layer_at, norms["final_norm"], norms["lm_head"],
                                    position=position, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, eps=eps,
-                                   theta=theta)
+                                   theta=theta, xn_bf16=xn_bf16)
     return logits, k_caches, v_caches
 
 

@@ -204,6 +204,52 @@ def test_decoder_step_matches_oracle(tokens: int) -> None:
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("tokens", (1, 3, 16))
+def test_fused_decoder_step_matches_oracle(tokens: int) -> None:
+    """The fused engine (one program for every layer: residual-stream norms, q/k norm + RoPE + cache append and
+    attention inside it) against the oracle with fp32 normalised activations; caches and shell path agree."""
+
+    from nanoquant_b200.decode_chain import DecoderShape, make_decoder_layers
+    from nanoquant_b200.decoder import Qwen3DecodeStep, random_shell_weights
+    from tests.test_cuda_parity import oracle_from_state
+
+    dev = _gpu()
+    shape = DecoderShape("fusable", 3, 512, 1024, 8, 2, 128, 1.0)
+    blocks = make_decoder_layers(shape, dev, layers=3, seed=24)
+    shell = random_shell_weights(shape, 2000, dev, layers=3, seed=25)
+    step = Qwen3DecodeStep(shape, blocks, shell, dev, tokens=tokens, position=300,
+                           kv_init=torch.Generator(device=dev).manual_seed(26))
+    assert step.engine == "fused" and step.kernel_launches() == 4
+    k0 = [layer["k_cache"].float().cpu().numpy() for layer in step.layers]
+    v0 = [layer["v_cache"].float().cpu().numpy() for layer in step.layers]
+    hidden = torch.randn(tokens, shape.hidden, generator=torch.Generator(device=dev).manual_seed(27), device=dev)
+    logits = step.step(hidden).cpu().numpy()
+    again = step.step(hidden).cpu().numpy()
+    torch.cuda.synchronize()
+    assert np.array_equal(logits, again)  # deterministic
+    layers = [{name: oracle_from_state(_host_state(state)) for name, state in block.items()} for block in blocks]
+    norms = {
+        "input_norm": [w.float().cpu().numpy() for w in shell.input_norm],
+        "post_norm": [w.float().cpu().numpy() for w in shell.post_norm],
+        "q_norm": [w.float().cpu().numpy() for w in shell.q_norm],
+        "k_norm": [w.float().cpu().numpy() for w in shell.k_norm],
+        "final_norm": shell.final_norm.float().cpu().numpy(),
+        "lm_head": shell.lm_head.float().cpu().numpy(),
+    }
+    ref, k1, v1 = do.decode_step(hidden.cpu().numpy(), layers, norms, k0, v0, position=300, q_heads=8, kv_heads=2,
+                                 head_dim=128, eps=1e-6, theta=1e6, xn_bf16=False)
+    for a, b in zip(logits, ref, strict=True):
+        cosine = float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+        assert cosine >= 0.99999, cosine
+    for i, layer in enumerate(step.layers):
+        np.testing.assert_allclose(layer["k_cache"].float().cpu().numpy()[:, 300:300 + tokens],
+                                   k1[i][:, 300:300 + tokens], rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(layer["v_cache"].float().cpu().numpy()[:, 300:300 + tokens],
+                                   v1[i][:, 300:300 + tokens], rtol=2e-2, atol=2e-2)
+        assert np.array_equal(layer["k_cache"].float().cpu().numpy()[:, :300], k0[i][:, :300])
+
+
+@pytest.mark.gpu
 def test_decoder_step_graph_replay_is_bitwise_eager() -> None:
     from nanoquant_b200.decoder import build_qwen3_step
 

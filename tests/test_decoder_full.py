@@ -76,7 +76,7 @@ def test_qwen3_8b_full_step_logits_match_oracle_at_bs16_and_bs1() -> None:
                                    shell.final_norm.float().cpu().numpy(), shell.lm_head.float().cpu().numpy(),
                                    position=POSITION, q_heads=shape.q_heads, kv_heads=shape.kv_heads,
                                    head_dim=shape.head_dim, eps=1e-6, theta=1e6, accumulate="float32",
-                                   head_accumulate="float32")
+                                   head_accumulate="float32", xn_bf16=False)
     cos16 = _cosines(logits16, ref)
     cos1 = _cosines(logits1, ref[:1])
     assert min(cos16) >= 0.9999, cos16

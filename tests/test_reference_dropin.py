@@ -148,7 +148,7 @@ def test_reference_loader_planner_and_linear_at_on_sm100(tokens: int) -> None:
     if not torch.cuda.is_available():
         pytest.fail("GPU test needs CUDA")
     artifact = rt.open_packed_artifact(GOLDEN / "packed_artifact")
-    names = artifact.layer_names()
+    names = tuple(layer.spec.name for block in artifact.manifest.blocks for layer in block.layers)
     states = {name: artifact.load_layer(name) for name in names}
     assert all(type(s).__module__.startswith("nanoquant.runtime") for s in states.values())
     kind = "decode" if tokens == 1 else "prefill"
