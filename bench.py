@@ -222,6 +222,45 @@ def cpu_gemma_baseline(tokens: int, steps: int = 3, warmup: int = 1) -> dict:
                       f"gated gelu), final norm; {threads} host threads ({_cpu_model()}); {steps} timed steps"}
 
 
+def cpu_codebook_baseline(tokens: int, sample_layers: int = 2, repeats: int = 3) -> dict:
+    """The oracle (product-codebook decode to layout v1 at prepare, then the reference's packed linear plus the
+    int8 row overlay) on ``sample_layers`` config-4 layers, scaled to 26 layers."""
+
+    import numpy as np
+
+    from nanoquant_b200.decode_chain import GEMMA3_1B, make_codebook_layers
+    from oracle import packed_oracle as po
+
+    blocks = make_codebook_layers(GEMMA3_1B, layers=sample_layers, seed=0)
+    rng = np.random.default_rng(1)
+    layers = []
+    for block in blocks:
+        for state in block.values():
+            packed = state.base.to_packed()
+            layer = po.OracleLayer(
+                packed.spec.in_features, packed.spec.out_features, packed.spec.rank, packed.left_words.numpy(),
+                packed.right_words.numpy(), packed.scale_pre.float().numpy(), packed.scale_mid.float().numpy(),
+                packed.scale_post.float().numpy())
+            layer.overlay_row_ids = state.overlay.row_ids.numpy()
+            layer.overlay_values = state.overlay.values.numpy()
+            layer.overlay_scales = state.overlay.scales.float().numpy()
+            layer.prepared()
+            layers.append((layer, rng.standard_normal((tokens, layer.in_features)).astype(np.float32)))
+    for layer, x in layers:
+        po.packed_linear(x, layer)
+    start = time.perf_counter()
+    for _ in range(repeats):
+        for layer, x in layers:
+            po.packed_linear(x, layer)
+    step = (time.perf_counter() - start) / repeats * GEMMA3_1B.layers / sample_layers
+    threads = _cpu_threads()
+    return {"value": tokens / step, "unit": UNIT, "cores": threads, "kind": "port", "ms_per_step": step * 1e3,
+            "cpu_model": _cpu_model(),
+            "sample": f"{sample_layers} of 26 config-4 layers x 7 projections, {tokens} token(s), {repeats} reps: the "
+                      f"oracle port (codebook decoded at prepare, fp32 packed linear, int8 row overlay) on {threads} "
+                      f"host threads ({_cpu_model()}); scaled to 26 layers"}
+
+
 def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200) -> dict:
     """The oracle port of ``PackedReferenceBackend.linear`` on one config-0 layer."""
 
@@ -371,6 +410,35 @@ class ChainRunner:
         return self.chain.algorithmic_bytes()
 
 
+class CodebookRunner:
+    """BASELINE config 4 on Gemma-3-1B shapes: 26 layers x 7 product-codebook linears with int8 outlier rows.
+
+    ``tokens`` <= 16: one persistent program per step (decode); more: the
+    per-call tensor-core prefill kernels.
+    """
+
+    def __init__(self, device, tokens: int, layers: int | None) -> None:
+        from nanoquant_b200.decode_chain import GEMMA3_1B, DecodeChain, make_codebook_layers
+
+        engine = "program" if tokens <= 16 else "calls"
+        self.bound = "hbm" if tokens <= 16 else "tensor"
+        self.chain = DecodeChain(GEMMA3_1B, make_codebook_layers(GEMMA3_1B, layers=layers, seed=0), device,
+                                 tokens=tokens, engine=engine)
+        self.tokens = tokens
+        self.layers = len(self.chain.blocks)
+        self.input = self.chain.inputs["hidden"]
+        self.launches_per_step = self.chain.launches_per_step
+
+    def run(self):
+        return self.chain.step()
+
+    def algorithmic_bytes(self) -> int:
+        return self.chain.algorithmic_bytes()
+
+    def algorithmic_flops(self) -> int:
+        return self.chain.algorithmic_flops()
+
+
 class PrefillRunner:
     """Llama-3-8B (0.55 bpw) packed linears on ``tokens`` tokens per rank (tensor-core prefill kernels)."""
 
@@ -493,6 +561,19 @@ WORKLOADS = {
                 "description": "llama-3-8b packed linears, prefill 8x4096 tokens ({layers} layers x "
                                "q,k,v,o,gate,up,down)",
                 "model": "llama-3-8b-shape random-init packed weights 0.55 bpw"},
+    "codebook-decode": {"kind": "codebook", "metric": "codebook decode tok/s (bs1, Gemma-3-1B shapes, product-"
+                                                      "codebook V + 1% int8 rows); HBM GB/s",
+                        "tokens": 1,
+                        "description": "gemma-3-1b product-codebook packed linears with int8 outlier rows, decode bs1 "
+                                       "({layers} layers x q,k,v,o,gate,up,down in one program)",
+                        "model": "config 4: 8-bit group indices into one 256-entry 16-bit table per layer, plain U, "
+                                 "1% int8 rows (scale 0.002)"},
+    "codebook-prefill": {"kind": "codebook", "metric": "codebook prefill tok/s (bs64, Gemma-3-1B shapes, product-"
+                                                       "codebook V + 1% int8 rows); TFLOP/s",
+                         "tokens": 64,
+                         "description": "gemma-3-1b product-codebook packed linears with int8 outlier rows, prefill 64 "
+                                        "tokens ({layers} layers x q,k,v,o,gate,up,down, tensor-core kernels)",
+                         "model": "config 4 (as codebook-decode)"},
     "single-linear": {"kind": "single", "metric": "single packed linear tok/s (2048x640 r480); HBM GB/s",
                       "tokens": 1,
                       "description": "one 640->2048 rank-480 packed linear (config 0), {tokens} token(s)",
@@ -514,6 +595,8 @@ def _build(name: str, device, tokens: int, layers: int | None, engine: str | Non
         return StepRunner(device, tokens, layers)
     if kind == "gemma":
         return GemmaStepRunner(device, tokens, layers)
+    if kind == "codebook":
+        return CodebookRunner(device, tokens, layers)
     if kind == "linears":
         return ChainRunner(decode_chain.QWEN3_8B, device, tokens, layers, engine)
     if kind == "prefill":
@@ -572,6 +655,30 @@ class Timer:
                 sampler.__exit__()
         (elapsed,) = self.max_over_ranks(start.elapsed_time(stop))
         return elapsed / steps, (sampler.summary() if sampler is not None else None)
+
+
+def _time_step_program(step, steps: int, warmup: int, timer: Timer) -> dict:
+    """Mean device time of the step's program launch: CUDA events around each launch (the residual copy and
+    statistics kernels before it run outside the event pair), max over ranks."""
+
+    import torch
+
+    from nanoquant_b200.decoder import residual_stats
+
+    stream = torch.cuda.current_stream(step.device)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(warmup + steps):
+        step.h.copy_(step.hidden_in)
+        residual_stats(step.h, step.stats)
+        if i >= warmup:
+            pairs[i - warmup][0].record(stream)
+        step.program.run()
+        if i >= warmup:
+            pairs[i - warmup][1].record(stream)
+    torch.cuda.synchronize(step.device)
+    _check_status("the step-program timing")
+    (ms,) = timer.max_over_ranks(sum(a.elapsed_time(b) for a, b in pairs) / steps)
+    return {"ms": ms, "bytes": step.program_bytes(), "launches": steps}
 
 
 def _check_status(where: str) -> None:
@@ -672,6 +779,8 @@ def run_reference(args, rank: int) -> None:
         base = cpu_prefill_baseline()
     elif kind in ("single", "stacked"):
         base = cpu_linear_baseline(640, 2048, 480, tokens)
+    elif kind == "codebook":
+        base = cpu_codebook_baseline(tokens)
     else:
         raise SystemExit(f"no CPU reference path for workload {args.workload}")
     line = {
@@ -796,7 +905,7 @@ def main() -> None:
         "gpu_launches": runner.launches_per_step * args.steps,
         "clocks": clocks,
     }
-    if kind == "prefill":
+    if kind == "prefill" or getattr(runner, "bound", "hbm") == "tensor":
         line["roofline"] = _tensor_roofline(runner.algorithmic_flops(), ms_per_step, peaks,
                                             "all packed-linear kernels of one step per GPU (2*r*(m+n) flops per "
                                             "token and linear / step time)")
@@ -805,25 +914,34 @@ def main() -> None:
         scope = {"step": "the whole decoder step: packed weights and scales, kv rows read, norms, lm head",
                  "gemma": "the whole decoder step: packed weights and scales, kv rows read, norms, embedding rows",
                  "linears": "the persistent decode program: every packed linear of the step in one launch",
-                 "single": "one launch pair of the config-0 layer", "stacked": "the program of 1024 layers"}[kind]
+                 "single": "one launch pair of the config-0 layer", "stacked": "the program of 1024 layers",
+                 "codebook": "the program of all config-4 linears (bytes of the compact format: U words, V group "
+                             "indices, tables, scales, int8 rows)"}[kind]
         line["roofline"] = _hbm_roofline(step_bytes, ms_per_step, peaks, scope)
+    step_program = None
+    if kind == "step" and getattr(runner.step_obj, "program", None) is not None:
+        step_program = _time_step_program(runner.step_obj, args.steps, args.warmup, timer)
     del runner
     torch.cuda.empty_cache()
 
     if kind == "step" and not args.no_extras:
-        # the dominant kernel of the step: the packed linears as one program launch
         line["step_roofline"] = line["roofline"]
         from nanoquant_b200.decode_chain import QWEN3_8B
 
+        if step_program is not None:
+            # the dominant kernel: the step's program (every layer in one launch), timed per launch
+            line["roofline"] = _hbm_roofline(step_program["bytes"], step_program["ms"], peaks,
+                                             "dominant kernel: the decode-step program (all 36 layers: packed "
+                                             "linears, norms, q/k norm + rope, attention; bytes per launch / mean "
+                                             "launch time, CUDA events around each of the timed launches)")
+            line["roofline"]["launches_timed"] = step_program["launches"]
+        # the packed linears alone as one program launch per step (no shell work)
         linears = ChainRunner(QWEN3_8B, device, tokens, args.layers)
         lin_ms, _ = timer.time(linears.run, args.steps, args.warmup)
         _check_status("the linears-only run")
-        line["roofline"] = _hbm_roofline(linears.algorithmic_bytes(), lin_ms, peaks,
-                                         "dominant kernel: the persistent decode program running all 252 packed "
-                                         "linears of the step in one launch (bytes per launch / launch time, CUDA "
-                                         "events over the same number of launches)")
         line["linears"] = {"value": tokens * world * 1000.0 / lin_ms, "unit": UNIT, "ms_per_step": lin_ms,
-                           "algorithmic_bytes_per_step": linears.algorithmic_bytes()}
+                           "algorithmic_bytes_per_step": linears.algorithmic_bytes(),
+                           "roofline_frac": linears.algorithmic_bytes() / (lin_ms * 1e-3) / 1e9 / peaks["hbm"][0]}
         del linears
         torch.cuda.empty_cache()
     if not args.no_extras and kind != "prefill":
@@ -840,6 +958,8 @@ def main() -> None:
             base = cpu_prefill_baseline()
         elif kind in ("single", "stacked"):
             base = cpu_linear_baseline(640, 2048, 480, tokens)
+        elif kind == "codebook":
+            base = cpu_codebook_baseline(tokens)
         else:
             base = None
         if base is not None:

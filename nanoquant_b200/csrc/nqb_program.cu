@@ -126,8 +126,20 @@ struct OpDev {
   int64_t cache_len, position;
   __nv_bfloat16 *attn_out;
   int32_t att_splits;
-  int64_t att_chunk;
+  int64_t att_chunk;         // keys per split, a multiple of 16
+  int32_t att_ring_blocks;   // at most this many 16-row K/V blocks of a unit arrive through the sign ring
 };
+
+// 16-row K and V blocks of attention unit (split sp) that stream through the
+// sign ring: the unit's rows before this step's tokens (they do not change
+// during the program), whole blocks only, at most op.att_ring_blocks.  The
+// host lists the same blocks in the CTA's slice addresses.
+__host__ __device__ inline int att_unit_ring_blocks(const OpDev &op, int sp) {
+  const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+  const int64_t old_end = op.position < k0 + op.att_chunk ? op.position : k0 + op.att_chunk;
+  const int64_t blocks = old_end > k0 ? (old_end - k0) / 16 : 0;
+  return static_cast<int>(blocks < op.att_ring_blocks ? blocks : op.att_ring_blocks);
+}
 
 struct Item {
   int32_t member;
@@ -598,13 +610,30 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // shared memory (fixed order) and one partial per (token, q head, split) goes
 // to the workspace.  K/V rows are read through L2 (.cg): this step's rows were
 // written by the preceding stage.
-__device__ __noinline__ void attention_partials(const Params &p, const OpDev &op, float *scratch) {
+//
+// The unit's rows before this step's tokens arrive ahead of time as 16-row
+// blocks through the sign ring (K block, then V block; the producer streams
+// them with the sign slices, across the stage barriers), so most K/V reads
+// come from shared memory; the remaining rows (this step's, and any past the
+// ring's share) are read from global memory.  Every consumer warp waits for
+// the unit's ring slots first and hands them back after the last token.
+__device__ __noinline__ void attention_partials(const Params &p, const OpDev &op, float *scratch,
+                                                const uint8_t *ring, uint64_t *s_full, uint64_t *s_empty,
+                                                int &slot, uint32_t &phase, bool &ok) {
   const int T = p.tokens;
   const int units = op.kv_heads * op.att_splits;
   const int cta = static_cast<int>(blockIdx.x);
   if (cta >= units) return;  // uniform over the CTA
   const int kvh = cta / op.att_splits, sp = cta - kvh * op.att_splits;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int R = p.ring;
+  const int nb = att_unit_ring_blocks(op, sp);
+  for (int j = 0; j < 2 * nb; ++j) {
+    const int sj = (slot + j) % R;
+    const uint32_t ph = phase + static_cast<uint32_t>((slot + j) / R);
+    if (!wait_local(&s_full[sj], ph & 1)) ok = false;
+  }
+  const int64_t ring_rows = 16 * static_cast<int64_t>(nb);
   const float scale = rsqrtf(static_cast<float>(kAttHd));
   const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
   const __nv_bfloat16 *vbase = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
@@ -629,11 +658,22 @@ __device__ __noinline__ void attention_partials(const Params &p, const OpDev &op
     for (int64_t b0 = k0 + warp * kAttSub; b0 < k1; b0 += kAttSub * mmad::kWarps) {
       const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
       uint2 kr[kAttSub], vr[kAttSub];
+      if (b0 - k0 < ring_rows) {  // a whole sub-block inside a ring block (16 nb is a multiple of 8)
+        const int blk = static_cast<int>((b0 - k0) >> 4), within = static_cast<int>((b0 - k0) & 15);
+        const uint8_t *kslot = ring + static_cast<size_t>((slot + 2 * blk) % R) * kStageWeightBytes;
+        const uint8_t *vslot = ring + static_cast<size_t>((slot + 2 * blk + 1) % R) * kStageWeightBytes;
 #pragma unroll
-      for (int j = 0; j < kAttSub; ++j) {
-        const int64_t row = b0 + (j < nk ? j : 0);  // rows past the block re-read row b0 (masked below)
-        kr[j] = __ldcg(reinterpret_cast<const uint2 *>(kbase + row * kAttHd));
-        vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + row * kAttHd));
+        for (int j = 0; j < kAttSub; ++j) {
+          kr[j] = *reinterpret_cast<const uint2 *>(kslot + (within + j) * (kAttHd * 2) + lane * 8);
+          vr[j] = *reinterpret_cast<const uint2 *>(vslot + (within + j) * (kAttHd * 2) + lane * 8);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kAttSub; ++j) {
+          const int64_t row = b0 + (j < nk ? j : 0);  // rows past the block re-read row b0 (masked below)
+          kr[j] = __ldcg(reinterpret_cast<const uint2 *>(kbase + row * kAttHd));
+          vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + row * kAttHd));
+        }
       }
       float sv[32];
 #pragma unroll
@@ -716,6 +756,11 @@ __device__ __noinline__ void attention_partials(const Params &p, const OpDev &op
     }
     mmad::consumer_sync();  // the scratch is reused by the next token
   }
+  // every warp is done with the unit's ring blocks: hand them back
+  if (lane == 0)
+    for (int j = 0; j < 2 * nb; ++j) mbar_arrive_cta(&s_empty[(slot + j) % R]);
+  phase += static_cast<uint32_t>((slot + 2 * nb) / R);
+  slot = (slot + 2 * nb) % R;
 }
 
 // Joins the splits' partials of every (token, q head) in split order, one
@@ -755,7 +800,7 @@ __device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
 // tile's sums of squares of the new h per token to out_stats.
 template <int kT>
 __device__ __forceinline__ void residual_epilogue(const OpDev &op, const MemberDev &md, int tile, const float (&outv)[kT],
-                                                  int T, float *red) {
+                                                  const float (&hprev)[kT], int T, float *red) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row = static_cast<int64_t>(tile) * kTileRows + tid;
   float sq[kT];
@@ -763,9 +808,8 @@ __device__ __forceinline__ void residual_epilogue(const OpDev &op, const MemberD
   for (int t = 0; t < kT; ++t) {
     sq[t] = 0.0f;
     if (t < T && row < md.rows) {
-      const int64_t i = static_cast<int64_t>(t) * md.rows + row;
-      const float hn = __ldcg(md.y + i) + outv[t];
-      md.y[i] = hn;
+      const float hn = hprev[t] + outv[t];  // hprev: h of this row, loaded with the row scales
+      md.y[static_cast<int64_t>(t) * md.rows + row] = hn;
       sq[t] = hn * hn;
     }
   }
@@ -980,9 +1024,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       const StageInfo &op = s_info[g & 1];
       const int ib = 0;
       const int ie = op.n_items;
+      NQB_TRACE_BEGIN
       const OpDev &gop = p.ops[g >> 1];  // the op's decoder-step fields (read-only, global)
       int op_kind = NQB_OP_LINEAR, op_epi = NQB_EPI_STORE;
       bool normed = false;
+      float rms_part[kT];  // residual-stream input: warp 0's partial sums of h^2 (lane: tiles lane, lane + 32, ..)
+#pragma unroll
+      for (int t = 0; t < kT; ++t) rms_part[t] = 0.0f;
+      bool rms_pending = false;
       if constexpr (kStep) {
         op_kind = gop.kind;
         op_epi = st == 1 ? gop.epilogue : NQB_EPI_STORE;
@@ -991,14 +1040,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           // split-K partials over the CTAs (stage 1 of the op), then their join;
           // the CTA's exchange buffers are idle during these stages
           if (st == 0)
-            attention_partials(p, gop, s_acc);
+            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok);
           else
             attention_join(p, gop);
-        } else if (normed && tid < T) {
-          // h's per-tile sums of squares (written before this stage) -> the norm factor
-          float ss = 0.0f;
-          for (int i = 0; i < gop.stat_tiles; ++i) ss += __ldcg(gop.norm_stats + static_cast<int64_t>(i) * T + tid);
-          s_rms[tid] = rsqrtf(ss * gop.inv_n + gop.eps);  // read in the leader epilogue, after several barriers
+          NQB_TRACE(kTraceMma);
+        } else if (normed) {
+          // h's per-tile sums of squares (written before this stage): warp 0
+          // issues the loads now and reduces them while the quarters land
+          rms_pending = true;
+          if (warp == 0)
+            for (int i = lane; i < gop.stat_tiles; i += 32)
+#pragma unroll
+              for (int t = 0; t < kT; ++t)
+                if (t < T) rms_part[t] += __ldcg(gop.norm_stats + static_cast<int64_t>(i) * T + t);
         }
       }
       // kMixed: item j's slices, the records of a coded tile decoded where a
@@ -1031,7 +1085,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
         }
       };
-      NQB_TRACE_BEGIN
       for (int gb = ib; gb < ie; gb += p.group) {
         const int ge = min(gb + p.group, ie);
         for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
@@ -1217,10 +1270,15 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         }
         // leaders load the row scales and bias of their tiles while the quarters land
         float lead_scale[kLead], lead_bias[kLead];
+        float lead_h[kStep ? kLead : 1][kT];  // residual epilogues: h of the led rows, loaded early
 #pragma unroll
         for (int sidx = 0; sidx < kLead; ++sidx) {
           lead_scale[sidx] = 0.0f;
           lead_bias[sidx] = 0.0f;
+          if constexpr (kStep) {
+#pragma unroll
+            for (int t = 0; t < kT; ++t) lead_h[sidx][t] = 0.0f;
+          }
           const int jj = static_cast<int>(rank) + sidx * kClusterSize;
           if (jj < ge - gb && tid < kTileRows) {
             const Item item = op.items[gb + jj];
@@ -1229,7 +1287,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             if (row < md.rows) {
               lead_scale[sidx] = __ldg(md.row_scale + row);
               if (md.bias != nullptr) lead_bias[sidx] = __ldg(md.bias + row);
+              if constexpr (kStep) {
+                if (op_epi == NQB_EPI_RESIDUAL)
+#pragma unroll
+                  for (int t = 0; t < kT; ++t)
+                    if (t < T) lead_h[sidx][t] = __ldcg(md.y + static_cast<int64_t>(t) * md.rows + row);
+              }
             }
+          }
+        }
+        if constexpr (kStep) {
+          if (rms_pending) {  // the norm factors, read by the leader epilogue after the next consumer barrier
+            if (warp == 0) {
+#pragma unroll
+              for (int t = 0; t < kT; ++t) {
+                const float ss = warp_sum(rms_part[t]);
+                if (lane == 0 && t < T) s_rms[t] = rsqrtf(ss * gop.inv_n + gop.eps);
+              }
+            }
+            rms_pending = false;
           }
         }
         NQB_TRACE(kTraceSend);
@@ -1312,7 +1388,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           }
           if constexpr (kStep) {
             if (op_epi == NQB_EPI_RESIDUAL && tid < kTileRows)
-              residual_epilogue<kT>(gop, md, item.tile, outv, T, s_epi + kT * kTileRows);
+              residual_epilogue<kT>(gop, md, item.tile, outv, lead_h[kStep ? sidx : 0], T, s_epi + kT * kTileRows);
             else if (op_epi == NQB_EPI_QK_ROPE && tid < kTileRows)
               qk_rope_epilogue<kT>(gop, item.member, item.tile, outv, T, s_epi, s_epi + kT * kTileRows);
           }
@@ -1829,9 +1905,12 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   for (int i = 0; i < op_count; ++i) {
     OpDev &od = opdev[i];
     if (od.kind != NQB_OP_ATTENTION) continue;
-    od.att_splits = std::max(1, std::min(32, ctas / od.kv_heads));
+    const int want = std::max(1, std::min(32, ctas / od.kv_heads));
     const int64_t most = od.position + tokens;  // keys the last token sees
-    od.att_chunk = (most + od.att_splits - 1) / od.att_splits;
+    od.att_chunk = ((most + want - 1) / want + 15) / 16 * 16;
+    od.att_splits = static_cast<int32_t>((most + od.att_chunk - 1) / od.att_chunk);
+    // K and V blocks of a unit must fit the ring at once (the consumers hold them all)
+    od.att_ring_blocks = std::max(0, sp.ring / 2 - 1);
     att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.q_heads * od.att_splits * kAttRow);
   }
 
@@ -1918,6 +1997,19 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
           }
         }
         std::vector<uint64_t> &addrs = lists[c * kClusterSize + q];
+        if (op.kind == NQB_OP_ATTENTION && st == 0) {
+          // this CTA's attention unit: its old K and V rows as 16-row blocks (4 KB each, K then V)
+          const int cta_id = c * kClusterSize + q;
+          if (cta_id < op.kv_heads * op.att_splits) {
+            const int kvh = cta_id / op.att_splits, spl = cta_id % op.att_splits;
+            const int nb = att_unit_ring_blocks(op, spl);
+            for (int b = 0; b < nb; ++b) {
+              const int64_t row = static_cast<int64_t>(kvh) * op.cache_len + static_cast<int64_t>(spl) * op.att_chunk + 16 * b;
+              addrs.push_back(reinterpret_cast<uint64_t>(op.k_cache + row * kAttHd));
+              addrs.push_back(reinterpret_cast<uint64_t>(op.v_cache + row * kAttHd));
+            }
+          }
+        }
         for (size_t gb = 0; gb < list.size(); gb += sp.group) {
           const size_t ge = std::min(list.size(), gb + sp.group);
           for (size_t j0 = gb; j0 < ge;) {

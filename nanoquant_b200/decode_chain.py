@@ -20,6 +20,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from nanoquant_b200.backend import PreparedLayer, QuantizedLinearSpec
@@ -95,6 +96,73 @@ def random_packed_layer(name: str, n: int, m: int, r: int, generator: torch.Gene
                             torch.ones(r, device=device).half(), scales(m))
 
 
+def random_codebook_layer(name: str, n: int, m: int, r: int, rng: np.random.Generator, *,
+                          overlay_fraction: float = 0.01):
+    """A product-codebook layer with int8 outlier rows, on the host.
+
+    Every 16-sign group of V is an 8-bit index into one per-layer table of 256
+    random 16-bit sign words: a 32-bit word of V is the record ``lo | hi << 8``
+    of ``product-codebook-free-k16-v1`` with both half tables equal to that
+    table.  The format keeps at least one free row, so row 0 stores its
+    table-decoded words plainly (bit-identical).  U is plain packed signs.
+    ``ceil(overlay_fraction * m)`` uniformly chosen output rows carry an int8
+    residual row (uniform in [-127, 127]) with fp16 row scale 0.002.  Scales
+    ``|N(0,1)| * 0.05 + 0.01`` in fp16, ``scale_mid = 1``.
+    """
+
+    from nanoquant_b200.overlay import OutlierRowOverlay, OverlaidLayerState
+    from nanoquant_b200.product_codebook import (
+        PRODUCT_CODEBOOK_FORMAT_VERSION,
+        ProductCodebookLayerState,
+        pack_product_codebook_indices,
+    )
+
+    words_u = packed_word_count(r)
+    words_v = packed_word_count(n)
+    left = rng.integers(0, 2**32, size=(m, words_u), dtype=np.uint64).astype(np.uint32)
+    if r % 32:
+        left[:, -1] &= np.uint32((1 << (r % 32)) - 1)
+    table = rng.integers(0, 2**16, size=256, dtype=np.uint32).astype(np.uint16)
+    records = rng.integers(0, 256, size=(r, words_v, 2), dtype=np.uint32)
+    if n % 32:  # signs past the last column are zero: the tail word's groups index an all-zero entry
+        raise ValueError("config-4 layers have widths that are multiples of 32")
+    record = records[..., 0] | (records[..., 1] << 8)
+    free = (table[records[:1, :, 0]].astype(np.uint32) | (table[records[:1, :, 1]].astype(np.uint32) << 16))
+    scales = lambda k: torch.from_numpy((np.abs(rng.standard_normal(k)) * 0.05 + 0.01).astype(np.float16))  # noqa
+    spec = QuantizedLinearSpec(name, "nanoquant-v1", n, m, r, "float32", "float16")
+    half = torch.from_numpy(table.view(np.int16).copy())
+    state = ProductCodebookLayerState(
+        spec, PRODUCT_CODEBOOK_FORMAT_VERSION, False, 1,
+        torch.from_numpy(left.view(np.int32).copy()), torch.from_numpy(free.view(np.int32).copy()),
+        pack_product_codebook_indices(torch.from_numpy(record[1:].astype(np.int32))), half, half.clone(),
+        scales(n), torch.ones(r, dtype=torch.float16), scales(m))
+    rows = max(1, -(-int(round(overlay_fraction * m * 1000)) // 1000))
+    ids = np.sort(rng.choice(m, size=rows, replace=False)).astype(np.int32)
+    overlay = OutlierRowOverlay(torch.from_numpy(ids), torch.from_numpy(rng.integers(-127, 128, size=(rows, n),
+                                                                                     dtype=np.int8)),
+                                torch.full((rows,), 0.002, dtype=torch.float16))
+    return OverlaidLayerState(state, overlay)
+
+
+def make_codebook_layers(shape: DecoderShape, *, layers: int | None = None, seed: int = 0) -> list[dict]:
+    """Config-4 layers (product-codebook V, int8 outlier rows) of ``shape``, on the host."""
+
+    rng = np.random.default_rng(seed)
+    result = []
+    for index in range(shape.layers if layers is None else layers):
+        result.append({proj: random_codebook_layer(f"blocks.{index}.{proj}", n, m, shape.rank(n, m), rng)
+                       for proj, (n, m) in shape.projections().items()})
+    return result
+
+
+def codebook_layer_bytes(n: int, m: int, r: int, overlay_rows: int) -> int:
+    """Algorithmic bytes of one config-4 layer: U words, V's 8-bit group indices, the 512-byte table pair, fp16
+    scales and the int8 overlay rows with their fp16 scales and int32 ids."""
+
+    return (4 * m * packed_word_count(r) + r * ((n + 15) // 16) + 512 + 2 * (n + r + m)
+            + overlay_rows * (n + 6))
+
+
 def make_decoder_layers(shape: DecoderShape, device: torch.device, *, layers: int | None = None,
                         seed: int = 0) -> list[dict[str, PackedLayerState]]:
     generator = torch.Generator(device=device).manual_seed(seed)
@@ -132,6 +200,9 @@ class DecodeChain:
         self.engine = engine
         self.backend = CudaPackedSm100Backend()
         self.blocks: list[_PreparedBlock] = []
+        first = blocks[0] if blocks else {}
+        self.codebook_rows = ({proj: int(state.overlay.row_ids.numel()) for proj, state in first.items()}
+                              if first and all(hasattr(state, "overlay") for state in first.values()) else None)
         for block in blocks:
             prepared = {name: self.backend.prepare(state, device) for name, state in block.items()}
             qkv = prepare_sm100_projection_group((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]))
@@ -183,12 +254,19 @@ class DecodeChain:
         return total * len(self.blocks)
 
     def algorithmic_bytes(self) -> int:
-        """Weight bytes plus activation traffic (bf16 in, fp32 out) of one step."""
+        """Weight bytes plus activation traffic (bf16 in, fp32 out) of one step.
+
+        Config-4 layers (product-codebook V with outlier rows) count their
+        compact format: U words, V's group indices, tables, scales and rows.
+        """
 
         total = 0
         for proj, (n, m) in self.shape.projections().items():
             r = self.shape.rank(n, m)
-            total += layer_bytes(n, m, r) + self.tokens * (2 * n + 4 * m)
+            if self.codebook_rows is not None:
+                total += codebook_layer_bytes(n, m, r, self.codebook_rows[proj]) + self.tokens * (2 * n + 4 * m)
+            else:
+                total += layer_bytes(n, m, r) + self.tokens * (2 * n + 4 * m)
         return total * len(self.blocks)
 
     def step(self) -> torch.Tensor:

@@ -359,6 +359,11 @@ class Qwen3DecodeStep:
         self.graph.replay()
         return self.logits
 
+    def program_bytes(self) -> int:
+        """Bytes the fused program must move: everything of the step but the final norm and the lm head."""
+
+        return self.algorithmic_bytes() - self.shell.lm_head.numel() * 2 - self.shape.hidden * 2
+
     def algorithmic_bytes(self) -> int:
         """Bytes one step must move: packed weights and scales, KV rows read, lm head, norms."""
 
