@@ -101,16 +101,9 @@ struct MemberDev {
   int32_t coded_from;         // first coded tile (INT32_MAX: none)
 };
 
-struct OpDev {
-  MemberDev s[2][kMaxMembersTc];  // [stage][member]
-  int32_t count;
-  const void *x;
-  const void *x2;  // NQB_X_SWIGLU / NQB_X_GEGLU: the up projection (x is the gate)
-  int32_t x_dtype;
-  int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
-  int64_t n;
-  int64_t latent_stride;
-  // decoder-step extensions (nqb_program_op_ext)
+// The decoder-step extensions of an op (nqb_program_op_ext), staged into
+// shared memory with the op's other tables.
+struct __align__(8) StepDev {
   int32_t kind;            // NQB_OP_LINEAR / NQB_OP_ATTENTION
   int32_t epilogue;        // NQB_EPI_*
   const float *norm_stats;  // residual-stream input: [stat_tiles][tokens] partial sums of h^2
@@ -126,15 +119,27 @@ struct OpDev {
   int64_t cache_len, position;
   __nv_bfloat16 *attn_out;
   int32_t att_splits;
-  int64_t att_chunk;         // keys per split, a multiple of 16
   int32_t att_ring_blocks;   // at most this many 16-row K/V blocks of a unit arrive through the sign ring
+  int64_t att_chunk;         // keys per split, a multiple of 16
+};
+
+struct OpDev {
+  MemberDev s[2][kMaxMembersTc];  // [stage][member]
+  int32_t count;
+  const void *x;
+  const void *x2;  // NQB_X_SWIGLU / NQB_X_GEGLU: the up projection (x is the gate)
+  int32_t x_dtype;
+  int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
+  int64_t n;
+  int64_t latent_stride;
+  StepDev step;  // decoder-step extensions
 };
 
 // 16-row K and V blocks of attention unit (split sp) that stream through the
 // sign ring: the unit's rows before this step's tokens (they do not change
 // during the program), whole blocks only, at most op.att_ring_blocks.  The
 // host lists the same blocks in the CTA's slice addresses.
-__host__ __device__ inline int att_unit_ring_blocks(const OpDev &op, int sp) {
+__host__ __device__ inline int att_unit_ring_blocks(const StepDev &op, int sp) {
   const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
   const int64_t old_end = op.position < k0 + op.att_chunk ? op.position : k0 + op.att_chunk;
   const int64_t blocks = old_end > k0 ? (old_end - k0) / 16 : 0;
@@ -159,6 +164,7 @@ struct __align__(16) StageInfo {
   int32_t x_dtype;
   int32_t n_items;
   int32_t patch_rows;
+  StepDev step;
   Item items[kMaxStageItems];
 };
 
@@ -397,6 +403,11 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
   const uint32_t *it_src = reinterpret_cast<const uint32_t *>(p.items + ib);
   uint32_t *it_dst = reinterpret_cast<uint32_t *>(&info.items[0]);
   for (int i = lane; i < n_items * 2; i += 32) it_dst[i] = it_src[i];
+  {
+    const uint32_t *sd_src = reinterpret_cast<const uint32_t *>(&op.step);
+    uint32_t *sd_dst = reinterpret_cast<uint32_t *>(&info.step);
+    for (int i = lane; i < static_cast<int>(sizeof(StepDev) / 4); i += 32) sd_dst[i] = sd_src[i];
+  }
   if (lane == 0) {
     info.x = op.x;
     info.x2 = op.x2;
@@ -617,7 +628,7 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // come from shared memory; the remaining rows (this step's, and any past the
 // ring's share) are read from global memory.  Every consumer warp waits for
 // the unit's ring slots first and hands them back after the last token.
-__device__ __noinline__ void attention_partials(const Params &p, const OpDev &op, float *scratch,
+__device__ __noinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
                                                 const uint8_t *ring, uint64_t *s_full, uint64_t *s_empty,
                                                 int &slot, uint32_t &phase, bool &ok) {
   const int T = p.tokens;
@@ -765,7 +776,7 @@ __device__ __noinline__ void attention_partials(const Params &p, const OpDev &op
 
 // Joins the splits' partials of every (token, q head) in split order, one
 // warp per row (lane: 4 dims), and writes the bf16 attention output.
-__device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
+__device__ __noinline__ void attention_join(const Params &p, const StepDev &op) {
   const int rows = p.tokens * op.q_heads;
   const int lane = threadIdx.x & 31;
   const int stride = static_cast<int>(gridDim.x) * mmad::kWarps;
@@ -773,6 +784,12 @@ __device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
     const float *base = p.att_part + static_cast<int64_t>(r) * op.att_splits * kAttRow;
     const float m0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd) : -INFINITY;
     const float l0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd + 1) : 0.0f;
+    // the splits' vectors, kJoin at a time, all in flight together (issued before the weights are known)
+    constexpr int kJoin = 16;
+    float4 v[kJoin];
+#pragma unroll
+    for (int u = 0; u < kJoin; ++u)
+      v[u] = __ldcg(reinterpret_cast<const float4 *>(base + min(u, op.att_splits - 1) * kAttRow + lane * 4));
     float mx = m0;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -781,13 +798,23 @@ __device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
     float num[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int sidx = 0; sidx < op.att_splits; ++sidx) {
-      const float f = __shfl_sync(0xffffffffu, f0, sidx);
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(base + sidx * kAttRow + lane * 4));
-      num[0] += f * v.x;
-      num[1] += f * v.y;
-      num[2] += f * v.z;
-      num[3] += f * v.w;
+    for (int s0 = 0; s0 < op.att_splits; s0 += kJoin) {
+      if (s0 > 0) {
+#pragma unroll
+        for (int u = 0; u < kJoin; ++u)
+          v[u] = __ldcg(
+              reinterpret_cast<const float4 *>(base + min(s0 + u, op.att_splits - 1) * kAttRow + lane * 4));
+      }
+#pragma unroll
+      for (int u = 0; u < kJoin; ++u) {
+        const float f = __shfl_sync(0xffffffffu, f0, (s0 + u) & 31);
+        if (s0 + u < op.att_splits) {
+          num[0] += f * v[u].x;
+          num[1] += f * v[u].y;
+          num[2] += f * v[u].z;
+          num[3] += f * v[u].w;
+        }
+      }
     }
     const float inv = den > 0.0f ? 1.0f / den : 0.0f;
     __nv_bfloat16 *o = op.attn_out + static_cast<int64_t>(r) * kAttHd + lane * 4;
@@ -799,7 +826,7 @@ __device__ __noinline__ void attention_join(const Params &p, const OpDev &op) {
 // NQB_EPI_RESIDUAL for one tile (the 128 leader threads): h += out, and the
 // tile's sums of squares of the new h per token to out_stats.
 template <int kT>
-__device__ __forceinline__ void residual_epilogue(const OpDev &op, const MemberDev &md, int tile, const float (&outv)[kT],
+__device__ __forceinline__ void residual_epilogue(const StepDev &op, const MemberDev &md, int tile, const float (&outv)[kT],
                                                   const float (&hprev)[kT], int T, float *red) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t row = static_cast<int64_t>(tile) * kTileRows + tid;
@@ -827,7 +854,7 @@ __device__ __forceinline__ void residual_epilogue(const OpDev &op, const MemberD
 // q and k heads get RMSNorm and rotate-half RoPE, v heads are copied; all go
 // out as bf16 (q to op.q, k and v to the caches at row position + t).
 template <int kT>
-__device__ __forceinline__ void qk_rope_epilogue(const OpDev &op, int member, int tile, const float (&outv)[kT], int T,
+__device__ __forceinline__ void qk_rope_epilogue(const StepDev &op, int member, int tile, const float (&outv)[kT], int T,
                                                  float *xs, float *red) {
   const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
   if (member == 2) {
@@ -1025,7 +1052,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
       const int ib = 0;
       const int ie = op.n_items;
       NQB_TRACE_BEGIN
-      const OpDev &gop = p.ops[g >> 1];  // the op's decoder-step fields (read-only, global)
+      const StepDev &gop = op.step;  // the op's decoder-step fields (staged in shared memory)
       int op_kind = NQB_OP_LINEAR, op_epi = NQB_EPI_STORE;
       bool normed = false;
       float rms_part[kT];  // residual-stream input: warp 0's partial sums of h^2 (lane: tiles lane, lane + 32, ..)
@@ -1823,28 +1850,28 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     OpDev &od = opdev[i];
     std::memset(&od, 0, sizeof(od));
     const nqb_program_op_ext *e = o.ext;
-    od.kind = e != nullptr ? e->kind : NQB_OP_LINEAR;
+    od.step.kind = e != nullptr ? e->kind : NQB_OP_LINEAR;
     if (e != nullptr) {
-      od.epilogue = e->epilogue;
-      od.eps = e->eps;
-      od.out_stats = e->out_stats;
-      od.q_heads = e->q_heads;
-      od.kv_heads = e->kv_heads;
-      od.cos_t = e->cos_table;
-      od.sin_t = e->sin_table;
-      od.q = static_cast<__nv_bfloat16 *>(e->q);
-      od.k_cache = static_cast<__nv_bfloat16 *>(e->k_cache);
-      od.v_cache = static_cast<__nv_bfloat16 *>(e->v_cache);
-      od.cache_len = e->cache_len;
-      od.position = e->position;
-      od.attn_out = static_cast<__nv_bfloat16 *>(e->attn_out);
-      od.q_norm = f32(op_scales[i].q_norm);
-      od.k_norm = f32(op_scales[i].k_norm);
+      od.step.epilogue = e->epilogue;
+      od.step.eps = e->eps;
+      od.step.out_stats = e->out_stats;
+      od.step.q_heads = e->q_heads;
+      od.step.kv_heads = e->kv_heads;
+      od.step.cos_t = e->cos_table;
+      od.step.sin_t = e->sin_table;
+      od.step.q = static_cast<__nv_bfloat16 *>(e->q);
+      od.step.k_cache = static_cast<__nv_bfloat16 *>(e->k_cache);
+      od.step.v_cache = static_cast<__nv_bfloat16 *>(e->v_cache);
+      od.step.cache_len = e->cache_len;
+      od.step.position = e->position;
+      od.step.attn_out = static_cast<__nv_bfloat16 *>(e->attn_out);
+      od.step.q_norm = f32(op_scales[i].q_norm);
+      od.step.k_norm = f32(op_scales[i].k_norm);
       if (e->kind == NQB_OP_ATTENTION) continue;  // no members; the splits are set once the grid is known
       if (e->norm_stats != nullptr) {
-        od.norm_stats = e->norm_stats;
-        od.stat_tiles = static_cast<int32_t>((o.layers[0].in_features + kTileRows - 1) / kTileRows);
-        od.inv_n = 1.0f / static_cast<float>(o.layers[0].in_features);
+        od.step.norm_stats = e->norm_stats;
+        od.step.stat_tiles = static_cast<int32_t>((o.layers[0].in_features + kTileRows - 1) / kTileRows);
+        od.step.inv_n = 1.0f / static_cast<float>(o.layers[0].in_features);
       }
     }
     od.count = o.count;
@@ -1904,14 +1931,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   size_t att_floats = 0;
   for (int i = 0; i < op_count; ++i) {
     OpDev &od = opdev[i];
-    if (od.kind != NQB_OP_ATTENTION) continue;
-    const int want = std::max(1, std::min(32, ctas / od.kv_heads));
-    const int64_t most = od.position + tokens;  // keys the last token sees
-    od.att_chunk = ((most + want - 1) / want + 15) / 16 * 16;
-    od.att_splits = static_cast<int32_t>((most + od.att_chunk - 1) / od.att_chunk);
+    if (od.step.kind != NQB_OP_ATTENTION) continue;
+    const int want = std::max(1, std::min(32, ctas / od.step.kv_heads));
+    const int64_t most = od.step.position + tokens;  // keys the last token sees
+    od.step.att_chunk = ((most + want - 1) / want + 15) / 16 * 16;
+    od.step.att_splits = static_cast<int32_t>((most + od.step.att_chunk - 1) / od.step.att_chunk);
     // K and V blocks of a unit must fit the ring at once (the consumers hold them all)
-    od.att_ring_blocks = std::max(0, sp.ring / 2 - 1);
-    att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.q_heads * od.att_splits * kAttRow);
+    od.step.att_ring_blocks = std::max(0, sp.ring / 2 - 1);
+    att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.step.q_heads * od.step.att_splits * kAttRow);
   }
 
   // tiles per (stage, cluster), then every CTA's slice addresses in consumption order
@@ -1940,20 +1967,20 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   for (int g = 0; g < stages; ++g) {
     const OpDev &op = opdev[g >> 1];
     const int st = g & 1;
-    if (op.kind == NQB_OP_ATTENTION && st == 0) {
+    if (op.step.kind == NQB_OP_ATTENTION && st == 0) {
       // each CTA's unit (kv head, key split): its K and V rows go on the L2
       // prefetch list of the stage two ahead of this one (the rows before this
       // step's tokens do not change during the program)
       const int target = std::max(0, g - 2);
-      for (int c = 0; c < ctas && c < op.kv_heads * op.att_splits; ++c) {
-        const int kvh = c / op.att_splits, spl = c % op.att_splits;
-        const int64_t k0 = static_cast<int64_t>(spl) * op.att_chunk;
-        const int64_t k1 = std::min(k0 + op.att_chunk, op.position + tokens);
+      for (int c = 0; c < ctas && c < op.step.kv_heads * op.step.att_splits; ++c) {
+        const int kvh = c / op.step.att_splits, spl = c % op.step.att_splits;
+        const int64_t k0 = static_cast<int64_t>(spl) * op.step.att_chunk;
+        const int64_t k1 = std::min(k0 + op.step.att_chunk, op.step.position + tokens);
         if (k1 <= k0) continue;
-        const int64_t off = (static_cast<int64_t>(kvh) * op.cache_len + k0) * kAttHd;
+        const int64_t off = (static_cast<int64_t>(kvh) * op.step.cache_len + k0) * kAttHd;
         std::vector<uint64_t> &lines = pf[static_cast<size_t>(target) * ctas + c];
-        add_lines(lines, op.k_cache + off, (k1 - k0) * kAttHd * 2);
-        add_lines(lines, op.v_cache + off, (k1 - k0) * kAttHd * 2);
+        add_lines(lines, op.step.k_cache + off, (k1 - k0) * kAttHd * 2);
+        add_lines(lines, op.step.v_cache + off, (k1 - k0) * kAttHd * 2);
       }
     }
     assign_stage(op, st, clusters, per_cluster);
@@ -1997,16 +2024,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
           }
         }
         std::vector<uint64_t> &addrs = lists[c * kClusterSize + q];
-        if (op.kind == NQB_OP_ATTENTION && st == 0) {
+        if (op.step.kind == NQB_OP_ATTENTION && st == 0) {
           // this CTA's attention unit: its old K and V rows as 16-row blocks (4 KB each, K then V)
           const int cta_id = c * kClusterSize + q;
-          if (cta_id < op.kv_heads * op.att_splits) {
-            const int kvh = cta_id / op.att_splits, spl = cta_id % op.att_splits;
-            const int nb = att_unit_ring_blocks(op, spl);
+          if (cta_id < op.step.kv_heads * op.step.att_splits) {
+            const int kvh = cta_id / op.step.att_splits, spl = cta_id % op.step.att_splits;
+            const int nb = att_unit_ring_blocks(op.step, spl);
             for (int b = 0; b < nb; ++b) {
-              const int64_t row = static_cast<int64_t>(kvh) * op.cache_len + static_cast<int64_t>(spl) * op.att_chunk + 16 * b;
-              addrs.push_back(reinterpret_cast<uint64_t>(op.k_cache + row * kAttHd));
-              addrs.push_back(reinterpret_cast<uint64_t>(op.v_cache + row * kAttHd));
+              const int64_t row = static_cast<int64_t>(kvh) * op.step.cache_len + static_cast<int64_t>(spl) * op.step.att_chunk + 16 * b;
+              addrs.push_back(reinterpret_cast<uint64_t>(op.step.k_cache + row * kAttHd));
+              addrs.push_back(reinterpret_cast<uint64_t>(op.step.v_cache + row * kAttHd));
             }
           }
         }
