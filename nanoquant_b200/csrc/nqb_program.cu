@@ -226,6 +226,7 @@ __device__ long long g_trace[kTraceMaxCtas][kTraceMaxStages][kTracePhases];
     trace_c[phase] += now - trace_t; \
     trace_t = now;                   \
   } while (0)
+#define NQB_TRACE_RESET() trace_t = clock64()
 #define NQB_TRACE_FLUSH(stage)                                                                 \
   do {                                                                                         \
     if (threadIdx.x == 0 && blockIdx.x < kTraceMaxCtas && (stage) < kTraceMaxStages)           \
@@ -239,6 +240,9 @@ __device__ long long g_trace[kTraceMaxCtas][kTraceMaxStages][kTracePhases];
   } while (0)
 #define NQB_TRACE_FLUSH(stage) \
   do {                         \
+  } while (0)
+#define NQB_TRACE_RESET() \
+  do {                    \
   } while (0)
 #endif
 
@@ -630,7 +634,23 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // the unit's ring slots first and hands them back after the last token.
 __device__ __noinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
                                                 const uint8_t *ring, uint64_t *s_full, uint64_t *s_empty,
-                                                int &slot, uint32_t &phase, bool &ok) {
+                                                int &slot, uint32_t &phase, bool &ok, long long *trace) {
+#ifdef NQB_PHASE_TRACE
+  // trace build: ring waits -> wait-signs, q loads and the key loop -> mma, the
+  // warps' join and the partial stores -> drain (consumer thread 0's cycles)
+  long long tr_t = clock64();
+#define NQB_ATT_TRACE(phase)                         \
+  do {                                               \
+    const long long tr_now = clock64();              \
+    if (trace != nullptr) trace[phase] += tr_now - tr_t; \
+    tr_t = tr_now;                                   \
+  } while (0)
+#else
+  (void)trace;
+#define NQB_ATT_TRACE(phase) \
+  do {                       \
+  } while (0)
+#endif
   const int T = p.tokens;
   const int units = op.kv_heads * op.att_splits;
   const int cta = static_cast<int>(blockIdx.x);
@@ -644,6 +664,7 @@ __device__ __noinline__ void attention_partials(const Params &p, const StepDev &
     const uint32_t ph = phase + static_cast<uint32_t>((slot + j) / R);
     if (!wait_local(&s_full[sj], ph & 1)) ok = false;
   }
+  NQB_ATT_TRACE(kTraceWaitSigns);
   const int64_t ring_rows = 16 * static_cast<int64_t>(nb);
   const float scale = rsqrtf(static_cast<float>(kAttHd));
   const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
@@ -730,6 +751,7 @@ __device__ __noinline__ void attention_partials(const Params &p, const StepDev &
         }
       }
     }
+    NQB_ATT_TRACE(kTraceMma);
     // the warps' partials -> shared memory [warp][head][kAttRow]
 #pragma unroll
     for (int h = 0; h < kAttGroup; ++h) {
@@ -766,7 +788,9 @@ __device__ __noinline__ void attention_partials(const Params &p, const StepDev &
       }
     }
     mmad::consumer_sync();  // the scratch is reused by the next token
+    NQB_ATT_TRACE(kTraceDrain);
   }
+#undef NQB_ATT_TRACE
   // every warp is done with the unit's ring blocks: hand them back
   if (lane == 0)
     for (int j = 0; j < 2 * nb; ++j) mbar_arrive_cta(&s_empty[(slot + j) % R]);
@@ -1066,11 +1090,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         if (op_kind == NQB_OP_ATTENTION) {
           // split-K partials over the CTAs (stage 1 of the op), then their join;
           // the CTA's exchange buffers are idle during these stages
+          NQB_TRACE(kTraceTables);
           if (st == 0)
-            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok);
+#ifdef NQB_PHASE_TRACE
+            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, tid == 0 ? trace_c : nullptr);
+#else
+            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, nullptr);
+#endif
           else
             attention_join(p, gop);
-          NQB_TRACE(kTraceMma);
+          if (st == 0) {
+            NQB_TRACE_RESET();  // attention_partials added its own phases
+          } else {
+            NQB_TRACE(kTraceMma);
+          }
         } else if (normed) {
           // h's per-tile sums of squares (written before this stage): warp 0
           // issues the loads now and reduces them while the quarters land
