@@ -14,9 +14,13 @@
 //   (a2/a3): bytes bit * 2^j of columns 32*word + 8b + j + 4h.  Each j has its
 //   own accumulator; the drain adds D_j >> j (exact).
 // * B (32 K x 8 columns): the activations of a K chunk quantised per token to
-//   22-bit fixed point, three signed base-256 digits per token, so column
-//   n = 3t + d; stored in shared memory as ready fragments (one 64-bit load per
-//   lane and MMA).
+//   fixed point, D signed base-256 digits per token, so column n = D t + d;
+//   stored in shared memory as ready fragments (one 64-bit load per lane and
+//   MMA).  Up to 2 tokens D = 3 (22-bit: the columns fit one 8-column N tile
+//   anyway); from 3 tokens (the 4-token instance) on D = 2 (14-bit), which
+//   takes the N tiles, and so the MMAs, from 2 to 1 at 4 tokens, 3 to 2 at 8
+//   and 6 to 4 at 16.  Error of the 14-bit form: about 1e-4 of max|y| per
+//   stage (measured against a float64 oracle), inside the 2e-3 bound.
 // * sum_k sign_k q_k = Q - 2 * sum_k bit_k q_k, Q = sum_k q_k per token.
 #pragma once
 
@@ -34,7 +38,29 @@ constexpr int kSliceBytes = 4096;         // 128 rows x 8 words
 constexpr uint32_t kFragBytes = 256;      // one (K block, N tile) B fragment block: 32 lanes x 8 bytes
 constexpr int kMaxSliceQuant = 16;        // slices quantised at once
 
-__host__ __device__ constexpr int n_tiles(int tokens) { return (3 * tokens + 7) / 8; }
+// Digits per token and fixed-point bits of the instance for `tokens` (a token bucket: 1, 2, 4, 8 or 16).
+__host__ __device__ constexpr int digits_for(int tokens) { return tokens >= 4 ? 2 : 3; }
+__host__ __device__ constexpr int fixed_bits(int tokens) { return tokens >= 4 ? 14 : 22; }
+
+__host__ __device__ constexpr int n_tiles(int tokens) { return (digits_for(tokens) * tokens + 7) / 8; }
+
+// q (|q| < 2^(8 kD - 2)) as kD signed base-256 digits, byte b of w[d] from q[b].
+template <int kD>
+__device__ __forceinline__ void split_digits_n(const int32_t (&q)[4], uint32_t (&w)[kD]) {
+#pragma unroll
+  for (int d = 0; d < kD; ++d) w[d] = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    int32_t v = q[b];
+#pragma unroll
+    for (int d = 0; d < kD - 1; ++d) {
+      const int32_t dk = static_cast<int8_t>(v & 0xFF);
+      v = (v - dk) >> 8;
+      w[d] |= (static_cast<uint32_t>(dk) & 0xFFu) << (8 * b);
+    }
+    w[kD - 1] |= (static_cast<uint32_t>(v) & 0xFFu) << (8 * b);
+  }
+}
 
 // B-fragment bytes of one slice for kNT N tiles.
 __host__ __device__ constexpr uint32_t slice_frag_bytes(int nt) { return 8u * nt * kFragBytes; }
@@ -194,7 +220,7 @@ __device__ __forceinline__ void quantize_loaded(const ChunkValues<kT, kQPT> &cv,
     int ex = 0, et = 0;
     if (m > 0.0f && isfinite(m)) {
       frexpf(m, &ex);  // m < 2^ex
-      et = min(22 - ex, 126);
+      et = min(fixed_bits(kT) - ex, 126);
     }
     e[t] = et;
     qs[t] = 0;
@@ -217,11 +243,12 @@ __device__ __forceinline__ void quantize_loaded(const ChunkValues<kT, kQPT> &cv,
             q[b] = __float2int_rn(v[i][b][t] * scale);
             qs[t] += q[b];
           }
-          uint32_t digits[tc::kDigits];
-          tc::split_digits(q, digits);
+          constexpr int kD = digits_for(kT);
+          uint32_t digits[kD];
+          split_digits_n<kD>(q, digits);
 #pragma unroll
-          for (int d = 0; d < tc::kDigits; ++d) {
-            const int n = 3 * t + d;
+          for (int d = 0; d < kD; ++d) {
+            const int n = kD * t + d;
             const int nt = n >> 3, gg = n & 7;
             const uint32_t offset =
                 ((static_cast<uint32_t>(sl) * 8 + kb) * kNT + nt) * kFragBytes + (gg * 4 + tig) * 8 + hi * 4;
@@ -322,23 +349,26 @@ __device__ __forceinline__ void drain_to_acc(int32_t (&d)[acc_sets(n_tiles(kT))]
       v[nt][c] = x;
     }
   const int r0 = warp * 16 + g;
+  constexpr int kD = digits_for(kT);
 #pragma unroll
   for (int t = 0; t < kT; ++t) {
-    // digit dd of token t sits in column 3t + dd: N tile (3t+dd)/8, lane tig ((3t+dd)%8)/2, register (3t+dd)%2
-    int32_t dig[2][3];
+    // digit dd of token t sits in column kD t + dd: N tile (kD t+dd)/8, lane tig ((kD t+dd)%8)/2, register (..)%2
+    int32_t dig[2][kD];
 #pragma unroll
-    for (int dd = 0; dd < 3; ++dd) {
-      const int n = 3 * t + dd;
+    for (int dd = 0; dd < kD; ++dd) {
+      const int n = kD * t + dd;
       const int nt = n >> 3, cc = n & 7;
       const int src = g * 4 + (cc >> 1);
       dig[0][dd] = __shfl_sync(0xffffffffu, v[nt][cc & 1], src);
       dig[1][dd] = __shfl_sync(0xffffffffu, v[nt][2 + (cc & 1)], src);
     }
-    if (t < T && tig == ((3 * t) & 7) >> 1) {
+    if (t < T && tig == ((kD * t) & 7) >> 1) {
       const float unscale = tc::exp2_int(-e[t]);
 #pragma unroll
       for (int rr = 0; rr < 2; ++rr) {
-        const long long s = static_cast<long long>(dig[rr][0]) + 256ll * dig[rr][1] + 65536ll * dig[rr][2];
+        long long s = 0;
+#pragma unroll
+        for (int dd = kD - 1; dd >= 0; --dd) s = s * 256 + dig[rr][dd];
         acc[t * kTileRows + r0 + rr * 8] += __ll2float_rn(Q[t] - 2 * s) * unscale;
       }
     }

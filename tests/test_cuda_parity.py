@@ -34,6 +34,19 @@ from tests.fixtures import as_numpy_f32, linear_names, load
 pytestmark = pytest.mark.gpu
 
 RTOL, ATOL = 2e-5, 2e-4
+# Persistent decode programs quantise activations to 22-bit fixed point up to
+# 2 tokens and to 14-bit from 3 tokens on (two int8 digits per token: fewer
+# MMAs); the 14-bit outputs are bounded by 1e-3 of max|y|, inside the
+# operator's 2e-3 bound (and measured near 1e-4).
+PROGRAM_WIDE_BOUND = 1e-3
+
+
+def program_tolerance(tokens: int, scale: float) -> tuple[float, float]:
+    """(rtol, atol) for a program output of `tokens` tokens whose reference has max|y| = scale."""
+
+    if tokens >= 3:
+        return 0.0, PROGRAM_WIDE_BOUND * scale
+    return RTOL, max(ATOL, 1e-5 * scale)
 
 
 @pytest.fixture(scope="module", autouse=True)

@@ -128,7 +128,7 @@ def test_gated_gelu_program_input_matches_oracle(tokens: int) -> None:
     act = do.gelu_tanh(gate.cpu().numpy()) * up.cpu().numpy()
     ref = po.packed_linear(act, oracle_from_state(down_state), accumulate="float64")
     err = float(np.abs(out.cpu().numpy() - ref).max() / np.abs(ref).max())
-    assert err <= 2e-5, err
+    assert err <= (2e-5 if tokens < 3 else 1e-3), err  # programs: 14-bit activations from 3 tokens on
 
 
 def _host_state(state):

@@ -22,7 +22,7 @@ from nanoquant_b200 import CudaPackedSm100Backend
 from nanoquant_b200.mixed_v import MixedVLayerState, mixed_v_correction_pair_table
 from nanoquant_b200.program import DecodeProgram, ProgramOp
 from oracle import packed_oracle as po
-from tests.test_cuda_parity import ATOL, RTOL, ctypes_status, oracle_from_state
+from tests.test_cuda_parity import ATOL, RTOL, ctypes_status, oracle_from_state, program_tolerance
 from tests.test_mixed_v import mixed_v_state
 
 pytestmark = pytest.mark.gpu
@@ -82,8 +82,8 @@ def _check(got: torch.Tensor, x: torch.Tensor, state) -> None:
     if isinstance(state, MixedVLayerState):
         state = state.to_packed()
     expected = po.packed_linear(x.float().cpu().numpy(), oracle_from_state(state), accumulate="float64")
-    scale = float(np.abs(expected).max())
-    np.testing.assert_allclose(got.cpu().numpy(), expected, rtol=RTOL, atol=max(ATOL, 1e-5 * scale))
+    rtol, atol = program_tolerance(x.numel() // x.shape[-1], float(np.abs(expected).max()))
+    np.testing.assert_allclose(got.cpu().numpy(), expected, rtol=rtol, atol=atol)
 
 
 @pytest.mark.parametrize("tokens", (1, 5, 16))
