@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "nqb.h"
@@ -542,6 +543,89 @@ __global__ void __launch_bounds__(256) gemv_bf16_kernel(const __nv_bfloat16 *w, 
   }
 }
 
+// out[t][r] = sum_c W[r][c] x[t][c] for 2 .. 8 * kNT tokens on the tensor
+// cores: mma.sync m16n8k16 bf16 with fp32 accumulation, A = a 16-row tile of W,
+// B = the tokens (kNT tiles of 8).  One warp per 16-row tile, tiles strided
+// over the grid's warps.  K goes in 32-column blocks; lane (g, q) = (lane / 4,
+// lane % 4) loads W[row g][8q .. 8q + 7] and W[row g + 8][8q .. 8q + 7] as
+// 16-byte streaming loads (kU blocks in flight) and x[token][8q .. 8q + 7]
+// from shared memory, and uses the eight values as its fragment elements of
+// two 16-wide k-steps: columns 8q + {0,1}, 8q + {2,3} for the first and
+// 8q + {4,5}, 8q + {6,7} for the second.  That is a permutation of K applied
+// to A and B alike, so the sums are unchanged and every load is one
+// contiguous vector.  x rows in shared memory are padded by 16 bytes, which
+// spreads a fragment load's 32 lanes over the banks (4 wavefronts for 512 B).
+template <int kNT>
+__global__ void __launch_bounds__(256) gemv_bf16_mma_kernel(const __nv_bfloat16 *w, const __nv_bfloat16 *x,
+                                                            int64_t rows, int64_t cols, int tokens, float *out,
+                                                            int64_t out_stride) {
+  constexpr int kU = 8;  // 32-column blocks of W in flight per lane
+  extern __shared__ uint4 xs_units[];  // [kNT * 8][cols / 8 + 1] (16-byte units, one unit of padding per row)
+  allow_dependents();
+  const int64_t units = cols / 8;
+  const int64_t stride = units + 1;
+  for (int64_t i = threadIdx.x; i < kNT * 8 * units; i += blockDim.x) {
+    const int64_t t = i / units, u = i - t * units;
+    xs_units[t * stride + u] =
+        t < tokens ? __ldg(reinterpret_cast<const uint4 *>(x + t * cols) + u) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t blocks = cols / 32;
+  for (int64_t tile = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); tile * 16 < rows;
+       tile += warps) {
+    const int64_t r0 = tile * 16 + g, r1 = r0 + 8;
+    const uint4 *wa = reinterpret_cast<const uint4 *>(w + min(r0, rows - 1) * cols) + q;
+    const uint4 *wb = reinterpret_cast<const uint4 *>(w + min(r1, rows - 1) * cols) + q;
+    float acc[kNT][4];
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+    for (int64_t b0 = 0; b0 < blocks; b0 += kU) {
+      uint4 a0[kU], a1[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t b = min(b0 + u, blocks - 1);  // past the row's end: re-read its last block (unused)
+        a0[u] = __ldcs(wa + 4 * b);
+        a1[u] = __ldcs(wb + 4 * b);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (b0 + u >= blocks) break;
+#pragma unroll
+        for (int nt = 0; nt < kNT; ++nt) {
+          const uint4 bx = xs_units[static_cast<int64_t>(nt * 8 + g) * stride + 4 * (b0 + u) + q];
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(acc[nt][0]), "+f"(acc[nt][1]), "+f"(acc[nt][2]), "+f"(acc[nt][3])
+              : "r"(a0[u].x), "r"(a1[u].x), "r"(a0[u].y), "r"(a1[u].y), "r"(bx.x), "r"(bx.y));
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(acc[nt][0]), "+f"(acc[nt][1]), "+f"(acc[nt][2]), "+f"(acc[nt][3])
+              : "r"(a0[u].z), "r"(a1[u].z), "r"(a0[u].w), "r"(a1[u].w), "r"(bx.z), "r"(bx.w));
+        }
+      }
+    }
+    // D: c0, c1 = rows g, columns (tokens) 2q, 2q + 1; c2, c3 = row g + 8
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt) {
+      const int t0 = nt * 8 + 2 * q;
+      if (r0 < rows) {
+        if (t0 < tokens) out[t0 * out_stride + r0] = acc[nt][0];
+        if (t0 + 1 < tokens) out[(t0 + 1) * out_stride + r0] = acc[nt][1];
+      }
+      if (r1 < rows) {
+        if (t0 < tokens) out[t0 * out_stride + r1] = acc[nt][2];
+        if (t0 + 1 < tokens) out[(t0 + 1) * out_stride + r1] = acc[nt][3];
+      }
+    }
+  }
+}
+
 // Splits of the attention: 64 keys each (eight blocks of eight per warp), at
 // most 64.  (32-key splits measured slower: the combine over twice as many
 // partials costs more than the shorter key loop saves.)
@@ -733,6 +817,27 @@ int nqb_gemv_bf16(const void *weight, int64_t rows, int64_t cols, const void *x,
   const unsigned grid = static_cast<unsigned>(shell::launch_sm_count() * 8);
   auto *w = static_cast<const __nv_bfloat16 *>(weight);
   auto *xp = static_cast<const __nv_bfloat16 *>(x);
+  // 2..16 tokens: tensor-core tiles of 8 tokens (16-byte aligned x, columns a multiple of 32)
+  if (tokens >= 2 && cols % 32 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0) {
+    for (int64_t t0 = 0; t0 < tokens; t0 += 16) {
+      const int n = static_cast<int>(std::min<int64_t>(16, tokens - t0));
+      const int tiles = n > 8 ? 2 : 1;
+      const size_t smem = static_cast<size_t>(tiles) * 8 * (cols / 8 + 1) * 16;
+      if (smem > 200 * 1024) break;  // too long a row for shared memory: the CUDA-core kernels below
+      const void *fn = tiles == 2 ? reinterpret_cast<const void *>(shell::gemv_bf16_mma_kernel<2>)
+                                  : reinterpret_cast<const void *>(shell::gemv_bf16_mma_kernel<1>);
+      NQB_CHECK(ensure_dynamic_smem(fn, smem));
+      const unsigned mma_grid = static_cast<unsigned>(shell::launch_sm_count() * (tiles == 2 ? 1 : 2));
+      if (tiles == 2)
+        shell::gemv_bf16_mma_kernel<2><<<mma_grid, 256, smem, s>>>(w, xp + t0 * cols, rows, cols, n, out + t0 * rows,
+                                                                    rows);
+      else
+        shell::gemv_bf16_mma_kernel<1><<<mma_grid, 256, smem, s>>>(w, xp + t0 * cols, rows, cols, n, out + t0 * rows,
+                                                                    rows);
+      NQB_CUDA(cudaGetLastError(), "gemv launch");
+      if (t0 + n == tokens) return ok();
+    }
+  }
   for (int64_t t0 = 0; t0 < tokens;) {
     const int64_t left = tokens - t0;
     const int group = left >= 8 && cols * 8 * 4 <= 200 * 1024   ? 8

@@ -149,6 +149,25 @@ def test_silu_mul_and_gemv_kernels(tokens: int) -> None:
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize(("tokens", "cols"), ((2, 4096), (8, 4096), (9, 4096), (16, 4096), (19, 4096), (5, 1000),
+                                              (16, 2048)))
+def test_gemv_tensor_core_tiles(tokens: int, cols: int) -> None:
+    """2..16 tokens per launch take the mma.sync kernel (columns a multiple of 32), other widths the CUDA cores;
+    more than 16 tokens run in chunks.  Rows past a 16-row tile and tokens past an 8-token tile are masked."""
+
+    from nanoquant_b200.decoder import gemv_bf16
+
+    dev = _gpu()
+    g = torch.Generator(device=dev).manual_seed(tokens * cols)
+    w = (0.02 * torch.randn(2053, cols, generator=g, device=dev)).bfloat16()
+    x = torch.randn(tokens, cols, generator=g, device=dev).bfloat16()
+    out = torch.full((tokens, 2053), 7.0, device=dev)
+    gemv_bf16(w, x, out)
+    ref = (x.double() @ w.double().T).float()
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+
+
 def _tiny_shape():
     from nanoquant_b200.decode_chain import DecoderShape
 
