@@ -54,6 +54,7 @@ METRIC = "decode tok/s (bs1, Qwen3-8B shape ~1 bpw); packed-GEMV HBM GB/s vs pea
 UNIT = "tok/s"
 STEP_VOCAB, STEP_POSITION = 151936, 2048
 GEMMA_POSITION = 1024
+STACKED_LAYERS = 1024  # config-0 layers in the stacked workload's program
 PREFILL_TOKENS = 8 * 4096
 
 
@@ -261,8 +262,12 @@ def cpu_codebook_baseline(tokens: int, sample_layers: int = 2, repeats: int = 3)
                       f"host threads ({_cpu_model()}); scaled to 26 layers"}
 
 
-def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200) -> dict:
-    """The oracle port of ``PackedReferenceBackend.linear`` on one config-0 layer."""
+def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200, layers: int = 1) -> dict:
+    """The oracle port of ``PackedReferenceBackend.linear`` on one config-0 layer.
+
+    ``layers`` > 1 states the rate for a step through that many such layers
+    (the stacked workload): the per-call time of one layer times ``layers``.
+    """
 
     import numpy as np
 
@@ -287,10 +292,11 @@ def cpu_linear_baseline(n: int, m: int, r: int, tokens: int, repeats: int = 200)
         po.packed_linear(x, layer)
     per = (time.perf_counter() - start) / repeats
     threads = _cpu_threads()
-    return {"value": tokens / per, "unit": UNIT, "cores": threads, "kind": "port", "ms_per_step": per * 1e3,
-            "cpu_model": _cpu_model(),
+    scaled = f"; scaled to a step through {layers} layers" if layers > 1 else ""
+    return {"value": tokens / (per * layers), "unit": UNIT, "cores": threads, "kind": "port",
+            "ms_per_step": per * layers * 1e3, "cpu_model": _cpu_model(),
             "sample": f"one {n}->{m} r{r} layer, {tokens} token(s), {repeats} calls of the oracle port of "
-                      f"PackedReferenceBackend.linear (fp32) on {threads} host threads ({_cpu_model()})"}
+                      f"PackedReferenceBackend.linear (fp32) on {threads} host threads ({_cpu_model()}){scaled}"}
 
 
 def cpu_prefill_baseline(tokens: int = 128) -> dict:
@@ -515,7 +521,10 @@ class StackedLinearRunner:
         self.input = torch.randn(tokens, n, generator=g, device=device).bfloat16()
         self.layers_prepared = [backend.prepare(random_packed_layer(f"stack.{i}.up_proj", n, m, r, g, device), device)
                                 for i in range(count)]
-        self.program = DecodeProgram([ProgramOp((layer,), self.input) for layer in self.layers_prepared])
+        # the layers share their input: three per program op (one grouped projection)
+        group = 3
+        self.program = DecodeProgram([ProgramOp(tuple(self.layers_prepared[i:i + group]), self.input)
+                                      for i in range(0, count, group)])
         self.tokens = tokens
         self.layers = count
         self.launches_per_step = 1
@@ -581,8 +590,8 @@ WORKLOADS = {
     "single-linear-stacked": {"kind": "stacked",
                               "metric": "stacked packed linears tok/s (1024 x 2048x640 r480); HBM GB/s",
                               "tokens": 1,
-                              "description": "1024 independent 640->2048 rank-480 layers (config 0) in one program, "
-                                             "{tokens} token(s)",
+                              "description": "1024 independent 640->2048 rank-480 layers (config 0) on one input "
+                                             "in one program, three per op, {tokens} token(s)",
                               "model": "config 0 x 1024 (165 MB of weights, larger than L2)"},
 }
 
@@ -603,7 +612,7 @@ def _build(name: str, device, tokens: int, layers: int | None, engine: str | Non
         return PrefillRunner(device, tokens, layers)
     if kind == "single":
         return SingleLinearRunner(device, tokens)
-    return StackedLinearRunner(device, tokens, 1024)
+    return StackedLinearRunner(device, tokens, STACKED_LAYERS)
 
 
 # ----------------------------------------------------------------- timing ---
@@ -778,7 +787,7 @@ def run_reference(args, rank: int) -> None:
     elif kind == "prefill":
         base = cpu_prefill_baseline()
     elif kind in ("single", "stacked"):
-        base = cpu_linear_baseline(640, 2048, 480, tokens)
+        base = cpu_linear_baseline(640, 2048, 480, tokens, layers=STACKED_LAYERS if kind == "stacked" else 1)
     elif kind == "codebook":
         base = cpu_codebook_baseline(tokens)
     else:
@@ -957,7 +966,7 @@ def main() -> None:
         elif kind == "prefill":
             base = cpu_prefill_baseline()
         elif kind in ("single", "stacked"):
-            base = cpu_linear_baseline(640, 2048, 480, tokens)
+            base = cpu_linear_baseline(640, 2048, 480, tokens, layers=STACKED_LAYERS if kind == "stacked" else 1)
         elif kind == "codebook":
             base = cpu_codebook_baseline(tokens)
         else:

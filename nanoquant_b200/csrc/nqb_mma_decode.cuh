@@ -78,8 +78,15 @@ __device__ __forceinline__ void mma_s8(int32_t (&d)[4], uint32_t a0, uint32_t a1
 // Where a K chunk of activations comes from.  Column indices are relative
 // to k0; past k_valid reads 0.  Activations are read through L2 (.cg): an
 // earlier grid stage may have written them.
+//
+// Each loader also splits a value into loads and arithmetic: scale(col) and
+// fetch(t, col) only load (the column's factor, the token's raw element),
+// finish(raw, scale) computes the value, so load_chunk can issue every load
+// of a chunk before the first arithmetic waits on one.
 template <typename XT>
 struct XLoader {  // stage 1: x * pre, pre in fp32
+  using Raw = XT;
+  static constexpr bool kTwoPhase = false;
   const XT *x;
   const float *pre;
   int64_t stride;  // elements per token row
@@ -90,6 +97,15 @@ struct XLoader {  // stage 1: x * pre, pre in fp32
     if (k >= k_valid) return 0.0f;
     return to_f32(__ldcg(x + static_cast<int64_t>(t) * stride + k)) * __ldg(pre + k);
   }
+  __device__ __forceinline__ float scale(int col) const {
+    const int64_t k = k0 + col;
+    return k < k_valid ? __ldg(pre + k) : 0.0f;
+  }
+  __device__ __forceinline__ Raw fetch(int t, int col) const {
+    const int64_t k = k0 + col;
+    return k < k_valid ? __ldcg(x + static_cast<int64_t>(t) * stride + k) : Raw{};
+  }
+  __device__ __forceinline__ float finish(Raw r, float s) const { return to_f32(r) * s; }
 };
 
 struct SwigluLoader {  // stage 1 of a down projection: silu(gate) * up * pre, gate and up fp32
@@ -99,16 +115,29 @@ struct SwigluLoader {  // stage 1 of a down projection: silu(gate) * up * pre, g
   int64_t stride;
   int64_t k0;
   int64_t k_valid;
+  using Raw = float2;  // (gate, up)
+  static constexpr bool kTwoPhase = true;
+  // fast exp and divide keep the T=1 prefetch loop free of spills; clamping
+  // the exponent at 80 keeps the divisor below 2^126, inside __fdividef's
+  // range (silu(g) for g < -80 is below 1e-33 either way)
+  __device__ __forceinline__ static float silu(float g) { return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f))); }
   __device__ __forceinline__ float operator()(int t, int col) const {
     const int64_t k = k0 + col;
     if (k >= k_valid) return 0.0f;
     const int64_t i = static_cast<int64_t>(t) * stride + k;
-    const float g = __ldcg(gate + i);
-    // fast exp and divide keep the T=1 prefetch loop free of spills; clamping
-    // the exponent at 80 keeps the divisor below 2^126, inside __fdividef's
-    // range (silu(g) for g < -80 is below 1e-33 either way)
-    return __fdividef(g, 1.0f + __expf(fminf(-g, 80.0f))) * __ldcg(up + i) * __ldg(pre + k);
+    return silu(__ldcg(gate + i)) * __ldcg(up + i) * __ldg(pre + k);
   }
+  __device__ __forceinline__ float scale(int col) const {
+    const int64_t k = k0 + col;
+    return k < k_valid ? __ldg(pre + k) : 0.0f;
+  }
+  __device__ __forceinline__ Raw fetch(int t, int col) const {
+    const int64_t k = k0 + col;
+    if (k >= k_valid) return make_float2(0.0f, 0.0f);
+    const int64_t i = static_cast<int64_t>(t) * stride + k;
+    return make_float2(__ldcg(gate + i), __ldcg(up + i));
+  }
+  __device__ __forceinline__ float finish(Raw r, float s) const { return silu(r.x) * r.y * s; }
 };
 
 // GELU (tanh form, Hendrycks & Gimpel 2016) of g: 0.5 g (1 + tanh(u)),
@@ -128,15 +157,30 @@ struct GegluLoader {  // stage 1 of a gated-GELU down projection: gelu_tanh(gate
   int64_t stride;
   int64_t k0;
   int64_t k_valid;
+  using Raw = float2;  // (gate, up)
+  static constexpr bool kTwoPhase = true;
   __device__ __forceinline__ float operator()(int t, int col) const {
     const int64_t k = k0 + col;
     if (k >= k_valid) return 0.0f;
     const int64_t i = static_cast<int64_t>(t) * stride + k;
     return gelu_tanh(__ldcg(gate + i)) * __ldcg(up + i) * __ldg(pre + k);
   }
+  __device__ __forceinline__ float scale(int col) const {
+    const int64_t k = k0 + col;
+    return k < k_valid ? __ldg(pre + k) : 0.0f;
+  }
+  __device__ __forceinline__ Raw fetch(int t, int col) const {
+    const int64_t k = k0 + col;
+    if (k >= k_valid) return make_float2(0.0f, 0.0f);
+    const int64_t i = static_cast<int64_t>(t) * stride + k;
+    return make_float2(__ldcg(gate + i), __ldcg(up + i));
+  }
+  __device__ __forceinline__ float finish(Raw r, float s) const { return gelu_tanh(r.x) * r.y * s; }
 };
 
 struct LatentLoader {  // stage 2: the fp32 latent slice of one member
+  using Raw = float;
+  static constexpr bool kTwoPhase = false;
   const float *latent;
   int64_t stride;
   int64_t offset;
@@ -147,6 +191,9 @@ struct LatentLoader {  // stage 2: the fp32 latent slice of one member
     if (k >= k_valid) return 0.0f;
     return __ldcg(latent + static_cast<int64_t>(t) * stride + offset + k);
   }
+  __device__ __forceinline__ float scale(int) const { return 1.0f; }
+  __device__ __forceinline__ Raw fetch(int t, int col) const { return (*this)(t, col); }
+  __device__ __forceinline__ float finish(Raw r, float) const { return r; }
 };
 
 // Per-warp partials of the chunk quantiser (consumer warps).
@@ -166,22 +213,50 @@ struct ChunkValues {
   float v[kQPT][4][kT];
 };
 
-// Issues every load of the chunk's activations; nothing here waits for them,
-// so a caller can issue the next chunk's loads before the current chunk's MMAs.
+// The chunk's activations.  For the gated loaders (long arithmetic per value)
+// up to two tokens, every load is issued first and the arithmetic follows, so
+// the chunk costs one memory round trip; otherwise each value is loaded and
+// computed in turn (the compiler batches those loads itself, with fewer live
+// registers).
 template <int kT, int kQPT, typename Loader>
 __device__ __forceinline__ void load_chunk(const Loader &src, int nst, int T, ChunkValues<kT, kQPT> &cv) {
   const int tid = threadIdx.x;
   const int nquads = nst * 64;
+  if constexpr (kT <= 2 && Loader::kTwoPhase) {
+    float scl[kQPT][4];
+    typename Loader::Raw raw[kQPT][4][kT];
 #pragma unroll
-  for (int i = 0; i < kQPT; ++i) {
-    const int qd = tid + i * kThreads;
-    const int sl = qd >> 6, r = qd & 63;
-    const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
-    const int c0 = sl * kSliceCols + 32 * wi + j + 4 * s;
+    for (int i = 0; i < kQPT; ++i) {
+      const int qd = tid + i * kThreads;
+      const int sl = qd >> 6, r = qd & 63;
+      const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
+      const int c0 = sl * kSliceCols + 32 * wi + j + 4 * s;
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
+      for (int b = 0; b < 4; ++b) {
+        scl[i][b] = qd < nquads ? src.scale(c0 + 8 * b) : 0.0f;
 #pragma unroll
-      for (int t = 0; t < kT; ++t) cv.v[i][b][t] = (qd < nquads && t < T) ? src(t, c0 + 8 * b) : 0.0f;
+        for (int t = 0; t < kT; ++t)
+          raw[i][b][t] = (qd < nquads && t < T) ? src.fetch(t, c0 + 8 * b) : typename Loader::Raw{};
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kQPT; ++i)
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int t = 0; t < kT; ++t) cv.v[i][b][t] = src.finish(raw[i][b][t], scl[i][b]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kQPT; ++i) {
+      const int qd = tid + i * kThreads;
+      const int sl = qd >> 6, r = qd & 63;
+      const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
+      const int c0 = sl * kSliceCols + 32 * wi + j + 4 * s;
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+#pragma unroll
+        for (int t = 0; t < kT; ++t) cv.v[i][b][t] = (qd < nquads && t < T) ? src(t, c0 + 8 * b) : 0.0f;
+    }
   }
 }
 

@@ -67,6 +67,7 @@ constexpr int kMaxDynamicSmem = 220 * 1024;  // + static shared memory <= 227 KB
 constexpr uint32_t kCodedSliceBytes = 2560;
 constexpr uint32_t kCodedRowBits = 160;
 constexpr int kCodebookWords = 1024;
+constexpr int64_t kOverlaySegCols = 1024;  // columns of one int8 overlay row segment (a multiple of 16)
 
 struct MemberDev {
   const uint8_t *tiles;  // row-interleaved sign tiles
@@ -90,6 +91,8 @@ struct MemberDev {
   const int8_t *overlay_values;
   const void *overlay_scales;
   int32_t overlay_scale_dtype;
+  const int32_t *overlay_slot;  // stage 2: [rows] overlay row index of each output row, -1 without (program-owned)
+  int64_t overlay_offset;       // first latent column of the member's overlay partial dot products
   float *y;
   int64_t patch_rank;         // low-rank patch: stage 1 reads R [p, n], stage 2 L [m, p]
   const void *patch_factor;
@@ -129,7 +132,8 @@ struct OpDev {
   const void *x;
   const void *x2;  // NQB_X_SWIGLU / NQB_X_GEGLU: the up projection (x is the gate)
   int32_t x_dtype;
-  int32_t patch_rows;  // patch rows of all members (stage 1 forms their latents)
+  int32_t side_rows;  // patch rows and int8 overlay row segments of all members (stage 1 forms their latents)
+  int32_t ovl_segs;   // segments (kOverlaySegCols columns each) per int8 overlay row
   int64_t n;
   int64_t latent_stride;
   StepDev step;  // decoder-step extensions
@@ -163,7 +167,8 @@ struct __align__(16) StageInfo {
   int64_t latent_stride;
   int32_t x_dtype;
   int32_t n_items;
-  int32_t patch_rows;
+  int32_t side_rows;
+  int32_t ovl_segs;
   StepDev step;
   Item items[kMaxStageItems];
 };
@@ -419,7 +424,8 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
     info.latent_stride = op.latent_stride;
     info.x_dtype = op.x_dtype;
     info.n_items = n_items;
-    info.patch_rows = op.patch_rows;
+    info.side_rows = op.side_rows;
+    info.ovl_segs = op.ovl_segs;
   }
 }
 
@@ -448,18 +454,66 @@ __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index, ui
   mmad::consumer_sync();
 }
 
-// Stage 1's patch latents, formed by the info warp of every CTA while the
-// consumer warps run the stage's tiles: the op's patched members' patch rows,
-// numbered across members, go to CTAs round-robin; row q of member k is
-// latent[t][patch_offset_k + q] = sum_i x[t, i] R_k[q, i] (fp32, fixed order).
-// Inputs are read through L2: an earlier op of the program may have written them.
-__device__ __forceinline__ void patch_rows_warp(const Params &p, const OpDev &op, int cta, int ctas, int lane) {
+// Stage 1's side latents, formed by the two side warps of every CTA while
+// the consumer warps run the stage's tiles.  Rows numbered across the op --
+// the patched members' patch rows, then the stage-2 members' int8 overlay
+// rows -- go to the grid's side warps round-robin:
+//   patch row q of member k:   latent[t][patch_offset_k + q]   = sum_i x[t, i] R_k[q, i]
+//   overlay row j of member k, segment s (columns [s S, s S + S), S = kOverlaySegCols):
+//     latent[t][overlay_offset_k + j segs + s] = scale_j sum_i x[t, i] v_k[j, i]
+// (fp32, each lane's share then the warp's sum in fixed order).  Stage 2's
+// epilogue adds L_k P and each overlay row's segments in order.  Inputs are read through
+// L2: an earlier op of the program may have written them.
+__device__ __forceinline__ float load_x_cg(const void *x, int64_t i, int32_t dtype) {
+  if (dtype == NQB_F32) return __ldcg(static_cast<const float *>(x) + i);
+  if (dtype == NQB_BF16) return __bfloat162float(__ldcg(static_cast<const __nv_bfloat16 *>(x) + i));
+  return __half2float(__ldcg(static_cast<const __half *>(x) + i));
+}
+
+__device__ __forceinline__ float dot_i8x4(uint32_t w, float a0, float a1, float a2, float a3) {
+  return static_cast<float>(static_cast<int8_t>(w & 0xFFu)) * a0 +
+         static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFFu)) * a1 +
+         static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFFu)) * a2 +
+         static_cast<float>(static_cast<int8_t>(w >> 24)) * a3;
+}
+
+__device__ __forceinline__ float2 unpack_pair(uint32_t v, int32_t dtype) {
+  if (dtype == NQB_BF16) return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  return __half22float2(*reinterpret_cast<const __half2 *>(&v));
+}
+
+// sum over 16 elements of int8 w (one 16-byte word) times x[i0 .. i0 + 16)
+// (x 16-byte aligned there), read through L2
+__device__ __forceinline__ float dot_i8x16(uint4 w, const void *x, int64_t i0, int32_t dtype) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  float s = 0.0f;
+  if (dtype == NQB_F32) {
+    const float4 *xv = reinterpret_cast<const float4 *>(static_cast<const float *>(x) + i0);
+    float4 a[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) a[q] = __ldcg(xv + q);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s += dot_i8x4(ww[q], a[q].x, a[q].y, a[q].z, a[q].w);
+  } else {
+    const uint4 *xv = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(x) + i0);
+    const uint4 h0 = __ldcg(xv), h1 = __ldcg(xv + 1);
+    const uint32_t hh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 lo = unpack_pair(hh[2 * q], dtype), hi = unpack_pair(hh[2 * q + 1], dtype);
+      s += dot_i8x4(ww[q], lo.x, lo.y, hi.x, hi.y);
+    }
+  }
+  return s;
+}
+
+__device__ __forceinline__ void side_rows_warp(const Params &p, const OpDev &op, int worker, int workers, int lane) {
   const int T = p.tokens;
-  int64_t base = 0;  // patch rows of earlier members
+  int64_t base = 0;  // side rows of earlier members
   for (int k = 0; k < op.count; ++k) {
     const MemberDev &md = op.s[0][k];
     if (md.patch_rank <= 0) continue;
-    for (int64_t q = ((cta - base) % ctas + ctas) % ctas; q < md.patch_rank; q += ctas) {
+    for (int64_t q = ((worker - base) % workers + workers) % workers; q < md.patch_rank; q += workers) {
       for (int t0 = 0; t0 < T; t0 += 4) {  // four tokens at a time: few registers beside the consumers'
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         for (int64_t i = lane; i < op.n; i += 32) {
@@ -467,12 +521,7 @@ __device__ __forceinline__ void patch_rows_warp(const Params &p, const OpDev &op
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             if (t0 + u >= T) break;
-            const int64_t xi = static_cast<int64_t>(t0 + u) * op.n + i;
-            float xv;
-            if (op.x_dtype == NQB_F32) xv = __ldcg(static_cast<const float *>(op.x) + xi);
-            else if (op.x_dtype == NQB_BF16) xv = __bfloat162float(__ldcg(static_cast<const __nv_bfloat16 *>(op.x) + xi));
-            else xv = __half2float(__ldcg(static_cast<const __half *>(op.x) + xi));
-            part[u] += xv * r;
+            part[u] += load_x_cg(op.x, static_cast<int64_t>(t0 + u) * op.n + i, op.x_dtype) * r;
           }
         }
 #pragma unroll
@@ -485,6 +534,41 @@ __device__ __forceinline__ void patch_rows_warp(const Params &p, const OpDev &op
       }
     }
     base += md.patch_rank;
+  }
+  for (int k = 0; k < op.count; ++k) {
+    const MemberDev &md = op.s[1][k];
+    if (md.overlay_rows <= 0) continue;
+    // 16-element chunks: one 16-byte load of int8 values and 16-byte loads of x
+    const bool vec = op.n % 16 == 0 && reinterpret_cast<uintptr_t>(op.x) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(md.overlay_values) % 16 == 0;
+    const int segs = op.ovl_segs;
+    const int n = static_cast<int>(op.n);
+    const int items = static_cast<int>(md.overlay_rows) * segs;
+    for (int it = ((worker - static_cast<int>(base)) % workers + workers) % workers; it < items; it += workers) {
+      const int j = it / segs;
+      const int c0 = (it - j * segs) * static_cast<int>(kOverlaySegCols);
+      const int c1 = min(c0 + static_cast<int>(kOverlaySegCols), n);
+      const int8_t *row = md.overlay_values + static_cast<int64_t>(j) * n;
+      for (int t = 0; t < T; ++t) {
+        float part = 0.0f;
+        if (vec) {
+#pragma unroll 1
+          for (int c = c0 / 16 + lane; c < c1 / 16; c += 32)
+            part += dot_i8x16(__ldg(reinterpret_cast<const uint4 *>(row) + c), op.x,
+                              static_cast<int64_t>(t) * n + 16 * c, op.x_dtype);
+        } else {
+#pragma unroll 4
+          for (int i = c0 + lane; i < c1; i += 32)
+            part += load_x_cg(op.x, static_cast<int64_t>(t) * n + i, op.x_dtype) * static_cast<float>(row[i]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        if (lane == 0)
+          p.latent[static_cast<int64_t>(t) * op.latent_stride + md.overlay_offset + it] =
+              part * load_as_float(md.overlay_scales, j, md.overlay_scale_dtype);
+      }
+    }
+    base += items;
   }
 }
 
@@ -540,12 +624,27 @@ struct Producer {
   }
 };
 
-// 8 consumer warps, the sign-ring producer warp, and a warp that stages each
-// stage's tables and prefetches its scales (two warps, so that neither
-// role's waiting can starve the other within one warp).
-constexpr int kBlockThreads = mmad::kThreads + 64;
+// 8 consumer warps (warpgroups 0 and 1), then warpgroup 2: the sign-ring
+// producer warp, a warp that stages each stage's tables and prefetches its
+// scales (two warps, so that neither role's waiting can starve the other
+// within one warp) and two idle warps.  Twelve warps launch with 168
+// registers each (65536 / 384, rounded down to 8); warpgroup 2 then hands
+// registers back (setmaxnreg) so each consumer thread holds up to 224:
+// 256 x 224 + 128 x 56 = 64512 = 384 x 168, and per SM sub-partition (two
+// consumer warps and one of warpgroup 2) 32 x (2 x 224 + 56) <= 16384.  The
+// host launches an instance only if it was built with exactly 168 registers
+// (a smaller launch could not serve the consumers' increase).
+constexpr int kBlockThreads = mmad::kThreads + 128;
 constexpr int kProducerWarp = mmad::kWarps;
 constexpr int kInfoWarp = mmad::kWarps + 1;
+constexpr int kSideWarp = mmad::kWarps + 2;  // and kSideWarp + 1: stage 1's patch and overlay rows
+constexpr int kLaunchRegs = 168;
+constexpr int kConsumerRegs = 224;
+constexpr int kHelperRegs = 56;
+static_assert(mmad::kThreads * kConsumerRegs + (kBlockThreads - mmad::kThreads) * kHelperRegs <=
+                  kBlockThreads * kLaunchRegs,
+              "register split exceeds the launch's registers");
+static_assert(32 * (2 * kConsumerRegs + kHelperRegs) <= 16384, "register split exceeds a sub-partition");
 
 // Slices quantised at once (B fragments and activations held for them).
 __host__ __device__ constexpr int slices_per_chunk(int bucket) {
@@ -632,7 +731,9 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // come from shared memory; the remaining rows (this step's, and any past the
 // ring's share) are read from global memory.  Every consumer warp waits for
 // the unit's ring slots first and hands them back after the last token.
-__device__ __noinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
+// Inlined, like attention_join: a call would make the kernel keep its stage
+// loop's state across the call (spills), slowing every linear stage.
+__device__ __forceinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
                                                 const uint8_t *ring, uint64_t *s_full, uint64_t *s_empty,
                                                 int &slot, uint32_t &phase, bool &ok, long long *trace) {
 #ifdef NQB_PHASE_TRACE
@@ -800,7 +901,7 @@ __device__ __noinline__ void attention_partials(const Params &p, const StepDev &
 
 // Joins the splits' partials of every (token, q head) in split order, one
 // warp per row (lane: 4 dims), and writes the bf16 attention output.
-__device__ __noinline__ void attention_join(const Params &p, const StepDev &op) {
+__device__ __forceinline__ void attention_join(const Params &p, const StepDev &op) {
   const int rows = p.tokens * op.q_heads;
   const int lane = threadIdx.x & 31;
   const int stride = static_cast<int>(gridDim.x) * mmad::kWarps;
@@ -922,7 +1023,24 @@ __device__ __forceinline__ void qk_rope_epilogue(const StepDev &op, int member, 
   leader_sync();  // xs and red are reused by the next tile
 }
 
-// kPatch: some op has a patched member; kMixed: some member streams coded
+// A CTA's exit steps, run by every warp: a failed wait is recorded, every CTA
+// stays until its cluster peers have made their last remote arrivals, and the
+// last CTA of the grid zeroes the barrier counters for the next run.
+__device__ __forceinline__ void finish_cta(const Params &p, bool ok) {
+  if (!ok) record_error(NQB_ERR_TIMEOUT);
+  cluster_sync();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t finished = atomicAdd(p.counters + 1, 1u);
+    if (finished == gridDim.x - 1) {
+      p.counters[0] = 0;
+      p.counters[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+// kPatch: some op has a patched member or int8 overlay rows; kMixed: some member streams coded
 // mixed-V tiles; kStep: some op uses the decoder-step extensions (residual
 // input norm, fused epilogues, attention).  Programs without them run
 // instances with those steps compiled out (the steps cost time in the stage
@@ -944,8 +1062,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   __shared__ uint64_t s_info_free[2];  // the consumers are done with s_info[b]'s stage
   __shared__ StageInfo s_info[2];
   __shared__ mmad::Scratch<kT> s_sc;
-  __shared__ float s_red_f[mmad::kWarps];
-  __shared__ uint64_t s_patch_done;  // the info warp formed this CTA's patch rows of the current stage 1
+  __shared__ uint64_t s_patch_done;  // the side warps formed this CTA's side rows of the current stage 1
   __shared__ float s_rms[kT];        // residual-stream input: the stage's per-token norm factors
 
   const int tid = threadIdx.x;
@@ -980,311 +1097,262 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
     ptx::fence_mbar_init();
   }
   cluster_sync();  // every CTA's barriers exist before any remote arrive
+  // Each warpgroup runs its roles inside one branch that starts with its
+  // register split (setmaxnreg is warpgroup-uniform) and ends with the CTA's
+  // exit steps, so no code is shared between the two register budgets.
+  //
   // Run by nqb_program_run_dependent, the program is a programmatic dependent
   // of the preceding kernel: only the producer warp runs ahead (sign words,
   // which no kernel writes); every other warp first waits for the preceding
   // kernel to complete (its outputs are this program's inputs).  After a
-  // plain launch the wait returns at once.
-  if (warp != kProducerWarp) asm volatile("griddepcontrol.wait;" ::: "memory");
-
+  // plain launch the wait returns at once.  The split comes first, so the
+  // producer's warpgroup never waits on that dependency.
   bool ok = true;
-  if (warp == kProducerWarp) {
-    // ---- producer: stream this CTA's sign slices through the ring, as far
-    // ahead as the ring allows, independent of the stage barriers
-    if (lane == 0) {
-      Producer prod;
-      prod.addrs = p.slice_addrs + p.slice_begin[cta];
-      prod.count = p.slice_count[cta];
-      prod.padded = ((prod.count + kAddrChunk - 1) / kAddrChunk) * kAddrChunk;
-      prod.cache = addr_cache;
-      prod.addr_bar = s_addr_bar;
-      prod.ring = ring;
-      prod.full = s_full;
-      prod.ring_slots = R;
-      for (int c = 0; c < kAddrSlots; ++c) prod.issue_addr_chunk(c);
-      int slot = 0;
-      uint32_t phase = 0;  // ring passes completed
-      for (int pos = 0; pos < prod.count; ++pos) {
-        if (phase > 0 && !wait_local_backoff(&s_empty[slot], (phase - 1) & 1)) ok = false;
-        ok &= prod.template produce<kMixed>(pos, slot);
-        if (++slot == R) {
-          slot = 0;
-          ++phase;
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == kInfoWarp) {
-    // ---- stage g's tables into s_info[g % 2] and an L2 prefetch of its
-    // scales and inputs, once stage g - 1 has started (so stage g - 2, the
-    // buffer's previous user, is finished everywhere); then, when stage g - 1
-    // is a stage 1 with patched members, this CTA's share of their patch
-    // latents (stage g - 1's inputs are complete once stage g - 2 is)
-    for (int g = 0; g < p.stages; ++g) {
-      if (g >= 2) {
-        // stage g - 2 (the buffer's previous user) finished everywhere, so
-        // stage g - 1's inputs are complete; then, even when that grid wait
-        // gave up, this CTA's consumers are done with the buffer
-        if (lane == 0) {
-          if (!wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x + p.barrier_skew, p.barrier_limit))
-            ok = false;
-          if (!wait_local(&s_info_free[g & 1], ((g >> 1) - 1) & 1)) ok = false;
-        }
-        __syncwarp();
-      }
-      stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
-      __syncwarp();
+  if (warp >= mmad::kWarps) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kHelperRegs));
+    if (warp != kProducerWarp) asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (warp == kProducerWarp) {
+      // ---- producer: stream this CTA's sign slices through the ring, as far
+      // ahead as the ring allows, independent of the stage barriers
       if (lane == 0) {
-        // a stage 1 with mixed-V members also brings their codebooks (the
-        // previous stage 1, their last reader, has finished everywhere)
-        uint32_t coded = 0;
-        if constexpr (kMixed) {
-          if ((g & 1) == 0)
-            for (int k = 0; k < kMaxMembersTc; ++k) coded += s_info[g & 1].md[k].coded_tiles != nullptr ? 1u : 0u;
-        }
-        if (coded == 0) {
-          mbar_arrive_cta(&s_info_full[g & 1]);
-        } else {
-          uint32_t *cb = reinterpret_cast<uint32_t *>(smem + p.off_cb);
-          expect_tx(&s_info_full[g & 1], coded * kCodebookWords * 4u);
-          for (int k = 0; k < kMaxMembersTc; ++k)
-            if (s_info[g & 1].md[k].coded_tiles != nullptr)
-              bulk_load(cb + k * kCodebookWords, s_info[g & 1].md[k].codebook, kCodebookWords * 4u,
-                        &s_info_full[g & 1]);
-        }
-      }
-      if constexpr (kPatch) {
-        if ((g & 1) == 1 && s_info[(g - 1) & 1].patch_rows > 0) {  // stage g - 1's tables, staged last pass
-          patch_rows_warp(p, p.ops[g >> 1], cta, static_cast<int>(gridDim.x), lane);
-          __threadfence();  // the rows are visible GPU-wide before the consumers' barrier release
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cta(&s_patch_done);
-        }
-      }
-      prefetch_stage(p, g, lane);
-    }
-  } else {
-    // ---- consumers: 8 warps x 16 rows of the current 128-row tile
-    int slot = 0;         // ring slot of the next slice
-    uint32_t phase = 0;   // ring passes completed
-    uint32_t xg = 0;      // exchange groups done
-    uint32_t patched = 0;  // patched stage 1s done
-    for (int g = 0; g < p.stages; ++g) {
-      const int st = g & 1;
-      if (!wait_local(&s_info_full[g & 1], (g >> 1) & 1)) ok = false;
-      const StageInfo &op = s_info[g & 1];
-      const int ib = 0;
-      const int ie = op.n_items;
-      NQB_TRACE_BEGIN
-      const StepDev &gop = op.step;  // the op's decoder-step fields (staged in shared memory)
-      int op_kind = NQB_OP_LINEAR, op_epi = NQB_EPI_STORE;
-      bool normed = false;
-      float rms_part[kT];  // residual-stream input: warp 0's partial sums of h^2 (lane: tiles lane, lane + 32, ..)
-#pragma unroll
-      for (int t = 0; t < kT; ++t) rms_part[t] = 0.0f;
-      bool rms_pending = false;
-      if constexpr (kStep) {
-        op_kind = gop.kind;
-        op_epi = st == 1 ? gop.epilogue : NQB_EPI_STORE;
-        normed = st == 0 && gop.norm_stats != nullptr;
-        if (op_kind == NQB_OP_ATTENTION) {
-          // split-K partials over the CTAs (stage 1 of the op), then their join;
-          // the CTA's exchange buffers are idle during these stages
-          NQB_TRACE(kTraceTables);
-          if (st == 0)
-#ifdef NQB_PHASE_TRACE
-            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, tid == 0 ? trace_c : nullptr);
-#else
-            attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, nullptr);
-#endif
-          else
-            attention_join(p, gop);
-          if (st == 0) {
-            NQB_TRACE_RESET();  // attention_partials added its own phases
-          } else {
-            NQB_TRACE(kTraceMma);
-          }
-        } else if (normed) {
-          // h's per-tile sums of squares (written before this stage): warp 0
-          // issues the loads now and reduces them while the quarters land
-          rms_pending = true;
-          if (warp == 0)
-            for (int i = lane; i < gop.stat_tiles; i += 32)
-#pragma unroll
-              for (int t = 0; t < kT; ++t)
-                if (t < T) rms_part[t] += __ldcg(gop.norm_stats + static_cast<int64_t>(i) * T + t);
-        }
-      }
-      // kMixed: item j's slices, the records of a coded tile decoded where a
-      // plain tile's words are loaded (whether item j is coded is read once)
-      auto mixed_slices = [&](int j, int nst, auto &d) {
-        const Item item = op.items[j];
-        const uint32_t *cb = (st == 0 && item.tile >= op.md[item.member].coded_from)
-                                 ? reinterpret_cast<const uint32_t *>(smem + p.off_cb) + item.member * kCodebookWords
-                                 : nullptr;
-        for (int sl = 0; sl < nst; ++sl) {
-          if (!wait_local(&s_full[slot], phase & 1)) ok = false;
-          const uint8_t *src = ring + static_cast<size_t>(slot) * kStageWeightBytes;
-          mmad::SliceWords w;
-          if (cb != nullptr) {
-            const uint32_t *rw = reinterpret_cast<const uint32_t *>(src);
-            const int r0 = warp * 16 + (lane >> 2), tig = lane & 3;
-            w.w00 = decode_record(cb, coded_record(rw, r0, tig));
-            w.w10 = decode_record(cb, coded_record(rw, r0 + 8, tig));
-            w.w01 = decode_record(cb, coded_record(rw, r0, 4 + tig));
-            w.w11 = decode_record(cb, coded_record(rw, r0 + 8, 4 + tig));
-          } else {
-            w = mmad::load_slice_words(src, warp, lane);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+        Producer prod;
+        prod.addrs = p.slice_addrs + p.slice_begin[cta];
+        prod.count = p.slice_count[cta];
+        prod.padded = ((prod.count + kAddrChunk - 1) / kAddrChunk) * kAddrChunk;
+        prod.cache = addr_cache;
+        prod.addr_bar = s_addr_bar;
+        prod.ring = ring;
+        prod.full = s_full;
+        prod.ring_slots = R;
+        for (int c = 0; c < kAddrSlots; ++c) prod.issue_addr_chunk(c);
+        int slot = 0;
+        uint32_t phase = 0;  // ring passes completed
+        for (int pos = 0; pos < prod.count; ++pos) {
+          if (phase > 0 && !wait_local_backoff(&s_empty[slot], (phase - 1) & 1)) ok = false;
+          ok &= prod.template produce<kMixed>(pos, slot);
           if (++slot == R) {
             slot = 0;
             ++phase;
           }
-          mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
         }
-      };
-      for (int gb = ib; gb < ie; gb += p.group) {
-        const int ge = min(gb + p.group, ie);
-        for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
-        if constexpr (kPrefetchUnits) {
-          // ---- this CTA's quarter of every item of the group, one (member run,
-          // chunk) unit at a time.  At one token the next unit's activation
-          // loads are issued before this unit's MMAs, so their L2 round trip
-          // is hidden behind the MMAs instead of opening the next unit.
-          auto load_unit = [&](int j, int c0, int hi, mmad::ChunkValues<kT, kQPT> &cv) {
-            const MemberDev &md = op.md[op.items[j].member];
-            const int nst = min(p.sc, hi - c0);
-            const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
-            if (st == 1) {
-              mmad::load_chunk<kT, kQPT>(mmad::LatentLoader{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid},
-                                         nst, T, cv);
-            } else if (op.x_dtype == NQB_X_SWIGLU) {
-              mmad::load_chunk<kT, kQPT>(mmad::SwigluLoader{static_cast<const float *>(op.x),
-                                                            static_cast<const float *>(op.x2), md.pre, op.n, k0,
-                                                            md.k_valid},
-                                         nst, T, cv);
-            } else if (op.x_dtype == NQB_X_GEGLU) {
-              mmad::load_chunk<kT, kQPT>(mmad::GegluLoader{static_cast<const float *>(op.x),
-                                                           static_cast<const float *>(op.x2), md.pre, op.n, k0,
-                                                           md.k_valid},
-                                         nst, T, cv);
-            } else if (op.x_dtype == NQB_BF16) {
-              mmad::load_chunk<kT, kQPT>(mmad::XLoader<__nv_bfloat16>{static_cast<const __nv_bfloat16 *>(op.x), md.pre,
-                                                                     op.n, k0, md.k_valid},
-                                         nst, T, cv);
-            } else if (op.x_dtype == NQB_F16) {
-              mmad::load_chunk<kT, kQPT>(
-                  mmad::XLoader<__half>{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
-            } else {
-              mmad::load_chunk<kT, kQPT>(
-                  mmad::XLoader<float>{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
-            }
-          };
-          int j0 = gb, j1 = gb, c0 = 0, hi = 0;
-          bool have = next_unit(op, ge, static_cast<int>(rank), p.sc, j0, j1, c0, hi);
-          mmad::ChunkValues<kT, kQPT> cur;
-          if (have) load_unit(j0, c0, hi, cur);
-          while (have) {
-            int nj0 = j0, nj1 = j1, nc0 = c0, nhi = hi;
-            const bool more = next_unit(op, ge, static_cast<int>(rank), p.sc, nj0, nj1, nc0, nhi);
-            mmad::ChunkValues<kT, kQPT> nxt;
-            if (kPrefetchUnits && more) load_unit(nj0, nc0, nhi, nxt);
-            const int nst = min(p.sc, hi - c0);
-            int e[kT];
-            long long Q[kT];
+      }
+      __syncwarp();
+    } else if (warp == kInfoWarp) {
+      // ---- stage g's tables into s_info[g % 2] and an L2 prefetch of its
+      // scales and inputs, once stage g - 1 has started (so stage g - 2, the
+      // buffer's previous user, is finished everywhere)
+      for (int g = 0; g < p.stages; ++g) {
+        if (g >= 2) {
+          // stage g - 2 (the buffer's previous user) finished everywhere, so
+          // stage g - 1's inputs are complete; then, even when that grid wait
+          // gave up, this CTA's consumers are done with the buffer
+          if (lane == 0) {
+            if (!wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x + p.barrier_skew, p.barrier_limit))
+              ok = false;
+            if (!wait_local(&s_info_free[g & 1], ((g >> 1) - 1) & 1)) ok = false;
+          }
+          __syncwarp();
+        }
+        stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
+        __syncwarp();
+        if (lane == 0) {
+          // a stage 1 with mixed-V members also brings their codebooks (the
+          // previous stage 1, their last reader, has finished everywhere)
+          uint32_t coded = 0;
+          if constexpr (kMixed) {
+            if ((g & 1) == 0)
+              for (int k = 0; k < kMaxMembersTc; ++k) coded += s_info[g & 1].md[k].coded_tiles != nullptr ? 1u : 0u;
+          }
+          if (coded == 0) {
+            mbar_arrive_cta(&s_info_full[g & 1]);
+          } else {
+            uint32_t *cb = reinterpret_cast<uint32_t *>(smem + p.off_cb);
+            expect_tx(&s_info_full[g & 1], coded * kCodebookWords * 4u);
+            for (int k = 0; k < kMaxMembersTc; ++k)
+              if (s_info[g & 1].md[k].coded_tiles != nullptr)
+                bulk_load(cb + k * kCodebookWords, s_info[g & 1].md[k].codebook, kCodebookWords * 4u,
+                          &s_info_full[g & 1]);
+          }
+        }
+        prefetch_stage(p, g, lane);
+      }
+    } else if (kPatch && warp >= kSideWarp) {
+      // ---- side warps: for each stage 1 with side rows (patch or overlay
+      // rows), once its inputs are complete (the stage before it finished
+      // everywhere), this CTA's share of them; then one arrival on s_patch_done
+      const int worker = cta * 2 + (warp - kSideWarp);
+      for (int g = 0; g < p.stages; g += 2) {
+        const OpDev &op = p.ops[g >> 1];
+        if (op.side_rows <= 0) continue;
+        if (g >= 2) {
+          if (lane == 0 &&
+              !wait_counter(p.counters, static_cast<uint32_t>(g) * gridDim.x + p.barrier_skew, p.barrier_limit))
+            ok = false;
+          __syncwarp();
+        }
+        side_rows_warp(p, op, worker, 2 * static_cast<int>(gridDim.x), lane);
+        __threadfence();  // the rows are visible GPU-wide before the consumers' barrier release
+        asm volatile("bar.sync 3, 64;" ::: "memory");  // both side warps are done
+        if (warp == kSideWarp && lane == 0) mbar_arrive_cta(&s_patch_done);
+      }
+    }
+    finish_cta(p, ok);
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    {
+      // ---- consumers: 8 warps x 16 rows of the current 128-row tile
+      int slot = 0;         // ring slot of the next slice
+      uint32_t phase = 0;   // ring passes completed
+      uint32_t xg = 0;      // exchange groups done
+      uint32_t patched = 0;  // patched stage 1s done
+      for (int g = 0; g < p.stages; ++g) {
+        const int st = g & 1;
+        if (!wait_local(&s_info_full[g & 1], (g >> 1) & 1)) ok = false;
+        const StageInfo &op = s_info[g & 1];
+        const int ib = 0;
+        const int ie = op.n_items;
+        NQB_TRACE_BEGIN
+        const StepDev &gop = op.step;  // the op's decoder-step fields (staged in shared memory)
+        int op_kind = NQB_OP_LINEAR, op_epi = NQB_EPI_STORE;
+        bool normed = false;
+        float rms_part[kT];  // residual-stream input: warp 0's partial sums of h^2 (lane: tiles lane, lane + 32, ..)
+        float rms_next[kT];  // up to two tokens: tile lane + 32, loaded without waiting, added at the reduction
+  #pragma unroll
+        for (int t = 0; t < kT; ++t) rms_part[t] = rms_next[t] = 0.0f;
+        bool rms_pending = false;
+        if constexpr (kStep) {
+          op_kind = gop.kind;
+          op_epi = st == 1 ? gop.epilogue : NQB_EPI_STORE;
+          normed = st == 0 && gop.norm_stats != nullptr;
+          if (op_kind == NQB_OP_ATTENTION) {
+            // split-K partials over the CTAs (stage 1 of the op), then their join;
+            // the CTA's exchange buffers are idle during these stages
             NQB_TRACE(kTraceTables);
-            mmad::quantize_loaded<kT, kQPT>(cur, nst, T, smem_b, s_sc, e, Q);
-            NQB_TRACE(kTraceQuantise);
-            for (int j = j0; j < j1; ++j) {
-              int32_t d[kSets][kNT][4];
-  #pragma unroll
-              for (int c = 0; c < kSets; ++c)
-  #pragma unroll
-                for (int nt = 0; nt < kNT; ++nt)
-  #pragma unroll
-                  for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
-              if constexpr (kMixed) {
-                mixed_slices(j, nst, d);
-              } else {
-                for (int sl = 0; sl < nst; ++sl) {
-                  NQB_TRACE(kTraceMma);
-                  if (!wait_local(&s_full[slot], phase & 1)) ok = false;
-                  NQB_TRACE(kTraceWaitSigns);
-                  const mmad::SliceWords w =
-                      mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
-                  __syncwarp();
-                  if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
-                  if (++slot == R) {
-                    slot = 0;
-                    ++phase;
-                  }
-                  mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
-                }
-              }
+            if (st == 0)
+  #ifdef NQB_PHASE_TRACE
+              attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, tid == 0 ? trace_c : nullptr);
+  #else
+              attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, nullptr);
+  #endif
+            else
+              attention_join(p, gop);
+            if (st == 0) {
+              NQB_TRACE_RESET();  // attention_partials added its own phases
+            } else {
               NQB_TRACE(kTraceMma);
-              mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
-              NQB_TRACE(kTraceDrain);
             }
-            j0 = nj0;
-            j1 = nj1;
-            c0 = nc0;
-            hi = nhi;
-            have = more;
-            if (have) {
-              if constexpr (kPrefetchUnits) {
-                cur = nxt;
+          } else if (normed) {
+            // h's per-tile sums of squares (written before this stage): warp 0
+            // issues the loads now and reduces them while the quarters land
+            rms_pending = true;
+            if (warp == 0) {
+              if (kT <= 2 && gop.stat_tiles <= 64) {
+                // two independent loads per token, no arithmetic on them before the reduction
+  #pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                  if (t < T && lane < gop.stat_tiles) rms_part[t] = __ldcg(gop.norm_stats + static_cast<int64_t>(lane) * T + t);
+                  if (t < T && lane + 32 < gop.stat_tiles)
+                    rms_next[t] = __ldcg(gop.norm_stats + static_cast<int64_t>(lane + 32) * T + t);
+                }
               } else {
-                load_unit(j0, c0, hi, cur);
+                for (int i = lane; i < gop.stat_tiles; i += 32)
+  #pragma unroll
+                  for (int t = 0; t < kT; ++t)
+                    if (t < T) rms_part[t] += __ldcg(gop.norm_stats + static_cast<int64_t>(i) * T + t);
               }
             }
           }
-        } else {
-          // ---- this CTA's quarter of every item of the group, member by member
-          for (int j0 = gb; j0 < ge;) {
-            const int mi = op.items[j0].member;
-            int j1 = j0 + 1;
-            while (j1 < ge && op.items[j1].member == mi) ++j1;
-            const MemberDev &md = op.md[mi];
-            const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
-            const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
-            for (int c0 = lo; c0 < hi; c0 += p.sc) {
+        }
+        // kMixed: item j's slices, the records of a coded tile decoded where a
+        // plain tile's words are loaded (whether item j is coded is read once)
+        auto mixed_slices = [&](int j, int nst, auto &d) {
+          const Item item = op.items[j];
+          const uint32_t *cb = (st == 0 && item.tile >= op.md[item.member].coded_from)
+                                   ? reinterpret_cast<const uint32_t *>(smem + p.off_cb) + item.member * kCodebookWords
+                                   : nullptr;
+          for (int sl = 0; sl < nst; ++sl) {
+            if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+            const uint8_t *src = ring + static_cast<size_t>(slot) * kStageWeightBytes;
+            mmad::SliceWords w;
+            if (cb != nullptr) {
+              const uint32_t *rw = reinterpret_cast<const uint32_t *>(src);
+              const int r0 = warp * 16 + (lane >> 2), tig = lane & 3;
+              w.w00 = decode_record(cb, coded_record(rw, r0, tig));
+              w.w10 = decode_record(cb, coded_record(rw, r0 + 8, tig));
+              w.w01 = decode_record(cb, coded_record(rw, r0, 4 + tig));
+              w.w11 = decode_record(cb, coded_record(rw, r0 + 8, 4 + tig));
+            } else {
+              w = mmad::load_slice_words(src, warp, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+            if (++slot == R) {
+              slot = 0;
+              ++phase;
+            }
+            mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
+          }
+        };
+        for (int gb = ib; gb < ie; gb += p.group) {
+          const int ge = min(gb + p.group, ie);
+          for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
+          if constexpr (kPrefetchUnits) {
+            // ---- this CTA's quarter of every item of the group, one (member run,
+            // chunk) unit at a time.  At one token the next unit's activation
+            // loads are issued before this unit's MMAs, so their L2 round trip
+            // is hidden behind the MMAs instead of opening the next unit.
+            auto load_unit = [&](int j, int c0, int hi, mmad::ChunkValues<kT, kQPT> &cv) {
+              const MemberDev &md = op.md[op.items[j].member];
               const int nst = min(p.sc, hi - c0);
               const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+              if (st == 1) {
+                mmad::load_chunk<kT, kQPT>(mmad::LatentLoader{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid},
+                                           nst, T, cv);
+              } else if (op.x_dtype == NQB_X_SWIGLU) {
+                mmad::load_chunk<kT, kQPT>(mmad::SwigluLoader{static_cast<const float *>(op.x),
+                                                              static_cast<const float *>(op.x2), md.pre, op.n, k0,
+                                                              md.k_valid},
+                                           nst, T, cv);
+              } else if (op.x_dtype == NQB_X_GEGLU) {
+                mmad::load_chunk<kT, kQPT>(mmad::GegluLoader{static_cast<const float *>(op.x),
+                                                             static_cast<const float *>(op.x2), md.pre, op.n, k0,
+                                                             md.k_valid},
+                                           nst, T, cv);
+              } else if (op.x_dtype == NQB_BF16) {
+                mmad::load_chunk<kT, kQPT>(mmad::XLoader<__nv_bfloat16>{static_cast<const __nv_bfloat16 *>(op.x), md.pre,
+                                                                       op.n, k0, md.k_valid},
+                                           nst, T, cv);
+              } else if (op.x_dtype == NQB_F16) {
+                mmad::load_chunk<kT, kQPT>(
+                    mmad::XLoader<__half>{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
+              } else {
+                mmad::load_chunk<kT, kQPT>(
+                    mmad::XLoader<float>{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid}, nst, T, cv);
+              }
+            };
+            int j0 = gb, j1 = gb, c0 = 0, hi = 0;
+            bool have = next_unit(op, ge, static_cast<int>(rank), p.sc, j0, j1, c0, hi);
+            mmad::ChunkValues<kT, kQPT> cur;
+            if (have) load_unit(j0, c0, hi, cur);
+            while (have) {
+              int nj0 = j0, nj1 = j1, nc0 = c0, nhi = hi;
+              const bool more = next_unit(op, ge, static_cast<int>(rank), p.sc, nj0, nj1, nc0, nhi);
+              mmad::ChunkValues<kT, kQPT> nxt;
+              if (kPrefetchUnits && more) load_unit(nj0, nc0, nhi, nxt);
+              const int nst = min(p.sc, hi - c0);
               int e[kT];
               long long Q[kT];
               NQB_TRACE(kTraceTables);
-              if (st == 1) {
-                const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              } else if (op.x_dtype == NQB_X_SWIGLU) {
-                const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
-                                            md.pre, op.n, k0, md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              } else if (op.x_dtype == NQB_X_GEGLU) {
-                const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
-                                           md.pre, op.n, k0, md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              } else if (op.x_dtype == NQB_BF16) {
-                const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
-                                                      md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              } else if (op.x_dtype == NQB_F16) {
-                const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              } else {
-                const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
-                mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-              }
+              mmad::quantize_loaded<kT, kQPT>(cur, nst, T, smem_b, s_sc, e, Q);
               NQB_TRACE(kTraceQuantise);
               for (int j = j0; j < j1; ++j) {
                 int32_t d[kSets][kNT][4];
-  #pragma unroll
+    #pragma unroll
                 for (int c = 0; c < kSets; ++c)
-  #pragma unroll
+    #pragma unroll
                   for (int nt = 0; nt < kNT; ++nt)
-  #pragma unroll
+    #pragma unroll
                     for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
                 if constexpr (kMixed) {
                   mixed_slices(j, nst, d);
@@ -1308,209 +1376,261 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
                 mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
                 NQB_TRACE(kTraceDrain);
               }
+              j0 = nj0;
+              j1 = nj1;
+              c0 = nc0;
+              hi = nhi;
+              have = more;
+              if (have) {
+                if constexpr (kPrefetchUnits) {
+                  cur = nxt;
+                } else {
+                  load_unit(j0, c0, hi, cur);
+                }
+              }
             }
-            j0 = j1;
+          } else {
+            // ---- this CTA's quarter of every item of the group, member by member
+            for (int j0 = gb; j0 < ge;) {
+              const int mi = op.items[j0].member;
+              int j1 = j0 + 1;
+              while (j1 < ge && op.items[j1].member == mi) ++j1;
+              const MemberDev &md = op.md[mi];
+              const int lo = md.ks * static_cast<int>(rank) / kClusterSize;
+              const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
+              for (int c0 = lo; c0 < hi; c0 += p.sc) {
+                const int nst = min(p.sc, hi - c0);
+                const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+                int e[kT];
+                long long Q[kT];
+                NQB_TRACE(kTraceTables);
+                if (st == 1) {
+                  const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                } else if (op.x_dtype == NQB_X_SWIGLU) {
+                  const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                              md.pre, op.n, k0, md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                } else if (op.x_dtype == NQB_X_GEGLU) {
+                  const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                             md.pre, op.n, k0, md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                } else if (op.x_dtype == NQB_BF16) {
+                  const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
+                                                        md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                } else if (op.x_dtype == NQB_F16) {
+                  const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                } else {
+                  const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
+                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+                }
+                NQB_TRACE(kTraceQuantise);
+                for (int j = j0; j < j1; ++j) {
+                  int32_t d[kSets][kNT][4];
+    #pragma unroll
+                  for (int c = 0; c < kSets; ++c)
+    #pragma unroll
+                    for (int nt = 0; nt < kNT; ++nt)
+    #pragma unroll
+                      for (int r = 0; r < 4; ++r) d[c][nt][r] = 0;
+                  if constexpr (kMixed) {
+                    mixed_slices(j, nst, d);
+                  } else {
+                    for (int sl = 0; sl < nst; ++sl) {
+                      NQB_TRACE(kTraceMma);
+                      if (!wait_local(&s_full[slot], phase & 1)) ok = false;
+                      NQB_TRACE(kTraceWaitSigns);
+                      const mmad::SliceWords w =
+                          mmad::load_slice_words(ring + static_cast<size_t>(slot) * kStageWeightBytes, warp, lane);
+                      __syncwarp();
+                      if (lane == 0) mbar_arrive_cta(&s_empty[slot]);
+                      if (++slot == R) {
+                        slot = 0;
+                        ++phase;
+                      }
+                      mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
+                    }
+                  }
+                  NQB_TRACE(kTraceMma);
+                  mmad::drain_to_acc<kT>(d, T, warp, lane, e, Q, s_acc + static_cast<size_t>(j - gb) * T * kTileRows);
+                  NQB_TRACE(kTraceDrain);
+                }
+              }
+              j0 = j1;
+            }
           }
-        }
-        // ---- quarters -> leaders: asynchronous stores into their shared
-        // memory, counted on each leader's s_x_full
-        if (xg > 0 && !wait_cluster(&s_x_free, (xg - 1) & 1)) ok = false;
-        mmad::consumer_sync();  // every lane's accumulation is in s_acc
-        const int per_item = T * kTileRows;
-        if (tid == 0) {
-          const int led = (ge - gb - static_cast<int>(rank) + kClusterSize - 1) / kClusterSize;
-          expect_tx(&s_x_full, static_cast<uint32_t>(led > 0 ? led : 0) * kClusterSize * per_item * 4);
-        }
-        for (int i = tid * 4; i < (ge - gb) * per_item; i += kC * 4) {
-          const int jj = i / per_item;
-          const int rest = i - jj * per_item;
-          float *dst = s_exch + (static_cast<size_t>(jj / kClusterSize) * kClusterSize + rank) * per_item + rest;
-          st_async_v4(dst, static_cast<uint32_t>(jj % kClusterSize), *reinterpret_cast<const float4 *>(s_acc + i),
-                      &s_x_full);
-        }
-        // leaders load the row scales and bias of their tiles while the quarters land
-        float lead_scale[kLead], lead_bias[kLead];
-        float lead_h[kStep ? kLead : 1][kT];  // residual epilogues: h of the led rows, loaded early
-#pragma unroll
-        for (int sidx = 0; sidx < kLead; ++sidx) {
-          lead_scale[sidx] = 0.0f;
-          lead_bias[sidx] = 0.0f;
+          // ---- quarters -> leaders: asynchronous stores into their shared
+          // memory, counted on each leader's s_x_full
+          if (xg > 0 && !wait_cluster(&s_x_free, (xg - 1) & 1)) ok = false;
+          mmad::consumer_sync();  // every lane's accumulation is in s_acc
+          const int per_item = T * kTileRows;
+          if (tid == 0) {
+            const int led = (ge - gb - static_cast<int>(rank) + kClusterSize - 1) / kClusterSize;
+            expect_tx(&s_x_full, static_cast<uint32_t>(led > 0 ? led : 0) * kClusterSize * per_item * 4);
+          }
+          for (int i = tid * 4; i < (ge - gb) * per_item; i += kC * 4) {
+            const int jj = i / per_item;
+            const int rest = i - jj * per_item;
+            float *dst = s_exch + (static_cast<size_t>(jj / kClusterSize) * kClusterSize + rank) * per_item + rest;
+            st_async_v4(dst, static_cast<uint32_t>(jj % kClusterSize), *reinterpret_cast<const float4 *>(s_acc + i),
+                        &s_x_full);
+          }
+          // leaders load the row scales and bias of their tiles while the quarters land
+          float lead_scale[kLead], lead_bias[kLead];
+          float lead_h[kStep ? kLead : 1][kT];  // residual epilogues: h of the led rows, loaded early
+          int lead_slot[kPatch ? kLead : 1];    // int8 overlay rows: the led rows' overlay row index (-1: none)
+  #pragma unroll
+          for (int sidx = 0; sidx < kLead; ++sidx) {
+            lead_scale[sidx] = 0.0f;
+            lead_bias[sidx] = 0.0f;
+            if constexpr (kPatch) lead_slot[sidx] = -1;
+            if constexpr (kStep) {
+  #pragma unroll
+              for (int t = 0; t < kT; ++t) lead_h[sidx][t] = 0.0f;
+            }
+            const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+            if (jj < ge - gb && tid < kTileRows) {
+              const Item item = op.items[gb + jj];
+              const MemberDev &md = op.md[item.member];
+              const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
+              if (row < md.rows) {
+                lead_scale[sidx] = __ldg(md.row_scale + row);
+                if (md.bias != nullptr) lead_bias[sidx] = __ldg(md.bias + row);
+                if constexpr (kPatch) {
+                  if (md.overlay_slot != nullptr) lead_slot[sidx] = __ldg(md.overlay_slot + row);
+                }
+                if constexpr (kStep) {
+                  if (op_epi == NQB_EPI_RESIDUAL)
+  #pragma unroll
+                    for (int t = 0; t < kT; ++t)
+                      if (t < T) lead_h[sidx][t] = __ldcg(md.y + static_cast<int64_t>(t) * md.rows + row);
+                }
+              }
+            }
+          }
           if constexpr (kStep) {
-#pragma unroll
-            for (int t = 0; t < kT; ++t) lead_h[sidx][t] = 0.0f;
+            if (rms_pending) {  // the norm factors, read by the leader epilogue after the next consumer barrier
+              if (warp == 0) {
+  #pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                  const float ss = warp_sum(rms_part[t] + rms_next[t]);
+                  if (lane == 0 && t < T) s_rms[t] = rsqrtf(ss * gop.inv_n + gop.eps);
+                }
+              }
+              rms_pending = false;
+            }
           }
-          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
-          if (jj < ge - gb && tid < kTileRows) {
+          NQB_TRACE(kTraceSend);
+          if (!wait_cluster(&s_x_full, xg & 1)) ok = false;
+          NQB_TRACE(kTraceWaitQuarters);
+          // ---- leaders: fixed-order sum of the four quarters into registers,
+          // then release the exchange buffers before any global store
+          float vsum[kLead][kT];
+  #pragma unroll
+          for (int sidx = 0; sidx < kLead; ++sidx) {
+            const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+            const float *ex = s_exch + static_cast<size_t>(sidx) * kClusterSize * per_item;
+  #pragma unroll
+            for (int t = 0; t < kT; ++t) {
+              float v = 0.0f;
+              if (jj < ge - gb && t < T && tid < kTileRows) {
+  #pragma unroll
+                for (int q = 0; q < kClusterSize; ++q) v += ex[(q * T + t) * kTileRows + tid];
+              }
+              vsum[sidx][t] = v;
+            }
+          }
+          NQB_TRACE(kTraceSum);
+          mmad::consumer_sync();  // done reading this CTA's leader buffers
+          if (tid == 0)
+            for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive_relaxed(&s_x_free, r);
+          ++xg;
+          NQB_TRACE(kTraceRelease);
+          // ---- epilogue of the led tiles
+  #pragma unroll
+          for (int sidx = 0; sidx < kLead; ++sidx) {
+            const int jj = static_cast<int>(rank) + sidx * kClusterSize;
+            if (jj >= ge - gb) break;
             const Item item = op.items[gb + jj];
             const MemberDev &md = op.md[item.member];
-            const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
-            if (row < md.rows) {
-              lead_scale[sidx] = __ldg(md.row_scale + row);
-              if (md.bias != nullptr) lead_bias[sidx] = __ldg(md.bias + row);
-              if constexpr (kStep) {
-                if (op_epi == NQB_EPI_RESIDUAL)
-#pragma unroll
-                  for (int t = 0; t < kT; ++t)
-                    if (t < T) lead_h[sidx][t] = __ldcg(md.y + static_cast<int64_t>(t) * md.rows + row);
-              }
-            }
-          }
-        }
-        if constexpr (kStep) {
-          if (rms_pending) {  // the norm factors, read by the leader epilogue after the next consumer barrier
-            if (warp == 0) {
-#pragma unroll
-              for (int t = 0; t < kT; ++t) {
-                const float ss = warp_sum(rms_part[t]);
-                if (lane == 0 && t < T) s_rms[t] = rsqrtf(ss * gop.inv_n + gop.eps);
-              }
-            }
-            rms_pending = false;
-          }
-        }
-        NQB_TRACE(kTraceSend);
-        if (!wait_cluster(&s_x_full, xg & 1)) ok = false;
-        NQB_TRACE(kTraceWaitQuarters);
-        // ---- leaders: fixed-order sum of the four quarters into registers,
-        // then release the exchange buffers before any global store
-        float vsum[kLead][kT];
-#pragma unroll
-        for (int sidx = 0; sidx < kLead; ++sidx) {
-          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
-          const float *ex = s_exch + static_cast<size_t>(sidx) * kClusterSize * per_item;
-#pragma unroll
-          for (int t = 0; t < kT; ++t) {
-            float v = 0.0f;
-            if (jj < ge - gb && t < T && tid < kTileRows) {
-#pragma unroll
-              for (int q = 0; q < kClusterSize; ++q) v += ex[(q * T + t) * kTileRows + tid];
-            }
-            vsum[sidx][t] = v;
-          }
-        }
-        NQB_TRACE(kTraceSum);
-        mmad::consumer_sync();  // done reading this CTA's leader buffers
-        if (tid == 0)
-          for (uint32_t r = 0; r < kClusterSize; ++r) remote_arrive_relaxed(&s_x_free, r);
-        ++xg;
-        NQB_TRACE(kTraceRelease);
-        // ---- epilogue of the led tiles
-#pragma unroll
-        for (int sidx = 0; sidx < kLead; ++sidx) {
-          const int jj = static_cast<int>(rank) + sidx * kClusterSize;
-          if (jj >= ge - gb) break;
-          const Item item = op.items[gb + jj];
-          const MemberDev &md = op.md[item.member];
-          float outv[kT];  // stage-2 values for the fused epilogues
-#pragma unroll
-          for (int t = 0; t < kT; ++t) outv[t] = 0.0f;
-          if (tid < kTileRows) {
-            const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
-            if (row < md.rows) {
-#pragma unroll
-              for (int t = 0; t < kT; ++t) {
-                if (t >= T) break;
-                float v = vsum[sidx][t];
-                if (st == 0) {
-                  float f = lead_scale[sidx];
-                  if constexpr (kStep) {
-                    if (normed) f *= s_rms[t];
-                  }
-                  p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * f;
-                } else {
-                  v *= lead_scale[sidx];
-                  if (md.outlier_count > 0) {
-                    float sal = 0.0f;
-                    for (int64_t s = 0; s < md.outlier_count; ++s) {
-                      float w = load_as_float(md.outlier_values, row * md.outlier_count + s, md.outlier_value_dtype);
-                      if (md.outlier_scales != nullptr) w *= load_as_float(md.outlier_scales, s, md.outlier_scale_dtype);
-                      sal += load_as_float(op.x, static_cast<int64_t>(t) * op.n + md.outlier_indices[s], op.x_dtype) *
-                             w;
+            float outv[kT];  // stage-2 values for the fused epilogues
+  #pragma unroll
+            for (int t = 0; t < kT; ++t) outv[t] = 0.0f;
+            if (tid < kTileRows) {
+              const int64_t row = static_cast<int64_t>(item.tile) * kTileRows + tid;
+              if (row < md.rows) {
+  #pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                  if (t >= T) break;
+                  float v = vsum[sidx][t];
+                  if (st == 0) {
+                    float f = lead_scale[sidx];
+                    if constexpr (kStep) {
+                      if (normed) f *= s_rms[t];
                     }
-                    v += sal;
-                  }
-                  if constexpr (kPatch) {
-                    if (md.patch_rank > 0) {
-                      const float *pl = p.latent + static_cast<int64_t>(t) * op.latent_stride + md.patch_offset;
-                      float pv = 0.0f;
-                      for (int64_t q = 0; q < md.patch_rank; ++q)
-                        pv += load_as_float(md.patch_factor, row * md.patch_rank + q, md.patch_dtype) * __ldcg(pl + q);
-                      v += pv;
+                    p.latent[static_cast<int64_t>(t) * op.latent_stride + md.out_offset + row] = v * f;
+                  } else {
+                    v *= lead_scale[sidx];
+                    if (md.outlier_count > 0) {
+                      float sal = 0.0f;
+                      for (int64_t s = 0; s < md.outlier_count; ++s) {
+                        float w = load_as_float(md.outlier_values, row * md.outlier_count + s, md.outlier_value_dtype);
+                        if (md.outlier_scales != nullptr) w *= load_as_float(md.outlier_scales, s, md.outlier_scale_dtype);
+                        sal += load_as_float(op.x, static_cast<int64_t>(t) * op.n + md.outlier_indices[s], op.x_dtype) *
+                               w;
+                      }
+                      v += sal;
                     }
+                    if constexpr (kPatch) {
+                      if (md.patch_rank > 0) {
+                        const float *pl = p.latent + static_cast<int64_t>(t) * op.latent_stride + md.patch_offset;
+                        float pv = 0.0f;
+                        for (int64_t q = 0; q < md.patch_rank; ++q)
+                          pv += load_as_float(md.patch_factor, row * md.patch_rank + q, md.patch_dtype) * __ldcg(pl + q);
+                        v += pv;
+                      }
+                      // the row's int8 overlay value (formed in stage 1 by the side-row warps)
+                      if (lead_slot[sidx] >= 0) {
+                        const float *ov = p.latent + static_cast<int64_t>(t) * op.latent_stride + md.overlay_offset +
+                                          static_cast<int64_t>(lead_slot[sidx]) * op.ovl_segs;
+                        float o = 0.0f;
+                        for (int sg = 0; sg < op.ovl_segs; ++sg) o += __ldcg(ov + sg);
+                        v += o;
+                      }
+                    }
+                    if (kStep && op_epi != NQB_EPI_STORE)
+                      outv[t] = v + lead_bias[sidx];
+                    else
+                      md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
                   }
-                  if (kStep && op_epi != NQB_EPI_STORE)
-                    outv[t] = v + lead_bias[sidx];
-                  else
-                    md.y[static_cast<int64_t>(t) * md.rows + row] = v + lead_bias[sidx];
                 }
               }
             }
-          }
-          if constexpr (kStep) {
-            if (op_epi == NQB_EPI_RESIDUAL && tid < kTileRows)
-              residual_epilogue<kT>(gop, md, item.tile, outv, lead_h[kStep ? sidx : 0], T, s_epi + kT * kTileRows);
-            else if (op_epi == NQB_EPI_QK_ROPE && tid < kTileRows)
-              qk_rope_epilogue<kT>(gop, item.member, item.tile, outv, T, s_epi, s_epi + kT * kTileRows);
-          }
-          if (st == 1 && md.overlay_rows > 0) {
-            // int8 residual rows of this tile: all consumer threads compute each dot product
-            mmad::consumer_sync();
-            const int64_t first = static_cast<int64_t>(item.tile) * kTileRows;
-            const int64_t last = min(first + kTileRows, md.rows);
-            int64_t lo = 0, hi = md.overlay_rows;
-            while (lo < hi) {
-              const int64_t mid = (lo + hi) >> 1;
-              if (md.overlay_row_ids[mid] < first) lo = mid + 1; else hi = mid;
-            }
-            for (int64_t jr = lo; jr < md.overlay_rows && md.overlay_row_ids[jr] < last; ++jr) {
-              const int64_t orow = md.overlay_row_ids[jr];
-              const float oscale = load_as_float(md.overlay_scales, jr, md.overlay_scale_dtype);
-              const int8_t *rv = md.overlay_values + jr * op.n;
-              for (int t = 0; t < T; ++t) {
-                float part = 0.0f;
-                for (int64_t i = tid; i < op.n; i += kC)
-                  part += static_cast<float>(rv[i]) * load_as_float(op.x, static_cast<int64_t>(t) * op.n + i, op.x_dtype);
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-                if (lane == 0) s_red_f[warp] = part;
-                mmad::consumer_sync();
-                if (tid == 0) {
-                  float dot = 0.0f;
-#pragma unroll
-                  for (int w = 0; w < mmad::kWarps; ++w) dot += s_red_f[w];
-                  md.y[static_cast<int64_t>(t) * md.rows + orow] += dot * oscale;
-                }
-                mmad::consumer_sync();
-              }
+            if constexpr (kStep) {
+              if (op_epi == NQB_EPI_RESIDUAL && tid < kTileRows)
+                residual_epilogue<kT>(gop, md, item.tile, outv, lead_h[kStep ? sidx : 0], T, s_epi + kT * kTileRows);
+              else if (op_epi == NQB_EPI_QK_ROPE && tid < kTileRows)
+                qk_rope_epilogue<kT>(gop, item.member, item.tile, outv, T, s_epi, s_epi + kT * kTileRows);
             }
           }
         }
-      }
-      NQB_TRACE(kTraceEpilogue);
-      if constexpr (kPatch) {
-        if (st == 0 && op.patch_rows > 0) {
-          // this CTA's patch rows (info warp) are written before its barrier arrival
-          if (tid == 0 && !wait_local(&s_patch_done, patched & 1)) ok = false;
-          ++patched;
+        NQB_TRACE(kTraceEpilogue);
+        if constexpr (kPatch) {
+          if (st == 0 && op.side_rows > 0) {
+            // this CTA's side rows (side warps) are written before its barrier arrival
+            if (tid == 0 && !wait_local(&s_patch_done, patched & 1)) ok = false;
+            ++patched;
+          }
         }
+        if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g), &s_info_free[g & 1]);
+        NQB_TRACE(kTraceGridBarrier);
+        NQB_TRACE_FLUSH(g);
       }
-      if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g), &s_info_free[g & 1]);
-      NQB_TRACE(kTraceGridBarrier);
-      NQB_TRACE_FLUSH(g);
     }
-  }
 
-  if (!ok) record_error(NQB_ERR_TIMEOUT);
-  // every CTA stays until its peers have made their last remote arrivals
-  cluster_sync();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t finished = atomicAdd(p.counters + 1, 1u);
-    if (finished == gridDim.x - 1) {  // the last CTA zeroes the counters for the next run
-      p.counters[0] = 0;
-      p.counters[1] = 0;
-      __threadfence();
-    }
+    finish_cta(p, ok);
   }
 }
 
@@ -1761,6 +1881,10 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       if (d.patch_rank < 0 || d.patch_rank > (1ll << 20) ||
           (d.patch_rank > 0 && (d.patch_left == nullptr || d.patch_right == nullptr || !is_float_dtype(d.patch_dtype))))
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has an invalid low-rank patch", i, k);
+      if (d.overlay_rows < 0 || d.overlay_rows > d.out_features ||
+          (d.overlay_rows > 0 && (d.overlay_row_ids == nullptr || d.overlay_values == nullptr ||
+                                  d.overlay_scales == nullptr || !is_float_dtype(d.overlay_scale_dtype))))
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has invalid int8 overlay rows", i, k);
       if (d.coded_right_tiles != nullptr &&
           (d.coded_codebook == nullptr || d.coded_free_rows <= 0 || d.coded_free_rows >= d.rank ||
            reinterpret_cast<uintptr_t>(d.coded_right_tiles) % 16 || reinterpret_cast<uintptr_t>(d.coded_codebook) % 16))
@@ -1772,9 +1896,10 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     }
     if (!tc_eligible(o.layers, o.count, swiglu ? NQB_F32 : o.x_dtype, tokens))
       return fail(NQB_ERR_UNSUPPORTED, "op %d does not take the tensor-core decode path", i);
-    int64_t patch_total = 0;
-    for (int k = 0; k < o.count; ++k) patch_total += o.layers[k].patch_rank;
-    latent_cols = std::max(latent_cols, rank_total + patch_total);
+    int64_t side_total = 0;  // patch latents and overlay row segments after the ranks
+    const int64_t segs = (o.layers[0].in_features + kOverlaySegCols - 1) / kOverlaySegCols;
+    for (int k = 0; k < o.count; ++k) side_total += o.layers[k].patch_rank + o.layers[k].overlay_rows * segs;
+    latent_cols = std::max(latent_cols, rank_total + side_total);
     if (e != nullptr) {
       for (int k = 0; k < o.count; ++k)
         if (o.layers[k].patch_rank > 0 || o.layers[k].coded_right_tiles != nullptr || o.layers[k].overlay_rows > 0)
@@ -1825,8 +1950,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   };
   struct MemberScales {
     size_t pre, mid, post, bias;
+    size_t slot = SIZE_MAX;  // int8 overlay rows: [out_features] int32 row -> overlay row index (-1: none)
   };
   std::vector<MemberScales> member_scales;
+  struct SlotMap {
+    size_t at;
+    std::vector<int32_t> slots;
+  };
+  std::vector<SlotMap> slot_maps;
   struct OpScales {
     size_t norm_weight = SIZE_MAX, q_norm = SIZE_MAX, k_norm = SIZE_MAX;
   };
@@ -1849,6 +1980,25 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       ms.mid = add_copy(d.scale_mid, d.scale_dtype, d.rank);
       ms.post = add_copy(d.scale_post, d.scale_dtype, d.out_features);
       ms.bias = add_copy(d.bias, d.bias_dtype, d.out_features);
+      if (d.overlay_rows > 0) {
+        // the overlay's row ids (device) -> a per-row index map owned by the program
+        std::vector<int32_t> ids(static_cast<size_t>(d.overlay_rows));
+        if (cudaMemcpy(ids.data(), d.overlay_row_ids, ids.size() * sizeof(int32_t), cudaMemcpyDeviceToHost) !=
+            cudaSuccess) {
+          cudaGetLastError();
+          return fail(NQB_ERR_CUDA, "op %d member %d: reading the overlay row ids failed", i, k);
+        }
+        SlotMap map{(scale_floats + 63) & ~size_t(63), std::vector<int32_t>(static_cast<size_t>(d.out_features), -1)};
+        for (size_t j = 0; j < ids.size(); ++j) {
+          if (ids[j] < 0 || ids[j] >= d.out_features || (j > 0 && ids[j] <= ids[j - 1]))
+            return fail(NQB_ERR_INVALID_ARGUMENT,
+                        "op %d member %d: overlay row ids must be strictly increasing and below out_features", i, k);
+          map.slots[ids[j]] = static_cast<int32_t>(j);
+        }
+        scale_floats = map.at + map.slots.size();
+        ms.slot = map.at;
+        slot_maps.push_back(std::move(map));
+      }
       member_scales.push_back(ms);
     }
   float *scales = nullptr;
@@ -1860,6 +2010,13 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const int64_t blocks = std::min<int64_t>((c.n + 255) / 256, 1024);
     to_f32_kernel<<<static_cast<unsigned>(blocks), 256>>>(c.src, c.dtype, c.n, scales + c.offset);
   }
+  for (const SlotMap &m : slot_maps)
+    if (cudaMemcpy(scales + m.at, m.slots.data(), m.slots.size() * sizeof(int32_t), cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(scales);
+      return fail(NQB_ERR_CUDA, "copying the overlay row maps failed");
+    }
   // residual-stream inputs: the norm weight folds into each member's input scale (pre := pre * w)
   for (int i = 0, mi = 0; i < op_count; ++i) {
     const bool attention = ops[i].ext != nullptr && ops[i].ext->kind == NQB_OP_ATTENTION;
@@ -1922,7 +2079,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     for (int k = 0; k < o.count; ++k) {  // patch latents after the ranks
       od.s[0][k].patch_offset = od.s[1][k].patch_offset = offset;
       offset += o.layers[k].patch_rank;
-      od.patch_rows += static_cast<int32_t>(o.layers[k].patch_rank);
+      od.side_rows += static_cast<int32_t>(o.layers[k].patch_rank);
+    }
+    od.ovl_segs = static_cast<int32_t>((od.n + kOverlaySegCols - 1) / kOverlaySegCols);
+    for (int k = 0; k < o.count; ++k) {  // then the int8 overlay rows' partial dot products
+      const MemberScales &ms = member_scales[member_index - o.count + k];
+      if (o.layers[k].overlay_rows <= 0) continue;
+      od.s[1][k].overlay_offset = offset;
+      od.s[1][k].overlay_slot = reinterpret_cast<const int32_t *>(scales + ms.slot);
+      offset += o.layers[k].overlay_rows * od.ovl_segs;
+      od.side_rows += static_cast<int32_t>(o.layers[k].overlay_rows * od.ovl_segs);
     }
     od.latent_stride = offset;
   }
@@ -1931,13 +2097,21 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   NQB_CUDA(cudaGetDevice(&device), "cudaGetDevice");
   bool patch = false, mixed = false;
   for (int i = 0; i < op_count; ++i) {
-    patch = patch || opdev[i].patch_rows > 0;
+    patch = patch || opdev[i].side_rows > 0;
     for (int k = 0; k < opdev[i].count; ++k) mixed = mixed || opdev[i].s[0][k].coded_tiles != nullptr;
   }
   if (step && (patch || mixed)) return fail(NQB_ERR_UNSUPPORTED, "decoder-step programs take no patch or mixed-V tiles");
   const SmemPlan sp = smem_plan(bucket, mixed);
   if (sp.off_cb % 16) return fail(NQB_ERR_UNSUPPORTED, "codebook buffer is misaligned");
   const void *fn = kernel_for(bucket, patch, mixed, step);
+  {
+    // the kernel's register split assumes the launch count (kLaunchRegs)
+    cudaFuncAttributes attr;
+    NQB_CUDA(cudaFuncGetAttributes(&attr, fn), "cudaFuncGetAttributes");
+    if (attr.numRegs != kLaunchRegs)
+      return fail(NQB_ERR_UNSUPPORTED, "program kernel built with %d registers; its register split needs %d",
+                  attr.numRegs, kLaunchRegs);
+  }
   NQB_CHECK(ensure_dynamic_smem(fn, static_cast<int>(sp.total)));
   int sms = 0;
   NQB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
