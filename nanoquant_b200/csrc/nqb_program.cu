@@ -379,12 +379,6 @@ __device__ __forceinline__ void prefetch_stage(const Params &p, int g, int lane)
   for (int i = b + lane; i < e; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.pf_lines[i]));
 }
 
-__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *ptr) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
-  return v;
-}
-
 // Until the grid-barrier counter reaches `target`; false after `limit` polls
 // (or at once when a grid barrier has failed).
 __device__ __forceinline__ bool wait_counter(const uint32_t *counter, uint32_t target, uint32_t limit) {
@@ -441,6 +435,8 @@ __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index, ui
     // release: this CTA's stores (ordered before this thread by the named
     // barrier) are visible to every CTA that acquires the count
     red_release_gpu_add(counter, 1);
+    // acquire polls (relaxed polls with one acquire fence at the end
+    // measured slower on B200)
     const uint32_t target = (index + 1) * ctas + p.barrier_skew;
     uint32_t polls = 0;
     while (ld_acquire_gpu(counter) < target) {
@@ -2175,14 +2171,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     const OpDev &op = opdev[g >> 1];
     const int st = g & 1;
     if (op.step.kind == NQB_OP_ATTENTION && st == 0) {
-      // each CTA's unit (kv head, key split): its K and V rows go on the L2
-      // prefetch list of the stage two ahead of this one (the rows before this
-      // step's tokens do not change during the program)
+      // each CTA's unit (kv head, key split): its K and V rows that do not
+      // stream through the sign ring go on the L2 prefetch list of the stage
+      // two ahead of this one (the rows before this step's tokens do not
+      // change during the program)
       const int target = std::max(0, g - 2);
       for (int c = 0; c < ctas && c < op.step.kv_heads * op.step.att_splits; ++c) {
         const int kvh = c / op.step.att_splits, spl = c % op.step.att_splits;
-        const int64_t k0 = static_cast<int64_t>(spl) * op.step.att_chunk;
-        const int64_t k1 = std::min(k0 + op.step.att_chunk, op.step.position + tokens);
+        const int64_t k0 = static_cast<int64_t>(spl) * op.step.att_chunk + 16 * att_unit_ring_blocks(op.step, spl);
+        const int64_t k1 = std::min(static_cast<int64_t>(spl) * op.step.att_chunk + op.step.att_chunk,
+                                    op.step.position + tokens);
         if (k1 <= k0) continue;
         const int64_t off = (static_cast<int64_t>(kvh) * op.step.cache_len + k0) * kAttHd;
         std::vector<uint64_t> &lines = pf[static_cast<size_t>(target) * ctas + c];
