@@ -725,8 +725,8 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // blocks through the sign ring (K block, then V block; the producer streams
 // them with the sign slices, across the stage barriers), so most K/V reads
 // come from shared memory; the remaining rows (this step's, and any past the
-// ring's share) are read from global memory.  Every consumer warp waits for
-// the unit's ring slots first and hands them back after the last token.
+// ring's share) are read from global memory.  The consumers wait for the
+// unit's ring slots first and every warp hands them back after the last token.
 // Inlined, like attention_join: a call would make the kernel keep its stage
 // loop's state across the call (spills), slowing every linear stage.
 __device__ __forceinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
@@ -756,11 +756,14 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = p.ring;
   const int nb = att_unit_ring_blocks(op, sp);
-  for (int j = 0; j < 2 * nb; ++j) {
-    const int sj = (slot + j) % R;
-    const uint32_t ph = phase + static_cast<uint32_t>((slot + j) / R);
+  // one consumer thread per ring slot of the unit waits, then a consumer
+  // barrier: every warp polling every slot in turn cost microseconds
+  if (tid < 2 * nb) {
+    const int sj = (slot + tid) % R;
+    const uint32_t ph = phase + static_cast<uint32_t>((slot + tid) / R);
     if (!wait_local(&s_full[sj], ph & 1)) ok = false;
   }
+  mmad::consumer_sync();
   NQB_ATT_TRACE(kTraceWaitSigns);
   const int64_t ring_rows = 16 * static_cast<int64_t>(nb);
   const float scale = rsqrtf(static_cast<float>(kAttHd));
