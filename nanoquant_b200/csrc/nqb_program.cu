@@ -197,6 +197,13 @@ struct Params {
   uint32_t off_cb;              // mixed-V codebooks [kMaxMembersTc][1024]
   uint32_t off_epi;             // decoder-step epilogue scratch: [tokens][128] + [4][tokens] floats
   float *att_part;              // attention partials [tokens * q_heads][splits][kAttRow]
+  // 8 and 16 tokens: each linear stage's activation chunks are quantised once,
+  // by all CTAs, into qbuf (one slot of qunit_bytes per chunk), before a grid
+  // barrier; the stage's consumers then copy the digits instead of
+  // re-quantising them in every cluster
+  uint8_t *qbuf;
+  int32_t qunit_bytes;
+  const int32_t *bar_end;       // [stages] index of the grid barrier that ends each stage
 };
 
 __device__ int g_prog_error;
@@ -424,14 +431,15 @@ __device__ __forceinline__ void stage_info_copy(const Params &p, int g, uint32_t
 }
 
 // Grid barrier number `index` over every CTA of the grid (consumer warps;
-// thread 0 adds and polls).  On entry every consumer is done with the stage's
-// tables: thread 0 first hands their buffer back (`info_free`).
+// thread 0 adds and polls).  At a stage's end every consumer is done with the
+// stage's tables: thread 0 first hands their buffer back (`info_free`; NULL
+// for the barrier after a pre-quantisation pass).
 __device__ __forceinline__ void grid_barrier(const Params &p, uint32_t index, uint64_t *info_free) {
   uint32_t *counter = p.counters;
   const uint32_t ctas = gridDim.x;
   mmad::consumer_sync();
   if (threadIdx.x == 0) {
-    mbar_arrive_cta(info_free);
+    if (info_free != nullptr) mbar_arrive_cta(info_free);
     // release: this CTA's stores (ordered before this thread by the named
     // barrier) are visible to every CTA that acquires the count
     red_release_gpu_add(counter, 1);
@@ -642,6 +650,11 @@ static_assert(mmad::kThreads * kConsumerRegs + (kBlockThreads - mmad::kThreads) 
               "register split exceeds the launch's registers");
 static_assert(32 * (2 * kConsumerRegs + kHelperRegs) <= 16384, "register split exceeds a sub-partition");
 
+// Instances whose linear stages quantise their activation chunks once, over
+// the grid, before the stage (a grid barrier more per stage; each cluster
+// re-quantising every chunk itself costs more from 8 tokens on).
+__host__ __device__ constexpr bool pre_quantised(int bucket) { return bucket >= 8; }
+
 // Slices quantised at once (B fragments and activations held for them).
 __host__ __device__ constexpr int slices_per_chunk(int bucket) {
   return bucket <= 2 ? 16 : (bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2));
@@ -650,6 +663,47 @@ __host__ __device__ constexpr int slices_per_chunk(int bucket) {
 // Tiles each CTA leads per exchange group: 16 KB of exchange buffer.
 __host__ __device__ constexpr int leader_slots(int bucket) {
   return 16384 / (kClusterSize * bucket * kTileRows * 4) > 1 ? 16384 / (kClusterSize * bucket * kTileRows * 4) : 1;
+}
+
+// Pre-quantised stages (8 and 16 tokens): the stage's activation chunks in a
+// fixed order -- member k, then K quarter q (slices [ks q / 4, ks (q + 1) / 4)),
+// then chunks of sc slices -- are units 0, 1, ..; unit u's digits, exponents
+// and digit sums go to qbuf slot u.
+__host__ __device__ inline int quarter_chunks(int ks, int q, int sc) {
+  const int lo = ks * q / kClusterSize, hi = ks * (q + 1) / kClusterSize;
+  return (hi - lo + sc - 1) / sc;
+}
+
+__host__ __device__ inline int member_chunks(int ks, int sc) {
+  int n = 0;
+  for (int q = 0; q < kClusterSize; ++q) n += quarter_chunks(ks, q, sc);
+  return n;
+}
+
+// The unit of member k's quarter q starting at slice c0.
+__device__ __forceinline__ int unit_of(const StageInfo &op, int k, int q, int c0, int sc) {
+  int u = 0;
+  for (int m = 0; m < k; ++m) u += member_chunks(op.md[m].ks, sc);
+  for (int r = 0; r < q; ++r) u += quarter_chunks(op.md[k].ks, r, sc);
+  return u + (c0 - op.md[k].ks * q / kClusterSize) / sc;
+}
+
+// Unit u -> member, first slice and slice count; false past the stage's units.
+__device__ __forceinline__ bool unit_at(const StageInfo &op, int u, int sc, int &k, int &c0, int &nst) {
+  for (k = 0; k < kMaxMembersTc; ++k) {
+    const int ks = op.md[k].ks;
+    for (int q = 0; q < kClusterSize; ++q) {
+      const int n = quarter_chunks(ks, q, sc);
+      if (u < n) {
+        const int lo = ks * q / kClusterSize, hi = ks * (q + 1) / kClusterSize;
+        c0 = lo + u * sc;
+        nst = min(sc, hi - c0);
+        return true;
+      }
+      u -= n;
+    }
+  }
+  return false;
 }
 
 // Advances (j0, j1, c0, hi) to the next (member run, chunk) unit of the
@@ -1050,6 +1104,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
   constexpr int kSets = mmad::acc_sets(kNT);
   constexpr int kQPT = mmad::quads_per_thread(slices_per_chunk(kT));
   constexpr bool kPrefetchUnits = kT == 1;  // two chunks of activations in registers only at one token
+  constexpr bool kPreQ = pre_quantised(kT);  // linear stages quantise their activation chunks once, grid-wide
   constexpr int kLead = leader_slots(kT);  // tiles this CTA leads per exchange group
   constexpr int kC = mmad::kThreads;  // consumer threads
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -1146,7 +1201,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           // stage g - 1's inputs are complete; then, even when that grid wait
           // gave up, this CTA's consumers are done with the buffer
           if (lane == 0) {
-            if (!wait_counter(p.counters, static_cast<uint32_t>(g - 1) * gridDim.x + p.barrier_skew, p.barrier_limit))
+            if (!wait_counter(p.counters, static_cast<uint32_t>(p.bar_end[g - 2] + 1) * gridDim.x + p.barrier_skew,
+                              p.barrier_limit))
               ok = false;
             if (!wait_local(&s_info_free[g & 1], ((g >> 1) - 1) & 1)) ok = false;
           }
@@ -1185,7 +1241,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         if (op.side_rows <= 0) continue;
         if (g >= 2) {
           if (lane == 0 &&
-              !wait_counter(p.counters, static_cast<uint32_t>(g) * gridDim.x + p.barrier_skew, p.barrier_limit))
+              !wait_counter(p.counters, static_cast<uint32_t>(p.bar_end[g - 1] + 1) * gridDim.x + p.barrier_skew,
+                            p.barrier_limit))
             ok = false;
           __syncwarp();
         }
@@ -1293,6 +1350,73 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             mmad::slice_mmas<kNT>(w, smem_b + static_cast<size_t>(sl) * mmad::slice_frag_bytes(kNT), lane, d);
           }
         };
+        // one chunk of this stage's activations -> B fragments in smem_b, with
+        // per-token exponents e and digit sums Q
+        auto quantize_input = [&](const MemberDev &md, int c0, int nst, int (&e)[kT], long long (&Q)[kT]) {
+          const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+          if (st == 1) {
+            const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          } else if (op.x_dtype == NQB_X_SWIGLU) {
+            const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2), md.pre,
+                                        op.n, k0, md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          } else if (op.x_dtype == NQB_X_GEGLU) {
+            const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2), md.pre,
+                                       op.n, k0, md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          } else if (op.x_dtype == NQB_BF16) {
+            const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
+                                                  md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          } else if (op.x_dtype == NQB_F16) {
+            const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          } else {
+            const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
+            mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
+          }
+        };
+        const uint32_t q_frag = static_cast<uint32_t>(p.sc) * mmad::slice_frag_bytes(kNT);  // e, then Q follow
+        if constexpr (kPreQ) {
+          if (op_kind == NQB_OP_LINEAR) {
+            // ---- the stage's activation chunks, quantised once over the grid
+            // (unit u by CTA u mod grid), then a grid barrier
+            int k = 0, c0 = 0, nst = 0;
+            for (int u = cta; unit_at(op, u, p.sc, k, c0, nst); u += static_cast<int>(gridDim.x)) {
+              int e[kT];
+              long long Q[kT];
+              quantize_input(op.md[k], c0, nst, e, Q);  // ends with a consumer barrier after the fragment writes
+              uint8_t *dst = p.qbuf + static_cast<size_t>(u) * p.qunit_bytes;
+              const uint32_t fb = static_cast<uint32_t>(nst) * mmad::slice_frag_bytes(kNT);
+              for (uint32_t i = static_cast<uint32_t>(tid) * 16; i < fb; i += kC * 16)
+                *reinterpret_cast<uint4 *>(dst + i) = *reinterpret_cast<const uint4 *>(smem_b + i);
+              if (tid == 0) {
+#pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                  reinterpret_cast<int32_t *>(dst + q_frag)[t] = e[t];
+                  reinterpret_cast<long long *>(dst + q_frag + 4 * kT)[t] = Q[t];
+                }
+              }
+            }
+            grid_barrier(p, static_cast<uint32_t>(p.bar_end[g] - 1), nullptr);
+            NQB_TRACE(kTraceQuantise);
+          }
+        }
+        // this CTA's pre-quantised unit u: fragments -> smem_b, e and Q
+        auto load_quantised = [&](int u, int nst, int (&e)[kT], long long (&Q)[kT]) {
+          mmad::consumer_sync();  // every warp is done with the previous chunk's fragments
+          const uint8_t *src = p.qbuf + static_cast<size_t>(u) * p.qunit_bytes;
+          const uint32_t fb = static_cast<uint32_t>(nst) * mmad::slice_frag_bytes(kNT);
+          for (uint32_t i = static_cast<uint32_t>(tid) * 16; i < fb; i += kC * 16)
+            *reinterpret_cast<uint4 *>(smem_b + i) = __ldcg(reinterpret_cast<const uint4 *>(src + i));
+#pragma unroll
+          for (int t = 0; t < kT; ++t) {
+            e[t] = __ldcg(reinterpret_cast<const int32_t *>(src + q_frag) + t);
+            Q[t] = __ldcg(reinterpret_cast<const long long *>(src + q_frag + 4 * kT) + t);
+          }
+          mmad::consumer_sync();
+        };
         for (int gb = ib; gb < ie; gb += p.group) {
           const int ge = min(gb + p.group, ie);
           for (int i = tid; i < (ge - gb) * T * kTileRows; i += kC) s_acc[i] = 0.0f;
@@ -1399,32 +1523,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
               const int hi = md.ks * (static_cast<int>(rank) + 1) / kClusterSize;
               for (int c0 = lo; c0 < hi; c0 += p.sc) {
                 const int nst = min(p.sc, hi - c0);
-                const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
                 int e[kT];
                 long long Q[kT];
                 NQB_TRACE(kTraceTables);
-                if (st == 1) {
-                  const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                } else if (op.x_dtype == NQB_X_SWIGLU) {
-                  const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
-                                              md.pre, op.n, k0, md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                } else if (op.x_dtype == NQB_X_GEGLU) {
-                  const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
-                                             md.pre, op.n, k0, md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                } else if (op.x_dtype == NQB_BF16) {
-                  const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
-                                                        md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                } else if (op.x_dtype == NQB_F16) {
-                  const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                } else {
-                  const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
-                  mmad::quantize_chunk<kT, kQPT>(ld, nst, T, smem_b, s_sc, e, Q);
-                }
+                if constexpr (kPreQ)
+                  load_quantised(unit_of(op, mi, static_cast<int>(rank), c0, p.sc), nst, e, Q);
+                else
+                  quantize_input(md, c0, nst, e, Q);
                 NQB_TRACE(kTraceQuantise);
                 for (int j = j0; j < j1; ++j) {
                   int32_t d[kSets][kNT][4];
@@ -1623,7 +1728,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             ++patched;
           }
         }
-        if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(g), &s_info_free[g & 1]);
+        if (g + 1 < p.stages) grid_barrier(p, static_cast<uint32_t>(p.bar_end[g]), &s_info_free[g & 1]);
         NQB_TRACE(kTraceGridBarrier);
         NQB_TRACE_FLUSH(g);
       }
@@ -1679,6 +1784,7 @@ struct nqb_program {
   bool mixed = false;  // runs the coded mixed-V instance
   bool step = false;   // runs the decoder-step instance
   size_t att_part_bytes = 0;  // attention partials after the latent in the workspace
+  size_t qbuf_bytes = 0;      // pre-quantised activation chunks after the partials
   int ctas = 0;
   int clusters = 0;
   int smem = 0;
@@ -2272,6 +2378,26 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     }
   }
   stage_items.back() = static_cast<int32_t>(items.size());
+  // grid barriers: pre-quantised instances add one before every linear stage
+  // (index bar_end[g] - 1), and every stage but the last ends with bar_end[g]
+  const bool pre_q = pre_quantised(bucket);
+  const int32_t qunit_bytes = static_cast<int32_t>(
+      align_up(static_cast<size_t>(sp.sc) * mmad::slice_frag_bytes(mmad::n_tiles(bucket)) + 12u * bucket, 16));
+  size_t qbuf_bytes = 0;
+  std::vector<int32_t> bar_end(stages);
+  {
+    int32_t index = 0;
+    for (int g = 0; g < stages; ++g) {
+      const OpDev &op = opdev[g >> 1];
+      if (pre_q && op.step.kind == NQB_OP_LINEAR) {
+        ++index;
+        size_t units = 0;
+        for (int k = 0; k < op.count; ++k) units += static_cast<size_t>(member_chunks(op.s[g & 1][k].ks, sp.sc));
+        qbuf_bytes = std::max(qbuf_bytes, units * static_cast<size_t>(qunit_bytes));
+      }
+      bar_end[g] = index++;
+    }
+  }
   std::vector<int64_t> slice_begin(ctas);
   std::vector<int32_t> slice_count(ctas);
   std::vector<uint64_t> flat;
@@ -2301,7 +2427,8 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   const size_t b_count = section(sizeof(int32_t) * ctas);
   const size_t b_pfb = section(sizeof(int32_t) * pf_begin.size());
   const size_t b_pfl = section(sizeof(uint64_t) * pf_lines.size());
-  const size_t total = b_ops + b_si + b_items + b_addrs + b_begin + b_count + b_pfb + b_pfl;
+  const size_t b_bar = section(sizeof(int32_t) * bar_end.size());
+  const size_t total = b_ops + b_si + b_items + b_addrs + b_begin + b_count + b_pfb + b_pfl + b_bar;
   nqb_program *prog = new (std::nothrow) nqb_program();
   if (prog == nullptr) {
     cudaFree(scales);
@@ -2334,6 +2461,8 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   pp.slice_count = static_cast<const int32_t *>(put(slice_count.data(), sizeof(int32_t) * ctas, b_count));
   pp.pf_begin = static_cast<const int32_t *>(put(pf_begin.data(), sizeof(int32_t) * pf_begin.size(), b_pfb));
   pp.pf_lines = static_cast<const uint64_t *>(put(pf_lines.data(), sizeof(uint64_t) * pf_lines.size(), b_pfl));
+  pp.bar_end = static_cast<const int32_t *>(put(bar_end.data(), sizeof(int32_t) * bar_end.size(), b_bar));
+  pp.qunit_bytes = qunit_bytes;
   const cudaError_t copy_status = cudaDeviceSynchronize();
   if (copy_status != cudaSuccess) {
     cudaFree(prog->arena);
@@ -2362,6 +2491,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   prog->smem = static_cast<int>(sp.total);
   prog->latent_bytes = align_up(static_cast<size_t>(tokens) * latent_cols * sizeof(float), 256);
   prog->att_part_bytes = align_up(att_floats * sizeof(float), 256);
+  prog->qbuf_bytes = align_up(qbuf_bytes, 256);
   prog->step = step;
   pp.off_epi = sp.off_epi;
   *program = prog;
@@ -2370,7 +2500,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
 
 int nqb_program_workspace_bytes(const nqb_program *program, size_t *bytes) {
   if (program == nullptr || bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program or bytes is NULL");
-  *bytes = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes;
+  *bytes = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes + program->qbuf_bytes;
   return ok();
 }
 
@@ -2386,7 +2516,7 @@ static std::atomic<uint32_t> g_barrier_limit{0};
 static int launch_program(const nqb_program *program, void *workspace, size_t workspace_bytes, void *stream,
                           bool dependent) {
   if (program == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "program is NULL");
-  const size_t need = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes;
+  const size_t need = kCounterRegionBytes + program->latent_bytes + program->att_part_bytes + program->qbuf_bytes;
   if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(NQB_ERR_WORKSPACE, "program workspace needs %zu bytes aligned to 256, got %zu", need, workspace_bytes);
   Params params = program->params;
@@ -2394,6 +2524,9 @@ static int launch_program(const nqb_program *program, void *workspace, size_t wo
   params.latent = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes);
   params.att_part =
       reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegionBytes + program->latent_bytes);
+  params.qbuf = program->qbuf_bytes > 0 ? static_cast<uint8_t *>(workspace) + kCounterRegionBytes +
+                                              program->latent_bytes + program->att_part_bytes
+                                        : nullptr;
   const uint32_t limit = g_barrier_limit.load();
   params.barrier_limit = limit != 0 ? limit : kBarrierSpinLimit;
   params.barrier_skew = program->barrier_skew;

@@ -40,7 +40,7 @@ def _check(got: torch.Tensor, x: torch.Tensor, state) -> None:
     np.testing.assert_allclose(got.cpu().numpy(), expected, rtol=rtol, atol=atol)
 
 
-@pytest.mark.parametrize("tokens", (1, 3, 16))
+@pytest.mark.parametrize("tokens", (1, 3, 8, 11, 16))
 def test_program_chain_matches_oracle(tokens: int) -> None:
     backend = CudaPackedSm100Backend()
     g = torch.Generator().manual_seed(tokens)
