@@ -222,7 +222,7 @@ template <int kT, int kQPT, typename Loader>
 __device__ __forceinline__ void load_chunk(const Loader &src, int nst, int T, ChunkValues<kT, kQPT> &cv) {
   const int tid = threadIdx.x;
   const int nquads = nst * 64;
-  if constexpr (kT <= 2 && Loader::kTwoPhase) {
+  if constexpr (kT >= 4 || Loader::kTwoPhase) {
     float scl[kQPT][4];
     typename Loader::Raw raw[kQPT][4][kT];
 #pragma unroll
@@ -351,6 +351,120 @@ __device__ __forceinline__ void quantize_loaded(const ChunkValues<kT, kQPT> &cv,
 }
 
 // load_chunk then quantize_loaded.
+// quantize_chunk for the kG tokens t0 .. t0 + kG - 1 of a kT-token instance
+// (two digits per token, kG x 2 = 4 N columns: one half of an N tile): the
+// same exponents, digits and digit sums as quantize_chunk gives those tokens,
+// written to the same fragment positions.  Used by the grid-wide
+// pre-quantisation pass, which splits a chunk's tokens over several CTAs.
+template <int kT, int kG, int kQPT, typename Loader>
+__device__ __forceinline__ void quantize_tokens(const Loader &src, int nst, int t0, int T, uint8_t *smem_b,
+                                                Scratch<kT> &sc, int (&e)[kG], long long (&Q)[kG]) {
+  constexpr int kNT = n_tiles(kT);
+  constexpr int kD = digits_for(kT);
+  static_assert(kD * kG == 4, "a token group fills half an N tile");
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nquads = nst * 64;
+  float scl[kQPT][4];
+  typename Loader::Raw raw[kQPT][4][kG];
+#pragma unroll
+  for (int i = 0; i < kQPT; ++i) {
+    const int qd = tid + i * kThreads;
+    const int sl = qd >> 6, r = qd & 63;
+    const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
+    const int c0 = sl * kSliceCols + 32 * wi + j + 4 * s;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      scl[i][b] = qd < nquads ? src.scale(c0 + 8 * b) : 0.0f;
+#pragma unroll
+      for (int t = 0; t < kG; ++t)
+        raw[i][b][t] = (qd < nquads && t0 + t < T) ? src.fetch(t0 + t, c0 + 8 * b) : typename Loader::Raw{};
+    }
+  }
+  float v[kQPT][4][kG];
+  float mx[kG];
+#pragma unroll
+  for (int t = 0; t < kG; ++t) mx[t] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kQPT; ++i)
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+#pragma unroll
+      for (int t = 0; t < kG; ++t) {
+        v[i][b][t] = src.finish(raw[i][b][t], scl[i][b]);
+        mx[t] = fmaxf(mx[t], fabsf(v[i][b][t]));
+      }
+#pragma unroll
+  for (int t = 0; t < kG; ++t) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx[t] = fmaxf(mx[t], __shfl_xor_sync(0xffffffffu, mx[t], off));
+    if (lane == 0) sc.red_f[warp * kT + t] = mx[t];
+  }
+  consumer_sync();
+  long long qs[kG];
+#pragma unroll
+  for (int t = 0; t < kG; ++t) {
+    float m = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, sc.red_f[w * kT + t]);
+    int ex = 0, et = 0;
+    if (m > 0.0f && isfinite(m)) {
+      frexpf(m, &ex);  // m < 2^ex
+      et = min(fixed_bits(kT) - ex, 126);
+    }
+    e[t] = et;
+    qs[t] = 0;
+  }
+#pragma unroll
+  for (int i = 0; i < kQPT; ++i) {
+    const int qd = tid + i * kThreads;
+    if (qd < nquads) {
+      const int sl = qd >> 6, r = qd & 63;
+      const int wi = r >> 3, j = (r >> 1) & 3, s = r & 1;
+      const int tig = wi & 3, hi = wi >> 2;
+      const int kb = j * 2 + s;
+#pragma unroll
+      for (int t = 0; t < kG; ++t) {
+        if (t0 + t < T) {
+          const float scale = tc::exp2_int(e[t]);
+          int32_t q[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            q[b] = __float2int_rn(v[i][b][t] * scale);
+            qs[t] += q[b];
+          }
+          uint32_t digits[kD];
+          split_digits_n<kD>(q, digits);
+#pragma unroll
+          for (int d = 0; d < kD; ++d) {
+            const int n = kD * (t0 + t) + d;
+            const int nt = n >> 3, gg = n & 7;
+            const uint32_t offset =
+                ((static_cast<uint32_t>(sl) * 8 + kb) * kNT + nt) * kFragBytes + (gg * 4 + tig) * 8 + hi * 4;
+            *reinterpret_cast<uint32_t *>(smem_b + offset) = digits[d];
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kG; ++t) {
+    long long x = qs[t];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+    if (lane == 0) sc.red_q[warp * kT + t] = x;
+  }
+  consumer_sync();
+#pragma unroll
+  for (int t = 0; t < kG; ++t) {
+    long long x = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) x += sc.red_q[w * kT + t];
+    Q[t] = x;
+  }
+}
+
 template <int kT, int kQPT, typename Loader>
 __device__ __forceinline__ void quantize_chunk(const Loader &src, int nst, int T, uint8_t *smem_b, Scratch<kT> &sc,
                                                int (&e)[kT], long long (&Q)[kT]) {

@@ -657,7 +657,7 @@ __host__ __device__ constexpr bool pre_quantised(int bucket) { return bucket >= 
 
 // Slices quantised at once (B fragments and activations held for them).
 __host__ __device__ constexpr int slices_per_chunk(int bucket) {
-  return bucket <= 2 ? 16 : (bucket <= 4 ? 8 : (bucket <= 8 ? 4 : 2));
+  return bucket <= 2 ? 16 : (bucket <= 4 ? 8 : 4);
 }
 
 // Tiles each CTA leads per exchange group: 16 KB of exchange buffer.
@@ -1380,22 +1380,56 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         const uint32_t q_frag = static_cast<uint32_t>(p.sc) * mmad::slice_frag_bytes(kNT);  // e, then Q follow
         if constexpr (kPreQ) {
           if (op_kind == NQB_OP_LINEAR) {
-            // ---- the stage's activation chunks, quantised once over the grid
-            // (unit u by CTA u mod grid), then a grid barrier
+            // ---- the stage's activation chunks, quantised once over the grid:
+            // unit u = (chunk u / groups, tokens 2 (u % groups) ..) by CTA u mod
+            // grid, each writing its half N tile of the chunk's fragments and
+            // its tokens' e and Q into the chunk's slot; then a grid barrier
+            constexpr int kG = 2;
+            constexpr int kGroups = kT / kG;
             int k = 0, c0 = 0, nst = 0;
-            for (int u = cta; unit_at(op, u, p.sc, k, c0, nst); u += static_cast<int>(gridDim.x)) {
-              int e[kT];
-              long long Q[kT];
-              quantize_input(op.md[k], c0, nst, e, Q);  // ends with a consumer barrier after the fragment writes
-              uint8_t *dst = p.qbuf + static_cast<size_t>(u) * p.qunit_bytes;
-              const uint32_t fb = static_cast<uint32_t>(nst) * mmad::slice_frag_bytes(kNT);
-              for (uint32_t i = static_cast<uint32_t>(tid) * 16; i < fb; i += kC * 16)
-                *reinterpret_cast<uint4 *>(dst + i) = *reinterpret_cast<const uint4 *>(smem_b + i);
+            for (int u = cta;; u += static_cast<int>(gridDim.x)) {
+              const int cu = u / kGroups, t0 = (u - cu * kGroups) * kG;
+              if (!unit_at(op, cu, p.sc, k, c0, nst)) break;
+              if (t0 >= T) continue;
+              const MemberDev &md = op.md[k];
+              const int64_t k0 = static_cast<int64_t>(c0) * kStageCols;
+              int e[kG];
+              long long Q[kG];
+              if (st == 1) {
+                const mmad::LatentLoader ld{p.latent, op.latent_stride, md.act_offset, k0, md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_X_SWIGLU) {
+                const mmad::SwigluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                            md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_X_GEGLU) {
+                const mmad::GegluLoader ld{static_cast<const float *>(op.x), static_cast<const float *>(op.x2),
+                                           md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_BF16) {
+                const mmad::XLoader<__nv_bfloat16> ld{static_cast<const __nv_bfloat16 *>(op.x), md.pre, op.n, k0,
+                                                      md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              } else if (op.x_dtype == NQB_F16) {
+                const mmad::XLoader<__half> ld{static_cast<const __half *>(op.x), md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              } else {
+                const mmad::XLoader<float> ld{static_cast<const float *>(op.x), md.pre, op.n, k0, md.k_valid};
+                mmad::quantize_tokens<kT, kG, kQPT>(ld, nst, t0, T, smem_b, s_sc, e, Q);
+              }
+              // (the quantiser ends with a consumer barrier after its fragment writes)
+              uint8_t *dst = p.qbuf + static_cast<size_t>(cu) * p.qunit_bytes;
+              const int n0 = 2 * t0;  // first N column of the group (two digits per token)
+              const uint32_t part = static_cast<uint32_t>(n0 >> 3) * mmad::kFragBytes + ((n0 & 7) >> 2) * 128u;
+              for (int i = tid; i < nst * 8 * 8; i += kC) {  // 8 fragment blocks per slice, 8 x 16 bytes each
+                const uint32_t off = static_cast<uint32_t>(i >> 3) * kNT * mmad::kFragBytes + part + (i & 7) * 16u;
+                *reinterpret_cast<uint4 *>(dst + off) = *reinterpret_cast<const uint4 *>(smem_b + off);
+              }
               if (tid == 0) {
 #pragma unroll
-                for (int t = 0; t < kT; ++t) {
-                  reinterpret_cast<int32_t *>(dst + q_frag)[t] = e[t];
-                  reinterpret_cast<long long *>(dst + q_frag + 4 * kT)[t] = Q[t];
+                for (int t = 0; t < kG; ++t) {
+                  reinterpret_cast<int32_t *>(dst + q_frag)[t0 + t] = e[t];
+                  reinterpret_cast<long long *>(dst + q_frag + 4 * kT)[t0 + t] = Q[t];
                 }
               }
             }
