@@ -823,11 +823,11 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
   const float scale = rsqrtf(static_cast<float>(kAttHd));
   const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
   const __nv_bfloat16 *vbase = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
-  for (int t = 0; t < T; ++t) {
-    const int64_t visible = op.position + 1 + t;
-    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
-    const int64_t k1 = min(k0 + op.att_chunk, visible);
-    float qv[kAttGroup][4], acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
+  // token t over this split's keys b0 = first, first + step, .. (8-key sub-blocks):
+  // the online-softmax state of the unit's four q heads in acc, m, l (lane: 4 dims)
+  auto token_keys = [&](int t, int64_t k0, int64_t k1, int64_t first, int64_t step, float (&acc)[kAttGroup][4],
+                        float (&m)[kAttGroup], float (&l)[kAttGroup]) {
+    float qv[kAttGroup][4];
 #pragma unroll
     for (int h = 0; h < kAttGroup; ++h) {
       const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(
@@ -841,7 +841,7 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
       m[h] = -INFINITY;
       l[h] = 0.0f;
     }
-    for (int64_t b0 = k0 + warp * kAttSub; b0 < k1; b0 += kAttSub * mmad::kWarps) {
+    for (int64_t b0 = first; b0 < k1; b0 += step) {
       const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
       uint2 kr[kAttSub], vr[kAttSub];
       if (b0 - k0 < ring_rows) {  // a whole sub-block inside a ring block (16 nb is a multiple of 8)
@@ -905,6 +905,33 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
         }
       }
     }
+  };
+  if (T >= mmad::kWarps) {
+    // many tokens: each warp takes whole tokens over all of the split's keys
+    // and writes their partials directly (no join across warps)
+    for (int t = warp; t < T; t += mmad::kWarps) {
+      const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+      const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
+      float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
+      token_keys(t, k0, k1, k0, kAttSub, acc, m, l);
+#pragma unroll
+      for (int h = 0; h < kAttGroup; ++h) {
+        float *out = p.att_part +
+                     ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * op.att_splits + sp) * kAttRow;
+        *reinterpret_cast<float4 *>(out + lane * 4) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        if (lane == 0) {
+          out[kAttHd] = m[h];
+          out[kAttHd + 1] = l[h];
+        }
+      }
+    }
+    NQB_ATT_TRACE(kTraceMma);
+  } else {
+  for (int t = 0; t < T; ++t) {
+    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+    const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
+    float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
+    token_keys(t, k0, k1, k0 + warp * kAttSub, static_cast<int64_t>(kAttSub) * mmad::kWarps, acc, m, l);
     NQB_ATT_TRACE(kTraceMma);
     // the warps' partials -> shared memory [warp][head][kAttRow]
 #pragma unroll
@@ -943,6 +970,7 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
     }
     mmad::consumer_sync();  // the scratch is reused by the next token
     NQB_ATT_TRACE(kTraceDrain);
+  }
   }
 #undef NQB_ATT_TRACE
   // every warp is done with the unit's ring blocks: hand them back
