@@ -823,11 +823,78 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
   const float scale = rsqrtf(static_cast<float>(kAttHd));
   const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
   const __nv_bfloat16 *vbase = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
-  // token t over this split's keys b0 = first, first + step, .. (8-key sub-blocks):
-  // the online-softmax state of the unit's four q heads in acc, m, l (lane: 4 dims)
-  auto token_keys = [&](int t, int64_t k0, int64_t k1, int64_t first, int64_t step, float (&acc)[kAttGroup][4],
-                        float (&m)[kAttGroup], float (&l)[kAttGroup]) {
-    float qv[kAttGroup][4];
+  // one 8-key sub-block [b0, b0 + nk) of the split's K and V rows: from the
+  // ring where the unit's blocks are, else from global memory (L2)
+  auto load_block = [&](int64_t k0, int64_t b0, int nk, uint2 (&kr)[kAttSub], uint2 (&vr)[kAttSub]) {
+    if (b0 - k0 < ring_rows) {  // a whole sub-block inside a ring block (16 nb is a multiple of 8)
+      const int blk = static_cast<int>((b0 - k0) >> 4), within = static_cast<int>((b0 - k0) & 15);
+      const uint8_t *kslot = ring + static_cast<size_t>((slot + 2 * blk) % R) * kStageWeightBytes;
+      const uint8_t *vslot = ring + static_cast<size_t>((slot + 2 * blk + 1) % R) * kStageWeightBytes;
+#pragma unroll
+      for (int j = 0; j < kAttSub; ++j) {
+        kr[j] = *reinterpret_cast<const uint2 *>(kslot + (within + j) * (kAttHd * 2) + lane * 8);
+        vr[j] = *reinterpret_cast<const uint2 *>(vslot + (within + j) * (kAttHd * 2) + lane * 8);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kAttSub; ++j) {
+        const int64_t row = b0 + (j < nk ? j : 0);  // rows past the block re-read row b0 (masked below)
+        kr[j] = __ldcg(reinterpret_cast<const uint2 *>(kbase + row * kAttHd));
+        vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + row * kAttHd));
+      }
+    }
+  };
+  // one sub-block's scores, online-softmax step and P V for one token (q in
+  // qv; state acc, m, l of the unit's four q heads, lane: 4 dims)
+  auto block_update = [&](const uint2 (&kr)[kAttSub], const uint2 (&vr)[kAttSub], int nk,
+                          const float (&qv)[kAttGroup][4], float (&acc)[kAttGroup][4], float (&m)[kAttGroup],
+                          float (&l)[kAttGroup]) {
+    float sv[32];
+#pragma unroll
+    for (int j = 0; j < kAttSub; ++j) {
+      float kf[4];
+      bf16x4_to_float(kr[j], kf);
+#pragma unroll
+      for (int h = 0; h < kAttGroup; ++h)
+        sv[h * kAttSub + j] = qv[h][0] * kf[0] + qv[h][1] * kf[1] + qv[h][2] * kf[2] + qv[h][3] * kf[3];
+    }
+    const int own_h = lane / kAttSub, own_j = lane % kAttSub;
+    float sc = transposed_sum32(sv, lane);
+    if (own_j >= nk) sc = -INFINITY;
+    float mb = sc;
+#pragma unroll
+    for (int off = 1; off < kAttSub; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+    float mn[kAttGroup], corr[kAttGroup];
+#pragma unroll
+    for (int h = 0; h < kAttGroup; ++h) {
+      mn[h] = fmaxf(m[h], __shfl_sync(0xffffffffu, mb, h * kAttSub));  // finite: the block has a key
+      corr[h] = __expf(m[h] - mn[h]);  // exp(-inf) = 0 on the first block
+    }
+    const float pr = own_j < nk ? __expf(sc - mn[own_h]) : 0.0f;
+    float ps = pr;
+#pragma unroll
+    for (int off = 1; off < kAttSub; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+#pragma unroll
+    for (int h = 0; h < kAttGroup; ++h) {
+      l[h] = l[h] * corr[h] + __shfl_sync(0xffffffffu, ps, h * kAttSub);
+      m[h] = mn[h];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[h][e] *= corr[h];
+    }
+#pragma unroll
+    for (int j = 0; j < kAttSub; ++j) {
+      float vf[4];
+      bf16x4_to_float(vr[j], vf);
+#pragma unroll
+      for (int h = 0; h < kAttGroup; ++h) {
+        const float pj = __shfl_sync(0xffffffffu, pr, h * kAttSub + j);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[h][e] += pj * vf[e];
+      }
+    }
+  };
+  auto load_q = [&](int t, float (&qv)[kAttGroup][4], float (&acc)[kAttGroup][4], float (&m)[kAttGroup],
+                    float (&l)[kAttGroup]) {
 #pragma unroll
     for (int h = 0; h < kAttGroup; ++h) {
       const uint2 raw = __ldcg(reinterpret_cast<const uint2 *>(
@@ -841,79 +908,25 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
       m[h] = -INFINITY;
       l[h] = 0.0f;
     }
+  };
+  // token t over this split's keys b0 = first, first + step, .. (8-key sub-blocks)
+  auto token_keys = [&](int t, int64_t k0, int64_t k1, int64_t first, int64_t step, float (&acc)[kAttGroup][4],
+                        float (&m)[kAttGroup], float (&l)[kAttGroup]) {
+    float qv[kAttGroup][4];
+    load_q(t, qv, acc, m, l);
     for (int64_t b0 = first; b0 < k1; b0 += step) {
       const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
       uint2 kr[kAttSub], vr[kAttSub];
-      if (b0 - k0 < ring_rows) {  // a whole sub-block inside a ring block (16 nb is a multiple of 8)
-        const int blk = static_cast<int>((b0 - k0) >> 4), within = static_cast<int>((b0 - k0) & 15);
-        const uint8_t *kslot = ring + static_cast<size_t>((slot + 2 * blk) % R) * kStageWeightBytes;
-        const uint8_t *vslot = ring + static_cast<size_t>((slot + 2 * blk + 1) % R) * kStageWeightBytes;
-#pragma unroll
-        for (int j = 0; j < kAttSub; ++j) {
-          kr[j] = *reinterpret_cast<const uint2 *>(kslot + (within + j) * (kAttHd * 2) + lane * 8);
-          vr[j] = *reinterpret_cast<const uint2 *>(vslot + (within + j) * (kAttHd * 2) + lane * 8);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < kAttSub; ++j) {
-          const int64_t row = b0 + (j < nk ? j : 0);  // rows past the block re-read row b0 (masked below)
-          kr[j] = __ldcg(reinterpret_cast<const uint2 *>(kbase + row * kAttHd));
-          vr[j] = __ldcg(reinterpret_cast<const uint2 *>(vbase + row * kAttHd));
-        }
-      }
-      float sv[32];
-#pragma unroll
-      for (int j = 0; j < kAttSub; ++j) {
-        float kf[4];
-        bf16x4_to_float(kr[j], kf);
-#pragma unroll
-        for (int h = 0; h < kAttGroup; ++h)
-          sv[h * kAttSub + j] = qv[h][0] * kf[0] + qv[h][1] * kf[1] + qv[h][2] * kf[2] + qv[h][3] * kf[3];
-      }
-      const int own_h = lane / kAttSub, own_j = lane % kAttSub;
-      float sc = transposed_sum32(sv, lane);
-      if (own_j >= nk) sc = -INFINITY;
-      float mb = sc;
-#pragma unroll
-      for (int off = 1; off < kAttSub; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      float mn[kAttGroup], corr[kAttGroup];
-#pragma unroll
-      for (int h = 0; h < kAttGroup; ++h) {
-        mn[h] = fmaxf(m[h], __shfl_sync(0xffffffffu, mb, h * kAttSub));  // finite: the block has a key
-        corr[h] = __expf(m[h] - mn[h]);  // exp(-inf) = 0 on the first block
-      }
-      const float pr = own_j < nk ? __expf(sc - mn[own_h]) : 0.0f;
-      float ps = pr;
-#pragma unroll
-      for (int off = 1; off < kAttSub; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-#pragma unroll
-      for (int h = 0; h < kAttGroup; ++h) {
-        l[h] = l[h] * corr[h] + __shfl_sync(0xffffffffu, ps, h * kAttSub);
-        m[h] = mn[h];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[h][e] *= corr[h];
-      }
-#pragma unroll
-      for (int j = 0; j < kAttSub; ++j) {
-        float vf[4];
-        bf16x4_to_float(vr[j], vf);
-#pragma unroll
-        for (int h = 0; h < kAttGroup; ++h) {
-          const float pj = __shfl_sync(0xffffffffu, pr, h * kAttSub + j);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[h][e] += pj * vf[e];
-        }
-      }
+      load_block(k0, b0, nk, kr, vr);
+      block_update(kr, vr, nk, qv, acc, m, l);
     }
   };
   if (T >= mmad::kWarps) {
     // many tokens: each warp takes whole tokens over all of the split's keys
-    // and writes their partials directly (no join across warps)
-    for (int t = warp; t < T; t += mmad::kWarps) {
-      const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
-      const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
-      float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
-      token_keys(t, k0, k1, k0, kAttSub, acc, m, l);
+    // and writes their partials directly (no join across warps); tokens
+    // t and t + 8 go together, sharing every K/V sub-block load
+    auto store_partial = [&](int t, const float (&acc)[kAttGroup][4], const float (&m)[kAttGroup],
+                             const float (&l)[kAttGroup]) {
 #pragma unroll
       for (int h = 0; h < kAttGroup; ++h) {
         float *out = p.att_part +
@@ -924,6 +937,31 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
           out[kAttHd + 1] = l[h];
         }
       }
+    };
+    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+    for (int t = warp; t < T; t += 2 * mmad::kWarps) {
+      const int u = t + mmad::kWarps;  // the partner token (none past T)
+      const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
+      float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
+      if (u >= T) {
+        token_keys(t, k0, k1, k0, kAttSub, acc, m, l);
+        store_partial(t, acc, m, l);
+        continue;
+      }
+      const int64_t k1u = min(k0 + op.att_chunk, op.position + 1 + u);  // >= k1
+      float qt[kAttGroup][4], qu[kAttGroup][4], acu[kAttGroup][4], mu[kAttGroup], lu[kAttGroup];
+      load_q(t, qt, acc, m, l);
+      load_q(u, qu, acu, mu, lu);
+      for (int64_t b0 = k0; b0 < k1u; b0 += kAttSub) {
+        const int nku = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1u - b0));
+        const int nkt = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
+        uint2 kr[kAttSub], vr[kAttSub];
+        load_block(k0, b0, nku, kr, vr);
+        if (nkt > 0) block_update(kr, vr, nkt, qt, acc, m, l);
+        block_update(kr, vr, nku, qu, acu, mu, lu);
+      }
+      store_partial(t, acc, m, l);
+      store_partial(u, acu, mu, lu);
     }
     NQB_ATT_TRACE(kTraceMma);
   } else {
