@@ -122,6 +122,7 @@ struct __align__(8) StepDev {
   int64_t cache_len, position;
   __nv_bfloat16 *attn_out;
   int32_t att_splits;
+  int32_t att_parts;         // partials per (token, q head): splits, or 2 x splits from 8 tokens on (key halves)
   int32_t att_ring_blocks;   // at most this many 16-row K/V blocks of a unit arrive through the sign ring
   int64_t att_chunk;         // keys per split, a multiple of 16
 };
@@ -732,6 +733,10 @@ constexpr int kAttHd = 128;                 // head_dim of the fused attention a
 constexpr int kAttGroup = 4;                // q heads per kv head
 constexpr int kAttSub = 32 / kAttGroup;     // keys per warp sub-block (group x keys = 32 lanes)
 constexpr int kAttRow = kAttHd + 4;         // a partial: acc[128], m, l, two pad floats (16-byte rows)
+constexpr int kAttPadRow = kAttHd * 2 + 16;  // staged K/V row stride of the tensor-core path (conflict-free ldmatrix)
+// the tensor-core path stages two halves x (K, V) x 16 rows in the consumers'
+// accumulator and exchange buffers, which are idle during attention stages
+constexpr int kAttStageBytes = 2 * 2 * 16 * kAttPadRow;
 
 // Named barrier of the 128 leader threads (consumer warps 0..3).
 __device__ __forceinline__ void leader_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
@@ -765,6 +770,36 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
   out[3] = b.y;
 }
 
+// Tensor-core pieces of the many-token attention path: one m16n8k16 bf16 MMA
+// with fp32 accumulators, 8x8 b16 matrix loads from shared memory (four
+// matrices; .trans transposes each) and the named barrier of one key half's
+// four consumer warps (threads 128 hf .. +127).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(ptx::smem_u32(row)));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void *row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(ptx::smem_u32(row)));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void half_sync(int hf) { asm volatile("bar.sync %0, 128;" ::"r"(4 + hf) : "memory"); }
+
 // Attention partials of one CTA: unit `blockIdx.x` = (kv head, key split),
 // for every token of the step.  The 8 consumer warps take 8-key sub-blocks in
 // turn; per sub-block a lane loads its 4 dims of the 8 K and V rows (all
@@ -783,6 +818,7 @@ __device__ __forceinline__ void bf16x4_to_float(uint2 raw, float (&out)[4]) {
 // unit's ring slots first and every warp hands them back after the last token.
 // Inlined, like attention_join: a call would make the kernel keep its stage
 // loop's state across the call (spills), slowing every linear stage.
+template <bool kMany>  // kMany: the instance may run 8 or more tokens (the tensor-core path is compiled in)
 __device__ __forceinline__ void attention_partials(const Params &p, const StepDev &op, float *scratch,
                                                 const uint8_t *ring, uint64_t *s_full, uint64_t *s_empty,
                                                 int &slot, uint32_t &phase, bool &ok, long long *trace) {
@@ -921,47 +957,157 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
       block_update(kr, vr, nk, qv, acc, m, l);
     }
   };
-  if (T >= mmad::kWarps) {
-    // many tokens: each warp takes whole tokens over all of the split's keys
-    // and writes their partials directly (no join across warps); tokens
-    // t and t + 8 go together, sharing every K/V sub-block load
-    auto store_partial = [&](int t, const float (&acc)[kAttGroup][4], const float (&m)[kAttGroup],
-                             const float (&l)[kAttGroup]) {
+  if (kMany && T >= mmad::kWarps) {
+    // many tokens, on the tensor cores (mma.sync m16n8k16 bf16, fp32
+    // accumulators): the unit's query rows r = 4 tl + h (token 4 rb + tl, q
+    // head h of this kv head) in 16-row blocks rb; warp w < 4 takes block w
+    // over the split's first key half, warp w + 4 the same rows over the
+    // second half, and each writes its own partial (the join takes 2 per
+    // split).  Per 16-key block: the half's four warps stage K and V into
+    // shared memory (272-byte rows: the ring's 256-byte rows put the eight
+    // rows of every 8x8 matrix load on the same banks), then S = Q K^T, an
+    // online softmax and O += P V.
+    const int rbs = (T + 3) / 4;
+    const int rb = warp & 3, hf = warp >> 2;
+    const int g = lane >> 2, c = lane & 3;
+    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
+    const int64_t kend = min(k0 + op.att_chunk, op.position + T);  // past the last key any token sees
+    const int64_t kmid = k0 + (kend > k0 ? ((kend - k0 + 31) / 32) * 16 : 0);
+    const int64_t ka = hf == 0 ? k0 : kmid, kb = hf == 0 ? min(kmid, kend) : kend;
+    const int t_lo = 4 * rb + (g >> 2), t_hi = t_lo + 2, hq = g & 3;
+    const int64_t k1_lo = min(k0 + op.att_chunk, op.position + 1 + t_lo);
+    const int64_t k1_hi = min(k0 + op.att_chunk, op.position + 1 + t_hi);
+    float o[16][4];
 #pragma unroll
-      for (int h = 0; h < kAttGroup; ++h) {
-        float *out = p.att_part +
-                     ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * op.att_splits + sp) * kAttRow;
-        *reinterpret_cast<float4 *>(out + lane * 4) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-        if (lane == 0) {
-          out[kAttHd] = m[h];
-          out[kAttHd + 1] = l[h];
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.0f, l_hi = 0.0f;
+    uint32_t qa[8][4];  // A fragments of Q: 8 steps of 16 dims (rows of this warp's block)
+    if (rb < rbs) {
+      const __nv_bfloat16 *q_lo = op.q + (static_cast<int64_t>(t_lo) * op.q_heads + kvh * kAttGroup + hq) * kAttHd;
+      const __nv_bfloat16 *q_hi = op.q + (static_cast<int64_t>(t_hi) * op.q_heads + kvh * kAttGroup + hq) * kAttHd;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d0 = 16 * kk + 2 * c;
+        qa[kk][0] = t_lo < T ? __ldcg(reinterpret_cast<const uint32_t *>(q_lo + d0)) : 0u;
+        qa[kk][1] = t_hi < T ? __ldcg(reinterpret_cast<const uint32_t *>(q_hi + d0)) : 0u;
+        qa[kk][2] = t_lo < T ? __ldcg(reinterpret_cast<const uint32_t *>(q_lo + d0 + 8)) : 0u;
+        qa[kk][3] = t_hi < T ? __ldcg(reinterpret_cast<const uint32_t *>(q_hi + d0 + 8)) : 0u;
+      }
+    }
+    const __nv_bfloat16 *kg = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd;
+    const __nv_bfloat16 *vg = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd;
+    uint8_t *sk = reinterpret_cast<uint8_t *>(scratch) + hf * (2 * 16 * kAttPadRow);
+    uint8_t *sv = sk + 16 * kAttPadRow;
+    const int ht = tid & 127;  // thread within the half
+    for (int64_t b0 = ka; b0 < kb; b0 += 16) {
+      const bool in_ring = b0 - k0 < ring_rows;  // 16-key blocks from k0 coincide with the ring's blocks
+      const int blk = static_cast<int>((b0 - k0) >> 4);
+      const uint8_t *kslot = ring + static_cast<size_t>((slot + 2 * blk) % R) * kStageWeightBytes;
+      const uint8_t *vslot = ring + static_cast<size_t>((slot + 2 * blk + 1) % R) * kStageWeightBytes;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {  // 16 rows x 16 chunks of 16 bytes, two per thread
+        const int q = ht + 128 * u, row = q >> 4, col = q & 15;
+        uint4 kv, vv;
+        if (in_ring) {
+          kv = *reinterpret_cast<const uint4 *>(kslot + row * (kAttHd * 2) + col * 16);
+          vv = *reinterpret_cast<const uint4 *>(vslot + row * (kAttHd * 2) + col * 16);
+        } else {  // rows past the last key re-read the last key (their scores are masked)
+          const int64_t r = min(b0 + row, kend - 1);
+          kv = __ldcg(reinterpret_cast<const uint4 *>(kg + r * kAttHd) + col);
+          vv = __ldcg(reinterpret_cast<const uint4 *>(vg + r * kAttHd) + col);
+        }
+        *reinterpret_cast<uint4 *>(sk + row * kAttPadRow + col * 16) = kv;
+        *reinterpret_cast<uint4 *>(sv + row * kAttPadRow + col * 16) = vv;
+      }
+      half_sync(hf);
+      if (rb < rbs) {
+        float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+        const int mi = lane >> 3, mr = lane & 7;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t kb4[4];  // B fragments: keys 0-7 (dims lo, hi), keys 8-15 (dims lo, hi)
+          ldsm_x4(kb4, sk + ((mi >> 1) * 8 + mr) * kAttPadRow + (16 * kk + (mi & 1) * 8) * 2);
+          mma_bf16(sc[0], qa[kk], kb4[0], kb4[1]);
+          mma_bf16(sc[1], qa[kk], kb4[2], kb4[3]);
+        }
+        // scores -> online softmax of rows lo (regs 0, 1) and hi (regs 2, 3)
+        float pv[2][4];
+        float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int64_t key = b0 + 8 * nt + 2 * c + e;
+            sc[nt][e] = key < k1_lo ? sc[nt][e] * scale : -INFINITY;
+            sc[nt][2 + e] = key < k1_hi ? sc[nt][2 + e] * scale : -INFINITY;
+            mx_lo = fmaxf(mx_lo, sc[nt][e]);
+            mx_hi = fmaxf(mx_hi, sc[nt][2 + e]);
+          }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+          mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+          mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+        }
+        const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+        // a row that has seen no key yet keeps m = -inf, l = 0 and zero probabilities
+        const float cr_lo = mn_lo == -INFINITY ? 1.0f : __expf(m_lo - mn_lo);
+        const float cr_hi = mn_hi == -INFINITY ? 1.0f : __expf(m_hi - mn_hi);
+        float rs_lo = 0.0f, rs_hi = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            pv[nt][e] = mn_lo == -INFINITY ? 0.0f : __expf(sc[nt][e] - mn_lo);
+            pv[nt][2 + e] = mn_hi == -INFINITY ? 0.0f : __expf(sc[nt][2 + e] - mn_hi);
+            rs_lo += pv[nt][e];
+            rs_hi += pv[nt][2 + e];
+          }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+          rs_lo += __shfl_xor_sync(0xffffffffu, rs_lo, off);
+          rs_hi += __shfl_xor_sync(0xffffffffu, rs_hi, off);
+        }
+        l_lo = l_lo * cr_lo + rs_lo;
+        l_hi = l_hi * cr_hi + rs_hi;
+        m_lo = mn_lo;
+        m_hi = mn_hi;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          o[j][0] *= cr_lo;
+          o[j][1] *= cr_lo;
+          o[j][2] *= cr_hi;
+          o[j][3] *= cr_hi;
+        }
+        // P (the scores' accumulator layout is the next MMA's A layout) x V
+        const uint32_t pa[4] = {pack_bf16(pv[0][0], pv[0][1]), pack_bf16(pv[0][2], pv[0][3]),
+                                pack_bf16(pv[1][0], pv[1][1]), pack_bf16(pv[1][2], pv[1][3])};
+#pragma unroll
+        for (int j2 = 0; j2 < 8; ++j2) {  // dims 16 j2 .. +15: two N tiles
+          uint32_t vb[4];  // (keys 0-7, keys 8-15) for dims +0..7, then for dims +8..15
+          ldsm_x4_trans(vb, sv + ((mi & 1) * 8 + mr) * kAttPadRow + (16 * j2 + (mi >> 1) * 8) * 2);
+          mma_bf16(o[2 * j2], pa, vb[0], vb[1]);
+          mma_bf16(o[2 * j2 + 1], pa, vb[2], vb[3]);
         }
       }
-    };
-    const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
-    for (int t = warp; t < T; t += 2 * mmad::kWarps) {
-      const int u = t + mmad::kWarps;  // the partner token (none past T)
-      const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
-      float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
-      if (u >= T) {
-        token_keys(t, k0, k1, k0, kAttSub, acc, m, l);
-        store_partial(t, acc, m, l);
-        continue;
+      half_sync(hf);  // the half's staged block is free again
+    }
+    if (rb < rbs) {
+      // this half's partial of rows lo and hi (tokens past T write nothing)
+      const int part = sp * 2 + hf;
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int t = rr == 0 ? t_lo : t_hi;
+        if (t >= T) continue;
+        float *out = p.att_part +
+                     ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + hq) * op.att_parts + part) * kAttRow;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          *reinterpret_cast<float2 *>(out + 8 * j + 2 * c) = make_float2(o[j][2 * rr], o[j][2 * rr + 1]);
+        if (c == 0) {
+          out[kAttHd] = rr == 0 ? m_lo : m_hi;
+          out[kAttHd + 1] = rr == 0 ? l_lo : l_hi;
+        }
       }
-      const int64_t k1u = min(k0 + op.att_chunk, op.position + 1 + u);  // >= k1
-      float qt[kAttGroup][4], qu[kAttGroup][4], acu[kAttGroup][4], mu[kAttGroup], lu[kAttGroup];
-      load_q(t, qt, acc, m, l);
-      load_q(u, qu, acu, mu, lu);
-      for (int64_t b0 = k0; b0 < k1u; b0 += kAttSub) {
-        const int nku = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1u - b0));
-        const int nkt = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
-        uint2 kr[kAttSub], vr[kAttSub];
-        load_block(k0, b0, nku, kr, vr);
-        if (nkt > 0) block_update(kr, vr, nkt, qt, acc, m, l);
-        block_update(kr, vr, nku, qu, acu, mu, lu);
-      }
-      store_partial(t, acc, m, l);
-      store_partial(u, acu, mu, lu);
     }
     NQB_ATT_TRACE(kTraceMma);
   } else {
@@ -999,7 +1145,7 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
         ls += f * row[kAttHd + 1];
       }
       float *out = p.att_part +
-                   ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * op.att_splits + sp) * kAttRow;
+                   ((static_cast<int64_t>(t) * op.q_heads + kvh * kAttGroup + h) * op.att_parts + sp) * kAttRow;
       *reinterpret_cast<float2 *>(out + d) = make_float2(a0, a1);
       if ((tid & 63) == 0) {
         out[kAttHd] = mx;
@@ -1025,15 +1171,15 @@ __device__ __forceinline__ void attention_join(const Params &p, const StepDev &o
   const int lane = threadIdx.x & 31;
   const int stride = static_cast<int>(gridDim.x) * mmad::kWarps;
   for (int r = static_cast<int>(blockIdx.x) * mmad::kWarps + (threadIdx.x >> 5); r < rows; r += stride) {
-    const float *base = p.att_part + static_cast<int64_t>(r) * op.att_splits * kAttRow;
-    const float m0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd) : -INFINITY;
-    const float l0 = lane < op.att_splits ? __ldcg(base + lane * kAttRow + kAttHd + 1) : 0.0f;
+    const float *base = p.att_part + static_cast<int64_t>(r) * op.att_parts * kAttRow;
+    const float m0 = lane < op.att_parts ? __ldcg(base + lane * kAttRow + kAttHd) : -INFINITY;
+    const float l0 = lane < op.att_parts ? __ldcg(base + lane * kAttRow + kAttHd + 1) : 0.0f;
     // the splits' vectors, kJoin at a time, all in flight together (issued before the weights are known)
     constexpr int kJoin = 16;
     float4 v[kJoin];
 #pragma unroll
     for (int u = 0; u < kJoin; ++u)
-      v[u] = __ldcg(reinterpret_cast<const float4 *>(base + min(u, op.att_splits - 1) * kAttRow + lane * 4));
+      v[u] = __ldcg(reinterpret_cast<const float4 *>(base + min(u, op.att_parts - 1) * kAttRow + lane * 4));
     float mx = m0;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -1042,17 +1188,17 @@ __device__ __forceinline__ void attention_join(const Params &p, const StepDev &o
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
     float num[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int s0 = 0; s0 < op.att_splits; s0 += kJoin) {
+    for (int s0 = 0; s0 < op.att_parts; s0 += kJoin) {
       if (s0 > 0) {
 #pragma unroll
         for (int u = 0; u < kJoin; ++u)
           v[u] = __ldcg(
-              reinterpret_cast<const float4 *>(base + min(s0 + u, op.att_splits - 1) * kAttRow + lane * 4));
+              reinterpret_cast<const float4 *>(base + min(s0 + u, op.att_parts - 1) * kAttRow + lane * 4));
       }
 #pragma unroll
       for (int u = 0; u < kJoin; ++u) {
         const float f = __shfl_sync(0xffffffffu, f0, (s0 + u) & 31);
-        if (s0 + u < op.att_splits) {
+        if (s0 + u < op.att_parts) {
           num[0] += f * v[u].x;
           num[1] += f * v[u].y;
           num[2] += f * v[u].z;
@@ -1353,9 +1499,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
             NQB_TRACE(kTraceTables);
             if (st == 0)
   #ifdef NQB_PHASE_TRACE
-              attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, tid == 0 ? trace_c : nullptr);
+              attention_partials<(kT >= mmad::kWarps)>(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, tid == 0 ? trace_c : nullptr);
   #else
-              attention_partials(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, nullptr);
+              attention_partials<(kT >= mmad::kWarps)>(p, gop, s_acc, ring, s_full, s_empty, slot, phase, ok, nullptr);
   #endif
             else
               attention_join(p, gop);
@@ -2308,6 +2454,8 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   if (step && (patch || mixed)) return fail(NQB_ERR_UNSUPPORTED, "decoder-step programs take no patch or mixed-V tiles");
   const SmemPlan sp = smem_plan(bucket, mixed);
   if (sp.off_cb % 16) return fail(NQB_ERR_UNSUPPORTED, "codebook buffer is misaligned");
+  if (step && bucket >= mmad::kWarps && sp.off_cb - sp.off_acc < static_cast<uint32_t>(kAttStageBytes))
+    return fail(NQB_ERR_UNSUPPORTED, "the attention staging buffer does not fit the accumulator buffers");
   const void *fn = kernel_for(bucket, patch, mixed, step);
   {
     // the kernel's register split assumes the launch count (kLaunchRegs)
@@ -2339,18 +2487,22 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   clusters = std::min(clusters, sms / kClusterSize);
   if (clusters < 1) return fail(NQB_ERR_UNSUPPORTED, "no cluster of %d CTAs fits this device", kClusterSize);
   const int ctas = clusters * kClusterSize;
-  // fused attention: one (kv head, key split) unit per CTA, at most 32 splits
+  // fused attention: one (kv head, key split) unit per CTA, at most 32
+  // partials per (token, q head) -- from 8 tokens on a unit writes one per
+  // key half, so at most 16 splits
   size_t att_floats = 0;
   for (int i = 0; i < op_count; ++i) {
     OpDev &od = opdev[i];
     if (od.step.kind != NQB_OP_ATTENTION) continue;
-    const int want = std::max(1, std::min(32, ctas / od.step.kv_heads));
+    const int halves = tokens >= mmad::kWarps ? 2 : 1;
+    const int want = std::max(1, std::min(32 / halves, ctas / od.step.kv_heads));
     const int64_t most = od.step.position + tokens;  // keys the last token sees
     od.step.att_chunk = ((most + want - 1) / want + 15) / 16 * 16;
     od.step.att_splits = static_cast<int32_t>((most + od.step.att_chunk - 1) / od.step.att_chunk);
+    od.step.att_parts = od.step.att_splits * halves;
     // K and V blocks of a unit must fit the ring at once (the consumers hold them all)
     od.step.att_ring_blocks = std::max(0, sp.ring / 2 - 1);
-    att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.step.q_heads * od.step.att_splits * kAttRow);
+    att_floats = std::max(att_floats, static_cast<size_t>(tokens) * od.step.q_heads * od.step.att_parts * kAttRow);
   }
 
   // tiles per (stage, cluster), then every CTA's slice addresses in consumption order
