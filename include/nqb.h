@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NQB_ABI_VERSION 4
+#define NQB_ABI_VERSION 5
 
 /* status codes */
 #define NQB_OK 0
@@ -119,15 +119,23 @@ typedef struct nqb_linear_desc {
   const void *patch_right; /* [p, n] in patch_dtype */
   int32_t patch_dtype;     /* F32 / F16 / BF16 */
 
-  /* Mixed-V right factor kept coded for decode programs (optional; NULL
+  /* Right factor kept coded for decode programs (optional; NULL
    * coded_right_tiles = none).  Programs stream the coded tiles of V and
-   * decode the 19-bit records in stage 1; the 128-row tiles below
+   * decode their records in stage 1; the 128-row tiles below
    * ceil(coded_free_rows / 128) * 128 still come from right_tiles, which the
-   * per-call paths keep using for every row.                                 */
-  const void *coded_right_tiles;  /* nqb_repack_mixed_v(payload, r, n, coded_free_rows) */
-  const int32_t *coded_codebook;  /* [1024] full sign words, 16-byte aligned       */
+   * per-call paths keep using for every row.  coded_format says which
+   * records the tiles hold:
+   *   NQB_CODED_MIXED_V          nqb_repack_mixed_v tiles, coded_codebook the
+   *                              layer's 1024 full sign words;
+   *   NQB_CODED_PRODUCT_CODEBOOK nqb_repack_product_codebook tiles and table. */
+  const void *coded_right_tiles;
+  const int32_t *coded_codebook;  /* [1024] words, 16-byte aligned                 */
   int64_t coded_free_rows;        /* the layer's plain (free) rows                 */
+  int32_t coded_format;           /* NQB_CODED_*                                   */
 } nqb_linear_desc;
+
+#define NQB_CODED_MIXED_V 0
+#define NQB_CODED_PRODUCT_CODEBOOK 1
 
 /*
  * Coded tiles of a mixed-V right factor (mixed-v-free-k10-pair9-v1: rows
@@ -144,6 +152,28 @@ typedef struct nqb_linear_desc {
 int nqb_mixed_v_tiles_bytes(int64_t rank, int64_t in_features, int64_t free_rows, size_t *bytes);
 int nqb_repack_mixed_v(const int32_t *payload, int64_t rank, int64_t in_features, int64_t free_rows,
                        void *out, void *stream);
+
+/*
+ * Coded tiles of a product-codebook right factor (product-codebook-free-k16-v1,
+ * canonical orientation: rows below free_rows plain, every later word one
+ * 16-bit record, low byte indexing `first` for bits 0..15 and high byte
+ * indexing `second` for bits 16..31).  The tiles of 128 rows from
+ * ceil(free_rows / 128) on keep the records: per tile and per 256-column
+ * slice, row r's 8 records (words 8s .. 8s+7, zero past the row) are the
+ * 16-byte block at byte 16 r, so one tile slice is 2048 bytes against 4096
+ * for sign words.  `table_out` receives the 1024-word decode table of the
+ * programs' record decode (word = table[rec & 255] | table[256 + (rec >> 8)]):
+ * entries 0..255 the first half words, 256..511 the second half words
+ * shifted to bits 16..31, the rest zero.  No counterpart in the reference,
+ * whose runtime expands the records to sign words before its kernels run
+ * (product_codebook.py:110-143, :229-237); this layout feeds the decode
+ * programs' stage-1 record decode.  0 < free_rows < rank, as in
+ * nqb_decode_product_codebook.
+ */
+int nqb_product_codebook_tiles_bytes(int64_t rank, int64_t in_features, int64_t free_rows, size_t *bytes);
+int nqb_repack_product_codebook(const int32_t *payload, const int16_t *first, const int16_t *second,
+                                int64_t rank, int64_t in_features, int64_t free_rows, void *tiles_out,
+                                int32_t *table_out, void *stream);
 
 /* Library identity: NQB_ABI_VERSION of the loaded build. */
 int nqb_abi_version(void);

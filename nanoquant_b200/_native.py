@@ -36,6 +36,9 @@ NQB_I8 = 3
 NQB_I32 = 4
 NQB_X_SWIGLU = 16  # program-op input: silu(x) * x2, both fp32
 NQB_X_GEGLU = 17  # program-op input: gelu_tanh(x) * x2, both fp32
+NQB_CODED_MIXED_V = 0  # nqb_linear_desc.coded_format
+NQB_CODED_PRODUCT_CODEBOOK = 1
+ABI_VERSION = 5  # the NQB_ABI_VERSION whose structs this module lays out
 
 DTYPE_CODES = {
     torch.float32: NQB_F32,
@@ -89,6 +92,7 @@ class LinearDesc(ctypes.Structure):
         ("coded_right_tiles", _c_void_p),
         ("coded_codebook", _c_void_p),
         ("coded_free_rows", ctypes.c_int64),
+        ("coded_format", ctypes.c_int32),
     ]
 
 
@@ -199,6 +203,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nqb_decode_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "nqb_mixed_v_tiles_bytes": (ctypes.c_int, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
     "nqb_repack_mixed_v": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p]),
+    "nqb_product_codebook_tiles_bytes": (ctypes.c_int, [_i64, _i64, _i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "nqb_repack_product_codebook": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p,
+                                                   _c_void_p, _c_void_p]),
     "nqb_rmsnorm": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64, ctypes.c_float, _c_void_p, _i32,
                                    _c_void_p]),
     "nqb_qk_norm_rope": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p,
@@ -257,6 +264,9 @@ def library() -> ctypes.CDLL:
                 function = getattr(lib, name)
                 function.restype = restype
                 function.argtypes = argtypes
+            if lib.nqb_abi_version() != ABI_VERSION:
+                raise RuntimeError(f"{path.name} has ABI {lib.nqb_abi_version()}, this package lays out ABI "
+                                   f"{ABI_VERSION}; rebuild with `python -m nanoquant_b200.build`")
             _library = lib
         return _library
 

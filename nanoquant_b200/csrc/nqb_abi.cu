@@ -120,6 +120,8 @@ static int validate_layer(const nqb_linear_desc *d, const char *name) {
       return fail(NQB_ERR_INVALID_ARGUMENT, "%s: coded tiles need the codebook and the plain right tiles", name);
     if (d->coded_free_rows <= 0 || d->coded_free_rows >= d->rank)
       return fail(NQB_ERR_INVALID_ARGUMENT, "%s: coded free rows must be between zero and rank", name);
+    if (d->coded_format != NQB_CODED_MIXED_V && d->coded_format != NQB_CODED_PRODUCT_CODEBOOK)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "%s: coded format %d is not NQB_CODED_*", name, d->coded_format);
     if (!aligned(d->coded_right_tiles, 16) || !aligned(d->coded_codebook, 16))
       return fail(NQB_ERR_ALIGNMENT, "%s: coded tiles and codebook must be 16-byte aligned", name);
   }
@@ -495,6 +497,30 @@ int nqb_repack_mixed_v(const int32_t *payload, int64_t rank, int64_t in_features
   if (!aligned(out, 16)) return fail(NQB_ERR_ALIGNMENT, "coded tiles must be 16-byte aligned");
   NQB_CHECK(launch_repack_mixed_v(reinterpret_cast<const uint32_t *>(payload), rank, in_features, free_rows,
                                   static_cast<uint8_t *>(out), reinterpret_cast<cudaStream_t>(stream)));
+  return ok();
+}
+
+int nqb_product_codebook_tiles_bytes(int64_t rank, int64_t in_features, int64_t free_rows, size_t *bytes) {
+  if (bytes == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "bytes is NULL");
+  if (free_rows <= 0 || free_rows >= rank || in_features <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "product-codebook free rows must be between zero and rank");
+  *bytes = product_codebook_tiles_bytes(rank, in_features, free_rows);
+  return ok();
+}
+
+int nqb_repack_product_codebook(const int32_t *payload, const int16_t *first, const int16_t *second,
+                                int64_t rank, int64_t in_features, int64_t free_rows, void *tiles_out,
+                                int32_t *table_out, void *stream) {
+  if (payload == nullptr || first == nullptr || second == nullptr || tiles_out == nullptr || table_out == nullptr)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "product-codebook operand is NULL");
+  if (free_rows <= 0 || free_rows >= rank || in_features <= 0)
+    return fail(NQB_ERR_INVALID_ARGUMENT, "product-codebook free rows must be between zero and rank");
+  if (!aligned(tiles_out, 16) || !aligned(table_out, 16))
+    return fail(NQB_ERR_ALIGNMENT, "coded tiles and table must be 16-byte aligned");
+  NQB_CHECK(launch_repack_product_codebook(
+      reinterpret_cast<const uint16_t *>(payload), reinterpret_cast<const uint16_t *>(first),
+      reinterpret_cast<const uint16_t *>(second), rank, in_features, free_rows, static_cast<uint8_t *>(tiles_out),
+      reinterpret_cast<uint32_t *>(table_out), reinterpret_cast<cudaStream_t>(stream)));
   return ok();
 }
 

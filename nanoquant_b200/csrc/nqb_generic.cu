@@ -324,6 +324,39 @@ __global__ void repack_mixed_v_kernel(const uint32_t *payload, int64_t rank, int
   }
 }
 
+// Coded tiles of a product-codebook right factor (nqb_repack_product_codebook):
+// one thread per (coded tile, slice, row) writes the row's 16-byte block of 8
+// records, zero past the row and past the rank; threads past the tiles write
+// the 1024-word decode table (first half words, second half words << 16).
+__global__ void repack_product_codebook_kernel(const uint16_t *payload, const uint16_t *first,
+                                               const uint16_t *second, int64_t rank, int64_t wpr,
+                                               int64_t free_rows, int64_t first_tile, int64_t coded_tiles,
+                                               int32_t slices, uint8_t *out, uint32_t *table) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t items = coded_tiles * slices * kMixedTileRows;
+  if (i >= items) {
+    const int64_t e = i - items;
+    if (e < 1024)
+      table[e] = e < 256 ? static_cast<uint32_t>(first[e])
+                         : (e < 512 ? static_cast<uint32_t>(second[e - 256]) << 16 : 0u);
+    return;
+  }
+  const int64_t row_in_tile = i % kMixedTileRows;
+  const int64_t ts = i / kMixedTileRows;  // coded tile * slices + slice
+  const int64_t slice = ts % slices;
+  const int64_t row = (first_tile + ts / slices) * kMixedTileRows + row_in_tile;
+  uint32_t half[4] = {0u, 0u, 0u, 0u};
+  if (row < rank) {
+    const uint16_t *src = payload + (row - free_rows) * wpr;
+    for (int j = 0; j < 8; ++j) {
+      const int64_t w = slice * 8 + j;
+      if (w < wpr) half[j >> 1] |= static_cast<uint32_t>(src[w]) << (16 * (j & 1));
+    }
+  }
+  *reinterpret_cast<uint4 *>(out + ts * kCodebookTileSliceBytes + row_in_tile * 16) =
+      make_uint4(half[0], half[1], half[2], half[3]);
+}
+
 // --------------------------------------------------------------- launch ---
 
 static int set_smem(const void *fn, size_t bytes) { return ensure_dynamic_smem(fn, bytes); }
@@ -417,6 +450,27 @@ int launch_repack_mixed_v(const uint32_t *payload, int64_t rank, int64_t columns
   repack_mixed_v_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
       payload, rank, wpr, free_rows, first, tiles, slices, out);
   NQB_CUDA(cudaGetLastError(), "repack_mixed_v_kernel launch");
+  return NQB_OK;
+}
+
+size_t product_codebook_tiles_bytes(int64_t rank, int64_t columns, int64_t free_rows) {
+  const int64_t tiles = (rank + kMixedTileRows - 1) / kMixedTileRows - mixed_v_first_coded_tile(free_rows);
+  const int64_t slices = (words_for(columns) + 7) / 8;
+  return tiles > 0 ? static_cast<size_t>(tiles * slices) * kCodebookTileSliceBytes : 0;
+}
+
+int launch_repack_product_codebook(const uint16_t *payload, const uint16_t *first, const uint16_t *second,
+                                   int64_t rank, int64_t columns, int64_t free_rows, uint8_t *tiles,
+                                   uint32_t *table, cudaStream_t stream) {
+  const int64_t first_tile = mixed_v_first_coded_tile(free_rows);
+  const int64_t tile_count = (rank + kMixedTileRows - 1) / kMixedTileRows - first_tile;
+  const int64_t coded = tile_count > 0 ? tile_count : 0;
+  const int64_t wpr = words_for(columns);
+  const int32_t slices = static_cast<int32_t>((wpr + 7) / 8);
+  const int64_t items = coded * slices * kMixedTileRows + 1024;
+  repack_product_codebook_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, stream>>>(
+      payload, first, second, rank, wpr, free_rows, first_tile, coded, slices, tiles, table);
+  NQB_CUDA(cudaGetLastError(), "repack_product_codebook_kernel launch");
   return NQB_OK;
 }
 

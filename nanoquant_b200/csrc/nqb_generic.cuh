@@ -95,6 +95,13 @@ int64_t mixed_v_first_coded_tile(int64_t free_rows);
 size_t mixed_v_tiles_bytes(int64_t rank, int64_t columns, int64_t free_rows);
 int launch_repack_mixed_v(const uint32_t *payload, int64_t rank, int64_t columns, int64_t free_rows, uint8_t *out,
                           cudaStream_t stream);
+// Coded product-codebook tiles (nqb_repack_product_codebook): 128-row tiles,
+// per 256-column slice 8 16-bit records per row, row r's at byte 16 r.
+constexpr int kCodebookTileSliceBytes = kMixedTileRows * 8 * 2;  // 2048
+size_t product_codebook_tiles_bytes(int64_t rank, int64_t columns, int64_t free_rows);
+int launch_repack_product_codebook(const uint16_t *payload, const uint16_t *first, const uint16_t *second,
+                                   int64_t rank, int64_t columns, int64_t free_rows, uint8_t *tiles,
+                                   uint32_t *table, cudaStream_t stream);
 int launch_decode_mixed_v(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,
                           const uint32_t *payload, const uint32_t *codebook, uint32_t *out, cudaStream_t stream);
 int launch_decode_codebook(const uint32_t *free_words, int64_t free_rows, int64_t rank, int64_t cols,

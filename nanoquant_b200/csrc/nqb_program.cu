@@ -66,6 +66,10 @@ constexpr int kMaxDynamicSmem = 220 * 1024;  // + static shared memory <= 227 KB
 // 1024-word codebook is staged in shared memory per stage 1.
 constexpr uint32_t kCodedSliceBytes = 2560;
 constexpr uint32_t kCodedRowBits = 160;
+// Coded product-codebook slices (nqb_repack_product_codebook): 128 rows x 8
+// 16-bit records, row r's at byte 16 r; the member's 1024-word decode table
+// (first half words, second half words << 16) is staged like a codebook.
+constexpr uint32_t kCodebookSliceBytes = 2048;
 constexpr int kCodebookWords = 1024;
 constexpr int64_t kOverlaySegCols = 1024;  // columns of one int8 overlay row segment (a multiple of 16)
 
@@ -98,10 +102,11 @@ struct MemberDev {
   const void *patch_factor;
   int32_t patch_dtype;
   int64_t patch_offset;       // first latent column of the member's patch latent
-  // stage 1 of a mixed-V member: tiles from coded_from on stream as records
+  // stage 1 of a coded member: tiles from coded_from on stream as records
   const uint8_t *coded_tiles;
   const uint32_t *codebook;   // [1024] words, bulk-copied into shared memory per stage
   int32_t coded_from;         // first coded tile (INT32_MAX: none)
+  int32_t coded_format;       // NQB_CODED_MIXED_V / NQB_CODED_PRODUCT_CODEBOOK
 };
 
 // The decoder-step extensions of an op (nqb_program_op_ext), staged into
@@ -588,6 +593,14 @@ __device__ __forceinline__ uint32_t decode_record(const uint32_t *cb, uint32_t r
   return cb[rec & 1023u] ^ (1u << ((rec >> 10) & 31u)) ^ (1u << (rec >> 15));
 }
 
+// Product-codebook record (16 bits, row r's record j at halfword 8 r + j of
+// the slice) -> sign word: the two half words from the staged table.
+__device__ __forceinline__ uint32_t decode_product_record(const uint32_t *tab, const uint8_t *slice, int row,
+                                                          int j) {
+  const uint32_t rec = reinterpret_cast<const uint16_t *>(slice)[row * 8 + j];
+  return tab[rec & 255u] | tab[256u + (rec >> 8)];
+}
+
 // The producer lane's view of this CTA's slice-address list.
 struct Producer {
   const uint64_t *addrs;
@@ -608,7 +621,8 @@ struct Producer {
   }
 
   // Fill ring position `pos` (slot pos % ring) with slice `pos` of this CTA's
-  // list.  With kMixed, bit 0 of an address marks a coded slice (2432 bytes).
+  // list.  With kMixed, bit 0 of an address marks a coded mixed-V slice
+  // (2560 bytes) and bit 1 a coded product-codebook slice (2048 bytes).
   template <bool kMixed>
   __device__ bool produce(int pos, int slot) const {
     const int chunk = pos / kAddrChunk;
@@ -617,9 +631,9 @@ struct Producer {
     uint64_t src = cache[(chunk % kAddrSlots) * kAddrChunk + pos % kAddrChunk];
     uint32_t bytes = kStageWeightBytes;
     if constexpr (kMixed) {
-      if (src & 1u) {
-        bytes = kCodedSliceBytes;
-        src &= ~uint64_t(1);
+      if (src & 3u) {
+        bytes = (src & 2u) ? kCodebookSliceBytes : kCodedSliceBytes;
+        src &= ~uint64_t(3);
       }
     }
     expect_tx(full + slot, bytes);
@@ -1423,7 +1437,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
         stage_info_copy(p, g, cluster, lane, s_info[g & 1]);
         __syncwarp();
         if (lane == 0) {
-          // a stage 1 with mixed-V members also brings their codebooks (the
+          // a stage 1 with coded members also brings their tables (the
           // previous stage 1, their last reader, has finished everywhere)
           uint32_t coded = 0;
           if constexpr (kMixed) {
@@ -1539,17 +1553,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1) program_kernel(const __grid_
           const uint32_t *cb = (st == 0 && item.tile >= op.md[item.member].coded_from)
                                    ? reinterpret_cast<const uint32_t *>(smem + p.off_cb) + item.member * kCodebookWords
                                    : nullptr;
+          const bool product = op.md[item.member].coded_format == NQB_CODED_PRODUCT_CODEBOOK;
           for (int sl = 0; sl < nst; ++sl) {
             if (!wait_local(&s_full[slot], phase & 1)) ok = false;
             const uint8_t *src = ring + static_cast<size_t>(slot) * kStageWeightBytes;
             mmad::SliceWords w;
             if (cb != nullptr) {
-              const uint32_t *rw = reinterpret_cast<const uint32_t *>(src);
               const int r0 = warp * 16 + (lane >> 2), tig = lane & 3;
-              w.w00 = decode_record(cb, coded_record(rw, r0, tig));
-              w.w10 = decode_record(cb, coded_record(rw, r0 + 8, tig));
-              w.w01 = decode_record(cb, coded_record(rw, r0, 4 + tig));
-              w.w11 = decode_record(cb, coded_record(rw, r0 + 8, 4 + tig));
+              if (product) {
+                w.w00 = decode_product_record(cb, src, r0, tig);
+                w.w10 = decode_product_record(cb, src, r0 + 8, tig);
+                w.w01 = decode_product_record(cb, src, r0, 4 + tig);
+                w.w11 = decode_product_record(cb, src, r0 + 8, 4 + tig);
+              } else {
+                const uint32_t *rw = reinterpret_cast<const uint32_t *>(src);
+                w.w00 = decode_record(cb, coded_record(rw, r0, tig));
+                w.w10 = decode_record(cb, coded_record(rw, r0 + 8, tig));
+                w.w01 = decode_record(cb, coded_record(rw, r0, 4 + tig));
+                w.w11 = decode_record(cb, coded_record(rw, r0 + 8, 4 + tig));
+              }
             } else {
               w = mmad::load_slice_words(src, warp, lane);
             }
@@ -2094,7 +2116,7 @@ static const void *kernel_for_t(int bucket) {
   }
 }
 
-// Step programs (decoder-step extensions) take no patched or coded mixed-V members.
+// Step programs (decoder-step extensions) take no patched or coded members.
 static const void *kernel_for(int bucket, bool patch, bool mixed, bool step) {
   if (step) return kernel_for_t<false, false, true>(bucket);
   if (mixed) return patch ? kernel_for_t<true, true, false>(bucket) : kernel_for_t<false, true, false>(bucket);
@@ -2118,6 +2140,7 @@ static void fill_member(MemberDev &m, const nqb_linear_desc &d, int stage, int64
       m.coded_tiles = static_cast<const uint8_t *>(d.coded_right_tiles);
       m.codebook = reinterpret_cast<const uint32_t *>(d.coded_codebook);
       m.coded_from = static_cast<int32_t>((d.coded_free_rows + kTileRows - 1) / kTileRows);
+      m.coded_format = d.coded_format;
     }
   } else {
     m.tiles = static_cast<const uint8_t *>(d.left_tiles);
@@ -2238,8 +2261,9 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has invalid int8 overlay rows", i, k);
       if (d.coded_right_tiles != nullptr &&
           (d.coded_codebook == nullptr || d.coded_free_rows <= 0 || d.coded_free_rows >= d.rank ||
+           (d.coded_format != NQB_CODED_MIXED_V && d.coded_format != NQB_CODED_PRODUCT_CODEBOOK) ||
            reinterpret_cast<uintptr_t>(d.coded_right_tiles) % 16 || reinterpret_cast<uintptr_t>(d.coded_codebook) % 16))
-        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has invalid coded mixed-V tiles", i, k);
+        return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: member %d has invalid coded right-factor tiles", i, k);
       if (d.in_features != o.layers[0].in_features || d.scale_dtype != o.layers[0].scale_dtype)
         return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: members must share in_features and scale dtype", i);
       if (o.y[k] == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: output %d is NULL", i, k);
@@ -2254,7 +2278,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
     if (e != nullptr) {
       for (int k = 0; k < o.count; ++k)
         if (o.layers[k].patch_rank > 0 || o.layers[k].coded_right_tiles != nullptr || o.layers[k].overlay_rows > 0)
-          return fail(NQB_ERR_UNSUPPORTED, "op %d: decoder-step ops take no patch, coded mixed-V tiles or overlay rows", i);
+          return fail(NQB_ERR_UNSUPPORTED, "op %d: decoder-step ops take no patch, coded right-factor tiles or overlay rows", i);
       if (e->norm_stats != nullptr) {
         if (o.x_dtype != NQB_F32 || e->norm_weight == nullptr || !is_float_dtype(e->norm_weight_dtype) ||
             !(e->eps >= 0.0f))
@@ -2614,13 +2638,16 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
               const int nst = std::min(sp.sc, hi - c0);
               for (size_t j = j0; j < j1; ++j)
                 for (int sl = c0; sl < c0 + nst; ++sl) {
-                  if (st == 0 && list[j].tile >= md.coded_from)  // coded slice: bit 0 set
+                  if (st == 0 && list[j].tile >= md.coded_from) {  // coded slice: tag bit 0 or 1
+                    const bool product = md.coded_format == NQB_CODED_PRODUCT_CODEBOOK;
+                    const uint64_t bytes = product ? kCodebookSliceBytes : kCodedSliceBytes;
                     addrs.push_back((reinterpret_cast<uint64_t>(md.coded_tiles) +
-                                     (static_cast<uint64_t>(list[j].tile - md.coded_from) * md.ks + sl) *
-                                         kCodedSliceBytes) | 1u);
-                  else
+                                     (static_cast<uint64_t>(list[j].tile - md.coded_from) * md.ks + sl) * bytes) |
+                                    (product ? 2u : 1u));
+                  } else {
                     addrs.push_back(reinterpret_cast<uint64_t>(md.tiles) +
                                     (static_cast<uint64_t>(list[j].tile) * md.wc + 2ull * sl) * (kTileRows * kChunkBytes));
+                  }
                 }
             }
             j0 = j1;

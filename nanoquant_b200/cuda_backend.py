@@ -75,6 +75,7 @@ def _build_payload(
     device: torch.device,
     tensor_cores: bool = True,
     coded_mixed_v: bool = False,
+    coded_product_codebook: bool = True,
 ) -> _Sm100Payload:
     spec = state.spec
     tensors: dict[str, torch.Tensor] = {}
@@ -114,6 +115,19 @@ def _build_payload(
             tensors["right_tiles"] = _repack(right_words, spec.rank, spec.in_features)
             desc.left_tiles = tensors["left_tiles"].data_ptr()
             desc.right_tiles = tensors["right_tiles"].data_ptr()
+            if coded_product_codebook:
+                # decode programs stream V's coded rows as 16-bit records and
+                # decode them through the two half-word tables in stage 1
+                from nanoquant_b200.device_ops import repack_product_codebook_cuda
+
+                tensors["coded_right_tiles"], tensors["coded_codebook"] = repack_product_codebook_cuda(
+                    tensors["codebook_payload"].contiguous(), tensors["codebook_first"].contiguous(),
+                    tensors["codebook_second"].contiguous(), rank=spec.rank, columns=spec.in_features,
+                    free_rows=state.free_rows)
+                desc.coded_right_tiles = tensors["coded_right_tiles"].data_ptr()
+                desc.coded_codebook = tensors["coded_codebook"].data_ptr()
+                desc.coded_free_rows = state.free_rows
+                desc.coded_format = _native.NQB_CODED_PRODUCT_CODEBOOK
     else:
         if isinstance(state, MixedVLayerState):
             # expand the 19-bit records once on the device, like the reference
@@ -151,6 +165,7 @@ def _build_payload(
                 desc.coded_right_tiles = tensors["coded_right_tiles"].data_ptr()
                 desc.coded_codebook = codebook.data_ptr()
                 desc.coded_free_rows = state.free_rows
+                desc.coded_format = _native.NQB_CODED_MIXED_V
     desc.scale_pre = keep("scale_pre", scale_pre).data_ptr()
     desc.scale_mid = keep("scale_mid", scale_mid).data_ptr()
     desc.scale_post = keep("scale_post", scale_post).data_ptr()
@@ -321,15 +336,23 @@ class CudaPackedSm100Backend:
     version = CUDA_SM100_BACKEND_VERSION
     packed_layout = PACKED_LAYOUT_VERSION
 
-    def __init__(self, *, tensor_cores: bool = True, coded_mixed_v: bool = False) -> None:
+    def __init__(self, *, tensor_cores: bool = True, coded_mixed_v: bool = False,
+                 coded_product_codebook: bool = True) -> None:
         # tensor_cores=False keeps prepared layers on the CUDA-core kernels only
         # (no kernel-native tile copies); used to cross-check the two paths.
         # coded_mixed_v=True also keeps a mixed-V layer's V as coded tiles, which
         # decode programs stream and decode in stage 1 (38 % fewer V bytes; at
         # batch 1 the record decode costs more time than the bytes save, so the
         # expanded tiles are the default).
+        # coded_product_codebook (the default) does the same for a
+        # product-codebook layer's V: 16-bit records, half the bytes of sign
+        # words, decoded through the two half-word tables in the program's
+        # stage 1 (within 1 % of the expanded tiles' time at batch 1 and 16,
+        # where the step is latency-bound).  The per-call paths keep
+        # streaming the expanded tiles.
         self.tensor_cores = tensor_cores
         self.coded_mixed_v = coded_mixed_v
+        self.coded_product_codebook = coded_product_codebook
 
     def capabilities(self) -> BackendCapabilities:
         return BackendCapabilities(
@@ -385,7 +408,8 @@ class CudaPackedSm100Backend:
         target = _cuda_device(device)
         _native.library()
         with torch.cuda.device(target):
-            payload = _build_payload(base, overlay, target, self.tensor_cores, self.coded_mixed_v)
+            payload = _build_payload(base, overlay, target, self.tensor_cores, self.coded_mixed_v,
+                                     self.coded_product_codebook)
         return PreparedLayer(self.name, self.version, state.spec, payload)
 
     def linear(self, value: torch.Tensor, layer: PreparedLayer) -> torch.Tensor:

@@ -187,7 +187,8 @@ class DecodeChain:
     """All packed linears of a decoder, run for one decode step (batch ``tokens``)."""
 
     def __init__(self, shape: DecoderShape, blocks: list[dict[str, PackedLayerState]], device: torch.device,
-                 tokens: int = 1, engine: str | None = None) -> None:
+                 tokens: int = 1, engine: str | None = None,
+                 backend: CudaPackedSm100Backend | None = None) -> None:
         if engine is None:
             engine = "program" if tokens <= 16 else "calls"
         if engine not in ("program", "calls"):
@@ -198,7 +199,7 @@ class DecodeChain:
         self.device = device
         self.tokens = tokens
         self.engine = engine
-        self.backend = CudaPackedSm100Backend()
+        self.backend = backend if backend is not None else CudaPackedSm100Backend()
         self.blocks: list[_PreparedBlock] = []
         first = blocks[0] if blocks else {}
         self.codebook_rows = ({proj: int(state.overlay.row_ids.numel()) for proj, state in first.items()}

@@ -135,9 +135,10 @@ def decode_mixed_v_cuda(
 def repack_mixed_v_cuda(payload: torch.Tensor, *, rank: int, columns: int, free_rows: int) -> torch.Tensor:
     """Coded mixed-V tiles for decode programs (``nqb_repack_mixed_v``) -> uint8 bytes.
 
-    Tiles of 128 rows from ``ceil(free_rows / 128)`` on keep their 19-bit
-    records: per 256-column slice, row ``r``'s 8 records back to back from bit
-    ``152 r`` (2432 bytes per tile slice).
+    Tiles of 128 rows from ``ceil(free_rows / 128)`` on keep their records,
+    widened to 20 bits with the pair id resolved (index | a << 10 | b << 15):
+    per 256-column slice, row ``r``'s 8 records back to back from bit ``160 r``
+    (2560 bytes per tile slice).
     """
 
     _require_cuda(payload, "payload")
@@ -152,3 +153,32 @@ def repack_mixed_v_cuda(payload: torch.Tensor, *, rank: int, columns: int, free_
         _native.call("nqb_repack_mixed_v", payload.data_ptr(), rank, columns, free_rows, out.data_ptr(),
                      _native.current_stream_handle(payload.device))
     return out
+
+
+def repack_product_codebook_cuda(payload: torch.Tensor, first: torch.Tensor, second: torch.Tensor, *, rank: int,
+                                 columns: int, free_rows: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Coded product-codebook tiles and their decode table (``nqb_repack_product_codebook``).
+
+    Returns ``(tiles, table)``: tiles of 128 rows from ``ceil(free_rows /
+    128)`` on keep one 16-bit record per word, per 256-column slice row ``r``'s
+    8 records at byte ``16 r`` (2048 bytes per tile slice); ``table`` is int32
+    ``[1024]``: the first half words, the second half words shifted to bits
+    16..31, zeros.
+    """
+
+    for name, value in (("payload", payload), ("first", first), ("second", second)):
+        _require_cuda(value, name)
+    if payload.dtype != torch.int32 or not payload.is_contiguous():
+        raise ValueError("product-codebook payload must be contiguous int32")
+    for name, value in (("first", first), ("second", second)):
+        if value.dtype != torch.int16 or value.shape != (256,) or not value.is_contiguous():
+            raise ValueError(f"product-codebook {name} half table must be contiguous int16 [256]")
+    if payload.numel() * 2 < (rank - free_rows) * packed_word_count(columns):
+        raise ValueError("product-codebook payload is shorter than its records")
+    size = ctypes.c_size_t(0)
+    _native.call("nqb_product_codebook_tiles_bytes", rank, columns, free_rows, ctypes.byref(size))
+    tiles = torch.zeros(max(size.value, 16), dtype=torch.uint8, device=payload.device)
+    table = torch.empty(1024, dtype=torch.int32, device=payload.device)
+    _native.call("nqb_repack_product_codebook", payload.data_ptr(), first.data_ptr(), second.data_ptr(), rank,
+                 columns, free_rows, tiles.data_ptr(), table.data_ptr(), _native.current_stream_handle(payload.device))
+    return tiles, table

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol() -> None:
     lib = _native.library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.nqb_abi_version() == 4
+    assert lib.nqb_abi_version() == 5
 
 
 def _desc() -> _native.LinearDesc:
