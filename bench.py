@@ -574,7 +574,8 @@ WORKLOADS = {
                                                       "codebook V + 1% int8 rows); HBM GB/s",
                         "tokens": 1,
                         "description": "gemma-3-1b product-codebook packed linears with int8 outlier rows, decode bs1 "
-                                       "({layers} layers x q,k,v,o,gate,up,down in one program)",
+                                       "({layers} layers x q,k,v,o,gate,up,down in one program; V streamed as "
+                                       "16-bit records and decoded in stage 1)",
                         "model": "config 4: 8-bit group indices into one 256-entry 16-bit table per layer, plain U, "
                                  "1% int8 rows (scale 0.002)"},
     "codebook-prefill": {"kind": "codebook", "metric": "codebook prefill tok/s (bs64, Gemma-3-1B shapes, product-"

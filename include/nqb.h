@@ -67,7 +67,13 @@ typedef struct nqb_linear_desc {
 
   const int32_t *left_words;  /* U, [m, ceil(r/32)] layout v1                */
   const int32_t *right_words; /* V, [r, ceil(n/32)] layout v1; NULL when the
-                                 product-codebook fields below are used      */
+                                 product-codebook fields below are used.
+                                 A tiles-only layer sets both word pointers
+                                 and codebook_payload NULL and gives both tile
+                                 copies below: it runs on the tensor-core
+                                 decode, prefill and program paths, and a call
+                                 that would take the generic path returns
+                                 NQB_ERR_UNSUPPORTED                          */
 
   const void *scale_pre;  /* [n] */
   const void *scale_mid;  /* [r] */

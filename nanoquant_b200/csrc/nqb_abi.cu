@@ -72,7 +72,16 @@ static int validate_layer(const nqb_linear_desc *d, const char *name) {
     return fail(NQB_ERR_INVALID_ARGUMENT, "%s: in_features, out_features and rank must be positive", name);
   if (d->in_features > (1ll << 31) || d->out_features > (1ll << 31) || d->rank > (1ll << 31))
     return fail(NQB_ERR_UNSUPPORTED, "%s: dimensions above 2^31 are not supported", name);
-  if (d->left_words == nullptr) return fail(NQB_ERR_INVALID_ARGUMENT, "%s: left_words is NULL", name);
+  // A tiles-only layer (no layout-v1 words, no compact V) runs on the
+  // tensor-core decode, prefill and program paths, which read the tiles only.
+  const bool tiles_only = d->left_words == nullptr && d->right_words == nullptr && d->codebook_payload == nullptr;
+  if (tiles_only) {
+    if (d->left_tiles == nullptr || d->right_tiles == nullptr)
+      return fail(NQB_ERR_INVALID_ARGUMENT, "%s: left_words is NULL (a layer without words needs both tile copies)",
+                  name);
+  } else if (d->left_words == nullptr) {
+    return fail(NQB_ERR_INVALID_ARGUMENT, "%s: left_words is NULL", name);
+  }
   const bool codebook = d->codebook_payload != nullptr;
   if (codebook) {
     if (d->right_words != nullptr)
@@ -84,10 +93,10 @@ static int validate_layer(const nqb_linear_desc *d, const char *name) {
     if (!aligned(d->codebook_free_words, 4) || !aligned(d->codebook_payload, 4) ||
         !aligned(d->codebook_first, 2) || !aligned(d->codebook_second, 2))
       return fail(NQB_ERR_ALIGNMENT, "%s: product-codebook operands are misaligned", name);
-  } else if (d->right_words == nullptr) {
+  } else if (d->right_words == nullptr && !tiles_only) {
     return fail(NQB_ERR_INVALID_ARGUMENT, "%s: right_words is NULL", name);
   }
-  if (!aligned(d->left_words, 4) || (d->right_words && !aligned(d->right_words, 4)))
+  if ((d->left_words && !aligned(d->left_words, 4)) || (d->right_words && !aligned(d->right_words, 4)))
     return fail(NQB_ERR_ALIGNMENT, "%s: sign words must be 4-byte aligned", name);
   if (!is_float_dtype(d->scale_dtype))
     return fail(NQB_ERR_DTYPE, "%s: scale dtype %d is not F32/F16/BF16", name, d->scale_dtype);
@@ -323,6 +332,12 @@ static int run_layers(const nqb_linear_desc *layers, int count, const void *x, i
   if (prefill_eligible(layers, count, x_dtype, tokens)) {
     NQB_CHECK(run_prefill(layers, count, x, x_dtype, tokens, ys, latent, extra, tc_need, s));
   } else {
+    for (int i = 0; i < count; ++i)
+      if (layers[i].left_words == nullptr)
+        return fail(NQB_ERR_UNSUPPORTED,
+                    "layer %d keeps only its kernel-native tiles, and %lld token(s) of this input take the generic "
+                    "path, which reads the layout-v1 words",
+                    i, static_cast<long long>(tokens));
     NQB_CHECK(run_generic(layers, count, x, x_dtype, tokens, ys, latent, s));
   }
   int64_t patch_offset = 0;

@@ -69,6 +69,12 @@ def _repack(words: torch.Tensor, rows: int, columns: int) -> torch.Tensor:
     return tiles
 
 
+# A grouped call runs on the tensor-core paths while its members' 128-row
+# tiles (rank and output rows) fit the library's 4096 completion counters;
+# layers up to a third of that stay eligible in any group of three.
+_TILES_ONLY_MAX_ROW_TILES = 4096 // 3
+
+
 def _build_payload(
     state: PackedLayerState | ProductCodebookLayerState | MixedVLayerState,
     overlay: OutlierRowOverlay | None,
@@ -76,6 +82,7 @@ def _build_payload(
     tensor_cores: bool = True,
     coded_mixed_v: bool = False,
     coded_product_codebook: bool = True,
+    keep_words: bool = False,
 ) -> _Sm100Payload:
     spec = state.spec
     tensors: dict[str, torch.Tensor] = {}
@@ -193,6 +200,16 @@ def _build_payload(
         desc.patch_left = patch_left.data_ptr()
         desc.patch_right = patch_right.data_ptr()
         desc.patch_dtype = _native.dtype_code(patch_left.dtype)
+    row_tiles = -(-spec.rank // 128) + -(-spec.out_features // 128)
+    if tensor_cores and not keep_words and row_tiles <= _TILES_ONLY_MAX_ROW_TILES:
+        # tiles-only layer: every call shape it can take runs on the tensor-core
+        # decode, prefill or program paths, which read the tiles only, so the
+        # layout-v1 words (and a codebook layer's compact V) leave the device
+        for name in ("left_words", "right_words", "codebook_free_words", "codebook_payload", "codebook_first",
+                     "codebook_second"):
+            tensors.pop(name, None)
+        desc.left_words = desc.right_words = None
+        desc.codebook_free_words = desc.codebook_payload = desc.codebook_first = desc.codebook_second = None
     return _Sm100Payload(device, tensors, desc, patch_left, patch_right)
 
 
@@ -337,7 +354,7 @@ class CudaPackedSm100Backend:
     packed_layout = PACKED_LAYOUT_VERSION
 
     def __init__(self, *, tensor_cores: bool = True, coded_mixed_v: bool = False,
-                 coded_product_codebook: bool = True) -> None:
+                 coded_product_codebook: bool = True, keep_words: bool = False) -> None:
         # tensor_cores=False keeps prepared layers on the CUDA-core kernels only
         # (no kernel-native tile copies); used to cross-check the two paths.
         # coded_mixed_v=True also keeps a mixed-V layer's V as coded tiles, which
@@ -353,6 +370,11 @@ class CudaPackedSm100Backend:
         self.tensor_cores = tensor_cores
         self.coded_mixed_v = coded_mixed_v
         self.coded_product_codebook = coded_product_codebook
+        # keep_words=True keeps the layout-v1 words on the device after the
+        # tile copies are made; without it a tensor-core layer holds its
+        # tiles only (half the sign memory), and a call that would take the
+        # generic path (more than 2^22 tokens) raises.
+        self.keep_words = keep_words
 
     def capabilities(self) -> BackendCapabilities:
         return BackendCapabilities(
@@ -409,7 +431,7 @@ class CudaPackedSm100Backend:
         _native.library()
         with torch.cuda.device(target):
             payload = _build_payload(base, overlay, target, self.tensor_cores, self.coded_mixed_v,
-                                     self.coded_product_codebook)
+                                     self.coded_product_codebook, self.keep_words)
         return PreparedLayer(self.name, self.version, state.spec, payload)
 
     def linear(self, value: torch.Tensor, layer: PreparedLayer) -> torch.Tensor:

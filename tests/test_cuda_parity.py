@@ -466,3 +466,20 @@ def test_prefill_grouped_projection_and_overlay() -> None:
     for got, ref in ((gate_out, gate_ref), (up_out, oracle_from_state(up))):
         expected = po.packed_linear(x.float().numpy(), ref, accumulate="float64")
         assert _relative_max_error(got, expected) <= PREFILL_BOUND
+
+
+def test_prepared_layers_hold_tiles_only_unless_asked() -> None:
+    """After the tile copies are made the layout-v1 words leave the device; results do not change."""
+
+    state = _random_state(640, 384, 200, seed=11, outliers=2, bias=True)
+    lean = CudaPackedSm100Backend().prepare(state, "cuda")
+    full = CudaPackedSm100Backend(keep_words=True).prepare(state, "cuda")
+    assert not lean.payload.desc.left_words and not lean.payload.desc.right_words
+    assert "left_words" not in lean.payload.tensors and "right_words" not in lean.payload.tensors
+    assert full.payload.desc.left_words and full.payload.desc.right_words
+    backend = CudaPackedSm100Backend()
+    g = torch.Generator().manual_seed(11)
+    for tokens in (1, 7, 40):
+        x = torch.randn(tokens, 640, generator=g).bfloat16().cuda()
+        assert torch.equal(backend.linear(x, lean), backend.linear(x, full))
+    assert ctypes_status() == 0

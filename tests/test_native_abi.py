@@ -138,6 +138,25 @@ def test_input_and_workspace_validation() -> None:
     assert status == _native.NQB_ERR_WORKSPACE and "workspace" in text
 
 
+def test_tiles_only_layers_validate_and_refuse_the_generic_path() -> None:
+    desc = _desc()
+    desc.left_words = desc.right_words = None
+    size = ctypes.c_size_t(0)
+    status, text = _status("nqb_linear_workspace_bytes", ctypes.byref(desc), 8, ctypes.byref(size))
+    assert status == _native.NQB_ERR_INVALID_ARGUMENT and "needs both tile copies" in text
+    desc.left_tiles, desc.right_tiles = 0x90000, 0xA0000  # fake, never dereferenced
+    status, _ = _status("nqb_linear_workspace_bytes", ctypes.byref(desc), 8, ctypes.byref(size))
+    assert status == _native.NQB_OK
+    tokens = (1 << 22) + 1  # past the prefill path's token limit: only the generic kernels take it
+    path = ctypes.c_int32(-1)
+    status, _ = _status("nqb_linear_path", ctypes.byref(desc), 1, _native.NQB_BF16, tokens, ctypes.byref(path))
+    assert status == _native.NQB_OK and path.value == _native.NQB_PATH_GENERIC
+    # refused on the host before any launch
+    status, text = _status("nqb_linear", ctypes.byref(desc), 0x50000, _native.NQB_BF16, tokens, 0x60000, 0x100000,
+                           1 << 40, None)
+    assert status == _native.NQB_ERR_UNSUPPORTED and "generic path" in text
+
+
 def test_grouped_rejects_mismatched_inputs() -> None:
     descs = (_native.LinearDesc * 2)(_desc(), _desc())
     descs[1].in_features = 65
