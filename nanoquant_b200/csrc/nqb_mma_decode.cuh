@@ -539,6 +539,33 @@ __device__ __forceinline__ void drain_to_acc(int32_t (&d)[acc_sets(n_tiles(kT))]
     }
   const int r0 = warp * 16 + g;
   constexpr int kD = digits_for(kT);
+  if constexpr (kD == 2) {
+    // Two digits: columns 2t and 2t + 1 (both digits of token t = 4 nt + tig)
+    // are this lane's registers c and c + 1, so every lane combines its own
+    // tokens without shuffles (same arithmetic, same single writer per entry).
+    static_assert(kT == 4 * kNT, "two digits per token fill whole N tiles");
+#pragma unroll
+    for (int nt = 0; nt < kNT; ++nt) {
+      const int t = nt * 4 + tig;
+      int et = e[nt * 4];
+      long long qt = Q[nt * 4];
+#pragma unroll
+      for (int k = 1; k < 4; ++k)
+        if (tig == k) {
+          et = e[nt * 4 + k];
+          qt = Q[nt * 4 + k];
+        }
+      if (t < T) {
+        const float unscale = tc::exp2_int(-et);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const long long s = static_cast<long long>(v[nt][2 * rr + 1]) * 256 + v[nt][2 * rr];
+          acc[t * kTileRows + r0 + rr * 8] += __ll2float_rn(qt - 2 * s) * unscale;
+        }
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int t = 0; t < kT; ++t) {
     // digit dd of token t sits in column kD t + dd: N tile (kD t+dd)/8, lane tig ((kD t+dd)%8)/2, register (..)%2
