@@ -546,8 +546,8 @@ WORKLOADS = {
                         "lm head, bf16 kv cache N(0,1)"},
     "decode-bs16": {"kind": "step", "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); HBM GB/s vs peak",
                     "tokens": 16,
-                    "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head, 2048 cached "
-                                   "tokens)",
+                    "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head): 16 new "
+                                   "tokens of one sequence on its 2048-token cache (KV rows read once per step)",
                     "model": "qwen3-8b-shape random-init, as decode"},
     "gemma1b": {"kind": "gemma", "metric": "decode tok/s (bs1, Gemma-3-1B shape ~1 bpw); HBM GB/s vs peak",
                 "tokens": 1,
