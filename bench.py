@@ -22,7 +22,9 @@ The same line carries:
   one 4096-token sequence with every linear's U rows split over the ranks and
   the output slices all-gathered over NCCL.
 
-Other workloads (``--workload``): ``decode-bs16`` (config 2 at batch 16),
+Other workloads (``--workload``): ``decode-bs16`` (config 2 at batch 16: 16
+independent sequences, each on its own cache), ``decode-16tok`` (16 new
+tokens of one sequence),
 ``gemma1b`` (config 1: the full Gemma-3-1B-shaped step from token ids),
 ``linears`` / ``linears-bs16`` (the packed linears alone), ``prefill``
 (config 3 alone), ``single-linear`` (config 0, ``--tokens`` 1 or 8) and
@@ -150,16 +152,17 @@ def _device_status() -> int:
 
 # ----------------------------------------------------------- CPU baseline ---
 
-def _qwen3_cpu_step(tokens: int, layers: int = 36):
+def _qwen3_cpu_step(tokens: int, layers: int = 36, sequences: bool = False):
     from nanoquant_b200.decode_chain import QWEN3_8B as s
     from oracle.decoder_oracle import CpuDecodeStep
 
     return CpuDecodeStep(layers=layers, hidden=s.hidden, intermediate=s.intermediate, q_heads=s.q_heads,
                          kv_heads=s.kv_heads, head_dim=s.head_dim, vocab=STEP_VOCAB, position=STEP_POSITION,
-                         tokens=tokens, pool=1)
+                         tokens=tokens, pool=1, sequences=sequences)
 
 
-def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: float = 240.0) -> dict:
+def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: float = 240.0,
+                      sequences: bool = False) -> dict:
     """The reference's CPU path for the full step: ``warmup`` untimed then ``steps`` timed full steps.
 
     Every step runs all 36 layers and the lm head.  When ``warmup + steps``
@@ -168,7 +171,7 @@ def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: fl
     """
 
     setup = time.perf_counter()
-    cpu = _qwen3_cpu_step(tokens)
+    cpu = _qwen3_cpu_step(tokens, sequences=sequences)
     setup_s = time.perf_counter() - setup
     start = time.perf_counter()
     cpu.step()  # first warm-up step, also the estimate
@@ -191,7 +194,8 @@ def cpu_step_baseline(tokens: int, steps: int = 1, warmup: int = 1, budget_s: fl
     return {
         "value": tokens / per_step, "unit": UNIT, "cores": threads, "kind": "port",
         "cpu_model": _cpu_model(), "ms_per_step": per_step * 1e3, "steps": steps, "warmup": warmup,
-        "sample": f"full qwen3-8b decode step, {tokens} token(s): 36 layers of the oracle port of "
+        "sample": f"full qwen3-8b decode step, {tokens} token(s)"
+                  f"{' of independent sequences' if sequences else ''}: 36 layers of the oracle port of "
                   f"PackedReferenceBackend.linear (fp32 numpy/BLAS on dense +/-1 signs unpacked once) and the model "
                   f"shell (norms, q/k norm + rope, attention over {STEP_POSITION + 1} cached rows, swiglu), final "
                   f"norm and the {STEP_VOCAB} x 4096 lm head; {threads} host threads ({_cpu_model()}); {steps} timed "
@@ -342,12 +346,12 @@ class StepRunner:
 
     bound = "hbm"
 
-    def __init__(self, device, tokens: int, layers: int | None) -> None:
+    def __init__(self, device, tokens: int, layers: int | None, sequences: bool = False) -> None:
         from nanoquant_b200.decode_chain import QWEN3_8B
         from nanoquant_b200.decoder import build_qwen3_step
 
         self.step_obj = build_qwen3_step(QWEN3_8B, device, vocab=STEP_VOCAB, tokens=tokens, position=STEP_POSITION,
-                                         layers=layers)
+                                         layers=layers, sequences=sequences)
         self.tokens = tokens
         self.layers = len(self.step_obj.layers)
         self.input = self.step_obj.hidden_in
@@ -545,10 +549,16 @@ WORKLOADS = {
                "model": "qwen3-8b-shape random-init: packed weights ~1 bpw (layout v1, fp16 scales), bf16 norms and "
                         "lm head, bf16 kv cache N(0,1)"},
     "decode-bs16": {"kind": "step", "metric": "decode tok/s (bs16, Qwen3-8B shape ~1 bpw); HBM GB/s vs peak",
-                    "tokens": 16,
-                    "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head): 16 new "
-                                   "tokens of one sequence on its 2048-token cache (KV rows read once per step)",
+                    "tokens": 16, "sequences": True,
+                    "description": "qwen3-8b decode step bs16 ({layers} layers, full shell and lm head): 16 "
+                                   "independent sequences, each the next token on its own 2048-token cache",
                     "model": "qwen3-8b-shape random-init, as decode"},
+    "decode-16tok": {"kind": "step", "metric": "decode tok/s (16 new tokens of one sequence, Qwen3-8B shape ~1 bpw); "
+                                               "HBM GB/s vs peak",
+                     "tokens": 16,
+                     "description": "qwen3-8b decode step of 16 new tokens of one sequence ({layers} layers, full "
+                                    "shell and lm head) on its 2048-token cache (KV rows read once per step)",
+                     "model": "qwen3-8b-shape random-init, as decode"},
     "gemma1b": {"kind": "gemma", "metric": "decode tok/s (bs1, Gemma-3-1B shape ~1 bpw); HBM GB/s vs peak",
                 "tokens": 1,
                 "description": "gemma-3-1b decode step bs1 ({layers} layers: bf16 embedding, sandwich norms, packed "
@@ -602,7 +612,7 @@ def _build(name: str, device, tokens: int, layers: int | None, engine: str | Non
 
     kind = WORKLOADS[name]["kind"]
     if kind == "step":
-        return StepRunner(device, tokens, layers)
+        return StepRunner(device, tokens, layers, WORKLOADS[name].get("sequences", False))
     if kind == "gemma":
         return GemmaStepRunner(device, tokens, layers)
     if kind == "codebook":
@@ -782,7 +792,7 @@ def run_reference(args, rank: int) -> None:
     kind = spec["kind"]
     tokens = args.tokens or spec.get("tokens", 1)
     if kind == "step":
-        base = cpu_step_baseline(tokens, steps=args.steps, warmup=args.warmup)
+        base = cpu_step_baseline(tokens, steps=args.steps, warmup=args.warmup, sequences=spec.get("sequences", False))
     elif kind == "gemma":
         base = cpu_gemma_baseline(tokens, steps=args.steps, warmup=args.warmup)
     elif kind == "prefill":
@@ -961,7 +971,7 @@ def main() -> None:
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if kind == "step":
-            base = cpu_step_baseline(tokens)
+            base = cpu_step_baseline(tokens, sequences=WORKLOADS[args.workload].get("sequences", False))
         elif kind == "gemma":
             base = cpu_gemma_baseline(tokens)
         elif kind == "prefill":

@@ -482,6 +482,15 @@ typedef struct nqb_program_op_ext {
   int64_t cache_len;
   int64_t position;          /* first row of this step's tokens in the caches */
   void *attn_out;            /* NQB_OP_ATTENTION: bf16 [tokens, q_heads * head_dim] */
+  /* 0: the tokens are consecutive positions of one sequence (token t at
+   * cache row position + t, attending to rows [0, position + t]).  > 0: a
+   * batch of independent sequences, token t the next token of sequence t,
+   * whose caches start sequence_stride elements after sequence t - 1's
+   * (k_cache / v_cache then hold [tokens][kv_heads, cache_len, head_dim]):
+   * token t at row `position` of its own caches, attending to rows
+   * [0, position].  A multiple of 8, at least kv_heads * cache_len *
+   * head_dim; the same on an op's QK_ROPE epilogue and its attention op.   */
+  int64_t sequence_stride;
 } nqb_program_op_ext;
 
 typedef struct nqb_program_op {

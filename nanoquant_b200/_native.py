@@ -128,6 +128,7 @@ class ProgramOpExt(ctypes.Structure):
         ("cache_len", _i64),
         ("position", _i64),
         ("attn_out", _c_void_p),
+        ("sequence_stride", _i64),
     ]
 
 

@@ -125,6 +125,7 @@ struct __align__(8) StepDev {
   __nv_bfloat16 *q;              // [tokens][q_heads * 128]
   __nv_bfloat16 *k_cache, *v_cache;
   int64_t cache_len, position;
+  int64_t seq_stride;            // 0: one sequence; else token t's caches start t * seq_stride elements in
   __nv_bfloat16 *attn_out;
   int32_t att_splits;
   int32_t att_parts;         // partials per (token, q head): splits, or 2 x splits from 8 tokens on (key halves)
@@ -751,6 +752,30 @@ constexpr int kAttPadRow = kAttHd * 2 + 16;  // staged K/V row stride of the ten
 // the tensor-core path stages two halves x (K, V) x 16 rows in the consumers'
 // accumulator and exchange buffers, which are idle during attention stages
 constexpr int kAttStageBytes = 2 * 2 * 16 * kAttPadRow;
+constexpr int64_t kAttPrefetchRows = 512;  // K/V rows per attention unit on the L2 prefetch list
+constexpr int kAttAhead = 4;               // sub-blocks a warp prefetches ahead of its global K/V reads
+
+// Attention units: (kv head, key split), and with independent sequences
+// (seq_stride > 0) one set per token; unit u -> token tu (0 for one
+// sequence), kv head, split.
+__host__ __device__ inline int att_units(const StepDev &op, int tokens) {
+  return (op.seq_stride != 0 ? tokens : 1) * op.kv_heads * op.att_splits;
+}
+__host__ __device__ inline void att_unit_of(const StepDev &op, int u, int &tu, int &kvh, int &sp) {
+  const int per = op.kv_heads * op.att_splits;
+  tu = u / per;
+  const int r = u - tu * per;
+  kvh = r / op.att_splits;
+  sp = r - kvh * op.att_splits;
+}
+// Element offset of kv head `head`'s cache row `row` in the caches of token tu's sequence.
+__host__ __device__ inline int64_t att_cache_offset(const StepDev &op, int tu, int head, int64_t row) {
+  return static_cast<int64_t>(tu) * op.seq_stride + (static_cast<int64_t>(head) * op.cache_len + row) * kAttHd;
+}
+// Element offset of token t's new row of kv head `head`.
+__host__ __device__ inline int64_t att_new_row(const StepDev &op, int t, int head) {
+  return op.seq_stride != 0 ? att_cache_offset(op, t, head, op.position) : att_cache_offset(op, 0, head, op.position + t);
+}
 
 // Named barrier of the 128 leader threads (consumer warps 0..3).
 __device__ __forceinline__ void leader_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
@@ -853,10 +878,12 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
   } while (0)
 #endif
   const int T = p.tokens;
-  const int units = op.kv_heads * op.att_splits;
+  const int units = att_units(op, T);
   const int cta = static_cast<int>(blockIdx.x);
   if (cta >= units) return;  // uniform over the CTA
-  const int kvh = cta / op.att_splits, sp = cta - kvh * op.att_splits;
+  int tu, kvh, sp;
+  att_unit_of(op, cta, tu, kvh, sp);
+  const bool seqs = op.seq_stride != 0;  // independent sequences: this unit serves token tu only
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int R = p.ring;
   const int nb = att_unit_ring_blocks(op, sp);
@@ -871,8 +898,8 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
   NQB_ATT_TRACE(kTraceWaitSigns);
   const int64_t ring_rows = 16 * static_cast<int64_t>(nb);
   const float scale = rsqrtf(static_cast<float>(kAttHd));
-  const __nv_bfloat16 *kbase = op.k_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
-  const __nv_bfloat16 *vbase = op.v_cache + static_cast<int64_t>(kvh) * op.cache_len * kAttHd + lane * 4;
+  const __nv_bfloat16 *kbase = op.k_cache + att_cache_offset(op, tu, kvh, 0) + lane * 4;
+  const __nv_bfloat16 *vbase = op.v_cache + att_cache_offset(op, tu, kvh, 0) + lane * 4;
   // one 8-key sub-block [b0, b0 + nk) of the split's K and V rows: from the
   // ring where the unit's blocks are, else from global memory (L2)
   auto load_block = [&](int64_t k0, int64_t b0, int nk, uint2 (&kr)[kAttSub], uint2 (&vr)[kAttSub]) {
@@ -960,18 +987,32 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
     }
   };
   // token t over this split's keys b0 = first, first + step, .. (8-key sub-blocks)
+  // L2 prefetch of the sub-block at b0 when it is read from global memory:
+  // lanes 0-15 the K rows' 128-byte lines, lanes 16-31 the V rows'
+  const __nv_bfloat16 *krows = kbase - lane * 4, *vrows = vbase - lane * 4;
+  auto prefetch_block = [&](int64_t k0, int64_t b0, int64_t k1) {
+    const int64_t r = b0 + ((lane & 15) >> 1);
+    if (b0 - k0 >= ring_rows && r < k1) {
+      const __nv_bfloat16 *row = (lane < 16 ? krows : vrows) + r * kAttHd + (lane & 1) * (kAttHd / 2);
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(row));
+    }
+  };
   auto token_keys = [&](int t, int64_t k0, int64_t k1, int64_t first, int64_t step, float (&acc)[kAttGroup][4],
                         float (&m)[kAttGroup], float (&l)[kAttGroup]) {
     float qv[kAttGroup][4];
     load_q(t, qv, acc, m, l);
+    // sub-blocks kAttAhead steps ahead of the one being read are prefetched into L2
+#pragma unroll 1
+    for (int j = 0; j < kAttAhead; ++j) prefetch_block(k0, first + j * step, k1);
     for (int64_t b0 = first; b0 < k1; b0 += step) {
+      prefetch_block(k0, b0 + kAttAhead * step, k1);
       const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
       uint2 kr[kAttSub], vr[kAttSub];
       load_block(k0, b0, nk, kr, vr);
       block_update(kr, vr, nk, qv, acc, m, l);
     }
   };
-  if (kMany && T >= mmad::kWarps) {
+  if (kMany && T >= mmad::kWarps && !seqs) {
     // many tokens, on the tensor cores (mma.sync m16n8k16 bf16, fp32
     // accumulators): the unit's query rows r = 4 tl + h (token 4 rb + tl, q
     // head h of this kv head) in 16-row blocks rb; warp w < 4 takes block w
@@ -1125,9 +1166,9 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
     }
     NQB_ATT_TRACE(kTraceMma);
   } else {
-  for (int t = 0; t < T; ++t) {
+  for (int t = seqs ? tu : 0; t < (seqs ? tu + 1 : T); ++t) {
     const int64_t k0 = static_cast<int64_t>(sp) * op.att_chunk;
-    const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + t);
+    const int64_t k1 = min(k0 + op.att_chunk, op.position + 1 + (seqs ? 0 : t));
     float acc[kAttGroup][4], m[kAttGroup], l[kAttGroup];
     token_keys(t, k0, k1, k0 + warp * kAttSub, static_cast<int64_t>(kAttSub) * mmad::kWarps, acc, m, l);
     NQB_ATT_TRACE(kTraceMma);
@@ -1265,8 +1306,7 @@ __device__ __forceinline__ void qk_rope_epilogue(const StepDev &op, int member, 
 #pragma unroll
     for (int t = 0; t < kT; ++t)
       if (t < T)
-        op.v_cache[(static_cast<int64_t>(tile) * op.cache_len + op.position + t) * kAttHd + d] =
-            __float2bfloat16_rn(outv[t]);
+        op.v_cache[att_new_row(op, t, tile) + d] = __float2bfloat16_rn(outv[t]);
     return;
   }
   const float *w = member == 0 ? op.q_norm : op.k_norm;
@@ -1297,7 +1337,7 @@ __device__ __forceinline__ void qk_rope_epilogue(const StepDev &op, int member, 
     if (member == 0)
       op.q[(static_cast<int64_t>(t) * op.q_heads + tile) * kAttHd + d] = __float2bfloat16_rn(o);
     else
-      op.k_cache[(static_cast<int64_t>(tile) * op.cache_len + op.position + t) * kAttHd + d] = __float2bfloat16_rn(o);
+      op.k_cache[att_new_row(op, t, tile) + d] = __float2bfloat16_rn(o);
   }
   leader_sync();  // xs and red are reused by the next tile
 }
@@ -2069,6 +2109,16 @@ static int token_bucket(int64_t tokens) {
   return tokens <= 1 ? 1 : tokens <= 2 ? 2 : tokens <= 4 ? 4 : tokens <= 8 ? 8 : 16;
 }
 
+// The caches of a step op: one sequence (rows position .. position + tokens
+// - 1 new) or `tokens` independent sequences of sequence_stride elements
+// each (row `position` new in every one).
+static bool cache_layout_ok(const nqb_program_op_ext *e, int64_t tokens) {
+  if (e->position < 0) return false;
+  if (e->sequence_stride == 0) return e->position + tokens <= e->cache_len;
+  return e->sequence_stride > 0 && e->sequence_stride % 8 == 0 && e->position + 1 <= e->cache_len &&
+         e->sequence_stride >= static_cast<int64_t>(e->kv_heads) * e->cache_len * kAttHd;
+}
+
 struct SmemPlan {
   int sc, group, ring;
   uint32_t off_addr, off_b, off_acc, off_exch, off_cb, off_epi, total;
@@ -2231,7 +2281,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
           return fail(NQB_ERR_UNSUPPORTED, "op %d: fused attention takes head_dim %d and %d q heads per kv head", i,
                       kAttHd, kAttGroup);
         if (e->q == nullptr || e->k_cache == nullptr || e->v_cache == nullptr || e->attn_out == nullptr ||
-            e->position < 0 || e->position + tokens > e->cache_len)
+            !cache_layout_ok(e, tokens))
           return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: attention operands or cache position invalid", i);
         if (reinterpret_cast<uintptr_t>(e->q) % 16 || reinterpret_cast<uintptr_t>(e->k_cache) % 16 ||
             reinterpret_cast<uintptr_t>(e->v_cache) % 16 || reinterpret_cast<uintptr_t>(e->attn_out) % 16)
@@ -2297,7 +2347,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
             o.layers[2].out_features != static_cast<int64_t>(e->kv_heads) * kAttHd)
           return fail(NQB_ERR_UNSUPPORTED, "op %d: the q/k epilogue takes q, k, v members of head_dim %d", i, kAttHd);
         if (e->cos_table == nullptr || e->sin_table == nullptr || e->q == nullptr || e->k_cache == nullptr ||
-            e->v_cache == nullptr || e->position < 0 || e->position + tokens > e->cache_len ||
+            e->v_cache == nullptr || !cache_layout_ok(e, tokens) ||
             ((e->q_norm_weight != nullptr || e->k_norm_weight != nullptr) && !is_float_dtype(e->qk_norm_dtype)))
           return fail(NQB_ERR_INVALID_ARGUMENT, "op %d: q/k epilogue operands or cache position invalid", i);
       } else if (e->epilogue != NQB_EPI_STORE) {
@@ -2429,6 +2479,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       od.step.v_cache = static_cast<__nv_bfloat16 *>(e->v_cache);
       od.step.cache_len = e->cache_len;
       od.step.position = e->position;
+      od.step.seq_stride = e->sequence_stride;
       od.step.attn_out = static_cast<__nv_bfloat16 *>(e->attn_out);
       od.step.q_norm = f32(op_scales[i].q_norm);
       od.step.k_norm = f32(op_scales[i].k_norm);
@@ -2518,9 +2569,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   for (int i = 0; i < op_count; ++i) {
     OpDev &od = opdev[i];
     if (od.step.kind != NQB_OP_ATTENTION) continue;
-    const int halves = tokens >= mmad::kWarps ? 2 : 1;
-    const int want = std::max(1, std::min(32 / halves, ctas / od.step.kv_heads));
-    const int64_t most = od.step.position + tokens;  // keys the last token sees
+    const bool seqs = od.step.seq_stride != 0;
+    const int halves = tokens >= mmad::kWarps && !seqs ? 2 : 1;
+    const int64_t split_units = (seqs ? tokens : 1) * od.step.kv_heads;  // units per key split
+    if (split_units > ctas)
+      return fail(NQB_ERR_UNSUPPORTED, "op %d: %lld sequences x %d kv heads exceed the program's %d CTAs", i,
+                  static_cast<long long>(seqs ? tokens : 1), od.step.kv_heads, ctas);
+    const int want = std::max(1, std::min(32 / halves, static_cast<int>(ctas / split_units)));
+    const int64_t most = od.step.position + (seqs ? 1 : tokens);  // keys the last token sees
     od.step.att_chunk = ((most + want - 1) / want + 15) / 16 * 16;
     od.step.att_splits = static_cast<int32_t>((most + od.step.att_chunk - 1) / od.step.att_chunk);
     od.step.att_parts = od.step.att_splits * halves;
@@ -2561,13 +2617,17 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
       // two ahead of this one (the rows before this step's tokens do not
       // change during the program)
       const int target = std::max(0, g - 2);
-      for (int c = 0; c < ctas && c < op.step.kv_heads * op.step.att_splits; ++c) {
-        const int kvh = c / op.step.att_splits, spl = c % op.step.att_splits;
+      for (int c = 0; c < ctas && c < att_units(op.step, static_cast<int>(tokens)); ++c) {
+        int tu, kvh, spl;
+        att_unit_of(op.step, c, tu, kvh, spl);
         const int64_t k0 = static_cast<int64_t>(spl) * op.step.att_chunk + 16 * att_unit_ring_blocks(op.step, spl);
-        const int64_t k1 = std::min(static_cast<int64_t>(spl) * op.step.att_chunk + op.step.att_chunk,
-                                    op.step.position + tokens);
+        // at most kAttPrefetchRows rows: with independent sequences a step's
+        // K/V rows can exceed the L2, and the tables grow with the lines
+        const int64_t k1 = std::min({static_cast<int64_t>(spl) * op.step.att_chunk + op.step.att_chunk,
+                                     op.step.position + (op.step.seq_stride != 0 ? 1 : tokens),
+                                     k0 + kAttPrefetchRows});
         if (k1 <= k0) continue;
-        const int64_t off = (static_cast<int64_t>(kvh) * op.step.cache_len + k0) * kAttHd;
+        const int64_t off = att_cache_offset(op.step, tu, kvh, k0);
         std::vector<uint64_t> &lines = pf[static_cast<size_t>(target) * ctas + c];
         add_lines(lines, op.step.k_cache + off, (k1 - k0) * kAttHd * 2);
         add_lines(lines, op.step.v_cache + off, (k1 - k0) * kAttHd * 2);
@@ -2617,13 +2677,14 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
         if (op.step.kind == NQB_OP_ATTENTION && st == 0) {
           // this CTA's attention unit: its old K and V rows as 16-row blocks (4 KB each, K then V)
           const int cta_id = c * kClusterSize + q;
-          if (cta_id < op.step.kv_heads * op.step.att_splits) {
-            const int kvh = cta_id / op.step.att_splits, spl = cta_id % op.step.att_splits;
+          if (cta_id < att_units(op.step, static_cast<int>(tokens))) {
+            int tu, kvh, spl;
+            att_unit_of(op.step, cta_id, tu, kvh, spl);
             const int nb = att_unit_ring_blocks(op.step, spl);
             for (int b = 0; b < nb; ++b) {
-              const int64_t row = static_cast<int64_t>(kvh) * op.step.cache_len + static_cast<int64_t>(spl) * op.step.att_chunk + 16 * b;
-              addrs.push_back(reinterpret_cast<uint64_t>(op.step.k_cache + row * kAttHd));
-              addrs.push_back(reinterpret_cast<uint64_t>(op.step.v_cache + row * kAttHd));
+              const int64_t off = att_cache_offset(op.step, tu, kvh, static_cast<int64_t>(spl) * op.step.att_chunk + 16 * b);
+              addrs.push_back(reinterpret_cast<uint64_t>(op.step.k_cache + off));
+              addrs.push_back(reinterpret_cast<uint64_t>(op.step.v_cache + off));
             }
           }
         }

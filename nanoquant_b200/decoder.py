@@ -171,22 +171,31 @@ class Qwen3DecodeStep:
     step.  The normalised activations stay fp32 (no bf16 rounding).
     ``engine="shell"``: three programs per layer around separate shell kernels
     (norms, q/k norm + RoPE, attention), with bf16 normalised activations.
+
+    ``sequences=True`` (fused engine): the tokens are a batch of independent
+    sequences instead, token t the next token of sequence t with its own
+    caches (``k_cache[t]`` / ``v_cache[t]``, each ``[kv_heads, cache_len,
+    head_dim]``, ``position`` prior rows), all at position ``position``.
     """
 
     def __init__(self, shape: DecoderShape, blocks, shell: ShellWeights, device: torch.device, *, tokens: int = 1,
                  position: int = 0, cache_len: int | None = None, eps: float = 1e-6, rope_theta: float = 1e6,
-                 kv_init: torch.Generator | None = None, engine: str | None = None) -> None:
+                 kv_init: torch.Generator | None = None, engine: str | None = None, sequences: bool = False) -> None:
         if not 1 <= tokens <= 16:
             raise ValueError("a decode step takes 1 to 16 tokens")
         fusable = shape.head_dim == 128 and shape.q_heads == 4 * shape.kv_heads
         engine = engine or ("fused" if fusable else "shell")
         if engine not in ("fused", "shell") or (engine == "fused" and not fusable):
             raise ValueError(f"engine {engine!r} is not available for this shape")
+        if sequences and engine != "fused":
+            raise ValueError("independent sequences run on the fused engine only")
         self.engine = engine
+        self.sequences = sequences
         self.shape, self.device, self.tokens, self.position, self.eps = shape, device, tokens, position, eps
         self.shell = shell
-        self.cache_len = cache_len if cache_len is not None else position + tokens
-        if position + tokens > self.cache_len:
+        new_rows = 1 if sequences else tokens
+        self.cache_len = cache_len if cache_len is not None else position + new_rows
+        if position + new_rows > self.cache_len:
             raise ValueError("the cache is too short for the step's tokens")
         backend = CudaPackedSm100Backend()
         hd, hq, hkv = shape.head_dim, shape.q_heads, shape.kv_heads
@@ -202,8 +211,8 @@ class Qwen3DecodeStep:
         self.keys = position + 1
         self.attn_ws = torch.empty(attention_workspace_bytes(self.keys, tokens, hq, hd), dtype=torch.uint8,
                                    device=device)
-        self.cos, self.sin = (t.to(device) for t in rope_tables(
-            torch.arange(position, position + tokens), hd, rope_theta))
+        positions = torch.full((tokens,), position) if sequences else torch.arange(position, position + tokens)
+        self.cos, self.sin = (t.to(device) for t in rope_tables(positions, hd, rope_theta))
         g = kv_init if kv_init is not None else torch.Generator(device=device).manual_seed(2)
         self.layers = []
         for block in blocks:
@@ -215,11 +224,12 @@ class Qwen3DecodeStep:
             gate = torch.zeros(tokens, shape.intermediate, **f32)
             up = torch.zeros(tokens, shape.intermediate, **f32)
             down = torch.zeros(tokens, shape.hidden, **f32)
-            kc = torch.zeros(hkv, self.cache_len, hd, **bf16)
-            vc = torch.zeros(hkv, self.cache_len, hd, **bf16)
+            lead = (tokens,) if sequences else ()
+            kc = torch.zeros(*lead, hkv, self.cache_len, hd, **bf16)
+            vc = torch.zeros(*lead, hkv, self.cache_len, hd, **bf16)
             if position:
-                kc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
-                vc[:, :position] = torch.randn(hkv, position, hd, generator=g, device=device).bfloat16()
+                kc[..., :position, :] = torch.randn(*lead, hkv, position, hd, generator=g, device=device).bfloat16()
+                vc[..., :position, :] = torch.randn(*lead, hkv, position, hd, generator=g, device=device).bfloat16()
             layer = {"q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down, "k_cache": kc,
                      "v_cache": vc, "prepared": prepared}
             if engine == "shell":
@@ -256,7 +266,8 @@ class Qwen3DecodeStep:
             prepared = layer["prepared"]
             cache = {"q": self.q_rot.data_ptr(), "k_cache": layer["k_cache"].data_ptr(),
                      "v_cache": layer["v_cache"].data_ptr(), "cache_len": self.cache_len, "position": self.position,
-                     "q_heads": s.q_heads, "kv_heads": s.kv_heads, "head_dim": s.head_dim}
+                     "q_heads": s.q_heads, "kv_heads": s.kv_heads, "head_dim": s.head_dim,
+                     "sequence_stride": s.kv_heads * self.cache_len * s.head_dim if self.sequences else 0}
             ops.append(ProgramOp((prepared["q_proj"], prepared["k_proj"], prepared["v_proj"]), self.h, ext=ext(
                 epilogue=_native.NQB_EPI_QK_ROPE, norm_stats=self.stats.data_ptr(),
                 norm_weight=self.shell.input_norm[index].data_ptr(), norm_weight_dtype=w_dtype,
@@ -374,7 +385,8 @@ class Qwen3DecodeStep:
                 spec = prepared.spec
                 packed += (spec.out_features * ((spec.rank + 31) // 32) + spec.rank * ((spec.in_features + 31) // 32)) * 4
                 packed += (spec.in_features + spec.rank + spec.out_features) * 2
-        kv = len(self.layers) * 2 * s.kv_heads * (self.keys + self.tokens - 1) * s.head_dim * 2
+        rows = self.tokens * self.keys if self.sequences else self.keys + self.tokens - 1  # KV rows attention reads
+        kv = len(self.layers) * 2 * s.kv_heads * rows * s.head_dim * 2
         head = self.shell.lm_head.numel() * 2
         norms = len(self.layers) * (2 * s.hidden + 2 * s.head_dim) * 2 + s.hidden * 2
         return packed + kv + head + norms
@@ -583,12 +595,12 @@ def build_gemma3_step(shape: DecoderShape, device: torch.device, *, vocab: int =
 
 
 def build_qwen3_step(shape: DecoderShape, device: torch.device, *, vocab: int, tokens: int = 1, position: int = 0,
-                     layers: int | None = None, seed: int = 0) -> Qwen3DecodeStep:
+                     layers: int | None = None, seed: int = 0, sequences: bool = False) -> Qwen3DecodeStep:
     """Random-init packed layers and shell weights of ``shape`` wired into one decode step."""
 
     blocks = make_decoder_layers(shape, device, layers=layers, seed=seed)
     shell = random_shell_weights(shape, vocab, device, layers=len(blocks), seed=seed + 1)
-    return Qwen3DecodeStep(shape, blocks, shell, device, tokens=tokens, position=position)
+    return Qwen3DecodeStep(shape, blocks, shell, device, tokens=tokens, position=position, sequences=sequences)
 
 
 __all__ = [

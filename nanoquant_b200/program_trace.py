@@ -36,6 +36,8 @@ def main() -> None:
     parser.add_argument("--mhz", type=float, default=1965.0)
     parser.add_argument("--step", action="store_true", help="trace the fused decode-step program")
     parser.add_argument("--position", type=int, default=2048, help="--step: cached tokens")
+    parser.add_argument("--sequences", action="store_true",
+                        help="--step: the tokens are independent sequences with their own caches")
     args = parser.parse_args()
     os.environ["NQB_LIBRARY"] = "trace"  # before the library is first loaded
 
@@ -53,7 +55,7 @@ def main() -> None:
         from nanoquant_b200.decoder import build_qwen3_step
 
         step = build_qwen3_step(shape, device, vocab=1024, tokens=args.tokens, position=args.position,
-                                layers=args.layers)
+                                layers=args.layers, sequences=args.sequences)
         program, run, names = step.program, step.step, STEP_STAGES
     else:
         chain = decode_chain.DecodeChain(shape, decode_chain.make_decoder_layers(shape, device, layers=args.layers),

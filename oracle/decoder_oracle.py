@@ -76,7 +76,8 @@ def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, keys: int
 
 def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_cache: np.ndarray, *,
                  position: int, q_heads: int, kv_heads: int, head_dim: int, eps: float, cos: np.ndarray,
-                 sin: np.ndarray, accumulate: str = "float64", xn_bf16: bool = True) -> np.ndarray:
+                 sin: np.ndarray, accumulate: str = "float64", xn_bf16: bool = True,
+                 sequences: bool = False) -> np.ndarray:
     """One Qwen3-style layer on the residual stream ``h [T, hidden]``; returns the new ``h``.
 
     ``proj``: ``OracleLayer`` per projection name; ``norms``: this layer's
@@ -84,6 +85,9 @@ def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_
     updated in place at rows ``position + t``.  ``xn_bf16``: the normalised
     activations are rounded to bf16 before the projections (the device's
     shell engine stores them as bf16; its fused engine keeps them fp32).
+    ``sequences``: token t is the next token of its own sequence, caches
+    ``[T, Hkv, L, hd]``, updated at row ``position`` of cache t; each token
+    attends to rows ``[0, position]`` of its own caches.
     """
 
     tokens = h.shape[0]
@@ -98,10 +102,17 @@ def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_
     v = linear(xn, proj["v_proj"]).reshape(tokens, kv_heads, head_dim)
     q = bf16(rotate(rmsnorm(q, norms["q_norm"], eps), cos[:, None, :], sin[:, None, :]))
     k = bf16(rotate(rmsnorm(k, norms["k_norm"], eps), cos[:, None, :], sin[:, None, :]))
-    for t in range(tokens):
-        k_cache[:, position + t] = k[t]
-        v_cache[:, position + t] = bf16(v[t])
-    a = bf16(attention(q, k_cache, v_cache, position + 1).reshape(tokens, q_heads * head_dim))
+    if sequences:
+        for t in range(tokens):
+            k_cache[t, :, position] = k[t]
+            v_cache[t, :, position] = bf16(v[t])
+        a = np.concatenate([attention(q[t:t + 1], k_cache[t], v_cache[t], position + 1) for t in range(tokens)])
+        a = bf16(a.reshape(tokens, q_heads * head_dim))
+    else:
+        for t in range(tokens):
+            k_cache[:, position + t] = k[t]
+            v_cache[:, position + t] = bf16(v[t])
+        a = bf16(attention(q, k_cache, v_cache, position + 1).reshape(tokens, q_heads * head_dim))
     h = h + linear(a, proj["o_proj"])
     xn = rnd(rmsnorm(h, norms["post_norm"], eps))
     gate = linear(xn, proj["gate_proj"])
@@ -114,7 +125,8 @@ def decode_layer(h: np.ndarray, proj: dict, norms: dict, k_cache: np.ndarray, v_
 def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_norm: np.ndarray,
                           lm_head: np.ndarray, *, position: int, q_heads: int, kv_heads: int, head_dim: int,
                           eps: float, theta: float, accumulate: str = "float64",
-                          head_accumulate: str = "float64", xn_bf16: bool = True) -> np.ndarray:
+                          head_accumulate: str = "float64", xn_bf16: bool = True,
+                          sequences: bool = False) -> np.ndarray:
     """Logits ``[T, vocab]`` of a step whose layers arrive one at a time.
 
     ``layer_at(i)`` returns ``(proj, norms, k_cache, v_cache)`` of layer i (the
@@ -125,11 +137,13 @@ def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_
 
     tokens = hidden.shape[0]
     h = hidden.astype(np.float32).copy()
-    cos, sin = rope_tables(np.arange(position, position + tokens), head_dim, theta)
+    positions = np.full(tokens, position) if sequences else np.arange(position, position + tokens)
+    cos, sin = rope_tables(positions, head_dim, theta)
     for i in range(layer_count):
         proj, norms, k_cache, v_cache = layer_at(i)
         h = decode_layer(h, proj, norms, k_cache, v_cache, position=position, q_heads=q_heads, kv_heads=kv_heads,
-                         head_dim=head_dim, eps=eps, cos=cos, sin=sin, accumulate=accumulate, xn_bf16=xn_bf16)
+                         head_dim=head_dim, eps=eps, cos=cos, sin=sin, accumulate=accumulate, xn_bf16=xn_bf16,
+                         sequences=sequences)
     xn = bf16(rmsnorm(h, final_norm, eps))
     if head_accumulate == "float64":
         return (xn.astype(np.float64) @ lm_head.astype(np.float64).T).astype(np.float32)
@@ -138,12 +152,15 @@ def decode_step_streaming(hidden: np.ndarray, layer_count: int, layer_at, final_
 
 def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: list[np.ndarray],
                 v_caches: list[np.ndarray], *, position: int, q_heads: int, kv_heads: int, head_dim: int,
-                eps: float, theta: float, xn_bf16: bool = True) -> tuple[np.ndarray, list[np.ndarray], list[np.ndarray]]:
+                eps: float, theta: float, xn_bf16: bool = True,
+                sequences: bool = False) -> tuple[np.ndarray, list[np.ndarray], list[np.ndarray]]:
     """Logits ``[T, vocab]`` and the updated caches.
 
     ``layers[i]``: ``OracleLayer`` per projection name; ``norms``: lists
     ``input_norm``, ``post_norm``, ``q_norm``, ``k_norm`` (per layer) and
     ``final_norm``, ``lm_head`` (float32 arrays holding bf16 values).
+    ``sequences``: independent sequences with caches ``[T, Hkv, L, hd]``
+    (see :func:`decode_layer`).
     """
 
     k_caches = [c.copy() for c in k_caches]
@@ -155,7 +172,7 @@ def decode_step(hidden: np.ndarray, layers: list[dict], norms: dict, k_caches: l
 
     logits = decode_step_streaming(hidden, len(layers), layer_at, norms["final_norm"], norms["lm_head"],
                                    position=position, q_heads=q_heads, kv_heads=kv_heads, head_dim=head_dim, eps=eps,
-                                   theta=theta, xn_bf16=xn_bf16)
+                                   theta=theta, xn_bf16=xn_bf16, sequences=sequences)
     return logits, k_caches, v_caches
 
 
@@ -240,9 +257,10 @@ class CpuDecodeStep:
 
     def __init__(self, *, layers: int, hidden: int, intermediate: int, q_heads: int, kv_heads: int, head_dim: int,
                  vocab: int, position: int, tokens: int = 1, pool: int = 2, bpw: float = 1.0, seed: int = 0,
-                 eps: float = 1e-6, theta: float = 1e6, family: str = "qwen3") -> None:
+                 eps: float = 1e-6, theta: float = 1e6, family: str = "qwen3", sequences: bool = False) -> None:
         rng = np.random.default_rng(seed)
         self.family = family
+        self.sequences = sequences
         self.layers, self.tokens, self.position = layers, tokens, position
         self.q_heads, self.kv_heads, self.head_dim, self.eps = q_heads, kv_heads, head_dim, eps
         q, kv = q_heads * head_dim, kv_heads * head_dim
@@ -278,8 +296,9 @@ class CpuDecodeStep:
             else:
                 norms = {"input_norm": norm(hidden), "post_norm": norm(hidden), "q_norm": norm(head_dim),
                          "k_norm": norm(head_dim)}
-            k = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
-            v = bf16(rng.standard_normal((kv_heads, position + tokens, head_dim), dtype=np.float32))
+            cache = (tokens, kv_heads, position + 1, head_dim) if sequences else (kv_heads, position + tokens, head_dim)
+            k = bf16(rng.standard_normal(cache, dtype=np.float32))
+            v = bf16(rng.standard_normal(cache, dtype=np.float32))
             self.pool.append((proj, norms, k, v))
         self.final_norm = norm(hidden) + (1.0 if family == "gemma" else 0.0)
         self.theta = theta
@@ -305,7 +324,7 @@ class CpuDecodeStep:
         return decode_step_streaming(self.hidden, self.layers, lambda i: pool[i % len(pool)], self.final_norm,
                                      self.lm_head, position=self.position, q_heads=self.q_heads,
                                      kv_heads=self.kv_heads, head_dim=self.head_dim, eps=self.eps, theta=self.theta,
-                                     accumulate="float32", head_accumulate="float32")
+                                     accumulate="float32", head_accumulate="float32", sequences=self.sequences)
 
 
 __all__ = ["CpuDecodeStep", "attention", "bf16", "decode_layer", "decode_step", "decode_step_streaming",

@@ -14,6 +14,7 @@ import pytest
 import torch
 
 from oracle import decoder_oracle as do
+from oracle import packed_oracle as po
 
 
 def test_oracle_bf16_rounding_matches_torch() -> None:
@@ -287,3 +288,79 @@ def test_decoder_step_graph_replay_is_bitwise_eager() -> None:
     second = step.replay().clone()
     torch.cuda.synchronize()
     assert torch.equal(eager, first) and torch.equal(first, second)
+
+
+def test_oracle_independent_sequences_match_single_token_steps() -> None:
+    """The oracle's batch of independent sequences equals one single-token step per sequence (CPU)."""
+
+    rng = np.random.default_rng(40)
+    tokens, hidden, q_heads, kv_heads, hd, position = 3, 64, 4, 1, 32, 5
+
+    def layer(n: int, m: int) -> po.OracleLayer:
+        r = 16
+        left = rng.integers(0, 2**16, size=(m, 1), dtype=np.int64).astype(np.int32)
+        right = rng.integers(0, 2**31, size=(r, (n + 31) // 32), dtype=np.int64).astype(np.int32)
+        return po.OracleLayer(n, m, r, left, right, np.full(n, 0.05, np.float32), np.ones(r, np.float32),
+                              np.full(m, 0.05, np.float32))
+
+    proj = {"q_proj": layer(hidden, q_heads * hd), "k_proj": layer(hidden, kv_heads * hd),
+            "v_proj": layer(hidden, kv_heads * hd), "o_proj": layer(q_heads * hd, hidden),
+            "gate_proj": layer(hidden, 96), "up_proj": layer(hidden, 96), "down_proj": layer(96, hidden)}
+    norms = {"input_norm": [np.ones(hidden, np.float32)], "post_norm": [np.ones(hidden, np.float32)],
+             "q_norm": [np.ones(hd, np.float32)], "k_norm": [np.ones(hd, np.float32)],
+             "final_norm": np.ones(hidden, np.float32), "lm_head": rng.standard_normal((50, hidden)).astype(np.float32)}
+    hidden_in = rng.standard_normal((tokens, hidden)).astype(np.float32)
+    k = do.bf16(rng.standard_normal((tokens, kv_heads, position + 1, hd)).astype(np.float32))
+    v = do.bf16(rng.standard_normal((tokens, kv_heads, position + 1, hd)).astype(np.float32))
+    batch, kb, vb = do.decode_step(hidden_in, [proj], norms, [k], [v], position=position, q_heads=q_heads,
+                                   kv_heads=kv_heads, head_dim=hd, eps=1e-6, theta=1e6, sequences=True)
+    for t in range(tokens):
+        one, k1, v1 = do.decode_step(hidden_in[t:t + 1], [proj], norms, [k[t]], [v[t]], position=position,
+                                     q_heads=q_heads, kv_heads=kv_heads, head_dim=hd, eps=1e-6, theta=1e6)
+        np.testing.assert_allclose(batch[t], one[0], rtol=1e-5, atol=1e-6)
+        np.testing.assert_array_equal(kb[0][t], k1[0])
+        np.testing.assert_array_equal(vb[0][t], v1[0])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize(("tokens", "pos"), ((2, 300), (16, 300), (16, 9000)))
+def test_fused_step_over_independent_sequences_matches_oracle(tokens: int, pos: int) -> None:
+    """A batch of independent sequences (own caches per token, all at one position) in the fused program."""
+
+    from nanoquant_b200.decode_chain import DecoderShape, make_decoder_layers
+    from nanoquant_b200.decoder import Qwen3DecodeStep, random_shell_weights
+    from tests.test_cuda_parity import oracle_from_state
+
+    dev = _gpu()
+    shape = DecoderShape("fusable", 2, 512, 1024, 8, 2, 128, 1.0)
+    blocks = make_decoder_layers(shape, dev, layers=2, seed=44)
+    shell = random_shell_weights(shape, 2000, dev, layers=2, seed=45)
+    step = Qwen3DecodeStep(shape, blocks, shell, dev, tokens=tokens, position=pos, sequences=True,
+                           kv_init=torch.Generator(device=dev).manual_seed(46))
+    assert step.layers[0]["k_cache"].shape == (tokens, 2, pos + 1, 128)
+    k0 = [layer["k_cache"].float().cpu().numpy() for layer in step.layers]
+    v0 = [layer["v_cache"].float().cpu().numpy() for layer in step.layers]
+    hidden = torch.randn(tokens, shape.hidden, generator=torch.Generator(device=dev).manual_seed(47), device=dev)
+    logits = step.step(hidden).cpu().numpy()
+    again = step.step(hidden).cpu().numpy()
+    torch.cuda.synchronize()
+    assert np.array_equal(logits, again)
+    layers = [{name: oracle_from_state(_host_state(state)) for name, state in block.items()} for block in blocks]
+    norms = {
+        "input_norm": [w.float().cpu().numpy() for w in shell.input_norm],
+        "post_norm": [w.float().cpu().numpy() for w in shell.post_norm],
+        "q_norm": [w.float().cpu().numpy() for w in shell.q_norm],
+        "k_norm": [w.float().cpu().numpy() for w in shell.k_norm],
+        "final_norm": shell.final_norm.float().cpu().numpy(),
+        "lm_head": shell.lm_head.float().cpu().numpy(),
+    }
+    ref, k1, v1 = do.decode_step(hidden.cpu().numpy(), layers, norms, k0, v0, position=pos, q_heads=8, kv_heads=2,
+                                 head_dim=128, eps=1e-6, theta=1e6, xn_bf16=False, sequences=True)
+    for a, b in zip(logits, ref, strict=True):
+        cosine = float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+        assert cosine >= 0.99999, cosine
+    for i, layer in enumerate(step.layers):
+        kc, vc = layer["k_cache"].float().cpu().numpy(), layer["v_cache"].float().cpu().numpy()
+        np.testing.assert_allclose(kc[:, :, pos], k1[i][:, :, pos], rtol=2e-2, atol=2e-2)
+        np.testing.assert_allclose(vc[:, :, pos], v1[i][:, :, pos], rtol=2e-2, atol=2e-2)
+        assert np.array_equal(kc[:, :, :pos], k0[i][:, :, :pos])
