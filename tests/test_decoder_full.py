@@ -83,3 +83,46 @@ def test_qwen3_8b_full_step_logits_match_oracle_at_bs16_and_bs1() -> None:
     assert min(cos1) >= 0.9999, cos1
     # the two batch sizes run different kernel instances; their first token agrees as closely
     assert _cosines(logits1, logits16[:1])[0] >= 0.9999
+
+
+@pytest.mark.timeout(1800)
+def test_qwen3_8b_full_step_over_16_independent_sequences_matches_oracle() -> None:
+    """Config 2 at batch 16 as 16 independent sequences, each on its own 2048-token caches."""
+
+    from nanoquant_b200.decode_chain import QWEN3_8B as shape
+    from nanoquant_b200.decode_chain import make_decoder_layers
+    from nanoquant_b200.decoder import Qwen3DecodeStep, random_shell_weights
+    from tests.test_cuda_parity import oracle_from_state
+
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test needs CUDA")
+    dev = torch.device("cuda", 0)
+    blocks = make_decoder_layers(shape, dev, seed=31)
+    shell = random_shell_weights(shape, VOCAB, dev, seed=32)
+    hidden = torch.randn(TOKENS, shape.hidden, generator=torch.Generator(device=dev).manual_seed(33), device=dev)
+    step = Qwen3DecodeStep(shape, blocks, shell, dev, tokens=TOKENS, position=POSITION, sequences=True,
+                           kv_init=torch.Generator(device=dev).manual_seed(34))
+    # the prior rows as the device step found them (the step appends row POSITION of every cache); kept on the
+    # device and moved to the host one layer at a time
+    prior = [(layer["k_cache"][:, :, :POSITION].clone(), layer["v_cache"][:, :, :POSITION].clone())
+             for layer in step.layers]
+    logits = step.step(hidden).cpu().numpy()
+    torch.cuda.synchronize()
+
+    def layer_at(i: int):
+        proj = {name: oracle_from_state(_host_state(state)) for name, state in blocks[i].items()}
+        norms = {"input_norm": shell.input_norm[i].float().cpu().numpy(),
+                 "post_norm": shell.post_norm[i].float().cpu().numpy(),
+                 "q_norm": shell.q_norm[i].float().cpu().numpy(),
+                 "k_norm": shell.k_norm[i].float().cpu().numpy()}
+        pad = np.zeros((TOKENS, shape.kv_heads, 1, shape.head_dim), np.float32)
+        k, v = (np.concatenate((c.float().cpu().numpy(), pad), axis=2) for c in prior[i])
+        return proj, norms, k, v
+
+    ref = do.decode_step_streaming(hidden.cpu().numpy(), shape.layers, layer_at,
+                                   shell.final_norm.float().cpu().numpy(), shell.lm_head.float().cpu().numpy(),
+                                   position=POSITION, q_heads=shape.q_heads, kv_heads=shape.kv_heads,
+                                   head_dim=shape.head_dim, eps=1e-6, theta=1e6, accumulate="float32",
+                                   head_accumulate="float32", xn_bf16=False, sequences=True)
+    cos = _cosines(logits, ref)
+    assert min(cos) >= 0.9999, cos
