@@ -753,7 +753,6 @@ constexpr int kAttPadRow = kAttHd * 2 + 16;  // staged K/V row stride of the ten
 // accumulator and exchange buffers, which are idle during attention stages
 constexpr int kAttStageBytes = 2 * 2 * 16 * kAttPadRow;
 constexpr int64_t kAttPrefetchRows = 512;  // K/V rows per attention unit on the L2 prefetch list
-constexpr int kAttAhead = 4;               // sub-blocks a warp prefetches ahead of its global K/V reads
 
 // Attention units: (kv head, key split), and with independent sequences
 // (seq_stride > 0) one set per token; unit u -> token tu (0 for one
@@ -987,25 +986,11 @@ __device__ __forceinline__ void attention_partials(const Params &p, const StepDe
     }
   };
   // token t over this split's keys b0 = first, first + step, .. (8-key sub-blocks)
-  // L2 prefetch of the sub-block at b0 when it is read from global memory:
-  // lanes 0-15 the K rows' 128-byte lines, lanes 16-31 the V rows'
-  const __nv_bfloat16 *krows = kbase - lane * 4, *vrows = vbase - lane * 4;
-  auto prefetch_block = [&](int64_t k0, int64_t b0, int64_t k1) {
-    const int64_t r = b0 + ((lane & 15) >> 1);
-    if (b0 - k0 >= ring_rows && r < k1) {
-      const __nv_bfloat16 *row = (lane < 16 ? krows : vrows) + r * kAttHd + (lane & 1) * (kAttHd / 2);
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(row));
-    }
-  };
   auto token_keys = [&](int t, int64_t k0, int64_t k1, int64_t first, int64_t step, float (&acc)[kAttGroup][4],
                         float (&m)[kAttGroup], float (&l)[kAttGroup]) {
     float qv[kAttGroup][4];
     load_q(t, qv, acc, m, l);
-    // sub-blocks kAttAhead steps ahead of the one being read are prefetched into L2
-#pragma unroll 1
-    for (int j = 0; j < kAttAhead; ++j) prefetch_block(k0, first + j * step, k1);
     for (int64_t b0 = first; b0 < k1; b0 += step) {
-      prefetch_block(k0, b0 + kAttAhead * step, k1);
       const int nk = static_cast<int>(min(static_cast<int64_t>(kAttSub), k1 - b0));
       uint2 kr[kAttSub], vr[kAttSub];
       load_block(k0, b0, nk, kr, vr);
