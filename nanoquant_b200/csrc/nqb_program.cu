@@ -2596,7 +2596,7 @@ int nqb_program_create(const nqb_program_op *ops, int32_t op_count, int64_t toke
   for (int g = 0; g < stages; ++g) {
     const OpDev &op = opdev[g >> 1];
     const int st = g & 1;
-    if (op.step.kind == NQB_OP_ATTENTION && st == 0) {
+    if (op.step.kind == NQB_OP_ATTENTION && st == 0 && op.step.seq_stride == 0) {
       // each CTA's unit (kv head, key split): its K and V rows that do not
       // stream through the sign ring go on the L2 prefetch list of the stage
       // two ahead of this one (the rows before this step's tokens do not
