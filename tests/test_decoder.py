@@ -364,3 +364,22 @@ def test_fused_step_over_independent_sequences_matches_oracle(tokens: int, pos: 
         np.testing.assert_allclose(kc[:, :, pos], k1[i][:, :, pos], rtol=2e-2, atol=2e-2)
         np.testing.assert_allclose(vc[:, :, pos], v1[i][:, :, pos], rtol=2e-2, atol=2e-2)
         assert np.array_equal(kc[:, :, :pos], k0[i][:, :, :pos])
+
+
+@pytest.mark.gpu
+def test_program_rejects_sequence_caches_too_short() -> None:
+    """With independent sequences each cache must hold row ``position``: the host refuses the program otherwise."""
+
+    from nanoquant_b200 import _native
+    from nanoquant_b200.decode_chain import DecoderShape, make_decoder_layers
+    from nanoquant_b200.decoder import Qwen3DecodeStep, random_shell_weights
+
+    dev = _gpu()
+    shape = DecoderShape("fusable", 1, 512, 1024, 8, 2, 128, 1.0)
+    blocks = make_decoder_layers(shape, dev, layers=1, seed=48)
+    shell = random_shell_weights(shape, 500, dev, layers=1, seed=49)
+    step = Qwen3DecodeStep(shape, blocks, shell, dev, tokens=2, position=64, sequences=True)
+    step.cache_len = 64  # rows [0, 64) only: the new row 64 does not fit
+    with pytest.raises(_native.NativeError) as err:
+        step._fused_program()
+    assert err.value.status == _native.NQB_ERR_INVALID_ARGUMENT
