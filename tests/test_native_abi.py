@@ -74,7 +74,8 @@ def test_ctypes_structs_match_the_header(tmp_path) -> None:
     compiler = shutil.which("gcc") or shutil.which("cc")
     if compiler is None:
         pytest.skip("no C compiler")
-    structs = {"nqb_linear_desc": _native.LinearDesc, "nqb_program_op": _native.ProgramOp}
+    structs = {"nqb_linear_desc": _native.LinearDesc, "nqb_program_op": _native.ProgramOp,
+               "nqb_program_op_ext": _native.ProgramOpExt}
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "nqb.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
